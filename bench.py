@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""Benchmark of the DS-MeZO zeroth-order optimizer step on B200.
+
+One step = power iteration of every unique activation (3 iterations), AGZO perturbation
+with Philox-regenerated draws, pos/neg copies, Kalman/SPSA update and ZO-Muon
+Newton-Schulz of every adapter factor of every layer (ds_mezo/controller.py:165-292),
+plus, on N > 1 GPUs, the all-reduce of the Kalman sums and the all-gather of the updated
+factors. Synthetic seeded inputs of the named shapes stand in for a model's adapters and
+rollout activations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 7b|1.5b|toy|70b] [--impl ours|reference]
+
+Prints one JSON line (rank 0). N > 1 runs under torch.distributed.run, one rank per GPU,
+layers sharded in contiguous ranges.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ds-mezo_b200"))
+
+CONFIGS = {
+    # name: layers, hidden, intermediate, kv_out, rank, tokens, factor dtype, act dtype, schedule, seed
+    "toy": dict(layers=4, hidden=512, inter=1408, kv=128, rank=8, tokens=256, fdt="f32", adt="f32",
+                schedule="quintic", seed=0, workload="toy adapter set (4 layers x 7 modules, rank 8)"),
+    "1.5b": dict(layers=28, hidden=1536, inter=8960, kv=256, rank=16, tokens=2048, fdt="bf16", adt="bf16",
+                 schedule="quintic", seed=1, workload="Qwen2.5-1.5B-shaped adapter set (28 x 7 modules, rank 16)"),
+    "7b": dict(layers=28, hidden=3584, inter=18944, kv=512, rank=64, tokens=4096, fdt="bf16", adt="bf16",
+               schedule="cubic", seed=2, workload="Qwen2.5-7B-shaped adapter set (28 x 7 modules, rank 64)"),
+    "70b": dict(layers=80, hidden=8192, inter=28672, kv=1024, rank=128, tokens=8192, fdt="bf16", adt="bf16",
+                schedule="cubic", seed=3, workload="Llama-3-70B-shaped adapter set (80 x 7 modules, rank 128)"),
+}
+DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+METRIC = "ZO optimizer step ms (all adapters, 7B/70B shape) at 1/2/4/8 B200; % HBM roofline"
+EPS = 1e-3
+TOTAL_STEPS = 1000
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def layer_ranges(layers, world):
+    base, extra = divmod(layers, world)
+    out, s = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append(range(s, s + n))
+        s += n
+    return out
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", ",".join(str(g) for g in self.gpus), "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(smax), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- setup
+def build_set(cfg, lrange, device, rank_offset, layout, keep_ns=False):
+    from dsmezo_b200 import AdapterSet, transformer_adapter_shapes
+    mods, bases = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"],
+                                             layer_range=lrange)
+    aset = AdapterSet(mods, bases, cfg["rank"], cfg["rank"], factor_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
+                      device=device, keep_ns_output=keep_ns, rng_offset_before=rank_offset, layout=layout)
+    g = torch.Generator(device=device)
+    g.manual_seed(cfg["seed"] * 1000 + (lrange.start if lrange else 0))
+    aset.factors.copy_(torch.randn(aset.numel, generator=g, device=device))
+    aset.mu.normal_(generator=g)                  # update matrices ~ N(0,1)
+    aset.var.fill_(EPS ** 2)
+    for b, s in enumerate(aset.bases):
+        aset.V(b).copy_(torch.linalg.qr(torch.randn(s.D, cfg["rank"], generator=g, device=device))[0])
+        scale = torch.exp(torch.randn(s.D, generator=g, device=device))
+        aset.H(b).copy_(torch.randn(s.T, s.D, generator=g, device=device) * scale)
+    return aset
+
+
+def alg_bytes(aset, cfg):
+    """Algorithmic bytes per launch of each streaming kernel (whole set)."""
+    f = aset.factors.element_size()
+    N = aset.numel
+    hb = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
+    R = cfg["rank"]
+    vr = sum(b.D * R for b in aset.bases) * 4
+    yr = sum(b.T * R for b in aset.bases) * 4
+    nB = sum(R * m.d_in for m in aset.modules)
+    return {
+        "pi_y": hb + vr + yr,                      # read H, V; write Y
+        "pi_w": hb + yr + vr,                      # read H, Y; write W
+        "pi_gram": vr,                             # read W
+        "pi_apply": 2 * vr,                        # read W, write W or V
+        "bside": nB * (f + 4),                     # read B, var_B
+        "perturb": N * (3 * f + 12),               # read p, mu, var; write pos, neg, z
+        "gram": N * 12,                            # read mu, var, z
+        "apply": N * (2 * f + 20),                 # read p, mu, var, z; write p, mu, var
+    }
+
+
+def step_alg_bytes(aset):
+    """Compulsory bytes of one step: adapter phase 4f+16 per element (read p, mu, var;
+    write p, mu, var, pos, neg) + three passes over every activation."""
+    f = aset.factors.element_size()
+    hb = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
+    return aset.numel * (4 * f + 16) + 3 * hb
+
+
+# ----------------------------------------------------------------------------- CPU oracle
+def cpu_oracle_sample(cfg, layers_in_sample=1, steps=1, warmup=0):
+    """The oracle (reference algorithm restated on CPU, fp32) on `layers_in_sample` layers
+    of the workload; returns seconds per step for the sample."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle import reference_ops as ref
+    from step_harness import make_inputs, oracle_state
+    torch.set_num_threads(os.cpu_count() or 1)
+    mods, bases, A, B, V0, H = make_inputs(layers_in_sample, cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"],
+                                           cfg["tokens"], cfg["seed"], torch.float32, torch.float32)
+    st = oracle_state(mods, A, B, V0, EPS, TOTAL_STEPS, schedule=ref.get_schedule(cfg["schedule"]))
+    g = torch.Generator().manual_seed(cfg["seed"])
+    rca = cfg["rank"]
+    times = []
+    for i in range(warmup + steps):
+        draws = []
+        for m in mods:
+            draws.append(torch.randn(cfg["rank"], cfg["rank"], generator=g))
+            draws.append(torch.randn(m.d_out, rca, generator=g))
+        t0 = time.perf_counter()
+        st.step_count += 1
+        perts = ref.perturb_phase(st, H, draws, 3)
+        ref.update_phase(st, perts, 1.0)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return sum(times) / len(times), torch.get_num_threads()
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="7b", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, cfg, world, rank)
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        pg = dist.group.WORLD
+    from dsmezo_b200 import ZOController, device_layout, draw_increments, transformer_adapter_shapes
+    from dsmezo_b200._lib import KERNEL_IDS, lib
+    layout = device_layout(device)
+    ranges = layer_ranges(cfg["layers"], world)
+    all_mods, _ = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"])
+    incs = draw_increments(all_mods, cfg["rank"], cfg["rank"], *layout)
+    per_layer = len(all_mods) // cfg["layers"]
+    before = sum(incs[: ranges[rank].start * per_layer])
+    aset = build_set(cfg, ranges[rank], device, before, layout)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(cfg["seed"])
+    ctl = ZOController(aset, EPS, TOTAL_STEPS, gen, schedule=cfg["schedule"], process_group=pg,
+                       rng_increment_total=sum(incs))
+    # all-gather target: every rank's factor arena, padded to the largest shard
+    gather = None
+    if world > 1:
+        import torch.distributed as dist
+        sizes = []
+        for lr in ranges:
+            ms, _ = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"],
+                                               layer_range=lr)
+            sizes.append(sum(m.d_out * cfg["rank"] + cfg["rank"] * m.d_in for m in ms))
+        cap = max(sizes)
+        send = torch.zeros(cap, dtype=aset.factors.dtype, device=device)
+        gather = (send, torch.empty(cap * world, dtype=aset.factors.dtype, device=device))
+    dd_gen = torch.Generator().manual_seed(cfg["seed"])
+
+    def step():
+        ctl.perturb()
+        dd = float(torch.randn((), generator=dd_gen)) * 10.0
+        ctl.update(dd)
+        if gather is not None:
+            import torch.distributed as dist
+            send, recv = gather
+            send[: aset.numel].copy_(aset.factors)
+            dist.all_gather_into_tensor(recv, send, group=pg)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+
+    # per-kernel probes over the timed region
+    per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 6, "bside": 1, "coef": 1,
+                "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
+    probes = {}
+    for name, n in per_step.items():
+        cap = n * args.steps
+        st_ev = [torch.cuda.Event(enable_timing=True) for _ in range(cap)]
+        sp_ev = [torch.cuda.Event(enable_timing=True) for _ in range(cap)]
+        for e in st_ev + sp_ev:
+            e.record()                               # creates the underlying cudaEvent_t
+        probes[name] = [st_ev, sp_ev]
+    torch.cuda.synchronize()
+    for name, pr in probes.items():
+        st_ev, sp_ev = pr
+        arr_s = (ctypes_void_array(len(st_ev)))(*[e.cuda_event for e in st_ev])
+        arr_p = (ctypes_void_array(len(sp_ev)))(*[e.cuda_event for e in sp_ev])
+        pr += [arr_s, arr_p]                         # keep the arrays alive while probed
+        lib().dsmz_plan_set_probe(aset._plan, KERNEL_IDS[name], arr_s, arr_p, len(st_ev))
+
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler([local_rank] if world == 1 else list(range(world))) as clk:
+        t_start.record()
+        for _ in range(args.steps):
+            step()
+        t_stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms_local = t_start.elapsed_time(t_stop) / args.steps
+    kern = {}
+    for name, (st_ev, sp_ev, _, _) in probes.items():
+        cnt = lib().dsmz_plan_probe_count(aset._plan, KERNEL_IDS[name])
+        lib().dsmz_plan_set_probe(aset._plan, KERNEL_IDS[name], None, None, 0)
+        if cnt:
+            tot = sum(st_ev[i].elapsed_time(sp_ev[i]) for i in range(cnt))
+            kern[name] = {"launches": cnt, "total_ms": tot, "avg_ms": tot / cnt}
+    ms = ms_local
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms_local], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the public API: activations from pinned host memory each step,
+    # Kalman scalars read back each step
+    e2e = None
+    if not args.no_e2e:
+        host_H = torch.empty(aset.H_arena.numel(), dtype=aset.H_arena.dtype, pin_memory=True)
+        host_H.copy_(aset.H_arena)
+        host_out = torch.empty(2, dtype=torch.float64, pin_memory=True)
+        n_e2e = max(1, min(args.steps, 5))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n_e2e):
+            aset.H_arena.copy_(host_H, non_blocking=True)
+            ctl.perturb()
+            host_out.copy_(aset.kalman_sums(), non_blocking=True)
+            dd = float(torch.randn((), generator=dd_gen)) * 10.0
+            ctl.update(dd)
+            if gather is not None:
+                import torch.distributed as dist
+                send, recv = gather
+                send[: aset.numel].copy_(aset.factors)
+                dist.all_gather_into_tensor(recv, send, group=pg)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / n_e2e
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": host_H.numel() * host_H.element_size(),
+               "d2h_bytes_per_step": 16, "steps": n_e2e}
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    hbm, tf, src = peaks()
+    ab = alg_bytes(aset, cfg)
+    dom = max(kern, key=lambda k: kern[k]["total_ms"]) if kern else None
+    roof = None
+    if dom is not None and dom in ab:
+        achieved = ab[dom] / (kern[dom]["avg_ms"] * 1e-3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": None, "peak_source": src,
+                "alg_bytes_per_launch": ab[dom]}
+    for k, v in kern.items():
+        if k in ab:
+            v["alg_GBps"] = ab[k] / (v["avg_ms"] * 1e-3) / 1e9
+            v["frac_hbm"] = v["alg_GBps"] / hbm
+    step_bytes = step_alg_bytes(aset) * (world if world > 1 else 1)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
+        cpu = {"value": s * 1e3 * cfg["layers"], "unit": "ms", "cores": cores, "kind": "port",
+               "sample": f"oracle (fp32 torch CPU restatement of the reference step) on 1 of {cfg['layers']} "
+                         f"layers, one step, scaled x{cfg['layers']}"}
+    out = {
+        "metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": cfg["fdt"] if cfg["fdt"] == "bf16" else "f32", "data": "synthetic (seeded N(0,1) factors and "
+        "momentum, lognormal-scaled N(0,1) activations)",
+        "config": {"workload": cfg["workload"], "layers": cfg["layers"], "hidden": cfg["hidden"],
+                   "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
+                   "factor_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
+                   "power_iters": 3, "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (activations %.2f GB per step)" %
+                         (sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9)},
+        "roofline": roof,
+        "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
+                          "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1)},
+        "kernels": kern,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": aset.launch_count(3) * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def ctypes_void_array(n):
+    import ctypes
+    return ctypes.c_void_p * n
+
+
+def run_reference(args, cfg, world, rank):
+    """Reference arm: the reference algorithm on the host cores (the oracle port, since the
+    reference is Python/Triton with no CPU path of its own), bounded sample per step."""
+    if rank != 0:
+        return
+    times = []
+    cores = 1
+    for i in range(args.warmup + args.steps):
+        s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
+        if i >= args.warmup:
+            times.append(s)
+    ms = sum(times) / len(times) * 1e3 * cfg["layers"]
+    out = {"metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+           "config": {"workload": cfg["workload"], "parallelism": "host CPU"},
+           "cpu_baseline": {"value": ms, "unit": "ms", "cores": cores, "kind": "port",
+                            "sample": f"1 of {cfg['layers']} layers per step, scaled x{cfg['layers']}"},
+           "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

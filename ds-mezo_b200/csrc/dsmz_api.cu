@@ -1,0 +1,802 @@
+// C ABI of libdsmezo: plans, launch sequences and the per-op drop-ins declared in dsmezo.h.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "dsmz_kernels.cuh"
+
+using namespace dsmz;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+  return fail(DSMZ_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define DSMZ_LAUNCHED(what)                                  \
+  do {                                                        \
+    cudaError_t e_ = cudaGetLastError();                      \
+    if (e_ != cudaSuccess) return cuda_fail((what), e_);      \
+  } while (0)
+
+// ------------------------------------------------------------------ workspace layout
+struct Layout {
+  size_t bytes = 0;
+  size_t take(size_t n, size_t align = 256) {
+    bytes = (bytes + align - 1) & ~(align - 1);
+    const size_t off = bytes;
+    bytes += n;
+    return off;
+  }
+};
+
+int seg_vectors(int r) {
+  // ~128K elements per segment keeps the Gram partials small; a multiple of the sub-tile.
+  const int tv = tile_vectors(r);
+  int segv = (131072 / (r < 1 ? 1 : r)) / tv * tv;
+  return segv < tv ? tv : segv;
+}
+
+int gram_rb(int r) { return r <= 64 ? 4 : 8; }
+
+size_t gram_smem(int r) {
+  const int RB = gram_rb(r);
+  const int tpr = (r + RB - 1) / RB;
+  const int rp = tpr * RB;
+  const int ngroups = kThreads / (tpr * tpr);
+  const size_t xs = static_cast<size_t>(tile_vectors(r)) * (rp + 1) * sizeof(float);
+  const size_t red = ngroups > 1 ? static_cast<size_t>(ngroups) * rp * rp * sizeof(double) : 0;
+  return xs > red ? xs : red;
+}
+size_t apply_smem(int r) {
+  const int rp = pad4(r);
+  return (static_cast<size_t>(r) * rp + static_cast<size_t>(tile_vectors(r)) * (rp + 1)) * sizeof(float);
+}
+size_t perturb_smem(int r, int R, int RC) {
+  const int KW = RC;  // side B width; side A uses RCA <= RC
+  const int TV = tile_vectors(r);
+  return (static_cast<size_t>(KW) * R + static_cast<size_t>(TV) * (KW + 1) + static_cast<size_t>(TV) * (r + 1)) *
+         sizeof(float);
+}
+size_t coef_smem(int R, int RC) { return static_cast<size_t>(R) * RC * sizeof(double); }
+
+template <typename K>
+int set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+  }
+  return 0;
+}
+
+// One adapter matrix (or W basis matrix) with its segment and workspace slots.
+void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bool with_solve) {
+  m.segv = seg_vectors(static_cast<int>(m.r));
+  m.nseg = static_cast<int32_t>((m.nvec + m.segv - 1) / m.segv);
+  if (m.nseg < 1) m.nseg = 1;
+  m.seg0 = seg_counter;
+  seg_counter += m.nseg;
+  const size_t rr = static_cast<size_t>(m.r) * m.r;
+  m.gram_off = static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double));
+  m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
+  m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * rr * sizeof(double)) / sizeof(double)) : 0;
+  mats.push_back(m);
+}
+
+void fill_basis_tiles(BasisD& b, int& ytiles, int& wtiles) {
+  const int ntn = (b.R + 63) / 64;
+  b.ytile0 = ytiles;
+  b.nytile = static_cast<int32_t>(((b.T + 63) / 64) * ntn);
+  ytiles += b.nytile;
+  b.wtile0 = wtiles;
+  b.nwtile = static_cast<int32_t>(((b.D + 63) / 64) * ntn);
+  wtiles += b.nwtile;
+}
+
+NSArgs make_ns(const dsmz_ns_schedule* s, float floor_) {
+  NSArgs a{};
+  dsmz_ns_schedule cub;
+  if (!s) { dsmz_ns_schedule_cubic(&cub); s = &cub; }
+  a.iters = s->iters;
+  for (int i = 0; i < s->iters && i < DSMZ_MAX_NS_ITERS; ++i)
+    for (int j = 0; j < 3; ++j) a.c[i][j] = s->c[i][j];
+  a.norm_floor = floor_;
+  return a;
+}
+
+}  // namespace
+
+// ====================================================================== plan
+struct dsmz_plan {
+  std::vector<MatD> mats, w1, w2;
+  std::vector<ModD> mods;
+  std::vector<BasisD> bases;
+  Layout ws;                        // workspace layout
+  size_t off_mats = 0, off_w1 = 0, off_w2 = 0, off_mods = 0, off_bases = 0, table_bytes = 0;
+  std::vector<unsigned char> blob;  // host copy of the tables
+  char* dev_tables = nullptr;
+  char* workspace = nullptr;
+  int nsegs = 0, nwsegs = 0, nchunks = 0, nytiles = 0, nwtiles = 0;
+  int factor_dtype = DSMZ_F32;
+  int r = 0, R = 0, RC = 0;
+  int64_t seg_kal_off = 0, kal_sum_off = 0;
+  uint64_t rng_increment = 0;
+  struct Probe {
+    std::vector<cudaEvent_t> start, stop;
+    int count = 0;
+  };
+  mutable Probe probes[DSMZ_NUM_KIDS];
+
+  void probe_begin(int kid, cudaStream_t s) const {
+    Probe& p = probes[kid];
+    if (p.count < static_cast<int>(p.start.size())) cudaEventRecord(p.start[p.count], s);
+  }
+  void probe_end(int kid, cudaStream_t s) const {
+    Probe& p = probes[kid];
+    if (p.count < static_cast<int>(p.stop.size())) cudaEventRecord(p.stop[p.count++], s);
+  }
+
+  Tables tables() const {
+    Tables t{};
+    t.mats = reinterpret_cast<const MatD*>(dev_tables + off_mats);
+    t.nmats = static_cast<int32_t>(mats.size());
+    t.nsegs = nsegs;
+    t.mods = reinterpret_cast<const ModD*>(dev_tables + off_mods);
+    t.nmods = static_cast<int32_t>(mods.size());
+    t.nchunks = nchunks;
+    t.bases = reinterpret_cast<const BasisD*>(dev_tables + off_bases);
+    t.nbases = static_cast<int32_t>(bases.size());
+    t.nytiles = nytiles;
+    t.nwtiles = nwtiles;
+    t.wmats1 = reinterpret_cast<const MatD*>(dev_tables + off_w1);
+    t.wmats2 = reinterpret_cast<const MatD*>(dev_tables + off_w2);
+    t.nwsegs = nwsegs;
+    t.factor_dtype = factor_dtype;
+    t.ws = workspace;
+    t.seg_kal_off = seg_kal_off;
+    t.kal_sum_off = kal_sum_off;
+    return t;
+  }
+
+  // Lays the tables out in one blob; pointers into the workspace are patched at bind.
+  void pack() {
+    Layout T;
+    off_mats = T.take(mats.size() * sizeof(MatD), 64);
+    off_w1 = T.take(w1.size() * sizeof(MatD), 64);
+    off_w2 = T.take(w2.size() * sizeof(MatD), 64);
+    off_mods = T.take(mods.size() * sizeof(ModD), 64);
+    off_bases = T.take(bases.size() * sizeof(BasisD), 64);
+    table_bytes = T.bytes < 64 ? 64 : T.bytes;
+  }
+  void write_blob() {
+    blob.assign(table_bytes, 0);
+    if (!mats.empty()) std::memcpy(blob.data() + off_mats, mats.data(), mats.size() * sizeof(MatD));
+    if (!w1.empty()) std::memcpy(blob.data() + off_w1, w1.data(), w1.size() * sizeof(MatD));
+    if (!w2.empty()) std::memcpy(blob.data() + off_w2, w2.data(), w2.size() * sizeof(MatD));
+    if (!mods.empty()) std::memcpy(blob.data() + off_mods, mods.data(), mods.size() * sizeof(ModD));
+    if (!bases.empty()) std::memcpy(blob.data() + off_bases, bases.data(), bases.size() * sizeof(BasisD));
+  }
+};
+
+namespace {
+
+// Workspace-relative slots that hold device pointers (W, Y) are stored as offsets during
+// planning and turned into addresses once the workspace is known.
+void patch_ws_pointers(dsmz_plan* P) {
+  for (size_t i = 0; i < P->bases.size(); ++i) {
+    const BasisD& b = P->bases[i];
+    float* W = reinterpret_cast<float*>(P->workspace) + b.w_off;
+    P->w1[i].mu = W;
+    P->w1[i].param = W;
+    P->w2[i].mu = W;
+    P->w2[i].param = b.Vout;
+  }
+}
+
+// ---------------------------------------------------------------- launch sequences
+int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s) {
+  if (P->bases.empty() || iters <= 0) return 0;
+  const Tables tb = P->tables();
+  const int R = P->R;
+  const size_t gs = gram_smem(R), as = apply_smem(R);
+  int rc;
+  if (gram_rb(R) == 4) { if ((rc = set_smem(k_gram<0, 4>, gs))) return rc; }
+  else { if ((rc = set_smem(k_gram<0, 8>, gs))) return rc; }
+  if ((rc = set_smem(k_apply<0, 1>, as))) return rc;
+  const KalmanIn kin{};
+  const int nb = static_cast<int>(P->bases.size());
+  for (int it = 0; it < iters; ++it) {
+    P->probe_begin(DSMZ_KID_PI_Y, s);
+    k_pi_gemm<0><<<P->nytiles, kThreads, 0, s>>>(tb, it == 0 ? 1 : 0);
+    P->probe_end(DSMZ_KID_PI_Y, s);
+    DSMZ_LAUNCHED("power iteration Y = H V");
+    P->probe_begin(DSMZ_KID_PI_W, s);
+    k_pi_gemm<1><<<P->nwtiles, kThreads, 0, s>>>(tb, 0);
+    P->probe_end(DSMZ_KID_PI_W, s);
+    DSMZ_LAUNCHED("power iteration W = H^T Y");
+    for (int round = 0; round < 2; ++round) {
+      const MatD* wm = round == 0 ? tb.wmats1 : tb.wmats2;
+      P->probe_begin(DSMZ_KID_PI_GRAM, s);
+      if (gram_rb(R) == 4) k_gram<0, 4><<<P->nwsegs, kThreads, gs, s>>>(tb, tb.wmats1, nb, kin);
+      else k_gram<0, 8><<<P->nwsegs, kThreads, gs, s>>>(tb, tb.wmats1, nb, kin);
+      P->probe_end(DSMZ_KID_PI_GRAM, s);
+      DSMZ_LAUNCHED("power iteration Gram");
+      P->probe_begin(DSMZ_KID_PI_CHOL, s);
+      k_chol<<<nb, kThreads, 0, s>>>(tb, tb.wmats1, floor_);
+      P->probe_end(DSMZ_KID_PI_CHOL, s);
+      DSMZ_LAUNCHED("power iteration Cholesky");
+      P->probe_begin(DSMZ_KID_PI_APPLY, s);
+      k_apply<0, 1><<<P->nwsegs, kThreads, as, s>>>(tb, wm, nb, kin, 0.f, DSMZ_F32);
+      P->probe_end(DSMZ_KID_PI_APPLY, s);
+      DSMZ_LAUNCHED("power iteration apply");
+    }
+  }
+  return 0;
+}
+
+KalmanIn make_kin(float beta, float q, float dd, float floor_) {
+  KalmanIn k;
+  k.beta = beta;
+  k.beta2 = static_cast<float>(static_cast<double>(beta) * static_cast<double>(beta));
+  k.q = q;
+  k.dd = dd;
+  k.floor_ = floor_;
+  return k;
+}
+
+int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, KalmanIn kin, float floor_,
+                cudaStream_t s) {
+  if (P->mods.empty()) return 0;
+  const Tables tb = P->tables();
+  int rc;
+  const size_t cs = coef_smem(P->r, P->RC), ps = perturb_smem(P->r, P->r, P->RC);
+  if ((rc = set_smem(k_coef<0>, cs))) return rc;
+  if ((rc = set_smem(k_perturb<0>, ps))) return rc;
+  P->probe_begin(DSMZ_KID_BSIDE, s);
+  k_bside<<<P->nchunks, kThreads, 0, s>>>(tb);
+  P->probe_end(DSMZ_KID_BSIDE, s);
+  DSMZ_LAUNCHED("B-side sums");
+  P->probe_begin(DSMZ_KID_COEF, s);
+  k_coef<0><<<static_cast<int>(P->mods.size()), kThreads, cs, s>>>(tb, seed, offset, floor_);
+  P->probe_end(DSMZ_KID_COEF, s);
+  DSMZ_LAUNCHED("AGZO coefficients");
+  P->probe_begin(DSMZ_KID_PERTURB, s);
+  k_perturb<0><<<P->nsegs, kThreads, ps, s>>>(tb, seed, offset, eps, kin);
+  P->probe_end(DSMZ_KID_PERTURB, s);
+  DSMZ_LAUNCHED("perturbation");
+  P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
+  k_kalman_reduce<<<1, kThreads, 0, s>>>(tb);
+  P->probe_end(DSMZ_KID_KALMAN_SUM, s);
+  DSMZ_LAUNCHED("Kalman sums");
+  return 0;
+}
+
+int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cudaStream_t s) {
+  if (P->mats.empty()) return 0;
+  const Tables tb = P->tables();
+  const int r = P->r;
+  const int nm = static_cast<int>(P->mats.size());
+  const size_t gs = gram_smem(r), as = apply_smem(r);
+  int rc;
+  if ((rc = set_smem(k_gram<1, 4>, gs))) return rc;
+  if ((rc = set_smem(k_gram<1, 8>, gs))) return rc;
+  if ((rc = set_smem(k_apply<1, 0>, as))) return rc;
+  P->probe_begin(DSMZ_KID_GRAM, s);
+  if (gram_rb(r) == 4) k_gram<1, 4><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
+  else k_gram<1, 8><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
+  P->probe_end(DSMZ_KID_GRAM, s);
+  DSMZ_LAUNCHED("Kalman Gram");
+  P->probe_begin(DSMZ_KID_NS_SOLVE, s);
+  k_ns_solve<<<nm, kThreads, 0, s>>>(tb, tb.mats, ns);
+  P->probe_end(DSMZ_KID_NS_SOLVE, s);
+  DSMZ_LAUNCHED("Newton-Schulz solve");
+  P->probe_begin(DSMZ_KID_APPLY, s);
+  k_apply<1, 0><<<P->nsegs, kThreads, as, s>>>(tb, tb.mats, nm, kin, eta, P->factor_dtype);
+  P->probe_end(DSMZ_KID_APPLY, s);
+  DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
+  return 0;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+const char* dsmz_last_error(void) { return g_err.c_str(); }
+int dsmz_abi_version(void) { return DSMZ_ABI_VERSION; }
+
+int dsmz_ns_schedule_cubic(dsmz_ns_schedule* out) {
+  if (!out) return fail(DSMZ_ERR_INVALID, "dsmz_ns_schedule_cubic: null output");
+  std::memset(out, 0, sizeof(*out));
+  const double eps = static_cast<double>(1.1920928955078125e-07f);  // FLT_EPSILON
+  double lo = std::sqrt(eps), up = 1.0;
+  int n = 0;
+  while (1.0 - lo >= eps && n < DSMZ_MAX_NS_ITERS) {
+    const double s = up * up + lo * up + lo * lo;
+    const double alpha = std::sqrt(3.0 / s);
+    const double alpha3 = alpha * alpha * alpha;
+    const double beta = 4.0 / (2.0 + lo * up * (lo + up) * alpha3);
+    const double c1 = 1.5 * beta * alpha;
+    const double c3 = -0.5 * beta * alpha3;
+    out->c[n][0] = c1;
+    out->c[n][1] = c3;
+    out->c[n][2] = 0.0;
+    ++n;
+    lo = c1 * lo + c3 * lo * lo * lo;
+    up = 2.0 - lo;
+  }
+  out->iters = n;
+  return DSMZ_OK;
+}
+
+int dsmz_ns_schedule_quintic(dsmz_ns_schedule* out) {
+  if (!out) return fail(DSMZ_ERR_INVALID, "dsmz_ns_schedule_quintic: null output");
+  std::memset(out, 0, sizeof(*out));
+  out->iters = 5;
+  for (int i = 0; i < 5; ++i) {
+    out->c[i][0] = 3.4445;
+    out->c[i][1] = -4.7750;
+    out->c[i][2] = 2.0315;
+  }
+  return DSMZ_OK;
+}
+
+int64_t dsmz_randn_threads(int64_t n, int32_t sm_count, int32_t max_threads_per_sm) {
+  if (n <= 0) return 0;
+  const int64_t blocks = (n + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count) * (max_threads_per_sm / 256);
+  return 256 * (blocks < cap ? blocks : cap);
+}
+
+uint64_t dsmz_randn_offset_increment(int64_t n, int32_t sm_count, int32_t max_threads_per_sm) {
+  if (n <= 0) return 0;
+  const int64_t thr = dsmz_randn_threads(n, sm_count, max_threads_per_sm);
+  return static_cast<uint64_t>(((n - 1) / (thr * 4) + 1) * 4);
+}
+
+int dsmz_randn(float* out, int64_t n, uint64_t seed, uint64_t offset, int32_t sm_count, int32_t max_threads_per_sm,
+               dsmz_stream_t stream) {
+  if (n <= 0) return DSMZ_OK;
+  if (!out || sm_count <= 0 || max_threads_per_sm < 256) return fail(DSMZ_ERR_INVALID, "dsmz_randn: bad arguments");
+  const int64_t thr = dsmz_randn_threads(n, sm_count, max_threads_per_sm);
+  int64_t blocks = (n + kThreads - 1) / kThreads;
+  if (blocks > 65535) blocks = 65535;
+  k_randn<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(out, n, seed, offset, thr);
+  DSMZ_LAUNCHED("dsmz_randn");
+  return DSMZ_OK;
+}
+
+// ---------------------------------------------------------------------- plan
+int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
+  if (!d || !out) return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: null argument");
+  *out = nullptr;
+  if (d->factor_dtype != DSMZ_F32 && d->factor_dtype != DSMZ_BF16)
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: factor_dtype must be DSMZ_F32 or DSMZ_BF16");
+  if (d->num_modules < 0 || d->num_bases < 0 || (d->num_modules > 0 && !d->modules) ||
+      (d->num_bases > 0 && !d->bases))
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: bad module/basis arrays");
+  if (d->sm_count <= 0 || d->max_threads_per_sm < 256)
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: sm_count / max_threads_per_sm describe the device");
+  auto* P = new dsmz_plan();
+  P->factor_dtype = d->factor_dtype;
+  // bases
+  for (int i = 0; i < d->num_bases; ++i) {
+    const dsmz_basis_spec& b = d->bases[i];
+    if (!b.H || !b.V || b.T <= 0 || b.D <= 0 || b.R <= 0 || b.R > DSMZ_MAX_RANK || b.ld_H < b.D ||
+        (b.h_dtype != DSMZ_F32 && b.h_dtype != DSMZ_BF16)) {
+      delete P;
+      return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: basis " + std::to_string(i) + " is invalid");
+    }
+    if (i > 0 && b.R != P->R) {
+      delete P;
+      return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: all bases must share one width R");
+    }
+    P->R = static_cast<int>(b.R);
+    BasisD bd{};
+    bd.H = b.H; bd.hdt = b.h_dtype; bd.R = static_cast<int32_t>(b.R);
+    bd.T = b.T; bd.D = b.D; bd.h_s0 = b.ld_H; bd.h_s1 = 1;
+    bd.Vin = b.V; bd.v_s0 = b.R; bd.v_s1 = 1; bd.Vout = b.V;
+    bd.y_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(b.T) * b.R * sizeof(float)) / sizeof(float));
+    bd.w_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(b.D) * b.R * sizeof(float)) / sizeof(float));
+    fill_basis_tiles(bd, P->nytiles, P->nwtiles);
+    P->bases.push_back(bd);
+    MatD w{};
+    w.nvec = b.D; w.r = b.R; w.ld = b.R; w.cs = 1; w.side = 0; w.owner = i;
+    add_matrix(P->w1, P->ws, w, P->nwsegs, false);
+    MatD& w1 = P->w1.back();
+    w1.dw_off = static_cast<int64_t>(P->ws.take(3 * static_cast<size_t>(b.R) * b.R * sizeof(double)) / sizeof(double));
+    P->w2.push_back(w1);
+  }
+  // modules
+  uint64_t off = d->rng_offset_before;   // draws are placed relative to the step's base offset
+  for (int i = 0; i < d->num_modules; ++i) {
+    const dsmz_module_spec& m = d->modules[i];
+    const std::string who = "dsmz_plan_create: module " + std::to_string(i);
+    if (!m.A || !m.B || !m.pos_A || !m.pos_B || !m.neg_A || !m.neg_B || !m.mu_A || !m.mu_B || !m.var_A ||
+        !m.var_B || !m.z_A || !m.z_B) {
+      delete P;
+      return fail(DSMZ_ERR_INVALID, who + " has a null tensor pointer");
+    }
+    if (m.r <= 0 || m.r > DSMZ_MAX_RANK || m.d_out <= 0 || m.d_in <= 0 || m.ld_A < m.r || m.ld_B < m.d_in) {
+      delete P;
+      return fail(DSMZ_ERR_INVALID, who + " has an invalid shape or stride");
+    }
+    if (m.basis < 0 || m.basis >= d->num_bases || d->bases[m.basis].D != m.d_in) {
+      delete P;
+      return fail(DSMZ_ERR_INVALID, who + ": basis index out of range or basis D != d_in");
+    }
+    if (i > 0 && m.r != P->r) {
+      delete P;
+      return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: all modules must share one adapter rank r");
+    }
+    P->r = static_cast<int>(m.r);
+    const int RC = static_cast<int>(d->bases[m.basis].R);
+    P->RC = RC;
+    ModD md{};
+    md.r = static_cast<int32_t>(m.r); md.rc = RC; md.rca = md.r < RC ? md.r : RC;
+    md.d_out = m.d_out; md.d_in = m.d_in; md.basis = m.basis;
+    const int64_t nB = static_cast<int64_t>(md.r) * RC, nA = m.d_out * md.rca;
+    md.thrB = dsmz_randn_threads(nB, d->sm_count, d->max_threads_per_sm);
+    md.thrA = dsmz_randn_threads(nA, d->sm_count, d->max_threads_per_sm);
+    md.offB = off;
+    off += dsmz_randn_offset_increment(nB, d->sm_count, d->max_threads_per_sm);
+    md.offA = off;
+    off += dsmz_randn_offset_increment(nA, d->sm_count, d->max_threads_per_sm);
+    md.chunkw = 2048;
+    md.nchunk = static_cast<int32_t>((m.d_in + md.chunkw - 1) / md.chunkw);
+    md.chunk0 = P->nchunks;
+    P->nchunks += md.nchunk;
+    md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
+    md.bpart_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(md.nchunk) * 2 * nB * sizeof(float)) / sizeof(float));
+    md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1; md.bdt = d->factor_dtype;
+    md.a = static_cast<int32_t>(P->mats.size());
+    md.b = md.a + 1;
+    MatD a{};
+    a.param = m.A; a.pos = m.pos_A; a.neg = m.neg_A; a.mu = m.mu_A; a.var = m.var_A; a.z = m.z_A;
+    a.scratch = m.scratch_A; a.nvec = m.d_out; a.r = m.r; a.ld = m.ld_A; a.cs = 1; a.side = 0; a.owner = i;
+    add_matrix(P->mats, P->ws, a, P->nsegs, true);
+    MatD b{};
+    b.param = m.B; b.pos = m.pos_B; b.neg = m.neg_B; b.mu = m.mu_B; b.var = m.var_B; b.z = m.z_B;
+    b.scratch = m.scratch_B; b.nvec = m.d_in; b.r = m.r; b.ld = m.ld_B; b.cs = 1; b.side = 1; b.owner = i;
+    add_matrix(P->mats, P->ws, b, P->nsegs, true);
+    P->mods.push_back(md);
+  }
+  P->rng_increment = off - d->rng_offset_before;
+  P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
+  P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * sizeof(double)) / sizeof(double));
+  P->pack();
+  *out = P;
+  return DSMZ_OK;
+}
+
+void dsmz_plan_destroy(dsmz_plan* plan) { delete plan; }
+size_t dsmz_plan_table_bytes(const dsmz_plan* p) { return p ? p->table_bytes : 0; }
+size_t dsmz_plan_workspace_bytes(const dsmz_plan* p) { return p ? (p->ws.bytes < 256 ? 256 : p->ws.bytes) : 0; }
+uint64_t dsmz_plan_rng_increment(const dsmz_plan* p) { return p ? p->rng_increment : 0; }
+
+int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
+  if (!p) return 0;
+  int32_t n = 0;
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * (2 + 2 * 3);
+  if (!p->mods.empty()) n += 4 + 3;
+  return n;
+}
+
+int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* workspace, size_t workspace_bytes,
+                   dsmz_stream_t stream) {
+  if (!P || !device_tables || !workspace) return fail(DSMZ_ERR_INVALID, "dsmz_plan_bind: null argument");
+  if (table_bytes < P->table_bytes) return fail(DSMZ_ERR_WORKSPACE, "dsmz_plan_bind: table buffer too small");
+  if (workspace_bytes < dsmz_plan_workspace_bytes(P))
+    return fail(DSMZ_ERR_WORKSPACE, "dsmz_plan_bind: workspace too small (need " +
+                                        std::to_string(dsmz_plan_workspace_bytes(P)) + " bytes)");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0 || (reinterpret_cast<uintptr_t>(device_tables) & 63) != 0)
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_bind: workspace must be 256-byte and tables 64-byte aligned");
+  P->dev_tables = static_cast<char*>(device_tables);
+  P->workspace = static_cast<char*>(workspace);
+  patch_ws_pointers(P);
+  P->write_blob();
+  cudaError_t e = cudaMemcpyAsync(device_tables, P->blob.data(), P->table_bytes, cudaMemcpyHostToDevice,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("dsmz_plan_bind: table upload", e);
+  return DSMZ_OK;
+}
+
+static int plan_ready(const dsmz_plan* P, const char* who) {
+  if (!P) return fail(DSMZ_ERR_INVALID, std::string(who) + ": null plan");
+  if (!P->dev_tables || !P->workspace) return fail(DSMZ_ERR_INVALID, std::string(who) + ": plan is not bound");
+  return DSMZ_OK;
+}
+
+int dsmz_step_power_iteration(const dsmz_plan* P, int32_t num_iters, float norm_floor, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_step_power_iteration");
+  if (rc) return rc;
+  return run_power_iteration(P, num_iters, norm_floor, static_cast<cudaStream_t>(stream));
+}
+
+int dsmz_step_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, float beta, float q,
+                      float norm_floor, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_step_perturb");
+  if (rc) return rc;
+  return run_perturb(P, seed, offset, eps, make_kin(beta, q, 0.f, norm_floor), norm_floor,
+                     static_cast<cudaStream_t>(stream));
+}
+
+double* dsmz_step_kalman_sums(const dsmz_plan* P) {
+  if (!P || !P->workspace) return nullptr;
+  return reinterpret_cast<double*>(P->workspace) + P->kal_sum_off;
+}
+
+int dsmz_step_update(const dsmz_plan* P, float dd, float beta, float q, float eta, float norm_floor,
+                     const dsmz_ns_schedule* schedule, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_step_update");
+  if (rc) return rc;
+  if (schedule && (schedule->iters < 0 || schedule->iters > DSMZ_MAX_NS_ITERS))
+    return fail(DSMZ_ERR_INVALID, "dsmz_step_update: schedule iters out of range");
+  return run_update(P, make_kin(beta, q, dd, norm_floor), eta, make_ns(schedule, norm_floor),
+                    static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------- per-op drop-ins
+// Each builds a one-matrix (or one-basis, one-module) plan whose tables live at the head
+// of the caller's workspace, written by a kernel that takes them by value.
+static size_t table_head_bytes() { return 4096; }
+
+static int upload_small(dsmz_plan* P, char* ws, cudaStream_t s) {
+  P->dev_tables = ws;
+  if (P->table_bytes > table_head_bytes()) return fail(DSMZ_ERR_INVALID, "internal: table head overflow");
+  auto put_mats = [&](const std::vector<MatD>& v, size_t off) {
+    if (v.empty()) return;
+    Pack<MatD, 2> pk{};
+    for (size_t i = 0; i < v.size() && i < 2; ++i) pk.v[i] = v[i];
+    k_write_pack<MatD, 2><<<1, 32, 0, s>>>(pk, reinterpret_cast<MatD*>(ws + off), static_cast<int>(v.size()));
+  };
+  put_mats(P->mats, P->off_mats);
+  put_mats(P->w1, P->off_w1);
+  put_mats(P->w2, P->off_w2);
+  if (!P->mods.empty()) {
+    Pack<ModD, 1> pk{};
+    pk.v[0] = P->mods[0];
+    k_write_pack<ModD, 1><<<1, 32, 0, s>>>(pk, reinterpret_cast<ModD*>(ws + P->off_mods), 1);
+  }
+  if (!P->bases.empty()) {
+    Pack<BasisD, 1> pk{};
+    pk.v[0] = P->bases[0];
+    k_write_pack<BasisD, 1><<<1, 32, 0, s>>>(pk, reinterpret_cast<BasisD*>(ws + P->off_bases), 1);
+  }
+  DSMZ_LAUNCHED("table upload");
+  return 0;
+}
+
+static dsmz_plan muon_plan(int64_t M, int64_t N, Layout* L_out) {
+  dsmz_plan P;
+  P.ws.take(table_head_bytes());
+  MatD m{};
+  const bool tall = M >= N;
+  m.nvec = tall ? M : N;
+  m.r = tall ? N : M;
+  m.side = tall ? 0 : 1;
+  add_matrix(P.mats, P.ws, m, P.nsegs, true);
+  P.r = static_cast<int>(m.r);
+  P.pack();
+  if (L_out) *L_out = P.ws;
+  return P;
+}
+
+size_t dsmz_zo_muon_update_workspace_bytes(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  Layout L;
+  muon_plan(M, N, &L);
+  return L.bytes;
+}
+
+int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t ps1, const float* buf, int64_t bs0,
+                        int64_t bs1, float* scratch, int64_t ss0, int64_t ss1, int64_t M, int64_t N, float eta,
+                        float norm_floor, const dsmz_ns_schedule* schedule, void* workspace, size_t workspace_bytes,
+                        dsmz_stream_t stream) {
+  if (M <= 0 || N <= 0) return DSMZ_OK;
+  if (!param || !buf || !workspace) return fail(DSMZ_ERR_INVALID, "zo_muon_update: null pointer");
+  if (param_dtype != DSMZ_F32 && param_dtype != DSMZ_BF16) return fail(DSMZ_ERR_INVALID, "zo_muon_update: bad dtype");
+  if ((M < N ? M : N) > DSMZ_MAX_RANK)
+    return fail(DSMZ_ERR_UNSUPPORTED, "zo_muon_update: min(M, N) must be <= " + std::to_string(DSMZ_MAX_RANK));
+  if (bs0 != ps0 || bs1 != ps1 || (scratch && (ss0 != ps0 || ss1 != ps1)))
+    return fail(DSMZ_ERR_INVALID,
+                "zo_muon_update: buf and scratch must have param's strides (the reference indexes all three "
+                "with param.stride())");
+  if (schedule && (schedule->iters < 0 || schedule->iters > DSMZ_MAX_NS_ITERS))
+    return fail(DSMZ_ERR_INVALID, "zo_muon_update: schedule iters out of range");
+  Layout L;
+  dsmz_plan P = muon_plan(M, N, &L);
+  if (workspace_bytes < L.bytes) return fail(DSMZ_ERR_WORKSPACE, "zo_muon_update: workspace too small");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(DSMZ_ERR_INVALID, "zo_muon_update: workspace must be 256-byte aligned");
+  MatD& m = P.mats[0];
+  m.param = param; m.mu = const_cast<float*>(buf); m.scratch = scratch;
+  m.ld = ps0; m.cs = ps1;   // side B (wide) swaps roles inside vaddr2: element (k=row, v=col)
+  P.workspace = static_cast<char*>(workspace);
+  P.factor_dtype = param_dtype;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = upload_small(&P, static_cast<char*>(workspace), s);
+  if (rc) return rc;
+  const Tables tb = P.tables();
+  const int r = P.r;
+  const size_t gs = gram_smem(r), as = apply_smem(r);
+  const KalmanIn kin{};
+  if (gram_rb(r) == 4) {
+    if ((rc = set_smem(k_gram<0, 4>, gs))) return rc;
+    k_gram<0, 4><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
+  } else {
+    if ((rc = set_smem(k_gram<0, 8>, gs))) return rc;
+    k_gram<0, 8><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
+  }
+  DSMZ_LAUNCHED("zo_muon_update Gram");
+  k_ns_solve<<<1, kThreads, 0, s>>>(tb, tb.mats, make_ns(schedule, norm_floor));
+  DSMZ_LAUNCHED("zo_muon_update solve");
+  if ((rc = set_smem(k_apply<0, 0>, as))) return rc;
+  k_apply<0, 0><<<P.nsegs, kThreads, as, s>>>(tb, tb.mats, 1, kin, eta, param_dtype);
+  DSMZ_LAUNCHED("zo_muon_update apply");
+  return DSMZ_OK;
+}
+
+static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R) {
+  dsmz_plan P;
+  P.ws.take(table_head_bytes());
+  BasisD bd{};
+  bd.R = static_cast<int32_t>(R); bd.T = T; bd.D = D;
+  bd.y_off = static_cast<int64_t>(P.ws.take(static_cast<size_t>(T) * R * sizeof(float)) / sizeof(float));
+  bd.w_off = static_cast<int64_t>(P.ws.take(static_cast<size_t>(D) * R * sizeof(float)) / sizeof(float));
+  fill_basis_tiles(bd, P.nytiles, P.nwtiles);
+  P.bases.push_back(bd);
+  MatD w{};
+  w.nvec = D; w.r = R; w.ld = R; w.cs = 1; w.side = 0; w.owner = 0;
+  add_matrix(P.w1, P.ws, w, P.nwsegs, false);
+  P.w1[0].dw_off = static_cast<int64_t>(P.ws.take(3 * static_cast<size_t>(R) * R * sizeof(double)) / sizeof(double));
+  P.w2.push_back(P.w1[0]);
+  P.R = static_cast<int>(R);
+  P.pack();
+  return P;
+}
+
+size_t dsmz_power_iter_workspace_bytes(int64_t T, int64_t D, int64_t R) {
+  if (T <= 0 || D <= 0 || R <= 0) return 0;
+  return pi_plan(T, D, R).ws.bytes;
+}
+
+int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_t hs0, int64_t hs1, const float* V,
+                    int64_t R, int64_t vs0, int64_t vs1, float* out, int32_t num_iters, float norm_floor,
+                    void* workspace, size_t workspace_bytes, dsmz_stream_t stream) {
+  if (!H || !V || !out || !workspace) return fail(DSMZ_ERR_INVALID, "power_iter: null pointer");
+  if (T <= 0 || D <= 0 || R <= 0) return fail(DSMZ_ERR_INVALID, "power_iter: empty shape");
+  if (R > DSMZ_MAX_RANK) return fail(DSMZ_ERR_UNSUPPORTED, "power_iter: R must be <= " + std::to_string(DSMZ_MAX_RANK));
+  if (h_dtype != DSMZ_F32 && h_dtype != DSMZ_BF16) return fail(DSMZ_ERR_INVALID, "power_iter: bad dtype");
+  dsmz_plan P = pi_plan(T, D, R);
+  if (workspace_bytes < P.ws.bytes) return fail(DSMZ_ERR_WORKSPACE, "power_iter: workspace too small");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(DSMZ_ERR_INVALID, "power_iter: workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (num_iters <= 0) {
+    // zero iterations return the basis unchanged (contiguous copy)
+    if (vs1 != 1) return fail(DSMZ_ERR_UNSUPPORTED, "power_iter: num_iters == 0 needs unit column stride");
+    cudaError_t e = cudaMemcpy2DAsync(out, R * sizeof(float), V, vs0 * sizeof(float), R * sizeof(float), D,
+                                      cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_fail("power_iter copy", e);
+    return DSMZ_OK;
+  }
+  BasisD& b = P.bases[0];
+  b.H = H; b.hdt = h_dtype; b.h_s0 = hs0; b.h_s1 = hs1;
+  b.Vin = V; b.v_s0 = vs0; b.v_s1 = vs1; b.Vout = out;
+  P.workspace = static_cast<char*>(workspace);
+  patch_ws_pointers(&P);
+  int rc = upload_small(&P, static_cast<char*>(workspace), s);
+  if (rc) return rc;
+  return run_power_iteration(&P, num_iters, norm_floor, s);
+}
+
+static dsmz_plan agzo_plan(int64_t R, int64_t d_in, int64_t RC, int64_t d_out) {
+  dsmz_plan P;
+  P.ws.take(table_head_bytes());
+  const int rca = static_cast<int>(R < RC ? R : RC);
+  ModD md{};
+  md.r = static_cast<int32_t>(R); md.rc = static_cast<int32_t>(RC); md.rca = rca;
+  md.d_out = d_out; md.d_in = d_in; md.basis = 0;
+  md.chunkw = 2048;
+  md.nchunk = static_cast<int32_t>((d_in + md.chunkw - 1) / md.chunkw);
+  md.chunk0 = 0;
+  P.nchunks = md.nchunk;
+  const size_t nB = static_cast<size_t>(R) * RC;
+  md.coef_off = static_cast<int64_t>(P.ws.take((nB + static_cast<size_t>(R) * rca) * sizeof(float)) / sizeof(float));
+  md.bpart_off = static_cast<int64_t>(P.ws.take(md.nchunk * 2 * nB * sizeof(float)) / sizeof(float));
+  md.a = 0; md.b = 1;
+  P.mods.push_back(md);
+  MatD a{};
+  a.nvec = d_out; a.r = R; a.ld = R; a.cs = 1; a.side = 0; a.owner = 0;
+  add_matrix(P.mats, P.ws, a, P.nsegs, false);
+  MatD b{};
+  b.nvec = d_in; b.r = R; b.ld = d_in; b.cs = 1; b.side = 1; b.owner = 0;
+  add_matrix(P.mats, P.ws, b, P.nsegs, false);
+  BasisD bd{};
+  bd.R = static_cast<int32_t>(RC); bd.D = d_in;
+  P.bases.push_back(bd);
+  P.r = static_cast<int>(R);
+  P.RC = static_cast<int>(RC);
+  P.pack();
+  return P;
+}
+
+size_t dsmz_agzo_perturbation_workspace_bytes(int64_t R, int64_t d_in, int64_t RC, int64_t d_out) {
+  if (R <= 0 || d_in <= 0 || RC <= 0 || d_out <= 0) return 0;
+  return agzo_plan(R, d_in, RC, d_out).ws.bytes;
+}
+
+int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t bs0, int64_t bs1, const float* V,
+                           int64_t RC, int64_t vs0, int64_t vs1, const float* zcB, const float* zcA, int64_t d_out,
+                           float* z_A, float* z_B, float eps, float norm_floor, void* workspace,
+                           size_t workspace_bytes, dsmz_stream_t stream) {
+  if (!B || !V || !zcB || !zcA || !z_A || !z_B || !workspace)
+    return fail(DSMZ_ERR_INVALID, "agzo_perturbation: null pointer");
+  if (R <= 0 || d_in <= 0 || RC <= 0 || d_out <= 0) return fail(DSMZ_ERR_INVALID, "agzo_perturbation: empty shape");
+  if (R > DSMZ_MAX_RANK || RC > DSMZ_MAX_RANK)
+    return fail(DSMZ_ERR_UNSUPPORTED, "agzo_perturbation: R and RC must be <= " + std::to_string(DSMZ_MAX_RANK));
+  dsmz_plan P = agzo_plan(R, d_in, RC, d_out);
+  if (workspace_bytes < P.ws.bytes) return fail(DSMZ_ERR_WORKSPACE, "agzo_perturbation: workspace too small");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(DSMZ_ERR_INVALID, "agzo_perturbation: workspace must be 256-byte aligned");
+  ModD& md = P.mods[0];
+  md.zcB_ext = zcB; md.zcA_ext = zcA; md.Bp = B; md.varB = nullptr; md.b_s0 = bs0; md.b_s1 = bs1; md.bdt = DSMZ_F32;
+  P.mats[0].z = z_A;
+  P.mats[1].z = z_B;
+  BasisD& bd = P.bases[0];
+  bd.Vin = V; bd.v_s0 = vs0; bd.v_s1 = vs1;
+  P.workspace = static_cast<char*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = upload_small(&P, static_cast<char*>(workspace), s);
+  if (rc) return rc;
+  const Tables tb = P.tables();
+  const size_t cs = coef_smem(static_cast<int>(R), static_cast<int>(RC));
+  const size_t ps = perturb_smem(static_cast<int>(R), static_cast<int>(R), static_cast<int>(RC));
+  if ((rc = set_smem(k_coef<1>, cs))) return rc;
+  if ((rc = set_smem(k_perturb<1>, ps))) return rc;
+  k_bside<<<P.nchunks, kThreads, 0, s>>>(tb);
+  DSMZ_LAUNCHED("agzo B V");
+  k_coef<1><<<1, kThreads, cs, s>>>(tb, 0, 0, norm_floor);
+  DSMZ_LAUNCHED("agzo QR");
+  k_perturb<1><<<P.nsegs, kThreads, ps, s>>>(tb, 0, 0, eps, KalmanIn{});
+  DSMZ_LAUNCHED("agzo z");
+  return DSMZ_OK;
+}
+
+int dsmz_perturb_dual(int32_t dtype, const void* base, const float* z, void* pos, void* neg, int64_t n,
+                      dsmz_stream_t stream) {
+  if (n <= 0) return DSMZ_OK;
+  if (!base || !z || !pos || !neg) return fail(DSMZ_ERR_INVALID, "perturb_dual: null pointer");
+  if (dtype != DSMZ_F32 && dtype != DSMZ_BF16) return fail(DSMZ_ERR_INVALID, "perturb_dual: bad dtype");
+  int64_t blocks = (n + kThreads - 1) / kThreads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  k_dual<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(base, z, pos, neg, n, dtype);
+  DSMZ_LAUNCHED("perturb_dual");
+  return DSMZ_OK;
+}
+
+int dsmz_plan_set_probe(dsmz_plan* P, int32_t kernel, void** start_events, void** stop_events, int32_t capacity) {
+  if (!P || kernel < 0 || kernel >= DSMZ_NUM_KIDS || capacity < 0 || (capacity > 0 && (!start_events || !stop_events)))
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_probe: bad arguments");
+  auto& p = P->probes[kernel];
+  p.start.assign(reinterpret_cast<cudaEvent_t*>(start_events), reinterpret_cast<cudaEvent_t*>(start_events) + capacity);
+  p.stop.assign(reinterpret_cast<cudaEvent_t*>(stop_events), reinterpret_cast<cudaEvent_t*>(stop_events) + capacity);
+  p.count = 0;
+  return DSMZ_OK;
+}
+
+int32_t dsmz_plan_probe_count(const dsmz_plan* P, int32_t kernel) {
+  if (!P || kernel < 0 || kernel >= DSMZ_NUM_KIDS) return 0;
+  return P->probes[kernel].count;
+}
+
+}  // extern "C"

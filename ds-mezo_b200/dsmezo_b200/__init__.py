@@ -1,0 +1,17 @@
+"""B200-native (sm_100a) DS-MeZO optimizer hot path.
+
+* ``dsmezo_b200.kernels`` - drop-in for the reference module ``ds_mezo.kernels``
+  (zo_muon_update, fused_power_iter, fused_agzo_perturbation, fused_perturb_dual).
+* ``dsmezo_b200.AdapterSet`` / ``ZOController`` - the whole optimizer step over every
+  adapter of every layer as grouped launches (one sequence per phase).
+* ``dsmezo_b200.sharding`` - layer-sharded step over ranks (NCCL).
+
+All compute runs in libdsmezo.so (C ABI in include/dsmezo.h); there is no CPU path.
+"""
+from . import kernels  # noqa: F401
+from ._lib import DsmzError, lib  # noqa: F401
+from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ZOController, device_layout,  # noqa: F401
+                          draw_increments, kalman_beta_q, transformer_adapter_shapes)
+
+__all__ = ["kernels", "AdapterSet", "ZOController", "ModuleShape", "BasisShape", "transformer_adapter_shapes",
+           "draw_increments", "device_layout", "kalman_beta_q", "DsmzError", "lib"]

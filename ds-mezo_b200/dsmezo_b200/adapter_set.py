@@ -1,0 +1,299 @@
+"""Grouped optimizer step over a whole PiSSA adapter set.
+
+``AdapterSet`` keeps every adapter of every layer in contiguous HBM arenas, in the
+controller's module order (sorted by (layer, module name), ds_mezo/model_config.py:37):
+
+* factor arena (A then B of each module) in the factor dtype, and its +/- copies;
+* fp32 Kalman mean (momentum) and variance arenas, and the fp32 perturbation z
+  (the reference's ``perturbations`` dict, ds_mezo/controller.py:239);
+* one activation buffer H (T x D) and one basis V (D x R, fp32) per unique module input
+  (q/k/v share one, gate/up share one: ds_mezo/backend.py:49-52).
+
+A layer range is one contiguous slice of every arena, so layer sharding over ranks and
+the all-gather of the factors are single NCCL calls. ``ZOController`` runs the hot-path
+methods of DSMeZO_Controller (ds_mezo/controller.py:165-292) on it with one grouped
+launch sequence per phase.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import DSMZ_BF16, DSMZ_F32, BasisSpec, ModuleSpec, PlanDesc, check, lib
+
+FLT_MIN = float(torch.finfo(torch.float32).tiny)
+FLT_EPS = float(torch.finfo(torch.float32).eps)
+_DT = {torch.float32: DSMZ_F32, torch.bfloat16: DSMZ_BF16}
+
+MODULE_NAMES = ("down_proj", "gate_proj", "k_proj", "o_proj", "q_proj", "up_proj", "v_proj")
+INPUT_OF = {"q_proj": "qkv", "k_proj": "qkv", "v_proj": "qkv", "o_proj": "o",
+            "gate_proj": "gate_up", "up_proj": "gate_up", "down_proj": "down"}
+INPUT_ORDER = ("qkv", "o", "gate_up", "down")
+
+
+@dataclass(frozen=True)
+class ModuleShape:
+    layer: int
+    name: str
+    d_out: int
+    d_in: int
+    basis: int          # index into the basis list
+
+
+@dataclass(frozen=True)
+class BasisShape:
+    layer: int
+    name: str           # module input: qkv, o, gate_up, down
+    T: int              # activation rows (tokens)
+    D: int              # activation width
+
+
+def transformer_adapter_shapes(layers: int, hidden: int, intermediate: int, kv_out: int, tokens: int,
+                               layer_range: Optional[range] = None):
+    """Module and basis shapes of a Llama/Qwen-style decoder (q, k, v, o, gate, up, down)."""
+    dims = {"q_proj": (hidden, hidden), "k_proj": (kv_out, hidden), "v_proj": (kv_out, hidden),
+            "o_proj": (hidden, hidden), "gate_proj": (intermediate, hidden), "up_proj": (intermediate, hidden),
+            "down_proj": (hidden, intermediate)}
+    in_dim = {"qkv": hidden, "o": hidden, "gate_up": hidden, "down": intermediate}
+    lr = range(layers) if layer_range is None else layer_range
+    mods, bases = [], []
+    for li in lr:
+        base0 = len(bases)
+        for g in INPUT_ORDER:
+            bases.append(BasisShape(li, g, tokens, in_dim[g]))
+        for name in MODULE_NAMES:
+            d_out, d_in = dims[name]
+            mods.append(ModuleShape(li, name, d_out, d_in, base0 + INPUT_ORDER.index(INPUT_OF[name])))
+    return mods, bases
+
+
+def device_layout(device) -> tuple:
+    p = torch.cuda.get_device_properties(device)
+    return p.multi_processor_count, p.max_threads_per_multi_processor
+
+
+def draw_increments(modules: Sequence[ModuleShape], rank: int, basis_width: int, sm_count: int,
+                    max_threads_per_sm: int) -> List[int]:
+    """Generator offset advance of each module's two draws (Zc_B then Zc_A,
+    ds_mezo/controller.py:184-191) on a device with the given layout."""
+    L = lib()
+    out = []
+    rca = min(rank, basis_width)
+    for m in modules:
+        out.append(int(L.dsmz_randn_offset_increment(rank * basis_width, sm_count, max_threads_per_sm))
+                   + int(L.dsmz_randn_offset_increment(m.d_out * rca, sm_count, max_threads_per_sm)))
+    return out
+
+
+class AdapterSet:
+    """Arenas + bound plan for one set of modules (all of them, or one rank's layers)."""
+
+    def __init__(self, modules: Sequence[ModuleShape], bases: Sequence[BasisShape], rank: int, basis_width: int,
+                 factor_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
+                 keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None):
+        if factor_dtype not in _DT or act_dtype not in _DT:
+            raise ValueError("factor and activation dtypes must be float32 or bfloat16")
+        self.device = torch.device(device)
+        self.modules = list(modules)
+        self.bases = list(bases)
+        self.rank = int(rank)
+        self.basis_width = int(basis_width)
+        self.factor_dtype = factor_dtype
+        self.act_dtype = act_dtype
+        r = self.rank
+        self.offA, self.offB = [], []
+        n = 0
+        for m in self.modules:
+            self.offA.append(n)
+            n += m.d_out * r
+            self.offB.append(n)
+            n += r * m.d_in
+        self.numel = n
+        dev = self.device
+        self.factors = torch.zeros(n, dtype=factor_dtype, device=dev)
+        self.pos = torch.zeros(n, dtype=factor_dtype, device=dev)
+        self.neg = torch.zeros(n, dtype=factor_dtype, device=dev)
+        self.mu = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.var = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.z = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.scratch = torch.zeros(n, dtype=torch.float32, device=dev) if keep_ns_output else None
+        self.offH, self.offV = [], []
+        nh = nv = 0
+        for b in self.bases:
+            self.offH.append(nh)
+            nh += b.T * b.D
+            self.offV.append(nv)
+            nv += b.D * self.basis_width
+        self.H_arena = torch.zeros(max(nh, 1), dtype=act_dtype, device=dev)
+        self.V_arena = torch.zeros(max(nv, 1), dtype=torch.float32, device=dev)
+        self.layout = layout if layout is not None else device_layout(dev)
+        self._build_plan(int(rng_offset_before))
+
+    # ------------------------------------------------------------------ views
+    def A(self, i, t=None):
+        m = self.modules[i]
+        return (self.factors if t is None else t)[self.offA[i]:self.offA[i] + m.d_out * self.rank].view(m.d_out, self.rank)
+
+    def B(self, i, t=None):
+        m = self.modules[i]
+        return (self.factors if t is None else t)[self.offB[i]:self.offB[i] + self.rank * m.d_in].view(self.rank, m.d_in)
+
+    def H(self, b):
+        s = self.bases[b]
+        return self.H_arena[self.offH[b]:self.offH[b] + s.T * s.D].view(s.T, s.D)
+
+    def V(self, b):
+        s = self.bases[b]
+        return self.V_arena[self.offV[b]:self.offV[b] + s.D * self.basis_width].view(s.D, self.basis_width)
+
+    # ------------------------------------------------------------------ plan
+    def _build_plan(self, rng_offset_before: int):
+        L = lib()
+        fdt = _DT[self.factor_dtype]
+        fsz = self.factors.element_size()
+        specs = (ModuleSpec * max(len(self.modules), 1))()
+        for i, m in enumerate(self.modules):
+            s = specs[i]
+            a, b = self.offA[i], self.offB[i]
+            s.A = self.factors.data_ptr() + a * fsz
+            s.B = self.factors.data_ptr() + b * fsz
+            s.pos_A = self.pos.data_ptr() + a * fsz
+            s.pos_B = self.pos.data_ptr() + b * fsz
+            s.neg_A = self.neg.data_ptr() + a * fsz
+            s.neg_B = self.neg.data_ptr() + b * fsz
+            s.mu_A = self.mu.data_ptr() + a * 4
+            s.mu_B = self.mu.data_ptr() + b * 4
+            s.var_A = self.var.data_ptr() + a * 4
+            s.var_B = self.var.data_ptr() + b * 4
+            s.z_A = self.z.data_ptr() + a * 4
+            s.z_B = self.z.data_ptr() + b * 4
+            if self.scratch is not None:
+                s.scratch_A = self.scratch.data_ptr() + a * 4
+                s.scratch_B = self.scratch.data_ptr() + b * 4
+            s.d_out, s.d_in, s.r = m.d_out, m.d_in, self.rank
+            s.ld_A, s.ld_B = self.rank, m.d_in
+            s.basis, s.layer = m.basis, m.layer
+        bspecs = (BasisSpec * max(len(self.bases), 1))()
+        hsz = self.H_arena.element_size()
+        for i, b in enumerate(self.bases):
+            s = bspecs[i]
+            s.H = self.H_arena.data_ptr() + self.offH[i] * hsz
+            s.h_dtype = _DT[self.act_dtype]
+            s.T, s.D, s.ld_H = b.T, b.D, b.D
+            s.V = self.V_arena.data_ptr() + self.offV[i] * 4
+            s.R = self.basis_width
+        desc = PlanDesc()
+        desc.factor_dtype = fdt
+        desc.num_modules = len(self.modules)
+        desc.modules = specs
+        desc.num_bases = len(self.bases)
+        desc.bases = bspecs
+        desc.sm_count, desc.max_threads_per_sm = self.layout
+        desc.rng_offset_before = rng_offset_before
+        handle = ctypes.c_void_p()
+        check(L.dsmz_plan_create(ctypes.byref(desc), ctypes.byref(handle)), "dsmz_plan_create")
+        self._plan = handle
+        self.table = torch.empty(max(int(L.dsmz_plan_table_bytes(handle)), 64), dtype=torch.uint8, device=self.device)
+        self.workspace = torch.empty(int(L.dsmz_plan_workspace_bytes(handle)), dtype=torch.uint8, device=self.device)
+        self.rng_increment = int(L.dsmz_plan_rng_increment(handle))
+        check(L.dsmz_plan_bind(handle, self.table.data_ptr(), self.table.numel(), self.workspace.data_ptr(),
+                               self.workspace.numel(), self._stream()), "dsmz_plan_bind")
+        addr = L.dsmz_step_kalman_sums(handle)
+        off = addr - self.workspace.data_ptr()
+        self._kal = self.workspace[off:off + 16].view(torch.float64)
+
+    def __del__(self):
+        h = getattr(self, "_plan", None)
+        if h is not None and h.value:
+            try:
+                lib().dsmz_plan_destroy(h)
+            except Exception:
+                pass
+            self._plan = None
+
+    def _stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def launch_count(self, num_iters: int) -> int:
+        return int(lib().dsmz_plan_launch_count(self._plan, num_iters))
+
+    # ------------------------------------------------------------------ phases
+    def power_iteration(self, num_iters: int = 3, norm_floor: float = FLT_MIN):
+        check(lib().dsmz_step_power_iteration(self._plan, int(num_iters), float(norm_floor), self._stream()),
+              "power iteration")
+
+    def perturb(self, seed: int, offset: int, eps: float, beta: float, q: float, norm_floor: float = FLT_MIN):
+        check(lib().dsmz_step_perturb(self._plan, int(seed) & (2 ** 64 - 1), int(offset), float(eps), float(beta),
+                                      float(q), float(norm_floor), self._stream()), "perturbation")
+
+    def kalman_sums(self) -> torch.Tensor:
+        """Device view of the rank-local (sum z*mu1, sum z^2*var1); all-reduce it in place."""
+        return self._kal
+
+    def update(self, dd: float, beta: float, q: float, eta: float, norm_floor: float = FLT_MIN,
+               schedule="cubic"):
+        sched = _lib.schedule(schedule)
+        check(lib().dsmz_step_update(self._plan, float(dd), float(beta), float(q), float(eta), float(norm_floor),
+                                     sched, self._stream()), "update")
+
+
+def kalman_beta_q(step_count: int, total_steps: int, eps: float):
+    """ds_mezo/controller.py:255-258."""
+    beta = 1.0 - 1.0 / min(step_count, int(math.sqrt(total_steps)))
+    return beta, eps ** 2 * (1.0 - beta * beta)
+
+
+class ZOController:
+    """Hot path of DSMeZO_Controller (ds_mezo/controller.py:165-292) on an AdapterSet.
+
+    ``perturb()`` = _update_activation_bases + _get_perturbation for every module +
+    fused_perturb_dual (controller.py:236-251), drawing from ``generator`` exactly like
+    the reference's per-module torch.randn calls and advancing it by the same amount.
+    ``update(dd)`` = _update_weights + _step_lr (controller.py:253-292).
+    With a process group the set holds this rank's layers; the two Kalman sums are
+    all-reduced between the phases.
+    """
+
+    def __init__(self, aset: AdapterSet, eps: float, total_steps: int, generator: torch.Generator,
+                 power_iters: int = 3, schedule="cubic", process_group=None, rng_increment_total: Optional[int] = None,
+                 norm_floor: float = FLT_MIN):
+        self.aset = aset
+        self.eps = float(eps)
+        self.total_steps = int(total_steps)
+        self.gen = generator
+        self.power_iters = int(power_iters)
+        self.schedule = schedule
+        self.pg = process_group
+        self.norm_floor = norm_floor
+        self.rng_increment_total = aset.rng_increment if rng_increment_total is None else int(rng_increment_total)
+        self.step_count = 0
+        self.eta_max = self.eps
+        self.eta_min = self.eta_max * FLT_EPS ** (1.0 / 3.0)
+        self.eta = self.eta_max
+        self.beta = 0.0
+        self.q = 0.0
+
+    def _step_lr(self):
+        t = self.step_count
+        self.eta = self.eta_min + 0.5 * (self.eta_max - self.eta_min) * (1.0 + math.cos(math.pi * t / self.total_steps))
+
+    def perturb(self):
+        self.step_count += 1
+        self.beta, self.q = kalman_beta_q(self.step_count, self.total_steps, self.eps)
+        seed = self.gen.initial_seed()
+        off = self.gen.get_offset()
+        self.gen.set_offset(off + self.rng_increment_total)
+        self.aset.power_iteration(self.power_iters, self.norm_floor)
+        self.aset.perturb(seed, off, self.eps, self.beta, self.q, self.norm_floor)
+        if self.pg is not None:
+            import torch.distributed as dist
+            dist.all_reduce(self.aset.kalman_sums(), group=self.pg)
+
+    def update(self, dd: float):
+        self.aset.update(dd, self.beta, self.q, self.eta, self.norm_floor, self.schedule)
+        self._step_lr()

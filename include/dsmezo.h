@@ -1,0 +1,216 @@
+/*
+ * dsmezo.h - C ABI of the B200-native DS-MeZO optimizer hot path (libdsmezo.so).
+ *
+ * Plain pointers, sizes and a cudaStream_t (passed as void*); no torch types. Every
+ * entry point returns DSMZ_OK (0) or an error code, and dsmz_last_error() returns the
+ * message of the last failure on the calling thread. Device memory is never allocated
+ * inside: callers pass device workspaces sized by the *_workspace_bytes queries.
+ * Launches go to the given stream; nothing synchronises the host.
+ *
+ * Two layers:
+ *  1. Per-op drop-ins for the four functions of the reference module ds_mezo/kernels.py
+ *     (same arguments and results as the Python functions cited on each entry point).
+ *  2. The grouped optimizer step: one plan per adapter set (all modules of all layers),
+ *     then one launch sequence per phase for every matrix at once, replacing the
+ *     per-module Python loops of ds_mezo/controller.py:165-176, 236-292.
+ */
+#ifndef DSMEZO_H_
+#define DSMEZO_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSMZ_ABI_VERSION 1
+
+typedef void* dsmz_stream_t; /* cudaStream_t */
+
+enum dsmz_dtype { DSMZ_F32 = 0, DSMZ_BF16 = 1 };
+
+enum dsmz_status {
+  DSMZ_OK = 0,
+  DSMZ_ERR_INVALID = 1,     /* bad argument (shape, stride, alignment, null pointer) */
+  DSMZ_ERR_WORKSPACE = 2,   /* workspace too small */
+  DSMZ_ERR_CUDA = 3,        /* a CUDA launch or copy failed */
+  DSMZ_ERR_UNSUPPORTED = 4  /* size beyond what the kernels support */
+};
+
+#define DSMZ_MAX_RANK 128      /* adapter rank r and basis width R supported by the kernels */
+#define DSMZ_MAX_NS_ITERS 16
+
+/* Last error message of the calling thread ("" when none). */
+const char* dsmz_last_error(void);
+int dsmz_abi_version(void);
+
+/* ---------------------------------------------------------------------------------
+ * Newton-Schulz schedules: iteration k uses S_k = c[k][0] I + c[k][1] G + c[k][2] G^2.
+ * ------------------------------------------------------------------------------- */
+typedef struct dsmz_ns_schedule {
+  int32_t iters;
+  double c[DSMZ_MAX_NS_ITERS][3];
+} dsmz_ns_schedule;
+
+/* The 12-step degree-3 minimax schedule computed at import in ds_mezo/kernels.py:5-24. */
+int dsmz_ns_schedule_cubic(dsmz_ns_schedule* out);
+/* Five quintic steps (3.4445, -4.7750, 2.0315); no counterpart in ds_mezo/kernels.py. */
+int dsmz_ns_schedule_quintic(dsmz_ns_schedule* out);
+
+/* ---------------------------------------------------------------------------------
+ * Per-op drop-ins (ds_mezo/kernels.py).
+ * Strides are in elements. The factor tensor (param/base/pos/neg) is F32 or BF16,
+ * everything else is F32.
+ * ------------------------------------------------------------------------------- */
+
+/* Replaces zo_muon_update (ds_mezo/kernels.py:167-186): scratch <- NS(buf) (the final
+ * orthogonalised matrix X), param <- param - eta * X. M >= N takes the tall form
+ * (G = X^T X), otherwise the wide form (G = X X^T). min(M, N) <= DSMZ_MAX_RANK.
+ * scratch may be NULL (then X is not stored). schedule NULL = cubic. */
+size_t dsmz_zo_muon_update_workspace_bytes(int64_t M, int64_t N);
+int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t param_s0, int64_t param_s1,
+                        const float* buf, int64_t buf_s0, int64_t buf_s1,
+                        float* scratch, int64_t scratch_s0, int64_t scratch_s1,
+                        int64_t M, int64_t N, float eta, float norm_floor,
+                        const dsmz_ns_schedule* schedule,
+                        void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
+/* Replaces fused_power_iter (ds_mezo/kernels.py:249-265): out <- num_iters x
+ * {W = H^T (H V); QR(W)}, the Q factor with positive diagonal R (what the reference's
+ * modified Gram-Schmidt at ds_mezo/kernels.py:227-240 yields). H is T x D (F32 or BF16,
+ * any strides), V is D x R (F32, any strides), out is D x R contiguous F32. */
+size_t dsmz_power_iter_workspace_bytes(int64_t T, int64_t D, int64_t R);
+int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_t h_s0, int64_t h_s1,
+                    const float* V, int64_t R, int64_t v_s0, int64_t v_s1,
+                    float* out, int32_t num_iters, float norm_floor,
+                    void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
+/* Replaces fused_agzo_perturbation (ds_mezo/kernels.py:371-397):
+ * z_B = eps * Zc_B V^T (R x d_in), Q = QR(B V)[:, :min(R,RC)],
+ * z_A = eps * Zc_A Q^T (d_out x R). B: R x d_in (any strides), V: d_in x RC (any strides),
+ * z_coeff_B: R x RC contiguous, z_coeff_A: d_out x min(R,RC) contiguous,
+ * z_A, z_B contiguous outputs. */
+size_t dsmz_agzo_perturbation_workspace_bytes(int64_t R, int64_t d_in, int64_t RC, int64_t d_out);
+int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t b_s0, int64_t b_s1,
+                           const float* V, int64_t RC, int64_t v_s0, int64_t v_s1,
+                           const float* z_coeff_B, const float* z_coeff_A, int64_t d_out,
+                           float* z_A, float* z_B, float eps, float norm_floor,
+                           void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
+/* Replaces fused_perturb_dual (ds_mezo/kernels.py:415-422): pos = base + z,
+ * neg = base - z over n contiguous elements (base/pos/neg in `dtype`, z F32). */
+int dsmz_perturb_dual(int32_t dtype, const void* base, const float* z, void* pos, void* neg,
+                      int64_t n, dsmz_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * torch CUDA generator layout (ATen DistributionTemplates.h calc_execution_policy):
+ * a draw of n normals uses threads = 256 * min(ceil(n/256), sm_count*max_threads_per_sm/256)
+ * and advances the generator offset by ((n-1)/(4*threads)+1)*4.
+ * ------------------------------------------------------------------------------- */
+int64_t dsmz_randn_threads(int64_t n, int32_t sm_count, int32_t max_threads_per_sm);
+uint64_t dsmz_randn_offset_increment(int64_t n, int32_t sm_count, int32_t max_threads_per_sm);
+
+/* Writes n normals exactly as torch.randn(n, generator=g) on a CUDA device with the given
+ * layout would, for a generator at (seed, offset). Used to check the stream bit for bit. */
+int dsmz_randn(float* out, int64_t n, uint64_t seed, uint64_t offset, int32_t sm_count,
+               int32_t max_threads_per_sm, dsmz_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Grouped optimizer step over an adapter set.
+ * A module owns A (d_out x r) and B (r x d_in), each with Kalman mean/variance (F32),
+ * +/- copies (factor dtype), the fp32 perturbation z (the reference's z_A, z_B) and an
+ * optional NS output buffer. All tensors of one side share its row stride and have unit
+ * column stride. Modules must be given in the controller's order (sorted by
+ * (layer, module name), ds_mezo/model_config.py:37): it fixes the random draws.
+ * ------------------------------------------------------------------------------- */
+typedef struct dsmz_module_spec {
+  void* A;  void* B;
+  void* pos_A; void* pos_B; void* neg_A; void* neg_B;
+  float* mu_A; float* mu_B; float* var_A; float* var_B;
+  float* z_A; float* z_B;
+  float* scratch_A; float* scratch_B;   /* may be NULL */
+  int64_t d_out, d_in, r;
+  int64_t ld_A, ld_B;
+  int32_t basis;                        /* index of the module's activation basis */
+  int32_t layer;
+} dsmz_module_spec;
+
+typedef struct dsmz_basis_spec {
+  const void* H; int32_t h_dtype;       /* activation T x D (row stride ld_H, unit column stride) */
+  int64_t T, D, ld_H;
+  float* V; int64_t R;                  /* basis D x R contiguous F32, updated in place */
+} dsmz_basis_spec;
+
+typedef struct dsmz_plan_desc {
+  int32_t factor_dtype;
+  int32_t num_modules;
+  const dsmz_module_spec* modules;
+  int32_t num_bases;
+  const dsmz_basis_spec* bases;
+  int32_t sm_count;                     /* device layout of the torch generator */
+  int32_t max_threads_per_sm;
+  uint64_t rng_offset_before;           /* generator advance of the draws that precede
+                                           these modules (other ranks' modules); 0 on 1 GPU */
+} dsmz_plan_desc;
+
+typedef struct dsmz_plan dsmz_plan;
+
+/* Host-only: validates the specs and builds the launch schedule. All modules share one
+ * adapter rank r and all bases one width R (both <= DSMZ_MAX_RANK). */
+int dsmz_plan_create(const dsmz_plan_desc* desc, dsmz_plan** out);
+void dsmz_plan_destroy(dsmz_plan* plan);
+size_t dsmz_plan_table_bytes(const dsmz_plan* plan);      /* device bytes for the tables */
+size_t dsmz_plan_workspace_bytes(const dsmz_plan* plan);  /* device scratch of the step */
+uint64_t dsmz_plan_rng_increment(const dsmz_plan* plan);  /* generator advance of this plan's draws */
+int32_t dsmz_plan_launch_count(const dsmz_plan* plan, int32_t num_iters);  /* kernels per full step */
+/* Binds device memory for the tables and the workspace and copies the tables there
+ * (one async copy from host memory the plan keeps). Call once before the first step. */
+int dsmz_plan_bind(dsmz_plan* plan, void* device_tables, size_t table_bytes,
+                   void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
+/* Phase 1 (ds_mezo/controller.py:165-176): power iteration of every basis. */
+int dsmz_step_power_iteration(const dsmz_plan* plan, int32_t num_iters, float norm_floor, dsmz_stream_t stream);
+
+/* Phase 2 (ds_mezo/controller.py:178-193, 236-251, 260-270): Gaussian draws regenerated
+ * from the torch Philox stream at (seed, offset), AGZO perturbation z, pos/neg copies,
+ * and the rank-local Kalman sums (sum z*beta*mu, sum z^2*(beta^2 var + q)) as two
+ * doubles at dsmz_step_kalman_sums(). Sum those across ranks before phase 3. */
+int dsmz_step_perturb(const dsmz_plan* plan, uint64_t seed, uint64_t offset, float eps,
+                      float beta, float q, float norm_floor, dsmz_stream_t stream);
+double* dsmz_step_kalman_sums(const dsmz_plan* plan);
+
+/* Phase 3 (ds_mezo/controller.py:272-286): Kalman observation update of mu/var with the
+ * summed scalars, ZO-Muon Newton-Schulz of every updated mu, param -= eta * X.
+ * schedule NULL = cubic. */
+int dsmz_step_update(const dsmz_plan* plan, float dd, float beta, float q, float eta,
+                     float norm_floor, const dsmz_ns_schedule* schedule, dsmz_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Timing probes: while set, every launch of kernel `kernel` by the grouped step records
+ * start[i] / stop[i] (caller-created cudaEvent_t, passed as void*) on the launch stream,
+ * for i = 0 .. capacity-1 in launch order. capacity 0 removes the probe.
+ * ------------------------------------------------------------------------------- */
+enum dsmz_kernel_id {
+  DSMZ_KID_PI_Y = 0,       /* power iteration Y = H V */
+  DSMZ_KID_PI_W = 1,       /* power iteration W = H^T Y */
+  DSMZ_KID_PI_GRAM = 2,    /* Gram of W (CholeskyQR) */
+  DSMZ_KID_PI_CHOL = 3,    /* Cholesky + triangular inverse */
+  DSMZ_KID_PI_APPLY = 4,   /* W R^-1 */
+  DSMZ_KID_BSIDE = 5,      /* B V and var_B V^2 partial sums */
+  DSMZ_KID_COEF = 6,       /* Zc_B draw and QR(B V) per module */
+  DSMZ_KID_PERTURB = 7,    /* z, pos/neg, Kalman partial sums */
+  DSMZ_KID_KALMAN_SUM = 8, /* sum of the Kalman partials */
+  DSMZ_KID_GRAM = 9,       /* Gram of the Kalman-updated momentum */
+  DSMZ_KID_NS_SOLVE = 10,  /* Newton-Schulz in Gram space */
+  DSMZ_KID_APPLY = 11,     /* Kalman update + param -= eta X */
+  DSMZ_NUM_KIDS = 12
+};
+int dsmz_plan_set_probe(dsmz_plan* plan, int32_t kernel, void** start_events, void** stop_events,
+                        int32_t capacity);
+int32_t dsmz_plan_probe_count(const dsmz_plan* plan, int32_t kernel);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSMEZO_H_ */

@@ -1,0 +1,135 @@
+"""The C ABI without a GPU: the library loads, exports every function include/dsmezo.h
+declares, and its host-only entry points (schedules, torch generator layout, plan
+validation and layout) behave. No CUDA calls are made."""
+import ctypes
+import math
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import reference_ops as ref
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def L():
+    from dsmezo_b200 import build
+    build.build()
+    from dsmezo_b200 import _lib
+    return _lib.lib()
+
+
+def declared_functions():
+    text = (ROOT / "include" / "dsmezo.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"\b(dsmz_[a-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_every_declared_symbol_is_exported(L):
+    from dsmezo_b200 import _lib
+    names = declared_functions()
+    assert len(names) >= 25
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must mirror the header"
+
+
+def test_abi_version(L):
+    assert L.dsmz_abi_version() == 1
+
+
+def test_cubic_schedule_matches_reference(L):
+    from dsmezo_b200 import _lib
+    s = _lib.schedule("cubic")
+    want = ref.ns_cubic_schedule()
+    assert s.iters == len(want) == 12
+    for i, (c1, c3, c5) in enumerate(want):
+        assert s.c[i][0] == c1 and s.c[i][1] == c3 and s.c[i][2] == 0.0
+    q = _lib.schedule("quintic")
+    assert q.iters == 5 and tuple(q.c[0]) == (3.4445, -4.7750, 2.0315)
+    with pytest.raises(ValueError):
+        _lib.schedule("septic")
+
+
+def _torch_policy(n, sm, mt):
+    """ATen DistributionTemplates.h calc_execution_policy with unroll 4."""
+    block = 256
+    grid = (n + block - 1) // block
+    grid = min(sm * (mt // block), grid)
+    return ((n - 1) // (block * grid * 4) + 1) * 4, grid * block
+
+
+@pytest.mark.parametrize("n", [1, 2, 255, 256, 257, 303104, 303105, 1212416, 1212417, 10 ** 8])
+@pytest.mark.parametrize("sm,mt", [(148, 2048), (132, 2048), (80, 1024)])
+def test_generator_layout(L, n, sm, mt):
+    inc, thr = _torch_policy(n, sm, mt)
+    assert L.dsmz_randn_threads(n, sm, mt) == thr
+    assert L.dsmz_randn_offset_increment(n, sm, mt) == inc
+    assert L.dsmz_randn_offset_increment(0, sm, mt) == 0
+
+
+def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None):
+    from dsmezo_b200 import _lib, transformer_adapter_shapes
+    mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
+    specs = (_lib.ModuleSpec * len(mods))()
+    fake = 0x10000
+    for i, m in enumerate(mods):
+        s = specs[i]
+        for f in ("A", "B", "pos_A", "pos_B", "neg_A", "neg_B", "mu_A", "mu_B", "var_A", "var_B", "z_A", "z_B"):
+            setattr(s, f, fake)
+        s.d_out, s.d_in, s.r, s.ld_A, s.ld_B, s.basis, s.layer = m.d_out, m.d_in, rank, rank, m.d_in, m.basis, m.layer
+    bs = (_lib.BasisSpec * len(bases))()
+    for i, b in enumerate(bases):
+        bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = fake, 1, b.T, b.D, b.D, fake, rank
+    if bad == "rank":
+        specs[3].r = 200
+    if bad == "basis":
+        specs[0].basis = 99
+    if bad == "null":
+        specs[1].mu_B = None
+    d = _lib.PlanDesc()
+    d.factor_dtype, d.num_modules, d.modules = 1, len(mods), specs
+    d.num_bases, d.bases, d.sm_count, d.max_threads_per_sm = len(bases), bs, 148, 2048
+    return mods, d
+
+
+def test_plan_create_host_only(L):
+    from dsmezo_b200 import draw_increments
+    mods, d = _fake_set()
+    h = ctypes.c_void_p()
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
+    try:
+        assert L.dsmz_plan_table_bytes(h) > 0 and L.dsmz_plan_workspace_bytes(h) > 0
+        assert L.dsmz_plan_rng_increment(h) == sum(draw_increments(mods, 8, 8, 148, 2048))
+        assert L.dsmz_plan_launch_count(h, 3) == 3 * 8 + 7
+        # stepping an unbound plan is an error, not a launch
+        assert L.dsmz_step_update(h, 0.0, 0.0, 0.0, 0.0, 0.0, None, None) == 1
+        assert b"not bound" in L.dsmz_last_error()
+    finally:
+        L.dsmz_plan_destroy(h)
+
+
+@pytest.mark.parametrize("bad,msg", [("rank", b"invalid shape"), ("basis", b"basis index"), ("null", b"null")])
+def test_plan_create_rejects(L, bad, msg):
+    _, d = _fake_set(bad=bad)
+    h = ctypes.c_void_p()
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 1
+    assert msg in L.dsmz_last_error()
+
+
+def test_dropin_argument_errors_without_gpu(L):
+    # size checks happen before any CUDA call
+    rc = L.dsmz_zo_muon_update(0, 0x1000, 300, 1, 0x1000, 300, 1, None, 0, 0, 1000, 300, 0.1, 1e-38, None,
+                               0x1000, 1 << 20, None)
+    assert rc == 4 and b"min(M, N)" in L.dsmz_last_error()
+    rc = L.dsmz_zo_muon_update(0, 0x1000, 8, 1, 0x2000, 1, 8, None, 0, 0, 100, 8, 0.1, 1e-38, None,
+                               0x1000, 1 << 20, None)
+    assert rc == 1 and b"strides" in L.dsmz_last_error()
+    rc = L.dsmz_power_iter(0, 0x1000, 10, 10, 10, 1, 0x1000, 200, 200, 1, 0x1000, 3, 1e-38, 0x1000, 1 << 20, None)
+    assert rc == 4
+    assert L.dsmz_zo_muon_update_workspace_bytes(18944, 64) > 0
+    assert L.dsmz_power_iter_workspace_bytes(4096, 3584, 64) >= 4096 * 64 * 4 + 3584 * 64 * 4
