@@ -52,7 +52,8 @@ __device__ __forceinline__ int64_t vaddr2(const MatD& M, int64_t v, int64_t k) {
 }
 
 // =====================================================================================
-// Gram partials: for each segment of each matrix, G_seg = sum_v x_v x_v^T (r x r, fp64).
+// Gram partials: for each segment of each matrix, G_seg = sum_v x_v x_v^T (r x r), fp64
+// products and sums of the fp32 vectors.
 // SRC 0: x = mu (plain). SRC 1: x = Kalman-updated momentum mu2 (controller.py:283-284).
 // =====================================================================================
 template <int SRC, int RB>
@@ -106,25 +107,22 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
     }
     __syncthreads();
     if (active) {
-      float part[RB][RB];
-#pragma unroll
-      for (int i = 0; i < RB; ++i)
-#pragma unroll
-        for (int j = 0; j < RB; ++j) part[i][j] = 0.f;
+      // fp64 products and sums: the Gram squares the condition number, and the
+      // Newton-Schulz polynomial of an ill-conditioned momentum (a fresh start, where
+      // mu_B ~ Zc_B V^T with a square Gaussian Zc_B) needs its small eigenvalues intact.
       for (int v = grp; v < nv; v += ngroups) {
         const float* row = xs + v * xld;
-        float xa[RB], xb[RB];
+        double xa[RB], xb[RB];
 #pragma unroll
-        for (int i = 0; i < RB; ++i) { xa[i] = row[bi * RB + i]; xb[i] = row[bj * RB + i]; }
+        for (int i = 0; i < RB; ++i) {
+          xa[i] = static_cast<double>(row[bi * RB + i]);
+          xb[i] = static_cast<double>(row[bj * RB + i]);
+        }
 #pragma unroll
         for (int i = 0; i < RB; ++i)
 #pragma unroll
-          for (int j = 0; j < RB; ++j) part[i][j] = fmaf(xa[i], xb[j], part[i][j]);
+          for (int j = 0; j < RB; ++j) acc[i][j] = fma(xa[i], xb[j], acc[i][j]);
       }
-#pragma unroll
-      for (int i = 0; i < RB; ++i)
-#pragma unroll
-        for (int j = 0; j < RB; ++j) acc[i][j] += static_cast<double>(part[i][j]);
     }
     __syncthreads();
   }

@@ -90,14 +90,16 @@ def _poly(G: torch.Tensor, coeffs) -> torch.Tensor:
     return S
 
 
-def ns_orthogonalize(buf: torch.Tensor, norm_floor: float = FLT_MIN, schedule=None) -> torch.Tensor:
+def ns_orthogonalize(buf: torch.Tensor, norm_floor: float = FLT_MIN, schedule=None,
+                     dtype=torch.float32) -> torch.Tensor:
     """X_final of ds_mezo/kernels.py:26-164: Frobenius-normalise, then iterate in X space.
 
     Tall (M >= N, ds_mezo/kernels.py:169) uses G = X^T X and X <- X S; wide uses
-    G = X X^T and X <- S X. All in fp32 without TF32, like ``allow_tf32=False``.
+    G = X X^T and X <- S X. fp32 without TF32 by default, like ``allow_tf32=False``;
+    ``dtype=torch.float64`` gives the same algorithm without its fp32 rounding.
     """
     sched = ns_cubic_schedule() if schedule is None else schedule
-    X = buf.detach().to(torch.float32).clone()
+    X = buf.detach().to(dtype).clone()
     M, N = X.shape
     norm_sq = (X * X).sum()
     inv_norm = 1.0 / torch.sqrt(torch.clamp(norm_sq, min=norm_floor))
@@ -111,17 +113,22 @@ def ns_orthogonalize(buf: torch.Tensor, norm_floor: float = FLT_MIN, schedule=No
 
 
 def zo_muon_update(param, buf, scratch, eta, norm_floor=FLT_MIN, schedule=None):
-    """ds_mezo/kernels.py:167-186: scratch <- NS(buf); param <- param - eta * scratch."""
-    X = ns_orthogonalize(buf, norm_floor, schedule)
+    """ds_mezo/kernels.py:167-186: scratch <- NS(buf); param <- param - eta * scratch.
+
+    Arithmetic runs in buf's dtype (fp32 in the reference; fp64 for the exact variant).
+    """
+    cdt = torch.float64 if buf.dtype == torch.float64 else torch.float32
+    X = ns_orthogonalize(buf, norm_floor, schedule, cdt)
     scratch.copy_(X)
-    step = X * torch.tensor(eta, dtype=torch.float32)   # fp32 eta * orth, as the kernel computes
-    if param.dtype == torch.float32:
+    step = X * torch.tensor(eta, dtype=cdt)   # eta * orth in the compute dtype, as the kernel does
+    if param.dtype == cdt:
         param.sub_(step)
-    else:  # bf16 factors: fp32 arithmetic, one rounding on store
-        param.copy_((param.float() - step).to(param.dtype))
+    else:  # bf16 factors: compute-dtype arithmetic, one rounding on store
+        param.copy_((param.to(cdt) - step).to(param.dtype))
 
 
-def mgs_columns(W: torch.Tensor, norm_floor: float, ncols: Optional[int] = None) -> torch.Tensor:
+def mgs_columns(W: torch.Tensor, norm_floor: float, ncols: Optional[int] = None,
+                dtype=torch.float32) -> torch.Tensor:
     """Modified Gram-Schmidt over the first ``ncols`` columns, in place semantics of
     ds_mezo/kernels.py:227-240 (power iteration) and :328-340 (AGZO).
 
@@ -129,7 +136,7 @@ def mgs_columns(W: torch.Tensor, norm_floor: float, ncols: Optional[int] = None)
     running vector (MGS, not CGS), then divided by sqrt(max(|v|^2, norm_floor)).
     Columns past ``ncols`` are left as they are.
     """
-    Q = W.detach().to(torch.float32).clone()
+    Q = W.detach().to(dtype).clone()
     n = Q.shape[1] if ncols is None else ncols
     for col in range(n):
         v = Q[:, col].clone()
@@ -141,39 +148,40 @@ def mgs_columns(W: torch.Tensor, norm_floor: float, ncols: Optional[int] = None)
     return Q
 
 
-def fused_power_iter(H, V, num_iters, norm_floor=FLT_MIN):
-    """ds_mezo/kernels.py:188-265: num_iters x {W = H^T (H V); V = MGS(W)}; returns D x R fp32."""
-    Hf = H.detach().to(torch.float32)
-    Vk = V.detach().to(torch.float32).clone()
+def fused_power_iter(H, V, num_iters, norm_floor=FLT_MIN, dtype=torch.float32):
+    """ds_mezo/kernels.py:188-265: num_iters x {W = H^T (H V); V = MGS(W)}; returns D x R."""
+    Hf = H.detach().to(dtype)
+    Vk = V.detach().to(dtype).clone()
     for _ in range(num_iters):
         W = Hf.T @ (Hf @ Vk)
-        Vk = mgs_columns(W, norm_floor)
+        Vk = mgs_columns(W, norm_floor, dtype=dtype)
     return Vk.contiguous()
 
 
-def fused_agzo_perturbation(B, V, z_coeff_B, z_coeff_A, eps, norm_floor=FLT_MIN):
+def fused_agzo_perturbation(B, V, z_coeff_B, z_coeff_A, eps, norm_floor=FLT_MIN, dtype=torch.float32):
     """ds_mezo/kernels.py:267-397.
 
     z_B = eps * Zc_B V^T (R x d_in); BV = B V (R x RC); Q = MGS over the first
     RC_A = min(R, RC) columns of BV; z_A = eps * Zc_A Q[:, :RC_A]^T (d_out x R).
     """
     assert z_coeff_B.is_contiguous() and z_coeff_A.is_contiguous()
-    Bf = B.detach().to(torch.float32)
-    Vf = V.detach().to(torch.float32)
+    Bf = B.detach().to(dtype)
+    Vf = V.detach().to(dtype)
     R, _ = Bf.shape
     RC = Vf.shape[1]
     rca = min(R, RC)
-    z_B = (z_coeff_B @ Vf.T) * eps
+    z_B = (z_coeff_B.to(dtype) @ Vf.T) * eps
     BV = Bf @ Vf
-    Q = mgs_columns(BV, norm_floor, rca)
-    z_A = (z_coeff_A @ Q[:, :rca].T) * eps
+    Q = mgs_columns(BV, norm_floor, rca, dtype)
+    z_A = (z_coeff_A.to(dtype) @ Q[:, :rca].T) * eps
     return z_A.contiguous(), z_B.contiguous()
 
 
 def fused_perturb_dual(base, z, pos, neg):
     """ds_mezo/kernels.py:399-422: pos = base + z, neg = base - z (flat, contiguous)."""
-    b = base.reshape(-1).to(torch.float32)
-    zz = z.reshape(-1).to(torch.float32)
+    cdt = torch.float64 if (base.dtype == torch.float64 or z.dtype == torch.float64) else torch.float32
+    b = base.reshape(-1).to(cdt)
+    zz = z.reshape(-1).to(cdt)
     pos.view(-1).copy_((b + zz).to(pos.dtype))
     neg.view(-1).copy_((b - zz).to(neg.dtype))
 
@@ -223,15 +231,15 @@ def kalman_beta_q(step_count: int, total_steps: int, eps: float) -> Tuple[float,
     return beta, q
 
 
-def get_perturbation(A, B, V, var_B, randn_B, randn_A, eps, norm_floor=FLT_MIN):
+def get_perturbation(A, B, V, var_B, randn_B, randn_A, eps, norm_floor=FLT_MIN, dtype=torch.float32):
     """ds_mezo/controller.py:178-193 with the two Gaussian draws injected.
 
     randn_B: R x RC standard normals (first draw), randn_A: d_out x min(R, RC) (second draw).
     """
-    var_B_proj = var_B.float() @ (V.float() ** 2)
-    z_coeff_B = randn_B.float() * torch.sqrt(var_B_proj)
-    z_coeff_A = randn_A.float().contiguous()
-    return fused_agzo_perturbation(B, V, z_coeff_B.contiguous(), z_coeff_A, eps, norm_floor)
+    var_B_proj = var_B.to(dtype) @ (V.to(dtype) ** 2)
+    z_coeff_B = randn_B.to(dtype) * torch.sqrt(var_B_proj)
+    z_coeff_A = randn_A.to(dtype).contiguous()
+    return fused_agzo_perturbation(B, V, z_coeff_B.contiguous(), z_coeff_A, eps, norm_floor, dtype)
 
 
 def shrinkage_rloo(rewards: Sequence[float], reward_ema: float, momentum: float,
@@ -275,8 +283,9 @@ def kalman_update(mats: Sequence[Matrix], zs: Sequence[torch.Tensor], dd: float,
     ``mats`` and ``zs`` run in the controller's order: for each module (layer, name), A then B.
     Returns (y_hat, s_sum) as fp32 0-d tensors for inspection.
     """
-    y_hat = torch.zeros((), dtype=torch.float32)
-    s_sum = torch.zeros((), dtype=torch.float32)
+    cdt = mats[0].mu.dtype if mats else torch.float32
+    y_hat = torch.zeros((), dtype=cdt)
+    s_sum = torch.zeros((), dtype=cdt)
     for m, z in zip(mats, zs):
         m.mu.mul_(beta)
         m.var.mul_(beta * beta).add_(q)
@@ -319,7 +328,7 @@ class Module:
             p = getattr(self, k)
             for pre in ("scratch_", "pos_", "neg_"):
                 if getattr(self, pre + k) is None:
-                    setattr(self, pre + k, torch.zeros_like(p, dtype=torch.float32 if pre == "scratch_" else p.dtype))
+                    setattr(self, pre + k, torch.zeros_like(p, dtype=self.mu_A.dtype if pre == "scratch_" else p.dtype))
 
 
 @dataclass
@@ -333,6 +342,7 @@ class StepState:
     eta_min: float = 0.0
     eta: float = 0.0
     schedule: tuple = field(default_factory=ns_cubic_schedule)
+    dtype: torch.dtype = torch.float32     # float64: the same algorithm without fp32 rounding
 
     def __post_init__(self):
         if self.eta_max == 0.0:
@@ -359,12 +369,12 @@ def perturb_phase(st: StepState, activations: Sequence[torch.Tensor], draws: Seq
 
     ``draws`` holds the Gaussian draws in ``draw_shapes`` order. Returns [(z_A, z_B)].
     """
-    st.bases = [fused_power_iter(H, V, num_iters, norm_floor) for H, V in zip(activations, st.bases)]
+    st.bases = [fused_power_iter(H, V, num_iters, norm_floor, st.dtype) for H, V in zip(activations, st.bases)]
     perts = []
     for i, m in enumerate(st.modules):
         V = st.bases[m.basis]
-        z_A, z_B = get_perturbation(m.A.float(), m.B.float(), V, m.var_B, draws[2 * i], draws[2 * i + 1],
-                                    st.eps, norm_floor)
+        z_A, z_B = get_perturbation(m.A, m.B, V, m.var_B, draws[2 * i], draws[2 * i + 1],
+                                    st.eps, norm_floor, st.dtype)
         perts.append((z_A, z_B))
     for m, (z_A, z_B) in zip(st.modules, perts):
         fused_perturb_dual(m.A, z_A, m.pos_A, m.neg_A)

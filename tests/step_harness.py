@@ -44,19 +44,21 @@ def cuda_draws(mods, rank, basis_width, seed, offset, device):
     return out, gen.get_offset()
 
 
-def oracle_state(mods, A, B, V0, eps, total_steps, mu=None, var=None, schedule=None):
+def oracle_state(mods, A, B, V0, eps, total_steps, mu=None, var=None, schedule=None, dtype=torch.float32):
+    """Oracle step state; dtype float32 follows the reference's rounding, float64 gives the
+    same algorithm without it (the exact value the reference approximates)."""
     modules = []
     for i, m in enumerate(mods):
-        a = A[i].float().clone()
-        b = B[i].float().clone()
+        a = A[i].to(dtype).clone()
+        b = B[i].to(dtype).clone()
         modules.append(ref.Module(m.layer, m.name, a, b,
-                                  torch.zeros_like(a) if mu is None else mu[i][0].clone(),
-                                  torch.zeros_like(b) if mu is None else mu[i][1].clone(),
-                                  torch.full_like(a, eps ** 2) if var is None else var[i][0].clone(),
-                                  torch.full_like(b, eps ** 2) if var is None else var[i][1].clone(),
+                                  torch.zeros_like(a) if mu is None else mu[i][0].to(dtype).clone(),
+                                  torch.zeros_like(b) if mu is None else mu[i][1].to(dtype).clone(),
+                                  torch.full_like(a, eps ** 2) if var is None else var[i][0].to(dtype).clone(),
+                                  torch.full_like(b, eps ** 2) if var is None else var[i][1].to(dtype).clone(),
                                   basis=m.basis))
-    st = ref.StepState(modules, [v.clone() for v in V0], eps=eps, total_steps=total_steps,
-                       schedule=ref.ns_cubic_schedule() if schedule is None else schedule)
+    st = ref.StepState(modules, [v.to(dtype).clone() for v in V0], eps=eps, total_steps=total_steps,
+                       schedule=ref.ns_cubic_schedule() if schedule is None else schedule, dtype=dtype)
     return st
 
 

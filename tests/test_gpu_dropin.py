@@ -36,7 +36,8 @@ def test_zo_muon_golden(K, kern, name):
     K.zo_muon_update(param, c["buf"].to(DEV), scratch, c["eta"], FLOOR)
     torch.cuda.synchronize()
     assert rel(scratch, c["scratch_out"]) < 1e-5
-    assert rel(param.cpu() - c["param_in"], c["param_out"] - c["param_in"]) < 1e-5
+    # param is ~1 and the step ~1e-4, so compare values (ulp level), not differences
+    assert rel(param, c["param_out"]) < 1e-6
 
 
 @pytest.mark.parametrize("M,N", [(3584, 64), (64, 3584), (512, 64), (64, 64), (300, 5), (12, 700), (2048, 128),
@@ -51,7 +52,7 @@ def test_zo_muon_shapes(K, M, N, sched):
     X = ref.ns_orthogonalize(buf.double(), FLOOR, ref.get_schedule(sched)).double()  # fp64 X-space truth
     torch.cuda.synchronize()
     assert rel(s_d, X) < 1e-5
-    assert rel(p_d.cpu() - param, -0.01 * X) < 1e-5
+    assert rel(p_d, param.double() - 0.01 * X) < 1e-6
 
 
 def test_zo_muon_strided_and_bf16(K):
@@ -123,7 +124,8 @@ def test_agzo_strided_and_contiguity(K):
     zcB = torch.randn(R, RC, generator=g)
     zcA = torch.randn(d_out, RC, generator=g)
     z_A, z_B = K.fused_agzo_perturbation(B.to(DEV), V.to(DEV), zcB.to(DEV), zcA.to(DEV), 1e-3, FLOOR)
-    wA, wB = ref.fused_agzo_perturbation(B.contiguous(), V, zcB, zcA, 1e-3, FLOOR)
+    # square 64 x 64 B V: compare with the exact (fp64) algorithm; fp32 MGS carries ~1e-7*cond noise
+    wA, wB = ref.fused_agzo_perturbation(B.contiguous(), V, zcB, zcA, 1e-3, FLOOR, dtype=torch.float64)
     torch.cuda.synchronize()
     assert rel(z_B, wB) < 1e-5 and rel(z_A, wA) < 1e-5
     with pytest.raises(AssertionError):
