@@ -1,6 +1,7 @@
 // C ABI of libdsmezo: plans, launch sequences and the per-op drop-ins declared in dsmezo.h.
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -782,6 +783,46 @@ int dsmz_perturb_dual(int32_t dtype, const void* base, const float* z, void* pos
   k_dual<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(base, z, pos, neg, n, dtype);
   DSMZ_LAUNCHED("perturb_dual");
   return DSMZ_OK;
+}
+
+// ---------------------------------------------------------------------- allocation-free ZO-Muon
+// Scratch of dsmz_zo_muon_update_noalloc: a fixed array in this library, held by every GPU
+// that loads it until the process exits. Host code must not use the symbol's host-side
+// address; the device address is looked up once per device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DSMZ_NOALLOC_SCRATCH_BYTES];
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_addr[256];
+
+int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t ps0, int64_t ps1, const float* buf,
+                                int64_t bs0, int64_t bs1, float* scratch, int64_t ss0, int64_t ss1, int64_t M,
+                                int64_t N, float eta, float norm_floor, const dsmz_ns_schedule* schedule,
+                                dsmz_stream_t stream) {
+  if (M <= 0 || N <= 0) return DSMZ_OK;
+  const size_t need = dsmz_zo_muon_update_workspace_bytes(M, N);
+  if (need > DSMZ_NOALLOC_SCRATCH_BYTES)
+    return fail(DSMZ_ERR_UNSUPPORTED, "zo_muon_update_noalloc: a " + std::to_string(M) + " x " + std::to_string(N) +
+                                          " update needs " + std::to_string(need) + " scratch bytes, above the " +
+                                          std::to_string(DSMZ_NOALLOC_SCRATCH_BYTES) +
+                                          " built in; use dsmz_zo_muon_update with a workspace");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("zo_muon_update_noalloc: cudaGetDevice", e);
+  if (dev < 0 || dev >= 256) return fail(DSMZ_ERR_UNSUPPORTED, "zo_muon_update_noalloc: device index above 255");
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // once per device, that device current
+      if (e != cudaSuccess) return cuda_fail("zo_muon_update_noalloc: cudaGetSymbolAddress", e);
+      g_noalloc_addr[dev] = p;
+    }
+    ws = g_noalloc_addr[dev];
+  }
+  // Every slot the kernels read (tables, Gram partials, solve workspace, apply matrix) is
+  // written earlier in the same call, so nothing has to be cleared between calls.
+  return dsmz_zo_muon_update(param_dtype, param, ps0, ps1, buf, bs0, bs1, scratch, ss0, ss1, M, N, eta, norm_floor,
+                             schedule, ws, DSMZ_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int dsmz_plan_set_probe(dsmz_plan* P, int32_t kernel, void** start_events, void** stop_events, int32_t capacity) {

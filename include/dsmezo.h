@@ -76,6 +76,23 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t param_s0, int6
                         const dsmz_ns_schedule* schedule,
                         void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
 
+/* No counterpart in the reference. The same update as dsmz_zo_muon_update for callers that
+ * cannot allocate device memory when they update an adapter: a process whose rollout engine
+ * has reserved nearly all of HBM up front (the vLLM engine DS-MeZO drives is created with
+ * gpu_memory_utilization=0.95), or a plain C host without a device allocator of its own.
+ * Its scratch is a fixed DSMZ_NOALLOC_SCRATCH_BYTES array inside the library (every GPU
+ * that loads the library keeps it until exit); no cudaMalloc/cudaFree or allocating
+ * library call happens. Sizes whose workspace (dsmz_zo_muon_update_workspace_bytes) exceeds
+ * the array return DSMZ_ERR_UNSUPPORTED. The first call on a device looks up the array's
+ * device address, so make that first call before any stream capture. All calls share the
+ * array: calls that overlap on the GPU (other streams, other host threads) race. */
+#define DSMZ_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
+int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t param_s0, int64_t param_s1,
+                                const float* buf, int64_t buf_s0, int64_t buf_s1,
+                                float* scratch, int64_t scratch_s0, int64_t scratch_s1,
+                                int64_t M, int64_t N, float eta, float norm_floor,
+                                const dsmz_ns_schedule* schedule, dsmz_stream_t stream);
+
 /* Replaces fused_power_iter (ds_mezo/kernels.py:249-265): out <- num_iters x
  * {W = H^T (H V); QR(W)}, the Q factor with positive diagonal R (what the reference's
  * modified Gram-Schmidt at ds_mezo/kernels.py:227-240 yields). H is T x D (F32 or BF16,
