@@ -149,8 +149,9 @@ def alg_bytes(aset, cfg):
     return {
         "pi_y": hb + vr + yr,                      # read H, V; write Y
         "pi_w": hb + yr + vr,                      # read H, Y; write W
-        "pi_gram": vr,                             # read W
-        "pi_apply": 2 * vr,                        # read W, write W or V
+        "pi_gram": 2 * vr,                         # read W, write Q1 in place (QR round 2)
+        "pi_apply": 2 * vr,                        # read Q1, write V
+        "pi_split": 2 * vr,                        # read V, write bf16 [V_hi | V_lo]^T
         "bside": nB * (f + 4),                     # read B, var_B
         "perturb": N * (3 * f + 12),               # read p, mu, var; write pos, neg, z
         "gram": N * 12,                            # read mu, var, z
@@ -204,8 +205,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        cfg["layers"] = args.layers
+        cfg["workload"] += f" [first {args.layers} layers only]"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -268,8 +273,8 @@ def main():
     torch.cuda.synchronize()
 
     # per-kernel probes over the timed region
-    per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 6, "bside": 1, "coef": 1,
-                "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
+    per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 3, "pi_split": 3, "bside": 1,
+                "coef": 1, "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
     probes = {}
     for name, n in per_step.items():
         cap = n * args.steps

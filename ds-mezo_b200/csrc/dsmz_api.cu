@@ -5,7 +5,10 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "dsmz_kernels.cuh"
+#include "dsmz_tc.cuh"
 
 using namespace dsmz;
 
@@ -48,26 +51,29 @@ int seg_vectors(int r) {
 
 int gram_rb(int r) { return r <= 64 ? 4 : 8; }
 
-size_t gram_smem(int r) {
+size_t gram_smem(int r, bool round2 = false) {
   const int RB = gram_rb(r);
   const int tpr = (r + RB - 1) / RB;
   const int rp = tpr * RB;
   const int ngroups = kThreads / (tpr * tpr);
-  const size_t xs = static_cast<size_t>(tile_vectors(r)) * (rp + 1) * sizeof(float);
+  const size_t tv = static_cast<size_t>(tile_vectors(r));
+  const size_t xs = tv * (rp + 4) * sizeof(float) +
+                    (round2 ? (static_cast<size_t>(r) * pad8(r) + tv * (pad8(r) + 1)) * sizeof(float) : 0);
   const size_t red = ngroups > 1 ? static_cast<size_t>(ngroups) * rp * rp * sizeof(double) : 0;
   return xs > red ? xs : red;
 }
 size_t apply_smem(int r) {
-  const int rp = pad4(r);
-  return (static_cast<size_t>(r) * rp + static_cast<size_t>(tile_vectors(r)) * (rp + 1)) * sizeof(float);
+  const int r8 = pad8(r);
+  return (static_cast<size_t>(r) * r8 + 2 * static_cast<size_t>(tile_vectors(r)) * (r8 + 1)) * sizeof(float);
 }
 size_t perturb_smem(int r, int R, int RC) {
   const int KW = RC;  // side B width; side A uses RCA <= RC
   const int TV = tile_vectors(r);
-  return (static_cast<size_t>(KW) * R + static_cast<size_t>(TV) * (KW + 1) + static_cast<size_t>(TV) * (r + 1)) *
+  return (static_cast<size_t>(KW) * pad8(R) + static_cast<size_t>(TV) * (KW + 1) + static_cast<size_t>(TV) * (r + 1)) *
          sizeof(float);
 }
 size_t coef_smem(int R, int RC) { return static_cast<size_t>(R) * RC * sizeof(double); }
+size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
 template <typename K>
 int set_smem(K kernel, size_t bytes) {
@@ -113,6 +119,59 @@ NSArgs make_ns(const dsmz_ns_schedule* s, float floor_) {
   return a;
 }
 
+// ------------------------------------------------------------------ tensor-core power iteration
+// cuTensorMapEncodeTiled from the driver, looked up once per process.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map (inner dimension contiguous), 128-byte swizzle, zero fill outside.
+bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R).
+bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
+  return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
+         (reinterpret_cast<uintptr_t>(H) & 15) == 0;
+}
+
+// Ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
+int tc_stages(int R) {
+  const int sb = tc::stage_bytes(R);
+  const int half = (227 * 1024) / 2 - 2048;
+  const int two = half / sb;
+  if (two >= 3) return two > 6 ? 6 : two;
+  const int one = (227 * 1024 - 2048) / sb;
+  return one > 4 ? 4 : one;
+}
+size_t tc_smem(int R) { return static_cast<size_t>(tc_stages(R)) * tc::stage_bytes(R) + 1024 + 512; }
+
+struct TCSlots {             // workspace byte offsets of one basis
+  size_t v2t = 0, y2t = 0;
+  int64_t ldv2 = 0, ldy2 = 0;
+};
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
 }  // namespace
 
 // ====================================================================== plan
@@ -125,11 +184,17 @@ struct dsmz_plan {
   std::vector<unsigned char> blob;  // host copy of the tables
   char* dev_tables = nullptr;
   char* workspace = nullptr;
-  int nsegs = 0, nwsegs = 0, nchunks = 0, nytiles = 0, nwtiles = 0;
+  int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0;
   int factor_dtype = DSMZ_F32;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
   uint64_t rng_increment = 0;
+  // tensor-core power iteration
+  bool tc = false;
+  std::vector<tc::TCBasis> tcb;
+  std::vector<TCSlots> tcs;
+  size_t off_tcb = 0, err_off = 0;
+  int ntc_y = 0, ntc_w = 0, ntc_vt = 0;
   struct Probe {
     std::vector<cudaEvent_t> start, stop;
     int count = 0;
@@ -157,9 +222,10 @@ struct dsmz_plan {
     t.nbases = static_cast<int32_t>(bases.size());
     t.nytiles = nytiles;
     t.nwtiles = nwtiles;
-    t.wmats1 = reinterpret_cast<const MatD*>(dev_tables + off_w1);
-    t.wmats2 = reinterpret_cast<const MatD*>(dev_tables + off_w2);
-    t.nwsegs = nwsegs;
+    t.wA = reinterpret_cast<const MatD*>(dev_tables + off_w1);
+    t.wB = reinterpret_cast<const MatD*>(dev_tables + off_w2);
+    t.nwsegsA = nwsegsA;
+    t.nwsegsB = nwsegsB;
     t.factor_dtype = factor_dtype;
     t.ws = workspace;
     t.seg_kal_off = seg_kal_off;
@@ -175,6 +241,7 @@ struct dsmz_plan {
     off_w2 = T.take(w2.size() * sizeof(MatD), 64);
     off_mods = T.take(mods.size() * sizeof(ModD), 64);
     off_bases = T.take(bases.size() * sizeof(BasisD), 64);
+    off_tcb = T.take(tcb.size() * sizeof(tc::TCBasis), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -184,6 +251,7 @@ struct dsmz_plan {
     if (!w2.empty()) std::memcpy(blob.data() + off_w2, w2.data(), w2.size() * sizeof(MatD));
     if (!mods.empty()) std::memcpy(blob.data() + off_mods, mods.data(), mods.size() * sizeof(ModD));
     if (!bases.empty()) std::memcpy(blob.data() + off_bases, bases.data(), bases.size() * sizeof(BasisD));
+    if (!tcb.empty()) std::memcpy(blob.data() + off_tcb, tcb.data(), tcb.size() * sizeof(tc::TCBasis));
   }
 };
 
@@ -197,9 +265,80 @@ void patch_ws_pointers(dsmz_plan* P) {
     float* W = reinterpret_cast<float*>(P->workspace) + b.w_off;
     P->w1[i].mu = W;
     P->w1[i].param = W;
-    P->w2[i].mu = W;
+    P->w2[i].mu = W;          // round 2 overwrites W with Q1 before the apply reads it
     P->w2[i].param = b.Vout;
   }
+}
+
+// CholeskyQR2 tables of every basis W (D x R): round 1 (Gram of W, R1^-1) and round 2
+// (Q1 = W R1^-1 in place, its Gram, R2^-1, V = Q1 R2^-1). Round-1 segments are 128 rows
+// when the tensor-core W kernel writes their Gram partials.
+void add_w_tables(dsmz_plan* P, bool tc_segments) {
+  for (size_t i = 0; i < P->bases.size(); ++i) {
+    const BasisD& b = P->bases[i];
+    const size_t rr = static_cast<size_t>(b.R) * b.R;
+    MatD a{};
+    a.nvec = b.D; a.r = b.R; a.ld = b.R; a.cs = 1; a.side = 0; a.owner = static_cast<int32_t>(i);
+    a.segv = tc_segments ? tc::kBM : seg_vectors(b.R);
+    a.nseg = static_cast<int32_t>((b.D + a.segv - 1) / a.segv);
+    a.seg0 = P->nwsegsA;
+    P->nwsegsA += a.nseg;
+    a.gram_off = static_cast<int64_t>(P->ws.take(a.nseg * rr * sizeof(double)) / sizeof(double));
+    a.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
+    a.dw_off = static_cast<int64_t>(P->ws.take(3 * rr * sizeof(double)) / sizeof(double));
+    MatD m = a;
+    m.segv = seg_vectors(b.R);
+    m.nseg = static_cast<int32_t>((b.D + m.segv - 1) / m.segv);
+    m.seg0 = P->nwsegsB;
+    P->nwsegsB += m.nseg;
+    m.gram_off = static_cast<int64_t>(P->ws.take(m.nseg * rr * sizeof(double)) / sizeof(double));
+    m.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
+    m.p_prev_off = a.p_off;
+    P->w1.push_back(a);
+    P->w2.push_back(m);
+  }
+}
+
+// Reserves the tensor-core slots of every basis (host only, no CUDA calls).
+void plan_tc_layout(dsmz_plan* P) {
+  P->tcb.assign(P->bases.size(), tc::TCBasis{});
+  P->tcs.assign(P->bases.size(), TCSlots{});
+  for (size_t i = 0; i < P->bases.size(); ++i) {
+    const BasisD& b = P->bases[i];
+    TCSlots& t = P->tcs[i];
+    t.ldv2 = round_up(b.D, 64);
+    t.ldy2 = round_up(b.T, 64);
+    t.v2t = P->ws.take(static_cast<size_t>(2 * b.R) * t.ldv2 * 2, 1024);
+    t.y2t = P->ws.take(static_cast<size_t>(2 * b.R) * t.ldy2 * 2, 1024);
+    tc::TCBasis& c = P->tcb[i];
+    c.T = b.T; c.D = b.D; c.R = b.R; c.ldv2 = t.ldv2; c.ldy2 = t.ldy2;
+    c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + tc::kBM - 1) / tc::kBM); P->ntc_y += c.nytile;
+    c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + tc::kBM - 1) / tc::kBM); P->ntc_w += c.nwtile;
+    c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D * b.R + kThreads * 8 - 1) / (kThreads * 8)); P->ntc_vt += c.nvt;
+  }
+  P->err_off = P->ws.take(256);
+}
+
+// Fills pointers and tensor maps once the workspace is known; false if the driver refuses
+// a tensor map (the plan then keeps the CUDA-core path).
+bool bind_tc(dsmz_plan* P) {
+  for (size_t i = 0; i < P->bases.size(); ++i) {
+    const BasisD& b = P->bases[i];
+    const TCSlots& t = P->tcs[i];
+    tc::TCBasis& c = P->tcb[i];
+    c.V2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.v2t);
+    c.Y2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.y2t);
+    c.W = reinterpret_cast<float*>(P->workspace) + b.w_off;
+    c.g1 = reinterpret_cast<double*>(P->workspace) + P->w1[i].gram_off;
+    c.Vsrc = b.Vin; c.v_s0 = b.v_s0; c.v_s1 = b.v_s1; c.Vout = b.Vout;
+    const uint32_t n2 = static_cast<uint32_t>(2 * b.R);
+    if (!encode_bf16_2d(&c.mapHy, b.H, b.D, b.T, b.h_s0 * 2, 64, 128) ||
+        !encode_bf16_2d(&c.mapHw, b.H, b.D, b.T, b.h_s0 * 2, 64, 64) ||
+        !encode_bf16_2d(&c.mapV2, c.V2T, b.D, n2, t.ldv2 * 2, 64, n2) ||
+        !encode_bf16_2d(&c.mapY2, c.Y2T, b.T, n2, t.ldy2 * 2, 64, n2))
+      return false;
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- launch sequences
@@ -207,14 +346,41 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   if (P->bases.empty() || iters <= 0) return 0;
   const Tables tb = P->tables();
   const int R = P->R;
-  const size_t gs = gram_smem(R), as = apply_smem(R);
+  const size_t gs = gram_smem(R), gs2 = gram_smem(R, true), as = apply_smem(R);
   int rc;
-  if (gram_rb(R) == 4) { if ((rc = set_smem(k_gram<0, 4>, gs))) return rc; }
-  else { if ((rc = set_smem(k_gram<0, 8>, gs))) return rc; }
+  if (gram_rb(R) == 4) {
+    if ((rc = set_smem(k_gram<0, 4, double>, gs))) return rc;
+    if ((rc = set_smem(k_gram<2, 4, float>, gs2))) return rc;
+  } else {
+    if ((rc = set_smem(k_gram<0, 8, double>, gs))) return rc;
+    if ((rc = set_smem(k_gram<2, 8, float>, gs2))) return rc;
+  }
   if ((rc = set_smem(k_apply<0, 1>, as))) return rc;
+  if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
   const KalmanIn kin{};
   const int nb = static_cast<int>(P->bases.size());
+  const tc::TCBasis* dtcb = reinterpret_cast<const tc::TCBasis*>(P->dev_tables + P->off_tcb);
+  int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
+  const size_t tsm = P->tc ? tc_smem(R) : 0;
+  if (P->tc) {
+    if ((rc = set_smem(tc::k_pi_tc<0>, tsm))) return rc;
+    if ((rc = set_smem(tc::k_pi_tc<1>, tsm))) return rc;
+    P->probe_begin(DSMZ_KID_PI_SPLIT, s);
+    tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
+    P->probe_end(DSMZ_KID_PI_SPLIT, s);
+    DSMZ_LAUNCHED("power iteration basis split");
+  }
   for (int it = 0; it < iters; ++it) {
+    if (P->tc) {
+      P->probe_begin(DSMZ_KID_PI_Y, s);
+      tc::k_pi_tc<0><<<P->ntc_y, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
+      P->probe_end(DSMZ_KID_PI_Y, s);
+      DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
+      P->probe_begin(DSMZ_KID_PI_W, s);
+      tc::k_pi_tc<1><<<P->ntc_w, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
+      P->probe_end(DSMZ_KID_PI_W, s);
+      DSMZ_LAUNCHED("power iteration W = H^T Y (tcgen05)");
+    } else {
     P->probe_begin(DSMZ_KID_PI_Y, s);
     k_pi_gemm<0><<<P->nytiles, kThreads, 0, s>>>(tb, it == 0 ? 1 : 0);
     P->probe_end(DSMZ_KID_PI_Y, s);
@@ -223,21 +389,41 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     k_pi_gemm<1><<<P->nwtiles, kThreads, 0, s>>>(tb, 0);
     P->probe_end(DSMZ_KID_PI_W, s);
     DSMZ_LAUNCHED("power iteration W = H^T Y");
-    for (int round = 0; round < 2; ++round) {
-      const MatD* wm = round == 0 ? tb.wmats1 : tb.wmats2;
+    }
+    // CholeskyQR2 of W: round 1 from the fp64 Gram of W (written by the tensor-core W kernel,
+    // or by k_gram here), round 2 from the fp32 Gram of the rounded Q1 = W R1^-1.
+    if (!P->tc) {
       P->probe_begin(DSMZ_KID_PI_GRAM, s);
-      if (gram_rb(R) == 4) k_gram<0, 4><<<P->nwsegs, kThreads, gs, s>>>(tb, tb.wmats1, nb, kin);
-      else k_gram<0, 8><<<P->nwsegs, kThreads, gs, s>>>(tb, tb.wmats1, nb, kin);
+      if (gram_rb(R) == 4) k_gram<0, 4, double><<<P->nwsegsA, kThreads, gs, s>>>(tb, tb.wA, nb, kin);
+      else k_gram<0, 8, double><<<P->nwsegsA, kThreads, gs, s>>>(tb, tb.wA, nb, kin);
       P->probe_end(DSMZ_KID_PI_GRAM, s);
-      DSMZ_LAUNCHED("power iteration Gram");
-      P->probe_begin(DSMZ_KID_PI_CHOL, s);
-      k_chol<<<nb, kThreads, 0, s>>>(tb, tb.wmats1, floor_);
-      P->probe_end(DSMZ_KID_PI_CHOL, s);
-      DSMZ_LAUNCHED("power iteration Cholesky");
-      P->probe_begin(DSMZ_KID_PI_APPLY, s);
-      k_apply<0, 1><<<P->nwsegs, kThreads, as, s>>>(tb, wm, nb, kin, 0.f, DSMZ_F32);
-      P->probe_end(DSMZ_KID_PI_APPLY, s);
-      DSMZ_LAUNCHED("power iteration apply");
+      DSMZ_LAUNCHED("power iteration Gram of W");
+    }
+    const int bpm = (R * R + kThreads - 1) / kThreads;
+    P->probe_begin(DSMZ_KID_PI_CHOL, s);
+    k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wA, nb, bpm);
+    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_);
+    P->probe_end(DSMZ_KID_PI_CHOL, s);
+    DSMZ_LAUNCHED("power iteration Cholesky 1");
+    P->probe_begin(DSMZ_KID_PI_GRAM, s);
+    if (gram_rb(R) == 4) k_gram<2, 4, float><<<P->nwsegsB, kThreads, gs2, s>>>(tb, tb.wB, nb, kin);
+    else k_gram<2, 8, float><<<P->nwsegsB, kThreads, gs2, s>>>(tb, tb.wB, nb, kin);
+    P->probe_end(DSMZ_KID_PI_GRAM, s);
+    DSMZ_LAUNCHED("power iteration Q1 and its Gram");
+    P->probe_begin(DSMZ_KID_PI_CHOL, s);
+    k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wB, nb, bpm);
+    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wB, floor_);
+    P->probe_end(DSMZ_KID_PI_CHOL, s);
+    DSMZ_LAUNCHED("power iteration Cholesky 2");
+    P->probe_begin(DSMZ_KID_PI_APPLY, s);
+    k_apply<0, 1><<<P->nwsegsB, kThreads, as, s>>>(tb, tb.wB, nb, kin, 0.f, DSMZ_F32);
+    P->probe_end(DSMZ_KID_PI_APPLY, s);
+    DSMZ_LAUNCHED("power iteration V = Q1 R2^-1");
+    if (P->tc && it + 1 < iters) {
+      P->probe_begin(DSMZ_KID_PI_SPLIT, s);
+      tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 0);
+      P->probe_end(DSMZ_KID_PI_SPLIT, s);
+      DSMZ_LAUNCHED("power iteration basis split");
     }
   }
   return 0;
@@ -287,12 +473,12 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   const int nm = static_cast<int>(P->mats.size());
   const size_t gs = gram_smem(r), as = apply_smem(r);
   int rc;
-  if ((rc = set_smem(k_gram<1, 4>, gs))) return rc;
-  if ((rc = set_smem(k_gram<1, 8>, gs))) return rc;
+  if ((rc = set_smem(k_gram<1, 4, double>, gs))) return rc;
+  if ((rc = set_smem(k_gram<1, 8, double>, gs))) return rc;
   if ((rc = set_smem(k_apply<1, 0>, as))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (gram_rb(r) == 4) k_gram<1, 4><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
-  else k_gram<1, 8><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
+  if (gram_rb(r) == 4) k_gram<1, 4, double><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
+  else k_gram<1, 8, double><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
@@ -409,13 +595,19 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     bd.w_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(b.D) * b.R * sizeof(float)) / sizeof(float));
     fill_basis_tiles(bd, P->nytiles, P->nwtiles);
     P->bases.push_back(bd);
-    MatD w{};
-    w.nvec = b.D; w.r = b.R; w.ld = b.R; w.cs = 1; w.side = 0; w.owner = i;
-    add_matrix(P->w1, P->ws, w, P->nwsegs, false);
-    MatD& w1 = P->w1.back();
-    w1.dw_off = static_cast<int64_t>(P->ws.take(3 * static_cast<size_t>(b.R) * b.R * sizeof(double)) / sizeof(double));
-    P->w2.push_back(w1);
   }
+  if (!P->bases.empty() && !(d->flags & DSMZ_PLAN_SIMT_POWER_ITER)) {
+    bool ok = true;
+    for (int i = 0; i < d->num_bases; ++i) {
+      const dsmz_basis_spec& b = d->bases[i];
+      ok = ok && tc_shape_ok(b.h_dtype, b.D, b.ld_H, 1, b.R, b.H);
+    }
+    if (ok) {
+      P->tc = true;
+      plan_tc_layout(P);
+    }
+  }
+  add_w_tables(P, P->tc);
   // modules
   uint64_t off = d->rng_offset_before;   // draws are placed relative to the step's base offset
   for (int i = 0; i < d->num_modules; ++i) {
@@ -486,7 +678,9 @@ uint64_t dsmz_plan_rng_increment(const dsmz_plan* p) { return p ? p->rng_increme
 int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   if (!p) return 0;
   int32_t n = 0;
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * (2 + 2 * 3);
+  // per iteration: Y, W, [Gram of W on CUDA cores | basis split on the tensor-core path],
+  // 2 x (partial sums + Cholesky), Q1 + Gram, V
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * 9;
   if (!p->mods.empty()) n += 4 + 3;
   return n;
 }
@@ -503,11 +697,28 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   P->dev_tables = static_cast<char*>(device_tables);
   P->workspace = static_cast<char*>(workspace);
   patch_ws_pointers(P);
+  if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
+  if (P->tc) {
+    cudaError_t ez = cudaMemsetAsync(P->workspace + P->err_off, 0, sizeof(int), static_cast<cudaStream_t>(stream));
+    if (ez != cudaSuccess) return cuda_fail("dsmz_plan_bind: error word", ez);
+  }
   P->write_blob();
   cudaError_t e = cudaMemcpyAsync(device_tables, P->blob.data(), P->table_bytes, cudaMemcpyHostToDevice,
                                   static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail("dsmz_plan_bind: table upload", e);
   return DSMZ_OK;
+}
+
+int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* P) { return (P && P->tc) ? 1 : 0; }
+
+int32_t dsmz_plan_device_error(const dsmz_plan* P, dsmz_stream_t stream) {
+  if (!P || !P->workspace || !P->tc) return 0;
+  int v = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&v, P->workspace + P->err_off, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return -1;
+  if (v) cudaMemsetAsync(P->workspace + P->err_off, 0, sizeof(int), s);
+  return v;
 }
 
 static int plan_ready(const dsmz_plan* P, const char* who) {
@@ -572,6 +783,11 @@ static int upload_small(dsmz_plan* P, char* ws, cudaStream_t s) {
     pk.v[0] = P->bases[0];
     k_write_pack<BasisD, 1><<<1, 32, 0, s>>>(pk, reinterpret_cast<BasisD*>(ws + P->off_bases), 1);
   }
+  if (P->tc && !P->tcb.empty()) {
+    Pack<tc::TCBasis, 1> pk{};
+    pk.v[0] = P->tcb[0];
+    k_write_pack<tc::TCBasis, 1><<<1, 32, 0, s>>>(pk, reinterpret_cast<tc::TCBasis*>(ws + P->off_tcb), 1);
+  }
   DSMZ_LAUNCHED("table upload");
   return 0;
 }
@@ -631,11 +847,11 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
   const size_t gs = gram_smem(r), as = apply_smem(r);
   const KalmanIn kin{};
   if (gram_rb(r) == 4) {
-    if ((rc = set_smem(k_gram<0, 4>, gs))) return rc;
-    k_gram<0, 4><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
+    if ((rc = set_smem(k_gram<0, 4, double>, gs))) return rc;
+    k_gram<0, 4, double><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
   } else {
-    if ((rc = set_smem(k_gram<0, 8>, gs))) return rc;
-    k_gram<0, 8><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
+    if ((rc = set_smem(k_gram<0, 8, double>, gs))) return rc;
+    k_gram<0, 8, double><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
   }
   DSMZ_LAUNCHED("zo_muon_update Gram");
   k_ns_solve<<<1, kThreads, 0, s>>>(tb, tb.mats, make_ns(schedule, norm_floor));
@@ -646,7 +862,7 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
   return DSMZ_OK;
 }
 
-static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R) {
+static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R, bool tc) {
   dsmz_plan P;
   P.ws.take(table_head_bytes());
   BasisD bd{};
@@ -655,19 +871,18 @@ static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R) {
   bd.w_off = static_cast<int64_t>(P.ws.take(static_cast<size_t>(D) * R * sizeof(float)) / sizeof(float));
   fill_basis_tiles(bd, P.nytiles, P.nwtiles);
   P.bases.push_back(bd);
-  MatD w{};
-  w.nvec = D; w.r = R; w.ld = R; w.cs = 1; w.side = 0; w.owner = 0;
-  add_matrix(P.w1, P.ws, w, P.nwsegs, false);
-  P.w1[0].dw_off = static_cast<int64_t>(P.ws.take(3 * static_cast<size_t>(R) * R * sizeof(double)) / sizeof(double));
-  P.w2.push_back(P.w1[0]);
   P.R = static_cast<int>(R);
+  if (tc) plan_tc_layout(&P);
+  P.tc = tc;
+  add_w_tables(&P, tc);
   P.pack();
   return P;
 }
 
 size_t dsmz_power_iter_workspace_bytes(int64_t T, int64_t D, int64_t R) {
   if (T <= 0 || D <= 0 || R <= 0) return 0;
-  return pi_plan(T, D, R).ws.bytes;
+  const size_t a = pi_plan(T, D, R, false).ws.bytes, b = pi_plan(T, D, R, true).ws.bytes;
+  return a > b ? a : b;   // either path fits
 }
 
 int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_t hs0, int64_t hs1, const float* V,
@@ -677,7 +892,8 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
   if (T <= 0 || D <= 0 || R <= 0) return fail(DSMZ_ERR_INVALID, "power_iter: empty shape");
   if (R > DSMZ_MAX_RANK) return fail(DSMZ_ERR_UNSUPPORTED, "power_iter: R must be <= " + std::to_string(DSMZ_MAX_RANK));
   if (h_dtype != DSMZ_F32 && h_dtype != DSMZ_BF16) return fail(DSMZ_ERR_INVALID, "power_iter: bad dtype");
-  dsmz_plan P = pi_plan(T, D, R);
+  const bool want_tc = tc_shape_ok(h_dtype, D, hs0, hs1, R, H);
+  dsmz_plan P = pi_plan(T, D, R, want_tc);
   if (workspace_bytes < P.ws.bytes) return fail(DSMZ_ERR_WORKSPACE, "power_iter: workspace too small");
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(DSMZ_ERR_INVALID, "power_iter: workspace must be 256-byte aligned");
@@ -695,6 +911,18 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
   b.Vin = V; b.v_s0 = vs0; b.v_s1 = vs1; b.Vout = out;
   P.workspace = static_cast<char*>(workspace);
   patch_ws_pointers(&P);
+  if (P.tc && !bind_tc(&P)) {   // driver refused a tensor map: rebuild for the CUDA-core path
+    P = pi_plan(T, D, R, false);
+    BasisD& b2 = P.bases[0];
+    b2.H = H; b2.hdt = h_dtype; b2.h_s0 = hs0; b2.h_s1 = hs1;
+    b2.Vin = V; b2.v_s0 = vs0; b2.v_s1 = vs1; b2.Vout = out;
+    P.workspace = static_cast<char*>(workspace);
+    patch_ws_pointers(&P);
+  }
+  if (P.tc) {
+    cudaError_t ez = cudaMemsetAsync(P.workspace + P.err_off, 0, sizeof(int), s);
+    if (ez != cudaSuccess) return cuda_fail("power_iter: error word", ez);
+  }
   int rc = upload_small(&P, static_cast<char*>(workspace), s);
   if (rc) return rc;
   return run_power_iteration(&P, num_iters, norm_floor, s);

@@ -25,6 +25,7 @@ struct MatD {
   int64_t gram_off;           // doubles: nseg * r*r Gram partials
   int64_t p_off;              // floats: r*r apply matrix (fp32), then 4 floats of scalars
   int64_t dw_off;             // doubles: 4 * r*r fp64 solve workspace
+  int64_t p_prev_off;         // floats: r*r matrix applied in place before the Gram (QR round 2)
 };
 
 struct ModD {
@@ -59,8 +60,8 @@ struct Tables {
   const MatD* mats; int32_t nmats; int32_t nsegs;      // adapter matrices
   const ModD* mods; int32_t nmods; int32_t nchunks;
   const BasisD* bases; int32_t nbases; int32_t nytiles; int32_t nwtiles;
-  const MatD* wmats1; const MatD* wmats2;               // W of each basis: QR round 1 (in place), round 2 (-> V)
-  int32_t nwsegs; int32_t pad0;
+  const MatD* wA; const MatD* wB;                       // W of each basis: CholeskyQR round 1, round 2 (-> V)
+  int32_t nwsegsA; int32_t nwsegsB;
   int32_t factor_dtype; int32_t pad1;
   char* ws;                                            // workspace base
   int64_t seg_kal_off;        // doubles: nsegs * 2 per-segment Kalman partials

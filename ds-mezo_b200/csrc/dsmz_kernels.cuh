@@ -41,26 +41,93 @@ __device__ __forceinline__ void kal_observe(float mu1, float var1, float z, cons
   var2 = __fmul_rn(var1, __fsub_rn(1.0f, __fmul_rn(K, z)));
 }
 
+// Vectors per shared-memory sub-tile: about 8192 elements, so the 4 x 8 register blocks of
+// rows_x_mat cover all 256 threads at r = 64.
 __host__ __device__ inline int tile_vectors(int r) {
-  int tv = 2048 / (r < 1 ? 1 : r);
-  return tv < 16 ? 16 : (tv > 256 ? 256 : tv);
+  int tv = (8192 / (r < 1 ? 1 : r)) & ~3;   // a multiple of the 4-vector blocks
+  return tv < 16 ? 16 : (tv > 1024 ? 1024 : tv);
 }
 __host__ __device__ inline int pad4(int r) { return (r + 3) & ~3; }
+__host__ __device__ inline int pad8(int r) { return (r + 7) & ~7; }
+
+// out[v][c] = sum_{a<K} X[v*xld + a] * P[a*pld + c] for v < nv, c < nc, both operands in
+// shared memory. Each thread owns 4 vectors x 8 columns (32 fp32 accumulators) and reads a
+// P row segment as two float4 (pld % 4 == 0, columns zero-padded to a multiple of 8), so
+// the loop issues 6 shared loads per 32 FMAs. X needs ceil(nv/4)*4 readable rows; an odd
+// xld keeps the four row reads of a warp on distinct banks. sink(v, c0, acc) takes the 8
+// outputs of vector v starting at column c0.
+template <typename Sink>
+__device__ __forceinline__ void rows_x_mat(const float* __restrict__ X, int xld, const float* __restrict__ P, int pld,
+                                           int nv, int K, int nc, Sink sink) {
+  const int cbs = (nc + 7) >> 3;
+  const int vbs = (nv + 3) >> 2;
+  for (int blk = threadIdx.x; blk < vbs * cbs; blk += kThreads) {
+    const int vb = blk / cbs, cb = blk - vb * cbs;
+    const int v0 = vb * 4, c0 = cb * 8;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    const float* x0 = X + v0 * xld;
+    const float* pc = P + c0;
+#pragma unroll 4
+    for (int a = 0; a < K; ++a) {
+      const float4 p0 = *reinterpret_cast<const float4*>(pc + a * pld);
+      const float4 p1 = *reinterpret_cast<const float4*>(pc + a * pld + 4);
+      const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = x0[i * xld + a];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(x, pv[j], acc[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (v0 + i < nv) sink(v0 + i, c0, acc[i]);
+  }
+}
+
+// Element e of a sub-tile of nv vectors in coalesced memory order: side A walks each row
+// (vector) along its r components, side B walks each of the r rows along the vectors.
+__device__ __forceinline__ void elem_vk(int side, int e, int r, int nv, int& v, int& k) {
+  if (side == 0) { v = e / r; k = e - v * r; } else { k = e / nv; v = e - k * nv; }
+}
+constexpr int kUnroll = 8;   // elements in flight per thread in the streaming loops
+
+// Sum of n values spaced `stride` apart, four independent chains to overlap the loads.
+__device__ __forceinline__ double strided_sum(const double* p, int n, int64_t stride) {
+  double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+  int g = 0;
+  for (; g + 4 <= n; g += 4) {
+    s0 += p[(g + 0) * stride];
+    s1 += p[(g + 1) * stride];
+    s2 += p[(g + 2) * stride];
+    s3 += p[(g + 3) * stride];
+  }
+  for (; g < n; ++g) s0 += p[g * stride];
+  return (s0 + s1) + (s2 + s3);
+}
 
 __device__ __forceinline__ int64_t vaddr2(const MatD& M, int64_t v, int64_t k) {
   return M.side == 0 ? v * M.ld + k * M.cs : k * M.ld + v * M.cs;
 }
 
 // =====================================================================================
-// Gram partials: for each segment of each matrix, G_seg = sum_v x_v x_v^T (r x r), fp64
-// products and sums of the fp32 vectors.
+// Gram partials: for each segment of each matrix, G_seg = sum_v x_v x_v^T (r x r).
 // SRC 0: x = mu (plain). SRC 1: x = Kalman-updated momentum mu2 (controller.py:283-284).
+// SRC 2: x = w P_prev computed in fp32 and written back over w (CholeskyQR round 2: the
+//        Gram of the rounded Q1 = W R1^-1 measures what round 1 left unorthogonal).
+// ACC double: fp64 products and sums. The Gram squares the condition number, and the
+// Newton-Schulz polynomial of an ill-conditioned momentum (a fresh start, where
+// mu_B ~ Zc_B V^T with a square Gaussian Zc_B) and round 1 of the QR need its small
+// eigenvalues intact. ACC float serves the near-orthonormal Q1 of round 2.
 // =====================================================================================
-template <int SRC, int RB>
+template <int SRC, int RB, typename ACC>
 __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __restrict__ mats, int nmats,
                                                    KalmanIn kin) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* xs = reinterpret_cast<float*>(smem_raw);
   const int seg = blockIdx.x;
   const int mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
   const MatD M = mats[mi];
@@ -70,7 +137,11 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
   const int ngroups = kThreads / tpg;
   const int rp = tpr * RB;
   const int TV = tile_vectors(r);
-  const int xld = rp + 1;
+  const int xld = rp + 4;                                   // 16-byte rows for the float4 Gram loads
+  const int r8 = pad8(r), wld = r8 + 1;
+  float* Pp = reinterpret_cast<float*>(smem_raw);          // SRC 2: r x r8
+  float* ws_ = Pp + (SRC == 2 ? r * r8 : 0);               // SRC 2: raw rows, TV x wld
+  float* xs = ws_ + (SRC == 2 ? TV * wld : 0);             // TV x xld
   const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
   const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
   const int tid = threadIdx.x;
@@ -79,44 +150,102 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
   const bool active = grp < ngroups;
   KalScal ks{};
   if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
+  if (SRC == 2) {
+    const float* P1 = reinterpret_cast<const float*>(tb.ws) + M.p_prev_off;
+    for (int e = tid; e < r * r8; e += kThreads) {
+      const int a = e / r8, c = e - a * r8;
+      Pp[e] = (c < r) ? P1[a * r + c] : 0.f;
+    }
+    for (int e = tid; e < TV * (rp - r); e += kThreads) {   // padding columns stay zero
+      const int v = e / (rp - r);
+      xs[v * xld + r + (e - v * (rp - r))] = 0.f;
+    }
+  }
 
-  double acc[RB][RB];
+  ACC acc[RB][RB];
 #pragma unroll
   for (int i = 0; i < RB; ++i)
 #pragma unroll
-    for (int j = 0; j < RB; ++j) acc[i][j] = 0.0;
+    for (int j = 0; j < RB; ++j) acc[i][j] = ACC(0);
 
   for (int64_t s0 = v0; s0 < v1; s0 += TV) {
     const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
-    for (int e = tid; e < TV * rp; e += kThreads) {
-      int v, k;
-      if (M.side == 0) { v = e / rp; k = e - v * rp; } else { k = e / TV; v = e - k * TV; }
-      float x = 0.f;
-      if (v < nv && k < r) {
-        const int64_t a = vaddr2(M, s0 + v, k);
-        if (SRC == 0) {
-          x = M.mu[a];
-        } else {
-          float mu1, var1, mu2, var2;
-          kal_predict(M.mu[a], M.var[a], ks, mu1, var1);
-          kal_observe(mu1, var1, M.z[a], ks, mu2, var2);
-          x = mu2;
+    if (SRC == 2) {
+      const int n = nv * r;
+      for (int base = tid; base < n; base += kThreads * kUnroll) {
+        float w0[kUnroll];
+        int vv[kUnroll], kk[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int e = base + u * kThreads;
+          elem_vk(M.side, e, r, nv, vv[u], kk[u]);
+          if (e < n) w0[u] = M.mu[vaddr2(M, s0 + vv[u], kk[u])];
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (base + u * kThreads < n) ws_[vv[u] * wld + kk[u]] = w0[u];
+      }
+      __syncthreads();
+      // Q1 = W R1^-1 for the sub-tile, kept for the Gram and written over W
+      rows_x_mat(ws_, wld, Pp, r8, nv, r, r, [&](int v, int c0, const float (&acc)[8]) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + j;
+          if (c < r) {
+            xs[v * xld + c] = acc[j];
+            M.mu[vaddr2(M, s0 + v, c)] = acc[j];
+          }
+        }
+      });
+    } else {
+      const int n = nv * r;
+      for (int base = tid; base < n; base += kThreads * kUnroll) {
+        float m0[kUnroll], w0[kUnroll], z0[kUnroll];
+        int vv[kUnroll], kk[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {          // issue every load before using any
+          const int e = base + u * kThreads;
+          elem_vk(M.side, e, r, nv, vv[u], kk[u]);
+          if (e < n) {
+            const int64_t a = vaddr2(M, s0 + vv[u], kk[u]);
+            m0[u] = M.mu[a];
+            if (SRC == 1) { w0[u] = M.var[a]; z0[u] = M.z[a]; }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          if (base + u * kThreads < n) {
+            float x = m0[u];
+            if (SRC == 1) {
+              float mu1, var1, mu2, var2;
+              kal_predict(m0[u], w0[u], ks, mu1, var1);
+              kal_observe(mu1, var1, z0[u], ks, mu2, var2);
+              x = mu2;
+            }
+            xs[vv[u] * xld + kk[u]] = x;
+          }
         }
       }
-      xs[v * xld + k] = x;
+      if (rp > r || nv < TV) {                        // zero padding columns and rows past nv
+        for (int e = tid; e < TV * rp; e += kThreads) {
+          const int v = e / rp, k = e - v * rp;
+          if (v >= nv || k >= r) xs[v * xld + k] = 0.f;
+        }
+      }
     }
     __syncthreads();
     if (active) {
-      // fp64 products and sums: the Gram squares the condition number, and the
-      // Newton-Schulz polynomial of an ill-conditioned momentum (a fresh start, where
-      // mu_B ~ Zc_B V^T with a square Gaussian Zc_B) needs its small eigenvalues intact.
       for (int v = grp; v < nv; v += ngroups) {
         const float* row = xs + v * xld;
-        double xa[RB], xb[RB];
+        ACC xa[RB], xb[RB];
 #pragma unroll
-        for (int i = 0; i < RB; ++i) {
-          xa[i] = static_cast<double>(row[bi * RB + i]);
-          xb[i] = static_cast<double>(row[bj * RB + i]);
+        for (int i = 0; i < RB; i += 4) {
+          const float4 fa = *reinterpret_cast<const float4*>(row + bi * RB + i);
+          const float4 fb = *reinterpret_cast<const float4*>(row + bj * RB + i);
+          xa[i] = static_cast<ACC>(fa.x); xa[i + 1] = static_cast<ACC>(fa.y);
+          xa[i + 2] = static_cast<ACC>(fa.z); xa[i + 3] = static_cast<ACC>(fa.w);
+          xb[i] = static_cast<ACC>(fb.x); xb[i + 1] = static_cast<ACC>(fb.y);
+          xb[i + 2] = static_cast<ACC>(fb.z); xb[i + 3] = static_cast<ACC>(fb.w);
         }
 #pragma unroll
         for (int i = 0; i < RB; ++i)
@@ -135,7 +264,7 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
 #pragma unroll
         for (int j = 0; j < RB; ++j) {
           const int a = bi * RB + i, b = bj * RB + j;
-          if (a < r && b < r) out[a * r + b] = acc[i][j];
+          if (a < r && b < r) out[a * r + b] = static_cast<double>(acc[i][j]);
         }
     }
   } else {
@@ -145,14 +274,14 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
       for (int i = 0; i < RB; ++i)
 #pragma unroll
         for (int j = 0; j < RB; ++j)
-          red[(grp * rp + bi * RB + i) * rp + bj * RB + j] = acc[i][j];
+          red[(grp * rp + bi * RB + i) * rp + bj * RB + j] = static_cast<double>(acc[i][j]);
     }
     __syncthreads();
     for (int e = tid; e < r * r; e += kThreads) {
       const int a = e / r, b = e - a * r;
-      double s = 0.0;
-      for (int g = 0; g < ngroups; ++g) s += red[(g * rp + a) * rp + b];
-      out[e] = s;
+      double sum = 0.0;
+      for (int g = 0; g < ngroups; ++g) sum += red[(g * rp + a) * rp + b];
+      out[e] = sum;
     }
   }
 }
@@ -243,8 +372,7 @@ __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
   double tr = 0.0;
   for (int e = tid; e < rr; e += kThreads) {
-    double s = 0.0;
-    for (int g = 0; g < M.nseg; ++g) s += part[static_cast<int64_t>(g) * rr + e];
+    const double s = strided_sum(part + e, M.nseg, rr);
     G[e] = s;
     const int a = e / r;
     if (a * r + a == e) tr += s;
@@ -286,48 +414,61 @@ __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __
 // the Gram partials), G = R^T R with pivots sqrt(max(d, norm_floor)) (the clamp of the
 // reference MGS, ds_mezo/kernels.py:238), and the fp32 apply matrix R^{-1}.
 // =====================================================================================
+// Sums the Gram partials of every matrix into its fp64 workspace, 256 entries per CTA:
+// item -> (matrix, entry block). Many CTAs per matrix keep the loads in flight.
+__global__ void __launch_bounds__(kThreads) k_sum_partials(Tables tb, const MatD* __restrict__ mats, int nmats,
+                                                           int blocks_per_mat) {
+  const int mi = blockIdx.x / blocks_per_mat;
+  const int blk = blockIdx.x - mi * blocks_per_mat;
+  if (mi >= nmats) return;
+  const MatD M = mats[mi];
+  const int rr = static_cast<int>(M.r * M.r);
+  const int e = blk * kThreads + threadIdx.x;
+  if (e >= rr) return;
+  const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  double* G = reinterpret_cast<double*>(tb.ws) + M.dw_off;
+  G[e] = strided_sum(part + e, M.nseg, rr);
+}
+
+// Cholesky of the summed Gram in the matrix's fp64 workspace (k_sum_partials).
 __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __restrict__ mats, float norm_floor) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
   const int tid = threadIdx.x;
+  // r <= 64: factor and inverse in shared memory; larger r works on the fp64 workspace
+  const bool in_smem = r <= 64;
   double* dw = reinterpret_cast<double*>(tb.ws) + M.dw_off;
-  double* G = dw;
-  double* Rm = dw + rr;   // upper triangular factor
-  double* Ri = dw + 2 * rr;
-  const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  double* A = in_smem ? reinterpret_cast<double*>(smem_raw) : dw;        // lower-right part = Schur complement
+  double* Ri = in_smem ? A + rr : dw + 2 * rr;
   for (int e = tid; e < rr; e += kThreads) {
-    double s = 0.0;
-    for (int g = 0; g < M.nseg; ++g) s += part[static_cast<int64_t>(g) * rr + e];
-    G[e] = s;
-    Rm[e] = 0.0;
+    const double g = dw[e];
+    A[e] = g;
     Ri[e] = 0.0;
   }
   __syncthreads();
-  __shared__ double diag;
+  // Right-looking Cholesky: after step j, row j of A holds row j of the upper factor R
+  // (G = R^T R), with pivots sqrt(max(d, norm_floor)) like the reference MGS clamp.
   for (int j = 0; j < r; ++j) {
-    if (tid == 0) {
-      double d = G[j * r + j];
-      for (int k = 0; k < j; ++k) d -= Rm[k * r + j] * Rm[k * r + j];
-      diag = sqrt(fmax(d, static_cast<double>(norm_floor)));
-      Rm[j * r + j] = diag;
-    }
+    const double d = sqrt(fmax(A[j * r + j], static_cast<double>(norm_floor)));
     __syncthreads();
-    const double dj = diag;
-    for (int i = j + 1 + tid; i < r; i += kThreads) {
-      double s = G[j * r + i];
-      for (int k = 0; k < j; ++k) s -= Rm[k * r + j] * Rm[k * r + i];
-      Rm[j * r + i] = s / dj;
+    for (int i = j + tid; i < r; i += kThreads) A[j * r + i] = (i == j) ? d : A[j * r + i] / d;
+    __syncthreads();
+    const int m = r - j - 1;
+    for (int e = tid; e < m * m; e += kThreads) {
+      const int a = j + 1 + e / m, b = j + 1 + e % m;
+      A[a * r + b] -= A[j * r + a] * A[j * r + b];
     }
     __syncthreads();
   }
-  // R^{-1}: column j solves R x = e_j by back substitution.
-  for (int j = tid; j < r; j += kThreads) {
-    Ri[j * r + j] = 1.0 / Rm[j * r + j];
-    for (int i = j - 1; i >= 0; --i) {
-      double s = 0.0;
-      for (int k = i + 1; k <= j; ++k) s += Rm[i * r + k] * Ri[k * r + j];
-      Ri[i * r + j] = -s / Rm[i * r + i];
+  // R^{-1}: column c solves R x = e_c by back substitution, one thread per column
+  for (int c = tid; c < r; c += kThreads) {
+    Ri[c * r + c] = 1.0 / A[c * r + c];
+    for (int i = c - 1; i >= 0; --i) {
+      double sum = 0.0;
+      for (int k = i + 1; k <= c; ++k) sum += A[i * r + k] * Ri[k * r + c];
+      Ri[i * r + c] = -sum / A[i * r + i];
     }
   }
   __syncthreads();
@@ -338,8 +479,10 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
 // =====================================================================================
 // Apply: X[v,:] = x_v^T Pm for every vector of every matrix segment.
 // OUT 0: param -= eta * X (factor dtype), optional scratch = X  (ds_mezo/kernels.py:84-92).
-// OUT 1: param (fp32) = X (CholeskyQR: Q = W R^{-1}).
+// OUT 1: param (fp32) = X (CholeskyQR: V = Q1 R2^-1).
 // SRC 1 recomputes the Kalman update and writes mu, var (controller.py:283-285).
+// Loads and stores run in coalesced element order; the r x r product in between runs
+// from shared memory with rows_x_mat.
 // =====================================================================================
 template <int SRC, int OUT>
 __global__ void __launch_bounds__(kThreads) k_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
@@ -349,68 +492,82 @@ __global__ void __launch_bounds__(kThreads) k_apply(Tables tb, const MatD* __res
   const int mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
   const MatD M = mats[mi];
   const int r = static_cast<int>(M.r);
-  const int rp = pad4(r);
+  const int r8 = pad8(r);
   const int TV = tile_vectors(r);
-  const int xld = rp + 1;
-  float* Ps = reinterpret_cast<float*>(smem_raw);  // r x rp
-  float* xs = Ps + r * rp;                         // TV x xld
+  const int xld = r8 + 1;
+  float* Ps = reinterpret_cast<float*>(smem_raw);  // r x r8
+  float* xs = Ps + r * r8;                         // TV x xld
+  float* os = xs + TV * xld;                       // TV x xld
   const int tid = threadIdx.x;
   const float* Pm = reinterpret_cast<const float*>(tb.ws) + M.p_off;
-  for (int e = tid; e < r * rp; e += kThreads) {
-    const int a = e / rp, c = e - a * rp;
+  for (int e = tid; e < r * r8; e += kThreads) {
+    const int a = e / r8, c = e - a * r8;
     Ps[e] = (c < r) ? Pm[a * r + c] : 0.f;
   }
   KalScal ks{};
   if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
   const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
   const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
-  const int ncb = rp / 4;
   __syncthreads();
   for (int64_t s0 = v0; s0 < v1; s0 += TV) {
     const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
-    for (int e = tid; e < TV * r; e += kThreads) {
-      int v, k;
-      if (M.side == 0) { v = e / r; k = e - v * r; } else { k = e / TV; v = e - k * TV; }
-      if (v >= nv) continue;
-      const int64_t a = vaddr2(M, s0 + v, k);
-      float x;
-      if (SRC == 0) {
-        x = M.mu[a];
-      } else {
-        float mu1, var1, mu2, var2;
-        kal_predict(M.mu[a], M.var[a], ks, mu1, var1);
-        kal_observe(mu1, var1, M.z[a], ks, mu2, var2);
-        M.mu[a] = mu2;
-        M.var[a] = var2;
-        x = mu2;
+    const int n = nv * r;
+    for (int base = tid; base < n; base += kThreads * kUnroll) {
+      float m0[kUnroll], w0[kUnroll], z0[kUnroll];
+      int vv[kUnroll], kk[kUnroll];
+      int64_t ad[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {            // issue every load before using any
+        const int e = base + u * kThreads;
+        elem_vk(M.side, e, r, nv, vv[u], kk[u]);
+        ad[u] = vaddr2(M, s0 + vv[u], kk[u]);
+        if (e < n) {
+          m0[u] = M.mu[ad[u]];
+          if (SRC == 1) { w0[u] = M.var[ad[u]]; z0[u] = M.z[ad[u]]; }
+        }
       }
-      xs[v * xld + k] = x;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (base + u * kThreads >= n) continue;
+        float x = m0[u];
+        if (SRC == 1) {
+          float mu1, var1, mu2, var2;
+          kal_predict(m0[u], w0[u], ks, mu1, var1);
+          kal_observe(mu1, var1, z0[u], ks, mu2, var2);
+          M.mu[ad[u]] = mu2;
+          M.var[ad[u]] = var2;
+          x = mu2;
+        }
+        xs[vv[u] * xld + kk[u]] = x;
+      }
     }
     __syncthreads();
-    for (int it = tid; it < nv * ncb; it += kThreads) {
-      int v, cb;
-      if (M.side == 0) { v = it / ncb; cb = it - v * ncb; } else { cb = it / nv; v = it - cb * nv; }
-      const float* xr = xs + v * xld;
-      float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-      for (int a = 0; a < r; ++a) {
-        const float xa = xr[a];
-        const float4 p = *reinterpret_cast<const float4*>(Ps + a * rp + cb * 4);
-        acc0 = fmaf(xa, p.x, acc0); acc1 = fmaf(xa, p.y, acc1);
-        acc2 = fmaf(xa, p.z, acc2); acc3 = fmaf(xa, p.w, acc3);
-      }
-      const float accs[4] = {acc0, acc1, acc2, acc3};
+    rows_x_mat(xs, xld, Ps, r8, nv, r, r, [&](int v, int c0, const float (&acc)[8]) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = cb * 4 + j;
-        if (c >= r) break;
-        const int64_t ad = vaddr2(M, s0 + v, c);
-        const float X = accs[j];
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < r) os[v * xld + c0 + j] = acc[j];
+    });
+    __syncthreads();
+    for (int base = tid; base < n; base += kThreads * kUnroll) {
+      float p0[kUnroll];
+      int vv[kUnroll], kk[kUnroll];
+      int64_t ad[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int e = base + u * kThreads;
+        elem_vk(M.side, e, r, nv, vv[u], kk[u]);
+        ad[u] = vaddr2(M, s0 + vv[u], kk[u]);
+        if (OUT == 0 && e < n) p0[u] = ldf(M.param, ad[u], pdt);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (base + u * kThreads >= n) continue;
+        const float X = os[vv[u] * xld + kk[u]];
         if (OUT == 0) {
-          const float p = ldf(M.param, ad, pdt);
-          stf(M.param, ad, __fsub_rn(p, __fmul_rn(eta, X)), pdt);
-          if (M.scratch) M.scratch[ad] = X;
+          stf(M.param, ad[u], __fsub_rn(p0[u], __fmul_rn(eta, X)), pdt);
+          if (M.scratch) M.scratch[ad[u]] = X;
         } else {
-          reinterpret_cast<float*>(M.param)[ad] = X;
+          reinterpret_cast<float*>(M.param)[ad[u]] = X;
         }
       }
     }
@@ -499,7 +656,7 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   const ModD D = tb.mods[blockIdx.x];
   const int R = D.r, RC = D.rc, RCA = D.rca;
   const int tid = threadIdx.x;
-  double* BV = reinterpret_cast<double*>(smem_raw);   // R x RC
+  double* BVt = reinterpret_cast<double*>(smem_raw);  // RC x R (column-major B V)
   const float* part = reinterpret_cast<const float*>(tb.ws) + D.bpart_off;
   float* ZcB = reinterpret_cast<float*>(tb.ws) + D.coef_off;
   float* Qo = ZcB + static_cast<int64_t>(R) * RC;
@@ -509,7 +666,8 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       sbv += part[static_cast<int64_t>(c) * 2 * R * RC + e];
       svb += part[static_cast<int64_t>(c) * 2 * R * RC + R * RC + e];
     }
-    BV[e] = sbv;
+    const int i = e / RC, c = e - i * RC;
+    BVt[c * R + i] = sbv;
     if (MODE == 0) {
       const float g = torch_randn_at(seed, base_off + D.offB, D.thrB, e);
       ZcB[e] = __fmul_rn(g, sqrtf(static_cast<float>(svb)));
@@ -521,27 +679,29 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   if (tid < 32) {
     const int lane = tid;
     for (int col = 0; col < RCA; ++col) {
+      double* vc = BVt + col * R;
       for (int prev = 0; prev < col; ++prev) {
+        const double* qp = BVt + prev * R;
         double d = 0.0;
-        for (int i = lane; i < R; i += 32) d += BV[i * RC + col] * BV[i * RC + prev];
+        for (int i = lane; i < R; i += 32) d += vc[i] * qp[i];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        for (int i = lane; i < R; i += 32) BV[i * RC + col] -= d * BV[i * RC + prev];
+        for (int i = lane; i < R; i += 32) vc[i] -= d * qp[i];
         __syncwarp();
       }
       double n2 = 0.0;
-      for (int i = lane; i < R; i += 32) n2 += BV[i * RC + col] * BV[i * RC + col];
+      for (int i = lane; i < R; i += 32) n2 += vc[i] * vc[i];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
       const double inv = 1.0 / sqrt(fmax(n2, static_cast<double>(norm_floor)));
-      for (int i = lane; i < R; i += 32) BV[i * RC + col] *= inv;
+      for (int i = lane; i < R; i += 32) vc[i] *= inv;
       __syncwarp();
     }
   }
   __syncthreads();
   for (int e = tid; e < R * RCA; e += kThreads) {
     const int i = e / RCA, k = e - i * RCA;
-    Qo[e] = static_cast<float>(BV[i * RC + k]);
+    Qo[e] = static_cast<float>(BVt[k * R + i]);
   }
 }
 
@@ -568,15 +728,22 @@ __global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, 
   const int TV = tile_vectors(r);
   const int tid = threadIdx.x;
   const int KW = (M.side == 0) ? RCA : RC;     // inner width of the z product
-  float* Cs = reinterpret_cast<float*>(smem_raw);        // KW x R : Q^T (side A) or Zc_B^T (side B)
-  float* Ks = Cs + KW * R;                               // TV x (KW+1): Zc_A rows or V rows
+  const int R8 = pad8(R);
+  float* Cs = reinterpret_cast<float*>(smem_raw);        // KW x R8 : Q^T (side A) or Zc_B^T (side B)
+  float* Ks = Cs + KW * R8;                              // TV x (KW+1): Zc_A rows or V rows
   float* zs = Ks + TV * (KW + 1);                        // TV x (r+1)
   const float* coef = reinterpret_cast<const float*>(tb.ws) + D.coef_off;
   if (M.side == 0) {
     const float* Q = coef + static_cast<int64_t>(R) * RC;   // R x RCA
-    for (int e = tid; e < KW * R; e += kThreads) { const int k = e / R, c = e - k * R; Cs[e] = Q[c * RCA + k]; }
+    for (int e = tid; e < KW * R8; e += kThreads) {
+      const int k = e / R8, c = e - k * R8;
+      Cs[e] = (c < R) ? Q[c * RCA + k] : 0.f;
+    }
   } else {
-    for (int e = tid; e < KW * R; e += kThreads) { const int k = e / R, c = e - k * R; Cs[e] = coef[c * RC + k]; }
+    for (int e = tid; e < KW * R8; e += kThreads) {
+      const int k = e / R8, c = e - k * R8;
+      Cs[e] = (c < R) ? coef[c * RC + k] : 0.f;
+    }
   }
   const BasisD Bd = tb.bases[D.basis];
   float s_zmu = 0.f, s_zzv = 0.f;
@@ -597,28 +764,41 @@ __global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, 
       Ks[v * (KW + 1) + k] = x;
     }
     __syncthreads();
-    for (int e = tid; e < nv * r; e += kThreads) {
-      const int v = e / r, c = e - v * r;
-      const float* kr = Ks + v * (KW + 1);
-      float acc = 0.f;
-      for (int k = 0; k < KW; ++k) acc = fmaf(kr[k], Cs[k * R + c], acc);
-      zs[v * (r + 1) + c] = acc * eps;
-    }
+    rows_x_mat(Ks, KW + 1, Cs, R8, nv, KW, R, [&](int v, int c0, const float (&acc)[8]) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < R) zs[v * (r + 1) + c0 + j] = acc[j] * eps;
+    });
     __syncthreads();
-    for (int e = tid; e < nv * r; e += kThreads) {
-      int v, k;
-      if (M.side == 0) { v = e / r; k = e - v * r; } else { k = e / nv; v = e - k * nv; }
-      const int64_t a = vaddr2(M, s0 + v, k);
-      const float z = zs[v * (r + 1) + k];
-      M.z[a] = z;
-      if (MODE == 0) {
-        const float p = ldf(M.param, a, tb.factor_dtype);
-        stf(M.pos, a, __fadd_rn(p, z), tb.factor_dtype);
-        stf(M.neg, a, __fsub_rn(p, z), tb.factor_dtype);
-        const float mu1 = __fmul_rn(M.mu[a], kin.beta);
-        const float var1 = __fadd_rn(__fmul_rn(M.var[a], kin.beta2), kin.q);
-        s_zmu = fmaf(z, mu1, s_zmu);
-        s_zzv = fmaf(__fmul_rn(z, z), var1, s_zzv);
+    const int n = nv * r;
+    for (int base = tid; base < n; base += kThreads * kUnroll) {
+      float p0[kUnroll], m0[kUnroll], w0[kUnroll];
+      int vv[kUnroll], kk[kUnroll];
+      int64_t ad[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {            // issue every load before using any
+        const int e = base + u * kThreads;
+        elem_vk(M.side, e, r, nv, vv[u], kk[u]);
+        ad[u] = vaddr2(M, s0 + vv[u], kk[u]);
+        if (MODE == 0 && e < n) {
+          p0[u] = ldf(M.param, ad[u], tb.factor_dtype);
+          m0[u] = M.mu[ad[u]];
+          w0[u] = M.var[ad[u]];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (base + u * kThreads >= n) continue;
+        const float z = zs[vv[u] * (r + 1) + kk[u]];
+        M.z[ad[u]] = z;
+        if (MODE == 0) {
+          stf(M.pos, ad[u], __fadd_rn(p0[u], z), tb.factor_dtype);
+          stf(M.neg, ad[u], __fsub_rn(p0[u], z), tb.factor_dtype);
+          const float mu1 = __fmul_rn(m0[u], kin.beta);
+          const float var1 = __fadd_rn(__fmul_rn(w0[u], kin.beta2), kin.q);
+          s_zmu = fmaf(z, mu1, s_zmu);
+          s_zzv = fmaf(__fmul_rn(z, z), var1, s_zzv);
+        }
       }
     }
     __syncthreads();

@@ -1,0 +1,359 @@
+// Tensor-core (tcgen05 + TMEM + TMA) kernels for the power-iteration products on sm_100a.
+//
+// Y = H V and W = H^T Y with bf16 H. Three iterations of the reference power iteration
+// are not converged, so an operand rounded to bf16 once shows up in the result (measured
+// subspace sine ~1e-2); both products therefore take the fp32 operand as a bf16 hi/lo
+// pair, B = [X_hi | X_lo] with N = 2R columns, and add the two halves of the fp32 TMEM
+// accumulator in the epilogue (sine ~1e-5 against the exact algorithm).
+//
+// One CTA computes one 128-row output tile:
+//   warp 0     TMA producer (one lane): A and B tiles into a ring of smem stages
+//   warp 1     TMEM owner + MMA issuer (one lane): tcgen05.mma kind::f16, M=128, N=2R
+//   warps 2-5  epilogue: tcgen05.ld of the 128 x 2R fp32 accumulator, hi+lo, stores
+// Every mbarrier wait gives up after ~1 s of globaltimer, sets the error word and lets
+// the CTA drain and free its TMEM.
+#pragma once
+
+#include <cuda.h>
+
+#include "dsmz_internal.cuh"
+
+namespace dsmz {
+namespace tc {
+
+constexpr int kBM = 128;         // output rows per CTA (MMA M)
+constexpr int kBK = 64;          // bf16 elements of K per stage (one 128-byte swizzle row)
+constexpr int kThreadsTC = 192;  // 6 warps
+constexpr uint64_t kTimeoutNs = 1000000000ull;
+
+// Per-basis operands of the tensor-core power iteration. Tensor maps come first (64-byte
+// alignment); they are encoded on the host once the workspace addresses are known.
+struct alignas(64) TCBasis {
+  CUtensorMap mapHy;      // H (T x D), box {64 cols, 128 rows}: A of Y = H [V_hi|V_lo], K-major
+  CUtensorMap mapHw;      // H (T x D), box {64 cols, 64 rows}:  A of W = H^T [Y_hi|Y_lo], MN-major
+  CUtensorMap mapV2;      // V2T (2R x D) bf16, box {64, 2R}: B of the Y product, K-major
+  CUtensorMap mapY2;      // Y2T (2R x T) bf16, box {64, 2R}: B of the W product, K-major
+  __nv_bfloat16* V2T;     // [V_hi | V_lo]^T, row stride ldv2
+  __nv_bfloat16* Y2T;     // [Y_hi | Y_lo]^T, row stride ldy2
+  float* W;               // D x R fp32
+  double* g1;             // fp64 Gram partial of each 128-row W tile (CholeskyQR round 1)
+  const float* Vsrc;      // caller's basis, read on the first iteration (strides v_s0, v_s1)
+  const float* Vout;      // D x R contiguous basis of later iterations
+  int64_t v_s0, v_s1;
+  int64_t ldv2, ldy2;
+  int64_t T, D;
+  int32_t R, pad0;
+  int32_t ytile0, nytile, wtile0, nwtile;
+  int32_t vt0, nvt;       // blocks of the split kernel
+  int32_t pad1, pad2;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false after kTimeoutNs (error word set) or when another role failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (gtimer() - t0 > kTimeoutNs) {
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
+}
+// 2-D TMA load (no multicast) completing on `bar`; x is the innermost coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+// Instruction descriptor, kind::f16: bf16 A and B, fp32 accumulator, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
+         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive fp32 columns of TMEM -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__host__ __device__ inline int tmem_cols(int n) {
+  int c = 32;
+  while (c < n) c <<= 1;
+  return c;
+}
+__host__ __device__ inline int stage_bytes(int R) { return kBM * kBK * 2 + 2 * R * kBK * 2; }
+
+// MODE 0: Y2T = split(H V), tiles over T.  MODE 1: W = H^T Y, tiles over D.
+template <int MODE>
+__global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restrict__ bases, int nb, int stages,
+                                                         int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned base for the swizzled stages
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int item = blockIdx.x;
+  const int bi = (MODE == 0) ? find_owner(bases, nb, item, [](const TCBasis& b) { return b.ytile0; })
+                             : find_owner(bases, nb, item, [](const TCBasis& b) { return b.wtile0; });
+  const TCBasis* B = bases + bi;
+  const int R = B->R;
+  const int N = 2 * R;
+  const int tile = item - ((MODE == 0) ? B->ytile0 : B->wtile0);
+  const int64_t K = (MODE == 0) ? B->D : B->T;
+  const int nk = static_cast<int>((K + kBK - 1) / kBK);
+  const int sbytes = stage_bytes(R);
+  const int a_bytes = kBM * kBK * 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tmem_full = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncols = tmem_cols(N);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    mbar_init(tmem_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const CUtensorMap* mA = (MODE == 0) ? &B->mapHy : &B->mapHw;
+      const CUtensorMap* mB = (MODE == 0) ? &B->mapV2 : &B->mapY2;
+      tmap_acquire(mA);
+      tmap_acquire(mB);
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % stages;
+        const uint32_t u = static_cast<uint32_t>(i / stages);
+        if (i >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
+        unsigned char* As = smem + s * sbytes;
+        unsigned char* Bs = As + a_bytes;
+        mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
+        if (MODE == 0) {
+          tma_load_2d(As, mA, i * kBK, tile * kBM, full + s);
+        } else {
+          tma_load_2d(As, mA, tile * kBM, i * kBK, full + s);
+          tma_load_2d(As + a_bytes / 2, mA, tile * kBM + 64, i * kBK, full + s);
+        }
+        tma_load_2d(Bs, mB, i * kBK, 0, full + s);
+        issued = i + 1;
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA can exit
+        for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+          mbar_wait(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u, err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(N, MODE == 1 ? 1 : 0, 0);
+      bool ok = true;
+      int done = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(full + s, static_cast<uint32_t>(i / stages) & 1u, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * sbytes);
+        const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // A: K-major rows of 128 B (MODE 0) or MN-major 64 x 8 atoms, two along MN 8 KB apart (MODE 1)
+          const uint64_t ad = (MODE == 0) ? sdesc(a0 + kk * 32, 16, 1024) : sdesc(a0 + kk * 2048, 8192, 1024);
+          const uint64_t bd = sdesc(b0 + kk * 32, 16, 1024);
+          mma_bf16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(empty + s);
+        done = i + 1;
+      }
+      mma_commit(tmem_full);
+      if (!ok && done > 0) mbar_wait(tmem_full, 0, err);
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool mine = mbar_wait(tmem_full, 0, err);
+    // one verdict for the four epilogue warps, so none waits at a barrier the others skip
+    uint32_t all_ok;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(all_ok)
+        : "r"(static_cast<uint32_t>(mine))
+        : "memory");
+    const bool ok = all_ok != 0;
+    tc_fence_after();
+    if (ok) {
+      const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      if (MODE == 0) {
+        const int64_t t = static_cast<int64_t>(tile) * kBM + row;
+        for (int j = 0; j < R; j += 16) {
+          float hi[16], lo[16];
+          tmem_ld16(trow + j, hi);
+          tmem_ld16(trow + R + j, lo);
+          if (t < B->T) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const float y = hi[c] + lo[c];
+              const __nv_bfloat16 yh = __float2bfloat16_rn(y);
+              const __nv_bfloat16 yl = __float2bfloat16_rn(y - __bfloat162float(yh));
+              B->Y2T[static_cast<int64_t>(j + c) * B->ldy2 + t] = yh;
+              B->Y2T[static_cast<int64_t>(R + j + c) * B->ldy2 + t] = yl;
+            }
+          }
+        }
+      } else {
+        const int64_t d = static_cast<int64_t>(tile) * kBM + row;
+        // The pipeline stages are drained (every MMA completed before tmem_full), so the
+        // W tile is staged over them for its Gram.
+        float* wt = reinterpret_cast<float*>(smem);
+        const int tld = R + 4;                                // 16-byte rows for float4 reads
+        for (int j = 0; j < R; j += 16) {
+          float hi[16], lo[16];
+          tmem_ld16(trow + j, hi);
+          tmem_ld16(trow + R + j, lo);
+          float w[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) w[c] = hi[c] + lo[c];    // rows past D are zero (TMA fill)
+          if (d < B->D) {
+            float4* dst = reinterpret_cast<float4*>(B->W + d * R + j);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dst[c] = make_float4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          }
+#pragma unroll
+          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = w[c];
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
+        // fp64 Gram of the tile in 4 x 8 blocks (12 shared loads per 32 DFMA)
+        const int RR = R * R;
+        const int t = threadIdx.x - 64;
+        double* gout = B->g1 + static_cast<int64_t>(tile) * RR;
+        const int nbj = R / 8, nblk = (R / 4) * nbj;
+        for (int blk = t; blk < nblk; blk += kBM) {
+          const int a0 = (blk / nbj) * 4, b0 = (blk - (blk / nbj) * nbj) * 8;
+          double acc[4][8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+          for (int rr = 0; rr < kBM; ++rr) {
+            const float* wr = wt + rr * tld;
+            const float4 fa = *reinterpret_cast<const float4*>(wr + a0);
+            const float4 f0 = *reinterpret_cast<const float4*>(wr + b0);
+            const float4 f1 = *reinterpret_cast<const float4*>(wr + b0 + 4);
+            const double xa[4] = {fa.x, fa.y, fa.z, fa.w};
+            const double xb[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[i][j] = fma(xa[i], xb[j], acc[i][j]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gout[(a0 + i) * R + b0 + j] = acc[i][j];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+// [V_hi | V_lo]^T (2R x D bf16) from the fp32 basis, grouped over bases.
+__global__ void __launch_bounds__(kThreads) k_split_vt(const TCBasis* __restrict__ bases, int nb, int first) {
+  const int item = blockIdx.x;
+  const int bi = find_owner(bases, nb, item, [](const TCBasis& b) { return b.vt0; });
+  const TCBasis* B = bases + bi;
+  const int R = B->R;
+  const int64_t n = B->D * R;
+  const int64_t i0 = static_cast<int64_t>(item - B->vt0) * kThreads * 8;
+  const int64_t s0 = first ? B->v_s0 : R, s1 = first ? B->v_s1 : 1;
+  for (int k = 0; k < 8; ++k) {
+    const int64_t e = i0 + k * kThreads + threadIdx.x;
+    if (e >= n) break;
+    const int64_t r = e / B->D, d = e - r * B->D;   // d fastest: coalesced bf16 stores
+    const float v = (first ? B->Vsrc : B->Vout)[d * s0 + r * s1];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    B->V2T[r * B->ldv2 + d] = h;
+    B->V2T[(R + r) * B->ldv2 + d] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
+}  // namespace tc
+}  // namespace dsmz

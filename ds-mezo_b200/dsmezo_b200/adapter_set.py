@@ -95,7 +95,8 @@ class AdapterSet:
 
     def __init__(self, modules: Sequence[ModuleShape], bases: Sequence[BasisShape], rank: int, basis_width: int,
                  factor_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
-                 keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None):
+                 keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
+                 tensor_core_power_iter: bool = True):
         if factor_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("factor and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -132,6 +133,7 @@ class AdapterSet:
         self.H_arena = torch.zeros(max(nh, 1), dtype=act_dtype, device=dev)
         self.V_arena = torch.zeros(max(nv, 1), dtype=torch.float32, device=dev)
         self.layout = layout if layout is not None else device_layout(dev)
+        self._flags = 0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER
         self._build_plan(int(rng_offset_before))
 
     # ------------------------------------------------------------------ views
@@ -195,6 +197,7 @@ class AdapterSet:
         desc.bases = bspecs
         desc.sm_count, desc.max_threads_per_sm = self.layout
         desc.rng_offset_before = rng_offset_before
+        desc.flags = self._flags
         handle = ctypes.c_void_p()
         check(L.dsmz_plan_create(ctypes.byref(desc), ctypes.byref(handle)), "dsmz_plan_create")
         self._plan = handle
@@ -218,6 +221,15 @@ class AdapterSet:
 
     def _stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
+
+    @property
+    def uses_tensor_cores(self) -> bool:
+        """True when the power iteration runs on tcgen05 tensor cores."""
+        return bool(lib().dsmz_plan_uses_tensor_cores(self._plan))
+
+    def device_error(self) -> int:
+        """Reads and clears the device error word (synchronises the stream)."""
+        return int(lib().dsmz_plan_device_error(self._plan, self._stream()))
 
     def launch_count(self, num_iters: int) -> int:
         return int(lib().dsmz_plan_launch_count(self._plan, num_iters))

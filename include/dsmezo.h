@@ -169,7 +169,12 @@ typedef struct dsmz_plan_desc {
   int32_t max_threads_per_sm;
   uint64_t rng_offset_before;           /* generator advance of the draws that precede
                                            these modules (other ranks' modules); 0 on 1 GPU */
+  uint32_t flags;                       /* DSMZ_PLAN_* bits */
 } dsmz_plan_desc;
+
+/* Power iteration on CUDA cores (fp32 FFMA) even where the tcgen05 path applies. The
+ * tcgen05 path needs bf16 activations, D a multiple of 8 and R a multiple of 16. */
+#define DSMZ_PLAN_SIMT_POWER_ITER 1u
 
 typedef struct dsmz_plan dsmz_plan;
 
@@ -185,6 +190,12 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* plan, int32_t num_iters);  /* ke
  * (one async copy from host memory the plan keeps). Call once before the first step. */
 int dsmz_plan_bind(dsmz_plan* plan, void* device_tables, size_t table_bytes,
                    void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
+/* 1 when the plan runs the power iteration on tcgen05 tensor cores, 0 on CUDA cores. */
+int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* plan);
+/* Reads and clears the plan's device error word (synchronises the stream): nonzero when a
+ * tensor-core kernel gave up on a barrier wait after its time limit. */
+int32_t dsmz_plan_device_error(const dsmz_plan* plan, dsmz_stream_t stream);
 
 /* Phase 1 (ds_mezo/controller.py:165-176): power iteration of every basis. */
 int dsmz_step_power_iteration(const dsmz_plan* plan, int32_t num_iters, float norm_floor, dsmz_stream_t stream);
@@ -221,7 +232,8 @@ enum dsmz_kernel_id {
   DSMZ_KID_GRAM = 9,       /* Gram of the Kalman-updated momentum */
   DSMZ_KID_NS_SOLVE = 10,  /* Newton-Schulz in Gram space */
   DSMZ_KID_APPLY = 11,     /* Kalman update + param -= eta X */
-  DSMZ_NUM_KIDS = 12
+  DSMZ_KID_PI_SPLIT = 12,  /* [V_hi | V_lo]^T for the tensor-core products */
+  DSMZ_NUM_KIDS = 13
 };
 int dsmz_plan_set_probe(dsmz_plan* plan, int32_t kernel, void** start_events, void** stop_events,
                         int32_t capacity);

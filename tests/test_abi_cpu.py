@@ -72,7 +72,7 @@ def test_generator_layout(L, n, sm, mt):
     assert L.dsmz_randn_offset_increment(0, sm, mt) == 0
 
 
-def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None):
+def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None, h_dtype=1):
     from dsmezo_b200 import _lib, transformer_adapter_shapes
     mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
     specs = (_lib.ModuleSpec * len(mods))()
@@ -84,7 +84,7 @@ def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None
         s.d_out, s.d_in, s.r, s.ld_A, s.ld_B, s.basis, s.layer = m.d_out, m.d_in, rank, rank, m.d_in, m.basis, m.layer
     bs = (_lib.BasisSpec * len(bases))()
     for i, b in enumerate(bases):
-        bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = fake, 1, b.T, b.D, b.D, fake, rank
+        bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = fake, h_dtype, b.T, b.D, b.D, fake, rank
     if bad == "rank":
         specs[3].r = 200
     if bad == "basis":
@@ -97,15 +97,18 @@ def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None
     return mods, d
 
 
-def test_plan_create_host_only(L):
+@pytest.mark.parametrize("rank,h_dtype,tc", [(8, 1, 0), (16, 1, 1), (16, 0, 0), (64, 1, 1)])
+def test_plan_create_host_only(L, rank, h_dtype, tc):
     from dsmezo_b200 import draw_increments
-    mods, d = _fake_set()
+    mods, d = _fake_set(rank=rank, h_dtype=h_dtype)
     h = ctypes.c_void_p()
     assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
     try:
         assert L.dsmz_plan_table_bytes(h) > 0 and L.dsmz_plan_workspace_bytes(h) > 0
-        assert L.dsmz_plan_rng_increment(h) == sum(draw_increments(mods, 8, 8, 148, 2048))
-        assert L.dsmz_plan_launch_count(h, 3) == 3 * 8 + 7
+        assert L.dsmz_plan_rng_increment(h) == sum(draw_increments(mods, rank, rank, 148, 2048))
+        # tcgen05 power iteration for bf16 activations and R a multiple of 16
+        assert L.dsmz_plan_uses_tensor_cores(h) == tc
+        assert L.dsmz_plan_launch_count(h, 3) == 3 * 9 + 7
         # stepping an unbound plan is an error, not a launch
         assert L.dsmz_step_update(h, 0.0, 0.0, 0.0, 0.0, 0.0, None, None) == 1
         assert b"not bound" in L.dsmz_last_error()
