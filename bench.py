@@ -54,16 +54,6 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def layer_ranges(layers, world):
-    base, extra = divmod(layers, world)
-    out, s = [], 0
-    for r in range(world):
-        n = base + (1 if r < extra else 0)
-        out.append(range(s, s + n))
-        s += n
-    return out
-
-
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, gpus):
@@ -79,7 +69,7 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-i", ",".join(str(g) for g in self.gpus), "-lms", "200"],
+                                          "-i", ",".join(str(g) for g in self.gpus), "-lms", "100"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -119,22 +109,18 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- setup
-def build_set(cfg, lrange, device, rank_offset, layout, keep_ns=False):
-    from dsmezo_b200 import AdapterSet, transformer_adapter_shapes
-    mods, bases = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"],
-                                             layer_range=lrange)
-    aset = AdapterSet(mods, bases, cfg["rank"], cfg["rank"], factor_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
-                      device=device, keep_ns_output=keep_ns, rng_offset_before=rank_offset, layout=layout)
+def init_set(aset, cfg, device, layer0):
+    """Seeded synthetic state: factors and momentum ~ N(0,1), var = eps^2, bases = QR of a
+    Gaussian, activations N(0,1) x lognormal(0,1) channel scales."""
     g = torch.Generator(device=device)
-    g.manual_seed(cfg["seed"] * 1000 + (lrange.start if lrange else 0))
-    aset.factors.copy_(torch.randn(aset.numel, generator=g, device=device))
-    aset.mu.normal_(generator=g)                  # update matrices ~ N(0,1)
+    g.manual_seed(cfg["seed"] * 1000 + layer0)
+    aset.factors[: aset.numel].copy_(torch.randn(aset.numel, generator=g, device=device))
+    aset.mu.normal_(generator=g)
     aset.var.fill_(EPS ** 2)
     for b, s in enumerate(aset.bases):
         aset.V(b).copy_(torch.linalg.qr(torch.randn(s.D, cfg["rank"], generator=g, device=device))[0])
         scale = torch.exp(torch.randn(s.D, generator=g, device=device))
         aset.H(b).copy_(torch.randn(s.T, s.D, generator=g, device=device) * scale)
-    return aset
 
 
 def alg_bytes(aset, cfg):
@@ -157,14 +143,6 @@ def alg_bytes(aset, cfg):
         "gram": N * 12,                            # read mu, var, z
         "apply": N * (2 * f + 20),                 # read p, mu, var, z; write p, mu, var
     }
-
-
-def step_alg_bytes(aset):
-    """Compulsory bytes of one step: adapter phase 4f+16 per element (read p, mu, var;
-    write p, mu, var, pos, neg) + three passes over every activation."""
-    f = aset.factors.element_size()
-    hb = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
-    return aset.numel * (4 * f + 16) + 3 * hb
 
 
 # ----------------------------------------------------------------------------- CPU oracle
@@ -199,7 +177,7 @@ def cpu_oracle_sample(cfg, layers_in_sample=1, steps=1, warmup=0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="7b", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -226,42 +204,39 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         pg = dist.group.WORLD
-    from dsmezo_b200 import ZOController, device_layout, draw_increments, transformer_adapter_shapes
+    from dsmezo_b200 import ShardedStep
     from dsmezo_b200._lib import KERNEL_IDS, lib
-    layout = device_layout(device)
-    ranges = layer_ranges(cfg["layers"], world)
-    all_mods, _ = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"])
-    incs = draw_increments(all_mods, cfg["rank"], cfg["rank"], *layout)
-    per_layer = len(all_mods) // cfg["layers"]
-    before = sum(incs[: ranges[rank].start * per_layer])
-    aset = build_set(cfg, ranges[rank], device, before, layout)
     gen = torch.Generator(device=device)
     gen.manual_seed(cfg["seed"])
-    ctl = ZOController(aset, EPS, TOTAL_STEPS, gen, schedule=cfg["schedule"], process_group=pg,
-                       rng_increment_total=sum(incs))
-    # all-gather target: every rank's factor arena, padded to the largest shard
-    gather = None
-    if world > 1:
-        import torch.distributed as dist
-        sizes = []
-        for lr in ranges:
-            ms, _ = transformer_adapter_shapes(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["tokens"],
-                                               layer_range=lr)
-            sizes.append(sum(m.d_out * cfg["rank"] + cfg["rank"] * m.d_in for m in ms))
-        cap = max(sizes)
-        send = torch.zeros(cap, dtype=aset.factors.dtype, device=device)
-        gather = (send, torch.empty(cap * world, dtype=aset.factors.dtype, device=device))
+    sstep = ShardedStep(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"], cfg["tokens"], eps=EPS,
+                        total_steps=TOTAL_STEPS, generator=gen, factor_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
+                        schedule=cfg["schedule"], device=device, process_group=pg)
+    aset = sstep.aset
+    init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
+    gather_events = []
 
-    def step():
-        ctl.perturb()
-        dd = float(torch.randn((), generator=dd_gen)) * 10.0
-        ctl.update(dd)
-        if gather is not None:
-            import torch.distributed as dist
-            send, recv = gather
-            send[: aset.numel].copy_(aset.factors)
-            dist.all_gather_into_tensor(recv, send, group=pg)
+    def step(record=False):
+        sstep.perturb()
+        if world > 1:
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+            sstep.gather("pos", "neg")              # the +/- adapters the scoring pass needs
+            if record:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+        dd = sstep.broadcast_dd(float(torch.randn((), generator=dd_gen)) * 10.0)
+        sstep.update(dd)
+        if world > 1:
+            if record:
+                e2 = torch.cuda.Event(enable_timing=True)
+                e2.record()
+            sstep.gather("factors")                 # updated adapters for the next rollout
+            if record:
+                e3 = torch.cuda.Event(enable_timing=True)
+                e3.record()
+                gather_events.append((e0, e1, e2, e3))
 
     def barrier():
         if world > 1:
@@ -298,7 +273,7 @@ def main():
     with ClockSampler([local_rank] if world == 1 else list(range(world))) as clk:
         t_start.record()
         for _ in range(args.steps):
-            step()
+            step(record=True)
         t_stop.record()
         torch.cuda.synchronize()
         barrier()
@@ -310,6 +285,8 @@ def main():
         if cnt:
             tot = sum(st_ev[i].elapsed_time(sp_ev[i]) for i in range(cnt))
             kern[name] = {"launches": cnt, "total_ms": tot, "avg_ms": tot / cnt}
+    gather_ms = (sum(a.elapsed_time(b) + c.elapsed_time(d) for a, b, c, d in gather_events) / len(gather_events)
+                 if gather_events else 0.0)
     ms = ms_local
     if world > 1:
         import torch.distributed as dist
@@ -332,15 +309,14 @@ def main():
         e0.record()
         for _ in range(n_e2e):
             aset.H_arena.copy_(host_H, non_blocking=True)
-            ctl.perturb()
+            sstep.perturb()
             host_out.copy_(aset.kalman_sums(), non_blocking=True)
-            dd = float(torch.randn((), generator=dd_gen)) * 10.0
-            ctl.update(dd)
-            if gather is not None:
-                import torch.distributed as dist
-                send, recv = gather
-                send[: aset.numel].copy_(aset.factors)
-                dist.all_gather_into_tensor(recv, send, group=pg)
+            if world > 1:
+                sstep.gather("pos", "neg")
+            dd = sstep.broadcast_dd(float(torch.randn((), generator=dd_gen)) * 10.0)
+            sstep.update(dd)
+            if world > 1:
+                sstep.gather("factors")
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -371,7 +347,10 @@ def main():
         if k in ab:
             v["alg_GBps"] = ab[k] / (v["avg_ms"] * 1e-3) / 1e9
             v["frac_hbm"] = v["alg_GBps"] / hbm
-    step_bytes = step_alg_bytes(aset) * (world if world > 1 else 1)
+    # whole model: every rank's factors and activations
+    f = aset.factors.element_size()
+    act_layer = cfg["tokens"] * (3 * cfg["hidden"] + cfg["inter"]) * aset.H_arena.element_size()
+    step_bytes = sum(sstep.layout.sizes) * (4 * f + 16) + 3 * act_layer * cfg["layers"]
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
@@ -387,12 +366,13 @@ def main():
                    "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
                    "factor_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
                    "power_iters": 3, "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (activations %.2f GB per step)" %
+                   "l2": "inputs larger than L2 (activations %.2f GB per step per GPU)" %
                          (sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9)},
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1)},
         "kernels": kern,
+        "allgather_ms_per_step": gather_ms,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": aset.launch_count(3) * args.steps,

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
 }
-// 2-D TMA load (no multicast) completing on `bar`; x is the innermost coordinate.
+// 2-D TMA load into this CTA's shared memory, completing on `bar`; x is the innermost coordinate.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

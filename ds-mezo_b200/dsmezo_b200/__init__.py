@@ -12,6 +12,8 @@ from . import kernels  # noqa: F401
 from ._lib import DsmzError, lib  # noqa: F401
 from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ZOController, device_layout,  # noqa: F401
                           draw_increments, kalman_beta_q, transformer_adapter_shapes)
+from .sharding import ShardedStep, ShardLayout, partition_layers, shard_layout  # noqa: F401
 
 __all__ = ["kernels", "AdapterSet", "ZOController", "ModuleShape", "BasisShape", "transformer_adapter_shapes",
-           "draw_increments", "device_layout", "kalman_beta_q", "DsmzError", "lib"]
+           "draw_increments", "device_layout", "kalman_beta_q", "DsmzError", "lib", "ShardedStep", "ShardLayout",
+           "partition_layers", "shard_layout"]

@@ -96,7 +96,7 @@ class AdapterSet:
     def __init__(self, modules: Sequence[ModuleShape], bases: Sequence[BasisShape], rank: int, basis_width: int,
                  factor_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
-                 tensor_core_power_iter: bool = True):
+                 tensor_core_power_iter: bool = True, capacity: int = 0):
         if factor_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("factor and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -115,10 +115,14 @@ class AdapterSet:
             self.offB.append(n)
             n += r * m.d_in
         self.numel = n
+        # Factor arenas may be padded to `capacity` elements so that every rank of a
+        # layer-sharded set sends equal-sized buffers to an all-gather.
+        cap = max(n, int(capacity))
+        self.capacity = cap
         dev = self.device
-        self.factors = torch.zeros(n, dtype=factor_dtype, device=dev)
-        self.pos = torch.zeros(n, dtype=factor_dtype, device=dev)
-        self.neg = torch.zeros(n, dtype=factor_dtype, device=dev)
+        self.factors = torch.zeros(cap, dtype=factor_dtype, device=dev)
+        self.pos = torch.zeros(cap, dtype=factor_dtype, device=dev)
+        self.neg = torch.zeros(cap, dtype=factor_dtype, device=dev)
         self.mu = torch.zeros(n, dtype=torch.float32, device=dev)
         self.var = torch.zeros(n, dtype=torch.float32, device=dev)
         self.z = torch.zeros(n, dtype=torch.float32, device=dev)
@@ -303,8 +307,8 @@ class ZOController:
         self.aset.power_iteration(self.power_iters, self.norm_floor)
         self.aset.perturb(seed, off, self.eps, self.beta, self.q, self.norm_floor)
         if self.pg is not None:
-            import torch.distributed as dist
-            dist.all_reduce(self.aset.kalman_sums(), group=self.pg)
+            from .sharding import allreduce_sums
+            allreduce_sums(self.aset.kalman_sums(), self.pg)
 
     def update(self, dd: float):
         self.aset.update(dd, self.beta, self.q, self.eta, self.norm_floor, self.schedule)

@@ -1,0 +1,161 @@
+"""Layer-sharded optimizer step over one process per GPU.
+
+The step shards by layer (each matrix's work is independent); two things cross ranks:
+
+* the two Kalman sums (sum z*mu, sum z^2*var) are sums over every adapter of the model
+  (ds_mezo/controller.py:262-274), so they are all-reduced between the perturbation and
+  update phases;
+* the random draws: every rank keeps the same torch generator and places its modules'
+  draws after the draws of all lower-ranked modules (a prefix sum of the per-module
+  generator increments), so a sharded step draws exactly what one GPU would.
+
+After the phases, the rollout needs the full adapter set: pos/neg copies for scoring and
+the updated factors for the next rollout. Each rank's arenas are padded to the largest
+shard, so each all-gather is one NCCL call on contiguous buffers.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from .adapter_set import AdapterSet, ZOController, device_layout, draw_increments, transformer_adapter_shapes
+
+
+def partition_layers(layers: int, world: int, weights: Optional[Sequence[float]] = None) -> List[range]:
+    """Contiguous layer ranges, one per rank, balanced by per-layer weight (bytes).
+
+    Equal weights give sizes differing by at most one layer, larger ranges first."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    if weights is None:
+        base, extra = divmod(layers, world)
+        out, s = [], 0
+        for r in range(world):
+            n = base + (1 if r < extra else 0)
+            out.append(range(s, s + n))
+            s += n
+        return out
+    w = list(weights)
+    if len(w) != layers:
+        raise ValueError("one weight per layer")
+    total = float(sum(w))
+    out, s = [], 0
+    for r in range(world):
+        if r == world - 1:
+            out.append(range(s, layers))
+            break
+        target = total * (r + 1) / world
+        e, acc = s, float(sum(w[:s]))
+        while e < layers and acc + w[e] / 2.0 <= target:
+            acc += w[e]
+            e += 1
+        out.append(range(s, e))
+        s = e
+    return out
+
+
+# ----------------------------------------------------------------------------- collectives
+def allreduce_sums(t: torch.Tensor, group=None) -> torch.Tensor:
+    """In-place sum of the rank-local Kalman sums over the group."""
+    import torch.distributed as dist
+    dist.all_reduce(t, group=group)
+    return t
+
+
+def broadcast_scalar(x: float, group=None, src: int = 0, device="cpu") -> float:
+    """The scoring rank's scalar (dd) on every rank."""
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.broadcast(t, src=src, group=group)
+    return float(t.item())
+
+
+def gather_arena(out: torch.Tensor, local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather of equal-sized (padded) arenas into `out`, rank-major."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(out, local, group=group)
+    return out
+
+
+@dataclass
+class ShardLayout:
+    ranges: List[range]
+    modules_per_layer: int
+    increments: List[int]          # per module of the whole model, controller order
+    sizes: List[int]               # factor elements per rank
+    capacity: int                  # largest shard
+
+    def rng_offset_before(self, rank: int) -> int:
+        return sum(self.increments[: self.ranges[rank].start * self.modules_per_layer])
+
+    @property
+    def rng_increment_total(self) -> int:
+        return sum(self.increments)
+
+
+def shard_layout(layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, world: int,
+                 sm_count: int, max_threads_per_sm: int) -> ShardLayout:
+    mods, _ = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
+    per_layer = len(mods) // layers
+    incs = draw_increments(mods, rank_r, rank_r, sm_count, max_threads_per_sm)
+    ranges = partition_layers(layers, world)
+    sizes = []
+    for lr in ranges:
+        ms = mods[lr.start * per_layer: lr.stop * per_layer]
+        sizes.append(sum(m.d_out * rank_r + rank_r * m.d_in for m in ms))
+    return ShardLayout(ranges, per_layer, incs, sizes, max(sizes) if sizes else 0)
+
+
+class ShardedStep:
+    """One rank's part of the layer-sharded step (all of it when world == 1)."""
+
+    def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
+                 eps: float, total_steps: int, generator: torch.Generator, factor_dtype=torch.bfloat16,
+                 act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3):
+        import torch.distributed as dist
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if process_group is not None else 1
+        self.rank = dist.get_rank(process_group) if process_group is not None else 0
+        layout = device_layout(device)
+        self.layout = shard_layout(layers, hidden, inter, kv, rank_r, tokens, self.world, *layout)
+        lr = self.layout.ranges[self.rank]
+        mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)
+        self.aset = AdapterSet(mods, bases, rank_r, rank_r, factor_dtype=factor_dtype, act_dtype=act_dtype,
+                               device=device, rng_offset_before=self.layout.rng_offset_before(self.rank),
+                               layout=layout, capacity=self.layout.capacity)
+        self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
+                                process_group=process_group if self.world > 1 else None,
+                                rng_increment_total=self.layout.rng_increment_total)
+        cap = self.layout.capacity
+        self.gathered = {name: torch.empty(cap * self.world, dtype=factor_dtype, device=device)
+                         for name in ("factors", "pos", "neg")} if self.world > 1 else None
+
+    # ------------------------------------------------------------------ phases
+    def perturb(self):
+        """Power iteration, perturbation, pos/neg; Kalman sums all-reduced across ranks."""
+        self.ctl.perturb()
+
+    def broadcast_dd(self, dd: float, src: int = 0) -> float:
+        """The projected-gradient scalar dd = (L+ - L-) / (2 eps) from the scoring rank."""
+        if self.world == 1:
+            return float(dd)
+        return broadcast_scalar(dd, self.pg, src, self.aset.device)
+
+    def update(self, dd: float):
+        self.ctl.update(dd)
+
+    def gather(self, *names: str):
+        """All-gathers the named arenas ('factors', 'pos', 'neg') into full-model buffers
+        laid out rank by rank (each rank's slice padded to the largest shard)."""
+        if self.world == 1:
+            return {n: getattr(self.aset, n) for n in names}
+        for n in names:
+            gather_arena(self.gathered[n], getattr(self.aset, n), self.pg)
+        return {n: self.gathered[n] for n in names}
+
+    def full_view(self, buf: torch.Tensor, rank: int) -> torch.Tensor:
+        """Rank `rank`'s factor elements inside a gathered buffer."""
+        cap = self.layout.capacity
+        return buf[rank * cap: rank * cap + self.layout.sizes[rank]]

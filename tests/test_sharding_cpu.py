@@ -1,0 +1,164 @@
+"""Layer sharding on CPU: partitions, Philox offsets across ranks, and the collectives of
+the sharded step under gloo with world_size 2, including a rank that dies before the
+Kalman all-reduce (detected on the host, no GPU involved)."""
+import ctypes
+import datetime
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _paths():
+    for p in (ROOT, os.path.join(ROOT, "ds-mezo_b200"), os.path.join(ROOT, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+_paths()
+
+
+@pytest.fixture(scope="module")
+def L():
+    from dsmezo_b200 import build
+    build.build()
+    from dsmezo_b200 import _lib
+    return _lib.lib()
+
+
+@pytest.mark.parametrize("layers,world", [(28, 1), (28, 2), (28, 8), (80, 8), (4, 3), (3, 4)])
+def test_partition_is_contiguous_and_balanced(layers, world):
+    from dsmezo_b200 import partition_layers
+    parts = partition_layers(layers, world)
+    assert len(parts) == world
+    assert parts[0].start == 0 and parts[-1].stop == layers
+    for a, b in zip(parts, parts[1:]):
+        assert a.stop == b.start
+    sizes = [len(p) for p in parts]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_partition_by_weight():
+    from dsmezo_b200 import partition_layers
+    parts = partition_layers(6, 2, [1, 1, 1, 1, 1, 10])
+    assert [len(p) for p in parts] == [5, 1]
+
+
+def _plan_increment(L, mods, bases_all, rank_r, layer_range, before, per_layer):
+    """rng increment of a host-only plan over the modules of `layer_range`."""
+    from dsmezo_b200 import _lib
+    sel = mods[layer_range.start * per_layer: layer_range.stop * per_layer]
+    b0 = layer_range.start * 4
+    specs = (_lib.ModuleSpec * len(sel))()
+    for i, m in enumerate(sel):
+        s = specs[i]
+        for f in ("A", "B", "pos_A", "pos_B", "neg_A", "neg_B", "mu_A", "mu_B", "var_A", "var_B", "z_A", "z_B"):
+            setattr(s, f, 0x10000)
+        s.d_out, s.d_in, s.r, s.ld_A, s.ld_B = m.d_out, m.d_in, rank_r, rank_r, m.d_in
+        s.basis, s.layer = m.basis - b0, m.layer
+    nb = len(layer_range) * 4
+    bs = (_lib.BasisSpec * nb)()
+    for i in range(nb):
+        b = bases_all[b0 + i]
+        bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = 0x10000, 1, b.T, b.D, b.D, 0x10000, rank_r
+    d = _lib.PlanDesc()
+    d.factor_dtype, d.num_modules, d.modules, d.num_bases, d.bases = 1, len(sel), specs, nb, bs
+    d.sm_count, d.max_threads_per_sm, d.rng_offset_before = 148, 2048, before
+    h = ctypes.c_void_p()
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
+    inc = L.dsmz_plan_rng_increment(h)
+    L.dsmz_plan_destroy(h)
+    return inc
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_rank_offsets_chain_to_the_single_gpu_stream(L, world):
+    """Each rank's draws start where the previous rank's end, so the sharded step draws
+    the same Gaussians as one GPU (the reference's per-module torch.randn order)."""
+    from dsmezo_b200 import shard_layout, transformer_adapter_shapes
+    layers, rank_r = 8, 64
+    lay = shard_layout(layers, 3584, 18944, 512, rank_r, 4096, world, 148, 2048)
+    mods, bases = transformer_adapter_shapes(layers, 3584, 18944, 512, 4096)
+    total = _plan_increment(L, mods, bases, rank_r, range(layers), 0, 7)
+    assert total == lay.rng_increment_total
+    end = 0
+    for r in range(world):
+        before = lay.rng_offset_before(r)
+        assert before == end
+        end = before + _plan_increment(L, mods, bases, rank_r, lay.ranges[r], before, 7)
+    assert end == total
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, q):
+    _paths()
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        from dsmezo_b200.sharding import allreduce_sums, broadcast_scalar, gather_arena
+        if mode == "ok":
+            sums = torch.tensor([1.5 * (rank + 1), 2.0 ** rank], dtype=torch.float64)
+            allreduce_sums(sums)
+            dd = broadcast_scalar(3.25 if rank == 0 else -1.0)
+            cap = 6
+            local = torch.full((cap,), float(rank + 1))
+            local[4 + rank:] = 0.0                      # ranks of unequal size, padded
+            out = torch.empty(cap * world)
+            gather_arena(out, local)
+            q.put((rank, "ok", sums.tolist(), dd, out.tolist()))
+        else:
+            if rank == 1:
+                os._exit(3)                              # dies before the all-reduce
+            sums = torch.ones(2, dtype=torch.float64)
+            try:
+                allreduce_sums(sums)
+                q.put((rank, "no error", None, None, None))
+            except Exception as e:                      # peer gone: the collective fails
+                q.put((rank, "detected", type(e).__name__, None, None))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(mode, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(world if mode == "ok" else 1):
+        results.append(q.get(timeout=60))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return sorted(results)
+
+
+def test_collectives_of_the_sharded_step_gloo():
+    res = _run("ok")
+    for rank, status, sums, dd, out in res:
+        assert status == "ok"
+        assert sums == [1.5 + 3.0, 1.0 + 2.0]
+        assert dd == 3.25
+        assert out == [1.0] * 4 + [0.0] * 2 + [2.0] * 5 + [0.0]
+
+
+def test_rank_failure_is_detected_on_the_host():
+    res = _run("fail")
+    assert res[0][0] == 0 and res[0][1] == "detected"
