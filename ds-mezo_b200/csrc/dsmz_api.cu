@@ -51,14 +51,13 @@ int seg_vectors(int r) {
 
 int gram_rb(int r) { return r <= 64 ? 4 : 8; }
 
-size_t gram_smem(int r, bool round2 = false) {
+size_t gram_smem(int r) {
   const int RB = gram_rb(r);
   const int tpr = (r + RB - 1) / RB;
   const int rp = tpr * RB;
   const int ngroups = kThreads / (tpr * tpr);
   const size_t tv = static_cast<size_t>(tile_vectors(r));
-  const size_t xs = tv * (rp + 4) * sizeof(float) +
-                    (round2 ? (static_cast<size_t>(r) * pad8(r) + tv * (pad8(r) + 1)) * sizeof(float) : 0);
+  const size_t xs = tv * (rp + 4) * sizeof(float);
   const size_t red = ngroups > 1 ? static_cast<size_t>(ngroups) * rp * rp * sizeof(double) : 0;
   return xs > red ? xs : red;
 }
@@ -72,7 +71,15 @@ size_t perturb_smem(int r, int R, int RC) {
   return (static_cast<size_t>(KW) * pad8(R) + static_cast<size_t>(TV) * (KW + 1) + static_cast<size_t>(TV) * (r + 1)) *
          sizeof(float);
 }
-size_t coef_smem(int R, int RC) { return static_cast<size_t>(R) * RC * sizeof(double); }
+size_t coef_smem(int R, int RC) {
+  const size_t rca = static_cast<size_t>(R < RC ? R : RC);
+  return (static_cast<size_t>(R + 1) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
+}
+size_t ns_smem(int r) { return r <= 64 ? 4 * static_cast<size_t>(r) * r * sizeof(double) : 0; }
+size_t qr_apply_smem(int r) {
+  const size_t r8 = static_cast<size_t>(pad8(r)), tv = static_cast<size_t>(tile_vectors(r));
+  return r * r8 * sizeof(double) + 2 * tv * (r8 + 1) * sizeof(float);
+}
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
 template <typename K>
@@ -265,14 +272,19 @@ void patch_ws_pointers(dsmz_plan* P) {
     float* W = reinterpret_cast<float*>(P->workspace) + b.w_off;
     P->w1[i].mu = W;
     P->w1[i].param = W;
-    P->w2[i].mu = W;          // round 2 overwrites W with Q1 before the apply reads it
+    P->w2[i].mu = W;
     P->w2[i].param = b.Vout;
+    if (P->tc && i < P->tcs.size()) {
+      P->w2[i].v2t = reinterpret_cast<__nv_bfloat16*>(P->workspace + P->tcs[i].v2t);
+      P->w2[i].ldv2 = P->tcs[i].ldv2;
+    } else {
+      P->w2[i].v2t = nullptr;
+    }
   }
 }
 
-// CholeskyQR2 tables of every basis W (D x R): round 1 (Gram of W, R1^-1) and round 2
-// (Q1 = W R1^-1 in place, its Gram, R2^-1, V = Q1 R2^-1). Round-1 segments are 128 rows
-// when the tensor-core W kernel writes their Gram partials.
+// CholeskyQR tables of every basis W (D x R): the Gram segments (128 rows when the
+// tensor-core W kernel writes their fp64 partials) and the apply segments of V = W R^{-1}.
 void add_w_tables(dsmz_plan* P, bool tc_segments) {
   for (size_t i = 0; i < P->bases.size(); ++i) {
     const BasisD& b = P->bases[i];
@@ -286,14 +298,11 @@ void add_w_tables(dsmz_plan* P, bool tc_segments) {
     a.gram_off = static_cast<int64_t>(P->ws.take(a.nseg * rr * sizeof(double)) / sizeof(double));
     a.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
     a.dw_off = static_cast<int64_t>(P->ws.take(3 * rr * sizeof(double)) / sizeof(double));
-    MatD m = a;
+    MatD m = a;                 // apply segments: V = W R^{-1} (fp64 R^{-1} in a's workspace)
     m.segv = seg_vectors(b.R);
     m.nseg = static_cast<int32_t>((b.D + m.segv - 1) / m.segv);
     m.seg0 = P->nwsegsB;
     P->nwsegsB += m.nseg;
-    m.gram_off = static_cast<int64_t>(P->ws.take(m.nseg * rr * sizeof(double)) / sizeof(double));
-    m.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
-    m.p_prev_off = a.p_off;
     P->w1.push_back(a);
     P->w2.push_back(m);
   }
@@ -346,16 +355,14 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   if (P->bases.empty() || iters <= 0) return 0;
   const Tables tb = P->tables();
   const int R = P->R;
-  const size_t gs = gram_smem(R), gs2 = gram_smem(R, true), as = apply_smem(R);
+  const size_t gs = gram_smem(R), qs = qr_apply_smem(R);
   int rc;
   if (gram_rb(R) == 4) {
     if ((rc = set_smem(k_gram<0, 4, double>, gs))) return rc;
-    if ((rc = set_smem(k_gram<2, 4, float>, gs2))) return rc;
   } else {
     if ((rc = set_smem(k_gram<0, 8, double>, gs))) return rc;
-    if ((rc = set_smem(k_gram<2, 8, float>, gs2))) return rc;
   }
-  if ((rc = set_smem(k_apply<0, 1>, as))) return rc;
+  if ((rc = set_smem(k_qr_apply, qs))) return rc;
   if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
   const KalmanIn kin{};
   const int nb = static_cast<int>(P->bases.size());
@@ -390,8 +397,8 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_W, s);
     DSMZ_LAUNCHED("power iteration W = H^T Y");
     }
-    // CholeskyQR2 of W: round 1 from the fp64 Gram of W (written by the tensor-core W kernel,
-    // or by k_gram here), round 2 from the fp32 Gram of the rounded Q1 = W R1^-1.
+    // CholeskyQR of W from its exact fp64 Gram (written by the tensor-core W kernel, or
+    // by k_gram here); V = W R^{-1} accumulated in fp64, with the bf16 pair for the next Y.
     if (!P->tc) {
       P->probe_begin(DSMZ_KID_PI_GRAM, s);
       if (gram_rb(R) == 4) k_gram<0, 4, double><<<P->nwsegsA, kThreads, gs, s>>>(tb, tb.wA, nb, kin);
@@ -404,27 +411,11 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wA, nb, bpm);
     k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_);
     P->probe_end(DSMZ_KID_PI_CHOL, s);
-    DSMZ_LAUNCHED("power iteration Cholesky 1");
-    P->probe_begin(DSMZ_KID_PI_GRAM, s);
-    if (gram_rb(R) == 4) k_gram<2, 4, float><<<P->nwsegsB, kThreads, gs2, s>>>(tb, tb.wB, nb, kin);
-    else k_gram<2, 8, float><<<P->nwsegsB, kThreads, gs2, s>>>(tb, tb.wB, nb, kin);
-    P->probe_end(DSMZ_KID_PI_GRAM, s);
-    DSMZ_LAUNCHED("power iteration Q1 and its Gram");
-    P->probe_begin(DSMZ_KID_PI_CHOL, s);
-    k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wB, nb, bpm);
-    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wB, floor_);
-    P->probe_end(DSMZ_KID_PI_CHOL, s);
-    DSMZ_LAUNCHED("power iteration Cholesky 2");
+    DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
-    k_apply<0, 1><<<P->nwsegsB, kThreads, as, s>>>(tb, tb.wB, nb, kin, 0.f, DSMZ_F32);
+    k_qr_apply<<<P->nwsegsB, kThreads, qs, s>>>(tb, tb.wB, nb);
     P->probe_end(DSMZ_KID_PI_APPLY, s);
-    DSMZ_LAUNCHED("power iteration V = Q1 R2^-1");
-    if (P->tc && it + 1 < iters) {
-      P->probe_begin(DSMZ_KID_PI_SPLIT, s);
-      tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 0);
-      P->probe_end(DSMZ_KID_PI_SPLIT, s);
-      DSMZ_LAUNCHED("power iteration basis split");
-    }
+    DSMZ_LAUNCHED("power iteration V = W R^-1");
   }
   return 0;
 }
@@ -482,7 +473,8 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
-  k_ns_solve<<<nm, kThreads, 0, s>>>(tb, tb.mats, ns);
+  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
+  k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, tb.mats, ns);
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
@@ -678,9 +670,9 @@ uint64_t dsmz_plan_rng_increment(const dsmz_plan* p) { return p ? p->rng_increme
 int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   if (!p) return 0;
   int32_t n = 0;
-  // per iteration: Y, W, [Gram of W on CUDA cores | basis split on the tensor-core path],
-  // 2 x (partial sums + Cholesky), Q1 + Gram, V
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * 9;
+  // per iteration: Y, W, [Gram of W on the CUDA-core path], partial sums, Cholesky, V;
+  // plus the first bf16 split of the caller's basis on the tensor-core path
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->tc ? 5 : 6) + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 4 + 3;
   return n;
 }
@@ -854,7 +846,8 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
     k_gram<0, 8, double><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
   }
   DSMZ_LAUNCHED("zo_muon_update Gram");
-  k_ns_solve<<<1, kThreads, 0, s>>>(tb, tb.mats, make_ns(schedule, norm_floor));
+  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
+  k_ns_solve<<<1, kThreads, ns_smem(r), s>>>(tb, tb.mats, make_ns(schedule, norm_floor));
   DSMZ_LAUNCHED("zo_muon_update solve");
   if ((rc = set_smem(k_apply<0, 0>, as))) return rc;
   k_apply<0, 0><<<P.nsegs, kThreads, as, s>>>(tb, tb.mats, 1, kin, eta, param_dtype);

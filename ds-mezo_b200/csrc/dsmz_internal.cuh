@@ -25,7 +25,8 @@ struct MatD {
   int64_t gram_off;           // doubles: nseg * r*r Gram partials
   int64_t p_off;              // floats: r*r apply matrix (fp32), then 4 floats of scalars
   int64_t dw_off;             // doubles: 4 * r*r fp64 solve workspace
-  int64_t p_prev_off;         // floats: r*r matrix applied in place before the Gram (QR round 2)
+  __nv_bfloat16* v2t;         // power-iteration W only: [V_hi | V_lo]^T output (NULL: none)
+  int64_t ldv2;
 };
 
 struct ModD {

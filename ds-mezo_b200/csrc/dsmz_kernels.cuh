@@ -51,30 +51,30 @@ __host__ __device__ inline int pad4(int r) { return (r + 3) & ~3; }
 __host__ __device__ inline int pad8(int r) { return (r + 7) & ~7; }
 
 // out[v][c] = sum_{a<K} X[v*xld + a] * P[a*pld + c] for v < nv, c < nc, both operands in
-// shared memory. Each thread owns 4 vectors x 8 columns (32 fp32 accumulators) and reads a
-// P row segment as two float4 (pld % 4 == 0, columns zero-padded to a multiple of 8), so
-// the loop issues 6 shared loads per 32 FMAs. X needs ceil(nv/4)*4 readable rows; an odd
-// xld keeps the four row reads of a warp on distinct banks. sink(v, c0, acc) takes the 8
-// outputs of vector v starting at column c0.
+// shared memory. Each thread owns 4 vectors x 8 columns (32 fp32 accumulators): columns
+// 4cb..4cb+3 and pld/2+4cb..+3, so the eight column blocks of a warp read one contiguous
+// 128-byte run of a P row per float4 load (no bank conflicts). pld % 8 == 0 and columns
+// padded with zeros to pld; X needs ceil(nv/4)*4 readable rows, and an odd xld keeps the
+// four row reads of a warp on distinct banks. sink(v, c, value) takes each output.
 template <typename Sink>
 __device__ __forceinline__ void rows_x_mat(const float* __restrict__ X, int xld, const float* __restrict__ P, int pld,
                                            int nv, int K, int nc, Sink sink) {
-  const int cbs = (nc + 7) >> 3;
+  const int cbs = pld >> 3;
+  const int half = pld >> 1;
   const int vbs = (nv + 3) >> 2;
   for (int blk = threadIdx.x; blk < vbs * cbs; blk += kThreads) {
     const int vb = blk / cbs, cb = blk - vb * cbs;
-    const int v0 = vb * 4, c0 = cb * 8;
+    const int v0 = vb * 4, c0 = cb * 4;
     float acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
     const float* x0 = X + v0 * xld;
-    const float* pc = P + c0;
 #pragma unroll 4
     for (int a = 0; a < K; ++a) {
-      const float4 p0 = *reinterpret_cast<const float4*>(pc + a * pld);
-      const float4 p1 = *reinterpret_cast<const float4*>(pc + a * pld + 4);
+      const float4 p0 = *reinterpret_cast<const float4*>(P + a * pld + c0);
+      const float4 p1 = *reinterpret_cast<const float4*>(P + a * pld + half + c0);
       const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -84,8 +84,14 @@ __device__ __forceinline__ void rows_x_mat(const float* __restrict__ X, int xld,
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (v0 + i < nv) sink(v0 + i, c0, acc[i]);
+    for (int i = 0; i < 4; ++i) {
+      if (v0 + i >= nv) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j < 4) ? c0 + j : half + c0 + j - 4;
+        if (c < nc) sink(v0 + i, c, acc[i][j]);
+      }
+    }
   }
 }
 
@@ -117,12 +123,10 @@ __device__ __forceinline__ int64_t vaddr2(const MatD& M, int64_t v, int64_t k) {
 // =====================================================================================
 // Gram partials: for each segment of each matrix, G_seg = sum_v x_v x_v^T (r x r).
 // SRC 0: x = mu (plain). SRC 1: x = Kalman-updated momentum mu2 (controller.py:283-284).
-// SRC 2: x = w P_prev computed in fp32 and written back over w (CholeskyQR round 2: the
-//        Gram of the rounded Q1 = W R1^-1 measures what round 1 left unorthogonal).
 // ACC double: fp64 products and sums. The Gram squares the condition number, and the
 // Newton-Schulz polynomial of an ill-conditioned momentum (a fresh start, where
-// mu_B ~ Zc_B V^T with a square Gaussian Zc_B) and round 1 of the QR need its small
-// eigenvalues intact. ACC float serves the near-orthonormal Q1 of round 2.
+// mu_B ~ Zc_B V^T with a square Gaussian Zc_B) and the CholeskyQR of the power-iteration
+// W need its small eigenvalues intact. ACC float is the fp32-accumulate variant.
 // =====================================================================================
 template <int SRC, int RB, typename ACC>
 __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __restrict__ mats, int nmats,
@@ -138,10 +142,7 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
   const int rp = tpr * RB;
   const int TV = tile_vectors(r);
   const int xld = rp + 4;                                   // 16-byte rows for the float4 Gram loads
-  const int r8 = pad8(r), wld = r8 + 1;
-  float* Pp = reinterpret_cast<float*>(smem_raw);          // SRC 2: r x r8
-  float* ws_ = Pp + (SRC == 2 ? r * r8 : 0);               // SRC 2: raw rows, TV x wld
-  float* xs = ws_ + (SRC == 2 ? TV * wld : 0);             // TV x xld
+  float* xs = reinterpret_cast<float*>(smem_raw);          // TV x xld
   const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
   const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
   const int tid = threadIdx.x;
@@ -150,17 +151,6 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
   const bool active = grp < ngroups;
   KalScal ks{};
   if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
-  if (SRC == 2) {
-    const float* P1 = reinterpret_cast<const float*>(tb.ws) + M.p_prev_off;
-    for (int e = tid; e < r * r8; e += kThreads) {
-      const int a = e / r8, c = e - a * r8;
-      Pp[e] = (c < r) ? P1[a * r + c] : 0.f;
-    }
-    for (int e = tid; e < TV * (rp - r); e += kThreads) {   // padding columns stay zero
-      const int v = e / (rp - r);
-      xs[v * xld + r + (e - v * (rp - r))] = 0.f;
-    }
-  }
 
   ACC acc[RB][RB];
 #pragma unroll
@@ -170,34 +160,7 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
 
   for (int64_t s0 = v0; s0 < v1; s0 += TV) {
     const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
-    if (SRC == 2) {
-      const int n = nv * r;
-      for (int base = tid; base < n; base += kThreads * kUnroll) {
-        float w0[kUnroll];
-        int vv[kUnroll], kk[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int e = base + u * kThreads;
-          elem_vk(M.side, e, r, nv, vv[u], kk[u]);
-          if (e < n) w0[u] = M.mu[vaddr2(M, s0 + vv[u], kk[u])];
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (base + u * kThreads < n) ws_[vv[u] * wld + kk[u]] = w0[u];
-      }
-      __syncthreads();
-      // Q1 = W R1^-1 for the sub-tile, kept for the Gram and written over W
-      rows_x_mat(ws_, wld, Pp, r8, nv, r, r, [&](int v, int c0, const float (&acc)[8]) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int c = c0 + j;
-          if (c < r) {
-            xs[v * xld + c] = acc[j];
-            M.mu[vaddr2(M, s0 + v, c)] = acc[j];
-          }
-        }
-      });
-    } else {
+    {
       const int n = nv * r;
       for (int base = tid; base < n; base += kThreads * kUnroll) {
         float m0[kUnroll], w0[kUnroll], z0[kUnroll];
@@ -358,13 +321,15 @@ struct NSArgs {
 // matrix Pm with X[v,:] = x_v^T Pm for every vector x_v of the matrix.
 // =====================================================================================
 __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ double sh[2 * 16 * 64];
   __shared__ double red[kThreads];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
   const int tid = threadIdx.x;
-  double* dw = reinterpret_cast<double*>(tb.ws) + M.dw_off;
+  // r <= 64: the four r x r matrices live in shared memory; larger r in the fp64 workspace
+  double* dw = (r <= 64) ? reinterpret_cast<double*>(smem_raw) : reinterpret_cast<double*>(tb.ws) + M.dw_off;
   double* G = dw;
   double* P = dw + rr;
   double* S = dw + 2 * rr;
@@ -473,7 +438,124 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
   }
   __syncthreads();
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
-  for (int e = tid; e < rr; e += kThreads) Pm[e] = static_cast<float>(Ri[e]);
+  double* Rd = dw + rr;                       // fp64 copy for the fp64-accumulated apply
+  for (int e = tid; e < rr; e += kThreads) {
+    Pm[e] = static_cast<float>(Ri[e]);
+    Rd[e] = Ri[e];
+  }
+}
+
+// out[v][c] = sum_{a<K} X[v*xld + a] * P[a*pld + c] with fp32 X, fp64 P and fp64 sums,
+// 4 vectors x 8 columns per thread: column pairs 2cb + g*pld/4 (g < 4), so a warp's double2
+// loads of a P row are one contiguous run (pld % 8 == 0, columns zero-padded to pld).
+template <typename Sink>
+__device__ __forceinline__ void rows_x_mat_f64(const float* __restrict__ X, int xld, const double* __restrict__ P,
+                                               int pld, int nv, int K, int nc, Sink sink) {
+  const int cbs = pld >> 3;
+  const int quarter = pld >> 2;
+  const int vbs = (nv + 3) >> 2;
+  for (int blk = threadIdx.x; blk < vbs * cbs; blk += kThreads) {
+    const int vb = blk / cbs, cb = blk - vb * cbs;
+    const int v0 = vb * 4, c0 = cb * 2;
+    double acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    const float* x0 = X + v0 * xld;
+#pragma unroll 2
+    for (int a = 0; a < K; ++a) {
+      double pv[8];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const double2 t = *reinterpret_cast<const double2*>(P + a * pld + g * quarter + c0);
+        pv[2 * g] = t.x;
+        pv[2 * g + 1] = t.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const double x = static_cast<double>(x0[i * xld + a]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fma(x, pv[j], acc[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (v0 + i >= nv) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j >> 1) * quarter + c0 + (j & 1);
+        if (c < nc) sink(v0 + i, c, acc[i][j]);
+      }
+    }
+  }
+}
+
+// =====================================================================================
+// CholeskyQR of the power-iteration W: V = W R^{-1} with fp64 products and sums. With the
+// exact fp64 Gram behind R, one round leaves V orthonormal to fp32 rounding (the second
+// round of CholeskyQR2 only corrects an fp32-accumulated apply). Also writes the bf16
+// pair [V_hi | V_lo]^T that the next tensor-core Y = H V reads (M.v2t, when set).
+// Side A only (W rows are contiguous R-vectors).
+// =====================================================================================
+__global__ void __launch_bounds__(kThreads) k_qr_apply(Tables tb, const MatD* __restrict__ mats, int nmats) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int seg = blockIdx.x;
+  const int mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
+  const MatD M = mats[mi];
+  const int r = static_cast<int>(M.r);
+  const int r8 = pad8(r);
+  const int TV = tile_vectors(r);
+  const int xld = r8 + 1;
+  double* Ps = reinterpret_cast<double*>(smem_raw);            // r x r8 fp64
+  float* xs = reinterpret_cast<float*>(Ps + r * r8);           // TV x xld
+  float* os = xs + TV * xld;                                   // TV x xld
+  const int tid = threadIdx.x;
+  const double* Rd = reinterpret_cast<const double*>(tb.ws) + M.dw_off + static_cast<int64_t>(r) * r;
+  for (int e = tid; e < r * r8; e += kThreads) {
+    const int a = e / r8, c = e - a * r8;
+    Ps[e] = (c < r) ? Rd[a * r + c] : 0.0;
+  }
+  const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
+  const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
+  const float* W = M.mu;
+  float* V = reinterpret_cast<float*>(M.param);
+  __syncthreads();
+  for (int64_t s0 = v0; s0 < v1; s0 += TV) {
+    const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
+    const int n = nv * r;
+    for (int base = tid; base < n; base += kThreads * kUnroll) {
+      float w0[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int e = base + u * kThreads;
+        if (e < n) w0[u] = W[s0 * M.ld + e];          // rows are contiguous: ld == r
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int e = base + u * kThreads;
+        if (e < n) { const int v = e / r; xs[v * xld + (e - v * r)] = w0[u]; }
+      }
+    }
+    __syncthreads();
+    rows_x_mat_f64(xs, xld, Ps, r8, nv, r, r,
+                   [&](int v, int c, double x) { os[v * xld + c] = static_cast<float>(x); });
+    __syncthreads();
+    for (int e = tid; e < n; e += kThreads) {               // V rows, coalesced
+      const int v = e / r;
+      V[s0 * M.ld + e] = os[v * xld + (e - v * r)];
+    }
+    if (M.v2t) {
+      for (int e = tid; e < n; e += kThreads) {             // [V_hi | V_lo]^T, coalesced along d
+        const int c = e / nv, v = e - c * nv;
+        const float x = os[v * xld + c];
+        const __nv_bfloat16 h = __float2bfloat16_rn(x);
+        M.v2t[static_cast<int64_t>(c) * M.ldv2 + s0 + v] = h;
+        M.v2t[static_cast<int64_t>(r + c) * M.ldv2 + s0 + v] = __float2bfloat16_rn(x - __bfloat162float(h));
+      }
+    }
+    __syncthreads();
+  }
 }
 
 // =====================================================================================
@@ -542,11 +624,7 @@ __global__ void __launch_bounds__(kThreads) k_apply(Tables tb, const MatD* __res
       }
     }
     __syncthreads();
-    rows_x_mat(xs, xld, Ps, r8, nv, r, r, [&](int v, int c0, const float (&acc)[8]) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (c0 + j < r) os[v * xld + c0 + j] = acc[j];
-    });
+    rows_x_mat(xs, xld, Ps, r8, nv, r, r, [&](int v, int c, float x) { os[v * xld + c] = x; });
     __syncthreads();
     for (int base = tid; base < n; base += kThreads * kUnroll) {
       float p0[kUnroll];
@@ -604,16 +682,26 @@ __global__ void __launch_bounds__(kThreads) k_bside(Tables tb) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) { abv[i][j] = 0.f; avb[i][j] = 0.f; }
       for (int64_t jb = j0; jb < j1; jb += 32) {
-        for (int e = tid; e < 64 * 32; e += kThreads) {
+        float lb[8], lw[8], lv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {                 // 24 independent loads in flight
+          const int e = tid + u * kThreads;
           const int rr = e >> 5, jj = e & 31;
           const int64_t j = jb + jj;
           const bool ok = (rt + rr < R) && (j < j1);
           const int64_t a = static_cast<int64_t>(rt + rr) * D.b_s0 + j * D.b_s1;
-          Bs[rr][jj] = ok ? ldf(D.Bp, a, D.bdt) : 0.f;
-          Ws[rr][jj] = (ok && with_var) ? D.varB[a] : 0.f;
+          lb[u] = ok ? ldf(D.Bp, a, D.bdt) : 0.f;
+          lw[u] = (ok && with_var) ? D.varB[a] : 0.f;
           const int jv = e >> 6, cc = e & 63;
           const int64_t jv_g = jb + jv;
-          Vs[jv][cc] = (jv_g < j1 && ct + cc < RC) ? V[jv_g * vs0 + static_cast<int64_t>(ct + cc) * vs1] : 0.f;
+          lv[u] = (jv_g < j1 && ct + cc < RC) ? V[jv_g * vs0 + static_cast<int64_t>(ct + cc) * vs1] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int e = tid + u * kThreads;
+          Bs[e >> 5][e & 31] = lb[u];
+          Ws[e >> 5][e & 31] = lw[u];
+          Vs[e >> 6][e & 63] = lv[u];
         }
         __syncthreads();
 #pragma unroll 4
@@ -656,7 +744,8 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   const ModD D = tb.mods[blockIdx.x];
   const int R = D.r, RC = D.rc, RCA = D.rca;
   const int tid = threadIdx.x;
-  double* BVt = reinterpret_cast<double*>(smem_raw);  // RC x R (column-major B V)
+  const int bld = R + 1;                              // padded column stride (bank spread)
+  double* BVt = reinterpret_cast<double*>(smem_raw);  // RC x bld (column-major B V)
   const float* part = reinterpret_cast<const float*>(tb.ws) + D.bpart_off;
   float* ZcB = reinterpret_cast<float*>(tb.ws) + D.coef_off;
   float* Qo = ZcB + static_cast<int64_t>(R) * RC;
@@ -667,7 +756,7 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       svb += part[static_cast<int64_t>(c) * 2 * R * RC + R * RC + e];
     }
     const int i = e / RC, c = e - i * RC;
-    BVt[c * R + i] = sbv;
+    BVt[c * bld + i] = sbv;
     if (MODE == 0) {
       const float g = torch_randn_at(seed, base_off + D.offB, D.thrB, e);
       ZcB[e] = __fmul_rn(g, sqrtf(static_cast<float>(svb)));
@@ -676,12 +765,61 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
     }
   }
   __syncthreads();
-  if (tid < 32) {
+  // Q = QR(B V)[:, :RCA] with a positive diagonal, the factor the reference's modified
+  // Gram-Schmidt produces (ds_mezo/kernels.py:328-340), as CholeskyQR2 in fp64: two rounds of
+  // G = Q^T Q, G = R^T R, Q <- Q R^{-1}, every step parallel over the CTA.
+  if (RCA <= 64) {
+  double* G = BVt + RC * bld;                 // RCA x RCA
+  double* Rm = G + RCA * RCA;               // inverse of the upper factor
+  for (int round = 0; round < 2; ++round) {
+    for (int e = tid; e < RCA * RCA; e += kThreads) {
+      const int a = e / RCA, b = e - a * RCA;
+      const double* qa = BVt + a * bld;
+      const double* qb = BVt + b * bld;
+      double sacc = 0.0;
+      for (int i = 0; i < R; ++i) sacc = fma(qa[i], qb[i], sacc);
+      G[e] = sacc;
+    }
+    __syncthreads();
+    for (int j = 0; j < RCA; ++j) {          // right-looking Cholesky, pivots clamped like MGS norms
+      const double d = sqrt(fmax(G[j * RCA + j], static_cast<double>(norm_floor)));
+      __syncthreads();
+      for (int i = j + tid; i < RCA; i += kThreads) G[j * RCA + i] = (i == j) ? d : G[j * RCA + i] / d;
+      __syncthreads();
+      const int m = RCA - j - 1;
+      for (int e = tid; e < m * m; e += kThreads) {
+        const int a = j + 1 + e / m, b = j + 1 + e % m;
+        G[a * RCA + b] -= G[j * RCA + a] * G[j * RCA + b];
+      }
+      __syncthreads();
+    }
+    for (int c = tid; c < RCA; c += kThreads) {   // R^{-1}, one column per thread
+      Rm[c * RCA + c] = 1.0 / G[c * RCA + c];
+      for (int i = c - 1; i >= 0; --i) {
+        double sacc = 0.0;
+        for (int k = i + 1; k <= c; ++k) sacc += G[i * RCA + k] * Rm[k * RCA + c];
+        Rm[i * RCA + c] = -sacc / G[i * RCA + i];
+      }
+      for (int i = c + 1; i < RCA; ++i) Rm[i * RCA + c] = 0.0;
+    }
+    __syncthreads();
+    // Q <- Q R^{-1} in place: column c needs old columns a <= c, so go from the last column down
+    for (int i = tid; i < R; i += kThreads) {
+      for (int c = RCA - 1; c >= 0; --c) {
+        double sacc = 0.0;
+        for (int a = 0; a <= c; ++a) sacc = fma(BVt[a * bld + i], Rm[a * RCA + c], sacc);
+        BVt[c * bld + i] = sacc;
+      }
+    }
+    __syncthreads();
+  }
+  } else if (tid < 32) {
+    // RCA > 64: modified Gram-Schmidt by one warp (column-major, conflict-free lanes)
     const int lane = tid;
     for (int col = 0; col < RCA; ++col) {
-      double* vc = BVt + col * R;
+      double* vc = BVt + col * bld;
       for (int prev = 0; prev < col; ++prev) {
-        const double* qp = BVt + prev * R;
+        const double* qp = BVt + prev * bld;
         double d = 0.0;
         for (int i = lane; i < R; i += 32) d += vc[i] * qp[i];
 #pragma unroll
@@ -701,7 +839,7 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   __syncthreads();
   for (int e = tid; e < R * RCA; e += kThreads) {
     const int i = e / RCA, k = e - i * RCA;
-    Qo[e] = static_cast<float>(BVt[k * R + i]);
+    Qo[e] = static_cast<float>(BVt[k * bld + i]);
   }
 }
 
@@ -764,11 +902,7 @@ __global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, 
       Ks[v * (KW + 1) + k] = x;
     }
     __syncthreads();
-    rows_x_mat(Ks, KW + 1, Cs, R8, nv, KW, R, [&](int v, int c0, const float (&acc)[8]) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (c0 + j < R) zs[v * (r + 1) + c0 + j] = acc[j] * eps;
-    });
+    rows_x_mat(Ks, KW + 1, Cs, R8, nv, KW, R, [&](int v, int c, float x) { zs[v * (r + 1) + c] = x * eps; });
     __syncthreads();
     const int n = nv * r;
     for (int base = tid; base < n; base += kThreads * kUnroll) {
