@@ -256,7 +256,7 @@ def main():
 
     # per-kernel probes over the timed region
     per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 3, "pi_split": 3, "bside": 1,
-                "coef": 1, "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
+                "coef": 1, "draw": 1, "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
     probes = {}
     for name, n in per_step.items():
         cap = n * args.steps

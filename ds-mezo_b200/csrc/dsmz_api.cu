@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include "dsmz_kernels.cuh"
+#include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
 
 using namespace dsmz;
@@ -82,6 +83,9 @@ size_t qr_apply_smem(int r) {
 }
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
+// Dynamic shared memory of a streaming-kernel CTA (one CTA per SM).
+constexpr int kStreamSmem = 220 * 1024;
+
 template <typename K>
 int set_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) {
@@ -155,10 +159,16 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R).
+int tc_stages(int R);
+
+// Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R),
+// and a stage ring large enough to hold the fp64 W tile (128 x (R + 1) doubles) that the
+// W kernel's epilogue stages over it.
 bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
   return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
-         (reinterpret_cast<uintptr_t>(H) & 15) == 0;
+         (reinterpret_cast<uintptr_t>(H) & 15) == 0 &&
+         static_cast<int64_t>(tc::kBM) * (R + 1) * 8 <= static_cast<int64_t>(tc_stages(static_cast<int>(R))) *
+                                                          tc::stage_bytes(static_cast<int>(R));
 }
 
 // Ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
@@ -191,7 +201,9 @@ struct dsmz_plan {
   std::vector<unsigned char> blob;  // host copy of the tables
   char* dev_tables = nullptr;
   char* workspace = nullptr;
-  int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0;
+  int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
+  int sm_count = 0;
+  sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
   int factor_dtype = DSMZ_F32;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
@@ -234,6 +246,7 @@ struct dsmz_plan {
     t.nwsegsA = nwsegsA;
     t.nwsegsB = nwsegsB;
     t.factor_dtype = factor_dtype;
+    t.ndblk = ndblk;
     t.ws = workspace;
     t.seg_kal_off = seg_kal_off;
     t.kal_sum_off = kal_sum_off;
@@ -325,7 +338,6 @@ void plan_tc_layout(dsmz_plan* P) {
     c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + tc::kBM - 1) / tc::kBM); P->ntc_w += c.nwtile;
     c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D * b.R + kThreads * 8 - 1) / (kThreads * 8)); P->ntc_vt += c.nvt;
   }
-  P->err_off = P->ws.take(256);
 }
 
 // Fills pointers and tensor maps once the workspace is known; false if the driver refuses
@@ -350,6 +362,9 @@ bool bind_tc(dsmz_plan* P) {
   return true;
 }
 
+// Persistent grid of a streaming kernel: one CTA per SM, never more than the segments.
+int stream_grid(const dsmz_plan* P, int nsegs) { return nsegs < P->sm_count ? nsegs : P->sm_count; }
+
 // ---------------------------------------------------------------- launch sequences
 int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s) {
   if (P->bases.empty() || iters <= 0) return 0;
@@ -362,7 +377,8 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   } else {
     if ((rc = set_smem(k_gram<0, 8, double>, gs))) return rc;
   }
-  if ((rc = set_smem(k_qr_apply, qs))) return rc;
+  (void)qs;
+  if ((rc = set_smem(sk::k_sqr_apply, P->Lq.total))) return rc;
   if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
   const KalmanIn kin{};
   const int nb = static_cast<int>(P->bases.size());
@@ -413,7 +429,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_CHOL, s);
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
-    k_qr_apply<<<P->nwsegsB, kThreads, qs, s>>>(tb, tb.wB, nb);
+    sk::k_sqr_apply<<<stream_grid(P, P->nwsegsB), sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err);
     P->probe_end(DSMZ_KID_PI_APPLY, s);
     DSMZ_LAUNCHED("power iteration V = W R^-1");
   }
@@ -435,9 +451,16 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   if (P->mods.empty()) return 0;
   const Tables tb = P->tables();
   int rc;
-  const size_t cs = coef_smem(P->r, P->RC), ps = perturb_smem(P->r, P->r, P->RC);
+  const size_t cs = coef_smem(P->r, P->RC);
+  int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
   if ((rc = set_smem(k_coef<0>, cs))) return rc;
-  if ((rc = set_smem(k_perturb<0>, ps))) return rc;
+  const bool bf = P->factor_dtype == DSMZ_BF16;
+  if ((rc = set_smem(sk::k_sperturb<0, 2>, P->Lp.total))) return rc;
+  if ((rc = set_smem(sk::k_sperturb<0, 4>, P->Lp.total))) return rc;
+  P->probe_begin(DSMZ_KID_DRAW, s);
+  sk::k_draw_zca<<<P->ndblk, 256, 0, s>>>(tb, seed, offset);
+  P->probe_end(DSMZ_KID_DRAW, s);
+  DSMZ_LAUNCHED("Zc_A draws");
   P->probe_begin(DSMZ_KID_BSIDE, s);
   k_bside<<<P->nchunks, kThreads, 0, s>>>(tb);
   P->probe_end(DSMZ_KID_BSIDE, s);
@@ -447,7 +470,8 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   P->probe_end(DSMZ_KID_COEF, s);
   DSMZ_LAUNCHED("AGZO coefficients");
   P->probe_begin(DSMZ_KID_PERTURB, s);
-  k_perturb<0><<<P->nsegs, kThreads, ps, s>>>(tb, seed, offset, eps, kin);
+  if (bf) sk::k_sperturb<0, 2><<<stream_grid(P, P->nsegs), sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
+  else sk::k_sperturb<0, 4><<<stream_grid(P, P->nsegs), sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
   P->probe_end(DSMZ_KID_PERTURB, s);
   DSMZ_LAUNCHED("perturbation");
   P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
@@ -462,14 +486,13 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   const Tables tb = P->tables();
   const int r = P->r;
   const int nm = static_cast<int>(P->mats.size());
-  const size_t gs = gram_smem(r), as = apply_smem(r);
   int rc;
-  if ((rc = set_smem(k_gram<1, 4, double>, gs))) return rc;
-  if ((rc = set_smem(k_gram<1, 8, double>, gs))) return rc;
-  if ((rc = set_smem(k_apply<1, 0>, as))) return rc;
+  int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
+  if ((rc = set_smem(sk::k_sgram<1>, P->Lg.total))) return rc;
+  if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
+  if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (gram_rb(r) == 4) k_gram<1, 4, double><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
-  else k_gram<1, 8, double><<<P->nsegs, kThreads, gs, s>>>(tb, tb.mats, nm, kin);
+  sk::k_sgram<1><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
@@ -478,7 +501,10 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
-  k_apply<1, 0><<<P->nsegs, kThreads, as, s>>>(tb, tb.mats, nm, kin, eta, P->factor_dtype);
+  if (P->factor_dtype == DSMZ_BF16)
+    sk::k_sapply<2><<<stream_grid(P, P->nsegs), sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+  else
+    sk::k_sapply<4><<<stream_grid(P, P->nsegs), sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;
@@ -566,6 +592,8 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: sm_count / max_threads_per_sm describe the device");
   auto* P = new dsmz_plan();
   P->factor_dtype = d->factor_dtype;
+  P->sm_count = d->sm_count;
+  P->err_off = P->ws.take(256);      // device error word of the bounded waits
   // bases
   for (int i = 0; i < d->num_bases; ++i) {
     const dsmz_basis_spec& b = d->bases[i];
@@ -614,6 +642,10 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
       delete P;
       return fail(DSMZ_ERR_INVALID, who + " has an invalid shape or stride");
     }
+    if (m.ld_B * m.r > INT32_MAX || m.ld_A * 4096 > INT32_MAX) {   // 32-bit offsets within a streamed tile
+      delete P;
+      return fail(DSMZ_ERR_UNSUPPORTED, who + ": leading dimension too large");
+    }
     if (m.basis < 0 || m.basis >= d->num_bases || d->bases[m.basis].D != m.d_in) {
       delete P;
       return fail(DSMZ_ERR_INVALID, who + ": basis index out of range or basis D != d_in");
@@ -642,6 +674,10 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
     md.bpart_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(md.nchunk) * 2 * nB * sizeof(float)) / sizeof(float));
     md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1; md.bdt = d->factor_dtype;
+    md.zca_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(nA) * sizeof(float)) / sizeof(float));
+    md.dblk0 = P->ndblk;
+    md.ndblk = static_cast<int32_t>(md.thrA / 256);
+    P->ndblk += md.ndblk;
     md.a = static_cast<int32_t>(P->mats.size());
     md.b = md.a + 1;
     MatD a{};
@@ -657,6 +693,19 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   P->rng_increment = off - d->rng_offset_before;
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * sizeof(double)) / sizeof(double));
+  const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
+  if (P->r > 0) {
+    P->Lp = sk::perturb_layout(P->r, P->r, P->RC, P->r < P->RC ? P->r : P->RC, fes, 0, kStreamSmem);
+    P->Lg = sk::gram_layout(P->r, 1, kStreamSmem);
+    P->La = sk::apply_layout(P->r, fes, kStreamSmem);
+  }
+  if (P->R > 0) P->Lq = sk::qr_layout(P->R, kStreamSmem);
+  for (const sk::Layout* L : {&P->Lp, &P->Lg, &P->La, &P->Lq}) {
+    if (L->r > 0 && (L->S < 2 || L->total > kStreamSmem + 2048)) {
+      delete P;
+      return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");
+    }
+  }
   P->pack();
   *out = P;
   return DSMZ_OK;
@@ -673,7 +722,7 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   // per iteration: Y, W, [Gram of W on the CUDA-core path], partial sums, Cholesky, V;
   // plus the first bf16 split of the caller's basis on the tensor-core path
   if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->tc ? 5 : 6) + (p->tc ? 1 : 0);
-  if (!p->mods.empty()) n += 4 + 3;
+  if (!p->mods.empty()) n += 5 + 3;
   return n;
 }
 
@@ -690,7 +739,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   P->workspace = static_cast<char*>(workspace);
   patch_ws_pointers(P);
   if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
-  if (P->tc) {
+  {
     cudaError_t ez = cudaMemsetAsync(P->workspace + P->err_off, 0, sizeof(int), static_cast<cudaStream_t>(stream));
     if (ez != cudaSuccess) return cuda_fail("dsmz_plan_bind: error word", ez);
   }
@@ -704,7 +753,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
 int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* P) { return (P && P->tc) ? 1 : 0; }
 
 int32_t dsmz_plan_device_error(const dsmz_plan* P, dsmz_stream_t stream) {
-  if (!P || !P->workspace || !P->tc) return 0;
+  if (!P || !P->workspace) return 0;
   int v = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemcpyAsync(&v, P->workspace + P->err_off, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
@@ -858,6 +907,8 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
 static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R, bool tc) {
   dsmz_plan P;
   P.ws.take(table_head_bytes());
+  P.err_off = P.ws.take(256);
+  P.Lq = sk::qr_layout(static_cast<int>(R), kStreamSmem);
   BasisD bd{};
   bd.R = static_cast<int32_t>(R); bd.T = T; bd.D = D;
   bd.y_off = static_cast<int64_t>(P.ws.take(static_cast<size_t>(T) * R * sizeof(float)) / sizeof(float));
@@ -912,7 +963,11 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
     P.workspace = static_cast<char*>(workspace);
     patch_ws_pointers(&P);
   }
-  if (P.tc) {
+  {
+    int dev = 0;
+    cudaError_t ed = cudaGetDevice(&dev);
+    if (ed == cudaSuccess) ed = cudaDeviceGetAttribute(&P.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (ed != cudaSuccess) return cuda_fail("power_iter: device query", ed);
     cudaError_t ez = cudaMemsetAsync(P.workspace + P.err_off, 0, sizeof(int), s);
     if (ez != cudaSuccess) return cuda_fail("power_iter: error word", ez);
   }

@@ -44,6 +44,8 @@ struct ModD {
   const float* varB;          // NULL: skip var_B V^2 (drop-in op)
   int64_t b_s0, b_s1;
   int32_t bdt, pad1;
+  int64_t zca_off;            // floats: materialised Zc_A draw (d_out x RCA)
+  int32_t dblk0, ndblk;       // blocks of the Zc_A draw kernel (one torch thread each)
 };
 
 struct BasisD {
@@ -63,7 +65,7 @@ struct Tables {
   const BasisD* bases; int32_t nbases; int32_t nytiles; int32_t nwtiles;
   const MatD* wA; const MatD* wB;                       // W of each basis: CholeskyQR round 1, round 2 (-> V)
   int32_t nwsegsA; int32_t nwsegsB;
-  int32_t factor_dtype; int32_t pad1;
+  int32_t factor_dtype; int32_t ndblk;                 // ndblk: blocks of the Zc_A draw
   char* ws;                                            // workspace base
   int64_t seg_kal_off;        // doubles: nsegs * 2 per-segment Kalman partials
   int64_t kal_sum_off;        // doubles: 2 summed Kalman scalars

@@ -1,0 +1,85 @@
+// PTX helpers shared by the TMA / tcgen05 kernels and the bulk-copy streaming kernels:
+// shared-memory addresses, mbarriers with bounded waits, and 1-D bulk copies.
+#pragma once
+
+#include <stdint.h>
+
+namespace dsmz {
+
+constexpr uint64_t kTimeoutNs = 1000000000ull;   // a wait gives up after ~1 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// One arrival that also raises the phase's expected transaction bytes.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Plain arrival (release at CTA scope).
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false after kTimeoutNs (error word set) or when another role failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (gtimer() - t0 > kTimeoutNs) {
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+// Wait for copies already issued to land before the CTA may exit: ignores the error word,
+// gives up after kTimeoutNs.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = gtimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (gtimer() - t0 > kTimeoutNs) return;
+  }
+}
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// 16-byte asynchronous copy global -> shared (L2 only), both addresses 16-byte aligned.
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// One arrival on `bar` once every cp.async this thread issued so far has landed (the
+// barrier's expected count includes it).
+__device__ __forceinline__ void cp16_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier over the `n` threads of the consumer warps (id 1; warp-multiple n).
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+}  // namespace dsmz

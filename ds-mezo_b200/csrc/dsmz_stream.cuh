@@ -1,0 +1,1063 @@
+// Streaming kernels of the adapter phase on sm_100a: persistent CTAs, one producer warp
+// that moves each tile of TV vectors into a shared-memory ring (1-D bulk copies with
+// mbarrier transaction counts for contiguous tiles, 16-byte cp.async chunks tracked on the
+// same mbarrier for strided or padded rows), and consumer warps that run the math on the
+// staged tile while the next tiles are in flight.
+//
+//   k_draw_zca     Zc_A draws of every module, materialised in torch's launch layout
+//   k_sperturb     z = eps * (Zc_A Q^T | Zc_B V^T), pos/neg, Kalman partial sums
+//   k_sgram        fp64 Gram of the momentum (plain, or after the Kalman update, which it
+//                  also writes back to mu/var)
+//   k_sapply       param -= eta * X with X = mu Pm (Newton-Schulz apply)
+//   k_sqr_apply    V = W R^-1 in fp64 (power-iteration CholeskyQR) and [V_hi | V_lo]^T
+//
+// Tiles: a segment (MatD::segv vectors of one matrix) is cut into tiles of TV vectors; CTA
+// b takes segments b, b + grid, ... . Perturb / apply / QR apply hand consecutive tiles to
+// four consumer teams of two warps (a 4 x 8 register block per thread covers a whole tile
+// per team); the Gram uses all eight consumer warps on one tile. Every wait is bounded
+// (mbar_wait), and a consumer verdict is agreed with bar.red before any barrier that
+// depends on it, so a timeout ends the kernel instead of hanging it.
+#pragma once
+
+#include <type_traits>
+
+#include "dsmz_kernels.cuh"
+#include "dsmz_ptx.cuh"
+
+namespace dsmz {
+namespace sk {
+
+constexpr int kCW = 8;                   // consumer warps
+constexpr int kCT = 32 * kCW;            // consumer threads
+constexpr int kST = kCT + 32;            // + producer warp 0
+constexpr int kTeams = 4;                // perturb / apply / QR apply
+constexpr int kTT = kCT / kTeams;        // threads per team (two warps)
+constexpr int kBarAll = 1;               // named barrier: all consumer threads
+constexpr int kBarTeam0 = 2;             // named barriers 2..5: one per team
+
+// Vectors per tile: ~2048 elements, a multiple of 8 (16-byte bf16 rows of side-B tiles).
+__host__ __device__ inline int stream_tv(int r) {
+  int tv = (2048 / (r < 1 ? 1 : r)) & ~7;
+  return tv < 8 ? 8 : (tv > 512 ? 512 : tv);
+}
+__host__ __device__ inline int al16(int b) { return (b + 15) & ~15; }
+__host__ __device__ inline int al128(int b) { return (b + 127) & ~127; }
+
+// One input array of a tile. Side 0: vector v is the row at v*ld (components k*cs);
+// side 1: vector v is the column at v*cs (components k*ld). In shared memory, side 0
+// keeps vector v at dst + v*pitch and side 1 component row k at dst + k*pitch.
+struct Src {
+  const char* base;
+  int64_t ld, cs;
+  int32_t es, side, r, pad;
+};
+
+__device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es) {
+  Src a;
+  a.base = reinterpret_cast<const char*>(base);
+  a.ld = M.ld; a.cs = M.cs; a.es = es; a.side = M.side; a.r = static_cast<int>(M.r); a.pad = 0;
+  return a;
+}
+
+// How one array of a tile reaches shared memory: one bulk copy when the tile image is a
+// contiguous run of global memory (side-0 rows of exactly r elements, unpadded); 16-byte
+// cp.async chunks spread over the producer lanes when every row is 16-byte aligned (strided
+// or padded rows: many short rows would starve the bulk engine); element copies otherwise.
+enum { kCopyBulk = 0, kCopy16 = 1, kCopyPlain = 2 };
+
+__device__ __forceinline__ int copy_mode(const Src& a, int64_t s0, int nv, int pitch, const void* dst) {
+  if (a.cs != 1 || (reinterpret_cast<uintptr_t>(a.base) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15) ||
+      (pitch & 15))
+    return kCopyPlain;
+  const int64_t ldb = a.ld * a.es;
+  if (a.side == 0) {
+    const int rowb = a.r * a.es;
+    if (rowb & 15) return kCopyPlain;
+    if (a.ld == a.r && pitch == rowb) return kCopyBulk;
+    return (ldb & 15) ? kCopyPlain : kCopy16;
+  }
+  if ((ldb & 15) || ((s0 * a.es) & 15) || ((static_cast<int64_t>(nv) * a.es) & 15)) return kCopyPlain;
+  return kCopy16;
+}
+
+// 16-byte chunks of the tile's rows, lane-parallel: side 0 has nv rows of r*es bytes,
+// side 1 has r rows of nv*es bytes. When the chunks per row divide 32, each lane keeps one
+// chunk column and walks the rows by pointer increments (no per-chunk division).
+__device__ __forceinline__ void copy16_issue(const Src& a, int64_t s0, int nv, char* dst, int pitch, int lane) {
+  const int nrow = (a.side == 0) ? nv : a.r;
+  const int cpr = ((a.side == 0) ? a.r : nv) * a.es / 16;      // chunks per row
+  const int64_t srow = a.ld * a.es;                              // bytes between source rows
+  const char* src0 = (a.side == 0) ? a.base + s0 * srow : a.base + s0 * a.es;
+  if (cpr <= 32 && (32 % cpr) == 0) {
+    const int rstep = 32 / cpr;
+    int row = lane / cpr;
+    const int c = lane - row * cpr;
+    const char* sp = src0 + row * srow + c * 16;
+    char* dp = dst + row * pitch + c * 16;
+    const int64_t sstep = rstep * srow;
+    const int dstep = rstep * pitch;
+    for (; row < nrow; row += rstep, sp += sstep, dp += dstep) cp16(dp, sp);
+    return;
+  }
+  const int n = nrow * cpr;
+  for (int e = lane; e < n; e += 32) {
+    const int row = e / cpr, c = e - row * cpr;
+    cp16(dst + row * pitch + c * 16, src0 + row * srow + c * 16);
+  }
+}
+
+// Element-by-element copy for layouts neither engine can take (strides, odd sizes).
+__device__ __forceinline__ void plain_copy(const Src& a, int64_t s0, int nv, char* dst, int pitch, int lane) {
+  const int n = nv * a.r;
+  for (int e = lane; e < n; e += 32) {
+    int v, k;
+    if (a.side == 0) { v = e / a.r; k = e - v * a.r; } else { k = e / nv; v = e - k * nv; }
+    const int64_t off = (a.side == 0) ? ((s0 + v) * a.ld + k * a.cs) : (k * a.ld + (s0 + v) * a.cs);
+    char* d = dst + (a.side == 0 ? v * pitch + k * a.es : k * pitch + v * a.es);
+    if (a.es == 4) *reinterpret_cast<uint32_t*>(d) = *reinterpret_cast<const uint32_t*>(a.base + off * 4);
+    else *reinterpret_cast<uint16_t*>(d) = *reinterpret_cast<const uint16_t*>(a.base + off * 2);
+  }
+}
+
+// Fills one stage with up to NA arrays (null base: absent). The stage's `full` barrier
+// expects 33 arrivals: lane 0's expect_tx (bulk bytes, after the element copies) and one
+// cp.async-tracking arrival per lane. Called by all 32 producer lanes.
+constexpr int kFullArrivals = 33;
+template <int NA>
+__device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA], const int (&pitch)[NA],
+                                        int64_t s0, int nv, char* stage, uint64_t* full, int lane) {
+  int mode[NA];
+  uint32_t tx = 0;
+#pragma unroll
+  for (int i = 0; i < NA; ++i) {
+    mode[i] = -1;
+    if (a[i].base == nullptr) continue;
+    mode[i] = copy_mode(a[i], s0, nv, pitch[i], stage + off[i]);
+    if (mode[i] == kCopyBulk) tx += static_cast<uint32_t>(nv) * a[i].r * a[i].es;
+    else if (mode[i] == kCopyPlain) plain_copy(a[i], s0, nv, stage + off[i], pitch[i], lane);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_expect_tx(full, tx);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NA; ++i) {
+    if (mode[i] == kCopyBulk) {
+      if (lane == 0)
+        bulk_g2s(stage + off[i], a[i].base + s0 * a[i].ld * a[i].es, static_cast<uint32_t>(nv) * a[i].r * a[i].es,
+                 full);
+    } else if (mode[i] == kCopy16) {
+      copy16_issue(a[i], s0, nv, stage + off[i], pitch[i], lane);
+    }
+  }
+  cp16_arrive(full);
+}
+
+// Stage pitch of an unpadded tile image: side 0 rows of r elements, side 1 rows of TV.
+__device__ __forceinline__ int side_pitch(int side, int r, int TV, int es) { return (side == 0 ? r : TV) * es; }
+
+// Every consumer thread of a group of n threads passes `ok`; all get the AND.
+__device__ __forceinline__ bool agree(int bar_id, int n, bool ok) {
+  uint32_t all;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(all)
+      : "r"(static_cast<uint32_t>(ok)), "r"(bar_id), "r"(n)
+      : "memory");
+  return all != 0;
+}
+
+// The CTA's tile sequence: segments blockIdx.x, +gridDim.x, ...; TV-vector tiles within.
+struct TileIt {
+  const MatD* mats; int nmats, nsegs, TV;
+  int seg, mi;
+  int64_t s0, v1;
+  __device__ bool start_seg() {
+    if (seg >= nsegs) return false;
+    mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
+    const MatD& M = mats[mi];
+    s0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
+    v1 = min(s0 + static_cast<int64_t>(M.segv), M.nvec);
+    return true;
+  }
+  __device__ void init(const MatD* m, int n, int ns, int tv) {
+    mats = m; nmats = n; nsegs = ns; TV = tv; seg = blockIdx.x;
+  }
+  __device__ int nv() const { return static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0)); }
+  // advance; returns 1 on a new tile of the same segment, 2 on a new segment, 0 at the end
+  __device__ int next() {
+    s0 += TV;
+    if (s0 < v1) return 1;
+    seg += gridDim.x;
+    return start_seg() ? 2 : 0;
+  }
+};
+
+// out(v, c) = sum_a X(v, a) P[a*pld + c] with X(v, a) = X[v*vs + a*as] (as = 1 when AS1).
+// A thread block owns vectors {vb + i*Q} (Q = ceil(nv/4)) and columns {4cb..4cb+3,
+// pld/2 + 4cb..+3}: the four vectors a warp reads per step are consecutive rows (distinct
+// banks when vs = 4 mod 32, or vs = 1) and its eight column blocks one contiguous 128-byte
+// run of a P row. pld % 8 == 0, P padded with zero columns to pld; rows up to 4Q - 1
+// must be readable.
+template <bool AS1, typename Sink>
+__device__ __forceinline__ void mm_rows(const float* __restrict__ X, int vs, int as, const float* __restrict__ P,
+                                        int pld, int nv, int K, int nc, int t, int nt, Sink sink) {
+  const int cbs = pld >> 3, half = pld >> 1;
+  const int Q = (nv + 3) >> 2;
+  const int ast = AS1 ? 1 : as;
+  for (int blk = t; blk < Q * cbs; blk += nt) {
+    const int vb = blk / cbs, cb = blk - vb * cbs;
+    const int c0 = cb * 4;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    const float* x0 = X + vb * vs;
+    const float* x1 = x0 + Q * vs;
+    const float* x2 = x1 + Q * vs;
+    const float* x3 = x2 + Q * vs;
+    const float* pr = P + c0;
+#pragma unroll 4
+    for (int a = 0; a < K; ++a) {
+      const float4 p0 = *reinterpret_cast<const float4*>(pr);
+      const float4 p1 = *reinterpret_cast<const float4*>(pr + half);
+      pr += pld;
+      const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      const float xv[4] = {x0[a * ast], x1[a * ast], x2[a * ast], x3[a * ast]};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], pv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = vb + i * Q;
+      if (v >= nv) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j < 4) ? c0 + j : half + c0 + j - 4;
+        if (c < nc) sink(v, c, acc[i][j]);
+      }
+    }
+  }
+}
+
+// fp64 variant: P is r x pld doubles; columns {2cb, 2cb+1} + g*pld/4 for g < 4 (each
+// thread's double2 loads of a warp cover contiguous 256-byte runs). pld % 8 == 0.
+template <typename Sink>
+__device__ __forceinline__ void mm_rows_f64(const float* __restrict__ X, int vs, const double* __restrict__ P,
+                                            int pld, int nv, int K, int nc, int t, int nt, Sink sink) {
+  const int cbs = pld >> 3, quarter = pld >> 2;
+  const int Q = (nv + 3) >> 2;
+  for (int blk = t; blk < Q * cbs; blk += nt) {
+    const int vb = blk / cbs, cb = blk - vb * cbs;
+    const int c0 = cb * 2;
+    double acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    const float* x0 = X + vb * vs;
+    const float* x1 = x0 + Q * vs;
+    const float* x2 = x1 + Q * vs;
+    const float* x3 = x2 + Q * vs;
+    const double* pr = P + c0;
+#pragma unroll 2
+    for (int a = 0; a < K; ++a) {
+      double pv[8];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const double2 tt = *reinterpret_cast<const double2*>(pr + g * quarter);
+        pv[2 * g] = tt.x;
+        pv[2 * g + 1] = tt.y;
+      }
+      pr += pld;
+      const double xv[4] = {static_cast<double>(x0[a]), static_cast<double>(x1[a]), static_cast<double>(x2[a]),
+                            static_cast<double>(x3[a])};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fma(xv[i], pv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = vb + i * Q;
+      if (v >= nv) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j >> 1) * quarter + c0 + (j & 1);
+        if (c < nc) sink(v, c, acc[i][j]);
+      }
+    }
+  }
+}
+
+// Elements e = e0, e0 + step, ... of an nv x r tile in global memory order, as (vector v,
+// component k), advanced without division. Side 0 walks each vector's components, side 1
+// each component row along the vectors.
+template <int SIDE>
+struct Walk {
+  int v, k, dv, dk, lim;
+  __device__ __forceinline__ Walk(int e0, int step, int r, int nv) {
+    if (SIDE == 0) { v = e0 / r; k = e0 - v * r; dv = step / r; dk = step - dv * r; lim = r; }
+    else { k = e0 / nv; v = e0 - k * nv; dk = step / nv; dv = step - dk * nv; lim = nv; }
+  }
+  __device__ __forceinline__ void next() {
+    if (SIDE == 0) { k += dk; v += dv; if (k >= lim) { k -= lim; ++v; } }
+    else { v += dv; k += dk; if (v >= lim) { v -= lim; ++k; } }
+  }
+  // element offset from the tile's first element in global memory (32-bit) and in the
+  // unpadded shared-memory image
+  __device__ __forceinline__ int goff(int ld, int cs) const { return SIDE == 0 ? v * ld + k * cs : k * ld + v * cs; }
+  __device__ __forceinline__ int soff(int r, int TV) const { return SIDE == 0 ? v * r + k : k * TV + v; }
+};
+
+template <int FES>
+__device__ __forceinline__ float ld_fac(const void* p, int i) {
+  if (FES == 2) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+template <int FES>
+__device__ __forceinline__ void st_fac(void* p, int i, float x) {
+  if (FES == 2) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x);
+  else reinterpret_cast<float*>(p)[i] = x;
+}
+// Element pointer of the tile's first element (vector s0, component 0).
+template <typename T>
+__device__ __forceinline__ T* tile_ptr(T* base, const MatD& M, int64_t s0, int es) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(const_cast<typename std::remove_const<T>::type*>(base)) +
+                              s0 * (M.side == 0 ? M.ld : M.cs) * es);
+}
+
+// =====================================================================================
+// Layouts (host and device): stage ring and fixed buffers, byte offsets from a 128-byte
+// aligned base. Every plan has one rank r (modules) or R (bases).
+// =====================================================================================
+struct Layout {
+  int TV, S;             // vectors per tile, ring stages
+  int stage_bytes;
+  int off[4], pitch[4];  // per array in a stage
+  int fixed0;            // first byte after the ring
+  int o_c, o_z, o_x, o_red, o_tab, o_bar;
+  int total;             // dynamic shared memory bytes (+128 alignment slack)
+  int r, pld, zp, rp, xp, nsb, ng;
+};
+
+// Perturb: p, mu, var (unpadded, MODE 0 only) and the K operand rows (Zc_A rows of width
+// RCA, or basis rows of width RC), padded to pitch KW + 4 floats.
+__host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int fes, int mode, int budget) {
+  Layout L{};
+  L.r = r;
+  L.TV = stream_tv(r);
+  const int KW = RC > RCA ? RC : RCA;
+  const int kp = (KW + 3) / 4 * 4 + 4;
+  const int TV = L.TV;
+  int o = 0;
+  L.off[0] = o; L.pitch[0] = (mode == 0) ? r * fes : 0;               o += al128(mode == 0 ? TV * r * fes : 0);
+  L.off[1] = o; L.pitch[1] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
+  L.off[2] = o; L.pitch[2] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
+  L.off[3] = o; L.pitch[3] = kp * 4;                                  o += al128(TV * kp * 4);
+  L.stage_bytes = o;
+  L.pld = pad8(R);
+  L.zp = r + 1;
+  const int fixed = al128(KW * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + al128(2 * kCW * 8 * 2) + 1024;
+  int S = (budget - fixed) / L.stage_bytes;
+  S = S > 8 ? 8 : S;
+  L.S = S;
+  L.fixed0 = S * L.stage_bytes;
+  L.o_c = L.fixed0;
+  L.o_z = L.o_c + al128(KW * L.pld * 4);
+  L.o_red = L.o_z + kTeams * al128(TV * L.zp * 4);
+  L.o_bar = L.o_red + al128(2 * kCW * 8 * 2);
+  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  return L;
+}
+
+// Apply: p (unpadded) and mu (side 0 rows padded to r + 4 floats).
+__host__ __device__ inline Layout apply_layout(int r, int fes, int budget) {
+  Layout L{};
+  L.r = r;
+  L.TV = stream_tv(r);
+  const int TV = L.TV;
+  const int mp = (r + 3) / 4 * 4 + 4;
+  int o = 0;
+  L.off[0] = o; L.pitch[0] = r * fes;                                   o += al128(TV * r * fes);
+  L.off[1] = o; L.pitch[1] = mp * 4;                                    o += al128(TV * mp * 4);
+  L.stage_bytes = o;
+  L.pld = pad8(r);
+  L.zp = r + 1;
+  const int fixed = al128(r * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + 1024;
+  int S = (budget - fixed) / L.stage_bytes;
+  S = S > 8 ? 8 : S;
+  L.S = S;
+  L.fixed0 = S * L.stage_bytes;
+  L.o_c = L.fixed0;
+  L.o_z = L.o_c + al128(r * L.pld * 4);
+  L.o_bar = L.o_z + kTeams * al128(TV * L.zp * 4);
+  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  return L;
+}
+
+// QR apply: W rows padded to R + 4 floats; fp64 R^-1 (R x pld).
+__host__ __device__ inline Layout qr_layout(int R, int budget) {
+  Layout L{};
+  L.r = R;
+  L.TV = stream_tv(R);
+  const int TV = L.TV;
+  const int mp = (R + 3) / 4 * 4 + 4;
+  L.off[0] = 0; L.pitch[0] = mp * 4;
+  L.stage_bytes = al128(TV * mp * 4);
+  L.pld = pad8(R);
+  L.zp = R + 1;
+  const int fixed = al128(R * L.pld * 8) + kTeams * al128(TV * L.zp * 4) + 1024;
+  int S = (budget - fixed) / L.stage_bytes;
+  S = S > 8 ? 8 : S;
+  L.S = S;
+  L.fixed0 = S * L.stage_bytes;
+  L.o_c = L.fixed0;
+  L.o_z = L.o_c + al128(R * L.pld * 8);
+  L.o_bar = L.o_z + kTeams * al128(TV * L.zp * 4);
+  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  return L;
+}
+
+// Gram: mu (and var, z for the Kalman form), unpadded. fp64 copy of each tile in two
+// buffers (rows of rp + 1 doubles, columns permuted k -> (k % 4) * rp/4 + k / 4), the
+// upper 4 x 8 sub-blocks' accumulators, and the sub-block table.
+__host__ __device__ inline int gram_nsb(int rp) {
+  int n = 0;
+  for (int a = 0; a < rp / 4; ++a)
+    for (int b = 0; b < rp / 8; ++b)
+      if (8 * b + 7 >= 4 * a) ++n;
+  return n;
+}
+__host__ __device__ inline Layout gram_layout(int r, int kalman, int budget) {
+  Layout L{};
+  L.r = r;
+  L.TV = stream_tv(r);
+  const int TV = L.TV;
+  int o = 0;
+  L.off[0] = o; L.pitch[0] = r * 4; o += al128(TV * r * 4);
+  L.off[1] = o; L.pitch[1] = kalman ? r * 4 : 0; o += al128(kalman ? TV * r * 4 : 0);
+  L.off[2] = o; L.pitch[2] = kalman ? r * 4 : 0; o += al128(kalman ? TV * r * 4 : 0);
+  L.stage_bytes = o;
+  L.rp = pad8(r);
+  L.xp = L.rp + 1;
+  L.nsb = gram_nsb(L.rp);
+  L.ng = (kCT / L.nsb) >= 2 ? kCT / L.nsb : 1;
+  const int fixed = al128(TV * L.xp * 8) + al128(L.nsb * 32 * 8) + al128(L.nsb * 4) + 1024;
+  int S = (budget - fixed) / L.stage_bytes;
+  S = S > 8 ? 8 : S;
+  L.S = S;
+  L.fixed0 = S * L.stage_bytes;
+  L.o_x = L.fixed0;
+  L.o_red = L.o_x + al128(TV * L.xp * 8);
+  L.o_tab = L.o_red + al128(L.nsb * 32 * 8);
+  L.o_bar = L.o_tab + al128(L.nsb * 4);
+  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  return L;
+}
+
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 127) & ~uintptr_t(127));
+}
+
+// Producer loop shared by every streaming kernel: walks the CTA's tiles, waits for the
+// stage to be free, fills it. `fill(it, stage, full, lane)` issues the copies.
+template <typename Fill>
+__device__ __forceinline__ void producer_loop(TileIt it, const Layout& L, unsigned char* smem, uint64_t* full,
+                                              uint64_t* empty, int* err, Fill fill) {
+  const int lane = threadIdx.x & 31;
+  int i = 0;
+  bool ok = true;
+  if (it.start_seg()) {
+    while (true) {
+      const int s = i % L.S;
+      if (i >= L.S) {
+        const bool w = mbar_wait(empty + s, (static_cast<uint32_t>(i / L.S) & 1u) ^ 1u, err);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      }
+      fill(it, smem + s * L.stage_bytes, full + s, lane);
+      ++i;
+      if (it.next() == 0) break;
+    }
+  }
+  (void)ok;
+  // the copies already issued land before the CTA can exit, whatever the consumers did
+  if (threadIdx.x == 0)
+    for (int j = (i > L.S ? i - L.S : 0); j < i; ++j) mbar_drain(full + (j % L.S), static_cast<uint32_t>(j / L.S) & 1u);
+}
+
+__device__ __forceinline__ void init_bars(uint64_t* full, uint64_t* empty, int S, int empty_count) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(full + s, kFullArrivals); mbar_init(empty + s, empty_count); }
+    mbar_init_fence();
+  }
+  __syncthreads();
+}
+
+// =====================================================================================
+// Zc_A draws (controller.py:187-188) of every module, in torch's own launch layout: one
+// thread per torch thread idx, curand_init(seed, idx, offset) and one curand_normal4 per
+// grid-stride round, component c of round j -> element idx + threads*(4j + c). A draw no
+// larger than its thread count only ever uses component 0 of round 0 (curand_normal,
+// which returns the same first value of the Box-Muller pair).
+// =====================================================================================
+__global__ void __launch_bounds__(256) k_draw_zca(Tables tb, uint64_t seed, uint64_t base_off) {
+  const int mi = find_owner(tb.mods, tb.nmods, static_cast<int>(blockIdx.x), [](const ModD& d) { return d.dblk0; });
+  const ModD D = tb.mods[mi];
+  const int64_t idx = static_cast<int64_t>(blockIdx.x - D.dblk0) * 256 + threadIdx.x;
+  const int64_t thr = D.thrA;
+  const int64_t n = D.d_out * D.rca;
+  if (idx >= thr || idx >= n) return;
+  float* out = reinterpret_cast<float*>(tb.ws) + D.zca_off;
+  curandStatePhilox4_32_10_t st;
+  curand_init(seed, static_cast<unsigned long long>(idx), base_off + D.offA, &st);
+  if (n <= thr) {
+    out[idx] = curand_normal(&st);
+    return;
+  }
+  for (int64_t base = idx; base < n; base += 4 * thr) {
+    const float4 g = curand_normal4(&st);
+    out[base] = g.x;
+    if (base + thr < n) out[base + thr] = g.y;
+    if (base + 2 * thr < n) out[base + 2 * thr] = g.z;
+    if (base + 3 * thr < n) out[base + 3 * thr] = g.w;
+  }
+}
+
+// =====================================================================================
+// Consumer-side failure protocol of the team kernels: a team whose bounded wait failed is
+// "dead" (agreed within the team); it stops waiting and processing but keeps walking the
+// tile sequence, so every CTA-wide barrier (segment ends, matrix switches) is still met.
+// A failed wait sets the error word, which makes every later wait of the CTA fail fast.
+// =====================================================================================
+
+// =====================================================================================
+// Perturbation (controller.py:178-193, 241-248, 262-270; ds_mezo/kernels.py:290-368,
+// 399-412). Side A: z[i,:] = eps * Zc_A[i,:] Q^T; side B: z[:,j] = eps * Zc_B V[j,:]^T.
+// MODE 0 (step): z, pos = p + z, neg = p - z, per-segment Kalman partials
+//                (sum z * beta*mu, sum z*z * (beta^2 var + q)).
+// MODE 1 (drop-in op): z only, Zc_A from the caller.
+// =====================================================================================
+template <int MODE, int FES>
+__global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64_t seed, uint64_t base_off, float eps,
+                                                     KalmanIn kin, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
+  uint64_t* empty = full + L.S;
+  init_bars(full, empty, L.S, 2);
+  TileIt it;
+  it.init(tb.mats, tb.nmats, tb.nsegs, L.TV);
+  const int warp = threadIdx.x >> 5;
+  constexpr int fes = FES;
+  (void)seed; (void)base_off;
+
+  if (warp == 0) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+      const MatD& M = t.mats[t.mi];
+      const ModD& D = tb.mods[M.owner];
+      const int r = static_cast<int>(M.r);
+      Src a[4];
+      a[0] = make_src(MODE == 0 ? M.param : nullptr, M, fes);
+      a[1] = make_src(MODE == 0 ? M.mu : nullptr, M, 4);
+      a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4);
+      // K operand: rows s0.. of Zc_A (d_out x RCA) or of the basis (d_in x RC)
+      Src k{};
+      k.es = 4; k.side = 0; k.cs = 1;
+      if (M.side == 0) {
+        k.base = reinterpret_cast<const char*>(MODE == 0 ? reinterpret_cast<const float*>(tb.ws) + D.zca_off
+                                                         : D.zcA_ext);
+        k.ld = D.rca; k.r = D.rca;
+      } else {
+        const BasisD& Bd = tb.bases[D.basis];
+        k.base = reinterpret_cast<const char*>(Bd.Vin);
+        k.ld = Bd.v_s0; k.cs = Bd.v_s1; k.r = D.rc;
+      }
+      a[3] = k;
+      const int off[4] = {L.off[0], L.off[1], L.off[2], L.off[3]};
+      const int pitch[4] = {side_pitch(M.side, r, L.TV, fes), side_pitch(M.side, r, L.TV, 4),
+                            side_pitch(M.side, r, L.TV, 4), L.pitch[3]};
+      produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+    });
+    return;
+  }
+
+  const int ct = threadIdx.x - 32;
+  const int team = ct / kTT, tt = ct - team * kTT;
+  float* Cs = reinterpret_cast<float*>(smem + L.o_c);
+  float* zs = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
+  double* red = reinterpret_cast<double*>(smem + L.o_red);
+  float s_zmu = 0.f, s_zzv = 0.f;
+  int i = 0;
+  bool dead = false;
+  bool more = it.start_seg();
+  while (more) {
+    // segment start: the module side's coefficient matrix, shared by the four teams
+    const MatD M = it.mats[it.mi];
+    const ModD D = tb.mods[M.owner];
+    const int r = static_cast<int>(M.r);
+    const int KW = (M.side == 0) ? D.rca : D.rc;
+    const float* coef = reinterpret_cast<const float*>(tb.ws) + D.coef_off;
+    named_sync(kBarAll, kCT);                         // every team is done with the previous segment
+    if (M.side == 0) {
+      const float* Qm = coef + static_cast<int64_t>(D.r) * D.rc;   // R x RCA
+      for (int e = ct; e < KW * L.pld; e += kCT) {
+        const int k = e / L.pld, c = e - k * L.pld;
+        Cs[e] = (c < D.r) ? Qm[c * D.rca + k] : 0.f;
+      }
+    } else {
+      for (int e = ct; e < KW * L.pld; e += kCT) {
+        const int k = e / L.pld, c = e - k * L.pld;
+        Cs[e] = (c < D.r) ? coef[c * D.rc + k] : 0.f;
+      }
+    }
+    named_sync(kBarAll, kCT);
+    int adv, seg_done;
+    do {
+      const int nv = it.nv();
+      if ((i % kTeams) == team && !dead) {
+        const int s = i % L.S;
+        const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+        dead = !agree(kBarTeam0 + team, kTT, w);
+        if (!dead) {
+          const unsigned char* stage = smem + s * L.stage_bytes;
+          const float* Ks = reinterpret_cast<const float*>(stage + L.off[3]);
+          mm_rows<true>(Ks, L.pitch[3] / 4, 1, Cs, L.pld, nv, KW, r, tt, kTT,
+                        [&](int v, int c, float x) { zs[v * L.zp + c] = x * eps; });
+          named_sync(kBarTeam0 + team, kTT);
+          const int n = nv * r;
+          const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
+          float* zt = tile_ptr(M.z, M, it.s0, 4);
+          void* post = tile_ptr(reinterpret_cast<char*>(M.pos), M, it.s0, FES);
+          void* negt = tile_ptr(reinterpret_cast<char*>(M.neg), M, it.s0, FES);
+          const void* ps = stage + L.off[0];
+          const float* ms = reinterpret_cast<const float*>(stage + L.off[1]);
+          const float* vsg = reinterpret_cast<const float*>(stage + L.off[2]);
+          auto body = [&](auto side_tag) {
+            constexpr int SIDE = decltype(side_tag)::value;
+            Walk<SIDE> w(tt, kTT, r, nv);
+            for (int e = tt; e < n; e += kTT, w.next()) {
+              const float z = zs[w.v * L.zp + w.k];
+              const int g = w.goff(ld, cs);
+              zt[g] = z;
+              if (MODE == 0) {
+                const int so = w.soff(r, L.TV);
+                const float p0 = ld_fac<FES>(ps, so);
+                const float m0 = ms[so];
+                const float w0 = vsg[so];
+                st_fac<FES>(post, g, __fadd_rn(p0, z));
+                st_fac<FES>(negt, g, __fsub_rn(p0, z));
+                const float mu1 = __fmul_rn(m0, kin.beta);
+                const float var1 = __fadd_rn(__fmul_rn(w0, kin.beta2), kin.q);
+                s_zmu = fmaf(z, mu1, s_zmu);
+                s_zzv = fmaf(__fmul_rn(z, z), var1, s_zzv);
+              }
+            }
+          };
+          if (M.side == 0) body(std::integral_constant<int, 0>{});
+          else body(std::integral_constant<int, 1>{});
+          __syncwarp();
+          if ((tt & 31) == 0) mbar_arrive(empty + s);
+          named_sync(kBarTeam0 + team, kTT);          // zs is rewritten by the team's next tile
+        }
+      }
+      ++i;
+      seg_done = it.seg;
+      adv = it.next();
+    } while (adv == 1);
+    if (MODE == 0) {
+      // segment end: Kalman partials of the segment (fixed reduction order)
+      double a = s_zmu, b = s_zzv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+      }
+      if ((ct & 31) == 0) { red[2 * (ct >> 5)] = a; red[2 * (ct >> 5) + 1] = b; }
+      named_sync(kBarAll, kCT);
+      if (ct == 0) {
+        double sa = 0.0, sb = 0.0;
+        for (int w = 0; w < kCW; ++w) { sa += red[2 * w]; sb += red[2 * w + 1]; }
+        double* out = reinterpret_cast<double*>(tb.ws) + tb.seg_kal_off + 2 * static_cast<int64_t>(seg_done);
+        out[0] = sa;
+        out[1] = sb;
+      }
+      s_zmu = 0.f;
+      s_zzv = 0.f;
+    }
+    more = (adv == 2);
+  }
+}
+
+// =====================================================================================
+// Newton-Schulz apply (ds_mezo/kernels.py:84-92 rewritten in Gram space):
+// param -= eta * X, X[v,:] = x_v^T Pm with x_v the (already Kalman-updated) momentum;
+// optional scratch = X.
+// =====================================================================================
+template <int FES>
+__global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
+                                                   Layout L, float eta, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
+  uint64_t* empty = full + L.S;
+  init_bars(full, empty, L.S, 2);
+  TileIt it;
+  it.init(mats, nmats, nsegs, L.TV);
+  const int warp = threadIdx.x >> 5;
+  constexpr int fes = FES;
+
+  if (warp == 0) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+      const MatD& M = t.mats[t.mi];
+      Src a[2];
+      a[0] = make_src(M.param, M, fes);
+      a[1] = make_src(M.mu, M, 4);
+      const int off[2] = {L.off[0], L.off[1]};
+      const int pitch[2] = {side_pitch(M.side, static_cast<int>(M.r), L.TV, fes),
+                            M.side == 0 ? L.pitch[1] : L.TV * 4};
+      produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+    });
+    return;
+  }
+
+  const int ct = threadIdx.x - 32;
+  const int team = ct / kTT, tt = ct - team * kTT;
+  float* Ps = reinterpret_cast<float*>(smem + L.o_c);
+  float* os = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
+  int i = 0;
+  bool dead = false;
+  bool more = it.start_seg();
+  int cur = -1;
+  while (more) {
+    const MatD M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r);
+    if (it.mi != cur) {
+      named_sync(kBarAll, kCT);
+      const float* Pm = reinterpret_cast<const float*>(tb.ws) + M.p_off;
+      for (int e = ct; e < r * L.pld; e += kCT) {
+        const int a = e / L.pld, c = e - a * L.pld;
+        Ps[e] = (c < r) ? Pm[a * r + c] : 0.f;
+      }
+      named_sync(kBarAll, kCT);
+      cur = it.mi;
+    }
+    const int vs = (M.side == 0) ? L.pitch[1] / 4 : 1;
+    const int as = (M.side == 0) ? 1 : L.TV;
+    int adv;
+    do {
+      const int nv = it.nv();
+      if ((i % kTeams) == team && !dead) {
+        const int s = i % L.S;
+        const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+        dead = !agree(kBarTeam0 + team, kTT, w);
+        if (!dead) {
+          const unsigned char* stage = smem + s * L.stage_bytes;
+          const float* Xs = reinterpret_cast<const float*>(stage + L.off[1]);
+          if (M.side == 0) mm_rows<true>(Xs, vs, 1, Ps, L.pld, nv, r, r, tt, kTT, [&](int v, int c, float x) { os[v * L.zp + c] = x; });
+          else mm_rows<false>(Xs, 1, as, Ps, L.pld, nv, r, r, tt, kTT, [&](int v, int c, float x) { os[v * L.zp + c] = x; });
+          named_sync(kBarTeam0 + team, kTT);
+          const int n = nv * r;
+          const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
+          void* pt = tile_ptr(reinterpret_cast<char*>(M.param), M, it.s0, FES);
+          float* sct = M.scratch ? tile_ptr(M.scratch, M, it.s0, 4) : nullptr;
+          const void* ps = stage + L.off[0];
+          auto body = [&](auto side_tag) {
+            constexpr int SIDE = decltype(side_tag)::value;
+            Walk<SIDE> w(tt, kTT, r, nv);
+            for (int e = tt; e < n; e += kTT, w.next()) {
+              const float X = os[w.v * L.zp + w.k];
+              const float p0 = ld_fac<FES>(ps, w.soff(r, L.TV));
+              const int g = w.goff(ld, cs);
+              st_fac<FES>(pt, g, __fsub_rn(p0, __fmul_rn(eta, X)));
+              if (sct) sct[g] = X;
+            }
+          };
+          if (M.side == 0) body(std::integral_constant<int, 0>{});
+          else body(std::integral_constant<int, 1>{});
+          __syncwarp();
+          if ((tt & 31) == 0) mbar_arrive(empty + s);
+          named_sync(kBarTeam0 + team, kTT);
+        }
+      }
+      ++i;
+      adv = it.next();
+    } while (adv == 1);
+    more = (adv == 2);
+  }
+}
+
+// =====================================================================================
+// CholeskyQR apply of the power iteration: V = W R^{-1} in fp64 (R^{-1} exported by
+// k_chol after the fp64 workspace's first r*r doubles), V rows out and, when the next
+// product runs on the tensor cores, [V_hi | V_lo]^T (bf16, 2R x D).
+// =====================================================================================
+__global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
+                                                      Layout L, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
+  uint64_t* empty = full + L.S;
+  init_bars(full, empty, L.S, 2);
+  TileIt it;
+  it.init(mats, nmats, nsegs, L.TV);
+  const int warp = threadIdx.x >> 5;
+
+  if (warp == 0) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+      const MatD& M = t.mats[t.mi];
+      Src a[1];
+      a[0] = make_src(M.mu, M, 4);
+      const int off[1] = {0};
+      const int pitch[1] = {L.pitch[0]};
+      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+    });
+    return;
+  }
+
+  const int ct = threadIdx.x - 32;
+  const int team = ct / kTT, tt = ct - team * kTT;
+  double* Ps = reinterpret_cast<double*>(smem + L.o_c);
+  float* os = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
+  int i = 0;
+  bool dead = false;
+  bool more = it.start_seg();
+  int cur = -1;
+  while (more) {
+    const MatD M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r);
+    if (it.mi != cur) {
+      named_sync(kBarAll, kCT);
+      const double* Rd = reinterpret_cast<const double*>(tb.ws) + M.dw_off + static_cast<int64_t>(r) * r;
+      for (int e = ct; e < r * L.pld; e += kCT) {
+        const int a = e / L.pld, c = e - a * L.pld;
+        Ps[e] = (c < r) ? Rd[a * r + c] : 0.0;
+      }
+      named_sync(kBarAll, kCT);
+      cur = it.mi;
+    }
+    float* V = reinterpret_cast<float*>(M.param);
+    int adv;
+    do {
+      const int nv = it.nv();
+      if ((i % kTeams) == team && !dead) {
+        const int s = i % L.S;
+        const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+        dead = !agree(kBarTeam0 + team, kTT, w);
+        if (!dead) {
+          const float* Ws = reinterpret_cast<const float*>(smem + s * L.stage_bytes);
+          mm_rows_f64(Ws, L.pitch[0] / 4, Ps, L.pld, nv, r, r, tt, kTT,
+                      [&](int v, int c, double x) { os[v * L.zp + c] = static_cast<float>(x); });
+          __syncwarp();
+          if ((tt & 31) == 0) mbar_arrive(empty + s);   // W tile consumed
+          named_sync(kBarTeam0 + team, kTT);
+          const int n = nv * r;
+          for (int e = tt; e < n; e += kTT) {           // V rows, coalesced
+            const int v = e / r, c = e - v * r;
+            V[(it.s0 + v) * M.ld + c] = os[v * L.zp + c];
+          }
+          if (M.v2t) {
+            for (int e = tt; e < n; e += kTT) {         // [V_hi | V_lo]^T, coalesced along d
+              const int c = e / nv, v = e - c * nv;
+              const float x = os[v * L.zp + c];
+              const __nv_bfloat16 h = __float2bfloat16_rn(x);
+              M.v2t[static_cast<int64_t>(c) * M.ldv2 + it.s0 + v] = h;
+              M.v2t[static_cast<int64_t>(r + c) * M.ldv2 + it.s0 + v] = __float2bfloat16_rn(x - __bfloat162float(h));
+            }
+          }
+          named_sync(kBarTeam0 + team, kTT);
+        }
+      }
+      ++i;
+      adv = it.next();
+    } while (adv == 1);
+    more = (adv == 2);
+  }
+}
+
+// =====================================================================================
+// Gram partials per segment: G_seg = sum_v x_v x_v^T in fp64 (products of fp32 values are
+// exact in fp64). SRC 0: x = mu. SRC 1: x = mu2 of the Kalman update (controller.py:
+// 267-268, 283-285), and mu2 / var2 are written back to mu / var.
+// All eight consumer warps work on one tile: the elementwise pass writes the fp64 tile,
+// then thread groups accumulate the upper 4 x 8 sub-blocks (rows 4a.., columns 8b..)
+// over the tile's vectors. The per-tile verdict barrier (agree) also orders one tile's
+// products before the next tile's elementwise pass, so one fp64 buffer suffices.
+// =====================================================================================
+template <int SRC>
+__global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
+                                                  Layout L, KalmanIn kin, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
+  uint64_t* empty = full + L.S;
+  init_bars(full, empty, L.S, kCW);
+  TileIt it;
+  it.init(mats, nmats, nsegs, L.TV);
+  const int warp = threadIdx.x >> 5;
+
+  if (warp == 0) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+      const MatD& M = t.mats[t.mi];
+      Src a[3];
+      a[0] = make_src(M.mu, M, 4);
+      a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4);
+      a[2] = make_src(SRC == 1 ? M.z : nullptr, M, 4);
+      const int sp = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
+      const int off[3] = {L.off[0], L.off[1], L.off[2]};
+      const int pitch[3] = {sp, sp, sp};
+      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+    });
+    return;
+  }
+
+  const int ct = threadIdx.x - 32;
+  const int rp = L.rp, q4 = rp / 4, xp = L.xp;
+  double* X = reinterpret_cast<double*>(smem + L.o_x);
+  double* red = reinterpret_cast<double*>(smem + L.o_red);
+  int* tab = reinterpret_cast<int*>(smem + L.o_tab);
+  // sub-block table (a, b) with 8b + 7 >= 4a; zero padding columns of the fp64 tile
+  if (ct == 0) {
+    int n = 0;
+    for (int a = 0; a < rp / 4; ++a)
+      for (int b = 0; b < rp / 8; ++b)
+        if (8 * b + 7 >= 4 * a) tab[n++] = (a << 16) | b;
+  }
+  for (int e = ct; e < L.TV * xp; e += kCT) X[e] = 0.0;
+  named_sync(kBarAll, kCT);
+  const int nsb = L.nsb, ng = L.ng;
+  const bool regacc = ng >= 2;                 // accumulate a segment in registers
+  const int grp = regacc ? ct / nsb : 0;
+  const int myl = regacc ? ct - grp * nsb : ct;
+  KalScal ks{};
+  if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
+
+  double acc[4][8];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.0;
+
+  auto subblock = [&](int nv, int l, int v0, int vstep, double (&ac)[4][8]) {
+    const int t = tab[l];
+    const int a = t >> 16, b = t & 0xffff;
+#pragma unroll 2
+    for (int v = v0; v < nv; v += vstep) {
+      const double* xr = X + v * xp;
+      double xa[4], xb[8];
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) xa[i2] = xr[i2 * q4 + a];                    // rows 4a + i2
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xb[j] = xr[(j & 3) * q4 + 2 * b + (j >> 2)];    // columns 8b + j
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ac[i2][j] = fma(xa[i2], xb[j], ac[i2][j]);
+    }
+  };
+
+  int i = 0;
+  bool ok = it.start_seg();
+  if (ok && !regacc) {
+    for (int e = ct; e < nsb * 32; e += kCT) red[e] = 0.0;
+    named_sync(kBarAll, kCT);
+  }
+  while (ok) {
+    const MatD M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r);
+    int adv, seg_done;
+    do {
+      const int nv = it.nv();
+      const int s = i % L.S;
+      const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+      if (!agree(kBarAll, kCT, w)) { ok = false; break; }     // uniform over the consumers
+      const unsigned char* stage = smem + s * L.stage_bytes;
+      const float* mus = reinterpret_cast<const float*>(stage + L.off[0]);
+      const float* vas = reinterpret_cast<const float*>(stage + L.off[1]);
+      const float* zss = reinterpret_cast<const float*>(stage + L.off[2]);
+      const int n = nv * r;
+      const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
+      float* mut = tile_ptr(M.mu, M, it.s0, 4);
+      float* vat = tile_ptr(M.var, M, it.s0, 4);
+      auto body = [&](auto side_tag) {
+        constexpr int SIDE = decltype(side_tag)::value;
+        Walk<SIDE> w(ct, kCT, r, nv);
+        for (int e = ct; e < n; e += kCT, w.next()) {
+          const int so = w.soff(r, L.TV);
+          float x = mus[so];
+          if (SRC == 1) {
+            float mu1, var1, mu2, var2;
+            kal_predict(x, vas[so], ks, mu1, var1);
+            kal_observe(mu1, var1, zss[so], ks, mu2, var2);
+            const int g = w.goff(ld, cs);
+            mut[g] = mu2;
+            vat[g] = var2;
+            x = mu2;
+          }
+          X[w.v * xp + (w.k & 3) * q4 + (w.k >> 2)] = static_cast<double>(x);
+        }
+      };
+      if (M.side == 0) body(std::integral_constant<int, 0>{});
+      else body(std::integral_constant<int, 1>{});
+      __syncwarp();
+      if ((ct & 31) == 0) mbar_arrive(empty + s);
+      named_sync(kBarAll, kCT);                              // X complete
+      if (regacc) {
+        if (grp < ng) subblock(nv, myl, grp, ng, acc);
+      } else {
+        for (int l = ct; l < nsb; l += kCT) {      // acc is zero here
+          subblock(nv, l, 0, 1, acc);
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+              red[l * 32 + a * 8 + b] += acc[a][b];
+              acc[a][b] = 0.0;
+            }
+        }
+      }
+      ++i;
+      seg_done = it.seg;
+      adv = it.next();
+      if (adv != 1) {
+        // segment end: reduce the groups, write the full r x r partial (mirrored)
+        named_sync(kBarAll, kCT);
+        if (regacc) {
+          for (int g = 0; g < ng; ++g) {
+            if (grp == g) {
+#pragma unroll
+              for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                  double* d = red + myl * 32 + a * 8 + b;
+                  *d = (g == 0) ? acc[a][b] : *d + acc[a][b];
+                  acc[a][b] = 0.0;
+                }
+            }
+            named_sync(kBarAll, kCT);
+          }
+        }
+        double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
+        for (int e = ct; e < r * r; e += kCT) {
+          int row = e / r, col = e - row * r;
+          if (row > col) { const int t2 = row; row = col; col = t2; }
+          const int a = row >> 2, b = col >> 3;
+          // table index of sub-block (a, b): row a2 holds blocks b >= a2 / 2
+          const int l = a * (rp / 8) - ((a / 2) * (a / 2 - 1) + (a & 1) * (a / 2)) + (b - a / 2);
+          gout[e] = red[l * 32 + (row & 3) * 8 + (col & 7)];
+        }
+        named_sync(kBarAll, kCT);
+        if (!regacc && adv == 2) {
+          for (int e = ct; e < nsb * 32; e += kCT) red[e] = 0.0;
+          named_sync(kBarAll, kCT);
+        }
+        if (adv == 0) ok = false;
+      }
+    } while (ok && adv == 1);
+  }
+}
+
+}  // namespace sk
+}  // namespace dsmz

@@ -17,6 +17,7 @@
 #include <cuda.h>
 
 #include "dsmz_internal.cuh"
+#include "dsmz_ptx.cuh"
 
 namespace dsmz {
 namespace tc {
@@ -24,7 +25,6 @@ namespace tc {
 constexpr int kBM = 128;         // output rows per CTA (MMA M)
 constexpr int kBK = 64;          // bf16 elements of K per stage (one 128-byte swizzle row)
 constexpr int kThreadsTC = 192;  // 6 warps
-constexpr uint64_t kTimeoutNs = 1000000000ull;
 
 // Per-basis operands of the tensor-core power iteration. Tensor maps come first (64-byte
 // alignment); they are encoded on the host once the workspace addresses are known.
@@ -48,42 +48,6 @@ struct alignas(64) TCBasis {
   int32_t pad1, pad2;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false after kTimeoutNs (error word set) or when another role failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = gtimer();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (gtimer() - t0 > kTimeoutNs) {
-      atomicExch(err, 1);
-      return false;
-    }
-  }
-}
 __device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
 }
@@ -173,7 +137,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     mbar_init(tmem_full, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_init_fence();
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -213,7 +177,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
       if (!ok) {
         // let the loads already issued land before the CTA can exit
         for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
-          mbar_wait(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u, err);
+          mbar_drain(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u);
       }
     }
   } else if (warp == 1) {
@@ -274,46 +238,48 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
           }
         }
       } else {
-        const int64_t d = static_cast<int64_t>(tile) * kBM + row;
         // The pipeline stages are drained (every MMA completed before tmem_full), so the
-        // W tile is staged over them for its Gram.
-        float* wt = reinterpret_cast<float*>(smem);
-        const int tld = R + 4;                                // 16-byte rows for float4 reads
+        // W tile is staged over them once, converted to fp64: 128 rows of R + 1 doubles
+        // (the odd row length keeps the row-per-thread stores free of bank conflicts).
+        double* wt = reinterpret_cast<double*>(smem);
+        const int tld = R + 1;
         for (int j = 0; j < R; j += 16) {
           float hi[16], lo[16];
           tmem_ld16(trow + j, hi);
           tmem_ld16(trow + R + j, lo);
-          float w[16];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) w[c] = hi[c] + lo[c];    // rows past D are zero (TMA fill)
-          if (d < B->D) {
-            float4* dst = reinterpret_cast<float4*>(B->W + d * R + j);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) dst[c] = make_float4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-          }
-#pragma unroll
-          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = w[c];
+          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = static_cast<double>(hi[c] + lo[c]);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
-        // fp64 Gram of the tile in 4 x 8 blocks (12 shared loads per 32 DFMA)
-        const int RR = R * R;
         const int t = threadIdx.x - 64;
+        // W rows past D are TMA zero fill; the valid rows go out coalesced.
+        const int64_t d0 = static_cast<int64_t>(tile) * kBM;
+        const int nrow = static_cast<int>(min(static_cast<int64_t>(kBM), B->D - d0));
+        for (int e = t; e < nrow * R; e += kBM) {
+          const int rw = e / R, c = e - rw * R;
+          B->W[(d0 + rw) * R + c] = static_cast<float>(wt[rw * tld + c]);
+        }
+        // fp64 Gram of the tile. Thread block (ab, cb) owns rows ab + (R/4) i and columns
+        // cb + (R/8) j, so the 4 and 8 distinct addresses a warp reads per load are
+        // consecutive doubles (no bank conflicts).
+        const int RR = R * R;
+        const int ra = R / 4, rb = R / 8;
         double* gout = B->g1 + static_cast<int64_t>(tile) * RR;
-        const int nbj = R / 8, nblk = (R / 4) * nbj;
-        for (int blk = t; blk < nblk; blk += kBM) {
-          const int a0 = (blk / nbj) * 4, b0 = (blk - (blk / nbj) * nbj) * 8;
+        for (int blk = t; blk < ra * rb; blk += kBM) {
+          const int ab = blk / rb, cb = blk - ab * rb;
           double acc[4][8];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+#pragma unroll 2
           for (int rr = 0; rr < kBM; ++rr) {
-            const float* wr = wt + rr * tld;
-            const float4 fa = *reinterpret_cast<const float4*>(wr + a0);
-            const float4 f0 = *reinterpret_cast<const float4*>(wr + b0);
-            const float4 f1 = *reinterpret_cast<const float4*>(wr + b0 + 4);
-            const double xa[4] = {fa.x, fa.y, fa.z, fa.w};
-            const double xb[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+            const double* wr = wt + rr * tld;
+            double xa[4], xb[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xa[i] = wr[ab + ra * i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xb[j] = wr[cb + rb * j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -322,7 +288,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) gout[(a0 + i) * R + b0 + j] = acc[i][j];
+            for (int j = 0; j < 8; ++j) gout[(ab + ra * i) * R + cb + rb * j] = acc[i][j];
         }
       }
     }

@@ -106,7 +106,7 @@ SIGNATURES = {
 }
 
 KERNEL_IDS = {"pi_y": 0, "pi_w": 1, "pi_gram": 2, "pi_chol": 3, "pi_apply": 4, "bside": 5, "coef": 6,
-              "perturb": 7, "kalman_sum": 8, "gram": 9, "ns_solve": 10, "apply": 11, "pi_split": 12}
+              "perturb": 7, "kalman_sum": 8, "gram": 9, "ns_solve": 10, "apply": 11, "pi_split": 12, "draw": 13}
 
 _lib = None
 

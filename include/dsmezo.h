@@ -233,7 +233,8 @@ enum dsmz_kernel_id {
   DSMZ_KID_NS_SOLVE = 10,  /* Newton-Schulz in Gram space */
   DSMZ_KID_APPLY = 11,     /* Kalman update + param -= eta X */
   DSMZ_KID_PI_SPLIT = 12,  /* [V_hi | V_lo]^T for the tensor-core products */
-  DSMZ_NUM_KIDS = 13
+  DSMZ_KID_DRAW = 13,      /* Zc_A draws in torch's launch layout */
+  DSMZ_NUM_KIDS = 14
 };
 int dsmz_plan_set_probe(dsmz_plan* plan, int32_t kernel, void** start_events, void** stop_events,
                         int32_t capacity);
