@@ -488,11 +488,14 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   const int nm = static_cast<int>(P->mats.size());
   int rc;
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
-  if ((rc = set_smem(sk::k_sgram<1>, P->Lg.total))) return rc;
+  const bool small = sk::gram_maxb(r) <= 5;
+  if ((rc = set_smem(sk::k_sgram<1, 5>, P->Lg.total))) return rc;
+  if ((rc = set_smem(sk::k_sgram<1, 17>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  sk::k_sgram<1><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  if (small) sk::k_sgram<1, 5><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  else sk::k_sgram<1, 17><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);

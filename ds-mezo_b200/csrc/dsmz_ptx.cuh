@@ -39,16 +39,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (or the
+// hint runs out) instead of spinning, so waiting warps leave the issue slots to the warps
+// doing the work.
+constexpr uint32_t kSuspendNs = 1000000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: false after kTimeoutNs (error word set) or when another role failed.
+// The error word is one global address shared by every waiting thread of the grid, so it
+// is read only every kPollNs of waiting: polled on every spin it turns into an L2 hot
+// spot that slows the very copies being waited for.
+constexpr uint64_t kPollNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = gtimer();
+  uint64_t tchk = t0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (gtimer() - t0 > kTimeoutNs) {
-      atomicExch(err, 1);
-      return false;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    const uint64_t t = gtimer();
+    if (t - tchk > kPollNs) {
+      tchk = t;
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (t - t0 > kTimeoutNs) {
+        atomicExch(err, 1);
+        return false;
+      }
     }
   }
 }

@@ -424,13 +424,6 @@ __host__ __device__ inline Layout qr_layout(int R, int budget) {
 // Gram: mu (and var, z for the Kalman form), unpadded. fp64 copy of each tile in two
 // buffers (rows of rp + 1 doubles, columns permuted k -> (k % 4) * rp/4 + k / 4), the
 // upper 4 x 8 sub-blocks' accumulators, and the sub-block table.
-__host__ __device__ inline int gram_nsb(int rp) {
-  int n = 0;
-  for (int a = 0; a < rp / 4; ++a)
-    for (int b = 0; b < rp / 8; ++b)
-      if (8 * b + 7 >= 4 * a) ++n;
-  return n;
-}
 __host__ __device__ inline Layout gram_layout(int r, int kalman, int budget) {
   Layout L{};
   L.r = r;
@@ -442,24 +435,27 @@ __host__ __device__ inline Layout gram_layout(int r, int kalman, int budget) {
   L.off[2] = o; L.pitch[2] = kalman ? r * 4 : 0; o += al128(kalman ? TV * r * 4 : 0);
   L.stage_bytes = o;
   L.rp = pad8(r);
-  L.xp = L.rp + 1;
-  L.nsb = gram_nsb(L.rp);
-  L.ng = (kCT / L.nsb) >= 2 ? kCT / L.nsb : 1;
-  const int fixed = al128(TV * L.xp * 8) + al128(L.nsb * 32 * 8) + al128(L.nsb * 4) + 1024;
+  L.xp = L.rp + 8;                 // side 0 rows of the fp64 tile
+  L.zp = TV + 4;                   // side 1 rows
+  const int xa = TV * L.xp, xb = L.rp * L.zp;
+  const int xbytes = al128((xa > xb ? xa : xb) * 8);
+  const int fixed = xbytes + 1024 + 1024;
   int S = (budget - fixed) / L.stage_bytes;
   S = S > 8 ? 8 : S;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_x = L.fixed0;
-  L.o_red = L.o_x + al128(TV * L.xp * 8);
-  L.o_tab = L.o_red + al128(L.nsb * 32 * 8);
-  L.o_bar = L.o_tab + al128(L.nsb * 4);
+  L.o_red = L.o_x + xbytes;        // block table (<= 136 ints)
+  L.o_bar = L.o_red + 1024;
   L.total = L.o_bar + 2 * 8 * S + 128 + 128;
   return L;
 }
 
+// 128-byte aligned base of the dynamic shared memory. Pointer plus offset (not an integer
+// round trip) keeps the shared state space visible to the compiler, so accesses through it
+// compile to shared loads and stores rather than generic ones.
 __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
-  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 127) & ~uintptr_t(127));
+  return raw + ((128u - (smem_u32(raw) & 127u)) & 127u);
 }
 
 // Producer loop shared by every streaming kernel: walks the CTA's tiles, waits for the
@@ -881,12 +877,26 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
 // Gram partials per segment: G_seg = sum_v x_v x_v^T in fp64 (products of fp32 values are
 // exact in fp64). SRC 0: x = mu. SRC 1: x = mu2 of the Kalman update (controller.py:
 // 267-268, 283-285), and mu2 / var2 are written back to mu / var.
-// All eight consumer warps work on one tile: the elementwise pass writes the fp64 tile,
-// then thread groups accumulate the upper 4 x 8 sub-blocks (rows 4a.., columns 8b..)
-// over the tile's vectors. The per-tile verdict barrier (agree) also orders one tile's
-// products before the next tile's elementwise pass, so one fp64 buffer suffices.
+// All eight consumer warps work on one tile: the elementwise pass writes the tile in fp64,
+// then the fp64 tensor-core MMA (m8n8k4) accumulates the upper-triangle 8 x 8 blocks of G,
+// each block owned by one warp for the whole segment (fragments stay in registers), and
+// written out (mirrored) at the segment end. The per-tile verdict barrier (agree) orders
+// one tile's products before the next tile's elementwise pass.
+// Tile image: side 0 X[v][c] with pitch rp + 8 doubles, side 1 X[c][v] with pitch TV + 4
+// (either way a fragment load of a warp touches 256 bytes in two wavefronts).
 // =====================================================================================
-template <int SRC>
+__device__ __forceinline__ void dmma_8x8x4(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+// MAXB: upper 8 x 8 blocks per warp (5 up to r = 64, 17 up to r = 128)
+__host__ __device__ inline int gram_maxb(int r) {
+  const int nb = (r + 7) / 8;
+  return (nb * (nb + 1) / 2 + kCW - 1) / kCW;
+}
+
+template <int SRC, int MAXB>
 __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
                                                   Layout L, KalmanIn kin, int* err) {
   extern __shared__ unsigned char smem_raw[];
@@ -914,59 +924,35 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
   }
 
   const int ct = threadIdx.x - 32;
-  const int rp = L.rp, q4 = rp / 4, xp = L.xp;
+  const int cw = ct >> 5, lane = ct & 31;
+  const int rp = L.rp, nb = rp / 8;
+  const int nblk = nb * (nb + 1) / 2;
   double* X = reinterpret_cast<double*>(smem + L.o_x);
-  double* red = reinterpret_cast<double*>(smem + L.o_red);
-  int* tab = reinterpret_cast<int*>(smem + L.o_tab);
-  // sub-block table (a, b) with 8b + 7 >= 4a; zero padding columns of the fp64 tile
-  if (ct == 0) {
-    int n = 0;
-    for (int a = 0; a < rp / 4; ++a)
-      for (int b = 0; b < rp / 8; ++b)
-        if (8 * b + 7 >= 4 * a) tab[n++] = (a << 16) | b;
-  }
-  for (int e = ct; e < L.TV * xp; e += kCT) X[e] = 0.0;
-  named_sync(kBarAll, kCT);
-  const int nsb = L.nsb, ng = L.ng;
-  const bool regacc = ng >= 2;                 // accumulate a segment in registers
-  const int grp = regacc ? ct / nsb : 0;
-  const int myl = regacc ? ct - grp * nsb : ct;
+  const int xbytes = L.o_red - L.o_x;
+  for (int e = ct; e < xbytes / 8; e += kCT) X[e] = 0.0;    // zero padding columns / rows once
   KalScal ks{};
   if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
-
-  double acc[4][8];
+  // upper-triangle blocks (bi, bj), bi <= bj, in a shared table; warp cw owns entries
+  // cw, cw + 8, ...
+  int* btab = reinterpret_cast<int*>(smem + L.o_red);
+  if (ct == 0) {
+    int q = 0;
+    for (int bi = 0; bi < nb; ++bi)
+      for (int bj = bi; bj < nb; ++bj) btab[q++] = (bi << 8) | bj;
+  }
+  const int nmine = (nblk - cw + kCW - 1) / kCW;
+  double acc[MAXB][2];
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
-#pragma unroll
-    for (int b = 0; b < 8; ++b) acc[a][b] = 0.0;
-
-  auto subblock = [&](int nv, int l, int v0, int vstep, double (&ac)[4][8]) {
-    const int t = tab[l];
-    const int a = t >> 16, b = t & 0xffff;
-#pragma unroll 2
-    for (int v = v0; v < nv; v += vstep) {
-      const double* xr = X + v * xp;
-      double xa[4], xb[8];
-#pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2) xa[i2] = xr[i2 * q4 + a];                    // rows 4a + i2
-#pragma unroll
-      for (int j = 0; j < 8; ++j) xb[j] = xr[(j & 3) * q4 + 2 * b + (j >> 2)];    // columns 8b + j
-#pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ac[i2][j] = fma(xa[i2], xb[j], ac[i2][j]);
-    }
-  };
+  for (int q = 0; q < MAXB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
+  named_sync(kBarAll, kCT);
 
   int i = 0;
   bool ok = it.start_seg();
-  if (ok && !regacc) {
-    for (int e = ct; e < nsb * 32; e += kCT) red[e] = 0.0;
-    named_sync(kBarAll, kCT);
-  }
   while (ok) {
     const MatD M = it.mats[it.mi];
     const int r = static_cast<int>(M.r);
+    const int sv = (M.side == 0) ? L.xp : 1;                 // X(v, c) = X[v*sv + c*sc]
+    const int sc = (M.side == 0) ? 1 : L.zp;
     int adv, seg_done;
     do {
       const int nv = it.nv();
@@ -983,75 +969,88 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
       float* vat = tile_ptr(M.var, M, it.s0, 4);
       auto body = [&](auto side_tag) {
         constexpr int SIDE = decltype(side_tag)::value;
-        Walk<SIDE> w(ct, kCT, r, nv);
-        for (int e = ct; e < n; e += kCT, w.next()) {
-          const int so = w.soff(r, L.TV);
-          float x = mus[so];
-          if (SRC == 1) {
-            float mu1, var1, mu2, var2;
-            kal_predict(x, vas[so], ks, mu1, var1);
-            kal_observe(mu1, var1, zss[so], ks, mu2, var2);
-            const int g = w.goff(ld, cs);
-            mut[g] = mu2;
-            vat[g] = var2;
-            x = mu2;
+        constexpr int U = 4;
+        Walk<SIDE> wk(ct, kCT, r, nv);
+        for (int e = ct; e < n; e += U * kCT) {
+          int vv[U], kk[U], so[U];
+          float x[U], va[U], zz[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {                     // every load before any use
+            vv[u] = wk.v; kk[u] = wk.k;
+            so[u] = wk.soff(r, L.TV);
+            wk.next();
+            if (e + u * kCT < n) {
+              x[u] = mus[so[u]];
+              if (SRC == 1) { va[u] = vas[so[u]]; zz[u] = zss[so[u]]; }
+            }
           }
-          X[w.v * xp + (w.k & 3) * q4 + (w.k >> 2)] = static_cast<double>(x);
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (e + u * kCT >= n) continue;
+            float xv = x[u];
+            if (SRC == 1) {
+              float mu1, var1, mu2, var2;
+              kal_predict(xv, va[u], ks, mu1, var1);
+              kal_observe(mu1, var1, zz[u], ks, mu2, var2);
+              const int g = SIDE == 0 ? vv[u] * ld + kk[u] * cs : kk[u] * ld + vv[u] * cs;
+              mut[g] = mu2;
+              vat[g] = var2;
+              xv = mu2;
+            }
+            X[vv[u] * sv + kk[u] * sc] = static_cast<double>(xv);
+          }
         }
       };
       if (M.side == 0) body(std::integral_constant<int, 0>{});
       else body(std::integral_constant<int, 1>{});
+      const int nv4 = (nv + 3) & ~3;                          // zero vectors nv .. nv4-1
+      for (int e = ct; e < (nv4 - nv) * r; e += kCT) {
+        const int v = nv + e / r, c = e - (e / r) * r;
+        X[v * sv + c * sc] = 0.0;
+      }
       __syncwarp();
       if ((ct & 31) == 0) mbar_arrive(empty + s);
       named_sync(kBarAll, kCT);                              // X complete
-      if (regacc) {
-        if (grp < ng) subblock(nv, myl, grp, ng, acc);
-      } else {
-        for (int l = ct; l < nsb; l += kCT) {      // acc is zero here
-          subblock(nv, l, 0, 1, acc);
+      // fp64 MMA over the tile's vectors, 4 per step; fragment element (row lane>>2 of the
+      // block, vector lane&3) of both operands
+      const int fv = lane & 3, fc = lane >> 2;
+      int oa[MAXB], ob[MAXB];                                // fragment offsets of this warp's blocks
 #pragma unroll
-          for (int a = 0; a < 4; ++a)
+      for (int q = 0; q < MAXB; ++q) {
+        const int t = (q < nmine) ? btab[cw + q * kCW] : 0;
+        oa[q] = 8 * (t >> 8) * sc;
+        ob[q] = 8 * (t & 0xff) * sc;
+      }
+      const double* xr = X + fv * sv + fc * sc;
+      const int vstep = 4 * sv;
+      for (int v0 = 0; v0 < nv4; v0 += 4, xr += vstep) {
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-              red[l * 32 + a * 8 + b] += acc[a][b];
-              acc[a][b] = 0.0;
-            }
-        }
+        for (int q = 0; q < MAXB; ++q)
+          if (q < nmine) dmma_8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
       }
       ++i;
       seg_done = it.seg;
       adv = it.next();
       if (adv != 1) {
-        // segment end: reduce the groups, write the full r x r partial (mirrored)
-        named_sync(kBarAll, kCT);
-        if (regacc) {
-          for (int g = 0; g < ng; ++g) {
-            if (grp == g) {
-#pragma unroll
-              for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 8; ++b) {
-                  double* d = red + myl * 32 + a * 8 + b;
-                  *d = (g == 0) ? acc[a][b] : *d + acc[a][b];
-                  acc[a][b] = 0.0;
-                }
-            }
-            named_sync(kBarAll, kCT);
-          }
-        }
+        // segment end: each warp writes its blocks (and their mirror images)
         double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
-        for (int e = ct; e < r * r; e += kCT) {
-          int row = e / r, col = e - row * r;
-          if (row > col) { const int t2 = row; row = col; col = t2; }
-          const int a = row >> 2, b = col >> 3;
-          // table index of sub-block (a, b): row a2 holds blocks b >= a2 / 2
-          const int l = a * (rp / 8) - ((a / 2) * (a / 2 - 1) + (a & 1) * (a / 2)) + (b - a / 2);
-          gout[e] = red[l * 32 + (row & 3) * 8 + (col & 7)];
-        }
-        named_sync(kBarAll, kCT);
-        if (!regacc && adv == 2) {
-          for (int e = ct; e < nsb * 32; e += kCT) red[e] = 0.0;
-          named_sync(kBarAll, kCT);
+#pragma unroll
+        for (int q = 0; q < MAXB; ++q) {
+          if (q < nmine) {
+            const int t = btab[cw + q * kCW];
+            const int bi = t >> 8, bj = t & 0xff;
+            const int row = 8 * bi + (lane >> 2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int col = 8 * bj + 2 * (lane & 3) + h;
+              if (row < r && col < r) {
+                gout[row * r + col] = acc[q][h];
+                gout[col * r + row] = acc[q][h];
+              }
+            }
+            acc[q][0] = 0.0;
+            acc[q][1] = 0.0;
+          }
         }
         if (adv == 0) ok = false;
       }

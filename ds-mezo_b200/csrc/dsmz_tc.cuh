@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
                                                          int* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned base for the swizzled stages
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
   const int item = blockIdx.x;
   const int bi = (MODE == 0) ? find_owner(bases, nb, item, [](const TCBasis& b) { return b.ytile0; })
                              : find_owner(bases, nb, item, [](const TCBasis& b) { return b.wtile0; });
