@@ -95,18 +95,58 @@ int set_smem(K kernel, size_t bytes) {
   return 0;
 }
 
-// One adapter matrix (or W basis matrix) with its segment and workspace slots.
-void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bool with_solve) {
+// One adapter matrix (or W basis matrix) with its segment and workspace slots. Without
+// alloc_gram the Gram partials are placed later by chunk_matrices.
+void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bool with_solve,
+                bool alloc_gram = true) {
   m.segv = seg_vectors(static_cast<int>(m.r));
   m.nseg = static_cast<int32_t>((m.nvec + m.segv - 1) / m.segv);
   if (m.nseg < 1) m.nseg = 1;
   m.seg0 = seg_counter;
   seg_counter += m.nseg;
   const size_t rr = static_cast<size_t>(m.r) * m.r;
-  m.gram_off = static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double));
+  m.gram_off = alloc_gram ? static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double)) : 0;
   m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
   m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * rr * sizeof(double)) / sizeof(double)) : 0;
   mats.push_back(m);
+}
+
+// Streaming-kernel schedule of a matrix list: TV-vector tiles numbered across the list,
+// cut into G = min(max_ctas, T) contiguous chunks (one per CTA, [c*T/G, (c+1)*T/G)), so no
+// chunk is empty and every chunk between two that touch a matrix lies inside it; a segment
+// is a chunk's run within one matrix. Sets tile0/ntile/chunk0/seg0/nseg and, with L, places
+// the Gram partials (one r x r block per segment). Returns the number of segments; *grid
+// receives G, the grid every streaming kernel over this list must be launched with.
+int chunk_matrices(std::vector<MatD>& mats, int TV, int max_ctas, Layout* L, int* grid) {
+  int64_t T = 0;
+  for (MatD& m : mats) {
+    m.tile0 = static_cast<int32_t>(T);
+    m.ntile = static_cast<int32_t>((m.nvec + TV - 1) / TV);
+    T += m.ntile;
+  }
+  const int G = static_cast<int>(T < max_ctas ? T : max_ctas);
+  *grid = G;
+  auto chunk_of = [&](int64_t t) {   // largest c with c*T/G <= t
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if ((static_cast<int64_t>(mid) * T) / G <= t) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+  int nseg = 0;
+  for (MatD& m : mats) {
+    m.chunk0 = chunk_of(m.tile0);
+    const int c1 = chunk_of(static_cast<int64_t>(m.tile0) + m.ntile - 1);
+    m.nseg = c1 - m.chunk0 + 1;
+    m.seg0 = nseg;
+    nseg += m.nseg;
+    if (L) {
+      const size_t rr = static_cast<size_t>(m.r) * m.r;
+      m.gram_off = static_cast<int64_t>(L->take(m.nseg * rr * sizeof(double)) / sizeof(double));
+    }
+  }
+  return nseg;
 }
 
 void fill_basis_tiles(BasisD& b, int& ytiles, int& wtiles) {
@@ -203,6 +243,7 @@ struct dsmz_plan {
   char* workspace = nullptr;
   int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
   int sm_count = 0;
+  int grid_m = 0, grid_w = 0;        // streaming-kernel grids (chunks) of mats and w2
   sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
   int factor_dtype = DSMZ_F32;
   int r = 0, R = 0, RC = 0;
@@ -362,8 +403,6 @@ bool bind_tc(dsmz_plan* P) {
   return true;
 }
 
-// Persistent grid of a streaming kernel: one CTA per SM, never more than the segments.
-int stream_grid(const dsmz_plan* P, int nsegs) { return nsegs < P->sm_count ? nsegs : P->sm_count; }
 
 // ---------------------------------------------------------------- launch sequences
 int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s) {
@@ -429,7 +468,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_CHOL, s);
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
-    sk::k_sqr_apply<<<stream_grid(P, P->nwsegsB), sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err);
+    sk::k_sqr_apply<<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err);
     P->probe_end(DSMZ_KID_PI_APPLY, s);
     DSMZ_LAUNCHED("power iteration V = W R^-1");
   }
@@ -470,8 +509,8 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   P->probe_end(DSMZ_KID_COEF, s);
   DSMZ_LAUNCHED("AGZO coefficients");
   P->probe_begin(DSMZ_KID_PERTURB, s);
-  if (bf) sk::k_sperturb<0, 2><<<stream_grid(P, P->nsegs), sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
-  else sk::k_sperturb<0, 4><<<stream_grid(P, P->nsegs), sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
+  if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
+  else sk::k_sperturb<0, 4><<<P->grid_m, sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
   P->probe_end(DSMZ_KID_PERTURB, s);
   DSMZ_LAUNCHED("perturbation");
   P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
@@ -494,8 +533,8 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (small) sk::k_sgram<1, 5><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
-  else sk::k_sgram<1, 17><<<stream_grid(P, P->nsegs), sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  if (small) sk::k_sgram<1, 5><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  else sk::k_sgram<1, 17><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
@@ -505,9 +544,9 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
   if (P->factor_dtype == DSMZ_BF16)
-    sk::k_sapply<2><<<stream_grid(P, P->nsegs), sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<2><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   else
-    sk::k_sapply<4><<<stream_grid(P, P->nsegs), sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<4><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;
@@ -686,14 +725,16 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     MatD a{};
     a.param = m.A; a.pos = m.pos_A; a.neg = m.neg_A; a.mu = m.mu_A; a.var = m.var_A; a.z = m.z_A;
     a.scratch = m.scratch_A; a.nvec = m.d_out; a.r = m.r; a.ld = m.ld_A; a.cs = 1; a.side = 0; a.owner = i;
-    add_matrix(P->mats, P->ws, a, P->nsegs, true);
+    add_matrix(P->mats, P->ws, a, P->nsegs, true, false);
     MatD b{};
     b.param = m.B; b.pos = m.pos_B; b.neg = m.neg_B; b.mu = m.mu_B; b.var = m.var_B; b.z = m.z_B;
     b.scratch = m.scratch_B; b.nvec = m.d_in; b.r = m.r; b.ld = m.ld_B; b.cs = 1; b.side = 1; b.owner = i;
-    add_matrix(P->mats, P->ws, b, P->nsegs, true);
+    add_matrix(P->mats, P->ws, b, P->nsegs, true, false);
     P->mods.push_back(md);
   }
   P->rng_increment = off - d->rng_offset_before;
+  if (!P->mats.empty()) P->nsegs = chunk_matrices(P->mats, sk::stream_tv(P->r), P->sm_count, &P->ws, &P->grid_m);
+  if (!P->w2.empty()) chunk_matrices(P->w2, sk::stream_tv(P->R), P->sm_count, nullptr, &P->grid_w);
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * sizeof(double)) / sizeof(double));
   const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
@@ -974,6 +1015,7 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
     cudaError_t ez = cudaMemsetAsync(P.workspace + P.err_off, 0, sizeof(int), s);
     if (ez != cudaSuccess) return cuda_fail("power_iter: error word", ez);
   }
+  chunk_matrices(P.w2, sk::stream_tv(static_cast<int>(R)), P.sm_count, nullptr, &P.grid_w);
   int rc = upload_small(&P, static_cast<char*>(workspace), s);
   if (rc) return rc;
   return run_power_iteration(&P, num_iters, norm_floor, s);

@@ -27,6 +27,10 @@ struct MatD {
   int64_t dw_off;             // doubles: 4 * r*r fp64 solve workspace
   __nv_bfloat16* v2t;         // power-iteration W only: [V_hi | V_lo]^T output (NULL: none)
   int64_t ldv2;
+  // streaming kernels: the global tile space (TV-vector tiles of every matrix in order) is
+  // cut into one contiguous chunk per CTA; a segment is a chunk's run within one matrix
+  int32_t tile0, ntile;       // first global tile, tiles of this matrix
+  int32_t chunk0, pad1;       // chunk (CTA) holding tile0; segment seg0 + c - chunk0 of chunk c
 };
 
 struct ModD {

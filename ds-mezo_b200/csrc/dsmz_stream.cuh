@@ -166,29 +166,43 @@ __device__ __forceinline__ bool agree(int bar_id, int n, bool ok) {
   return all != 0;
 }
 
-// The CTA's tile sequence: segments blockIdx.x, +gridDim.x, ...; TV-vector tiles within.
+// The CTA's tile sequence: chunk blockIdx.x of the global tile space, tiles
+// [c*T/G, (c+1)*T/G) (T tiles, G CTAs), walked in matrix order. A segment is the run of
+// the chunk's tiles inside one matrix (global index MatD::seg0 + c - MatD::chunk0).
 struct TileIt {
-  const MatD* mats; int nmats, nsegs, TV;
-  int seg, mi;
-  int64_t s0, v1;
-  __device__ bool start_seg() {
-    if (seg >= nsegs) return false;
-    mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
+  const MatD* mats; int nmats, TV;
+  int t, t1;            // current global tile, end of the chunk
+  int mi, seg;
+  int64_t s0, nvec;     // first vector of the tile, vectors of the matrix
+  __device__ void init(const MatD* m, int n, int tv) {
+    mats = m; nmats = n; TV = tv;
+    const int64_t T = static_cast<int64_t>(m[n - 1].tile0) + m[n - 1].ntile;
+    const int64_t G = gridDim.x, c = blockIdx.x;
+    t = static_cast<int>((c * T) / G);
+    t1 = static_cast<int>(((c + 1) * T) / G);
+  }
+  __device__ void load() {
     const MatD& M = mats[mi];
-    s0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
-    v1 = min(s0 + static_cast<int64_t>(M.segv), M.nvec);
+    nvec = M.nvec;
+    seg = M.seg0 + static_cast<int>(blockIdx.x) - M.chunk0;
+  }
+  __device__ bool start_seg() {
+    if (t >= t1) return false;
+    mi = find_owner(mats, nmats, t, [](const MatD& m) { return m.tile0; });
+    load();
+    s0 = static_cast<int64_t>(t - mats[mi].tile0) * TV;
     return true;
   }
-  __device__ void init(const MatD* m, int n, int ns, int tv) {
-    mats = m; nmats = n; nsegs = ns; TV = tv; seg = blockIdx.x;
-  }
-  __device__ int nv() const { return static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0)); }
+  __device__ int nv() const { return static_cast<int>(min(static_cast<int64_t>(TV), nvec - s0)); }
   // advance; returns 1 on a new tile of the same segment, 2 on a new segment, 0 at the end
   __device__ int next() {
+    if (++t >= t1) return 0;
     s0 += TV;
-    if (s0 < v1) return 1;
-    seg += gridDim.x;
-    return start_seg() ? 2 : 0;
+    if (s0 < nvec) return 1;
+    ++mi;
+    s0 = 0;
+    load();
+    return 2;
   }
 };
 
@@ -545,7 +559,7 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
   uint64_t* empty = full + L.S;
   init_bars(full, empty, L.S, 2);
   TileIt it;
-  it.init(tb.mats, tb.nmats, tb.nsegs, L.TV);
+  it.init(tb.mats, tb.nmats, L.TV);
   const int warp = threadIdx.x >> 5;
   constexpr int fes = FES;
   (void)seed; (void)base_off;
@@ -701,7 +715,7 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
   uint64_t* empty = full + L.S;
   init_bars(full, empty, L.S, 2);
   TileIt it;
-  it.init(mats, nmats, nsegs, L.TV);
+  it.init(mats, nmats, L.TV);
   const int warp = threadIdx.x >> 5;
   constexpr int fes = FES;
 
@@ -798,7 +812,7 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
   uint64_t* empty = full + L.S;
   init_bars(full, empty, L.S, 2);
   TileIt it;
-  it.init(mats, nmats, nsegs, L.TV);
+  it.init(mats, nmats, L.TV);
   const int warp = threadIdx.x >> 5;
 
   if (warp == 0) {
@@ -905,7 +919,7 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
   uint64_t* empty = full + L.S;
   init_bars(full, empty, L.S, kCW);
   TileIt it;
-  it.init(mats, nmats, nsegs, L.TV);
+  it.init(mats, nmats, L.TV);
   const int warp = threadIdx.x >> 5;
 
   if (warp == 0) {

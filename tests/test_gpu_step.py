@@ -141,3 +141,15 @@ def test_step_rank64_bf16(tc):
 def test_step_rank128_bf16(tc):
     _run_case(1, 384, 1024, 128, 128, 256, seed=3, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16, steps=1,
               tc=tc)
+
+
+def test_step_on_reused_memory():
+    """Every workspace value the step reads is written by the step first: the set is built on
+    device memory that held NaNs and other data (the caching allocator hands it back), with
+    fewer streamed tiles than SMs so the per-CTA chunks of the streaming kernels are small."""
+    junk = torch.full((96 << 20,), float("nan"), device=DEV)
+    del junk
+    junk = torch.full((32 << 20,), 3.0e5, device=DEV)
+    del junk
+    _run_case(2, 384, 1280, 64, 16, 256, seed=7, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16,
+              schedule="quintic", tc=True)
