@@ -76,7 +76,7 @@ size_t coef_smem(int R, int RC) {
   const size_t rca = static_cast<size_t>(R < RC ? R : RC);
   return (static_cast<size_t>(R + 1) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
 }
-size_t ns_smem(int r) { return r <= 64 ? 4 * static_cast<size_t>(r) * r * sizeof(double) : 0; }
+size_t ns_smem(int r) { return r <= 64 ? 4 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
 size_t qr_apply_smem(int r) {
   const size_t r8 = static_cast<size_t>(pad8(r)), tv = static_cast<size_t>(tile_vectors(r));
   return r * r8 * sizeof(double) + 2 * tv * (r8 + 1) * sizeof(float);
@@ -107,7 +107,8 @@ void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bo
   const size_t rr = static_cast<size_t>(m.r) * m.r;
   m.gram_off = alloc_gram ? static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double)) : 0;
   m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
-  m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * rr * sizeof(double)) / sizeof(double)) : 0;
+  m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * static_cast<size_t>(pad8(static_cast<int>(m.r))) *
+                                                      ns_ld(static_cast<int>(m.r)) * sizeof(double)) / sizeof(double)) : 0;
   mats.push_back(m);
 }
 

@@ -249,47 +249,52 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
   }
 }
 
-// C = A B for r x r fp64 matrices in global memory, one CTA, 64 x 64 output tiles.
-// C must not alias A or B. Ends with a barrier so C is visible to the whole CTA.
-__device__ void cta_dgemm(double* __restrict__ C, const double* __restrict__ A, const double* __restrict__ B,
-                          int r, double* sh) {
-  double* As = sh;            // [16][64]
-  double* Bs = sh + 16 * 64;  // [16][64]
-  const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
-  for (int m0 = 0; m0 < r; m0 += 64) {
-    for (int n0 = 0; n0 < r; n0 += 64) {
-      double acc[4][4];
+// C = A B for r x r fp64 matrices that are symmetric and commute (polynomials of one
+// Gram matrix), so C is symmetric: only the upper 8 x 8 blocks are formed, with the fp64
+// MMA (m8n8k4), four blocks per warp at a time, and mirrored. Pitch ld (= rp + 4: a warp's
+// fragment loads fall in two wavefronts); rows and columns r..rp-1 are zero and stay zero.
+// Every position is written by exactly one thread. Ends with a barrier.
+__device__ __forceinline__ void dmma8x8x4(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+__device__ void cta_symm_mm(double* __restrict__ C, const double* __restrict__ A, const double* __restrict__ B,
+                            int rp, int ld) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int nb = rp >> 3, nq = nb * (nb + 1) / 2;
+  for (int q0 = warp; q0 < nq; q0 += 4 * (kThreads / 32)) {
+    int bi[4], bj[4];
+    double acc[4][2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-      for (int k0 = 0; k0 < r; k0 += 16) {
-        for (int e = tid; e < 1024; e += kThreads) {
-          const int mm = e >> 4, kk = e & 15;
-          As[kk * 64 + mm] = (m0 + mm < r && k0 + kk < r) ? A[(m0 + mm) * r + k0 + kk] : 0.0;
-          const int kb = e >> 6, nn = e & 63;
-          Bs[kb * 64 + nn] = (k0 + kb < r && n0 + nn < r) ? B[(k0 + kb) * r + n0 + nn] : 0.0;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          double a[4], b[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) { a[i] = As[kk * 64 + ti * 4 + i]; b[i] = Bs[kk * 64 + tj * 4 + i]; }
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
-        }
-        __syncthreads();
+    for (int u = 0; u < 4; ++u) {
+      int q = q0 + u * (kThreads / 32);
+      bi[u] = -1; bj[u] = 0;
+      acc[u][0] = 0.0; acc[u][1] = 0.0;
+      if (q < nq) {
+        int row = 0;
+        while (q >= nb - row) { q -= nb - row; ++row; }
+        bi[u] = row; bj[u] = row + q;
       }
+    }
+    for (int k0 = 0; k0 < rp; k0 += 4) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int u = 0; u < 4; ++u)
+        if (bi[u] >= 0)
+          dmma8x8x4(acc[u][0], acc[u][1], A[(8 * bi[u] + g) * ld + k0 + t], B[(k0 + t) * ld + 8 * bj[u] + g]);
+    }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = m0 + ti * 4 + i, n = n0 + tj * 4 + j;
-          if (m < r && n < r) C[m * r + n] = acc[i][j];
-        }
+    for (int u = 0; u < 4; ++u) {
+      if (bi[u] < 0) continue;
+      const int row = 8 * bi[u] + g;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = 8 * bj[u] + 2 * t + h;
+        if (bi[u] == bj[u] && col < row) continue;        // the mirror of the upper half
+        C[row * ld + col] = acc[u][h];
+        if (col != row) C[col * ld + row] = acc[u][h];
+      }
     }
   }
   __syncthreads();
@@ -314,63 +319,67 @@ struct NSArgs {
   float norm_floor;
 };
 
+// Pitch (doubles) of the r x r solve matrices: rows of pad8(r) + 4.
+__host__ __device__ inline int ns_ld(int r) { return pad8(r) + 4; }
+
 // =====================================================================================
 // Newton-Schulz in Gram space, one CTA per matrix (ds_mezo/kernels.py:26-164 rewritten):
 // X_k = X_0 P_k with P_k a polynomial of G_0 = X_0^T X_0, so the 12 X-space passes become
 // G <- S G S, P <- P S on r x r (fp64), S = c0 I + c1 G + c2 G^2. Stores the fp32 apply
-// matrix Pm with X[v,:] = x_v^T Pm for every vector x_v of the matrix.
+// matrix Pm with X[v,:] = x_v^T Pm for every vector x_v of the matrix (P is symmetric, so
+// tall and wide matrices use it alike).
 // =====================================================================================
 __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double sh[2 * 16 * 64];
   __shared__ double red[kThreads];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
+  const int rp = pad8(r), ld = ns_ld(r), mm = rp * ld;
   const int tid = threadIdx.x;
-  // r <= 64: the four r x r matrices live in shared memory; larger r in the fp64 workspace
+  // r <= 64: the four matrices live in shared memory; larger r in the fp64 workspace
   double* dw = (r <= 64) ? reinterpret_cast<double*>(smem_raw) : reinterpret_cast<double*>(tb.ws) + M.dw_off;
   double* G = dw;
-  double* P = dw + rr;
-  double* S = dw + 2 * rr;
-  double* U = dw + 3 * rr;
+  double* P = dw + mm;
+  double* S = dw + 2 * mm;
+  double* U = dw + 3 * mm;
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  for (int e = tid; e < 4 * mm; e += kThreads) dw[e] = 0.0;
+  __syncthreads();
   double tr = 0.0;
   for (int e = tid; e < rr; e += kThreads) {
-    const double s = strided_sum(part + e, M.nseg, rr);
-    G[e] = s;
-    const int a = e / r;
-    if (a * r + a == e) tr += s;
+    const double v = strided_sum(part + e, M.nseg, rr);
+    const int a = e / r, b = e - a * r;
+    G[a * ld + b] = v;
+    if (a == b) tr += v;
   }
   const double norm_sq = cta_sum(tr, red);
   const double inv = 1.0 / sqrt(fmax(norm_sq, static_cast<double>(ns.norm_floor)));
   const double inv2 = inv * inv;
   for (int e = tid; e < rr; e += kThreads) {
-    G[e] *= inv2;
-    const int a = e / r;
-    P[e] = (a * r + a == e) ? 1.0 : 0.0;
+    const int a = e / r, b = e - a * r;
+    G[a * ld + b] *= inv2;
+    P[a * ld + b] = (a == b) ? 1.0 : 0.0;
   }
   __syncthreads();
   for (int it = 0; it < ns.iters; ++it) {
     const double c0 = ns.c[it][0], c1 = ns.c[it][1], c2 = ns.c[it][2];
-    if (c2 != 0.0) cta_dgemm(S, G, G, r, sh);
+    if (c2 != 0.0) cta_symm_mm(S, G, G, rp, ld);
     for (int e = tid; e < rr; e += kThreads) {
-      const int a = e / r;
-      const double g2 = (c2 != 0.0) ? S[e] : 0.0;
-      S[e] = ((a * r + a == e) ? c0 : 0.0) + c1 * G[e] + c2 * g2;
+      const int a = e / r, b = e - a * r;
+      const double g2 = (c2 != 0.0) ? S[a * ld + b] : 0.0;
+      S[a * ld + b] = ((a == b) ? c0 : 0.0) + c1 * G[a * ld + b] + c2 * g2;
     }
     __syncthreads();
-    cta_dgemm(U, P, S, r, sh);
+    cta_symm_mm(U, P, S, rp, ld);            // P <- P S
     double* t = P; P = U; U = t;
-    cta_dgemm(U, S, G, r, sh);
-    cta_dgemm(G, U, S, r, sh);
+    cta_symm_mm(U, S, G, rp, ld);            // G <- S G S
+    cta_symm_mm(G, U, S, rp, ld);
   }
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   for (int e = tid; e < rr; e += kThreads) {
     const int a = e / r, b = e - a * r;
-    // tall (side A): X = X0 P -> row x^T P ; wide (side B): X = P X0 -> column P x = x^T P^T
-    const double pv = (M.side == 0) ? P[a * r + b] : P[b * r + a];
-    Pm[e] = static_cast<float>(pv * inv);
+    Pm[e] = static_cast<float>(P[a * ld + b] * inv);
   }
 }
 

@@ -435,9 +435,6 @@ __host__ __device__ inline Layout qr_layout(int R, int budget) {
   return L;
 }
 
-// Gram: mu (and var, z for the Kalman form), unpadded. fp64 copy of each tile in two
-// buffers (rows of rp + 1 doubles, columns permuted k -> (k % 4) * rp/4 + k / 4), the
-// upper 4 x 8 sub-blocks' accumulators, and the sub-block table.
 __host__ __device__ inline Layout gram_layout(int r, int kalman, int budget) {
   Layout L{};
   L.r = r;
@@ -899,11 +896,6 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
 // Tile image: side 0 X[v][c] with pitch rp + 8 doubles, side 1 X[c][v] with pitch TV + 4
 // (either way a fragment load of a warp touches 256 bytes in two wavefronts).
 // =====================================================================================
-__device__ __forceinline__ void dmma_8x8x4(double& d0, double& d1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-               : "+d"(d0), "+d"(d1)
-               : "d"(a), "d"(b));
-}
 // MAXB: upper 8 x 8 blocks per warp (5 up to r = 64, 17 up to r = 128)
 __host__ __device__ inline int gram_maxb(int r) {
   const int nb = (r + 7) / 8;
@@ -1040,7 +1032,7 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
       for (int v0 = 0; v0 < nv4; v0 += 4, xr += vstep) {
 #pragma unroll
         for (int q = 0; q < MAXB; ++q)
-          if (q < nmine) dmma_8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
+          if (q < nmine) dmma8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
       }
       ++i;
       seg_done = it.seg;
