@@ -38,6 +38,11 @@ CONFIGS = {
                schedule="cubic", seed=2, workload="Qwen2.5-7B-shaped adapter set (28 x 7 modules, rank 64)"),
     "70b": dict(layers=80, hidden=8192, inter=28672, kv=1024, rank=128, tokens=8192, fdt="bf16", adt="bf16",
                 schedule="cubic", seed=3, workload="Llama-3-70B-shaped adapter set (80 x 7 modules, rank 128)"),
+    # 16 SPSA directions per step: 32 +/- copies, per direction 8 Bernoulli(0.4) rollout
+    # rewards (4 per copy) turned into dd_k by the RLOO baseline, one joint Kalman update
+    "7b-k16": dict(layers=28, hidden=3584, inter=18944, kv=512, rank=64, tokens=4096, fdt="bf16", adt="bf16",
+                   schedule="cubic", seed=4, directions=16, rollouts=8,
+                   workload="Qwen2.5-7B-shaped adapter set (28 x 7 modules, rank 64), 16 SPSA directions"),
 }
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 METRIC = "ZO optimizer step ms (all adapters, 7B/70B shape) at 1/2/4/8 B200; % HBM roofline"
@@ -127,6 +132,7 @@ def alg_bytes(aset, cfg):
     """Algorithmic bytes per launch of each streaming kernel (whole set)."""
     f = aset.factors.element_size()
     N = aset.numel
+    K = aset.directions
     hb = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
     R = cfg["rank"]
     vr = sum(b.D * R for b in aset.bases) * 4
@@ -139,9 +145,10 @@ def alg_bytes(aset, cfg):
         "pi_apply": 3 * vr,                        # read W; write V (fp32) and [V_hi|V_lo]^T (bf16)
         "pi_split": 2 * vr,                        # read V, write bf16 [V_hi | V_lo]^T
         "bside": nB * (f + 4),                     # read B, var_B
-        "perturb": N * (3 * f + 12),               # read p, mu, var; write pos, neg, z
-        "gram": N * 12,                            # read mu, var, z
-        "apply": N * (2 * f + 20),                 # read p, mu, var, z; write p, mu, var
+        "perturb": N * (3 * f + 12),               # read p, mu, var; write pos, neg, z (one direction)
+        "gram": N * 12 if K == 1 else N * 4,       # read mu, var, z (K > 1: mu2 only)
+        "kalman_dirs": N * (16 + 4 * K),           # read mu, var, K z; write mu, var
+        "apply": N * (f + 4 + f),                  # read p, mu2; write p
     }
 
 
@@ -155,7 +162,8 @@ TRAFFIC_PER_ALG_BYTE = {"pi_y": 1.002, "pi_w": 1.020, "perturb": 0.999, "gram": 
 # ----------------------------------------------------------------------------- CPU oracle
 def cpu_oracle_sample(cfg, layers_in_sample=1, steps=1, warmup=0):
     """The oracle (reference algorithm restated on CPU, fp32) on `layers_in_sample` layers
-    of the workload; returns seconds per step for the sample."""
+    of the workload; returns seconds per step for the sample. With K directions the
+    perturbation runs K times and the joint update observes all K."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from oracle import reference_ops as ref
     from step_harness import make_inputs, oracle_state
@@ -166,15 +174,23 @@ def cpu_oracle_sample(cfg, layers_in_sample=1, steps=1, warmup=0):
     g = torch.Generator().manual_seed(cfg["seed"])
     rca = cfg["rank"]
     times = []
+    K = cfg.get("directions", 1)
     for i in range(warmup + steps):
-        draws = []
-        for m in mods:
-            draws.append(torch.randn(cfg["rank"], cfg["rank"], generator=g))
-            draws.append(torch.randn(m.d_out, rca, generator=g))
+        dirs = []
+        for _ in range(K):
+            draws = []
+            for m in mods:
+                draws.append(torch.randn(cfg["rank"], cfg["rank"], generator=g))
+                draws.append(torch.randn(m.d_out, rca, generator=g))
+            dirs.append(draws)
         t0 = time.perf_counter()
         st.step_count += 1
-        perts = ref.perturb_phase(st, H, draws, 3)
-        ref.update_phase(st, perts, 1.0)
+        if K == 1:
+            perts = ref.perturb_phase(st, H, dirs[0], 3)
+            ref.update_phase(st, perts, 1.0)
+        else:
+            perts = ref.perturb_phase_directions(st, H, dirs, 3)
+            ref.update_phase_directions(st, perts, [1.0] * K)
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     return sum(times) / len(times), torch.get_num_threads()
@@ -215,13 +231,23 @@ def main():
     from dsmezo_b200._lib import KERNEL_IDS, lib
     gen = torch.Generator(device=device)
     gen.manual_seed(cfg["seed"])
+    K = cfg.get("directions", 1)
     sstep = ShardedStep(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"], cfg["tokens"], eps=EPS,
                         total_steps=TOTAL_STEPS, generator=gen, factor_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
-                        schedule=cfg["schedule"], device=device, process_group=pg)
+                        schedule=cfg["schedule"], device=device, process_group=pg, directions=K)
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
     gather_events = []
+
+    def next_dd():
+        """The step's projected-gradient scalar(s): seeded N(0,1) x 10 for one direction; for K
+        directions the RLOO scalars of seeded Bernoulli(0.4) rollout rewards."""
+        if K == 1:
+            return float(torch.randn((), generator=dd_gen)) * 10.0
+        from dsmezo_b200 import rloo_direction_scalars
+        rewards = torch.bernoulli(torch.full((K, cfg["rollouts"]), 0.4), generator=dd_gen)
+        return rloo_direction_scalars(rewards, EPS)
 
     def step(record=False):
         sstep.perturb()
@@ -233,7 +259,7 @@ def main():
             if record:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
-        dd = sstep.broadcast_dd(float(torch.randn((), generator=dd_gen)) * 10.0)
+        dd = sstep.broadcast_dd(next_dd())
         sstep.update(dd)
         if world > 1:
             if record:
@@ -256,7 +282,8 @@ def main():
 
     # per-kernel probes over the timed region
     per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 3, "pi_split": 3, "bside": 1,
-                "coef": 1, "draw": 1, "perturb": 1, "kalman_sum": 1, "gram": 1, "ns_solve": 1, "apply": 1}
+                "coef": K, "draw": K, "perturb": K, "kalman_sum": K, "kalman_dirs": 1, "gram": 1, "ns_solve": 1,
+                "apply": 1}
     probes = {}
     for name, n in per_step.items():
         cap = n * args.steps
@@ -307,7 +334,7 @@ def main():
     if not args.no_e2e:
         host_H = torch.empty(aset.H_arena.numel(), dtype=aset.H_arena.dtype, pin_memory=True)
         host_H.copy_(aset.H_arena)
-        host_out = torch.empty(2, dtype=torch.float64, pin_memory=True)
+        host_out = torch.empty(aset.kalman_sums().numel(), dtype=torch.float64, pin_memory=True)
         n_e2e = max(1, min(args.steps, 5))
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -320,7 +347,7 @@ def main():
             host_out.copy_(aset.kalman_sums(), non_blocking=True)
             if world > 1:
                 sstep.gather("pos", "neg")
-            dd = sstep.broadcast_dd(float(torch.randn((), generator=dd_gen)) * 10.0)
+            dd = sstep.broadcast_dd(next_dd())
             sstep.update(dd)
             if world > 1:
                 sstep.gather("factors")
@@ -334,7 +361,7 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         e2e = {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": host_H.numel() * host_H.element_size(),
-               "d2h_bytes_per_step": 16, "steps": n_e2e}
+               "d2h_bytes_per_step": host_out.numel() * 8, "steps": n_e2e}
 
     if rank != 0:
         if world > 1:
@@ -358,7 +385,10 @@ def main():
     # whole model: every rank's factors and activations
     f = aset.factors.element_size()
     act_layer = cfg["tokens"] * (3 * cfg["hidden"] + cfg["inter"]) * aset.H_arena.element_size()
-    step_bytes = sum(sstep.layout.sizes) * (4 * f + 16) + 3 * act_layer * cfg["layers"]
+    # per element: read p, mu, var and write p, mu, var once; per direction write pos, neg, z
+    # and read z back (K > 1)
+    per_elem = 2 * f + 16 + K * (2 * f + (4 if K == 1 else 8))
+    step_bytes = sum(sstep.layout.sizes) * per_elem + 3 * act_layer * cfg["layers"]
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
@@ -373,6 +403,7 @@ def main():
         "config": {"workload": cfg["workload"], "layers": cfg["layers"], "hidden": cfg["hidden"],
                    "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
                    "factor_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
+                   "directions": K,
                    "power_iters": 3, "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (activations %.2f GB per step per GPU)" %
                          (sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9)},

@@ -245,6 +245,9 @@ struct dsmz_plan {
   int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
   int sm_count = 0;
   int grid_m = 0, grid_w = 0;        // streaming-kernel grids (chunks) of mats and w2
+  int ndir = 1;                      // SPSA directions per step
+  int64_t dstride_f = 0, dstride_z = 0;
+  uint64_t rng_inc1 = 0, rng_dir_stride = 0;   // one direction's generator advance (this plan / all ranks)
   sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
   int factor_dtype = DSMZ_F32;
   int r = 0, R = 0, RC = 0;
@@ -292,6 +295,10 @@ struct dsmz_plan {
     t.ws = workspace;
     t.seg_kal_off = seg_kal_off;
     t.kal_sum_off = kal_sum_off;
+    t.ndir = ndir;
+    t.dir = 0;
+    t.dstride_f = dstride_f;
+    t.dstride_z = dstride_z;
     return t;
   }
 
@@ -476,6 +483,45 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   return 0;
 }
 
+// K directions: joint Kalman observation (k_kalman_dirs) writes mu2 / var2, then the plain
+// fp64 Gram of mu2, the Newton-Schulz solve and the apply.
+int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, const NSArgs& ns, cudaStream_t s) {
+  if (P->mats.empty()) return 0;
+  const Tables tb = P->tables();
+  const int r = P->r;
+  const int nm = static_cast<int>(P->mats.size());
+  int rc;
+  int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
+  const bool small = sk::gram_maxb(r) <= 5;
+  if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lg.total))) return rc;
+  if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lg.total))) return rc;
+  if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
+  if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
+  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
+  P->probe_begin(DSMZ_KID_KALMAN_DIRS, s);
+  sk::k_kalman_dirs<<<8 * P->sm_count, 256, 0, s>>>(tb, kd, P->Lg.TV);   // plain stream: many CTAs per SM
+  P->probe_end(DSMZ_KID_KALMAN_DIRS, s);
+  DSMZ_LAUNCHED("K-direction Kalman update");
+  const KalmanIn none{};
+  P->probe_begin(DSMZ_KID_GRAM, s);
+  if (small) sk::k_sgram<0, 5><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
+  else sk::k_sgram<0, 17><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
+  P->probe_end(DSMZ_KID_GRAM, s);
+  DSMZ_LAUNCHED("Gram of the updated momentum");
+  P->probe_begin(DSMZ_KID_NS_SOLVE, s);
+  k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, tb.mats, ns);
+  P->probe_end(DSMZ_KID_NS_SOLVE, s);
+  DSMZ_LAUNCHED("Newton-Schulz solve");
+  P->probe_begin(DSMZ_KID_APPLY, s);
+  if (P->factor_dtype == DSMZ_BF16)
+    sk::k_sapply<2><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+  else
+    sk::k_sapply<4><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+  P->probe_end(DSMZ_KID_APPLY, s);
+  DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
+  return 0;
+}
+
 KalmanIn make_kin(float beta, float q, float dd, float floor_) {
   KalmanIn k;
   k.beta = beta;
@@ -497,27 +543,32 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   const bool bf = P->factor_dtype == DSMZ_BF16;
   if ((rc = set_smem(sk::k_sperturb<0, 2>, P->Lp.total))) return rc;
   if ((rc = set_smem(sk::k_sperturb<0, 4>, P->Lp.total))) return rc;
-  P->probe_begin(DSMZ_KID_DRAW, s);
-  sk::k_draw_zca<<<P->ndblk, 256, 0, s>>>(tb, seed, offset);
-  P->probe_end(DSMZ_KID_DRAW, s);
-  DSMZ_LAUNCHED("Zc_A draws");
   P->probe_begin(DSMZ_KID_BSIDE, s);
-  k_bside<<<P->nchunks, kThreads, 0, s>>>(tb);
+  k_bside<<<P->nchunks, kThreads, 0, s>>>(tb);     // B V and var_B V^2: the same for every direction
   P->probe_end(DSMZ_KID_BSIDE, s);
   DSMZ_LAUNCHED("B-side sums");
-  P->probe_begin(DSMZ_KID_COEF, s);
-  k_coef<0><<<static_cast<int>(P->mods.size()), kThreads, cs, s>>>(tb, seed, offset, floor_);
-  P->probe_end(DSMZ_KID_COEF, s);
-  DSMZ_LAUNCHED("AGZO coefficients");
-  P->probe_begin(DSMZ_KID_PERTURB, s);
-  if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
-  else sk::k_sperturb<0, 4><<<P->grid_m, sk::kST, P->Lp.total, s>>>(tb, P->Lp, seed, offset, eps, kin, err);
-  P->probe_end(DSMZ_KID_PERTURB, s);
-  DSMZ_LAUNCHED("perturbation");
-  P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
-  k_kalman_reduce<<<1, kThreads, 0, s>>>(tb);
-  P->probe_end(DSMZ_KID_KALMAN_SUM, s);
-  DSMZ_LAUNCHED("Kalman sums");
+  for (int k = 0; k < P->ndir; ++k) {
+    Tables td = tb;
+    td.dir = k;
+    const uint64_t off = offset + static_cast<uint64_t>(k) * P->rng_dir_stride;
+    P->probe_begin(DSMZ_KID_DRAW, s);
+    sk::k_draw_zca<<<P->ndblk, 256, 0, s>>>(td, seed, off);
+    P->probe_end(DSMZ_KID_DRAW, s);
+    DSMZ_LAUNCHED("Zc_A draws");
+    P->probe_begin(DSMZ_KID_COEF, s);
+    k_coef<0><<<static_cast<int>(P->mods.size()), kThreads, cs, s>>>(td, seed, off, floor_, k == 0 ? 1 : 0);
+    P->probe_end(DSMZ_KID_COEF, s);
+    DSMZ_LAUNCHED("AGZO coefficients");
+    P->probe_begin(DSMZ_KID_PERTURB, s);
+    if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kST, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    else sk::k_sperturb<0, 4><<<P->grid_m, sk::kST, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    P->probe_end(DSMZ_KID_PERTURB, s);
+    DSMZ_LAUNCHED("perturbation");
+    P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
+    k_kalman_reduce<<<1, kThreads, 0, s>>>(td);
+    P->probe_end(DSMZ_KID_KALMAN_SUM, s);
+    DSMZ_LAUNCHED("Kalman sums");
+  }
   return 0;
 }
 
@@ -633,9 +684,16 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: bad module/basis arrays");
   if (d->sm_count <= 0 || d->max_threads_per_sm < 256)
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: sm_count / max_threads_per_sm describe the device");
+  if (d->directions < 0 || d->directions > DSMZ_MAX_DIRECTIONS)
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: directions must be in [0, DSMZ_MAX_DIRECTIONS]");
+  if (d->directions > 1 && (d->dir_stride_factor <= 0 || d->dir_stride_z <= 0))
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: several directions need positive direction strides");
   auto* P = new dsmz_plan();
   P->factor_dtype = d->factor_dtype;
   P->sm_count = d->sm_count;
+  P->ndir = d->directions > 1 ? d->directions : 1;
+  P->dstride_f = P->ndir > 1 ? d->dir_stride_factor : 0;
+  P->dstride_z = P->ndir > 1 ? d->dir_stride_z : 0;
   P->err_off = P->ws.take(256);      // device error word of the bounded waits
   // bases
   for (int i = 0; i < d->num_bases; ++i) {
@@ -733,11 +791,13 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     add_matrix(P->mats, P->ws, b, P->nsegs, true, false);
     P->mods.push_back(md);
   }
-  P->rng_increment = off - d->rng_offset_before;
+  P->rng_inc1 = off - d->rng_offset_before;
+  P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
+  P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
   if (!P->mats.empty()) P->nsegs = chunk_matrices(P->mats, sk::stream_tv(P->r), P->sm_count, &P->ws, &P->grid_m);
   if (!P->w2.empty()) chunk_matrices(P->w2, sk::stream_tv(P->R), P->sm_count, nullptr, &P->grid_w);
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
-  P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * sizeof(double)) / sizeof(double));
+  P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * static_cast<size_t>(P->ndir) * sizeof(double)) / sizeof(double));
   const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
   if (P->r > 0) {
     P->Lp = sk::perturb_layout(P->r, P->r, P->RC, P->r < P->RC ? P->r : P->RC, fes, 0, kStreamSmem);
@@ -767,7 +827,7 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   // per iteration: Y, W, [Gram of W on the CUDA-core path], partial sums, Cholesky, V;
   // plus the first bf16 split of the caller's basis on the tensor-core path
   if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->tc ? 5 : 6) + (p->tc ? 1 : 0);
-  if (!p->mods.empty()) n += 5 + 3;
+  if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }
 
@@ -832,10 +892,31 @@ double* dsmz_step_kalman_sums(const dsmz_plan* P) {
   return reinterpret_cast<double*>(P->workspace) + P->kal_sum_off;
 }
 
+int32_t dsmz_plan_directions(const dsmz_plan* P) { return P ? P->ndir : 0; }
+
+int dsmz_step_update_directions(const dsmz_plan* P, const float* dd, int32_t n, float beta, float q, float eta,
+                                float norm_floor, const dsmz_ns_schedule* schedule, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_step_update_directions");
+  if (rc) return rc;
+  if (!dd || n != P->ndir) return fail(DSMZ_ERR_INVALID, "dsmz_step_update_directions: need one dd per direction");
+  if (schedule && (schedule->iters < 0 || schedule->iters > DSMZ_MAX_NS_ITERS))
+    return fail(DSMZ_ERR_INVALID, "dsmz_step_update_directions: schedule iters out of range");
+  if (n == 1) return dsmz_step_update(P, dd[0], beta, q, eta, norm_floor, schedule, stream);
+  sk::KalmanDirs kd{};
+  kd.beta = beta;
+  kd.beta2 = static_cast<float>(static_cast<double>(beta) * static_cast<double>(beta));
+  kd.q = q;
+  kd.floor_ = norm_floor;
+  kd.n = n;
+  for (int k = 0; k < n; ++k) kd.dd[k] = dd[k];
+  return run_update_dirs(P, kd, eta, make_ns(schedule, norm_floor), static_cast<cudaStream_t>(stream));
+}
+
 int dsmz_step_update(const dsmz_plan* P, float dd, float beta, float q, float eta, float norm_floor,
                      const dsmz_ns_schedule* schedule, dsmz_stream_t stream) {
   int rc = plan_ready(P, "dsmz_step_update");
   if (rc) return rc;
+  if (P->ndir != 1) return fail(DSMZ_ERR_INVALID, "dsmz_step_update: the plan has several directions");
   if (schedule && (schedule->iters < 0 || schedule->iters > DSMZ_MAX_NS_ITERS))
     return fail(DSMZ_ERR_INVALID, "dsmz_step_update: schedule iters out of range");
   return run_update(P, make_kin(beta, q, dd, norm_floor), eta, make_ns(schedule, norm_floor),
@@ -1088,7 +1169,7 @@ int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t bs0,
   if ((rc = set_smem(k_perturb<1>, ps))) return rc;
   k_bside<<<P.nchunks, kThreads, 0, s>>>(tb);
   DSMZ_LAUNCHED("agzo B V");
-  k_coef<1><<<1, kThreads, cs, s>>>(tb, 0, 0, norm_floor);
+  k_coef<1><<<1, kThreads, cs, s>>>(tb, 0, 0, norm_floor, 1);
   DSMZ_LAUNCHED("agzo QR");
   k_perturb<1><<<P.nsegs, kThreads, ps, s>>>(tb, 0, 0, eps, KalmanIn{});
   DSMZ_LAUNCHED("agzo z");

@@ -72,7 +72,10 @@ struct Tables {
   int32_t factor_dtype; int32_t ndblk;                 // ndblk: blocks of the Zc_A draw
   char* ws;                                            // workspace base
   int64_t seg_kal_off;        // doubles: nsegs * 2 per-segment Kalman partials
-  int64_t kal_sum_off;        // doubles: 2 summed Kalman scalars
+  int64_t kal_sum_off;        // doubles: 2 summed Kalman scalars per direction
+  int32_t ndir, dir;          // directions; the one a perturbation launch writes
+  int64_t dstride_f;          // factor elements between directions' pos/neg copies
+  int64_t dstride_z;          // fp32 elements between directions' z
 };
 
 // ------------------------------------------------------------------ dtype helpers

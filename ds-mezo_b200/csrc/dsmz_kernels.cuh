@@ -748,7 +748,8 @@ __global__ void __launch_bounds__(kThreads) k_bside(Tables tb) {
 // by one warp. MODE 0 draws Zc_B from the torch Philox stream, MODE 1 copies it.
 // =====================================================================================
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uint64_t base_off, float norm_floor) {
+__global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uint64_t base_off, float norm_floor,
+                                                   int with_qr) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const ModD D = tb.mods[blockIdx.x];
   const int R = D.r, RC = D.rc, RCA = D.rca;
@@ -773,6 +774,8 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       ZcB[e] = D.zcB_ext[e];
     }
   }
+  // Later directions of a many-direction step reuse the Q of direction 0 (B V is the same).
+  if (!with_qr) return;
   __syncthreads();
   // Q = QR(B V)[:, :RCA] with a positive diagonal, the factor the reference's modified
   // Gram-Schmidt produces (ds_mezo/kernels.py:328-340), as CholeskyQR2 in fp64: two rounds of
@@ -979,7 +982,7 @@ __global__ void __launch_bounds__(kThreads) k_kalman_reduce(Tables tb) {
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    double* out = reinterpret_cast<double*>(tb.ws) + tb.kal_sum_off;
+    double* out = reinterpret_cast<double*>(tb.ws) + tb.kal_sum_off + 2 * tb.dir;
     out[0] = red[0][0];
     out[1] = red[1][0];
   }

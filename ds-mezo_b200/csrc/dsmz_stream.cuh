@@ -636,9 +636,11 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
           named_sync(kBarTeam0 + team, kTT);
           const int n = nv * r;
           const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
-          float* zt = tile_ptr(M.z, M, it.s0, 4);
-          void* post = tile_ptr(reinterpret_cast<char*>(M.pos), M, it.s0, FES);
-          void* negt = tile_ptr(reinterpret_cast<char*>(M.neg), M, it.s0, FES);
+          // this launch's direction: its z and +/- copies sit a fixed stride past direction 0's
+          float* zt = tile_ptr(M.z + static_cast<int64_t>(tb.dir) * tb.dstride_z, M, it.s0, 4);
+          const int64_t fo = static_cast<int64_t>(tb.dir) * tb.dstride_f * FES;
+          void* post = tile_ptr(reinterpret_cast<char*>(M.pos) + fo, M, it.s0, FES);
+          void* negt = tile_ptr(reinterpret_cast<char*>(M.neg) + fo, M, it.s0, FES);
           const void* ps = stage + L.off[0];
           const float* ms = reinterpret_cast<const float*>(stage + L.off[1]);
           const float* vsg = reinterpret_cast<const float*>(stage + L.off[2]);
@@ -1062,6 +1064,77 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
       }
     } while (ok && adv == 1);
   }
+}
+
+// =====================================================================================
+// Kalman observation update for K directions (no reference counterpart; the reference
+// observes one direction per step): with innov_k = dd_k - y_hat_k and
+// inv_k = 1 / (s_k + norm_floor), per element
+//   mu1 = mu * beta, var1 = var * beta^2 + q                 (controller.py:267-268)
+//   mu2 = mu1 + var1 * sum_k z_k * inv_k * innov_k
+//   var2 = var1 * (1 - var1 * sum_k z_k^2 * inv_k)
+// i.e. the joint observation of the K directions with the innovation covariance's
+// diagonal (its off-diagonal terms are O(1/sqrt(n)) for independent directions). A plain
+// coalesced pass over a chunk of tiles per CTA (any grid: no per-segment output); the
+// fp64 Gram of mu2 follows (k_sgram<0>).
+// =====================================================================================
+struct KalmanDirs {
+  float beta, beta2, q, floor_;
+  int32_t n;
+  float dd[DSMZ_MAX_DIRECTIONS];
+};
+
+__global__ void __launch_bounds__(256) k_kalman_dirs(Tables tb, KalmanDirs kd, int TV) {
+  __shared__ float innov[DSMZ_MAX_DIRECTIONS], invs[DSMZ_MAX_DIRECTIONS];
+  const double* sums = reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off;
+  if (threadIdx.x < kd.n) {
+    const int k = threadIdx.x;
+    const float y_hat = static_cast<float>(sums[2 * k]);
+    const float S = __fadd_rn(static_cast<float>(sums[2 * k + 1]), kd.floor_);
+    invs[k] = __fdiv_rn(1.0f, S);
+    innov[k] = __fsub_rn(kd.dd[k], y_hat);
+  }
+  __syncthreads();
+  TileIt it;
+  it.init(tb.mats, tb.nmats, TV);
+  if (!it.start_seg()) return;
+  int adv;
+  do {
+    const MatD& M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r), nv = it.nv();
+    const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
+    float* mut = tile_ptr(M.mu, M, it.s0, 4);
+    float* vat = tile_ptr(M.var, M, it.s0, 4);
+    const float* zt = tile_ptr(M.z, M, it.s0, 4);
+    auto body = [&](auto side_tag) {
+      constexpr int SIDE = decltype(side_tag)::value;
+      Walk<SIDE> w(threadIdx.x, 256, r, nv);
+      for (int e = threadIdx.x; e < nv * r; e += 256, w.next()) {
+        const int g = w.goff(ld, cs);
+        const float mu1 = __fmul_rn(mut[g], kd.beta);
+        const float var1 = __fadd_rn(__fmul_rn(vat[g], kd.beta2), kd.q);
+        float am = 0.f, av = 0.f;
+        for (int k0 = 0; k0 < kd.n; k0 += 8) {       // eight independent loads in flight
+          float z[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            z[u] = (k0 + u < kd.n) ? zt[static_cast<int64_t>(k0 + u) * tb.dstride_z + g] : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (k0 + u >= kd.n) break;
+            const float zi = __fmul_rn(z[u], invs[k0 + u]);
+            am = __fmaf_rn(zi, innov[k0 + u], am);
+            av = __fmaf_rn(zi, z[u], av);
+          }
+        }
+        mut[g] = __fmaf_rn(var1, am, mu1);
+        vat[g] = __fmul_rn(var1, __fsub_rn(1.0f, __fmul_rn(var1, av)));
+      }
+    };
+    if (M.side == 0) body(std::integral_constant<int, 0>{});
+    else body(std::integral_constant<int, 1>{});
+    adv = it.next();
+  } while (adv != 0);
 }
 
 }  // namespace sk

@@ -11,9 +11,9 @@ All compute runs in libdsmezo.so (C ABI in include/dsmezo.h); there is no CPU pa
 from . import kernels  # noqa: F401
 from ._lib import DsmzError, lib  # noqa: F401
 from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ZOController, device_layout,  # noqa: F401
-                          draw_increments, kalman_beta_q, transformer_adapter_shapes)
+                          draw_increments, kalman_beta_q, rloo_direction_scalars, transformer_adapter_shapes)
 from .sharding import ShardedStep, ShardLayout, partition_layers, shard_layout  # noqa: F401
 
-__all__ = ["kernels", "AdapterSet", "ZOController", "ModuleShape", "BasisShape", "transformer_adapter_shapes",
+__all__ = ["kernels", "rloo_direction_scalars", "AdapterSet", "ZOController", "ModuleShape", "BasisShape", "transformer_adapter_shapes",
            "draw_increments", "device_layout", "kalman_beta_q", "DsmzError", "lib", "ShardedStep", "ShardLayout",
            "partition_layers", "shard_layout"]

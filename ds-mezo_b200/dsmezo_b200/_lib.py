@@ -55,7 +55,13 @@ class PlanDesc(ctypes.Structure):
         ("sm_count", c_int32), ("max_threads_per_sm", c_int32),
         ("rng_offset_before", c_uint64),
         ("flags", ctypes.c_uint32),
+        ("directions", c_int32), ("pad0", c_int32),
+        ("dir_stride_factor", c_int64), ("dir_stride_z", c_int64),
+        ("rng_direction_stride", c_uint64),
     ]
+
+
+MAX_DIRECTIONS = 32
 
 
 PLAN_SIMT_POWER_ITER = 1
@@ -95,6 +101,9 @@ SIGNATURES = {
     "dsmz_plan_launch_count": (c_int32, [c_void_p, c_int32]),
     "dsmz_plan_bind": (c_int32, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_void_p]),
     "dsmz_plan_uses_tensor_cores": (c_int32, [c_void_p]),
+    "dsmz_plan_directions": (c_int32, [c_void_p]),
+    "dsmz_step_update_directions": (c_int32, [c_void_p, POINTER(c_float), c_int32, c_float, c_float, c_float,
+                                              c_float, POINTER(NSSchedule), c_void_p]),
     "dsmz_plan_device_error": (c_int32, [c_void_p, c_void_p]),
     "dsmz_step_power_iteration": (c_int32, [c_void_p, c_int32, c_float, c_void_p]),
     "dsmz_step_perturb": (c_int32, [c_void_p, c_uint64, c_uint64, c_float, c_float, c_float, c_float, c_void_p]),
@@ -106,7 +115,8 @@ SIGNATURES = {
 }
 
 KERNEL_IDS = {"pi_y": 0, "pi_w": 1, "pi_gram": 2, "pi_chol": 3, "pi_apply": 4, "bside": 5, "coef": 6,
-              "perturb": 7, "kalman_sum": 8, "gram": 9, "ns_solve": 10, "apply": 11, "pi_split": 12, "draw": 13}
+              "perturb": 7, "kalman_sum": 8, "gram": 9, "ns_solve": 10, "apply": 11, "pi_split": 12, "draw": 13,
+              "kalman_dirs": 14}
 
 _lib = None
 

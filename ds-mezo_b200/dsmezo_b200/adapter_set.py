@@ -96,7 +96,8 @@ class AdapterSet:
     def __init__(self, modules: Sequence[ModuleShape], bases: Sequence[BasisShape], rank: int, basis_width: int,
                  factor_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
-                 tensor_core_power_iter: bool = True, capacity: int = 0):
+                 tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
+                 rng_direction_stride: int = 0):
         if factor_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("factor and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -106,6 +107,9 @@ class AdapterSet:
         self.basis_width = int(basis_width)
         self.factor_dtype = factor_dtype
         self.act_dtype = act_dtype
+        if not 1 <= int(directions) <= _lib.MAX_DIRECTIONS:
+            raise ValueError(f"directions must be in [1, {_lib.MAX_DIRECTIONS}]")
+        self.directions = int(directions)
         r = self.rank
         self.offA, self.offB = [], []
         n = 0
@@ -120,12 +124,15 @@ class AdapterSet:
         cap = max(n, int(capacity))
         self.capacity = cap
         dev = self.device
+        K = self.directions
         self.factors = torch.zeros(cap, dtype=factor_dtype, device=dev)
-        self.pos = torch.zeros(cap, dtype=factor_dtype, device=dev)
-        self.neg = torch.zeros(cap, dtype=factor_dtype, device=dev)
+        # direction k's +/- copies and z follow direction 0's at a fixed stride
+        self.pos = torch.zeros(K * cap, dtype=factor_dtype, device=dev)
+        self.neg = torch.zeros(K * cap, dtype=factor_dtype, device=dev)
         self.mu = torch.zeros(n, dtype=torch.float32, device=dev)
         self.var = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.z = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.z = torch.zeros(K * n, dtype=torch.float32, device=dev)
+        self._rng_dir_stride = int(rng_direction_stride)
         self.scratch = torch.zeros(n, dtype=torch.float32, device=dev) if keep_ns_output else None
         self.offH, self.offV = [], []
         nh = nv = 0
@@ -148,6 +155,16 @@ class AdapterSet:
     def B(self, i, t=None):
         m = self.modules[i]
         return (self.factors if t is None else t)[self.offB[i]:self.offB[i] + self.rank * m.d_in].view(self.rank, m.d_in)
+
+    def pos_dir(self, k: int) -> torch.Tensor:
+        """Direction k's + copy of the factor arena."""
+        return self.pos[k * self.capacity:(k + 1) * self.capacity]
+
+    def neg_dir(self, k: int) -> torch.Tensor:
+        return self.neg[k * self.capacity:(k + 1) * self.capacity]
+
+    def z_dir(self, k: int) -> torch.Tensor:
+        return self.z[k * self.numel:(k + 1) * self.numel]
 
     def H(self, b):
         s = self.bases[b]
@@ -202,6 +219,10 @@ class AdapterSet:
         desc.sm_count, desc.max_threads_per_sm = self.layout
         desc.rng_offset_before = rng_offset_before
         desc.flags = self._flags
+        desc.directions = self.directions
+        desc.dir_stride_factor = self.capacity
+        desc.dir_stride_z = self.numel
+        desc.rng_direction_stride = self._rng_dir_stride
         handle = ctypes.c_void_p()
         check(L.dsmz_plan_create(ctypes.byref(desc), ctypes.byref(handle)), "dsmz_plan_create")
         self._plan = handle
@@ -212,7 +233,7 @@ class AdapterSet:
                                self.workspace.numel(), self._stream()), "dsmz_plan_bind")
         addr = L.dsmz_step_kalman_sums(handle)
         off = addr - self.workspace.data_ptr()
-        self._kal = self.workspace[off:off + 16].view(torch.float64)
+        self._kal = self.workspace[off:off + 16 * self.directions].view(torch.float64)
 
     def __del__(self):
         h = getattr(self, "_plan", None)
@@ -248,14 +269,43 @@ class AdapterSet:
                                       float(q), float(norm_floor), self._stream()), "perturbation")
 
     def kalman_sums(self) -> torch.Tensor:
-        """Device view of the rank-local (sum z*mu1, sum z^2*var1); all-reduce it in place."""
+        """Device view of the rank-local (sum z*mu1, sum z^2*var1) of every direction
+        (2 doubles per direction); all-reduce it in place."""
         return self._kal
 
-    def update(self, dd: float, beta: float, q: float, eta: float, norm_floor: float = FLT_MIN,
-               schedule="cubic"):
+    def update(self, dd, beta: float, q: float, eta: float, norm_floor: float = FLT_MIN, schedule="cubic"):
+        """dd: the projected-gradient scalar (one direction) or one per direction."""
         sched = _lib.schedule(schedule)
-        check(lib().dsmz_step_update(self._plan, float(dd), float(beta), float(q), float(eta), float(norm_floor),
-                                     sched, self._stream()), "update")
+        dds = [float(dd)] if isinstance(dd, (int, float)) else [float(x) for x in dd]
+        if len(dds) != self.directions:
+            raise ValueError(f"need {self.directions} projected-gradient scalars, got {len(dds)}")
+        if self.directions == 1:
+            check(lib().dsmz_step_update(self._plan, dds[0], float(beta), float(q), float(eta), float(norm_floor),
+                                         sched, self._stream()), "update")
+            return
+        arr = (ctypes.c_float * len(dds))(*dds)
+        check(lib().dsmz_step_update_directions(self._plan, arr, len(dds), float(beta), float(q), float(eta),
+                                                float(norm_floor), sched, self._stream()), "update")
+
+
+def rloo_direction_scalars(rewards: torch.Tensor, eps: float) -> List[float]:
+    """Projected-gradient scalars of K directions from their rollout rewards.
+
+    rewards: (K, N) with the first N/2 rollouts of each direction scored under its + copy
+    and the rest under its - copy. Each rollout's advantage is its reward minus the RLOO
+    baseline of its direction, (sum - r) / (N - 1); the loss of a copy is minus the mean
+    advantage of its rollouts, and dd_k = (L+ - L-) / (2 eps) as in
+    ds_mezo/controller.py:307 (no reference counterpart for K > 1: the reference scores
+    one direction per step with shrinkage RLOO)."""
+    r = rewards.double()
+    K, N = r.shape
+    if N < 2 or N % 2:
+        raise ValueError("need an even number (>= 2) of rollouts per direction")
+    base = (r.sum(dim=1, keepdim=True) - r) / (N - 1)
+    adv = r - base
+    lp = -adv[:, : N // 2].mean(dim=1)
+    lm = -adv[:, N // 2:].mean(dim=1)
+    return ((lp - lm) / (2.0 * eps)).tolist()
 
 
 def kalman_beta_q(step_count: int, total_steps: int, eps: float):
@@ -310,6 +360,7 @@ class ZOController:
             from .sharding import allreduce_sums
             allreduce_sums(self.aset.kalman_sums(), self.pg)
 
-    def update(self, dd: float):
+    def update(self, dd):
+        """dd: one projected-gradient scalar, or one per direction."""
         self.aset.update(dd, self.beta, self.q, self.eta, self.norm_floor, self.schedule)
         self._step_lr()

@@ -113,7 +113,8 @@ class ShardedStep:
 
     def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
                  eps: float, total_steps: int, generator: torch.Generator, factor_dtype=torch.bfloat16,
-                 act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3):
+                 act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
+                 directions: int = 1):
         import torch.distributed as dist
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if process_group is not None else 1
@@ -122,14 +123,18 @@ class ShardedStep:
         self.layout = shard_layout(layers, hidden, inter, kv, rank_r, tokens, self.world, *layout)
         lr = self.layout.ranges[self.rank]
         mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)
+        # one direction's draws over the whole model: the stride between directions' draws
+        stride = self.layout.rng_increment_total
         self.aset = AdapterSet(mods, bases, rank_r, rank_r, factor_dtype=factor_dtype, act_dtype=act_dtype,
                                device=device, rng_offset_before=self.layout.rng_offset_before(self.rank),
-                               layout=layout, capacity=self.layout.capacity)
+                               layout=layout, capacity=self.layout.capacity, directions=directions,
+                               rng_direction_stride=stride)
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=process_group if self.world > 1 else None,
-                                rng_increment_total=self.layout.rng_increment_total)
+                                rng_increment_total=stride * directions)
         cap = self.layout.capacity
-        self.gathered = {name: torch.empty(cap * self.world, dtype=factor_dtype, device=device)
+        self.gathered = {name: torch.empty(cap * self.world * (1 if name == "factors" else directions),
+                                           dtype=factor_dtype, device=device)
                          for name in ("factors", "pos", "neg")} if self.world > 1 else None
 
     # ------------------------------------------------------------------ phases
@@ -137,13 +142,22 @@ class ShardedStep:
         """Power iteration, perturbation, pos/neg; Kalman sums all-reduced across ranks."""
         self.ctl.perturb()
 
-    def broadcast_dd(self, dd: float, src: int = 0) -> float:
-        """The projected-gradient scalar dd = (L+ - L-) / (2 eps) from the scoring rank."""
+    def broadcast_dd(self, dd, src: int = 0):
+        """The projected-gradient scalar(s) dd = (L+ - L-) / (2 eps) from the scoring rank
+        (one float, or one per direction)."""
+        if isinstance(dd, (int, float)):
+            if self.world == 1:
+                return float(dd)
+            return broadcast_scalar(dd, self.pg, src, self.aset.device)
+        vals = [float(x) for x in dd]
         if self.world == 1:
-            return float(dd)
-        return broadcast_scalar(dd, self.pg, src, self.aset.device)
+            return vals
+        import torch.distributed as dist
+        t = torch.tensor(vals, dtype=torch.float64, device=self.aset.device)
+        dist.broadcast(t, src=src, group=self.pg)
+        return t.tolist()
 
-    def update(self, dd: float):
+    def update(self, dd):
         self.ctl.update(dd)
 
     def gather(self, *names: str):

@@ -170,7 +170,21 @@ typedef struct dsmz_plan_desc {
   uint64_t rng_offset_before;           /* generator advance of the draws that precede
                                            these modules (other ranks' modules); 0 on 1 GPU */
   uint32_t flags;                       /* DSMZ_PLAN_* bits */
+  /* Many-direction SPSA (no reference counterpart: the reference perturbs one direction
+   * per step). directions K in [1, DSMZ_MAX_DIRECTIONS] (0 = 1). Direction k writes its
+   * +/- copies at the module's pos/neg pointers + k * dir_stride_factor elements and its z
+   * at z + k * dir_stride_z (fp32 elements), and draws from the generator at
+   * offset + k * rng_direction_stride (0 = this plan's own one-direction advance, i.e. the
+   * whole model is in this plan), so direction k takes exactly the draws that K successive
+   * one-direction steps would take. */
+  int32_t directions;
+  int32_t pad0;
+  int64_t dir_stride_factor;
+  int64_t dir_stride_z;
+  uint64_t rng_direction_stride;
 } dsmz_plan_desc;
+
+#define DSMZ_MAX_DIRECTIONS 32
 
 /* Power iteration on CUDA cores (fp32 FFMA) even where the tcgen05 path applies. The
  * tcgen05 path needs bf16 activations, D a multiple of 8 and R a multiple of 16. */
@@ -206,13 +220,26 @@ int dsmz_step_power_iteration(const dsmz_plan* plan, int32_t num_iters, float no
  * doubles at dsmz_step_kalman_sums(). Sum those across ranks before phase 3. */
 int dsmz_step_perturb(const dsmz_plan* plan, uint64_t seed, uint64_t offset, float eps,
                       float beta, float q, float norm_floor, dsmz_stream_t stream);
-double* dsmz_step_kalman_sums(const dsmz_plan* plan);
+double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per direction */
+int32_t dsmz_plan_directions(const dsmz_plan* plan);
 
 /* Phase 3 (ds_mezo/controller.py:272-286): Kalman observation update of mu/var with the
  * summed scalars, ZO-Muon Newton-Schulz of every updated mu, param -= eta * X.
  * schedule NULL = cubic. */
 int dsmz_step_update(const dsmz_plan* plan, float dd, float beta, float q, float eta,
                      float norm_floor, const dsmz_ns_schedule* schedule, dsmz_stream_t stream);
+
+/* Phase 3 for K directions (no reference counterpart; K = 1 is dsmz_step_update): one
+ * Kalman observation update with the K projected-gradient scalars dd[0..K-1] (host array)
+ * and the summed (y_hat_k, s_k), treating the K x K innovation covariance
+ * sum(var1 * z_k * z_l) as diagonal (its off-diagonal terms are O(1/sqrt(n)) for
+ * independent directions over n adapter elements):
+ *   mu2  = mu1 + var1 * sum_k z_k (dd_k - y_hat_k) / (s_k + norm_floor)
+ *   var2 = var1 * (1 - var1 * sum_k z_k^2 / (s_k + norm_floor))
+ * then the same Newton-Schulz update of param as dsmz_step_update. */
+int dsmz_step_update_directions(const dsmz_plan* plan, const float* dd, int32_t n, float beta, float q,
+                                float eta, float norm_floor, const dsmz_ns_schedule* schedule,
+                                dsmz_stream_t stream);
 
 /* ---------------------------------------------------------------------------------
  * Timing probes: while set, every launch of kernel `kernel` by the grouped step records
@@ -234,7 +261,8 @@ enum dsmz_kernel_id {
   DSMZ_KID_APPLY = 11,     /* Kalman update + param -= eta X */
   DSMZ_KID_PI_SPLIT = 12,  /* [V_hi | V_lo]^T for the tensor-core products */
   DSMZ_KID_DRAW = 13,      /* Zc_A draws in torch's launch layout */
-  DSMZ_NUM_KIDS = 14
+  DSMZ_KID_KALMAN_DIRS = 14, /* K-direction Kalman observation update */
+  DSMZ_NUM_KIDS = 15
 };
 int dsmz_plan_set_probe(dsmz_plan* plan, int32_t kernel, void** start_events, void** stop_events,
                         int32_t capacity);

@@ -394,3 +394,90 @@ def update_phase(st: StepState, perts, dd: float, norm_floor: float = FLT_MIN):
     y_hat, s_sum = kalman_update(mats, zs, dd, beta, q, st.eta, norm_floor, st.schedule)
     st.eta = cosine_eta(st.step_count, st.total_steps, st.eta_max, st.eta_min)
     return y_hat, s_sum
+
+
+# --------------------------------------------------------------------------------------
+# Many-direction SPSA (no reference counterpart: the reference perturbs and observes one
+# direction per step). Direction k takes the draws that the k-th of K successive
+# one-direction steps would take; the K observations update the Kalman state jointly
+# with the diagonal of the innovation covariance.
+# --------------------------------------------------------------------------------------
+def perturb_phase_directions(st: StepState, activations: Sequence[torch.Tensor], draws_per_dir,
+                             num_iters: int = 3, norm_floor: float = FLT_MIN):
+    """Power iteration once, then the AGZO perturbation of every module for each direction
+    (``draws_per_dir[k]`` in ``draw_shapes`` order). Returns [[(z_A, z_B)] per direction]."""
+    st.bases = [fused_power_iter(H, V, num_iters, norm_floor, st.dtype) for H, V in zip(activations, st.bases)]
+    out = []
+    for draws in draws_per_dir:
+        perts = []
+        for i, m in enumerate(st.modules):
+            V = st.bases[m.basis]
+            perts.append(get_perturbation(m.A, m.B, V, m.var_B, draws[2 * i], draws[2 * i + 1],
+                                          st.eps, norm_floor, st.dtype))
+        out.append(perts)
+    return out
+
+
+def kalman_update_directions(mats: Sequence[Matrix], zs_per_dir, dds: Sequence[float], beta: float, q: float,
+                             eta: float, norm_floor: float = FLT_MIN, schedule=None):
+    """Joint observation of K directions: with mu1 = beta mu, var1 = beta^2 var + q,
+    y_k = sum z_k mu1, s_k = sum z_k^2 var1, innov_k = dd_k - y_k, inv_k = 1 / (s_k + floor):
+    mu2 = mu1 + var1 sum_k z_k inv_k innov_k, var2 = var1 (1 - var1 sum_k z_k^2 inv_k);
+    then the ZO-Muon update of every factor. Returns [(y_k, s_k)]."""
+    cdt = mats[0].mu.dtype if mats else torch.float32
+    K = len(dds)
+    for m in mats:
+        m.mu.mul_(beta)
+        m.var.mul_(beta * beta).add_(q)
+    sums = []
+    for k in range(K):
+        y = torch.zeros((), dtype=cdt)
+        s = torch.zeros((), dtype=cdt)
+        for m, z in zip(mats, zs_per_dir[k]):
+            y += (z * m.mu).sum()
+            s += (z * z * m.var).sum()
+        sums.append((y, s))
+    innov = [dds[k] - sums[k][0] for k in range(K)]
+    inv = [1.0 / (sums[k][1] + norm_floor) for k in range(K)]
+    for j, m in enumerate(mats):
+        am = torch.zeros_like(m.mu)
+        av = torch.zeros_like(m.mu)
+        for k in range(K):
+            z = zs_per_dir[k][j]
+            zi = z * inv[k]
+            am += zi * innov[k]
+            av += zi * z
+        m.mu.add_(m.var * am)
+        m.var.mul_(1.0 - m.var * av)
+        zo_muon_update(m.param, m.mu, m.scratch, eta, norm_floor, schedule)
+    return sums
+
+
+def update_phase_directions(st: StepState, perts_per_dir, dds: Sequence[float], norm_floor: float = FLT_MIN):
+    beta, q = kalman_beta_q(st.step_count, st.total_steps, st.eps)
+    mats, zs = [], [[] for _ in perts_per_dir]
+    for i, m in enumerate(st.modules):
+        mats.append(Matrix(m.A, m.mu_A, m.var_A, m.scratch_A))
+        mats.append(Matrix(m.B, m.mu_B, m.var_B, m.scratch_B))
+        for k, perts in enumerate(perts_per_dir):
+            zs[k].append(perts[i][0])
+            zs[k].append(perts[i][1])
+    sums = kalman_update_directions(mats, zs, dds, beta, q, st.eta, norm_floor, st.schedule)
+    st.eta = cosine_eta(st.step_count, st.total_steps, st.eta_max, st.eta_min)
+    return sums
+
+
+def rloo_direction_scalars(rewards: torch.Tensor, eps: float) -> List[float]:
+    """K directions' projected-gradient scalars: rewards (K, N), the first N/2 rollouts under
+    the + copy; advantage = r - (sum - r) / (N - 1) within a direction; L = -mean advantage
+    of a copy; dd = (L+ - L-) / (2 eps) (ds_mezo/controller.py:307 for the last step)."""
+    K, N = rewards.shape
+    out = []
+    for k in range(K):
+        r = [float(x) for x in rewards[k]]
+        tot = sum(r)
+        adv = [ri - (tot - ri) / (N - 1) for ri in r]
+        lp = -sum(adv[: N // 2]) / (N // 2)
+        lm = -sum(adv[N // 2:]) / (N // 2)
+        out.append((lp - lm) / (2.0 * eps))
+    return out

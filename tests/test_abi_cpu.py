@@ -136,3 +136,41 @@ def test_dropin_argument_errors_without_gpu(L):
     assert rc == 4
     assert L.dsmz_zo_muon_update_workspace_bytes(18944, 64) > 0
     assert L.dsmz_power_iter_workspace_bytes(4096, 3584, 64) >= 4096 * 64 * 4 + 3584 * 64 * 4
+
+
+def test_rloo_direction_scalars_match_oracle():
+    from dsmezo_b200 import rloo_direction_scalars
+    g = torch.Generator().manual_seed(4)
+    r = torch.bernoulli(torch.full((16, 8), 0.4), generator=g)
+    ours = rloo_direction_scalars(r, 1e-3)
+    want = ref.rloo_direction_scalars(r, 1e-3)
+    assert len(ours) == 16
+    for a, b in zip(ours, want):
+        assert math.isclose(a, b, rel_tol=1e-12, abs_tol=1e-9)
+    # equal rewards under both copies: no signal
+    assert rloo_direction_scalars(torch.ones(2, 8), 1e-3) == [0.0, 0.0]
+    with pytest.raises(ValueError):
+        rloo_direction_scalars(torch.ones(2, 7), 1e-3)
+
+
+@pytest.mark.parametrize("K", [2, 16])
+def test_plan_directions_host_only(L, K):
+    from dsmezo_b200 import draw_increments
+    mods, d = _fake_set(rank=16)
+    d.directions, d.dir_stride_factor, d.dir_stride_z = K, 1 << 20, 1 << 20
+    h = ctypes.c_void_p()
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
+    try:
+        assert L.dsmz_plan_directions(h) == K
+        assert L.dsmz_plan_rng_increment(h) == K * sum(draw_increments(mods, 16, 16, 148, 2048))
+        # B-side sums once, 4 launches per direction, 4 update launches
+        assert L.dsmz_plan_launch_count(h, 3) == (3 * 5 + 1) + 1 + 4 * K + 4
+        dd = (ctypes.c_float * K)(*([0.0] * K))
+        assert L.dsmz_step_update_directions(h, dd, K, 0.0, 0.0, 0.0, 0.0, None, None) == 1   # not bound
+    finally:
+        L.dsmz_plan_destroy(h)
+    d.dir_stride_z = 0
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 1
+    assert b"direction strides" in L.dsmz_last_error()
+    d.directions = 33
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 1
