@@ -363,6 +363,13 @@ def main():
         e2e = {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": host_H.numel() * host_H.element_size(),
                "d2h_bytes_per_step": host_out.numel() * 8, "steps": n_e2e}
 
+    # a bounded wait that gave up sets the plan's error word and the kernels after it stop
+    # early: such a run has no valid timing
+    derr = aset.device_error()
+    if derr:
+        print(json.dumps({"metric": METRIC, "error": f"device error word {derr}: a bounded wait timed out",
+                          "rank": rank}), flush=True)
+        sys.exit(3)
     if rank != 0:
         if world > 1:
             import torch.distributed as dist

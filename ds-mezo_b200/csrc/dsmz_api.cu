@@ -412,6 +412,34 @@ bool bind_tc(dsmz_plan* P) {
 }
 
 
+// Tile width of the adapter matrices' streaming kernels: the widest (a multiple of 8, at
+// most sk::stream_tv(r)) whose perturbation, Gram and apply layouts all fit with a ring
+// of at least kTeams stages for the team kernels (two for the Gram). One width for all of
+// them: their segments (Kalman and Gram partials) follow the same tile chunks.
+bool choose_adapter_layouts(dsmz_plan* P, int fes) {
+  const int r = P->r, rca = P->r < P->RC ? P->r : P->RC;
+  for (int tv = sk::stream_tv(r); tv >= 8; tv = (tv / 2) & ~7) {
+    P->Lp = sk::perturb_layout(r, r, P->RC, rca, fes, 0, kStreamSmem, tv);
+    P->Lg = sk::gram_layout(r, 1, kStreamSmem, tv);
+    P->La = sk::apply_layout(r, fes, kStreamSmem, tv);
+    const bool ok = P->Lp.S >= sk::kTeams && P->La.S >= sk::kTeams && P->Lg.S >= 2 &&
+                    P->Lp.total <= kStreamSmem + 2048 && P->La.total <= kStreamSmem + 2048 &&
+                    P->Lg.total <= kStreamSmem + 2048;
+    if (ok) return true;
+    if (tv == 8) break;
+  }
+  return false;
+}
+
+bool choose_qr_layout(dsmz_plan* P) {
+  for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {
+    P->Lq = sk::qr_layout(P->R, kStreamSmem, tv);
+    if (P->Lq.S >= sk::kTeams && P->Lq.total <= kStreamSmem + 2048) return true;
+    if (tv == 8) break;
+  }
+  return false;
+}
+
 // ---------------------------------------------------------------- launch sequences
 int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s) {
   if (P->bases.empty() || iters <= 0) return 0;
@@ -794,23 +822,20 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   P->rng_inc1 = off - d->rng_offset_before;
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
-  if (!P->mats.empty()) P->nsegs = chunk_matrices(P->mats, sk::stream_tv(P->r), P->sm_count, &P->ws, &P->grid_m);
-  if (!P->w2.empty()) chunk_matrices(P->w2, sk::stream_tv(P->R), P->sm_count, nullptr, &P->grid_w);
+  // streaming layouts, then the tile chunks they imply, then the per-segment buffers
+  const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
+  if (P->r > 0 && !choose_adapter_layouts(P, fes)) {
+    delete P;
+    return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");
+  }
+  if (P->R > 0 && !choose_qr_layout(P)) {
+    delete P;
+    return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: basis width too large for the streaming kernels");
+  }
+  if (!P->mats.empty()) P->nsegs = chunk_matrices(P->mats, P->Lg.TV, P->sm_count, &P->ws, &P->grid_m);
+  if (!P->w2.empty()) chunk_matrices(P->w2, P->Lq.TV, P->sm_count, nullptr, &P->grid_w);
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * static_cast<size_t>(P->ndir) * sizeof(double)) / sizeof(double));
-  const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
-  if (P->r > 0) {
-    P->Lp = sk::perturb_layout(P->r, P->r, P->RC, P->r < P->RC ? P->r : P->RC, fes, 0, kStreamSmem);
-    P->Lg = sk::gram_layout(P->r, 1, kStreamSmem);
-    P->La = sk::apply_layout(P->r, fes, kStreamSmem);
-  }
-  if (P->R > 0) P->Lq = sk::qr_layout(P->R, kStreamSmem);
-  for (const sk::Layout* L : {&P->Lp, &P->Lg, &P->La, &P->Lq}) {
-    if (L->r > 0 && (L->S < 2 || L->total > kStreamSmem + 2048)) {
-      delete P;
-      return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");
-    }
-  }
   P->pack();
   *out = P;
   return DSMZ_OK;
@@ -1034,7 +1059,8 @@ static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R, bool tc) {
   dsmz_plan P;
   P.ws.take(table_head_bytes());
   P.err_off = P.ws.take(256);
-  P.Lq = sk::qr_layout(static_cast<int>(R), kStreamSmem);
+  P.R = static_cast<int>(R);
+  choose_qr_layout(&P);
   BasisD bd{};
   bd.R = static_cast<int32_t>(R); bd.T = T; bd.D = D;
   bd.y_off = static_cast<int64_t>(P.ws.take(static_cast<size_t>(T) * R * sizeof(float)) / sizeof(float));
@@ -1097,7 +1123,7 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
     cudaError_t ez = cudaMemsetAsync(P.workspace + P.err_off, 0, sizeof(int), s);
     if (ez != cudaSuccess) return cuda_fail("power_iter: error word", ez);
   }
-  chunk_matrices(P.w2, sk::stream_tv(static_cast<int>(R)), P.sm_count, nullptr, &P.grid_w);
+  chunk_matrices(P.w2, P.Lq.TV, P.sm_count, nullptr, &P.grid_w);
   int rc = upload_small(&P, static_cast<char*>(workspace), s);
   if (rc) return rc;
   return run_power_iteration(&P, num_iters, norm_floor, s);

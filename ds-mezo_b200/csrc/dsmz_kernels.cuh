@@ -4,6 +4,7 @@
 #pragma once
 
 #include "dsmz_internal.cuh"
+#include "dsmz_ptx.cuh"
 
 namespace dsmz {
 
@@ -254,11 +255,6 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
 // MMA (m8n8k4), four blocks per warp at a time, and mirrored. Pitch ld (= rp + 4: a warp's
 // fragment loads fall in two wavefronts); rows and columns r..rp-1 are zero and stay zero.
 // Every position is written by exactly one thread. Ends with a barrier.
-__device__ __forceinline__ void dmma8x8x4(double& d0, double& d1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-               : "+d"(d0), "+d"(d1)
-               : "d"(a), "d"(b));
-}
 __device__ void cta_symm_mm(double* __restrict__ C, const double* __restrict__ A, const double* __restrict__ B,
                             int rp, int ld) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -31,6 +31,9 @@ constexpr int kCW = 8;                   // consumer warps
 constexpr int kCT = 32 * kCW;            // consumer threads
 constexpr int kST = kCT + 32;            // + producer warp 0
 constexpr int kTeams = 4;                // perturb / apply / QR apply
+// A team waits for tile i only after its tile i - kTeams, so with a ring of S >= kTeams
+// stages every stage it waits on is at most one mbarrier phase ahead (a wait two phases
+// ahead would alias on the phase parity). Plans keep S >= kTeams for the team kernels.
 constexpr int kTT = kCT / kTeams;        // threads per team (two warps)
 constexpr int kBarAll = 1;               // named barrier: all consumer threads
 constexpr int kBarTeam0 = 2;             // named barriers 2..5: one per team
@@ -359,13 +362,12 @@ struct Layout {
 
 // Perturb: p, mu, var (unpadded, MODE 0 only) and the K operand rows (Zc_A rows of width
 // RCA, or basis rows of width RC), padded to pitch KW + 4 floats.
-__host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int fes, int mode, int budget) {
+__host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int fes, int mode, int budget, int TV) {
   Layout L{};
   L.r = r;
-  L.TV = stream_tv(r);
+  L.TV = TV;
   const int KW = RC > RCA ? RC : RCA;
   const int kp = (KW + 3) / 4 * 4 + 4;
-  const int TV = L.TV;
   int o = 0;
   L.off[0] = o; L.pitch[0] = (mode == 0) ? r * fes : 0;               o += al128(mode == 0 ? TV * r * fes : 0);
   L.off[1] = o; L.pitch[1] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
@@ -388,11 +390,10 @@ __host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, 
 }
 
 // Apply: p (unpadded) and mu (side 0 rows padded to r + 4 floats).
-__host__ __device__ inline Layout apply_layout(int r, int fes, int budget) {
+__host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int TV) {
   Layout L{};
   L.r = r;
-  L.TV = stream_tv(r);
-  const int TV = L.TV;
+  L.TV = TV;
   const int mp = (r + 3) / 4 * 4 + 4;
   int o = 0;
   L.off[0] = o; L.pitch[0] = r * fes;                                   o += al128(TV * r * fes);
@@ -413,11 +414,10 @@ __host__ __device__ inline Layout apply_layout(int r, int fes, int budget) {
 }
 
 // QR apply: W rows padded to R + 4 floats; fp64 R^-1 (R x pld).
-__host__ __device__ inline Layout qr_layout(int R, int budget) {
+__host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   Layout L{};
   L.r = R;
-  L.TV = stream_tv(R);
-  const int TV = L.TV;
+  L.TV = TV;
   const int mp = (R + 3) / 4 * 4 + 4;
   L.off[0] = 0; L.pitch[0] = mp * 4;
   L.stage_bytes = al128(TV * mp * 4);
@@ -435,11 +435,10 @@ __host__ __device__ inline Layout qr_layout(int R, int budget) {
   return L;
 }
 
-__host__ __device__ inline Layout gram_layout(int r, int kalman, int budget) {
+__host__ __device__ inline Layout gram_layout(int r, int kalman, int budget, int TV) {
   Layout L{};
   L.r = r;
-  L.TV = stream_tv(r);
-  const int TV = L.TV;
+  L.TV = TV;
   int o = 0;
   L.off[0] = o; L.pitch[0] = r * 4; o += al128(TV * r * 4);
   L.off[1] = o; L.pitch[1] = kalman ? r * 4 : 0; o += al128(kalman ? TV * r * 4 : 0);

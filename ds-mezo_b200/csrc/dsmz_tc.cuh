@@ -259,36 +259,47 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
           const int rw = e / R, c = e - rw * R;
           B->W[(d0 + rw) * R + c] = static_cast<float>(wt[rw * tld + c]);
         }
-        // fp64 Gram of the tile. Thread block (ab, cb) owns rows ab + (R/4) i and columns
-        // cb + (R/8) j, so the 4 and 8 distinct addresses a warp reads per load are
-        // consecutive doubles (no bank conflicts).
+        // fp64 Gram of the tile on the fp64 MMA (m8n8k4): upper-triangle 8 x 8 blocks of
+        // W^T W, up to nine per warp at a time; k-step s takes tile rows
+        // 32(s/8) + s%8 + 8kq (kq = lane & 3), which puts a warp's fragment loads in two
+        // wavefronts with the odd row pitch that keeps the staging stores conflict-free.
         const int RR = R * R;
-        const int ra = R / 4, rb = R / 8;
         double* gout = B->g1 + static_cast<int64_t>(tile) * RR;
-        for (int blk = t; blk < ra * rb; blk += kBM) {
-          const int ab = blk / rb, cb = blk - ab * rb;
-          double acc[4][8];
+        const int ew = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
+        const int g = lane >> 2, kq = lane & 3;
+        const int nb = R >> 3, nblk = nb * (nb + 1) / 2;
+        for (int q0 = ew; q0 < nblk; q0 += 4 * 9) {
+          int bi[9], bj[9];
+          double acc[9][2];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int u = 0; u < 9; ++u) {
+            int q = q0 + 4 * u;
+            bi[u] = -1; bj[u] = 0;
+            acc[u][0] = 0.0; acc[u][1] = 0.0;
+            if (q < nblk) {
+              int row = 0;
+              while (q >= nb - row) { q -= nb - row; ++row; }
+              bi[u] = row; bj[u] = row + q;
+            }
+          }
+          for (int s = 0; s < kBM / 4; ++s) {
+            const double* wr = wt + (32 * (s >> 3) + (s & 7) + 8 * kq) * tld + g;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-#pragma unroll 2
-          for (int rr = 0; rr < kBM; ++rr) {
-            const double* wr = wt + rr * tld;
-            double xa[4], xb[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) xa[i] = wr[ab + ra * i];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) xb[j] = wr[cb + rb * j];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc[i][j] = fma(xa[i], xb[j], acc[i][j]);
+            for (int u = 0; u < 9; ++u)
+              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], wr[8 * bi[u]], wr[8 * bj[u]]);
           }
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int u = 0; u < 9; ++u) {
+            if (bi[u] < 0) continue;
+            const int row = 8 * bi[u] + g;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) gout[(ab + ra * i) * R + cb + rb * j] = acc[i][j];
+            for (int h = 0; h < 2; ++h) {
+              const int col = 8 * bj[u] + 2 * kq + h;
+              if (bi[u] == bj[u] && col < row) continue;     // mirror of the upper half
+              gout[row * R + col] = acc[u][h];
+              if (col != row) gout[col * R + row] = acc[u][h];
+            }
+          }
         }
       }
     }

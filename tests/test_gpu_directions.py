@@ -76,6 +76,7 @@ def test_directions_step(K, fdt):
             ref.update_phase_directions(s, perts[dt], dds)
         ctl.update(dds)
         torch.cuda.synchronize()
+        assert aset.device_error() == 0
         o32, o64 = st[torch.float32], st[torch.float64]
         assert math.isclose(ctl.eta, o64.eta, rel_tol=1e-12)
         for i in range(len(mods)):

@@ -93,6 +93,7 @@ def _run_case(layers, hidden, inter, kv, rank, tokens, seed, factor_dtype, act_d
             ref.update_phase(s, perts[dt], dd)
         ctl.update(dd)
         torch.cuda.synchronize()
+        assert aset.device_error() == 0            # no bounded wait gave up
         assert math.isclose(ctl.eta, o64.eta, rel_tol=1e-12)
         for i in range(len(mods)):
             m32, m64 = o32.modules[i], o64.modules[i]
@@ -153,3 +154,9 @@ def test_step_on_reused_memory():
     del junk
     _run_case(2, 384, 1280, 64, 16, 256, seed=7, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16,
               schedule="quintic", tc=True)
+
+
+def test_step_rank128_fp32():
+    """fp32 factors at rank 128: the widest tiles leave too few ring stages for the four
+    consumer teams, so the plan narrows its tiles; the step must still be exact."""
+    _run_case(1, 256, 768, 128, 128, 256, seed=9, factor_dtype=torch.float32, act_dtype=torch.bfloat16, steps=1)
