@@ -106,6 +106,7 @@ void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bo
   seg_counter += m.nseg;
   const size_t rr = static_cast<size_t>(m.r) * m.r;
   m.gram_off = alloc_gram ? static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double)) : 0;
+  m.tmap = -1;
   m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
   m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * static_cast<size_t>(pad8(static_cast<int>(m.r))) *
                                                       ns_ld(static_cast<int>(m.r)) * sizeof(double)) / sizeof(double)) : 0;
@@ -186,6 +187,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// 2-D tensor map of fp32 or bf16 rows (inner dimension contiguous), no swizzle, zero fill
+// outside: the tile boxes of the streaming kernels' side-1 arrays.
+bool encode_rows_2d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, dtype == DSMZ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+            const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D bf16 tensor map (inner dimension contiguous), 128-byte swizzle, zero fill outside.
 bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                     uint32_t box_inner, uint32_t box_outer) {
@@ -203,12 +220,12 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 int tc_stages(int R);
 
 // Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R),
-// and a stage ring large enough to hold the fp64 W tile (128 x (R + 1) doubles) that the
-// W kernel's epilogue stages over it.
+// and a stage ring large enough to hold the W tile (128 x (R + 1) floats) that the W
+// kernel's epilogue stages over it.
 bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
   return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
          (reinterpret_cast<uintptr_t>(H) & 15) == 0 &&
-         static_cast<int64_t>(tc::kBM) * (R + 1) * 8 <= static_cast<int64_t>(tc_stages(static_cast<int>(R))) *
+         static_cast<int64_t>(tc::kBM) * (R + 1) * 4 <= static_cast<int64_t>(tc_stages(static_cast<int>(R))) *
                                                           tc::stage_bytes(static_cast<int>(R));
 }
 
@@ -244,17 +261,20 @@ struct dsmz_plan {
   char* workspace = nullptr;
   int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
   int sm_count = 0;
-  int grid_m = 0, grid_w = 0;        // streaming-kernel grids (chunks) of mats and w2
+  int grid_m = 0, grid_w = 0, grid_w1 = 0;   // streaming-kernel grids (chunks) of mats, w2, w1
   int ndir = 1;                      // SPSA directions per step
   int64_t dstride_f = 0, dstride_z = 0;
   uint64_t rng_inc1 = 0, rng_dir_stride = 0;   // one direction's generator advance (this plan / all ranks)
   sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
+  sk::Layout Lw{};                     // Gram of the power-iteration W
   int factor_dtype = DSMZ_F32;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
   uint64_t rng_increment = 0;
   // tensor-core power iteration
   bool tc = false;
+  std::vector<CUtensorMap> smaps;     // side-1 tile boxes of the adapter arrays (4 per matrix)
+  size_t off_smaps = 0;
   std::vector<tc::TCBasis> tcb;
   std::vector<TCSlots> tcs;
   size_t off_tcb = 0, err_off = 0;
@@ -295,6 +315,7 @@ struct dsmz_plan {
     t.ws = workspace;
     t.seg_kal_off = seg_kal_off;
     t.kal_sum_off = kal_sum_off;
+    t.smaps = smaps.empty() ? nullptr : reinterpret_cast<const CUtensorMap*>(dev_tables + off_smaps);
     t.ndir = ndir;
     t.dir = 0;
     t.dstride_f = dstride_f;
@@ -311,6 +332,7 @@ struct dsmz_plan {
     off_mods = T.take(mods.size() * sizeof(ModD), 64);
     off_bases = T.take(bases.size() * sizeof(BasisD), 64);
     off_tcb = T.take(tcb.size() * sizeof(tc::TCBasis), 64);
+    off_smaps = T.take(smaps.size() * sizeof(CUtensorMap), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -321,6 +343,7 @@ struct dsmz_plan {
     if (!mods.empty()) std::memcpy(blob.data() + off_mods, mods.data(), mods.size() * sizeof(ModD));
     if (!bases.empty()) std::memcpy(blob.data() + off_bases, bases.data(), bases.size() * sizeof(BasisD));
     if (!tcb.empty()) std::memcpy(blob.data() + off_tcb, tcb.data(), tcb.size() * sizeof(tc::TCBasis));
+    if (!smaps.empty()) std::memcpy(blob.data() + off_smaps, smaps.data(), smaps.size() * sizeof(CUtensorMap));
   }
 };
 
@@ -345,19 +368,17 @@ void patch_ws_pointers(dsmz_plan* P) {
   }
 }
 
-// CholeskyQR tables of every basis W (D x R): the Gram segments (128 rows when the
-// tensor-core W kernel writes their fp64 partials) and the apply segments of V = W R^{-1}.
-void add_w_tables(dsmz_plan* P, bool tc_segments) {
+// CholeskyQR tables of every basis W (D x R): the Gram pass (its segments and partials are
+// placed by chunk_matrices) and the apply segments of V = W R^{-1}.
+void add_w_tables(dsmz_plan* P) {
   for (size_t i = 0; i < P->bases.size(); ++i) {
     const BasisD& b = P->bases[i];
     const size_t rr = static_cast<size_t>(b.R) * b.R;
     MatD a{};
     a.nvec = b.D; a.r = b.R; a.ld = b.R; a.cs = 1; a.side = 0; a.owner = static_cast<int32_t>(i);
-    a.segv = tc_segments ? tc::kBM : seg_vectors(b.R);
+    a.tmap = -1;
+    a.segv = seg_vectors(b.R);
     a.nseg = static_cast<int32_t>((b.D + a.segv - 1) / a.segv);
-    a.seg0 = P->nwsegsA;
-    P->nwsegsA += a.nseg;
-    a.gram_off = static_cast<int64_t>(P->ws.take(a.nseg * rr * sizeof(double)) / sizeof(double));
     a.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
     a.dw_off = static_cast<int64_t>(P->ws.take(3 * rr * sizeof(double)) / sizeof(double));
     MatD m = a;                 // apply segments: V = W R^{-1} (fp64 R^{-1} in a's workspace)
@@ -389,6 +410,26 @@ void plan_tc_layout(dsmz_plan* P) {
   }
 }
 
+// The four tile-box maps (param, mu, var, z) of every side-1 adapter matrix; a matrix whose
+// arrays the driver refuses (alignment) keeps the copy-engine path (tmap = -1).
+void bind_side1_maps(dsmz_plan* P) {
+  const int TV = P->Lg.TV;
+  for (MatD& m : P->mats) {
+    if (m.tmap < 0) continue;
+    bool ok = TV <= 256 && m.r <= 256 && m.cs == 1;
+    const void* arr[4] = {m.param, m.mu, m.var, m.z};
+    const int dt[4] = {P->factor_dtype, DSMZ_F32, DSMZ_F32, DSMZ_F32};
+    for (int j = 0; j < 4 && ok; ++j) {
+      const int es = (dt[j] == DSMZ_BF16) ? 2 : 4;
+      ok = ((reinterpret_cast<uintptr_t>(arr[j]) & 15) == 0) && ((m.ld * es) % 16 == 0) &&
+           encode_rows_2d(&P->smaps[m.tmap + j], dt[j], arr[j], static_cast<uint64_t>(m.nvec),
+                          static_cast<uint64_t>(m.r), static_cast<uint64_t>(m.ld) * es, static_cast<uint32_t>(TV),
+                          static_cast<uint32_t>(m.r));
+    }
+    if (!ok) m.tmap = -1;
+  }
+}
+
 // Fills pointers and tensor maps once the workspace is known; false if the driver refuses
 // a tensor map (the plan then keeps the CUDA-core path).
 bool bind_tc(dsmz_plan* P) {
@@ -399,7 +440,6 @@ bool bind_tc(dsmz_plan* P) {
     c.V2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.v2t);
     c.Y2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.y2t);
     c.W = reinterpret_cast<float*>(P->workspace) + b.w_off;
-    c.g1 = reinterpret_cast<double*>(P->workspace) + P->w1[i].gram_off;
     c.Vsrc = b.Vin; c.v_s0 = b.v_s0; c.v_s1 = b.v_s1; c.Vout = b.Vout;
     const uint32_t n2 = static_cast<uint32_t>(2 * b.R);
     if (!encode_bf16_2d(&c.mapHy, b.H, b.D, b.T, b.h_s0 * 2, 64, 128) ||
@@ -432,12 +472,39 @@ bool choose_adapter_layouts(dsmz_plan* P, int fes) {
 }
 
 bool choose_qr_layout(dsmz_plan* P) {
+  bool ok = false;
   for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {
     P->Lq = sk::qr_layout(P->R, kStreamSmem, tv);
-    if (P->Lq.S >= sk::kTeams && P->Lq.total <= kStreamSmem + 2048) return true;
+    if (P->Lq.S >= sk::kTeams && P->Lq.total <= kStreamSmem + 2048) { ok = true; break; }
+    if (tv == 8) break;
+  }
+  if (!ok) return false;
+  for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {    // Gram of W (plain)
+    P->Lw = sk::gram_layout(P->R, 0, kStreamSmem, tv);
+    if (P->Lw.S >= 2 && P->Lw.total <= kStreamSmem + 2048) return true;
     if (tv == 8) break;
   }
   return false;
+}
+
+// Streaming schedule of the power-iteration tables once the SM count is known: the W Gram
+// (with its per-segment partials, placed here when alloc, else reserved beforehand by
+// reserve_w_gram) and the QR apply.
+void chunk_w_tables(dsmz_plan* P, bool alloc) {
+  if (P->w1.empty()) return;
+  P->nwsegsA = chunk_matrices(P->w1, P->Lw.TV, P->sm_count, alloc ? &P->ws : nullptr, &P->grid_w1);
+  chunk_matrices(P->w2, P->Lq.TV, P->sm_count, nullptr, &P->grid_w);
+}
+
+// One-basis plans are laid out before the device is known: room for the Gram partials of
+// up to kMaxChunks segments (one per CTA of a grid no wider than that).
+constexpr int kMaxChunks = 1024;
+void reserve_w_gram(dsmz_plan* P) {
+  for (MatD& a : P->w1) {
+    const int64_t tiles = (a.nvec + P->Lw.TV - 1) / P->Lw.TV;
+    const int64_t n = tiles < kMaxChunks ? tiles : kMaxChunks;
+    a.gram_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(n) * a.r * a.r * sizeof(double)) / sizeof(double));
+  }
 }
 
 // ---------------------------------------------------------------- launch sequences
@@ -445,14 +512,10 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   if (P->bases.empty() || iters <= 0) return 0;
   const Tables tb = P->tables();
   const int R = P->R;
-  const size_t gs = gram_smem(R), qs = qr_apply_smem(R);
   int rc;
-  if (gram_rb(R) == 4) {
-    if ((rc = set_smem(k_gram<0, 4, double>, gs))) return rc;
-  } else {
-    if ((rc = set_smem(k_gram<0, 8, double>, gs))) return rc;
-  }
-  (void)qs;
+  const bool small = sk::gram_maxb(R) <= 5;
+  if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lw.total))) return rc;
+  if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply, P->Lq.total))) return rc;
   if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
   const KalmanIn kin{};
@@ -488,15 +551,13 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_W, s);
     DSMZ_LAUNCHED("power iteration W = H^T Y");
     }
-    // CholeskyQR of W from its exact fp64 Gram (written by the tensor-core W kernel, or
-    // by k_gram here); V = W R^{-1} accumulated in fp64, with the bf16 pair for the next Y.
-    if (!P->tc) {
-      P->probe_begin(DSMZ_KID_PI_GRAM, s);
-      if (gram_rb(R) == 4) k_gram<0, 4, double><<<P->nwsegsA, kThreads, gs, s>>>(tb, tb.wA, nb, kin);
-      else k_gram<0, 8, double><<<P->nwsegsA, kThreads, gs, s>>>(tb, tb.wA, nb, kin);
-      P->probe_end(DSMZ_KID_PI_GRAM, s);
-      DSMZ_LAUNCHED("power iteration Gram of W");
-    }
+    // CholeskyQR of W from its exact fp64 Gram (streamed, fp64 MMA); V = W R^{-1}
+    // accumulated in fp64, with the bf16 pair for the next tensor-core Y.
+    P->probe_begin(DSMZ_KID_PI_GRAM, s);
+    if (small) sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
+    else sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
+    P->probe_end(DSMZ_KID_PI_GRAM, s);
+    DSMZ_LAUNCHED("power iteration Gram of W");
     const int bpm = (R * R + kThreads - 1) / kThreads;
     P->probe_begin(DSMZ_KID_PI_CHOL, s);
     k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wA, nb, bpm);
@@ -532,8 +593,8 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   DSMZ_LAUNCHED("K-direction Kalman update");
   const KalmanIn none{};
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (small) sk::k_sgram<0, 5><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
-  else sk::k_sgram<0, 17><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
+  if (small) sk::k_sgram<0, 5><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
+  else sk::k_sgram<0, 17><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Gram of the updated momentum");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
@@ -613,8 +674,8 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (small) sk::k_sgram<1, 5><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
-  else sk::k_sgram<1, 17><<<P->grid_m, sk::kST, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  if (small) sk::k_sgram<1, 5><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  else sk::k_sgram<1, 17><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
@@ -756,7 +817,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
       plan_tc_layout(P);
     }
   }
-  add_w_tables(P, P->tc);
+  add_w_tables(P);
   // modules
   uint64_t off = d->rng_offset_before;   // draws are placed relative to the step's base offset
   for (int i = 0; i < d->num_modules; ++i) {
@@ -833,7 +894,12 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: basis width too large for the streaming kernels");
   }
   if (!P->mats.empty()) P->nsegs = chunk_matrices(P->mats, P->Lg.TV, P->sm_count, &P->ws, &P->grid_m);
-  if (!P->w2.empty()) chunk_matrices(P->w2, P->Lq.TV, P->sm_count, nullptr, &P->grid_w);
+  chunk_w_tables(P, true);
+  for (MatD& m : P->mats) {           // tile-box tensor maps, encoded at bind
+    if (m.side != 1) continue;
+    m.tmap = static_cast<int32_t>(P->smaps.size());
+    P->smaps.resize(P->smaps.size() + 4);
+  }
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * static_cast<size_t>(P->ndir) * sizeof(double)) / sizeof(double));
   P->pack();
@@ -851,7 +917,7 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   int32_t n = 0;
   // per iteration: Y, W, [Gram of W on the CUDA-core path], partial sums, Cholesky, V;
   // plus the first bf16 split of the caller's basis on the tensor-core path
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->tc ? 5 : 6) + (p->tc ? 1 : 0);
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * 6 + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }
@@ -869,6 +935,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   P->workspace = static_cast<char*>(workspace);
   patch_ws_pointers(P);
   if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
+  bind_side1_maps(P);
   {
     cudaError_t ez = cudaMemsetAsync(P->workspace + P->err_off, 0, sizeof(int), static_cast<cudaStream_t>(stream));
     if (ez != cudaSuccess) return cuda_fail("dsmz_plan_bind: error word", ez);
@@ -1070,7 +1137,8 @@ static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R, bool tc) {
   P.R = static_cast<int>(R);
   if (tc) plan_tc_layout(&P);
   P.tc = tc;
-  add_w_tables(&P, tc);
+  add_w_tables(&P);
+  reserve_w_gram(&P);
   P.pack();
   return P;
 }
@@ -1123,7 +1191,8 @@ int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_
     cudaError_t ez = cudaMemsetAsync(P.workspace + P.err_off, 0, sizeof(int), s);
     if (ez != cudaSuccess) return cuda_fail("power_iter: error word", ez);
   }
-  chunk_matrices(P.w2, P.Lq.TV, P.sm_count, nullptr, &P.grid_w);
+  if (P.sm_count > kMaxChunks) return fail(DSMZ_ERR_UNSUPPORTED, "power_iter: too many SMs");
+  chunk_w_tables(&P, false);
   int rc = upload_small(&P, static_cast<char*>(workspace), s);
   if (rc) return rc;
   return run_power_iteration(&P, num_iters, norm_floor, s);

@@ -1,6 +1,7 @@
 // Internal device tables and helpers of libdsmezo (not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <curand_kernel.h>
@@ -30,7 +31,9 @@ struct MatD {
   // streaming kernels: the global tile space (TV-vector tiles of every matrix in order) is
   // cut into one contiguous chunk per CTA; a segment is a chunk's run within one matrix
   int32_t tile0, ntile;       // first global tile, tiles of this matrix
-  int32_t chunk0, pad1;       // chunk (CTA) holding tile0; segment seg0 + c - chunk0 of chunk c
+  int32_t chunk0;             // chunk (CTA) holding tile0; segment seg0 + c - chunk0 of chunk c
+  int32_t tmap;               // side 1: first of four 2-D tensor maps (param, mu, var, z) in
+                              // Tables::smaps, or -1
 };
 
 struct ModD {
@@ -73,6 +76,7 @@ struct Tables {
   char* ws;                                            // workspace base
   int64_t seg_kal_off;        // doubles: nsegs * 2 per-segment Kalman partials
   int64_t kal_sum_off;        // doubles: 2 summed Kalman scalars per direction
+  const CUtensorMap* smaps;   // 2-D tensor maps of the side-1 matrices' arrays (tile boxes)
   int32_t ndir, dir;          // directions; the one a perturbation launch writes
   int64_t dstride_f;          // factor elements between directions' pos/neg copies
   int64_t dstride_z;          // fp32 elements between directions' z

@@ -2,6 +2,7 @@
 // shared-memory addresses, mbarriers with bounded waits, and 1-D bulk copies.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace dsmz {
@@ -106,6 +107,18 @@ __device__ __forceinline__ void dmma8x8x4(double& d0, double& d1, double a, doub
   asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
                : "+d"(d0), "+d"(d1)
                : "d"(a), "d"(b));
+}
+__device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
+}
+// 2-D TMA load (no multicast) into this CTA's shared memory, completing on `bar`; x is the
+// innermost coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 // Barrier over the `n` threads of the consumer warps (id 1; warp-multiple n).
 __device__ __forceinline__ void named_sync(int id, int n) {

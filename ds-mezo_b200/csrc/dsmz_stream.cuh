@@ -53,12 +53,15 @@ struct Src {
   const char* base;
   int64_t ld, cs;
   int32_t es, side, r, pad;
+  const CUtensorMap* map;     // side 1 with a tile-box tensor map: one TMA copy per tile
 };
 
-__device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es) {
+// Array `which` (0 param, 1 mu, 2 var, 3 z) of matrix M, with its tensor map when M has them.
+__device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es, const Tables& tb, int which) {
   Src a;
   a.base = reinterpret_cast<const char*>(base);
   a.ld = M.ld; a.cs = M.cs; a.es = es; a.side = M.side; a.r = static_cast<int>(M.r); a.pad = 0;
+  a.map = (M.side == 1 && M.tmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.tmap + which : nullptr;
   return a;
 }
 
@@ -66,9 +69,12 @@ __device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es)
 // contiguous run of global memory (side-0 rows of exactly r elements, unpadded); 16-byte
 // cp.async chunks spread over the producer lanes when every row is 16-byte aligned (strided
 // or padded rows: many short rows would starve the bulk engine); element copies otherwise.
-enum { kCopyBulk = 0, kCopy16 = 1, kCopyPlain = 2 };
+enum { kCopyBulk = 0, kCopy16 = 1, kCopyPlain = 2, kCopyTensor = 3 };
 
 __device__ __forceinline__ int copy_mode(const Src& a, int64_t s0, int nv, int pitch, const void* dst) {
+  // side 1 with a tensor map: one 2-D TMA box (TV x r, dense rows of TV, zero fill past
+  // the matrix end); x = s0 is a multiple of the tile width (16-byte aligned)
+  if (a.map != nullptr && ((reinterpret_cast<uintptr_t>(dst) & 127) == 0)) return kCopyTensor;
   if (a.cs != 1 || (reinterpret_cast<uintptr_t>(a.base) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15) ||
       (pitch & 15))
     return kCopyPlain;
@@ -137,6 +143,7 @@ __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA]
     if (a[i].base == nullptr) continue;
     mode[i] = copy_mode(a[i], s0, nv, pitch[i], stage + off[i]);
     if (mode[i] == kCopyBulk) tx += static_cast<uint32_t>(nv) * a[i].r * a[i].es;
+    else if (mode[i] == kCopyTensor) tx += static_cast<uint32_t>(pitch[i]) * a[i].r;   // the whole box
     else if (mode[i] == kCopyPlain) plain_copy(a[i], s0, nv, stage + off[i], pitch[i], lane);
   }
   __syncwarp();
@@ -150,6 +157,11 @@ __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA]
                  full);
     } else if (mode[i] == kCopy16) {
       copy16_issue(a[i], s0, nv, stage + off[i], pitch[i], lane);
+    } else if (mode[i] == kCopyTensor) {
+      if (lane == 0) {
+        tmap_acquire(a[i].map);
+        tma_load_2d(stage + off[i], a[i].map, static_cast<int>(s0), 0, full);
+      }
     }
   }
   cp16_arrive(full);
@@ -448,22 +460,19 @@ __host__ __device__ inline Layout gram_layout(int r, int kalman, int budget, int
   L.xp = L.rp + 8;                 // side 0 rows of the fp64 tile
   L.zp = TV + 4;                   // side 1 rows
   const int xa = TV * L.xp, xb = L.rp * L.zp;
-  const int xbytes = al128((xa > xb ? xa : xb) * 8);
-  const int fixed = xbytes + 1024 + 1024;
+  const int xbytes = al128((xa > xb ? xa : xb) * 8);   // one buffer; two are kept
+  const int fixed = 2 * xbytes + 1024 + 1024;
   int S = (budget - fixed) / L.stage_bytes;
   S = S > 8 ? 8 : S;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_x = L.fixed0;
-  L.o_red = L.o_x + xbytes;        // block table (<= 136 ints)
+  L.o_red = L.o_x + 2 * xbytes;    // block table (<= 136 ints)
   L.o_bar = L.o_red + 1024;
-  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  L.total = L.o_bar + 2 * 8 * S + 4 * 8 + 128 + 128;
   return L;
 }
 
-// 128-byte aligned base of the dynamic shared memory. Pointer plus offset (not an integer
-// round trip) keeps the shared state space visible to the compiler, so accesses through it
-// compile to shared loads and stores rather than generic ones.
 __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
   return raw + ((128u - (smem_u32(raw) & 127u)) & 127u);
 }
@@ -566,12 +575,12 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
       const ModD& D = tb.mods[M.owner];
       const int r = static_cast<int>(M.r);
       Src a[4];
-      a[0] = make_src(MODE == 0 ? M.param : nullptr, M, fes);
-      a[1] = make_src(MODE == 0 ? M.mu : nullptr, M, 4);
-      a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4);
+      a[0] = make_src(MODE == 0 ? M.param : nullptr, M, fes, tb, 0);
+      a[1] = make_src(MODE == 0 ? M.mu : nullptr, M, 4, tb, 1);
+      a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4, tb, 2);
       // K operand: rows s0.. of Zc_A (d_out x RCA) or of the basis (d_in x RC)
       Src k{};
-      k.es = 4; k.side = 0; k.cs = 1;
+      k.es = 4; k.side = 0; k.cs = 1; k.map = nullptr;
       if (M.side == 0) {
         k.base = reinterpret_cast<const char*>(MODE == 0 ? reinterpret_cast<const float*>(tb.ws) + D.zca_off
                                                          : D.zcA_ext);
@@ -721,8 +730,8 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
       const MatD& M = t.mats[t.mi];
       Src a[2];
-      a[0] = make_src(M.param, M, fes);
-      a[1] = make_src(M.mu, M, 4);
+      a[0] = make_src(M.param, M, fes, tb, 0);
+      a[1] = make_src(M.mu, M, 4, tb, 1);
       const int off[2] = {L.off[0], L.off[1]};
       const int pitch[2] = {side_pitch(M.side, static_cast<int>(M.r), L.TV, fes),
                             M.side == 0 ? L.pitch[1] : L.TV * 4};
@@ -817,7 +826,7 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
       const MatD& M = t.mats[t.mi];
       Src a[1];
-      a[0] = make_src(M.mu, M, 4);
+      a[0] = make_src(M.mu, M, 4, tb, 1);
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
       produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
@@ -889,162 +898,196 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
 // Gram partials per segment: G_seg = sum_v x_v x_v^T in fp64 (products of fp32 values are
 // exact in fp64). SRC 0: x = mu. SRC 1: x = mu2 of the Kalman update (controller.py:
 // 267-268, 283-285), and mu2 / var2 are written back to mu / var.
-// All eight consumer warps work on one tile: the elementwise pass writes the tile in fp64,
-// then the fp64 tensor-core MMA (m8n8k4) accumulates the upper-triangle 8 x 8 blocks of G,
-// each block owned by one warp for the whole segment (fragments stay in registers), and
-// written out (mirrored) at the segment end. The per-tile verdict barrier (agree) orders
-// one tile's products before the next tile's elementwise pass.
+// Warp roles after the producer: four prep warps turn each staged tile into an fp64 tile
+// (Kalman update and write-back on the way) in one of two buffers; four MMA warps
+// accumulate the upper-triangle 8 x 8 blocks of G from the other buffer with the fp64
+// MMA (m8n8k4), each block owned by one warp for the whole segment (fragments in
+// registers) and written out, mirrored, at the segment end. Prep and MMA warps hand the
+// buffers over through mbarriers only (bounded waits), so a failed wait cannot leave one
+// role blocked at a barrier the other never reaches.
 // Tile image: side 0 X[v][c] with pitch rp + 8 doubles, side 1 X[c][v] with pitch TV + 4
 // (either way a fragment load of a warp touches 256 bytes in two wavefronts).
 // =====================================================================================
-// MAXB: upper 8 x 8 blocks per warp (5 up to r = 64, 17 up to r = 128)
+constexpr int kPrepWarps = 4, kMmaWarps = 8;
+constexpr int kSTG = 32 * (1 + kPrepWarps + kMmaWarps);   // threads of the Gram kernel
+// MAXB: upper 8 x 8 blocks per MMA warp (5 up to r = 64, 17 up to r = 128)
 __host__ __device__ inline int gram_maxb(int r) {
   const int nb = (r + 7) / 8;
-  return (nb * (nb + 1) / 2 + kCW - 1) / kCW;
+  return (nb * (nb + 1) / 2 + kMmaWarps - 1) / kMmaWarps;
 }
 
 template <int SRC, int MAXB>
-__global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
+__global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
                                                   Layout L, KalmanIn kin, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
   uint64_t* empty = full + L.S;
-  init_bars(full, empty, L.S, kCW);
+  uint64_t* xfull = empty + L.S;                 // [2]: prep -> MMA
+  uint64_t* xempty = xfull + 2;                  // [2]: MMA -> prep
+  const int rp = L.rp, nb = rp / 8;
+  const int nblk = nb * (nb + 1) / 2;
+  double* X0 = reinterpret_cast<double*>(smem + L.o_x);
+  const int xbuf = (L.o_red - L.o_x) / 16;       // doubles per buffer (two buffers)
+  int* btab = reinterpret_cast<int*>(smem + L.o_red);
+  // zero both fp64 buffers (padding columns stay zero), block table, barriers
+  for (int e = threadIdx.x; e < 2 * xbuf; e += kSTG) X0[e] = 0.0;
+  if (threadIdx.x == 0) {
+    int q = 0;
+    for (int bi = 0; bi < nb; ++bi)
+      for (int bj = bi; bj < nb; ++bj) btab[q++] = (bi << 8) | bj;
+    for (int i = 0; i < L.S; ++i) { mbar_init(full + i, kFullArrivals); mbar_init(empty + i, kPrepWarps); }
+    for (int i = 0; i < 2; ++i) { mbar_init(xfull + i, kPrepWarps); mbar_init(xempty + i, kMmaWarps); }
+    mbar_init_fence();
+  }
+  __syncthreads();
   TileIt it;
   it.init(mats, nmats, L.TV);
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == 0) {
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
       const MatD& M = t.mats[t.mi];
       Src a[3];
-      a[0] = make_src(M.mu, M, 4);
-      a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4);
-      a[2] = make_src(SRC == 1 ? M.z : nullptr, M, 4);
+      a[0] = make_src(M.mu, M, 4, tb, 1);
+      a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4, tb, 2);
+      a[2] = make_src(SRC == 1 ? M.z : nullptr, M, 4, tb, 3);
       const int sp = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
       const int off[3] = {L.off[0], L.off[1], L.off[2]};
       const int pitch[3] = {sp, sp, sp};
-      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln);
     });
     return;
   }
 
-  const int ct = threadIdx.x - 32;
-  const int cw = ct >> 5, lane = ct & 31;
-  const int rp = L.rp, nb = rp / 8;
-  const int nblk = nb * (nb + 1) / 2;
-  double* X = reinterpret_cast<double*>(smem + L.o_x);
-  const int xbytes = L.o_red - L.o_x;
-  for (int e = ct; e < xbytes / 8; e += kCT) X[e] = 0.0;    // zero padding columns / rows once
-  KalScal ks{};
-  if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
-  // upper-triangle blocks (bi, bj), bi <= bj, in a shared table; warp cw owns entries
-  // cw, cw + 8, ...
-  int* btab = reinterpret_cast<int*>(smem + L.o_red);
-  if (ct == 0) {
-    int q = 0;
-    for (int bi = 0; bi < nb; ++bi)
-      for (int bj = bi; bj < nb; ++bj) btab[q++] = (bi << 8) | bj;
+  if (warp <= kPrepWarps) {
+    // ------------------------------------------------------------ prep warps
+    const int pt = threadIdx.x - 32, npt = 32 * kPrepWarps;
+    KalScal ks{};
+    if (SRC == 1) ks = kal_derive(kin, reinterpret_cast<const double*>(tb.ws) + tb.kal_sum_off);
+    int i = 0;
+    bool dead = false;
+    if (!it.start_seg()) return;
+    int adv;
+    do {
+      const MatD& M = it.mats[it.mi];
+      const int r = static_cast<int>(M.r), nv = it.nv();
+      const int s = i % L.S, b = i & 1;
+      if (!dead) {
+        bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+        if (w && i >= 2) w = mbar_wait(xempty + b, (static_cast<uint32_t>(i >> 1) & 1u) ^ 1u, err);
+        dead = !__all_sync(0xffffffffu, w);
+      }
+      if (!dead) {
+        double* X = X0 + b * xbuf;
+        const int sv = (M.side == 0) ? L.xp : 1;
+        const int sc = (M.side == 0) ? 1 : L.zp;
+        const unsigned char* stage = smem + s * L.stage_bytes;
+        const float* mus = reinterpret_cast<const float*>(stage + L.off[0]);
+        const float* vas = reinterpret_cast<const float*>(stage + L.off[1]);
+        const float* zss = reinterpret_cast<const float*>(stage + L.off[2]);
+        const int n = nv * r;
+        const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
+        float* mut = tile_ptr(M.mu, M, it.s0, 4);
+        float* vat = tile_ptr(M.var, M, it.s0, 4);
+        auto body = [&](auto side_tag) {
+          constexpr int SIDE = decltype(side_tag)::value;
+          constexpr int U = 4;
+          Walk<SIDE> wk(pt, npt, r, nv);
+          for (int e = pt; e < n; e += U * npt) {
+            int vv[U], kk[U], so[U];
+            float x[U], va[U], zz[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {                   // every load before any use
+              vv[u] = wk.v; kk[u] = wk.k;
+              so[u] = wk.soff(r, L.TV);
+              wk.next();
+              if (e + u * npt < n) {
+                x[u] = mus[so[u]];
+                if (SRC == 1) { va[u] = vas[so[u]]; zz[u] = zss[so[u]]; }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              if (e + u * npt >= n) continue;
+              float xv = x[u];
+              if (SRC == 1) {
+                float mu1, var1, mu2, var2;
+                kal_predict(xv, va[u], ks, mu1, var1);
+                kal_observe(mu1, var1, zz[u], ks, mu2, var2);
+                const int g = SIDE == 0 ? vv[u] * ld + kk[u] * cs : kk[u] * ld + vv[u] * cs;
+                mut[g] = mu2;
+                vat[g] = var2;
+                xv = mu2;
+              }
+              X[vv[u] * sv + kk[u] * sc] = static_cast<double>(xv);
+            }
+          }
+        };
+        if (M.side == 0) body(std::integral_constant<int, 0>{});
+        else body(std::integral_constant<int, 1>{});
+        const int nv4 = (nv + 3) & ~3;                        // zero vectors nv .. nv4-1
+        for (int e = pt; e < (nv4 - nv) * r; e += npt) {
+          const int v = nv + e / r, c = e - (e / r) * r;
+          X[v * sv + c * sc] = 0.0;
+        }
+        __syncwarp();
+        if (lane == 0) { mbar_arrive(empty + s); mbar_arrive(xfull + b); }
+      }
+      ++i;
+      adv = it.next();
+    } while (adv != 0);
+    return;
   }
-  const int nmine = (nblk - cw + kCW - 1) / kCW;
+
+  // -------------------------------------------------------------- MMA warps
+  const int mw = warp - 1 - kPrepWarps;
+  const int fv = lane & 3, fc = lane >> 2;
+  const int nmine = (nblk - mw + kMmaWarps - 1) / kMmaWarps;
   double acc[MAXB][2];
 #pragma unroll
   for (int q = 0; q < MAXB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
-  named_sync(kBarAll, kCT);
-
   int i = 0;
-  bool ok = it.start_seg();
-  while (ok) {
-    const MatD M = it.mats[it.mi];
-    const int r = static_cast<int>(M.r);
-    const int sv = (M.side == 0) ? L.xp : 1;                 // X(v, c) = X[v*sv + c*sc]
-    const int sc = (M.side == 0) ? 1 : L.zp;
-    int adv, seg_done;
-    do {
-      const int nv = it.nv();
-      const int s = i % L.S;
-      const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
-      if (!agree(kBarAll, kCT, w)) { ok = false; break; }     // uniform over the consumers
-      const unsigned char* stage = smem + s * L.stage_bytes;
-      const float* mus = reinterpret_cast<const float*>(stage + L.off[0]);
-      const float* vas = reinterpret_cast<const float*>(stage + L.off[1]);
-      const float* zss = reinterpret_cast<const float*>(stage + L.off[2]);
-      const int n = nv * r;
-      const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
-      float* mut = tile_ptr(M.mu, M, it.s0, 4);
-      float* vat = tile_ptr(M.var, M, it.s0, 4);
-      auto body = [&](auto side_tag) {
-        constexpr int SIDE = decltype(side_tag)::value;
-        constexpr int U = 4;
-        Walk<SIDE> wk(ct, kCT, r, nv);
-        for (int e = ct; e < n; e += U * kCT) {
-          int vv[U], kk[U], so[U];
-          float x[U], va[U], zz[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {                     // every load before any use
-            vv[u] = wk.v; kk[u] = wk.k;
-            so[u] = wk.soff(r, L.TV);
-            wk.next();
-            if (e + u * kCT < n) {
-              x[u] = mus[so[u]];
-              if (SRC == 1) { va[u] = vas[so[u]]; zz[u] = zss[so[u]]; }
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            if (e + u * kCT >= n) continue;
-            float xv = x[u];
-            if (SRC == 1) {
-              float mu1, var1, mu2, var2;
-              kal_predict(xv, va[u], ks, mu1, var1);
-              kal_observe(mu1, var1, zz[u], ks, mu2, var2);
-              const int g = SIDE == 0 ? vv[u] * ld + kk[u] * cs : kk[u] * ld + vv[u] * cs;
-              mut[g] = mu2;
-              vat[g] = var2;
-              xv = mu2;
-            }
-            X[vv[u] * sv + kk[u] * sc] = static_cast<double>(xv);
-          }
-        }
-      };
-      if (M.side == 0) body(std::integral_constant<int, 0>{});
-      else body(std::integral_constant<int, 1>{});
-      const int nv4 = (nv + 3) & ~3;                          // zero vectors nv .. nv4-1
-      for (int e = ct; e < (nv4 - nv) * r; e += kCT) {
-        const int v = nv + e / r, c = e - (e / r) * r;
-        X[v * sv + c * sc] = 0.0;
-      }
-      __syncwarp();
-      if ((ct & 31) == 0) mbar_arrive(empty + s);
-      named_sync(kBarAll, kCT);                              // X complete
-      // fp64 MMA over the tile's vectors, 4 per step; fragment element (row lane>>2 of the
-      // block, vector lane&3) of both operands
-      const int fv = lane & 3, fc = lane >> 2;
-      int oa[MAXB], ob[MAXB];                                // fragment offsets of this warp's blocks
+  bool dead = false;
+  if (!it.start_seg()) return;
+  int adv;
+  do {
+    const MatD& M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r), nv = it.nv();
+    const int b = i & 1;
+    if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(xfull + b, static_cast<uint32_t>(i >> 1) & 1u, err));
+    if (!dead) {
+      const double* X = X0 + b * xbuf;
+      const int sv = (M.side == 0) ? L.xp : 1;
+      const int sc = (M.side == 0) ? 1 : L.zp;
+      int oa[MAXB], ob[MAXB];
 #pragma unroll
       for (int q = 0; q < MAXB; ++q) {
-        const int t = (q < nmine) ? btab[cw + q * kCW] : 0;
+        const int t = (q < nmine) ? btab[mw + q * kMmaWarps] : 0;
         oa[q] = 8 * (t >> 8) * sc;
         ob[q] = 8 * (t & 0xff) * sc;
       }
+      const int nv4 = (nv + 3) & ~3;
       const double* xr = X + fv * sv + fc * sc;
-      const int vstep = 4 * sv;
-      for (int v0 = 0; v0 < nv4; v0 += 4, xr += vstep) {
+      for (int v0 = 0; v0 < nv4; v0 += 4, xr += 4 * sv) {
 #pragma unroll
         for (int q = 0; q < MAXB; ++q)
           if (q < nmine) dmma8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
       }
-      ++i;
-      seg_done = it.seg;
-      adv = it.next();
-      if (adv != 1) {
-        // segment end: each warp writes its blocks (and their mirror images)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xempty + b);
+    }
+    ++i;
+    const int seg_done = it.seg;
+    adv = it.next();
+    if (adv != 1) {
+      // segment end: this warp's blocks (and their mirror images) of the partial
+      if (!dead) {
         double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
 #pragma unroll
         for (int q = 0; q < MAXB; ++q) {
           if (q < nmine) {
-            const int t = btab[cw + q * kCW];
+            const int t = btab[mw + q * kMmaWarps];
             const int bi = t >> 8, bj = t & 0xff;
             const int row = 8 * bi + (lane >> 2);
 #pragma unroll
@@ -1055,14 +1098,13 @@ __global__ void __launch_bounds__(kST, 1) k_sgram(Tables tb, const MatD* __restr
                 gout[col * r + row] = acc[q][h];
               }
             }
-            acc[q][0] = 0.0;
-            acc[q][1] = 0.0;
           }
         }
-        if (adv == 0) ok = false;
       }
-    } while (ok && adv == 1);
-  }
+#pragma unroll
+      for (int q = 0; q < MAXB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
+    }
+  } while (adv != 0);
 }
 
 // =====================================================================================

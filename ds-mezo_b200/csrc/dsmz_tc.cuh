@@ -36,7 +36,6 @@ struct alignas(64) TCBasis {
   __nv_bfloat16* V2T;     // [V_hi | V_lo]^T, row stride ldv2
   __nv_bfloat16* Y2T;     // [Y_hi | Y_lo]^T, row stride ldy2
   float* W;               // D x R fp32
-  double* g1;             // fp64 Gram partial of each 128-row W tile (CholeskyQR round 1)
   const float* Vsrc;      // caller's basis, read on the first iteration (strides v_s0, v_s1)
   const float* Vout;      // D x R contiguous basis of later iterations
   int64_t v_s0, v_s1;
@@ -48,17 +47,6 @@ struct alignas(64) TCBasis {
   int32_t pad1, pad2;
 };
 
-__device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
-  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
-}
-// 2-D TMA load into this CTA's shared memory, completing on `bar`; x is the innermost coordinate.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -239,67 +227,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
         }
       } else {
         // The pipeline stages are drained (every MMA completed before tmem_full), so the
-        // W tile is staged over them once, converted to fp64: 128 rows of R + 1 doubles
-        // (the odd row length keeps the row-per-thread stores free of bank conflicts).
-        double* wt = reinterpret_cast<double*>(smem);
+        // W tile is staged over them (rows of R + 1 floats: the row-per-thread stores are
+        // free of bank conflicts) and written out coalesced. Its fp64 Gram for the
+        // CholeskyQR is formed by the streaming Gram kernel over W.
+        float* wt = reinterpret_cast<float*>(smem);
         const int tld = R + 1;
         for (int j = 0; j < R; j += 16) {
           float hi[16], lo[16];
           tmem_ld16(trow + j, hi);
           tmem_ld16(trow + R + j, lo);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = static_cast<double>(hi[c] + lo[c]);
+          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = hi[c] + lo[c];
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
         const int t = threadIdx.x - 64;
-        // W rows past D are TMA zero fill; the valid rows go out coalesced.
         const int64_t d0 = static_cast<int64_t>(tile) * kBM;
         const int nrow = static_cast<int>(min(static_cast<int64_t>(kBM), B->D - d0));
         for (int e = t; e < nrow * R; e += kBM) {
           const int rw = e / R, c = e - rw * R;
-          B->W[(d0 + rw) * R + c] = static_cast<float>(wt[rw * tld + c]);
-        }
-        // fp64 Gram of the tile on the fp64 MMA (m8n8k4): upper-triangle 8 x 8 blocks of
-        // W^T W, up to nine per warp at a time; k-step s takes tile rows
-        // 32(s/8) + s%8 + 8kq (kq = lane & 3), which puts a warp's fragment loads in two
-        // wavefronts with the odd row pitch that keeps the staging stores conflict-free.
-        const int RR = R * R;
-        double* gout = B->g1 + static_cast<int64_t>(tile) * RR;
-        const int ew = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
-        const int g = lane >> 2, kq = lane & 3;
-        const int nb = R >> 3, nblk = nb * (nb + 1) / 2;
-        for (int q0 = ew; q0 < nblk; q0 += 4 * 9) {
-          int bi[9], bj[9];
-          double acc[9][2];
-#pragma unroll
-          for (int u = 0; u < 9; ++u) {
-            int q = q0 + 4 * u;
-            bi[u] = -1; bj[u] = 0;
-            acc[u][0] = 0.0; acc[u][1] = 0.0;
-            if (q < nblk) {
-              int row = 0;
-              while (q >= nb - row) { q -= nb - row; ++row; }
-              bi[u] = row; bj[u] = row + q;
-            }
-          }
-          for (int s = 0; s < kBM / 4; ++s) {
-            const double* wr = wt + (32 * (s >> 3) + (s & 7) + 8 * kq) * tld + g;
-#pragma unroll
-            for (int u = 0; u < 9; ++u)
-              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], wr[8 * bi[u]], wr[8 * bj[u]]);
-          }
-#pragma unroll
-          for (int u = 0; u < 9; ++u) {
-            if (bi[u] < 0) continue;
-            const int row = 8 * bi[u] + g;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int col = 8 * bj[u] + 2 * kq + h;
-              if (bi[u] == bj[u] && col < row) continue;     // mirror of the upper half
-              gout[row * R + col] = acc[u][h];
-              if (col != row) gout[col * R + row] = acc[u][h];
-            }
-          }
+          B->W[(d0 + rw) * R + c] = wt[rw * tld + c];
         }
       }
     }
