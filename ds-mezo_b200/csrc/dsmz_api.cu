@@ -77,10 +77,6 @@ size_t coef_smem(int R, int RC) {
   return (static_cast<size_t>(R + 1) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
 }
 size_t ns_smem(int r) { return r <= 64 ? 4 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
-size_t qr_apply_smem(int r) {
-  const size_t r8 = static_cast<size_t>(pad8(r)), tv = static_cast<size_t>(tile_vectors(r));
-  return r * r8 * sizeof(double) + 2 * tv * (r8 + 1) * sizeof(float);
-}
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
 // Dynamic shared memory of a streaming-kernel CTA (one CTA per SM).
@@ -473,10 +469,10 @@ bool choose_adapter_layouts(dsmz_plan* P, int fes) {
 
 bool choose_qr_layout(dsmz_plan* P) {
   bool ok = false;
-  for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {
+  for (int tv = sk::stream_tv(P->R); tv >= 8 && !ok; tv -= 8) {    // QR apply: widest tile that fits
+    if (sk::qr_variant(tv, P->R) < 0) continue;
     P->Lq = sk::qr_layout(P->R, kStreamSmem, tv);
-    if (P->Lq.S >= sk::kTeams && P->Lq.total <= kStreamSmem + 2048) { ok = true; break; }
-    if (tv == 8) break;
+    ok = P->Lq.S >= 2 && P->Lq.total <= kStreamSmem + 2048;
   }
   if (!ok) return false;
   for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {    // Gram of W (plain)
@@ -516,7 +512,10 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const bool small = sk::gram_maxb(R) <= 5;
   if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lw.total))) return rc;
-  if ((rc = set_smem(sk::k_sqr_apply, P->Lq.total))) return rc;
+  if ((rc = set_smem(sk::k_sqr_apply<2, 4>, P->Lq.total))) return rc;
+  if ((rc = set_smem(sk::k_sqr_apply<4, 2>, P->Lq.total))) return rc;
+  if ((rc = set_smem(sk::k_sqr_apply<1, 8>, P->Lq.total))) return rc;
+  if ((rc = set_smem(sk::k_sqr_apply<8, 1>, P->Lq.total))) return rc;
   if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
   const KalmanIn kin{};
   const int nb = static_cast<int>(P->bases.size());
@@ -565,7 +564,12 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_CHOL, s);
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
-    sk::k_sqr_apply<<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err);
+    switch (sk::qr_variant(P->Lq.TV, P->R)) {
+      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+    }
     P->probe_end(DSMZ_KID_PI_APPLY, s);
     DSMZ_LAUNCHED("power iteration V = W R^-1");
   }

@@ -31,11 +31,15 @@ constexpr int kCW = 8;                   // consumer warps
 constexpr int kCT = 32 * kCW;            // consumer threads
 constexpr int kST = kCT + 32;            // + producer warp 0
 constexpr int kTeams = 4;                // perturb / apply / QR apply
-// A team waits for tile i only after its tile i - kTeams, so with a ring of S >= kTeams
-// stages every stage it waits on is at most one mbarrier phase ahead (a wait two phases
-// ahead would alias on the phase parity). Plans keep S >= kTeams for the team kernels.
+// Tile i goes to team i % kTeams and ring stage i % S. With S a multiple of kTeams each
+// stage only ever holds one team's tiles, so the phase a team waits on directly follows the
+// phase it consumed itself there (a stage two phases behind would alias on the phase
+// parity). The team kernels' layouts round S down to a multiple of kTeams.
 constexpr int kTT = kCT / kTeams;        // threads per team (two warps)
-constexpr int kBarAll = 1;               // named barrier: all consumer threads
+constexpr int kBarAll = 1;               // named barrier: all consumer threads (one role)
+// Role-split fp64 Gram: producer warp, prep warps, MMA warps.
+constexpr int kPrepWarps = 4, kMmaWarps = 8;
+constexpr int kSTG = 32 * (1 + kPrepWarps + kMmaWarps);
 constexpr int kBarTeam0 = 2;             // named barriers 2..5: one per team
 
 // Vectors per tile: ~2048 elements, a multiple of 8 (16-byte bf16 rows of side-B tiles).
@@ -390,7 +394,7 @@ __host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, 
   L.zp = r + 1;
   const int fixed = al128(KW * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + al128(2 * kCW * 8 * 2) + 1024;
   int S = (budget - fixed) / L.stage_bytes;
-  S = S > 8 ? 8 : S;
+  S = S > 8 ? 8 : S / kTeams * kTeams;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
@@ -415,7 +419,7 @@ __host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int T
   L.zp = r + 1;
   const int fixed = al128(r * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + 1024;
   int S = (budget - fixed) / L.stage_bytes;
-  S = S > 8 ? 8 : S;
+  S = S > 8 ? 8 : S / kTeams * kTeams;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
@@ -425,24 +429,29 @@ __host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int T
   return L;
 }
 
-// QR apply: W rows padded to R + 4 floats; fp64 R^-1 (R x pld).
+// QR apply: W rows padded to R + 4 floats per stage (an even number of stages, at most 8);
+// fp64 R^{-1} zero-padded to rp x pld (rp = R rounded up to 8, pld = rp + 4: each half-warp's
+// B fragment on distinct banks); four fp32 result tiles (TV x zp, zp = rp + 1), two per group.
 __host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   Layout L{};
   L.r = R;
   L.TV = TV;
   const int mp = (R + 3) / 4 * 4 + 4;
+  const int rp = pad8(R);
   L.off[0] = 0; L.pitch[0] = mp * 4;
   L.stage_bytes = al128(TV * mp * 4);
-  L.pld = pad8(R);
-  L.zp = R + 1;
-  const int fixed = al128(R * L.pld * 8) + kTeams * al128(TV * L.zp * 4) + 1024;
+  L.rp = rp;
+  L.pld = rp + 4;
+  L.zp = rp + 1;
+  const int osz = al128(TV * L.zp * 4);
+  const int fixed = al128(rp * L.pld * 8) + 4 * osz + 1024;
   int S = (budget - fixed) / L.stage_bytes;
-  S = S > 8 ? 8 : S;
+  S = S > 8 ? 8 : S & ~1;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
-  L.o_z = L.o_c + al128(R * L.pld * 8);
-  L.o_bar = L.o_z + kTeams * al128(TV * L.zp * 4);
+  L.o_z = L.o_c + al128(rp * L.pld * 8);
+  L.o_bar = L.o_z + 4 * osz;
   L.total = L.o_bar + 2 * 8 * S + 128 + 128;
   return L;
 }
@@ -807,91 +816,210 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
 }
 
 // =====================================================================================
-// CholeskyQR apply of the power iteration: V = W R^{-1} in fp64 (R^{-1} exported by
-// k_chol after the fp64 workspace's first r*r doubles), V rows out and, when the next
-// product runs on the tensor cores, [V_hi | V_lo]^T (bf16, 2R x D).
+// CholeskyQR apply of the power iteration: V = W R^{-1} in fp64 (R^{-1}, upper
+// triangular, exported by k_chol after the fp64 workspace's first r*r doubles), V rows out
+// and, when the next product runs on the tensor cores, [V_hi | V_lo]^T (bf16, 2R x D).
+// Two groups of four warps take alternate tiles straight from the ring (an even number
+// of stages, so each stage has one consumer group). In a group each warp owns MV row
+// blocks x MC column blocks of 8 x 8 and forms them with the fp64 MMA: A fragments are
+// fp32 W read from the stage and widened in registers, B fragments R^{-1} in fp64. Column
+// blocks are dealt snake-wise (ascending per warp), so the k-extent of block column cb
+// (k < 8cb + 8, R^{-1} being upper triangular) shrinks the active set one block at a time
+// and every warp has the same number of MMAs. V rows are stored from the accumulators;
+// the bf16 pair goes through an fp32 tile per group (two, alternating), eight vectors per
+// thread and 16-byte stores. Waits are bounded; a group agrees on each tile's verdict.
 // =====================================================================================
-__global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
-                                                      Layout L, int* err) {
+constexpr int kQrGroups = 2;
+constexpr int kQrGroupWarps = kCW / kQrGroups;
+
+// Warp shape of the QR apply for tiles of TV vectors and width R: the first of
+// (MV, MC) = (2,4), (4,2), (1,8), (8,1) whose warp grid fits a group; -1 if none.
+__host__ __device__ inline int qr_variant(int TV, int R) {
+  const int nvb = (TV + 7) / 8, ncb = (R + 7) / 8;
+  const int mv[4] = {2, 4, 1, 8}, mc[4] = {4, 2, 8, 1};
+  for (int v = 0; v < 4; ++v)
+    if (((nvb + mv[v] - 1) / mv[v]) * ((ncb + mc[v] - 1) / mc[v]) <= kQrGroupWarps) return v;
+  return -1;
+}
+
+// [hi | lo] bf16 rows of eight fp32 values x[0..7] (hi = bf16(x), lo = bf16(x - hi)).
+__device__ __forceinline__ void bf16_pair8(const float* x, uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(x[2 * q], x[2 * q + 1]);
+    const float2 hf = __bfloat1622float2(hh);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(x[2 * q] - hf.x, x[2 * q + 1] - hf.y);
+    h[q] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[q] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <int MV, int MC>
+__global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
+                                                      int nsegs, Layout L, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
   uint64_t* empty = full + L.S;
-  init_bars(full, empty, L.S, 2);
+  double* Ps = reinterpret_cast<double*>(smem + L.o_c);        // rp x pld fp64 R^{-1}
+  const int osz = (L.o_bar - L.o_z) / 16;                       // floats per fp32 tile (four)
+  {                                                             // stage columns r .. mp-1 stay zero
+    uint4* z = reinterpret_cast<uint4*>(smem);
+    for (int e = threadIdx.x; e < L.fixed0 / 16; e += kST) z[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < L.S; ++i) { mbar_init(full + i, kFullArrivals); mbar_init(empty + i, kQrGroupWarps); }
+    mbar_init_fence();
+  }
+  __syncthreads();
   TileIt it;
   it.init(mats, nmats, L.TV);
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == 0) {
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
       const MatD& M = t.mats[t.mi];
       Src a[1];
       a[0] = make_src(M.mu, M, 4, tb, 1);
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
-      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln);
     });
     return;
   }
 
-  const int ct = threadIdx.x - 32;
-  const int team = ct / kTT, tt = ct - team * kTT;
-  double* Ps = reinterpret_cast<double*>(smem + L.o_c);
-  float* os = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
-  int i = 0;
+  const int mw = warp - 1;
+  const int grp = mw / kQrGroupWarps, gw = mw - grp * kQrGroupWarps;
+  const int ct = threadIdx.x - 32, gt = ct - grp * 32 * kQrGroupWarps;
+  const int g = lane >> 2, kq = lane & 3;
+  const int wp = L.pitch[0] / 4;
+  const int WV = ((L.TV + 7) / 8 + MV - 1) / MV;
+  const int wv = gw % WV, wc = gw / WV;
+  int i = 0, jt = 0;
   bool dead = false;
-  bool more = it.start_seg();
   int cur = -1;
-  while (more) {
-    const MatD M = it.mats[it.mi];
-    const int r = static_cast<int>(M.r);
-    if (it.mi != cur) {
+  if (!it.start_seg()) return;
+  int adv;
+  do {
+    const MatD& M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r), nv = it.nv();
+    if (it.mi != cur) {                            // R^{-1} of this basis (both groups)
       named_sync(kBarAll, kCT);
       const double* Rd = reinterpret_cast<const double*>(tb.ws) + M.dw_off + static_cast<int64_t>(r) * r;
-      for (int e = ct; e < r * L.pld; e += kCT) {
-        const int a = e / L.pld, c = e - a * L.pld;
-        Ps[e] = (c < r) ? Rd[a * r + c] : 0.0;
+      for (int e = ct; e < L.rp * L.pld; e += kCT) {
+        const int a2 = e / L.pld, c = e - a2 * L.pld;
+        Ps[e] = (a2 < r && c < r) ? Rd[a2 * r + c] : 0.0;
       }
       named_sync(kBarAll, kCT);
       cur = it.mi;
     }
-    float* V = reinterpret_cast<float*>(M.param);
-    int adv;
-    do {
-      const int nv = it.nv();
-      if ((i % kTeams) == team && !dead) {
-        const int s = i % L.S;
-        const bool w = mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
-        dead = !agree(kBarTeam0 + team, kTT, w);
-        if (!dead) {
-          const float* Ws = reinterpret_cast<const float*>(smem + s * L.stage_bytes);
-          mm_rows_f64(Ws, L.pitch[0] / 4, Ps, L.pld, nv, r, r, tt, kTT,
-                      [&](int v, int c, double x) { os[v * L.zp + c] = static_cast<float>(x); });
-          __syncwarp();
-          if ((tt & 31) == 0) mbar_arrive(empty + s);   // W tile consumed
-          named_sync(kBarTeam0 + team, kTT);
-          const int n = nv * r;
-          for (int e = tt; e < n; e += kTT) {           // V rows, coalesced
-            const int v = e / r, c = e - v * r;
-            V[(it.s0 + v) * M.ld + c] = os[v * L.zp + c];
-          }
-          if (M.v2t) {
-            for (int e = tt; e < n; e += kTT) {         // [V_hi | V_lo]^T, coalesced along d
-              const int c = e / nv, v = e - c * nv;
-              const float x = os[v * L.zp + c];
-              const __nv_bfloat16 h = __float2bfloat16_rn(x);
-              M.v2t[static_cast<int64_t>(c) * M.ldv2 + it.s0 + v] = h;
-              M.v2t[static_cast<int64_t>(r + c) * M.ldv2 + it.s0 + v] = __float2bfloat16_rn(x - __bfloat162float(h));
+    if ((i & 1) == grp) {
+      const int s = i % L.S;
+      const bool w = dead ? false : mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
+      dead = !agree(kBarTeam0 + grp, 32 * kQrGroupWarps, w);
+      if (!dead) {
+        const float* Ws = reinterpret_cast<const float*>(smem + s * L.stage_bytes);
+        const int nvb = (nv + 7) >> 3, ncb = (r + 7) >> 3;
+        const int WC = (ncb + MC - 1) / MC;
+        int rv[MV], cc[MC], kb[MC];
+        bool rok[MV], cok[MC];
+#pragma unroll
+        for (int j = 0; j < MV; ++j) { rv[j] = wv + WV * j; rok[j] = wc < WC && rv[j] < nvb; }
+#pragma unroll
+        for (int j = 0; j < MC; ++j) {              // ascending; k-extent 8cc + 8 (0 if none)
+          cc[j] = (j >> 1) * 2 * WC + ((j & 1) ? 2 * WC - 1 - wc : wc);
+          cok[j] = wc < WC && cc[j] < ncb;
+          kb[j] = cok[j] ? 8 * cc[j] + 8 : (j > 0 ? kb[j - 1] : 0);
+          if (!cok[j]) cc[j] = 0;
+        }
+        double acc[MV][MC][2];
+#pragma unroll
+        for (int jv = 0; jv < MV; ++jv)
+#pragma unroll
+          for (int jc = 0; jc < MC; ++jc) { acc[jv][jc][0] = 0.0; acc[jv][jc][1] = 0.0; }
+        const float* xa[MV];
+        const double* pb[MC];
+#pragma unroll
+        for (int jv = 0; jv < MV; ++jv) xa[jv] = Ws + (8 * (rok[jv] ? rv[jv] : 0) + g) * wp + kq;
+#pragma unroll
+        for (int jc = 0; jc < MC; ++jc) pb[jc] = Ps + kq * L.pld + 8 * cc[jc] + g;
+        const int pstep = 4 * L.pld;
+        int k0 = 0;
+#pragma unroll
+        for (int j0 = 0; j0 < MC; ++j0) {           // blocks j0 .. MC-1 active for k < kb[j0]
+          for (; k0 < kb[j0]; k0 += 4) {
+            double av[MV];
+#pragma unroll
+            for (int jv = 0; jv < MV; ++jv) av[jv] = static_cast<double>(xa[jv][k0]);
+            const int po = (k0 >> 2) * pstep;
+#pragma unroll
+            for (int jc = j0; jc < MC; ++jc) {
+              const double bv = pb[jc][po];
+#pragma unroll
+              for (int jv = 0; jv < MV; ++jv)
+                if (rok[jv] && cok[jc]) dmma8x8x4(acc[jv][jc][0], acc[jv][jc][1], av[jv], bv);
             }
           }
-          named_sync(kBarTeam0 + team, kTT);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);      // W tile consumed
+        float* V = reinterpret_cast<float*>(M.param);
+        const int64_t ldV = M.ld;
+        __nv_bfloat16* const v2t = M.v2t;
+        const int64_t ldv2 = M.ldv2;
+        const bool vec2 = (ldV % 2) == 0 && (reinterpret_cast<uintptr_t>(V) % 8) == 0;
+        float* os = reinterpret_cast<float*>(smem + L.o_z) + (2 * grp + (jt & 1)) * osz;
+#pragma unroll
+        for (int jv = 0; jv < MV; ++jv) {
+#pragma unroll
+          for (int jc = 0; jc < MC; ++jc) {
+            if (!rok[jv] || !cok[jc]) continue;
+            const int v = 8 * rv[jv] + g, c = 8 * cc[jc] + 2 * kq;
+            const float x0 = static_cast<float>(acc[jv][jc][0]), x1 = static_cast<float>(acc[jv][jc][1]);
+            if (v < nv) {                           // V rows, from the accumulators
+              float* row = V + static_cast<int64_t>(it.s0 + v) * ldV;
+              if (vec2 && c + 1 < r) {
+                *reinterpret_cast<float2*>(row + c) = make_float2(x0, x1);
+              } else {
+                if (c < r) row[c] = x0;
+                if (c + 1 < r) row[c + 1] = x1;
+              }
+            }
+            if (v2t) { os[v * L.zp + c] = x0; os[v * L.zp + c + 1] = x1; }
+          }
+        }
+        if (v2t) {                                  // [V_hi | V_lo]^T, coalesced along d
+          named_sync(kBarTeam0 + grp, 32 * kQrGroupWarps);
+          const int nu = r * (nv >> 3);             // eight vectors per unit
+          for (int u = gt; u < nu; u += 32 * kQrGroupWarps) {
+            const int c = u % r, v0 = (u / r) * 8;
+            float x[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) x[q] = os[(v0 + q) * L.zp + c];
+            uint4 hi, lo;
+            bf16_pair8(x, hi, lo);
+            *reinterpret_cast<uint4*>(v2t + static_cast<int64_t>(c) * ldv2 + it.s0 + v0) = hi;
+            *reinterpret_cast<uint4*>(v2t + static_cast<int64_t>(r + c) * ldv2 + it.s0 + v0) = lo;
+          }
+          for (int e = (nv & ~7) * r + gt; e < nv * r; e += 32 * kQrGroupWarps) {   // ragged tail
+            const int v = e / r, c = e - v * r;
+            const float x = os[v * L.zp + c];
+            const __nv_bfloat16 h = __float2bfloat16_rn(x);
+            v2t[static_cast<int64_t>(c) * ldv2 + it.s0 + v] = h;
+            v2t[static_cast<int64_t>(r + c) * ldv2 + it.s0 + v] = __float2bfloat16_rn(x - __bfloat162float(h));
+          }
+        }
+        // the group's next tile writes the other fp32 tile; the barrier there orders the
+        // reads above before this tile is written again
       }
-      ++i;
-      adv = it.next();
-    } while (adv == 1);
-    more = (adv == 2);
-  }
+      ++jt;
+    }
+    ++i;
+    adv = it.next();
+  } while (adv != 0);
 }
 
 // =====================================================================================
@@ -908,8 +1036,6 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
 // Tile image: side 0 X[v][c] with pitch rp + 8 doubles, side 1 X[c][v] with pitch TV + 4
 // (either way a fragment load of a warp touches 256 bytes in two wavefronts).
 // =====================================================================================
-constexpr int kPrepWarps = 4, kMmaWarps = 8;
-constexpr int kSTG = 32 * (1 + kPrepWarps + kMmaWarps);   // threads of the Gram kernel
 // MAXB: upper 8 x 8 blocks per MMA warp (5 up to r = 64, 17 up to r = 128)
 __host__ __device__ inline int gram_maxb(int r) {
   const int nb = (r + 7) / 8;
