@@ -103,6 +103,8 @@ void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bo
   const size_t rr = static_cast<size_t>(m.r) * m.r;
   m.gram_off = alloc_gram ? static_cast<int64_t>(L.take(m.nseg * rr * sizeof(double)) / sizeof(double)) : 0;
   m.tmap = -1;
+  m.kmap = -1;
+  m.rmap = -1;
   m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
   m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * static_cast<size_t>(pad8(static_cast<int>(m.r))) *
                                                       ns_ld(static_cast<int>(m.r)) * sizeof(double)) / sizeof(double)) : 0;
@@ -196,6 +198,21 @@ bool encode_rows_2d(CUtensorMap* m, int dtype, const void* base, uint64_t inner,
   return fn(m, dtype == DSMZ_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
             const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D fp32 tensor map over rows of `cols` floats with boxes of 32 columns x TV rows and the
+// 128-byte swizzle (the streaming kernels' swizzled row image), zero fill outside.
+bool encode_rows_swz(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes,
+                     uint32_t TV) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {32, TV};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -373,6 +390,8 @@ void add_w_tables(dsmz_plan* P) {
     MatD a{};
     a.nvec = b.D; a.r = b.R; a.ld = b.R; a.cs = 1; a.side = 0; a.owner = static_cast<int32_t>(i);
     a.tmap = -1;
+    a.kmap = -1;
+    a.rmap = -1;
     a.segv = seg_vectors(b.R);
     a.nseg = static_cast<int32_t>((b.D + a.segv - 1) / a.segv);
     a.p_off = static_cast<int64_t>(P->ws.take((rr + 4) * sizeof(float)) / sizeof(float));
@@ -424,6 +443,31 @@ void bind_side1_maps(dsmz_plan* P) {
     }
     if (!ok) m.tmap = -1;
   }
+}
+
+// Swizzled row boxes (32 fp32 columns x TV rows) of the perturbation's K operand (Zc_A rows
+// in the workspace, or the basis rows), of side-0 mu and of W; a slot the driver refuses
+// (alignment, strides) falls back to element copies into the same image (slot = -1).
+void bind_swz_maps(dsmz_plan* P) {
+  auto enc = [&](int32_t& slot, const void* base, int64_t cols, int64_t rows, int64_t ld, int64_t cs, int TV) {
+    if (slot < 0) return;
+    const bool ok = base != nullptr && cs == 1 && TV <= 256 && TV % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * 4) % 16 == 0 &&
+                    encode_rows_swz(&P->smaps[slot], base, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
+                                    static_cast<uint64_t>(ld) * 4, static_cast<uint32_t>(TV));
+    if (!ok) slot = -1;
+  };
+  for (MatD& m : P->mats) {
+    const ModD& D = P->mods[m.owner];
+    if (m.side == 0) {
+      enc(m.kmap, reinterpret_cast<const float*>(P->workspace) + D.zca_off, D.rca, m.nvec, D.rca, 1, P->Lp.TV);
+      enc(m.rmap, m.mu, m.r, m.nvec, m.ld, m.cs, P->La.TV);
+    } else {
+      const BasisD& Bd = P->bases[D.basis];
+      enc(m.kmap, Bd.Vin, D.rc, Bd.D, Bd.v_s0, Bd.v_s1, P->Lp.TV);
+    }
+  }
+  for (MatD& m : P->w2) enc(m.rmap, m.mu, m.r, m.nvec, m.ld, m.cs, P->Lq.TV);
 }
 
 // Fills pointers and tensor maps once the workspace is known; false if the driver refuses
@@ -904,6 +948,17 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     m.tmap = static_cast<int32_t>(P->smaps.size());
     P->smaps.resize(P->smaps.size() + 4);
   }
+  for (MatD& m : P->mats) {           // swizzled row boxes: K operand, side-0 own rows
+    m.kmap = static_cast<int32_t>(P->smaps.size());
+    P->smaps.resize(P->smaps.size() + 1);
+    if (m.side != 0) continue;
+    m.rmap = static_cast<int32_t>(P->smaps.size());
+    P->smaps.resize(P->smaps.size() + 1);
+  }
+  for (MatD& m : P->w2) {             // W rows of the QR apply
+    m.rmap = static_cast<int32_t>(P->smaps.size());
+    P->smaps.resize(P->smaps.size() + 1);
+  }
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * static_cast<size_t>(P->ndir) * sizeof(double)) / sizeof(double));
   P->pack();
@@ -940,6 +995,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   patch_ws_pointers(P);
   if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
   bind_side1_maps(P);
+  bind_swz_maps(P);
   {
     cudaError_t ez = cudaMemsetAsync(P->workspace + P->err_off, 0, sizeof(int), static_cast<cudaStream_t>(stream));
     if (ez != cudaSuccess) return cuda_fail("dsmz_plan_bind: error word", ez);

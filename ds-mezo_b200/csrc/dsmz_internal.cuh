@@ -34,6 +34,10 @@ struct MatD {
   int32_t chunk0;             // chunk (CTA) holding tile0; segment seg0 + c - chunk0 of chunk c
   int32_t tmap;               // side 1: first of four 2-D tensor maps (param, mu, var, z) in
                               // Tables::smaps, or -1
+  int32_t kmap;               // 128-byte-swizzled row boxes (Tables::smaps) of the perturbation's
+                              // K operand (Zc_A rows on side 0, basis rows on side 1), or -1
+  int32_t rmap;               // the same for the matrix's own rows (side-0 mu; W), or -1
+  int32_t pad1;
 };
 
 struct ModD {

@@ -49,6 +49,18 @@ __host__ __device__ inline int stream_tv(int r) {
 }
 __host__ __device__ inline int al16(int b) { return (b + 15) & ~15; }
 __host__ __device__ inline int al128(int b) { return (b + 127) & ~127; }
+__host__ __device__ inline int al1024(int b) { return (b + 1023) & ~1023; }
+
+// Swizzled row image: rows of a tile (TV vectors, each of w fp32 components) stored as
+// ceil(w / 32) boxes of TV rows x 128 bytes with the 128-byte swizzle of a 2-D TMA copy
+// (16-byte chunk c of row v at chunk c ^ (v % 8)). A box is 1024-byte aligned (TV % 8 == 0).
+// Four consecutive components of a row are one aligned 16-byte chunk, and eight rows read
+// at the same column fall into eight different chunks.
+__host__ __device__ inline int swz_boxes(int w) { return (w + 31) / 32; }
+__host__ __device__ inline int swz_bytes(int w, int TV) { return swz_boxes(w) * TV * 128; }
+__host__ __device__ inline int swz_off(int v, int a, int TV) {
+  return (a >> 5) * TV * 128 + v * 128 + ((((a >> 2) & 7) ^ (v & 7)) << 4) + (a & 3) * 4;
+}
 
 // One input array of a tile. Side 0: vector v is the row at v*ld (components k*cs);
 // side 1: vector v is the column at v*cs (components k*ld). In shared memory, side 0
@@ -56,15 +68,16 @@ __host__ __device__ inline int al128(int b) { return (b + 127) & ~127; }
 struct Src {
   const char* base;
   int64_t ld, cs;
-  int32_t es, side, r, pad;
-  const CUtensorMap* map;     // side 1 with a tile-box tensor map: one TMA copy per tile
+  int32_t es, side, r, swz;   // swz: the stage holds the swizzled row image (side-0 fp32 rows)
+  const CUtensorMap* map;     // side 1: tile-box tensor map (one TMA copy); swz: 32-column
+                              // swizzled boxes (one TMA copy per box)
 };
 
 // Array `which` (0 param, 1 mu, 2 var, 3 z) of matrix M, with its tensor map when M has them.
 __device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es, const Tables& tb, int which) {
   Src a;
   a.base = reinterpret_cast<const char*>(base);
-  a.ld = M.ld; a.cs = M.cs; a.es = es; a.side = M.side; a.r = static_cast<int>(M.r); a.pad = 0;
+  a.ld = M.ld; a.cs = M.cs; a.es = es; a.side = M.side; a.r = static_cast<int>(M.r); a.swz = 0;
   a.map = (M.side == 1 && M.tmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.tmap + which : nullptr;
   return a;
 }
@@ -73,9 +86,12 @@ __device__ __forceinline__ Src make_src(const void* base, const MatD& M, int es,
 // contiguous run of global memory (side-0 rows of exactly r elements, unpadded); 16-byte
 // cp.async chunks spread over the producer lanes when every row is 16-byte aligned (strided
 // or padded rows: many short rows would starve the bulk engine); element copies otherwise.
-enum { kCopyBulk = 0, kCopy16 = 1, kCopyPlain = 2, kCopyTensor = 3 };
+enum { kCopyBulk = 0, kCopy16 = 1, kCopyPlain = 2, kCopyTensor = 3, kCopySwzTma = 4, kCopySwzPlain = 5 };
 
 __device__ __forceinline__ int copy_mode(const Src& a, int64_t s0, int nv, int pitch, const void* dst) {
+  // swizzled row image: a TMA copy per 32-column box (zero fill past the rows and columns),
+  // or element copies into the same image
+  if (a.swz) return (a.map != nullptr && (reinterpret_cast<uintptr_t>(dst) & 1023) == 0) ? kCopySwzTma : kCopySwzPlain;
   // side 1 with a tensor map: one 2-D TMA box (TV x r, dense rows of TV, zero fill past
   // the matrix end); x = s0 is a multiple of the tile width (16-byte aligned)
   if (a.map != nullptr && ((reinterpret_cast<uintptr_t>(dst) & 127) == 0)) return kCopyTensor;
@@ -132,6 +148,19 @@ __device__ __forceinline__ void plain_copy(const Src& a, int64_t s0, int nv, cha
   }
 }
 
+// Element copies of side-0 fp32 rows into the swizzled row image (pitch = bytes per box,
+// TV x 128): every column of the boxes is written, zeros past the row width r.
+__device__ __forceinline__ void swz_plain_copy(const Src& a, int64_t s0, int nv, char* dst, int pitch, int lane) {
+  const int TV = pitch / 128;
+  const int w = 32 * swz_boxes(a.r);
+  const int n = nv * w;
+  for (int e = lane; e < n; e += 32) {
+    const int v = e / w, k = e - v * w;
+    const float x = (k < a.r) ? *reinterpret_cast<const float*>(a.base + ((s0 + v) * a.ld + k * a.cs) * 4) : 0.f;
+    *reinterpret_cast<float*>(dst + swz_off(v, k, TV)) = x;
+  }
+}
+
 // Fills one stage with up to NA arrays (null base: absent). The stage's `full` barrier
 // expects 33 arrivals: lane 0's expect_tx (bulk bytes, after the element copies) and one
 // cp.async-tracking arrival per lane. Called by all 32 producer lanes.
@@ -148,7 +177,9 @@ __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA]
     mode[i] = copy_mode(a[i], s0, nv, pitch[i], stage + off[i]);
     if (mode[i] == kCopyBulk) tx += static_cast<uint32_t>(nv) * a[i].r * a[i].es;
     else if (mode[i] == kCopyTensor) tx += static_cast<uint32_t>(pitch[i]) * a[i].r;   // the whole box
+    else if (mode[i] == kCopySwzTma) tx += static_cast<uint32_t>(pitch[i]) * swz_boxes(a[i].r);   // whole boxes
     else if (mode[i] == kCopyPlain) plain_copy(a[i], s0, nv, stage + off[i], pitch[i], lane);
+    else if (mode[i] == kCopySwzPlain) swz_plain_copy(a[i], s0, nv, stage + off[i], pitch[i], lane);
   }
   __syncwarp();
   if (lane == 0) mbar_expect_tx(full, tx);
@@ -165,6 +196,12 @@ __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA]
       if (lane == 0) {
         tmap_acquire(a[i].map);
         tma_load_2d(stage + off[i], a[i].map, static_cast<int>(s0), 0, full);
+      }
+    } else if (mode[i] == kCopySwzTma) {
+      if (lane == 0) {
+        tmap_acquire(a[i].map);
+        for (int b = 0; b < swz_boxes(a[i].r); ++b)
+          tma_load_2d(stage + off[i] + b * pitch[i], a[i].map, 32 * b, static_cast<int>(s0), full);
       }
     }
   }
@@ -275,6 +312,66 @@ __device__ __forceinline__ void mm_rows(const float* __restrict__ X, int vs, int
   }
 }
 
+// mm_rows with X the swizzled row image of the tile (boxes of TV rows, swz_off): a thread
+// block's four vectors read four consecutive components as one 16-byte chunk each (eight
+// distinct chunks for the rows a warp touches: no bank conflicts). K4 = K rounded up to 4;
+// the image's columns K .. K4-1 are zero and P has K4 rows (zero past K).
+template <typename Sink>
+__device__ __forceinline__ void mm_rows_sw(const unsigned char* __restrict__ X, int TV, const float* __restrict__ P,
+                                           int pld, int nv, int K4, int nc, int t, int nt, Sink sink) {
+  const int cbs = pld >> 3, half = pld >> 1;
+  const int Q = (nv + 3) >> 2;
+  const int boxb = TV * 128;
+  for (int blk = t; blk < Q * cbs; blk += nt) {
+    const int vb = blk / cbs, cb = blk - vb * cbs;
+    const int c0 = cb * 4;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    const unsigned char* xr[4];
+    int sw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = vb + i * Q;
+      xr[i] = X + v * 128;
+      sw[i] = v & 7;
+    }
+    const float* pr = P + c0;
+    for (int a4 = 0; a4 < K4; a4 += 4) {
+      const int boff = (a4 >> 5) * boxb, ch = (a4 >> 2) & 7;
+      float4 x4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x4[i] = *reinterpret_cast<const float4*>(xr[i] + boff + ((ch ^ sw[i]) << 4));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 p0 = *reinterpret_cast<const float4*>(pr);
+        const float4 p1 = *reinterpret_cast<const float4*>(pr + half);
+        pr += pld;
+        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        float xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xv[i] = u == 0 ? x4[i].x : u == 1 ? x4[i].y : u == 2 ? x4[i].z : x4[i].w;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], pv[j], acc[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = vb + i * Q;
+      if (v >= nv) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j < 4) ? c0 + j : half + c0 + j - 4;
+        if (c < nc) sink(v, c, acc[i][j]);
+      }
+    }
+  }
+}
+
 // fp64 variant: P is r x pld doubles; columns {2cb, 2cb+1} + g*pld/4 for g < 4 (each
 // thread's double2 loads of a warp cover contiguous 256-byte runs). pld % 8 == 0.
 template <typename Sink>
@@ -355,6 +452,43 @@ __device__ __forceinline__ void st_fac(void* p, int i, float x) {
   if (FES == 2) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x);
   else reinterpret_cast<float*>(p)[i] = x;
 }
+// Four consecutive factor elements (8 bytes of bf16 or 16 of fp32, aligned).
+template <int FES>
+__device__ __forceinline__ float4 ld_fac4(const void* p, int i) {
+  if (FES == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+}
+template <int FES>
+__device__ __forceinline__ void st_fac4(void* p, int i, float4 x) {
+  if (FES == 2) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x.x, x.y), b = __floats2bfloat162_rn(x.z, x.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = u;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = x;
+  }
+}
+__device__ __forceinline__ bool aligned_to(const void* p, int bytes) {
+  return (reinterpret_cast<uintptr_t>(p) & static_cast<uintptr_t>(bytes - 1)) == 0;
+}
+// Steps of four consecutive elements of a tile along its contiguous direction (component
+// k on side 0, vector v on side 1): (v, k) of the step's first element.
+template <int SIDE>
+struct Walk4 {
+  Walk<SIDE> w;
+  __device__ __forceinline__ Walk4(int e0, int step, int r, int nv)
+      : w(e0, step, SIDE == 0 ? r / 4 : r, SIDE == 0 ? nv : nv / 4) {}
+  __device__ __forceinline__ int v() const { return SIDE == 0 ? w.v : 4 * w.v; }
+  __device__ __forceinline__ int k() const { return SIDE == 0 ? 4 * w.k : w.k; }
+  __device__ __forceinline__ void next() { w.next(); }
+};
 // Element pointer of the tile's first element (vector s0, component 0).
 template <typename T>
 __device__ __forceinline__ T* tile_ptr(T* base, const MatD& M, int64_t s0, int es) {
@@ -377,74 +511,78 @@ struct Layout {
 };
 
 // Perturb: p, mu, var (unpadded, MODE 0 only) and the K operand rows (Zc_A rows of width
-// RCA, or basis rows of width RC), padded to pitch KW + 4 floats.
+// RCA, or basis rows of width RC) as a swizzled row image (pitch[3]: bytes per box); the
+// coefficient matrix with KW rounded up to 4 rows (zero rows past KW).
 __host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int fes, int mode, int budget, int TV) {
   Layout L{};
   L.r = r;
   L.TV = TV;
   const int KW = RC > RCA ? RC : RCA;
-  const int kp = (KW + 3) / 4 * 4 + 4;
+  const int K4 = (KW + 3) & ~3;
   int o = 0;
   L.off[0] = o; L.pitch[0] = (mode == 0) ? r * fes : 0;               o += al128(mode == 0 ? TV * r * fes : 0);
   L.off[1] = o; L.pitch[1] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
   L.off[2] = o; L.pitch[2] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
-  L.off[3] = o; L.pitch[3] = kp * 4;                                  o += al128(TV * kp * 4);
-  L.stage_bytes = o;
+  o = al1024(o);
+  L.off[3] = o; L.pitch[3] = TV * 128;                                o += swz_bytes(KW, TV);
+  L.stage_bytes = al1024(o);
   L.pld = pad8(R);
   L.zp = r + 1;
-  const int fixed = al128(KW * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + al128(2 * kCW * 8 * 2) + 1024;
+  const int fixed = al128(K4 * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + al128(2 * kCW * 8 * 2) + 2048;
   int S = (budget - fixed) / L.stage_bytes;
   S = S > 8 ? 8 : S / kTeams * kTeams;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
-  L.o_z = L.o_c + al128(KW * L.pld * 4);
+  L.o_z = L.o_c + al128(K4 * L.pld * 4);
   L.o_red = L.o_z + kTeams * al128(TV * L.zp * 4);
   L.o_bar = L.o_red + al128(2 * kCW * 8 * 2);
-  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  L.total = L.o_bar + 2 * 8 * S + 1024 + 128;
   return L;
 }
 
-// Apply: p (unpadded) and mu (side 0 rows padded to r + 4 floats).
+// Apply: p (unpadded) and mu (side 0: swizzled row image, pitch[1] bytes per box; side 1:
+// dense rows of TV); the r x r apply matrix with r rounded up to 4 rows (zero rows past r).
 __host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int TV) {
   Layout L{};
   L.r = r;
   L.TV = TV;
-  const int mp = (r + 3) / 4 * 4 + 4;
+  const int r4 = (r + 3) & ~3;
+  const int mub = swz_bytes(r, TV) > TV * r * 4 ? swz_bytes(r, TV) : TV * r * 4;
   int o = 0;
   L.off[0] = o; L.pitch[0] = r * fes;                                   o += al128(TV * r * fes);
-  L.off[1] = o; L.pitch[1] = mp * 4;                                    o += al128(TV * mp * 4);
-  L.stage_bytes = o;
+  o = al1024(o);
+  L.off[1] = o; L.pitch[1] = TV * 128;                                  o += mub;
+  L.stage_bytes = al1024(o);
   L.pld = pad8(r);
   L.zp = r + 1;
-  const int fixed = al128(r * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + 1024;
+  const int fixed = al128(r4 * L.pld * 4) + kTeams * al128(TV * L.zp * 4) + 2048;
   int S = (budget - fixed) / L.stage_bytes;
   S = S > 8 ? 8 : S / kTeams * kTeams;
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
-  L.o_z = L.o_c + al128(r * L.pld * 4);
+  L.o_z = L.o_c + al128(r4 * L.pld * 4);
   L.o_bar = L.o_z + kTeams * al128(TV * L.zp * 4);
-  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  L.total = L.o_bar + 2 * 8 * S + 1024 + 128;
   return L;
 }
 
-// QR apply: W rows padded to R + 4 floats per stage (an even number of stages, at most 8);
+// QR apply: W rows as a swizzled row image per stage (an even number of stages, at most 8);
 // fp64 R^{-1} zero-padded to rp x pld (rp = R rounded up to 8, pld = rp + 4: each half-warp's
 // B fragment on distinct banks); four fp32 result tiles (TV x zp, zp = rp + 1), two per group.
 __host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   Layout L{};
   L.r = R;
   L.TV = TV;
-  const int mp = (R + 3) / 4 * 4 + 4;
   const int rp = pad8(R);
-  L.off[0] = 0; L.pitch[0] = mp * 4;
-  L.stage_bytes = al128(TV * mp * 4);
+  L.off[0] = 0; L.pitch[0] = TV * 128;
+  L.stage_bytes = swz_bytes(R, TV);
   L.rp = rp;
   L.pld = rp + 4;
   L.zp = rp + 1;
   const int osz = al128(TV * L.zp * 4);
-  const int fixed = al128(rp * L.pld * 8) + 4 * osz + 1024;
+  const int fixed = al128(rp * L.pld * 8) + 4 * osz + 2048;
   int S = (budget - fixed) / L.stage_bytes;
   S = S > 8 ? 8 : S & ~1;
   L.S = S;
@@ -452,7 +590,7 @@ __host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   L.o_c = L.fixed0;
   L.o_z = L.o_c + al128(rp * L.pld * 8);
   L.o_bar = L.o_z + 4 * osz;
-  L.total = L.o_bar + 2 * 8 * S + 128 + 128;
+  L.total = L.o_bar + 2 * 8 * S + 1024 + 128;
   return L;
 }
 
@@ -478,12 +616,12 @@ __host__ __device__ inline Layout gram_layout(int r, int kalman, int budget, int
   L.o_x = L.fixed0;
   L.o_red = L.o_x + 2 * xbytes;    // block table (<= 136 ints)
   L.o_bar = L.o_red + 1024;
-  L.total = L.o_bar + 2 * 8 * S + 4 * 8 + 128 + 128;
+  L.total = L.o_bar + 2 * 8 * S + 4 * 8 + 1024 + 128;
   return L;
 }
 
 __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
-  return raw + ((128u - (smem_u32(raw) & 127u)) & 127u);
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
 }
 
 // Producer loop shared by every streaming kernel: walks the CTA's tiles, waits for the
@@ -589,7 +727,8 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
       a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4, tb, 2);
       // K operand: rows s0.. of Zc_A (d_out x RCA) or of the basis (d_in x RC)
       Src k{};
-      k.es = 4; k.side = 0; k.cs = 1; k.map = nullptr;
+      k.es = 4; k.side = 0; k.cs = 1; k.swz = 1;
+      k.map = (M.kmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.kmap : nullptr;
       if (M.side == 0) {
         k.base = reinterpret_cast<const char*>(MODE == 0 ? reinterpret_cast<const float*>(tb.ws) + D.zca_off
                                                          : D.zcA_ext);
@@ -625,16 +764,17 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
     const int KW = (M.side == 0) ? D.rca : D.rc;
     const float* coef = reinterpret_cast<const float*>(tb.ws) + D.coef_off;
     named_sync(kBarAll, kCT);                         // every team is done with the previous segment
+    const int K4 = (KW + 3) & ~3;                     // rows past KW are zero
     if (M.side == 0) {
       const float* Qm = coef + static_cast<int64_t>(D.r) * D.rc;   // R x RCA
-      for (int e = ct; e < KW * L.pld; e += kCT) {
+      for (int e = ct; e < K4 * L.pld; e += kCT) {
         const int k = e / L.pld, c = e - k * L.pld;
-        Cs[e] = (c < D.r) ? Qm[c * D.rca + k] : 0.f;
+        Cs[e] = (k < KW && c < D.r) ? Qm[c * D.rca + k] : 0.f;
       }
     } else {
-      for (int e = ct; e < KW * L.pld; e += kCT) {
+      for (int e = ct; e < K4 * L.pld; e += kCT) {
         const int k = e / L.pld, c = e - k * L.pld;
-        Cs[e] = (c < D.r) ? coef[c * D.rc + k] : 0.f;
+        Cs[e] = (k < KW && c < D.r) ? coef[c * D.rc + k] : 0.f;
       }
     }
     named_sync(kBarAll, kCT);
@@ -647,9 +787,8 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
         dead = !agree(kBarTeam0 + team, kTT, w);
         if (!dead) {
           const unsigned char* stage = smem + s * L.stage_bytes;
-          const float* Ks = reinterpret_cast<const float*>(stage + L.off[3]);
-          mm_rows<true>(Ks, L.pitch[3] / 4, 1, Cs, L.pld, nv, KW, r, tt, kTT,
-                        [&](int v, int c, float x) { zs[v * L.zp + c] = x * eps; });
+          mm_rows_sw(stage + L.off[3], L.TV, Cs, L.pld, nv, K4, r, tt, kTT,
+                     [&](int v, int c, float x) { zs[v * L.zp + c] = x * eps; });
           named_sync(kBarTeam0 + team, kTT);
           const int n = nv * r;
           const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
@@ -661,6 +800,41 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
           const void* ps = stage + L.off[0];
           const float* ms = reinterpret_cast<const float*>(stage + L.off[1]);
           const float* vsg = reinterpret_cast<const float*>(stage + L.off[2]);
+          // four elements per step along the contiguous direction when rows and pointers
+          // allow vector accesses; element by element otherwise
+          const bool vec = cs == 1 && (ld & 3) == 0 && ((M.side == 0 ? r : nv) & 3) == 0 && aligned_to(zt, 16) &&
+                           aligned_to(post, 4 * FES) && aligned_to(negt, 4 * FES);
+          auto body4 = [&](auto side_tag) {
+            constexpr int SIDE = decltype(side_tag)::value;
+            Walk4<SIDE> w(tt, kTT, r, nv);
+            const int n4 = n / 4;
+            for (int e = tt; e < n4; e += kTT, w.next()) {
+              const int v = w.v(), k = w.k();
+              float z[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) z[q] = SIDE == 0 ? zs[v * L.zp + k + q] : zs[(v + q) * L.zp + k];
+              const int g = SIDE == 0 ? v * ld + k : k * ld + v;
+              *reinterpret_cast<float4*>(zt + g) = make_float4(z[0], z[1], z[2], z[3]);
+              if (MODE == 0) {
+                const int so = SIDE == 0 ? v * r + k : k * L.TV + v;
+                const float4 p4 = ld_fac4<FES>(ps, so);
+                const float4 m4 = *reinterpret_cast<const float4*>(ms + so);
+                const float4 w4 = *reinterpret_cast<const float4*>(vsg + so);
+                st_fac4<FES>(post, g, make_float4(__fadd_rn(p4.x, z[0]), __fadd_rn(p4.y, z[1]), __fadd_rn(p4.z, z[2]),
+                                                  __fadd_rn(p4.w, z[3])));
+                st_fac4<FES>(negt, g, make_float4(__fsub_rn(p4.x, z[0]), __fsub_rn(p4.y, z[1]), __fsub_rn(p4.z, z[2]),
+                                                  __fsub_rn(p4.w, z[3])));
+                const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float mu1 = __fmul_rn(mv[q], kin.beta);
+                  const float var1 = __fadd_rn(__fmul_rn(wv[q], kin.beta2), kin.q);
+                  s_zmu = fmaf(z[q], mu1, s_zmu);
+                  s_zzv = fmaf(__fmul_rn(z[q], z[q]), var1, s_zzv);
+                }
+              }
+            }
+          };
           auto body = [&](auto side_tag) {
             constexpr int SIDE = decltype(side_tag)::value;
             Walk<SIDE> w(tt, kTT, r, nv);
@@ -682,8 +856,13 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
               }
             }
           };
-          if (M.side == 0) body(std::integral_constant<int, 0>{});
-          else body(std::integral_constant<int, 1>{});
+          if (vec) {
+            if (M.side == 0) body4(std::integral_constant<int, 0>{});
+            else body4(std::integral_constant<int, 1>{});
+          } else {
+            if (M.side == 0) body(std::integral_constant<int, 0>{});
+            else body(std::integral_constant<int, 1>{});
+          }
           __syncwarp();
           if ((tt & 31) == 0) mbar_arrive(empty + s);
           named_sync(kBarTeam0 + team, kTT);          // zs is rewritten by the team's next tile
@@ -741,6 +920,10 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
       Src a[2];
       a[0] = make_src(M.param, M, fes, tb, 0);
       a[1] = make_src(M.mu, M, 4, tb, 1);
+      if (M.side == 0) {                        // mu rows as the swizzled row image
+        a[1].swz = 1;
+        a[1].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
+      }
       const int off[2] = {L.off[0], L.off[1]};
       const int pitch[2] = {side_pitch(M.side, static_cast<int>(M.r), L.TV, fes),
                             M.side == 0 ? L.pitch[1] : L.TV * 4};
@@ -763,15 +946,14 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
     if (it.mi != cur) {
       named_sync(kBarAll, kCT);
       const float* Pm = reinterpret_cast<const float*>(tb.ws) + M.p_off;
-      for (int e = ct; e < r * L.pld; e += kCT) {
+      for (int e = ct; e < ((r + 3) & ~3) * L.pld; e += kCT) {   // rows past r are zero
         const int a = e / L.pld, c = e - a * L.pld;
-        Ps[e] = (c < r) ? Pm[a * r + c] : 0.f;
+        Ps[e] = (a < r && c < r) ? Pm[a * r + c] : 0.f;
       }
       named_sync(kBarAll, kCT);
       cur = it.mi;
     }
-    const int vs = (M.side == 0) ? L.pitch[1] / 4 : 1;
-    const int as = (M.side == 0) ? 1 : L.TV;
+    const int as = L.TV;                        // side 1: mu dense along the tile
     int adv;
     do {
       const int nv = it.nv();
@@ -781,15 +963,37 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
         dead = !agree(kBarTeam0 + team, kTT, w);
         if (!dead) {
           const unsigned char* stage = smem + s * L.stage_bytes;
-          const float* Xs = reinterpret_cast<const float*>(stage + L.off[1]);
-          if (M.side == 0) mm_rows<true>(Xs, vs, 1, Ps, L.pld, nv, r, r, tt, kTT, [&](int v, int c, float x) { os[v * L.zp + c] = x; });
-          else mm_rows<false>(Xs, 1, as, Ps, L.pld, nv, r, r, tt, kTT, [&](int v, int c, float x) { os[v * L.zp + c] = x; });
+          if (M.side == 0) {
+            mm_rows_sw(stage + L.off[1], L.TV, Ps, L.pld, nv, (r + 3) & ~3, r, tt, kTT,
+                       [&](int v, int c, float x) { os[v * L.zp + c] = x; });
+          } else {
+            const float* Xs = reinterpret_cast<const float*>(stage + L.off[1]);
+            mm_rows<false>(Xs, 1, as, Ps, L.pld, nv, r, r, tt, kTT, [&](int v, int c, float x) { os[v * L.zp + c] = x; });
+          }
           named_sync(kBarTeam0 + team, kTT);
           const int n = nv * r;
           const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
           void* pt = tile_ptr(reinterpret_cast<char*>(M.param), M, it.s0, FES);
           float* sct = M.scratch ? tile_ptr(M.scratch, M, it.s0, 4) : nullptr;
           const void* ps = stage + L.off[0];
+          const bool vec = cs == 1 && (ld & 3) == 0 && ((M.side == 0 ? r : nv) & 3) == 0 && aligned_to(pt, 4 * FES) &&
+                           aligned_to(sct, 16);
+          auto body4 = [&](auto side_tag) {             // four elements per step
+            constexpr int SIDE = decltype(side_tag)::value;
+            Walk4<SIDE> w(tt, kTT, r, nv);
+            const int n4 = n / 4;
+            for (int e = tt; e < n4; e += kTT, w.next()) {
+              const int v = w.v(), k = w.k();
+              float X[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) X[q] = SIDE == 0 ? os[v * L.zp + k + q] : os[(v + q) * L.zp + k];
+              const float4 p4 = ld_fac4<FES>(ps, SIDE == 0 ? v * r + k : k * L.TV + v);
+              const int g = SIDE == 0 ? v * ld + k : k * ld + v;
+              st_fac4<FES>(pt, g, make_float4(__fsub_rn(p4.x, __fmul_rn(eta, X[0])), __fsub_rn(p4.y, __fmul_rn(eta, X[1])),
+                                              __fsub_rn(p4.z, __fmul_rn(eta, X[2])), __fsub_rn(p4.w, __fmul_rn(eta, X[3]))));
+              if (sct) *reinterpret_cast<float4*>(sct + g) = make_float4(X[0], X[1], X[2], X[3]);
+            }
+          };
           auto body = [&](auto side_tag) {
             constexpr int SIDE = decltype(side_tag)::value;
             Walk<SIDE> w(tt, kTT, r, nv);
@@ -801,8 +1005,13 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
               if (sct) sct[g] = X;
             }
           };
-          if (M.side == 0) body(std::integral_constant<int, 0>{});
-          else body(std::integral_constant<int, 1>{});
+          if (vec) {
+            if (M.side == 0) body4(std::integral_constant<int, 0>{});
+            else body4(std::integral_constant<int, 1>{});
+          } else {
+            if (M.side == 0) body(std::integral_constant<int, 0>{});
+            else body(std::integral_constant<int, 1>{});
+          }
           __syncwarp();
           if ((tt & 31) == 0) mbar_arrive(empty + s);
           named_sync(kBarTeam0 + team, kTT);
@@ -866,10 +1075,6 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
   uint64_t* empty = full + L.S;
   double* Ps = reinterpret_cast<double*>(smem + L.o_c);        // rp x pld fp64 R^{-1}
   const int osz = (L.o_bar - L.o_z) / 16;                       // floats per fp32 tile (four)
-  {                                                             // stage columns r .. mp-1 stay zero
-    uint4* z = reinterpret_cast<uint4*>(smem);
-    for (int e = threadIdx.x; e < L.fixed0 / 16; e += kST) z[e] = make_uint4(0u, 0u, 0u, 0u);
-  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < L.S; ++i) { mbar_init(full + i, kFullArrivals); mbar_init(empty + i, kQrGroupWarps); }
     mbar_init_fence();
@@ -884,6 +1089,8 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
       const MatD& M = t.mats[t.mi];
       Src a[1];
       a[0] = make_src(M.mu, M, 4, tb, 1);
+      a[0].swz = 1;                                 // W rows as the swizzled row image
+      a[0].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
       produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln);
@@ -895,7 +1102,7 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
   const int grp = mw / kQrGroupWarps, gw = mw - grp * kQrGroupWarps;
   const int ct = threadIdx.x - 32, gt = ct - grp * 32 * kQrGroupWarps;
   const int g = lane >> 2, kq = lane & 3;
-  const int wp = L.pitch[0] / 4;
+  const int boxb = L.TV * 128;
   const int WV = ((L.TV + 7) / 8 + MV - 1) / MV;
   const int wv = gw % WV, wc = gw / WV;
   int i = 0, jt = 0;
@@ -921,7 +1128,7 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
       const bool w = dead ? false : mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
       dead = !agree(kBarTeam0 + grp, 32 * kQrGroupWarps, w);
       if (!dead) {
-        const float* Ws = reinterpret_cast<const float*>(smem + s * L.stage_bytes);
+        const unsigned char* Ws = smem + s * L.stage_bytes;   // swizzled row image of W
         const int nvb = (nv + 7) >> 3, ncb = (r + 7) >> 3;
         const int WC = (ncb + MC - 1) / MC;
         int rv[MV], cc[MC], kb[MC];
@@ -940,10 +1147,12 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
         for (int jv = 0; jv < MV; ++jv)
 #pragma unroll
           for (int jc = 0; jc < MC; ++jc) { acc[jv][jc][0] = 0.0; acc[jv][jc][1] = 0.0; }
-        const float* xa[MV];
+        // A fragment (row 8 rv + g, column k0 + kq): row start + chunk ((k0 / 4) % 8) ^ g
+        // (the row's swizzle is g) of box k0 / 32
+        const unsigned char* xa[MV];
         const double* pb[MC];
 #pragma unroll
-        for (int jv = 0; jv < MV; ++jv) xa[jv] = Ws + (8 * (rok[jv] ? rv[jv] : 0) + g) * wp + kq;
+        for (int jv = 0; jv < MV; ++jv) xa[jv] = Ws + (8 * (rok[jv] ? rv[jv] : 0) + g) * 128 + kq * 4;
 #pragma unroll
         for (int jc = 0; jc < MC; ++jc) pb[jc] = Ps + kq * L.pld + 8 * cc[jc] + g;
         const int pstep = 4 * L.pld;
@@ -952,8 +1161,9 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
         for (int j0 = 0; j0 < MC; ++j0) {           // blocks j0 .. MC-1 active for k < kb[j0]
           for (; k0 < kb[j0]; k0 += 4) {
             double av[MV];
+            const int xo = (k0 >> 5) * boxb + ((((k0 >> 2) & 7) ^ g) << 4);
 #pragma unroll
-            for (int jv = 0; jv < MV; ++jv) av[jv] = static_cast<double>(xa[jv][k0]);
+            for (int jv = 0; jv < MV; ++jv) av[jv] = static_cast<double>(*reinterpret_cast<const float*>(xa[jv] + xo));
             const int po = (k0 >> 2) * pstep;
 #pragma unroll
             for (int jc = j0; jc < MC; ++jc) {
