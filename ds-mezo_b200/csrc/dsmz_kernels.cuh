@@ -661,11 +661,33 @@ __global__ void __launch_bounds__(kThreads) k_apply(Tables tb, const MatD* __res
 // =====================================================================================
 // B-side reductions per (module, chunk of d_in): B V and var_B (V*V), both R x RC
 // (ds_mezo/kernels.py:325-326 and controller.py:183). Partials summed by k_coef.
+// 64 x 64 output blocks; a thread holds 4 x 4 of each product. The chunk is walked 32
+// columns of d_in at a time: the next 32 columns' global loads are in flight while the
+// current ones are multiplied, and the shared tiles are stored transposed (j-major, V*V
+// formed once per element) so that a thread's four rows or four columns are one 16-byte
+// load: per j, four 16-byte loads feed 32 FMAs.
 // =====================================================================================
-__global__ void __launch_bounds__(kThreads) k_bside(Tables tb) {
-  __shared__ float Bs[64][33];
-  __shared__ float Ws[64][33];
-  __shared__ float Vs[32][65];
+constexpr int kBsJ = 32, kBsP = 68;
+// Read-only loads with a 256-byte L2 fill: a CTA walks each row 32 columns at a time, so
+// the next steps' columns are already in L2.
+__device__ __forceinline__ float ldg_l2pf(const float* p) {
+  float v;
+  asm("ld.global.nc.L2::256B.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ldg_l2pf(const void* p, int64_t i, int dt) {
+  if (dt == DSMZ_BF16) {
+    unsigned short u;
+    asm("ld.global.nc.L2::256B.u16 %0, [%1];" : "=h"(u) : "l"(reinterpret_cast<const __nv_bfloat16*>(p) + i));
+    return __bfloat162float(__ushort_as_bfloat16(u));
+  }
+  return ldg_l2pf(reinterpret_cast<const float*>(p) + i);
+}
+__global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb) {
+  __shared__ __align__(16) float Bs[kBsJ][kBsP];
+  __shared__ __align__(16) float Ws[kBsJ][kBsP];
+  __shared__ __align__(16) float Vs[kBsJ][kBsP];
+  __shared__ __align__(16) float Qs[kBsJ][kBsP];
   const int item = blockIdx.x;
   const int mi = find_owner(tb.mods, tb.nmods, item, [](const ModD& d) { return d.chunk0; });
   const ModD D = tb.mods[mi];
@@ -686,43 +708,57 @@ __global__ void __launch_bounds__(kThreads) k_bside(Tables tb) {
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) { abv[i][j] = 0.f; avb[i][j] = 0.f; }
-      for (int64_t jb = j0; jb < j1; jb += 32) {
-        float lb[8], lw[8], lv[8];
+      float lb[8], lw[8], lv[8];
+      auto gload = [&](int64_t jb) {                // 24 independent loads per thread
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {                 // 24 independent loads in flight
+        for (int u = 0; u < 8; ++u) {
           const int e = tid + u * kThreads;
           const int rr = e >> 5, jj = e & 31;
           const int64_t j = jb + jj;
           const bool ok = (rt + rr < R) && (j < j1);
           const int64_t a = static_cast<int64_t>(rt + rr) * D.b_s0 + j * D.b_s1;
-          lb[u] = ok ? ldf(D.Bp, a, D.bdt) : 0.f;
-          lw[u] = (ok && with_var) ? D.varB[a] : 0.f;
+          // out-of-range elements load element 0 (always valid) and are replaced by zero
+          const int64_t ac = ok ? a : 0;
+          const float b0 = ldg_l2pf(D.Bp, ac, D.bdt);
+          const float w0 = with_var ? ldg_l2pf(D.varB + ac) : 0.f;
+          lb[u] = ok ? b0 : 0.f;
+          lw[u] = ok ? w0 : 0.f;
           const int jv = e >> 6, cc = e & 63;
           const int64_t jv_g = jb + jv;
-          lv[u] = (jv_g < j1 && ct + cc < RC) ? V[jv_g * vs0 + static_cast<int64_t>(ct + cc) * vs1] : 0.f;
+          const bool vok = jv_g < j1 && ct + cc < RC;
+          const float v0 = ldg_l2pf(V + (vok ? jv_g * vs0 + static_cast<int64_t>(ct + cc) * vs1 : 0));
+          lv[u] = vok ? v0 : 0.f;
         }
+      };
+      gload(j0);
+      for (int64_t jb = j0; jb < j1; jb += kBsJ) {
+        __syncthreads();                            // the previous columns are consumed
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int e = tid + u * kThreads;
-          Bs[e >> 5][e & 31] = lb[u];
-          Ws[e >> 5][e & 31] = lw[u];
+          Bs[e & 31][e >> 5] = lb[u];
+          Ws[e & 31][e >> 5] = lw[u];
           Vs[e >> 6][e & 63] = lv[u];
+          Qs[e >> 6][e & 63] = lv[u] * lv[u];
         }
         __syncthreads();
+        if (jb + kBsJ < j1) gload(jb + kBsJ);
 #pragma unroll 4
-        for (int jj = 0; jj < 32; ++jj) {
-          float b[4], w[4], v[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) { b[i] = Bs[ti * 4 + i][jj]; w[i] = Ws[ti * 4 + i][jj]; v[i] = Vs[jj][tj * 4 + i]; }
+        for (int jj = 0; jj < kBsJ; ++jj) {
+          const float4 b = *reinterpret_cast<const float4*>(&Bs[jj][ti * 4]);
+          const float4 w = *reinterpret_cast<const float4*>(&Ws[jj][ti * 4]);
+          const float4 v = *reinterpret_cast<const float4*>(&Vs[jj][tj * 4]);
+          const float4 q = *reinterpret_cast<const float4*>(&Qs[jj][tj * 4]);
+          const float bb[4] = {b.x, b.y, b.z, b.w}, ww[4] = {w.x, w.y, w.z, w.w};
+          const float vv[4] = {v.x, v.y, v.z, v.w}, qq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              abv[i][j] = fmaf(b[i], v[j], abv[i][j]);
-              avb[i][j] = fmaf(w[i], v[j] * v[j], avb[i][j]);
+              abv[i][j] = fmaf(bb[i], vv[j], abv[i][j]);
+              avb[i][j] = fmaf(ww[i], qq[j], avb[i][j]);
             }
         }
-        __syncthreads();
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -734,6 +770,7 @@ __global__ void __launch_bounds__(kThreads) k_bside(Tables tb) {
             outp[R * RC + rr * RC + cc] = avb[i][j];
           }
         }
+      __syncthreads();                              // the tiles are rewritten by the next block
     }
   }
 }

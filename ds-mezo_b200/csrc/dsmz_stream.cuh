@@ -167,7 +167,7 @@ __device__ __forceinline__ void swz_plain_copy(const Src& a, int64_t s0, int nv,
 constexpr int kFullArrivals = 33;
 template <int NA>
 __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA], const int (&pitch)[NA],
-                                        int64_t s0, int nv, char* stage, uint64_t* full, int lane) {
+                                        int64_t s0, int nv, char* stage, uint64_t* full, int lane, bool acquire) {
   int mode[NA];
   uint32_t tx = 0;
 #pragma unroll
@@ -194,12 +194,12 @@ __device__ __forceinline__ void produce(const Src (&a)[NA], const int (&off)[NA]
       copy16_issue(a[i], s0, nv, stage + off[i], pitch[i], lane);
     } else if (mode[i] == kCopyTensor) {
       if (lane == 0) {
-        tmap_acquire(a[i].map);
+        if (acquire) tmap_acquire(a[i].map);       // once per matrix (maps are fixed per launch)
         tma_load_2d(stage + off[i], a[i].map, static_cast<int>(s0), 0, full);
       }
     } else if (mode[i] == kCopySwzTma) {
       if (lane == 0) {
-        tmap_acquire(a[i].map);
+        if (acquire) tmap_acquire(a[i].map);
         for (int b = 0; b < swz_boxes(a[i].r); ++b)
           tma_load_2d(stage + off[i] + b * pitch[i], a[i].map, 32 * b, static_cast<int>(s0), full);
       }
@@ -230,6 +230,7 @@ struct TileIt {
   int t, t1;            // current global tile, end of the chunk
   int mi, seg;
   int64_t s0, nvec;     // first vector of the tile, vectors of the matrix
+  bool fresh;           // the tile is the first of its segment
   __device__ void init(const MatD* m, int n, int tv) {
     mats = m; nmats = n; TV = tv;
     const int64_t T = static_cast<int64_t>(m[n - 1].tile0) + m[n - 1].ntile;
@@ -247,6 +248,7 @@ struct TileIt {
     mi = find_owner(mats, nmats, t, [](const MatD& m) { return m.tile0; });
     load();
     s0 = static_cast<int64_t>(t - mats[mi].tile0) * TV;
+    fresh = true;
     return true;
   }
   __device__ int nv() const { return static_cast<int>(min(static_cast<int64_t>(TV), nvec - s0)); }
@@ -254,7 +256,8 @@ struct TileIt {
   __device__ int next() {
     if (++t >= t1) return 0;
     s0 += TV;
-    if (s0 < nvec) return 1;
+    fresh = s0 >= nvec;
+    if (!fresh) return 1;
     ++mi;
     s0 = 0;
     load();
@@ -742,7 +745,7 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
       const int off[4] = {L.off[0], L.off[1], L.off[2], L.off[3]};
       const int pitch[4] = {side_pitch(M.side, r, L.TV, fes), side_pitch(M.side, r, L.TV, 4),
                             side_pitch(M.side, r, L.TV, 4), L.pitch[3]};
-      produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+      produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
     });
     return;
   }
@@ -927,7 +930,7 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
       const int off[2] = {L.off[0], L.off[1]};
       const int pitch[2] = {side_pitch(M.side, static_cast<int>(M.r), L.TV, fes),
                             M.side == 0 ? L.pitch[1] : L.TV * 4};
-      produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane);
+      produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
     });
     return;
   }
@@ -1093,7 +1096,7 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
       a[0].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
-      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln);
+      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
     });
     return;
   }
@@ -1291,7 +1294,7 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
       const int sp = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
       const int off[3] = {L.off[0], L.off[1], L.off[2]};
       const int pitch[3] = {sp, sp, sp};
-      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln);
+      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
     });
     return;
   }
