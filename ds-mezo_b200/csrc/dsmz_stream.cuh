@@ -720,11 +720,13 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
   (void)seed; (void)base_off;
 
   if (warp == 0) {
+    Src a[4];                                   // the segment's copy sources, built at its first tile
+    int pitch[4];
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
+      if (t.fresh) {
       const MatD& M = t.mats[t.mi];
       const ModD& D = tb.mods[M.owner];
       const int r = static_cast<int>(M.r);
-      Src a[4];
       a[0] = make_src(MODE == 0 ? M.param : nullptr, M, fes, tb, 0);
       a[1] = make_src(MODE == 0 ? M.mu : nullptr, M, 4, tb, 1);
       a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4, tb, 2);
@@ -742,9 +744,11 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
         k.ld = Bd.v_s0; k.cs = Bd.v_s1; k.r = D.rc;
       }
       a[3] = k;
+      pitch[0] = side_pitch(M.side, r, L.TV, fes);
+      pitch[1] = pitch[2] = side_pitch(M.side, r, L.TV, 4);
+      pitch[3] = L.pitch[3];
+      }
       const int off[4] = {L.off[0], L.off[1], L.off[2], L.off[3]};
-      const int pitch[4] = {side_pitch(M.side, r, L.TV, fes), side_pitch(M.side, r, L.TV, 4),
-                            side_pitch(M.side, r, L.TV, 4), L.pitch[3]};
       produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
     });
     return;
@@ -918,18 +922,21 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
   constexpr int fes = FES;
 
   if (warp == 0) {
+    Src a[2];                                   // the segment's copy sources, built at its first tile
+    int pitch[2];
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
-      const MatD& M = t.mats[t.mi];
-      Src a[2];
-      a[0] = make_src(M.param, M, fes, tb, 0);
-      a[1] = make_src(M.mu, M, 4, tb, 1);
-      if (M.side == 0) {                        // mu rows as the swizzled row image
-        a[1].swz = 1;
-        a[1].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
+      if (t.fresh) {
+        const MatD& M = t.mats[t.mi];
+        a[0] = make_src(M.param, M, fes, tb, 0);
+        a[1] = make_src(M.mu, M, 4, tb, 1);
+        if (M.side == 0) {                      // mu rows as the swizzled row image
+          a[1].swz = 1;
+          a[1].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
+        }
+        pitch[0] = side_pitch(M.side, static_cast<int>(M.r), L.TV, fes);
+        pitch[1] = M.side == 0 ? L.pitch[1] : L.TV * 4;
       }
       const int off[2] = {L.off[0], L.off[1]};
-      const int pitch[2] = {side_pitch(M.side, static_cast<int>(M.r), L.TV, fes),
-                            M.side == 0 ? L.pitch[1] : L.TV * 4};
       produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
     });
     return;
@@ -1088,12 +1095,14 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == 0) {
+    Src a[1];                                       // the segment's copy source, built at its first tile
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
-      const MatD& M = t.mats[t.mi];
-      Src a[1];
-      a[0] = make_src(M.mu, M, 4, tb, 1);
-      a[0].swz = 1;                                 // W rows as the swizzled row image
-      a[0].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
+      if (t.fresh) {
+        const MatD& M = t.mats[t.mi];
+        a[0] = make_src(M.mu, M, 4, tb, 1);
+        a[0].swz = 1;                               // W rows as the swizzled row image
+        a[0].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
+      }
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
       produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
@@ -1285,15 +1294,17 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == 0) {
+    Src a[3];                                       // the segment's copy sources, built at its first tile
+    int pitch[3];
     producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
-      const MatD& M = t.mats[t.mi];
-      Src a[3];
-      a[0] = make_src(M.mu, M, 4, tb, 1);
-      a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4, tb, 2);
-      a[2] = make_src(SRC == 1 ? M.z : nullptr, M, 4, tb, 3);
-      const int sp = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
+      if (t.fresh) {
+        const MatD& M = t.mats[t.mi];
+        a[0] = make_src(M.mu, M, 4, tb, 1);
+        a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4, tb, 2);
+        a[2] = make_src(SRC == 1 ? M.z : nullptr, M, 4, tb, 3);
+        pitch[0] = pitch[1] = pitch[2] = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
+      }
       const int off[3] = {L.off[0], L.off[1], L.off[2]};
-      const int pitch[3] = {sp, sp, sp};
       produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
     });
     return;
