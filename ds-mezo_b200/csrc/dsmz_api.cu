@@ -609,10 +609,10 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
     switch (sk::qr_variant(P->Lq.TV, P->R)) {
-      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kST, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
     }
     P->probe_end(DSMZ_KID_PI_APPLY, s);
     DSMZ_LAUNCHED("power iteration V = W R^-1");
@@ -651,9 +651,9 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
   if (P->factor_dtype == DSMZ_BF16)
-    sk::k_sapply<2><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   else
-    sk::k_sapply<4><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;
@@ -697,8 +697,8 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
     P->probe_end(DSMZ_KID_COEF, s);
     DSMZ_LAUNCHED("AGZO coefficients");
     P->probe_begin(DSMZ_KID_PERTURB, s);
-    if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kST, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
-    else sk::k_sperturb<0, 4><<<P->grid_m, sk::kST, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    else sk::k_sperturb<0, 4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
     P->probe_end(DSMZ_KID_PERTURB, s);
     DSMZ_LAUNCHED("perturbation");
     P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
@@ -733,9 +733,9 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
   if (P->factor_dtype == DSMZ_BF16)
-    sk::k_sapply<2><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   else
-    sk::k_sapply<4><<<P->grid_m, sk::kST, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;

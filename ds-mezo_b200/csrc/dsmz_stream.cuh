@@ -30,6 +30,11 @@ namespace sk {
 constexpr int kCW = 8;                   // consumer warps
 constexpr int kCT = 32 * kCW;            // consumer threads
 constexpr int kST = kCT + 32;            // + producer warp 0
+// Team kernels and the QR apply: two producer warps (0 and 1) take alternate tiles. A TMA
+// issue costs a producer a few hundred cycles while the consumers keep the memory
+// instruction queue busy, and a tile needs up to five of them.
+constexpr int kProd = 2;
+constexpr int kSTP = kCT + 32 * kProd;
 constexpr int kTeams = 4;                // perturb / apply / QR apply
 // Tile i goes to team i % kTeams and ring stage i % S. With S a multiple of kTeams each
 // stage only ever holds one team's tiles, so the phase a team waits on directly follows the
@@ -627,30 +632,37 @@ __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
   return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
 }
 
-// Producer loop shared by every streaming kernel: walks the CTA's tiles, waits for the
-// stage to be free, fills it. `fill(it, stage, full, lane)` issues the copies.
-template <typename Fill>
+// Producer loop shared by every streaming kernel: NP producer warps (warps 0 .. NP-1) walk
+// the CTA's tiles; warp p fills the tiles i with i % NP == p (every stage then has one
+// producer: S is a multiple of NP). Waits for the stage to be free, then
+// `fill(it, stage, full, lane, fresh)` issues the copies; fresh: the first tile of a
+// matrix this warp fills (copy sources are rebuilt, tensor maps acquired).
+template <int NP, typename Fill>
 __device__ __forceinline__ void producer_loop(TileIt it, const Layout& L, unsigned char* smem, uint64_t* full,
                                               uint64_t* empty, int* err, Fill fill) {
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, pw = static_cast<int>(threadIdx.x >> 5);
   int i = 0;
-  bool ok = true;
+  int cur = -1;
   if (it.start_seg()) {
     while (true) {
-      const int s = i % L.S;
-      if (i >= L.S) {
-        const bool w = mbar_wait(empty + s, (static_cast<uint32_t>(i / L.S) & 1u) ^ 1u, err);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      if (i % NP == pw) {
+        const int s = i % L.S;
+        if (i >= L.S) {
+          const bool w = mbar_wait(empty + s, (static_cast<uint32_t>(i / L.S) & 1u) ^ 1u, err);
+          if (!__all_sync(0xffffffffu, w)) break;
+        }
+        const bool fresh = it.mi != cur;
+        cur = it.mi;
+        fill(it, smem + s * L.stage_bytes, full + s, lane, fresh);
       }
-      fill(it, smem + s * L.stage_bytes, full + s, lane);
       ++i;
       if (it.next() == 0) break;
     }
   }
-  (void)ok;
   // the copies already issued land before the CTA can exit, whatever the consumers did
-  if (threadIdx.x == 0)
-    for (int j = (i > L.S ? i - L.S : 0); j < i; ++j) mbar_drain(full + (j % L.S), static_cast<uint32_t>(j / L.S) & 1u);
+  if (lane == 0)
+    for (int j = (i > L.S ? i - L.S : 0); j < i; ++j)
+      if (j % NP == pw) mbar_drain(full + (j % L.S), static_cast<uint32_t>(j / L.S) & 1u);
 }
 
 __device__ __forceinline__ void init_bars(uint64_t* full, uint64_t* empty, int S, int empty_count) {
@@ -706,7 +718,7 @@ __global__ void __launch_bounds__(256) k_draw_zca(Tables tb, uint64_t seed, uint
 // MODE 1 (drop-in op): z only, Zc_A from the caller.
 // =====================================================================================
 template <int MODE, int FES>
-__global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64_t seed, uint64_t base_off, float eps,
+__global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint64_t seed, uint64_t base_off, float eps,
                                                      KalmanIn kin, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
@@ -719,11 +731,11 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
   constexpr int fes = FES;
   (void)seed; (void)base_off;
 
-  if (warp == 0) {
+  if (warp < kProd) {
     Src a[4];                                   // the segment's copy sources, built at its first tile
     int pitch[4];
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
-      if (t.fresh) {
+    producer_loop<kProd>(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane, bool fresh) {
+      if (fresh) {
       const MatD& M = t.mats[t.mi];
       const ModD& D = tb.mods[M.owner];
       const int r = static_cast<int>(M.r);
@@ -749,12 +761,12 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
       pitch[3] = L.pitch[3];
       }
       const int off[4] = {L.off[0], L.off[1], L.off[2], L.off[3]};
-      produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
+      produce<4>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, fresh);
     });
     return;
   }
 
-  const int ct = threadIdx.x - 32;
+  const int ct = threadIdx.x - 32 * kProd;
   const int team = ct / kTT, tt = ct - team * kTT;
   float* Cs = reinterpret_cast<float*>(smem + L.o_c);
   float* zs = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
@@ -909,7 +921,7 @@ __global__ void __launch_bounds__(kST, 1) k_sperturb(Tables tb, Layout L, uint64
 // optional scratch = X.
 // =====================================================================================
 template <int FES>
-__global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
+__global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
                                                    Layout L, float eta, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
@@ -921,11 +933,11 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
   const int warp = threadIdx.x >> 5;
   constexpr int fes = FES;
 
-  if (warp == 0) {
+  if (warp < kProd) {
     Src a[2];                                   // the segment's copy sources, built at its first tile
     int pitch[2];
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane) {
-      if (t.fresh) {
+    producer_loop<kProd>(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane, bool fresh) {
+      if (fresh) {
         const MatD& M = t.mats[t.mi];
         a[0] = make_src(M.param, M, fes, tb, 0);
         a[1] = make_src(M.mu, M, 4, tb, 1);
@@ -937,12 +949,12 @@ __global__ void __launch_bounds__(kST, 1) k_sapply(Tables tb, const MatD* __rest
         pitch[1] = M.side == 0 ? L.pitch[1] : L.TV * 4;
       }
       const int off[2] = {L.off[0], L.off[1]};
-      produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, t.fresh);
+      produce<2>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, lane, fresh);
     });
     return;
   }
 
-  const int ct = threadIdx.x - 32;
+  const int ct = threadIdx.x - 32 * kProd;
   const int team = ct / kTT, tt = ct - team * kTT;
   float* Ps = reinterpret_cast<float*>(smem + L.o_c);
   float* os = reinterpret_cast<float*>(smem + L.o_z + team * al128(L.TV * L.zp * 4));
@@ -1077,7 +1089,7 @@ __device__ __forceinline__ void bf16_pair8(const float* x, uint4& hi, uint4& lo)
 }
 
 template <int MV, int MC>
-__global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
+__global__ void __launch_bounds__(kSTP, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
                                                       int nsegs, Layout L, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
@@ -1094,10 +1106,10 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
   it.init(mats, nmats, L.TV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (warp == 0) {
+  if (warp < kProd) {
     Src a[1];                                       // the segment's copy source, built at its first tile
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
-      if (t.fresh) {
+    producer_loop<kProd>(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln, bool fresh) {
+      if (fresh) {
         const MatD& M = t.mats[t.mi];
         a[0] = make_src(M.mu, M, 4, tb, 1);
         a[0].swz = 1;                               // W rows as the swizzled row image
@@ -1105,14 +1117,14 @@ __global__ void __launch_bounds__(kST, 1) k_sqr_apply(Tables tb, const MatD* __r
       }
       const int off[1] = {0};
       const int pitch[1] = {L.pitch[0]};
-      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
+      produce<1>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, fresh);
     });
     return;
   }
 
-  const int mw = warp - 1;
+  const int mw = warp - kProd;
   const int grp = mw / kQrGroupWarps, gw = mw - grp * kQrGroupWarps;
-  const int ct = threadIdx.x - 32, gt = ct - grp * 32 * kQrGroupWarps;
+  const int ct = threadIdx.x - 32 * kProd, gt = ct - grp * 32 * kQrGroupWarps;
   const int g = lane >> 2, kq = lane & 3;
   const int boxb = L.TV * 128;
   const int WV = ((L.TV + 7) / 8 + MV - 1) / MV;
@@ -1296,8 +1308,8 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
   if (warp == 0) {
     Src a[3];                                       // the segment's copy sources, built at its first tile
     int pitch[3];
-    producer_loop(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln) {
-      if (t.fresh) {
+    producer_loop<1>(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int ln, bool fresh) {
+      if (fresh) {
         const MatD& M = t.mats[t.mi];
         a[0] = make_src(M.mu, M, 4, tb, 1);
         a[1] = make_src(SRC == 1 ? M.var : nullptr, M, 4, tb, 2);
@@ -1305,7 +1317,7 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
         pitch[0] = pitch[1] = pitch[2] = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
       }
       const int off[3] = {L.off[0], L.off[1], L.off[2]};
-      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, t.fresh);
+      produce<3>(a, off, pitch, t.s0, t.nv(), reinterpret_cast<char*>(stage), fb, ln, fresh);
     });
     return;
   }
