@@ -1386,8 +1386,53 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
             }
           }
         };
-        if (M.side == 0) body(std::integral_constant<int, 0>{});
-        else body(std::integral_constant<int, 1>{});
+        // four consecutive elements per step along the contiguous direction when rows and
+        // pointers allow 16-byte accesses (fp64 tile: two 16-byte stores)
+        const bool vec = cs == 1 && (ld & 3) == 0 && ((M.side == 0 ? r : nv) & 3) == 0 &&
+                         (SRC == 0 || (aligned_to(mut, 16) && aligned_to(vat, 16)));
+        auto body4 = [&](auto side_tag) {
+          constexpr int SIDE = decltype(side_tag)::value;
+          Walk4<SIDE> wk(pt, npt, r, nv);
+          const int n4 = n / 4;
+          for (int e = pt; e < n4; e += npt, wk.next()) {
+            const int v = wk.v(), k = wk.k();
+            const int so = SIDE == 0 ? v * r + k : k * L.TV + v;
+            float4 x4 = *reinterpret_cast<const float4*>(mus + so);
+            if (SRC == 1) {
+              const float4 va4 = *reinterpret_cast<const float4*>(vas + so);
+              const float4 zz4 = *reinterpret_cast<const float4*>(zss + so);
+              const float xi[4] = {x4.x, x4.y, x4.z, x4.w}, vi[4] = {va4.x, va4.y, va4.z, va4.w};
+              const float zi[4] = {zz4.x, zz4.y, zz4.z, zz4.w};
+              float mo[4], vo[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float mu1, var1;
+                kal_predict(xi[q], vi[q], ks, mu1, var1);
+                kal_observe(mu1, var1, zi[q], ks, mo[q], vo[q]);
+              }
+              const int g = SIDE == 0 ? v * ld + k : k * ld + v;
+              *reinterpret_cast<float4*>(mut + g) = make_float4(mo[0], mo[1], mo[2], mo[3]);
+              *reinterpret_cast<float4*>(vat + g) = make_float4(vo[0], vo[1], vo[2], vo[3]);
+              x4 = make_float4(mo[0], mo[1], mo[2], mo[3]);
+            }
+            if (SIDE == 0) {
+              double2* xd = reinterpret_cast<double2*>(X + v * sv + k);
+              xd[0] = make_double2(x4.x, x4.y);
+              xd[1] = make_double2(x4.z, x4.w);
+            } else {
+              double2* xd = reinterpret_cast<double2*>(X + v + k * sc);
+              xd[0] = make_double2(x4.x, x4.y);
+              xd[1] = make_double2(x4.z, x4.w);
+            }
+          }
+        };
+        if (vec) {
+          if (M.side == 0) body4(std::integral_constant<int, 0>{});
+          else body4(std::integral_constant<int, 1>{});
+        } else {
+          if (M.side == 0) body(std::integral_constant<int, 0>{});
+          else body(std::integral_constant<int, 1>{});
+        }
         const int nv4 = (nv + 3) & ~3;                        // zero vectors nv .. nv4-1
         for (int e = pt; e < (nv4 - nv) * r; e += npt) {
           const int v = nv + e / r, c = e - (e / r) * r;
