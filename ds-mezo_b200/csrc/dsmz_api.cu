@@ -76,7 +76,7 @@ size_t coef_smem(int R, int RC) {
   const size_t rca = static_cast<size_t>(R < RC ? R : RC);
   return (static_cast<size_t>(R + 1) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
 }
-size_t ns_smem(int r) { return r <= 64 ? 4 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
+size_t ns_smem(int r) { return r <= 64 ? 3 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
 // Dynamic shared memory of a streaming-kernel CTA (one CTA per SM).
@@ -421,7 +421,7 @@ void plan_tc_layout(dsmz_plan* P) {
     c.T = b.T; c.D = b.D; c.R = b.R; c.ldv2 = t.ldv2; c.ldy2 = t.ldy2;
     c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + tc::kBM - 1) / tc::kBM); P->ntc_y += c.nytile;
     c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + tc::kBM - 1) / tc::kBM); P->ntc_w += c.nwtile;
-    c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D * b.R + kThreads * 8 - 1) / (kThreads * 8)); P->ntc_vt += c.nvt;
+    c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D + tc::kSplitD - 1) / tc::kSplitD); P->ntc_vt += c.nvt;
   }
 }
 

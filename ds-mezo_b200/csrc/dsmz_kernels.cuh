@@ -252,20 +252,23 @@ __global__ void __launch_bounds__(kThreads) k_gram(Tables tb, const MatD* __rest
 
 // C = A B for r x r fp64 matrices that are symmetric and commute (polynomials of one
 // Gram matrix), so C is symmetric: only the upper 8 x 8 blocks are formed, with the fp64
-// MMA (m8n8k4), four blocks per warp at a time, and mirrored. Pitch ld (= rp + 4: a warp's
-// fragment loads fall in two wavefronts); rows and columns r..rp-1 are zero and stay zero.
-// Every position is written by exactly one thread. Ends with a barrier.
-__device__ void cta_symm_mm(double* __restrict__ C, const double* __restrict__ A, const double* __restrict__ B,
-                            int rp, int ld) {
+// MMA (m8n8k4), and mirrored. Up to kSymmU blocks per warp per pass (one pass for r <= 64).
+// The products are held in registers across a barrier before C is written, so with one
+// pass (r <= 64) C may be A or B (in place); with several, C must be distinct. Pitch ld (= rp + 4: a warp's fragment loads fall in two wavefronts);
+// rows and columns r..rp-1 are zero and stay zero. Every position is written by exactly one
+// thread. Ends with a barrier.
+constexpr int kSymmU = 5;
+__device__ void cta_symm_mm(double* C, const double* A, const double* B, int rp, int ld) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  const int nw = kThreads / 32;
   const int nb = rp >> 3, nq = nb * (nb + 1) / 2;
-  for (int q0 = warp; q0 < nq; q0 += 4 * (kThreads / 32)) {
-    int bi[4], bj[4];
-    double acc[4][2];
+  for (int q0 = warp; q0 < ((nq + nw - 1) / nw + kSymmU - 1) / kSymmU * kSymmU * nw; q0 += kSymmU * nw) {
+    int bi[kSymmU], bj[kSymmU];
+    double acc[kSymmU][2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int q = q0 + u * (kThreads / 32);
+    for (int u = 0; u < kSymmU; ++u) {
+      int q = q0 + u * nw;
       bi[u] = -1; bj[u] = 0;
       acc[u][0] = 0.0; acc[u][1] = 0.0;
       if (q < nq) {
@@ -276,12 +279,13 @@ __device__ void cta_symm_mm(double* __restrict__ C, const double* __restrict__ A
     }
     for (int k0 = 0; k0 < rp; k0 += 4) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < kSymmU; ++u)
         if (bi[u] >= 0)
           dmma8x8x4(acc[u][0], acc[u][1], A[(8 * bi[u] + g) * ld + k0 + t], B[(k0 + t) * ld + 8 * bj[u] + g]);
     }
+    __syncthreads();                                   // every read of A and B is done
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kSymmU; ++u) {
       if (bi[u] < 0) continue;
       const int row = 8 * bi[u] + g;
 #pragma unroll
@@ -292,8 +296,8 @@ __device__ void cta_symm_mm(double* __restrict__ C, const double* __restrict__ A
         if (col != row) C[col * ld + row] = acc[u][h];
       }
     }
+    __syncthreads();
   }
-  __syncthreads();
 }
 
 __device__ double cta_sum(double v, double* red) {
@@ -325,7 +329,7 @@ __host__ __device__ inline int ns_ld(int r) { return pad8(r) + 4; }
 // matrix Pm with X[v,:] = x_v^T Pm for every vector x_v of the matrix (P is symmetric, so
 // tall and wide matrices use it alike).
 // =====================================================================================
-__global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
+__global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ double red[kThreads];
   const MatD M = mats[blockIdx.x];
@@ -333,21 +337,38 @@ __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __
   const int rr = r * r;
   const int rp = pad8(r), ld = ns_ld(r), mm = rp * ld;
   const int tid = threadIdx.x;
-  // r <= 64: the four matrices live in shared memory; larger r in the fp64 workspace
-  double* dw = (r <= 64) ? reinterpret_cast<double*>(smem_raw) : reinterpret_cast<double*>(tb.ws) + M.dw_off;
+  // r <= 64: three matrices in shared memory (two CTAs per SM), products in place (one
+  // pass of cta_symm_mm); larger r: four in the fp64 workspace, products out of place.
+  const bool small = r <= 64;
+  double* dw = small ? reinterpret_cast<double*>(smem_raw) : reinterpret_cast<double*>(tb.ws) + M.dw_off;
   double* G = dw;
   double* P = dw + mm;
   double* S = dw + 2 * mm;
   double* U = dw + 3 * mm;
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
-  for (int e = tid; e < 4 * mm; e += kThreads) dw[e] = 0.0;
+  for (int e = tid; e < (small ? 3 : 4) * mm; e += kThreads) dw[e] = 0.0;
   __syncthreads();
   double tr = 0.0;
-  for (int e = tid; e < rr; e += kThreads) {
-    const double v = strided_sum(part + e, M.nseg, rr);
-    const int a = e / r, b = e - a * r;
-    G[a * ld + b] = v;
-    if (a == b) tr += v;
+  constexpr int kSumU = 8;                             // independent partial loads in flight
+  for (int e0 = tid; e0 < rr; e0 += kSumU * kThreads) {
+    double v[kSumU];
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) v[u] = 0.0;
+    for (int sg = 0; sg < M.nseg; ++sg) {
+#pragma unroll
+      for (int u = 0; u < kSumU; ++u) {
+        const int e = e0 + u * kThreads;
+        if (e < rr) v[u] += part[static_cast<int64_t>(sg) * rr + e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) {
+      const int e = e0 + u * kThreads;
+      if (e >= rr) continue;
+      const int a = e / r, b = e - a * r;
+      G[a * ld + b] = v[u];
+      if (a == b) tr += v[u];
+    }
   }
   const double norm_sq = cta_sum(tr, red);
   const double inv = 1.0 / sqrt(fmax(norm_sq, static_cast<double>(ns.norm_floor)));
@@ -367,10 +388,16 @@ __global__ void __launch_bounds__(kThreads) k_ns_solve(Tables tb, const MatD* __
       S[a * ld + b] = ((a == b) ? c0 : 0.0) + c1 * G[a * ld + b] + c2 * g2;
     }
     __syncthreads();
-    cta_symm_mm(U, P, S, rp, ld);            // P <- P S
-    double* t = P; P = U; U = t;
-    cta_symm_mm(U, S, G, rp, ld);            // G <- S G S
-    cta_symm_mm(G, U, S, rp, ld);
+    if (small) {
+      cta_symm_mm(P, P, S, rp, ld);          // P <- P S
+      cta_symm_mm(G, S, G, rp, ld);          // G <- S G S
+      cta_symm_mm(G, G, S, rp, ld);
+    } else {
+      cta_symm_mm(U, P, S, rp, ld);
+      double* t = P; P = U; U = t;
+      cta_symm_mm(U, S, G, rp, ld);
+      cta_symm_mm(G, U, S, rp, ld);
+    }
   }
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   for (int e = tid; e < rr; e += kThreads) {

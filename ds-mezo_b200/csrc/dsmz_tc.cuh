@@ -258,23 +258,48 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
   }
 }
 
-// [V_hi | V_lo]^T (2R x D bf16) from the fp32 basis, grouped over bases.
+// [V_hi | V_lo]^T (2R x D bf16) from the fp32 basis, grouped over bases: one CTA per tile of
+// kSplitD vectors. The tile's rows are read coalesced into shared memory (pitch R + 1), and
+// each thread writes eight consecutive vectors of one component as two 16-byte stores.
+constexpr int kSplitD = 64;
 __global__ void __launch_bounds__(kThreads) k_split_vt(const TCBasis* __restrict__ bases, int nb, int first) {
+  __shared__ float tile[kSplitD * (DSMZ_MAX_RANK + 1)];
   const int item = blockIdx.x;
   const int bi = find_owner(bases, nb, item, [](const TCBasis& b) { return b.vt0; });
   const TCBasis* B = bases + bi;
-  const int R = B->R;
-  const int64_t n = B->D * R;
-  const int64_t i0 = static_cast<int64_t>(item - B->vt0) * kThreads * 8;
+  const int R = B->R, tp = R + 1;
+  const int64_t d0 = static_cast<int64_t>(item - B->vt0) * kSplitD;
+  const int nd = static_cast<int>(min(static_cast<int64_t>(kSplitD), B->D - d0));
   const int64_t s0 = first ? B->v_s0 : R, s1 = first ? B->v_s1 : 1;
-  for (int k = 0; k < 8; ++k) {
-    const int64_t e = i0 + k * kThreads + threadIdx.x;
-    if (e >= n) break;
-    const int64_t r = e / B->D, d = e - r * B->D;   // d fastest: coalesced bf16 stores
-    const float v = (first ? B->Vsrc : B->Vout)[d * s0 + r * s1];
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    B->V2T[r * B->ldv2 + d] = h;
-    B->V2T[(R + r) * B->ldv2 + d] = __float2bfloat16_rn(v - __bfloat162float(h));
+  const float* V = first ? B->Vsrc : B->Vout;
+  for (int e = threadIdx.x; e < nd * R; e += kThreads) {
+    const int d = e / R, r = e - d * R;
+    tile[d * tp + r] = V[(d0 + d) * s0 + r * s1];
+  }
+  __syncthreads();
+  const int nu = R * (nd >> 3);                       // eight vectors per unit
+  for (int u = threadIdx.x; u < nu; u += kThreads) {
+    const int r = u / (nd >> 3), j = (u - r * (nd >> 3)) * 8;
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float x0 = tile[(j + 2 * q) * tp + r], x1 = tile[(j + 2 * q + 1) * tp + r];
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+      const float2 hf = __bfloat1622float2(hh);
+      const __nv_bfloat162 ll = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+      h[q] = *reinterpret_cast<const uint32_t*>(&hh);
+      l[q] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    *reinterpret_cast<uint4*>(B->V2T + static_cast<int64_t>(r) * B->ldv2 + d0 + j) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(B->V2T + static_cast<int64_t>(R + r) * B->ldv2 + d0 + j) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+  for (int e = (nd & ~7) + threadIdx.x % 8; e < nd; e += 8) {   // ragged tail (D % 8 != 0)
+    for (int r = threadIdx.x / 8; r < R; r += kThreads / 8) {
+      const float x = tile[e * tp + r];
+      const __nv_bfloat16 hh = __float2bfloat16_rn(x);
+      B->V2T[static_cast<int64_t>(r) * B->ldv2 + d0 + e] = hh;
+      B->V2T[static_cast<int64_t>(R + r) * B->ldv2 + d0 + e] = __float2bfloat16_rn(x - __bfloat162float(hh));
+    }
   }
 }
 
