@@ -601,9 +601,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     else sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
     P->probe_end(DSMZ_KID_PI_GRAM, s);
     DSMZ_LAUNCHED("power iteration Gram of W");
-    const int bpm = (R * R + kThreads - 1) / kThreads;
     P->probe_begin(DSMZ_KID_PI_CHOL, s);
-    k_sum_partials<<<nb * bpm, kThreads, 0, s>>>(tb, tb.wA, nb, bpm);
     k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_);
     P->probe_end(DSMZ_KID_PI_CHOL, s);
     DSMZ_LAUNCHED("power iteration Cholesky");
@@ -974,9 +972,9 @@ uint64_t dsmz_plan_rng_increment(const dsmz_plan* p) { return p ? p->rng_increme
 int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   if (!p) return 0;
   int32_t n = 0;
-  // per iteration: Y, W, [Gram of W on the CUDA-core path], partial sums, Cholesky, V;
-  // plus the first bf16 split of the caller's basis on the tensor-core path
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * 6 + (p->tc ? 1 : 0);
+  // per iteration: Y, W, Gram of W, Cholesky, V; plus the first bf16 split of the caller's
+  // basis on the tensor-core path
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * 5 + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }

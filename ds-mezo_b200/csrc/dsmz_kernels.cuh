@@ -407,68 +407,81 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
 }
 
 // =====================================================================================
-// CholeskyQR step for the power-iteration bases, one CTA per W matrix: G = W^T W (from
-// the Gram partials), G = R^T R with pivots sqrt(max(d, norm_floor)) (the clamp of the
-// reference MGS, ds_mezo/kernels.py:238), and the fp32 apply matrix R^{-1}.
+// CholeskyQR step for the power-iteration bases, one CTA per W matrix: G = W^T W (the
+// Gram partials, one per segment, summed here), G = R^T R with pivots
+// sqrt(max(d, norm_floor)) (the clamp of the reference MGS, ds_mezo/kernels.py:238), and
+// R^{-1}. The factorization is right-looking with one barrier per column on the upper
+// triangle (row j of A ends as row j of R; it is scaled one step later, when nothing reads
+// it any more); R^{-1} is formed row by row from the bottom with four threads per column
+// (shuffle-reduced). Exports R^{-1} in fp32 (apply matrix) and fp64 (after the
+// workspace's first r*r doubles).
 // =====================================================================================
-// Sums the Gram partials of every matrix into its fp64 workspace, 256 entries per CTA:
-// item -> (matrix, entry block). Many CTAs per matrix keep the loads in flight.
-__global__ void __launch_bounds__(kThreads) k_sum_partials(Tables tb, const MatD* __restrict__ mats, int nmats,
-                                                           int blocks_per_mat) {
-  const int mi = blockIdx.x / blocks_per_mat;
-  const int blk = blockIdx.x - mi * blocks_per_mat;
-  if (mi >= nmats) return;
-  const MatD M = mats[mi];
-  const int rr = static_cast<int>(M.r * M.r);
-  const int e = blk * kThreads + threadIdx.x;
-  if (e >= rr) return;
-  const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
-  double* G = reinterpret_cast<double*>(tb.ws) + M.dw_off;
-  G[e] = strided_sum(part + e, M.nseg, rr);
-}
-
-// Cholesky of the summed Gram in the matrix's fp64 workspace (k_sum_partials).
 __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __restrict__ mats, float norm_floor) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const double fl = static_cast<double>(norm_floor);
   // r <= 64: factor and inverse in shared memory; larger r works on the fp64 workspace
   const bool in_smem = r <= 64;
   double* dw = reinterpret_cast<double*>(tb.ws) + M.dw_off;
-  double* A = in_smem ? reinterpret_cast<double*>(smem_raw) : dw;        // lower-right part = Schur complement
+  double* A = in_smem ? reinterpret_cast<double*>(smem_raw) : dw;
   double* Ri = in_smem ? A + rr : dw + 2 * rr;
-  for (int e = tid; e < rr; e += kThreads) {
-    const double g = dw[e];
-    A[e] = g;
-    Ri[e] = 0.0;
+  const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  constexpr int kSumU = 8;                             // independent partial loads in flight
+  for (int e0 = tid; e0 < rr; e0 += kSumU * kThreads) {
+    double v[kSumU];
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) v[u] = 0.0;
+    for (int sg = 0; sg < M.nseg; ++sg) {
+#pragma unroll
+      for (int u = 0; u < kSumU; ++u) {
+        const int e = e0 + u * kThreads;
+        if (e < rr) v[u] += part[static_cast<int64_t>(sg) * rr + e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) {
+      const int e = e0 + u * kThreads;
+      if (e < rr) { A[e] = v[u]; Ri[e] = 0.0; }
+    }
   }
   __syncthreads();
-  // Right-looking Cholesky: after step j, row j of A holds row j of the upper factor R
-  // (G = R^T R), with pivots sqrt(max(d, norm_floor)) like the reference MGS clamp.
+  __shared__ double piv[DSMZ_MAX_RANK];                // pivots, read back one step later
   for (int j = 0; j < r; ++j) {
-    const double d = sqrt(fmax(A[j * r + j], static_cast<double>(norm_floor)));
-    __syncthreads();
-    for (int i = j + tid; i < r; i += kThreads) A[j * r + i] = (i == j) ? d : A[j * r + i] / d;
-    __syncthreads();
-    const int m = r - j - 1;
-    for (int e = tid; e < m * m; e += kThreads) {
-      const int a = j + 1 + e / m, b = j + 1 + e % m;
-      A[a * r + b] -= A[j * r + a] * A[j * r + b];
+    const double dd = fmax(A[j * r + j], fl);          // nothing writes A[j][j] in step j
+    if (tid == 0) piv[j] = sqrt(dd);
+    if (j > 0) {                                       // row j - 1 of R (no longer read)
+      const double dp = piv[j - 1], idp = 1.0 / dp;
+      for (int i = j - 1 + tid; i < r; i += kThreads) A[(j - 1) * r + i] = (i == j - 1) ? dp : A[(j - 1) * r + i] * idp;
+    }
+    const double idd = 1.0 / dd;                       // (x / d)(y / d) = x y / d^2
+    for (int a = j + 1 + warp; a < r; a += kThreads / 32) {
+      const double sa = A[j * r + a] * idd;
+      for (int b = a + lane; b < r; b += 32) A[a * r + b] = fma(-sa, A[j * r + b], A[a * r + b]);
     }
     __syncthreads();
   }
-  // R^{-1}: column c solves R x = e_c by back substitution, one thread per column
-  for (int c = tid; c < r; c += kThreads) {
-    Ri[c * r + c] = 1.0 / A[c * r + c];
-    for (int i = c - 1; i >= 0; --i) {
-      double sum = 0.0;
-      for (int k = i + 1; k <= c; ++k) sum += A[i * r + k] * Ri[k * r + c];
-      Ri[i * r + c] = -sum / A[i * r + i];
-    }
-  }
+  if (tid == 0) A[(r - 1) * r + r - 1] = piv[r - 1];
   __syncthreads();
+  // R^{-1}, rows from the bottom: Ri[i][c] = -(sum_{i<k<=c} R[i][k] Ri[k][c]) / R[i][i]
+  for (int i = r - 1; i >= 0; --i) {
+    const double irii = 1.0 / A[i * r + i];
+    for (int c0 = 0; c0 < r; c0 += kThreads / 4) {
+      const int c = c0 + (tid >> 2), sl = tid & 3;
+      double acc = 0.0;
+      if (c > i && c < r)
+        for (int k = i + 1 + sl; k <= c; k += 4) acc += A[i * r + k] * Ri[k * r + c];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (sl == 0 && c < r) {
+        if (c == i) Ri[i * r + i] = irii;
+        else if (c > i) Ri[i * r + c] = -acc * irii;
+      }
+    }
+    __syncthreads();
+  }
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   double* Rd = dw + rr;                       // fp64 copy for the fp64-accumulated apply
   for (int e = tid; e < rr; e += kThreads) {

@@ -108,7 +108,7 @@ def test_plan_create_host_only(L, rank, h_dtype, tc):
         assert L.dsmz_plan_rng_increment(h) == sum(draw_increments(mods, rank, rank, 148, 2048))
         # tcgen05 power iteration for bf16 activations and R a multiple of 16
         assert L.dsmz_plan_uses_tensor_cores(h) == tc
-        assert L.dsmz_plan_launch_count(h, 3) == (3 * 6 + 1 if tc else 3 * 6) + 8
+        assert L.dsmz_plan_launch_count(h, 3) == (3 * 5 + 1 if tc else 3 * 5) + 8
         # stepping an unbound plan is an error, not a launch
         assert L.dsmz_step_update(h, 0.0, 0.0, 0.0, 0.0, 0.0, None, None) == 1
         assert b"not bound" in L.dsmz_last_error()
@@ -164,7 +164,7 @@ def test_plan_directions_host_only(L, K):
         assert L.dsmz_plan_directions(h) == K
         assert L.dsmz_plan_rng_increment(h) == K * sum(draw_increments(mods, 16, 16, 148, 2048))
         # B-side sums once, 4 launches per direction, 4 update launches
-        assert L.dsmz_plan_launch_count(h, 3) == (3 * 6 + 1) + 1 + 4 * K + 4
+        assert L.dsmz_plan_launch_count(h, 3) == (3 * 5 + 1) + 1 + 4 * K + 4
         dd = (ctypes.c_float * K)(*([0.0] * K))
         assert L.dsmz_step_update_directions(h, dd, K, 0.0, 0.0, 0.0, 0.0, None, None) == 1   # not bound
     finally:
