@@ -233,13 +233,13 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 int tc_stages(int R);
 
 // Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R),
-// and a stage ring large enough to hold the W tile (128 x (R + 1) floats) that the W
+// and a stage ring large enough to hold the W tile (128 x w_stage_ld(R) floats) that the W
 // kernel's epilogue stages over it.
 bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
   return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
          (reinterpret_cast<uintptr_t>(H) & 15) == 0 &&
-         static_cast<int64_t>(tc::kBM) * (R + 1) * 4 <= static_cast<int64_t>(tc_stages(static_cast<int>(R))) *
-                                                          tc::stage_bytes(static_cast<int>(R));
+         static_cast<int64_t>(tc::kBM) * tc::w_stage_ld(static_cast<int>(R)) * 4 <=
+             static_cast<int64_t>(tc_stages(static_cast<int>(R))) * tc::stage_bytes(static_cast<int>(R));
 }
 
 // Ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
@@ -255,6 +255,7 @@ size_t tc_smem(int R) { return static_cast<size_t>(tc_stages(R)) * tc::stage_byt
 
 struct TCSlots {             // workspace byte offsets of one basis
   size_t v2t = 0, y2t = 0;
+  size_t gp = 0;             // fused W Gram partials (R <= 64), 0: none
   int64_t ldv2 = 0, ldy2 = 0;
 };
 
@@ -422,6 +423,11 @@ void plan_tc_layout(dsmz_plan* P) {
     c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + tc::kBM - 1) / tc::kBM); P->ntc_y += c.nytile;
     c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + tc::kBM - 1) / tc::kBM); P->ntc_w += c.nwtile;
     c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D + tc::kSplitD - 1) / tc::kSplitD); P->ntc_vt += c.nvt;
+    if (b.R <= 64) {           // the W epilogue forms the Gram: one block-major partial per W tile
+      const int nb = b.R / 8;
+      c.nq = nb * (nb + 1) / 2;
+      t.gp = P->ws.take(static_cast<size_t>(c.nwtile) * c.nq * 64 * sizeof(double));
+    }
   }
 }
 
@@ -480,6 +486,7 @@ bool bind_tc(dsmz_plan* P) {
     c.V2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.v2t);
     c.Y2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.y2t);
     c.W = reinterpret_cast<float*>(P->workspace) + b.w_off;
+    c.Gp = t.gp ? reinterpret_cast<double*>(P->workspace + t.gp) : nullptr;
     c.Vsrc = b.Vin; c.v_s0 = b.v_s0; c.v_s1 = b.v_s1; c.Vout = b.Vout;
     const uint32_t n2 = static_cast<uint32_t>(2 * b.R);
     if (!encode_bf16_2d(&c.mapHy, b.H, b.D, b.T, b.h_s0 * 2, 64, 128) ||
@@ -566,6 +573,8 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const tc::TCBasis* dtcb = reinterpret_cast<const tc::TCBasis*>(P->dev_tables + P->off_tcb);
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
   const size_t tsm = P->tc ? tc_smem(R) : 0;
+  const bool fused = P->tc && R <= 64;                 // W Gram formed in the W epilogue
+  const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
   if (P->tc) {
     if ((rc = set_smem(tc::k_pi_tc<0>, tsm))) return rc;
     if ((rc = set_smem(tc::k_pi_tc<1>, tsm))) return rc;
@@ -594,15 +603,21 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     P->probe_end(DSMZ_KID_PI_W, s);
     DSMZ_LAUNCHED("power iteration W = H^T Y");
     }
-    // CholeskyQR of W from its exact fp64 Gram (streamed, fp64 MMA); V = W R^{-1}
-    // accumulated in fp64, with the bf16 pair for the next tensor-core Y.
+    // CholeskyQR of W from its exact fp64 Gram (fp64 MMA: fused into the tensor-core W
+    // epilogue for R <= 64, else streamed); V = W R^{-1} accumulated in fp64, with the bf16
+    // pair for the next tensor-core Y.
     P->probe_begin(DSMZ_KID_PI_GRAM, s);
-    if (small) sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
-    else sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
+    if (fused) {
+      tc::k_gsum<<<nb * gpb, kThreads, 0, s>>>(dtcb, tb, tb.wA, gpb);
+    } else if (small) {
+      sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
+    } else {
+      sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
+    }
     P->probe_end(DSMZ_KID_PI_GRAM, s);
     DSMZ_LAUNCHED("power iteration Gram of W");
     P->probe_begin(DSMZ_KID_PI_CHOL, s);
-    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_);
+    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_, fused ? 1 : 0);
     P->probe_end(DSMZ_KID_PI_CHOL, s);
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);

@@ -416,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
 // (shuffle-reduced). Exports R^{-1} in fp32 (apply matrix) and fp64 (after the
 // workspace's first r*r doubles).
 // =====================================================================================
-__global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __restrict__ mats, float norm_floor) {
+__global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __restrict__ mats, float norm_floor,
+                                                   int summed) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
@@ -429,12 +430,13 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
   double* A = in_smem ? reinterpret_cast<double*>(smem_raw) : dw;
   double* Ri = in_smem ? A + rr : dw + 2 * rr;
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  const int nsg = summed ? 1 : M.nseg;              // summed: the Gram is in the first slot already
   constexpr int kSumU = 8;                             // independent partial loads in flight
   for (int e0 = tid; e0 < rr; e0 += kSumU * kThreads) {
     double v[kSumU];
 #pragma unroll
     for (int u = 0; u < kSumU; ++u) v[u] = 0.0;
-    for (int sg = 0; sg < M.nseg; ++sg) {
+    for (int sg = 0; sg < nsg; ++sg) {
 #pragma unroll
       for (int u = 0; u < kSumU; ++u) {
         const int e = e0 + u * kThreads;

@@ -103,10 +103,11 @@ __device__ __forceinline__ void cp16_arrive(uint64_t* bar) {
 // D += A B on the fp64 tensor path (m8n8k4): per thread one element of A (row lane/4,
 // column lane%4), one of B (row lane%4, column lane/4) and two of D (row lane/4, columns
 // 2(lane%4) and 2(lane%4)+1).
+// Not volatile: a pure register computation, so loads may be scheduled across it.
 __device__ __forceinline__ void dmma8x8x4(double& d0, double& d1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-               : "+d"(d0), "+d"(d1)
-               : "d"(a), "d"(b));
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+      : "+d"(d0), "+d"(d1)
+      : "d"(a), "d"(b));
 }
 __device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");

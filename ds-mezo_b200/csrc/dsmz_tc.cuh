@@ -44,8 +44,15 @@ struct alignas(64) TCBasis {
   int32_t R, pad0;
   int32_t ytile0, nytile, wtile0, nwtile;
   int32_t vt0, nvt;       // blocks of the split kernel
-  int32_t pad1, pad2;
+  double* Gp;             // fused W Gram (R <= 64): per W tile, its upper 8 x 8 blocks of
+                          // W_tile^T W_tile (block-major, 64 doubles each); NULL: not fused
+  int32_t nq, pad1;       // upper blocks per tile
 };
+
+// Pitch (floats) of the W tile staged by the W kernel's epilogue: at least R, 8 mod 32, so
+// that the fused Gram's fragments (four rows x eight columns) fall on 32 distinct banks.
+__host__ __device__ inline int w_stage_ld(int R) { return R <= 8 ? 8 : (R - 8 + 31) / 32 * 32 + 8; }
+constexpr int kGramMaxBlocks = 9;   // upper blocks per epilogue warp (R <= 64: 36 / 4)
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -227,17 +234,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
         }
       } else {
         // The pipeline stages are drained (every MMA completed before tmem_full), so the
-        // W tile is staged over them (rows of R + 1 floats: the row-per-thread stores are
-        // free of bank conflicts) and written out coalesced. Its fp64 Gram for the
-        // CholeskyQR is formed by the streaming Gram kernel over W.
+        // W tile is staged over them (rows of w_stage_ld(R) floats, 16-byte stores) and
+        // written out coalesced. With Gp, the four warps then form the tile's fp64 Gram
+        // W_tile^T W_tile on the fp64 MMA (rows past D are zero: the H box there is zero
+        // filled); each warp owns the upper blocks q = warp, warp + 4, ...
         float* wt = reinterpret_cast<float*>(smem);
-        const int tld = R + 1;
+        const int tld = w_stage_ld(R);
         for (int j = 0; j < R; j += 16) {
           float hi[16], lo[16];
           tmem_ld16(trow + j, hi);
           tmem_ld16(trow + R + j, lo);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) wt[row * tld + j + c] = hi[c] + lo[c];
+          for (int c = 0; c < 16; c += 4)
+            *reinterpret_cast<float4*>(wt + row * tld + j + c) =
+                make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
         const int t = threadIdx.x - 64;
@@ -246,6 +256,53 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
         for (int e = t; e < nrow * R; e += kBM) {
           const int rw = e / R, c = e - rw * R;
           B->W[(d0 + rw) * R + c] = wt[rw * tld + c];
+        }
+        if (B->Gp != nullptr) {
+          const int g = lane >> 2, kq = lane & 3;
+          const int nb = R >> 3;
+          int bi[kGramMaxBlocks], bj[kGramMaxBlocks];
+          double acc[kGramMaxBlocks][2];
+#pragma unroll
+          for (int u = 0; u < kGramMaxBlocks; ++u) {
+            int qq = q + 4 * u;
+            bi[u] = -1; bj[u] = 0;
+            acc[u][0] = 0.0; acc[u][1] = 0.0;
+            if (qq < B->nq) {
+              int rb = 0;
+              while (qq >= nb - rb) { qq -= nb - rb; ++rb; }
+              bi[u] = rb; bj[u] = rb + qq;
+            }
+          }
+          int oa[kGramMaxBlocks], ob[kGramMaxBlocks];
+#pragma unroll
+          for (int u = 0; u < kGramMaxBlocks; ++u) {
+            oa[u] = kq * tld + 8 * (bi[u] < 0 ? 0 : bi[u]) + g;
+            ob[u] = kq * tld + 8 * bj[u] + g;
+          }
+          // every fragment of a k-step is loaded one step ahead of its MMAs
+          float na[kGramMaxBlocks], nbv[kGramMaxBlocks];
+#pragma unroll
+          for (int u = 0; u < kGramMaxBlocks; ++u) { na[u] = wt[oa[u]]; nbv[u] = wt[ob[u]]; }
+          for (int k0 = 0; k0 < kBM; k0 += 4) {
+            float ca[kGramMaxBlocks], cb[kGramMaxBlocks];
+#pragma unroll
+            for (int u = 0; u < kGramMaxBlocks; ++u) { ca[u] = na[u]; cb[u] = nbv[u]; }
+            if (k0 + 4 < kBM) {
+              const float* wr = wt + (k0 + 4) * tld;
+#pragma unroll
+              for (int u = 0; u < kGramMaxBlocks; ++u) { na[u] = wr[oa[u]]; nbv[u] = wr[ob[u]]; }
+            }
+#pragma unroll
+            for (int u = 0; u < kGramMaxBlocks; ++u)
+              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], static_cast<double>(ca[u]), static_cast<double>(cb[u]));
+          }
+          double* gp = B->Gp + static_cast<int64_t>(tile) * B->nq * 64;
+#pragma unroll
+          for (int u = 0; u < kGramMaxBlocks; ++u) {
+            if (bi[u] < 0) continue;
+            const int qq = q + 4 * u;
+            *reinterpret_cast<double2*>(gp + qq * 64 + g * 8 + 2 * kq) = make_double2(acc[u][0], acc[u][1]);
+          }
         }
       }
     }
@@ -256,6 +313,38 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
   }
+}
+
+// Sums the fused W Gram's per-tile partials of every basis (fixed order over the tiles)
+// into the basis's Gram, the first partial slot of its W table (r x r, mirrored): per
+// CTA 256 entries of the block-major partial; gpb CTAs per basis.
+__global__ void __launch_bounds__(kThreads) k_gsum(const TCBasis* __restrict__ bases, Tables tb,
+                                                   const MatD* __restrict__ wA, int gpb) {
+  const int bi = blockIdx.x / gpb, blk = blockIdx.x - bi * gpb;
+  const TCBasis* B = bases + bi;
+  const int e = blk * kThreads + threadIdx.x;
+  if (e >= B->nq * 64) return;
+  const int R = B->R, nb = R >> 3;
+  int q = e >> 6, rb = 0;
+  while (q >= nb - rb) { q -= nb - rb; ++rb; }
+  const int row = 8 * rb + ((e & 63) >> 3), col = 8 * (rb + q) + (e & 7);
+  if (q == 0 && row > col) return;                    // diagonal block: its upper half suffices
+  const double* p = B->Gp + e;
+  const int64_t st = static_cast<int64_t>(B->nq) * 64;
+  constexpr int kU = 8;                               // independent loads in flight
+  double acc[kU];
+#pragma unroll
+  for (int u = 0; u < kU; ++u) acc[u] = 0.0;
+  int t = 0;
+  for (; t + kU <= B->nwtile; t += kU) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) acc[u] += p[(t + u) * st];
+  }
+  for (; t < B->nwtile; ++t) acc[0] += p[t * st];
+  const double sum = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  double* G = reinterpret_cast<double*>(tb.ws) + wA[bi].gram_off;
+  G[row * R + col] = sum;
+  G[col * R + row] = sum;
 }
 
 // [V_hi | V_lo]^T (2R x D bf16) from the fp32 basis, grouped over bases: one CTA per tile of
