@@ -233,12 +233,12 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 int tc_stages(int R);
 
 // Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R),
-// and a stage ring large enough to hold the W tile (128 x w_stage_ld(R) floats) that the W
-// kernel's epilogue stages over it.
+// and a stage ring large enough to hold the fp64 W tile (128 x w_stage_ld(R) doubles) that
+// the W kernel's epilogue stages over it for the fused Gram.
 bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
   return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
          (reinterpret_cast<uintptr_t>(H) & 15) == 0 &&
-         static_cast<int64_t>(tc::kBM) * tc::w_stage_ld(static_cast<int>(R)) * 4 <=
+         static_cast<int64_t>(tc::kBM) * tc::w_stage_ld(static_cast<int>(R)) * 8 <=
              static_cast<int64_t>(tc_stages(static_cast<int>(R))) * tc::stage_bytes(static_cast<int>(R));
 }
 

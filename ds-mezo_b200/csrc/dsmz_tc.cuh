@@ -49,9 +49,10 @@ struct alignas(64) TCBasis {
   int32_t nq, pad1;       // upper blocks per tile
 };
 
-// Pitch (floats) of the W tile staged by the W kernel's epilogue: at least R, 8 mod 32, so
-// that the fused Gram's fragments (four rows x eight columns) fall on 32 distinct banks.
-__host__ __device__ inline int w_stage_ld(int R) { return R <= 8 ? 8 : (R - 8 + 31) / 32 * 32 + 8; }
+// Pitch (doubles) of the fp64 W tile staged by the W kernel's epilogue for the fused Gram:
+// R + 4 (R % 16 == 0, so 4 mod 16): each half-warp's fragment (four rows x four columns of
+// 8-byte words) falls on distinct banks.
+__host__ __device__ inline int w_stage_ld(int R) { return R + 4; }
 constexpr int kGramMaxBlocks = 9;   // upper blocks per epilogue warp (R <= 64: 36 / 4)
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
@@ -106,7 +107,7 @@ __host__ __device__ inline int stage_bytes(int R) { return kBM * kBK * 2 + 2 * R
 
 // MODE 0: Y2T = split(H V), tiles over T.  MODE 1: W = H^T Y, tiles over D.
 template <int MODE>
-__global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restrict__ bases, int nb, int stages,
+__global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restrict__ bases, int nb, int stages,
                                                          int* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned base for the swizzled stages
@@ -233,30 +234,32 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
           }
         }
       } else {
-        // The pipeline stages are drained (every MMA completed before tmem_full), so the
-        // W tile is staged over them (rows of w_stage_ld(R) floats, 16-byte stores) and
-        // written out coalesced. With Gp, the four warps then form the tile's fp64 Gram
-        // W_tile^T W_tile on the fp64 MMA (rows past D are zero: the H box there is zero
-        // filled); each warp owns the upper blocks q = warp, warp + 4, ...
-        float* wt = reinterpret_cast<float*>(smem);
+        // Each thread stores its W row straight from the accumulator (hi + lo, 16-byte
+        // stores). With Gp, the pipeline stages (drained: every MMA completed before
+        // tmem_full) take the tile as fp64 (rows of w_stage_ld(R) doubles) and the four warps
+        // form its Gram W_tile^T W_tile on the fp64 MMA (rows past D are zero: the H box
+        // there is zero filled); each warp owns the upper blocks q = warp, warp + 4, ...
+        double* wt = reinterpret_cast<double*>(smem);
         const int tld = w_stage_ld(R);
+        const int64_t d0 = static_cast<int64_t>(tile) * kBM;
+        const bool live = d0 + row < B->D;
+        float* wrow = B->W + (d0 + row) * R;
         for (int j = 0; j < R; j += 16) {
           float hi[16], lo[16];
           tmem_ld16(trow + j, hi);
           tmem_ld16(trow + R + j, lo);
 #pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            *reinterpret_cast<float4*>(wt + row * tld + j + c) =
-                make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
+          for (int c = 0; c < 16; c += 4) {
+            const float4 w4 = make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
+            if (live) *reinterpret_cast<float4*>(wrow + j + c) = w4;
+            if (B->Gp != nullptr) {
+              double2* st = reinterpret_cast<double2*>(wt + row * tld + j + c);
+              st[0] = make_double2(w4.x, w4.y);
+              st[1] = make_double2(w4.z, w4.w);
+            }
+          }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
-        const int t = threadIdx.x - 64;
-        const int64_t d0 = static_cast<int64_t>(tile) * kBM;
-        const int nrow = static_cast<int>(min(static_cast<int64_t>(kBM), B->D - d0));
-        for (int e = t; e < nrow * R; e += kBM) {
-          const int rw = e / R, c = e - rw * R;
-          B->W[(d0 + rw) * R + c] = wt[rw * tld + c];
-        }
         if (B->Gp != nullptr) {
           const int g = lane >> 2, kq = lane & 3;
           const int nb = R >> 3;
@@ -279,22 +282,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_tc(const TCBasis* __restri
             oa[u] = kq * tld + 8 * (bi[u] < 0 ? 0 : bi[u]) + g;
             ob[u] = kq * tld + 8 * bj[u] + g;
           }
-          // every fragment of a k-step is loaded one step ahead of its MMAs
-          float na[kGramMaxBlocks], nbv[kGramMaxBlocks];
+          for (int k0 = 0; k0 < kBM; k0 += 4) {           // all of a step's loads, then its MMAs
+            const double* wr = wt + k0 * tld;
+            double ca[kGramMaxBlocks], cb[kGramMaxBlocks];
 #pragma unroll
-          for (int u = 0; u < kGramMaxBlocks; ++u) { na[u] = wt[oa[u]]; nbv[u] = wt[ob[u]]; }
-          for (int k0 = 0; k0 < kBM; k0 += 4) {
-            float ca[kGramMaxBlocks], cb[kGramMaxBlocks];
-#pragma unroll
-            for (int u = 0; u < kGramMaxBlocks; ++u) { ca[u] = na[u]; cb[u] = nbv[u]; }
-            if (k0 + 4 < kBM) {
-              const float* wr = wt + (k0 + 4) * tld;
-#pragma unroll
-              for (int u = 0; u < kGramMaxBlocks; ++u) { na[u] = wr[oa[u]]; nbv[u] = wr[ob[u]]; }
-            }
+            for (int u = 0; u < kGramMaxBlocks; ++u) { ca[u] = wr[oa[u]]; cb[u] = wr[ob[u]]; }
 #pragma unroll
             for (int u = 0; u < kGramMaxBlocks; ++u)
-              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], static_cast<double>(ca[u]), static_cast<double>(cb[u]));
+              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], ca[u], cb[u]);
           }
           double* gp = B->Gp + static_cast<int64_t>(tile) * B->nq * 64;
 #pragma unroll
