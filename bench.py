@@ -138,15 +138,18 @@ def alg_bytes(aset, cfg):
     vr = sum(b.D * R for b in aset.bases) * 4
     yr = sum(b.T * R for b in aset.bases) * 4
     nB = sum(R * m.d_in for m in aset.modules)
+    # fused W Gram (tensor-core path, R <= 64): per 128-row W tile its upper 8 x 8 blocks
+    nq = (R // 8) * (R // 8 + 1) // 2
+    gp = sum((b.D + 127) // 128 for b in aset.bases) * nq * 64 * 8
     return {
         "pi_y": hb + vr + yr,                      # read H, bf16 [V_hi|V_lo]; write bf16 [Y_hi|Y_lo]
         "pi_w": hb + yr + vr,                      # read H, [Y_hi|Y_lo]; write W (fp32)
-        "pi_gram": vr,                             # read W (CUDA-core path only)
+        "pi_gram": gp if R <= 64 else vr,          # read the per-tile Gram partials (else W)
         "pi_apply": 3 * vr,                        # read W; write V (fp32) and [V_hi|V_lo]^T (bf16)
         "pi_split": 2 * vr,                        # read V, write bf16 [V_hi | V_lo]^T
-        "bside": nB * (f + 4),                     # read B, var_B
-        "perturb": N * (3 * f + 12),               # read p, mu, var; write pos, neg, z (one direction)
-        "gram": N * 12 if K == 1 else N * 4,       # read mu, var, z (K > 1: mu2 only)
+        "bside": nB * (f + 8),                     # read B, var_B and the basis rows
+        "perturb": N * (3 * f + 16),               # read p, mu, var, K-operand rows; write pos, neg, z
+        "gram": N * 20 if K == 1 else N * 4,       # read mu, var, z, write mu, var (K > 1: read mu2)
         "kalman_dirs": N * (16 + 4 * K),           # read mu, var, K z; write mu, var
         "apply": N * (f + 4 + f),                  # read p, mu2; write p
     }
@@ -156,7 +159,8 @@ def alg_bytes(aset, cfg):
 # dram__bytes_write.sum) on the 4-layer cut of the 7B workload, whose launches read more
 # than L2 holds; the full workload's launches do the same work per unit, so traffic scales
 # with the algorithmic bytes (the k_pi_tc and adapter-kernel summaries under profiles/).
-TRAFFIC_PER_ALG_BYTE = {"pi_y": 1.002, "pi_w": 1.020, "perturb": 0.999, "gram": 1.020, "apply": 0.912}
+TRAFFIC_PER_ALG_BYTE = {"pi_y": 1.001, "pi_w": 1.010, "perturb": 0.925, "gram": 0.899, "apply": 0.862,
+                        "bside": 0.926}
 
 
 # ----------------------------------------------------------------------------- CPU oracle
@@ -395,7 +399,8 @@ def main():
     # per element: read p, mu, var and write p, mu, var once; per direction write pos, neg, z
     # and read z back (K > 1)
     per_elem = 2 * f + 16 + K * (2 * f + (4 if K == 1 else 8))
-    step_bytes = sum(sstep.layout.sizes) * per_elem + 3 * act_layer * cfg["layers"]
+    # activations: each of the 3 power iterations reads H twice (Y = H V, then W = H^T Y)
+    step_bytes = sum(sstep.layout.sizes) * per_elem + 2 * 3 * act_layer * cfg["layers"]
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
