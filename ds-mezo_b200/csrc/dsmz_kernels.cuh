@@ -406,6 +406,47 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
   }
 }
 
+// Cholesky of the r x r symmetric matrix A (row-major, pitch r) in place and the inverse
+// of its upper factor: afterwards A's upper triangle holds R (G = R^T R, pivots
+// sqrt(max(d, fl)), the clamp of the reference MGS norms) and Ri holds R^{-1} (zero below
+// the diagonal). Right-looking on the upper triangle with one barrier per column (row j of
+// R is scaled one step later, when nothing reads it; piv carries the pivots across the
+// barrier), then R^{-1} row by row from the bottom with four threads per column
+// (shuffle-reduced). piv: r doubles of shared memory. Ends with a barrier.
+__device__ void cta_chol_rinv(double* A, double* Ri, double* piv, int r, double fl) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int j = 0; j < r; ++j) {
+    const double dd = fmax(A[j * r + j], fl);          // nothing writes A[j][j] in step j
+    if (tid == 0) piv[j] = sqrt(dd);
+    if (j > 0) {                                       // row j - 1 of R (no longer read)
+      const double dp = piv[j - 1], idp = 1.0 / dp;
+      for (int i = j - 1 + tid; i < r; i += kThreads) A[(j - 1) * r + i] = (i == j - 1) ? dp : A[(j - 1) * r + i] * idp;
+    }
+    const double idd = 1.0 / dd;                       // (x / d)(y / d) = x y / d^2
+    for (int a = j + 1 + warp; a < r; a += kThreads / 32) {
+      const double sa = A[j * r + a] * idd;
+      for (int b = a + lane; b < r; b += 32) A[a * r + b] = fma(-sa, A[j * r + b], A[a * r + b]);
+    }
+    __syncthreads();
+  }
+  if (tid == 0) A[(r - 1) * r + r - 1] = piv[r - 1];
+  __syncthreads();
+  // R^{-1}, rows from the bottom: Ri[i][c] = -(sum_{i<k<=c} R[i][k] Ri[k][c]) / R[i][i]
+  for (int i = r - 1; i >= 0; --i) {
+    const double irii = 1.0 / A[i * r + i];
+    for (int c0 = 0; c0 < r; c0 += kThreads / 4) {
+      const int c = c0 + (tid >> 2), sl = tid & 3;
+      double acc = 0.0;
+      if (c > i && c < r)
+        for (int k = i + 1 + sl; k <= c; k += 4) acc += A[i * r + k] * Ri[k * r + c];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (sl == 0 && c < r) Ri[i * r + c] = (c == i) ? irii : (c > i ? -acc * irii : 0.0);
+    }
+    __syncthreads();
+  }
+}
+
 // =====================================================================================
 // CholeskyQR step for the power-iteration bases, one CTA per W matrix: G = W^T W (the
 // Gram partials, one per segment, summed here), G = R^T R with pivots
@@ -422,7 +463,7 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
   const double fl = static_cast<double>(norm_floor);
   // r <= 64: factor and inverse in shared memory; larger r works on the fp64 workspace
   const bool in_smem = r <= 64;
@@ -450,40 +491,8 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
     }
   }
   __syncthreads();
-  __shared__ double piv[DSMZ_MAX_RANK];                // pivots, read back one step later
-  for (int j = 0; j < r; ++j) {
-    const double dd = fmax(A[j * r + j], fl);          // nothing writes A[j][j] in step j
-    if (tid == 0) piv[j] = sqrt(dd);
-    if (j > 0) {                                       // row j - 1 of R (no longer read)
-      const double dp = piv[j - 1], idp = 1.0 / dp;
-      for (int i = j - 1 + tid; i < r; i += kThreads) A[(j - 1) * r + i] = (i == j - 1) ? dp : A[(j - 1) * r + i] * idp;
-    }
-    const double idd = 1.0 / dd;                       // (x / d)(y / d) = x y / d^2
-    for (int a = j + 1 + warp; a < r; a += kThreads / 32) {
-      const double sa = A[j * r + a] * idd;
-      for (int b = a + lane; b < r; b += 32) A[a * r + b] = fma(-sa, A[j * r + b], A[a * r + b]);
-    }
-    __syncthreads();
-  }
-  if (tid == 0) A[(r - 1) * r + r - 1] = piv[r - 1];
-  __syncthreads();
-  // R^{-1}, rows from the bottom: Ri[i][c] = -(sum_{i<k<=c} R[i][k] Ri[k][c]) / R[i][i]
-  for (int i = r - 1; i >= 0; --i) {
-    const double irii = 1.0 / A[i * r + i];
-    for (int c0 = 0; c0 < r; c0 += kThreads / 4) {
-      const int c = c0 + (tid >> 2), sl = tid & 3;
-      double acc = 0.0;
-      if (c > i && c < r)
-        for (int k = i + 1 + sl; k <= c; k += 4) acc += A[i * r + k] * Ri[k * r + c];
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (sl == 0 && c < r) {
-        if (c == i) Ri[i * r + i] = irii;
-        else if (c > i) Ri[i * r + c] = -acc * irii;
-      }
-    }
-    __syncthreads();
-  }
+  __shared__ double piv[DSMZ_MAX_RANK];
+  cta_chol_rinv(A, Ri, piv, r, fl);
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   double* Rd = dw + rr;                       // fp64 copy for the fp64-accumulated apply
   for (int e = tid; e < rr; e += kThreads) {
@@ -855,7 +864,8 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   // Q = QR(B V)[:, :RCA] with a positive diagonal, the factor the reference's modified
   // Gram-Schmidt produces (ds_mezo/kernels.py:328-340), as CholeskyQR2 in fp64: two rounds of
   // G = Q^T Q, G = R^T R, Q <- Q R^{-1}, every step parallel over the CTA.
-  if (RCA <= 64) {
+  if (RCA <= 64 && R <= 64) {
+  __shared__ double piv[DSMZ_MAX_RANK];
   double* G = BVt + RC * bld;                 // RCA x RCA
   double* Rm = G + RCA * RCA;               // inverse of the upper factor
   for (int round = 0; round < 2; ++round) {
@@ -868,34 +878,34 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       G[e] = sacc;
     }
     __syncthreads();
-    for (int j = 0; j < RCA; ++j) {          // right-looking Cholesky, pivots clamped like MGS norms
-      const double d = sqrt(fmax(G[j * RCA + j], static_cast<double>(norm_floor)));
-      __syncthreads();
-      for (int i = j + tid; i < RCA; i += kThreads) G[j * RCA + i] = (i == j) ? d : G[j * RCA + i] / d;
-      __syncthreads();
-      const int m = RCA - j - 1;
-      for (int e = tid; e < m * m; e += kThreads) {
-        const int a = j + 1 + e / m, b = j + 1 + e % m;
-        G[a * RCA + b] -= G[j * RCA + a] * G[j * RCA + b];
+    cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
+    // Q <- Q R^{-1}: every output (i, c) = sum_{a<=c} Q[i][a] R^{-1}[a][c] held in registers
+    // across a barrier, then written in place. Thread: row i = tid % R, columns
+    // c = cg, cg + ncg, ... with cg = tid / R.
+    {
+      constexpr int kQc = 16;
+      double out[kQc];
+      const int i = tid % R, cg = tid / R, ncg = kThreads / R;
+      const bool act = R <= kThreads && cg < ncg && i < R;
+#pragma unroll
+      for (int j = 0; j < kQc; ++j) out[j] = 0.0;
+      if (act) {
+        for (int a = 0; a < RCA; ++a) {
+          const double qa = BVt[a * bld + i];
+#pragma unroll
+          for (int j = 0; j < kQc; ++j) {
+            const int c = cg + j * ncg;
+            if (c < RCA && a <= c) out[j] = fma(qa, Rm[a * RCA + c], out[j]);
+          }
+        }
       }
       __syncthreads();
-    }
-    for (int c = tid; c < RCA; c += kThreads) {   // R^{-1}, one column per thread
-      Rm[c * RCA + c] = 1.0 / G[c * RCA + c];
-      for (int i = c - 1; i >= 0; --i) {
-        double sacc = 0.0;
-        for (int k = i + 1; k <= c; ++k) sacc += G[i * RCA + k] * Rm[k * RCA + c];
-        Rm[i * RCA + c] = -sacc / G[i * RCA + i];
-      }
-      for (int i = c + 1; i < RCA; ++i) Rm[i * RCA + c] = 0.0;
-    }
-    __syncthreads();
-    // Q <- Q R^{-1} in place: column c needs old columns a <= c, so go from the last column down
-    for (int i = tid; i < R; i += kThreads) {
-      for (int c = RCA - 1; c >= 0; --c) {
-        double sacc = 0.0;
-        for (int a = 0; a <= c; ++a) sacc = fma(BVt[a * bld + i], Rm[a * RCA + c], sacc);
-        BVt[c * bld + i] = sacc;
+      if (act) {
+#pragma unroll
+        for (int j = 0; j < kQc; ++j) {
+          const int c = cg + j * ncg;
+          if (c < RCA) BVt[c * bld + i] = out[j];
+        }
       }
     }
     __syncthreads();
