@@ -74,7 +74,7 @@ size_t perturb_smem(int r, int R, int RC) {
 }
 size_t coef_smem(int R, int RC) {
   const size_t rca = static_cast<size_t>(R < RC ? R : RC);
-  return (static_cast<size_t>(R + 1) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
+  return (static_cast<size_t>(R + 4) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
 }
 size_t ns_smem(int r) { return r <= 64 ? 3 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
@@ -293,6 +293,7 @@ struct dsmz_plan {
   std::vector<TCSlots> tcs;
   size_t off_tcb = 0, err_off = 0;
   int ntc_y = 0, ntc_w = 0, ntc_vt = 0;
+  mutable bool split_current = false;   // [V_hi | V_lo]^T matches V (set by a power iteration)
   struct Probe {
     std::vector<cudaEvent_t> start, stop;
     int count = 0;
@@ -555,7 +556,7 @@ void reserve_w_gram(dsmz_plan* P) {
 }
 
 // ---------------------------------------------------------------- launch sequences
-int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s) {
+int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s, uint32_t flags = 0u) {
   if (P->bases.empty() || iters <= 0) return 0;
   const Tables tb = P->tables();
   const int R = P->R;
@@ -578,10 +579,13 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   if (P->tc) {
     if ((rc = set_smem(tc::k_pi_tc<0>, tsm))) return rc;
     if ((rc = set_smem(tc::k_pi_tc<1>, tsm))) return rc;
-    P->probe_begin(DSMZ_KID_PI_SPLIT, s);
-    tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
-    P->probe_end(DSMZ_KID_PI_SPLIT, s);
-    DSMZ_LAUNCHED("power iteration basis split");
+    if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
+      P->probe_begin(DSMZ_KID_PI_SPLIT, s);
+      tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
+      P->probe_end(DSMZ_KID_PI_SPLIT, s);
+      DSMZ_LAUNCHED("power iteration basis split");
+    }
+    P->split_current = true;            // the last QR apply writes [V_hi | V_lo]^T of V
   }
   for (int it = 0; it < iters; ++it) {
     if (P->tc) {
@@ -1005,6 +1009,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_bind: workspace must be 256-byte and tables 64-byte aligned");
   P->dev_tables = static_cast<char*>(device_tables);
   P->workspace = static_cast<char*>(workspace);
+  P->split_current = false;
   patch_ws_pointers(P);
   if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
   bind_side1_maps(P);
@@ -1039,9 +1044,14 @@ static int plan_ready(const dsmz_plan* P, const char* who) {
 }
 
 int dsmz_step_power_iteration(const dsmz_plan* P, int32_t num_iters, float norm_floor, dsmz_stream_t stream) {
+  return dsmz_step_power_iteration_ex(P, num_iters, norm_floor, 0u, stream);
+}
+
+int dsmz_step_power_iteration_ex(const dsmz_plan* P, int32_t num_iters, float norm_floor, uint32_t flags,
+                                 dsmz_stream_t stream) {
   int rc = plan_ready(P, "dsmz_step_power_iteration");
   if (rc) return rc;
-  return run_power_iteration(P, num_iters, norm_floor, static_cast<cudaStream_t>(stream));
+  return run_power_iteration(P, num_iters, norm_floor, static_cast<cudaStream_t>(stream), flags);
 }
 
 int dsmz_step_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, float beta, float q,

@@ -838,7 +838,8 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   const ModD D = tb.mods[blockIdx.x];
   const int R = D.r, RC = D.rc, RCA = D.rca;
   const int tid = threadIdx.x;
-  const int bld = R + 1;                              // padded column stride (bank spread)
+  const int bld = R + 4;                              // padded column stride: the MMA fragments
+                                                      // half-warp rows on distinct banks
   double* BVt = reinterpret_cast<double*>(smem_raw);  // RC x bld (column-major B V)
   const float* part = reinterpret_cast<const float*>(tb.ws) + D.bpart_off;
   float* ZcB = reinterpret_cast<float*>(tb.ws) + D.coef_off;
@@ -869,13 +870,38 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   double* G = BVt + RC * bld;                 // RCA x RCA
   double* Rm = G + RCA * RCA;               // inverse of the upper factor
   for (int round = 0; round < 2; ++round) {
-    for (int e = tid; e < RCA * RCA; e += kThreads) {
-      const int a = e / RCA, b = e - a * RCA;
-      const double* qa = BVt + a * bld;
-      const double* qb = BVt + b * bld;
-      double sacc = 0.0;
-      for (int i = 0; i < R; ++i) sacc = fma(qa[i], qb[i], sacc);
-      G[e] = sacc;
+    if ((R & 3) == 0 && (RCA & 7) == 0) {
+      // G = Q^T Q on the fp64 MMA: the upper 8 x 8 blocks, mirrored; Q^T is BVt row-major
+      // (pitch bld), so both fragments are BVt rows: A[g][k] = BVt[(8bi+g)*bld + k],
+      // B[k][g] = BVt[(8bj+g)*bld + k].
+      const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, kq = lane & 3;
+      const int nb = RCA >> 3, nq = nb * (nb + 1) / 2;
+      for (int q0 = warp; q0 < nq; q0 += kThreads / 32) {
+        int qq = q0, rb = 0;
+        while (qq >= nb - rb) { qq -= nb - rb; ++rb; }
+        const int bi = rb, bj = rb + qq;
+        double c0 = 0.0, c1 = 0.0;
+        const double* ar = BVt + (8 * bi + g) * bld + kq;
+        const double* br = BVt + (8 * bj + g) * bld + kq;
+        for (int k0 = 0; k0 < R; k0 += 4) dmma8x8x4(c0, c1, ar[k0], br[k0]);
+        const int row = 8 * bi + g;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = 8 * bj + 2 * kq + h;
+          const double v = h ? c1 : c0;
+          G[row * RCA + col] = v;
+          G[col * RCA + row] = v;
+        }
+      }
+    } else {
+      for (int e = tid; e < RCA * RCA; e += kThreads) {
+        const int a = e / RCA, b = e - a * RCA;
+        const double* qa = BVt + a * bld;
+        const double* qb = BVt + b * bld;
+        double sacc = 0.0;
+        for (int i = 0; i < R; ++i) sacc = fma(qa[i], qb[i], sacc);
+        G[e] = sacc;
+      }
     }
     __syncthreads();
     cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));

@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdsmezo.so")
@@ -62,6 +62,7 @@ class PlanDesc(ctypes.Structure):
 
 
 MAX_DIRECTIONS = 32
+PI_BASIS_UNCHANGED = 1        # dsmz_step_power_iteration_ex flag (include/dsmezo.h)
 
 
 PLAN_SIMT_POWER_ITER = 1
@@ -106,6 +107,7 @@ SIGNATURES = {
                                               c_float, POINTER(NSSchedule), c_void_p]),
     "dsmz_plan_device_error": (c_int32, [c_void_p, c_void_p]),
     "dsmz_step_power_iteration": (c_int32, [c_void_p, c_int32, c_float, c_void_p]),
+    "dsmz_step_power_iteration_ex": (c_int32, [c_void_p, c_int32, c_float, c_uint32, c_void_p]),
     "dsmz_step_perturb": (c_int32, [c_void_p, c_uint64, c_uint64, c_float, c_float, c_float, c_float, c_void_p]),
     "dsmz_step_kalman_sums": (c_void_p, [c_void_p]),
     "dsmz_step_update": (c_int32, [c_void_p, c_float, c_float, c_float, c_float, c_float, POINTER(NSSchedule),

@@ -234,6 +234,8 @@ class AdapterSet:
         addr = L.dsmz_step_kalman_sums(handle)
         off = addr - self.workspace.data_ptr()
         self._kal = self.workspace[off:off + 16 * self.directions].view(torch.float64)
+        self.launches = 0            # kernels this set has launched
+        self._v_version = None       # basis arena version after the last power iteration
 
     def __del__(self):
         h = getattr(self, "_plan", None)
@@ -261,12 +263,22 @@ class AdapterSet:
 
     # ------------------------------------------------------------------ phases
     def power_iteration(self, num_iters: int = 3, norm_floor: float = FLT_MIN):
-        check(lib().dsmz_step_power_iteration(self._plan, int(num_iters), float(norm_floor), self._stream()),
-              "power iteration")
+        """Power iteration of every basis. When no basis was written since this set's last
+        power iteration (torch's version counter of the basis arena is unchanged: the
+        library's own writes do not move it), the tensor-core path reuses that iteration's
+        bf16 split of the bases."""
+        unchanged = self._v_version is not None and self._v_version == self.V_arena._version
+        flags = _lib.PI_BASIS_UNCHANGED if unchanged else 0
+        check(lib().dsmz_step_power_iteration_ex(self._plan, int(num_iters), float(norm_floor), flags,
+                                                 self._stream()), "power iteration")
+        n = self.launch_count(num_iters) - self.launch_count(0)
+        self.launches += n - (1 if (unchanged and self.uses_tensor_cores and num_iters > 0) else 0)
+        self._v_version = self.V_arena._version if num_iters > 0 else self._v_version
 
     def perturb(self, seed: int, offset: int, eps: float, beta: float, q: float, norm_floor: float = FLT_MIN):
         check(lib().dsmz_step_perturb(self._plan, int(seed) & (2 ** 64 - 1), int(offset), float(eps), float(beta),
                                       float(q), float(norm_floor), self._stream()), "perturbation")
+        self.launches += 1 + 4 * self.directions if self.numel else 0
 
     def kalman_sums(self) -> torch.Tensor:
         """Device view of the rank-local (sum z*mu1, sum z^2*var1) of every direction
@@ -282,10 +294,12 @@ class AdapterSet:
         if self.directions == 1:
             check(lib().dsmz_step_update(self._plan, dds[0], float(beta), float(q), float(eta), float(norm_floor),
                                          sched, self._stream()), "update")
+            self.launches += 3 if self.numel else 0
             return
         arr = (ctypes.c_float * len(dds))(*dds)
         check(lib().dsmz_step_update_directions(self._plan, arr, len(dds), float(beta), float(q), float(eta),
                                                 float(norm_floor), sched, self._stream()), "update")
+        self.launches += 4 if self.numel else 0
 
 
 def rloo_direction_scalars(rewards: torch.Tensor, eps: float) -> List[float]:

@@ -213,6 +213,14 @@ int32_t dsmz_plan_device_error(const dsmz_plan* plan, dsmz_stream_t stream);
 
 /* Phase 1 (ds_mezo/controller.py:165-176): power iteration of every basis. */
 int dsmz_step_power_iteration(const dsmz_plan* plan, int32_t num_iters, float norm_floor, dsmz_stream_t stream);
+/* Same with flags. DSMZ_PI_BASIS_UNCHANGED: the caller guarantees that no basis was written
+ * since this plan's last power iteration; the tensor-core path then takes the first
+ * iteration's bf16 split of the bases from that iteration's QR apply instead of recomputing
+ * it (one launch less). Without a previous iteration on this binding the flag is ignored.
+ * No reference counterpart (the reference recomputes from the basis every call). */
+#define DSMZ_PI_BASIS_UNCHANGED 1u
+int dsmz_step_power_iteration_ex(const dsmz_plan* plan, int32_t num_iters, float norm_floor, uint32_t flags,
+                                 dsmz_stream_t stream);
 
 /* Phase 2 (ds_mezo/controller.py:178-193, 236-251, 260-270): Gaussian draws regenerated
  * from the torch Philox stream at (seed, offset), AGZO perturbation z, pos/neg copies,
