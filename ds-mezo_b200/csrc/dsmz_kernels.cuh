@@ -447,6 +447,102 @@ __device__ void cta_chol_rinv(double* A, double* Ri, double* piv, int r, double 
   }
 }
 
+// Blocked form of cta_chol_rinv for r % 8 == 0 (same factor and inverse up to rounding):
+// per 8-wide block column J, warp 0 factors the diagonal block (scalar steps, the same
+// pivot clamp) and inverts it into Ri's diagonal block; the row panel R_JK = R_JJ^{-T} A_JK
+// and the trailing update A_KL -= R_JK^T R_JL (upper blocks) run on the fp64 MMA, one
+// block per warp. R^{-1}'s off-diagonal blocks follow by block back-substitution,
+// X_IJ = -R_II^{-1} sum_{I<K<=J} R_IK X_KJ, block rows from the bottom. About 3 barriers per
+// block column instead of 2 per scalar column. A's lower triangle is left as it was.
+__device__ void cta_chol_rinv8(double* A, double* Ri, int r, double fl) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, kq = lane & 3;
+  const int nb = r >> 3, nw = kThreads / 32;
+  for (int e = tid; e < r * r; e += kThreads) Ri[e] = 0.0;
+  __syncthreads();
+  for (int J = 0; J < nb; ++J) {
+    double* AJJ = A + 8 * J * r + 8 * J;
+    double* RJJ = Ri + 8 * J * r + 8 * J;
+    if (warp == 0) {
+      for (int jj = 0; jj < 8; ++jj) {               // the 8 x 8 diagonal block, in place
+        const double dd = fmax(AJJ[jj * r + jj], fl);
+        const double idd = 1.0 / dd, d = sqrt(dd), id = 1.0 / d;
+        int p = lane, a = jj + 1;                    // pair (a, b), jj < a <= b < 8, per lane
+        while (a < 8 && p >= 8 - a) { p -= 8 - a; ++a; }
+        const int b = a + p;
+        double upd = 0.0, rowv = 0.0;
+        if (a < 8) upd = fma(-AJJ[jj * r + a] * idd, AJJ[jj * r + b], AJJ[a * r + b]);
+        if (lane > jj && lane < 8) rowv = AJJ[jj * r + lane] * id;
+        __syncwarp();
+        if (a < 8) AJJ[a * r + b] = upd;
+        if (lane == jj) AJJ[jj * r + jj] = d;
+        if (lane > jj && lane < 8) AJJ[jj * r + lane] = rowv;
+        __syncwarp();
+      }
+      for (int i = 7; i >= 0; --i) {                 // its inverse, rows from the bottom
+        const double irii = 1.0 / AJJ[i * r + i];
+        const int c = lane >> 2, sl = lane & 3;
+        double acc = 0.0;
+        if (c > i)
+          for (int k = i + 1 + sl; k <= c; k += 4) acc += AJJ[i * r + k] * RJJ[k * r + c];
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (sl == 0 && c >= i) RJJ[i * r + c] = (c == i) ? irii : -acc * irii;
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    for (int K = J + 1 + warp; K < nb; K += nw) {    // row panel: R_JK = R_JJ^{-T} A_JK
+      double* AJK = A + 8 * J * r + 8 * K;
+      double c0 = 0.0, c1 = 0.0;
+#pragma unroll
+      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(c0, c1, RJJ[(k0 + kq) * r + g], AJK[(k0 + kq) * r + g]);
+      __syncwarp();
+      AJK[g * r + 2 * kq] = c0;
+      AJK[g * r + 2 * kq + 1] = c1;
+    }
+    __syncthreads();
+    const int m = nb - 1 - J, np = m * (m + 1) / 2;
+    for (int p0 = warp; p0 < np; p0 += nw) {         // trailing update of the upper blocks
+      int p = p0, K = J + 1;
+      while (p >= nb - K) { p -= nb - K; ++K; }
+      const int L = K + p;
+      double* AKL = A + 8 * K * r + 8 * L;
+      const double* RJK = A + 8 * J * r + 8 * K;
+      const double* RJL = A + 8 * J * r + 8 * L;
+      double c0 = AKL[g * r + 2 * kq], c1 = AKL[g * r + 2 * kq + 1];
+#pragma unroll
+      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(c0, c1, -RJK[(k0 + kq) * r + g], RJL[(k0 + kq) * r + g]);
+      AKL[g * r + 2 * kq] = c0;
+      AKL[g * r + 2 * kq + 1] = c1;
+    }
+    __syncthreads();
+  }
+  for (int I = nb - 2; I >= 0; --I) {                // off-diagonal blocks of R^{-1}
+    for (int J = I + 1 + warp; J < nb; J += nw) {
+      double t0 = 0.0, t1 = 0.0;
+      for (int K = I + 1; K <= J; ++K) {
+        const double* RIK = A + 8 * I * r + 8 * K;
+        const double* XKJ = Ri + 8 * K * r + 8 * J;
+#pragma unroll
+        for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(t0, t1, RIK[g * r + k0 + kq], XKJ[(k0 + kq) * r + g]);
+      }
+      double* XIJ = Ri + 8 * I * r + 8 * J;          // stage T there, then X = -R_II^{-1} T
+      XIJ[g * r + 2 * kq] = t0;
+      XIJ[g * r + 2 * kq + 1] = t1;
+      __syncwarp();
+      const double* RII = Ri + 8 * I * r + 8 * I;
+      double x0 = 0.0, x1 = 0.0;
+#pragma unroll
+      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(x0, x1, -RII[g * r + k0 + kq], XIJ[(k0 + kq) * r + g]);
+      __syncwarp();
+      XIJ[g * r + 2 * kq] = x0;
+      XIJ[g * r + 2 * kq + 1] = x1;
+    }
+    __syncthreads();
+  }
+}
+
 // =====================================================================================
 // CholeskyQR step for the power-iteration bases, one CTA per W matrix: G = W^T W (the
 // Gram partials, one per segment, summed here), G = R^T R with pivots
@@ -492,7 +588,8 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
   }
   __syncthreads();
   __shared__ double piv[DSMZ_MAX_RANK];
-  cta_chol_rinv(A, Ri, piv, r, fl);
+  if ((r & 7) == 0) cta_chol_rinv8(A, Ri, r, fl);
+  else cta_chol_rinv(A, Ri, piv, r, fl);
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   double* Rd = dw + rr;                       // fp64 copy for the fp64-accumulated apply
   for (int e = tid; e < rr; e += kThreads) {
@@ -831,6 +928,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb) {
 // (controller.py:183-186), and Q = MGS(B V)[:, :RCA] (ds_mezo/kernels.py:328-340) in fp64
 // by one warp. MODE 0 draws Zc_B from the torch Philox stream, MODE 1 copies it.
 // =====================================================================================
+constexpr int kQBlocks = 8;    // output blocks per warp of the Q update (64 x 64: 64 blocks)
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uint64_t base_off, float norm_floor,
                                                    int with_qr) {
@@ -904,7 +1002,37 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       }
     }
     __syncthreads();
-    cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
+    if ((RCA & 7) == 0) cta_chol_rinv8(G, Rm, RCA, static_cast<double>(norm_floor));
+    else cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
+    if ((R & 7) == 0 && (RCA & 7) == 0 && R <= 64) {
+      // Q <- Q R^{-1} on the fp64 MMA, as Q^T <- R^{-T} Q^T on BVt (Q^T row-major): output
+      // block (column block cb of Q, row block ib of Q) = sum_{a < 8cb+8} R^{-1}[a][8cb+..]
+      // Q^T[a][8ib+..] (R^{-1} upper), held in registers across a barrier, then in place.
+      const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, kq = lane & 3;
+      const int ncb = RCA >> 3, nib = R >> 3, nblk = ncb * nib;
+      double o[kQBlocks][2];
+      int cbq[kQBlocks], ibq[kQBlocks];
+#pragma unroll
+      for (int u = 0; u < kQBlocks; ++u) {
+        const int q = warp + u * (kThreads / 32);
+        cbq[u] = q < nblk ? q / nib : -1;
+        ibq[u] = q < nblk ? q - (q / nib) * nib : 0;
+        o[u][0] = 0.0; o[u][1] = 0.0;
+        if (cbq[u] < 0) continue;
+        const double* ra = Rm + kq * RCA + 8 * cbq[u] + g;
+        const double* qb = BVt + kq * bld + 8 * ibq[u] + g;
+        for (int k0 = 0; k0 < 8 * cbq[u] + 8; k0 += 4)
+          dmma8x8x4(o[u][0], o[u][1], ra[k0 * RCA], qb[k0 * bld]);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < kQBlocks; ++u) {
+        if (cbq[u] < 0) continue;
+        double* dst = BVt + (8 * cbq[u] + g) * bld + 8 * ibq[u] + 2 * kq;
+        dst[0] = o[u][0];
+        dst[1] = o[u][1];
+      }
+    } else {
     // Q <- Q R^{-1}: every output (i, c) = sum_{a<=c} Q[i][a] R^{-1}[a][c] held in registers
     // across a barrier, then written in place. Thread: row i = tid % R, columns
     // c = cg, cg + ncg, ... with cg = tid / R.
@@ -933,6 +1061,7 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
           if (c < RCA) BVt[c * bld + i] = out[j];
         }
       }
+    }
     }
     __syncthreads();
   }
