@@ -112,7 +112,7 @@ __device__ __forceinline__ void dmma8x8x4(double& d0, double& d1, double a, doub
 __device__ __forceinline__ void tmap_acquire(const CUtensorMap* m) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(m) : "memory");
 }
-// 2-D TMA load (no multicast) into this CTA's shared memory, completing on `bar`; x is the
+// 2-D TMA load into this CTA's own shared memory, completing on `bar`; x is the
 // innermost coordinate.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
   asm volatile(
