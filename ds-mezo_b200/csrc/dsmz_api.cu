@@ -252,6 +252,14 @@ int tc_stages(int R) {
   return one > 4 ? 4 : one;
 }
 size_t tc_smem(int R) { return static_cast<size_t>(tc_stages(R)) * tc::stage_bytes(R) + 1024 + 512; }
+// Persistent W kernel (one CTA per SM): the ring takes what the fp64 staging region leaves.
+int pw_stages(int R) {
+  const int n = (227 * 1024 - 2048 - tc::w_stage_bytes(R)) / tc::stage_bytes(R);
+  return n > 6 ? 6 : n;
+}
+size_t pw_smem(int R) {
+  return static_cast<size_t>(pw_stages(R)) * tc::stage_bytes(R) + tc::w_stage_bytes(R) + 1024 + 512;
+}
 
 struct TCSlots {             // workspace byte offsets of one basis
   size_t v2t = 0, y2t = 0;
@@ -578,7 +586,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
   if (P->tc) {
     if ((rc = set_smem(tc::k_pi_tc<0>, tsm))) return rc;
-    if ((rc = set_smem(tc::k_pi_tc<1>, tsm))) return rc;
+    if ((rc = set_smem(tc::k_pi_w, pw_smem(R)))) return rc;
     if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
       P->probe_begin(DSMZ_KID_PI_SPLIT, s);
       tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
@@ -594,7 +602,8 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
       P->probe_end(DSMZ_KID_PI_Y, s);
       DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
       P->probe_begin(DSMZ_KID_PI_W, s);
-      tc::k_pi_tc<1><<<P->ntc_w, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
+      tc::k_pi_w<<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
+                                                                                  pw_stages(R), err);
       P->probe_end(DSMZ_KID_PI_W, s);
       DSMZ_LAUNCHED("power iteration W = H^T Y (tcgen05)");
     } else {

@@ -105,6 +105,49 @@ __host__ __device__ inline int tmem_cols(int n) {
 }
 __host__ __device__ inline int stage_bytes(int R) { return kBM * kBK * 2 + 2 * R * kBK * 2; }
 
+// Upper 8 x 8 blocks of a W tile's Gram W_tile^T W_tile on the fp64 MMA, accumulated over
+// rows staged in shared memory as fp64 (pitch tld); epilogue warp q (of four) owns the
+// blocks q, q + 4, ..., stored block-major (64 doubles each).
+struct TileGram {
+  int oa[kGramMaxBlocks], ob[kGramMaxBlocks];
+  bool on[kGramMaxBlocks];
+  double acc[kGramMaxBlocks][2];
+  int q, g, kq;
+  __device__ __forceinline__ TileGram(int tld, int R, int nq, int q_, int lane) : q(q_), g(lane >> 2), kq(lane & 3) {
+    const int nb = R >> 3;
+#pragma unroll
+    for (int u = 0; u < kGramMaxBlocks; ++u) {
+      int qq = q + 4 * u;
+      int bi = 0, bj = 0;
+      on[u] = qq < nq;
+      if (on[u]) {
+        while (qq >= nb - bi) { qq -= nb - bi; ++bi; }
+        bj = bi + qq;
+      }
+      oa[u] = kq * tld + 8 * bi + g;
+      ob[u] = kq * tld + 8 * bj + g;
+      acc[u][0] = 0.0; acc[u][1] = 0.0;
+    }
+  }
+  // rows [0, nrows) of the staged tile (nrows a multiple of 4)
+  __device__ __forceinline__ void rows(const double* wt, int tld, int nrows) {
+    for (int k0 = 0; k0 < nrows; k0 += 4) {        // all of a step's loads, then its MMAs
+      const double* wr = wt + k0 * tld;
+      double ca[kGramMaxBlocks], cb[kGramMaxBlocks];
+#pragma unroll
+      for (int u = 0; u < kGramMaxBlocks; ++u) { ca[u] = wr[oa[u]]; cb[u] = wr[ob[u]]; }
+#pragma unroll
+      for (int u = 0; u < kGramMaxBlocks; ++u)
+        if (on[u]) dmma8x8x4(acc[u][0], acc[u][1], ca[u], cb[u]);
+    }
+  }
+  __device__ __forceinline__ void store(double* gp) const {
+#pragma unroll
+    for (int u = 0; u < kGramMaxBlocks; ++u)
+      if (on[u]) *reinterpret_cast<double2*>(gp + (q + 4 * u) * 64 + g * 8 + 2 * kq) = make_double2(acc[u][0], acc[u][1]);
+  }
+};
+
 // MODE 0: Y2T = split(H V), tiles over T.  MODE 1: W = H^T Y, tiles over D.
 template <int MODE>
 __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restrict__ bases, int nb, int stages,
@@ -261,45 +304,213 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
         if (B->Gp != nullptr) {
-          const int g = lane >> 2, kq = lane & 3;
-          const int nb = R >> 3;
-          int bi[kGramMaxBlocks], bj[kGramMaxBlocks];
-          double acc[kGramMaxBlocks][2];
-#pragma unroll
-          for (int u = 0; u < kGramMaxBlocks; ++u) {
-            int qq = q + 4 * u;
-            bi[u] = -1; bj[u] = 0;
-            acc[u][0] = 0.0; acc[u][1] = 0.0;
-            if (qq < B->nq) {
-              int rb = 0;
-              while (qq >= nb - rb) { qq -= nb - rb; ++rb; }
-              bi[u] = rb; bj[u] = rb + qq;
-            }
-          }
-          int oa[kGramMaxBlocks], ob[kGramMaxBlocks];
-#pragma unroll
-          for (int u = 0; u < kGramMaxBlocks; ++u) {
-            oa[u] = kq * tld + 8 * (bi[u] < 0 ? 0 : bi[u]) + g;
-            ob[u] = kq * tld + 8 * bj[u] + g;
-          }
-          for (int k0 = 0; k0 < kBM; k0 += 4) {           // all of a step's loads, then its MMAs
-            const double* wr = wt + k0 * tld;
-            double ca[kGramMaxBlocks], cb[kGramMaxBlocks];
-#pragma unroll
-            for (int u = 0; u < kGramMaxBlocks; ++u) { ca[u] = wr[oa[u]]; cb[u] = wr[ob[u]]; }
-#pragma unroll
-            for (int u = 0; u < kGramMaxBlocks; ++u)
-              if (bi[u] >= 0) dmma8x8x4(acc[u][0], acc[u][1], ca[u], cb[u]);
-          }
-          double* gp = B->Gp + static_cast<int64_t>(tile) * B->nq * 64;
-#pragma unroll
-          for (int u = 0; u < kGramMaxBlocks; ++u) {
-            if (bi[u] < 0) continue;
-            const int qq = q + 4 * u;
-            *reinterpret_cast<double2*>(gp + qq * 64 + g * 8 + 2 * kq) = make_double2(acc[u][0], acc[u][1]);
-          }
+          TileGram gr(tld, R, B->nq, q, lane);
+          gr.rows(wt, tld, kBM);
+          gr.store(B->Gp + static_cast<int64_t>(tile) * B->nq * 64);
         }
       }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+// Shared-memory bytes of the fp64 staging region of the persistent W kernel's fused Gram
+// (R <= 64), beside the stage ring: one epilogue warp's 32 rows at a time.
+__host__ __device__ inline int w_stage_bytes(int R) { return R <= 64 ? 32 * w_stage_ld(R) * 8 : 0; }
+
+// Persistent W = H^T [Y_hi | Y_lo] (+ the fused fp64 Gram of each W tile for R <= 64).
+// One CTA per SM walks the W tiles of every basis, last basis first: the first tiles then
+// read the activations that the Y product read last, while they are still in L2. TMEM holds
+// two accumulators, so the epilogue of tile j (W rows stored from the accumulator, the tile
+// staged in fp64 and its Gram formed on the fp64 MMA) runs while the MMA warp accumulates
+// tile j + 1; the stage ring runs on across tiles. Every basis of a plan has the same R.
+//   warp 0     TMA producer (one lane)
+//   warp 1     TMEM owner + MMA issuer (one lane); buffer j & 1 for the CTA's j-th tile
+//   warps 2-5  epilogue; each frees its share of the buffer once its tcgen05.ld are done
+// Barriers per TMEM buffer: tfull (one commit per tile) and tempty (one arrival per
+// epilogue warp). Every wait is bounded; on an error each role stops, waits for its own
+// copies or MMAs in flight, and the CTA frees its TMEM.
+__global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restrict__ bases, int nb, int ntiles,
+                                                       int stages, int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
+  const int R = bases[0].R;
+  const int N = 2 * R;
+  const int sbytes = stage_bytes(R);
+  const int a_bytes = kBM * kBK * 2;
+  double* wt = reinterpret_cast<double*>(smem + stages * sbytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes + w_stage_bytes(R));
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;     // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int acc_cols = tmem_cols(N);
+  const int ncols = 2 * acc_cols;
+  const int G = gridDim.x;
+  const int nmine = (ntiles - static_cast<int>(blockIdx.x) + G - 1) / G;
+  auto item_of = [&](int j) { return ntiles - 1 - (static_cast<int>(blockIdx.x) + j * G); };
+  auto basis_of = [&](int item) { return find_owner(bases, nb, item, [](const TCBasis& b) { return b.wtile0; }); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 4); }
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;                        // k-steps issued (position in the ring)
+      int cur = -1;
+      bool ok = true;
+      for (int j = 0; j < nmine && ok; ++j) {
+        const int item = item_of(j);
+        const int bi = basis_of(item);
+        const TCBasis* B = bases + bi;
+        if (bi != cur) { tmap_acquire(&B->mapHw); tmap_acquire(&B->mapY2); cur = bi; }
+        const int tile = item - B->wtile0;
+        const int nk = static_cast<int>((B->T + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
+          const int s = g % stages;
+          const uint32_t u = static_cast<uint32_t>(g / stages);
+          if (g >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
+          unsigned char* As = smem + s * sbytes;
+          mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
+          tma_load_2d(As, &B->mapHw, tile * kBM, i * kBK, full + s);
+          tma_load_2d(As + a_bytes / 2, &B->mapHw, tile * kBM + 64, i * kBK, full + s);
+          tma_load_2d(As + a_bytes, &B->mapY2, i * kBK, 0, full + s);
+          ++g;
+        }
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA can exit
+        for (int i = (g > stages ? g - stages : 0); i < g; ++i)
+          mbar_drain(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(N, 1, 0);
+      int g = 0;
+      bool ok = true;
+      int last = -1;                    // the CTA's last tile whose accumulator was committed
+      for (int j = 0; j < nmine && ok; ++j) {
+        const int a = j & 1;
+        if (j >= 2 && !mbar_wait(tempty + a, static_cast<uint32_t>((j >> 1) - 1) & 1u, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dacc = tmem + static_cast<uint32_t>(a * acc_cols);
+        const TCBasis* B = bases + basis_of(item_of(j));
+        const int nk = static_cast<int>((B->T + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
+          const int s = g % stages;
+          if (!mbar_wait(full + s, static_cast<uint32_t>(g / stages) & 1u, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * sbytes);
+          const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // A: MN-major 64 x 8 atoms, two along MN 8 KB apart; B: K-major rows of 128 B
+            mma_bf16(dacc, sdesc(a0 + kk * 2048, 8192, 1024), sdesc(b0 + kk * 32, 16, 1024), idesc,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(empty + s);
+          ++g;
+        }
+        mma_commit(tfull + a);          // on an error too: it completes once the issued MMAs have
+        last = j;
+      }
+      if (!ok && last >= 0) mbar_drain(tfull + (last & 1), static_cast<uint32_t>(last >> 1) & 1u);
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int tld = w_stage_ld(R);
+    for (int j = 0; j < nmine; ++j) {
+      const int a = j & 1;
+      const bool mine = mbar_wait(tfull + a, static_cast<uint32_t>(j >> 1) & 1u, err);
+      // one verdict for the four epilogue warps, so none waits at a barrier the others skip
+      uint32_t all_ok;
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+          : "=r"(all_ok)
+          : "r"(static_cast<uint32_t>(mine))
+          : "memory");
+      if (all_ok == 0) break;
+      tc_fence_after();
+      const int item = item_of(j);
+      const TCBasis* B = bases + basis_of(item);
+      const int tile = item - B->wtile0;
+      const bool gram = B->Gp != nullptr;
+      const uint32_t trow = tmem + static_cast<uint32_t>(a * acc_cols) + (static_cast<uint32_t>(q * 32) << 16);
+      const int64_t d0 = static_cast<int64_t>(tile) * kBM;
+      const bool live = d0 + row < B->D;
+      float* wrow = B->W + (d0 + row) * R;
+      if (!gram) {
+        for (int c0 = 0; c0 < R; c0 += 16) {
+          float hi[16], lo[16];
+          tmem_ld16(trow + c0, hi);
+          tmem_ld16(trow + R + c0, lo);
+#pragma unroll
+          for (int c = 0; c < 16; c += 4)
+            if (live)
+              *reinterpret_cast<float4*>(wrow + c0 + c) =
+                  make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty + a);    // this warp's lanes of the buffer are read
+        continue;
+      }
+      // R <= 64: the row stays in registers; the buffer is released before the Gram
+      float w[64];
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        if (c0 < R) {
+          float hi[16], lo[16];
+          tmem_ld16(trow + c0, hi);
+          tmem_ld16(trow + R + c0, lo);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) w[c0 + c] = hi[c] + lo[c];
+#pragma unroll
+          for (int c = 0; c < 16; c += 4)
+            if (live) *reinterpret_cast<float4*>(wrow + c0 + c) = make_float4(w[c0 + c], w[c0 + c + 1], w[c0 + c + 2], w[c0 + c + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + a);
+      // Gram over the tile's four 32-row quarters, one epilogue warp's rows staged at a time
+      // (rows past D are zero: the H box there is zero filled)
+      TileGram gr(tld, R, B->nq, q, lane);
+#pragma unroll 1
+      for (int r = 0; r < 4; ++r) {
+        if (q == r) {
+          double* st = wt + lane * tld;
+#pragma unroll
+          for (int c = 0; c < 64; c += 2)
+            if (c < R) *reinterpret_cast<double2*>(st + c) = make_double2(w[c], w[c + 1]);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // the quarter is staged
+        gr.rows(wt, tld, 32);
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // the staging region is free again
+      }
+      gr.store(B->Gp + static_cast<int64_t>(tile) * B->nq * 64);
     }
   }
   tc_fence_before();
