@@ -532,7 +532,7 @@ bool choose_qr_layout(dsmz_plan* P) {
   for (int tv = sk::stream_tv(P->R); tv >= 8 && !ok; tv -= 8) {    // QR apply: widest tile that fits
     if (sk::qr_variant(tv, P->R) < 0) continue;
     P->Lq = sk::qr_layout(P->R, kStreamSmem, tv);
-    ok = P->Lq.S >= 2 && P->Lq.total <= kStreamSmem + 2048;
+    ok = P->Lq.S >= sk::kQrGroups && P->Lq.total <= kStreamSmem + 2048;
   }
   if (!ok) return false;
   for (int tv = sk::stream_tv(P->R); tv >= 8; tv = (tv / 2) & ~7) {    // Gram of W (plain)
@@ -635,10 +635,10 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     DSMZ_LAUNCHED("power iteration Cholesky");
     P->probe_begin(DSMZ_KID_PI_APPLY, s);
     switch (sk::qr_variant(P->Lq.TV, P->R)) {
-      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kSTP, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
+      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
     }
     P->probe_end(DSMZ_KID_PI_APPLY, s);
     DSMZ_LAUNCHED("power iteration V = W R^-1");

@@ -41,6 +41,12 @@ constexpr int kTeams = 4;                // perturb / apply / QR apply
 // phase it consumed itself there (a stage two phases behind would alias on the phase
 // parity). The team kernels' layouts round S down to a multiple of kTeams.
 constexpr int kTT = kCT / kTeams;        // threads per team (two warps)
+// QR apply: four groups of four consumer warps take tiles i % kQrGroups (four consumer
+// warps per scheduler, to hide the fp64 MMA and shared-memory latencies of its short tiles).
+constexpr int kQrGroups = 4;
+constexpr int kQrGroupWarps = 4;
+constexpr int kQrCT = 32 * kQrGroups * kQrGroupWarps;   // consumer threads
+constexpr int kQrThreads = kQrCT + 32 * kProd;
 constexpr int kBarAll = 1;               // named barrier: all consumer threads (one role)
 // Role-split fp64 Gram: producer warp, prep warps, MMA warps.
 constexpr int kPrepWarps = 4, kMmaWarps = 8;
@@ -576,9 +582,9 @@ __host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int T
   return L;
 }
 
-// QR apply: W rows as a swizzled row image per stage (an even number of stages, at most 8);
+// QR apply: W rows as a swizzled row image per stage (a multiple of kQrGroups stages, at most 8);
 // fp64 R^{-1} zero-padded to rp x pld (rp = R rounded up to 8, pld = rp + 4: each half-warp's
-// B fragment on distinct banks); four fp32 result tiles (TV x zp, zp = rp + 1), two per group.
+// B fragment on distinct banks); two fp32 result tiles (TV x zp, zp = rp + 1) per group.
 __host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   Layout L{};
   L.r = R;
@@ -590,14 +596,14 @@ __host__ __device__ inline Layout qr_layout(int R, int budget, int TV) {
   L.pld = rp + 4;
   L.zp = rp + 1;
   const int osz = al128(TV * L.zp * 4);
-  const int fixed = al128(rp * L.pld * 8) + 4 * osz + 2048;
+  const int fixed = al128(rp * L.pld * 8) + 2 * kQrGroups * osz + 2048;
   int S = (budget - fixed) / L.stage_bytes;
-  S = S > 8 ? 8 : S & ~1;
+  S = S > 8 ? 8 : S - S % kQrGroups;               // each stage serves one consumer group
   L.S = S;
   L.fixed0 = S * L.stage_bytes;
   L.o_c = L.fixed0;
   L.o_z = L.o_c + al128(rp * L.pld * 8);
-  L.o_bar = L.o_z + 4 * osz;
+  L.o_bar = L.o_z + 2 * kQrGroups * osz;
   L.total = L.o_bar + 2 * 8 * S + 1024 + 128;
   return L;
 }
@@ -1050,8 +1056,8 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
 // CholeskyQR apply of the power iteration: V = W R^{-1} in fp64 (R^{-1}, upper
 // triangular, exported by k_chol after the fp64 workspace's first r*r doubles), V rows out
 // and, when the next product runs on the tensor cores, [V_hi | V_lo]^T (bf16, 2R x D).
-// Two groups of four warps take alternate tiles straight from the ring (an even number
-// of stages, so each stage has one consumer group). In a group each warp owns MV row
+// Four groups of four warps take tiles i % 4 straight from the ring (a multiple of four
+// stages, so each stage has one consumer group). In a group each warp owns MV row
 // blocks x MC column blocks of 8 x 8 and forms them with the fp64 MMA: A fragments are
 // fp32 W read from the stage and widened in registers, B fragments R^{-1} in fp64. Column
 // blocks are dealt snake-wise (ascending per warp), so the k-extent of block column cb
@@ -1060,8 +1066,6 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
 // the bf16 pair goes through an fp32 tile per group (two, alternating), eight vectors per
 // thread and 16-byte stores. Waits are bounded; a group agrees on each tile's verdict.
 // =====================================================================================
-constexpr int kQrGroups = 2;
-constexpr int kQrGroupWarps = kCW / kQrGroups;
 
 // Warp shape of the QR apply for tiles of TV vectors and width R: the first of
 // (MV, MC) = (2,4), (4,2), (1,8), (8,1) whose warp grid fits a group; -1 if none.
@@ -1089,14 +1093,14 @@ __device__ __forceinline__ void bf16_pair8(const float* x, uint4& hi, uint4& lo)
 }
 
 template <int MV, int MC>
-__global__ void __launch_bounds__(kSTP, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
+__global__ void __launch_bounds__(kQrThreads, 1) k_sqr_apply(Tables tb, const MatD* __restrict__ mats, int nmats,
                                                       int nsegs, Layout L, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
   uint64_t* empty = full + L.S;
   double* Ps = reinterpret_cast<double*>(smem + L.o_c);        // rp x pld fp64 R^{-1}
-  const int osz = (L.o_bar - L.o_z) / 16;                       // floats per fp32 tile (four)
+  const int osz = (L.o_bar - L.o_z) / (8 * kQrGroups);           // floats per fp32 tile (two per group)
   if (threadIdx.x == 0) {
     for (int i = 0; i < L.S; ++i) { mbar_init(full + i, kFullArrivals); mbar_init(empty + i, kQrGroupWarps); }
     mbar_init_fence();
@@ -1138,16 +1142,16 @@ __global__ void __launch_bounds__(kSTP, 1) k_sqr_apply(Tables tb, const MatD* __
     const MatD& M = it.mats[it.mi];
     const int r = static_cast<int>(M.r), nv = it.nv();
     if (it.mi != cur) {                            // R^{-1} of this basis (both groups)
-      named_sync(kBarAll, kCT);
+      named_sync(kBarAll, kQrCT);
       const double* Rd = reinterpret_cast<const double*>(tb.ws) + M.dw_off + static_cast<int64_t>(r) * r;
-      for (int e = ct; e < L.rp * L.pld; e += kCT) {
+      for (int e = ct; e < L.rp * L.pld; e += kQrCT) {
         const int a2 = e / L.pld, c = e - a2 * L.pld;
         Ps[e] = (a2 < r && c < r) ? Rd[a2 * r + c] : 0.0;
       }
-      named_sync(kBarAll, kCT);
+      named_sync(kBarAll, kQrCT);
       cur = it.mi;
     }
-    if ((i & 1) == grp) {
+    if ((i % kQrGroups) == grp) {
       const int s = i % L.S;
       const bool w = dead ? false : mbar_wait(full + s, static_cast<uint32_t>(i / L.S) & 1u, err);
       dead = !agree(kBarTeam0 + grp, 32 * kQrGroupWarps, w);
