@@ -232,17 +232,16 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
 
 int tc_stages(int R);
 
+int pw_stages(int R);
+
 // Shapes the tcgen05 products take: bf16 H with 16-byte rows, R a multiple of 16 (N = 2R),
-// and a stage ring large enough to hold the fp64 W tile (128 x w_stage_ld(R) doubles) that
-// the W kernel's epilogue stages over it for the fused Gram.
+// and room for a ring of at least two stages beside the persistent W kernel's fp64 staging.
 bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, const void* H) {
   return hdt == DSMZ_BF16 && h_s1 == 1 && D % 8 == 0 && ld_H % 8 == 0 && R % 16 == 0 && R <= DSMZ_MAX_RANK &&
-         (reinterpret_cast<uintptr_t>(H) & 15) == 0 &&
-         static_cast<int64_t>(tc::kBM) * tc::w_stage_ld(static_cast<int>(R)) * 8 <=
-             static_cast<int64_t>(tc_stages(static_cast<int>(R))) * tc::stage_bytes(static_cast<int>(R));
+         (reinterpret_cast<uintptr_t>(H) & 15) == 0 && pw_stages(static_cast<int>(R)) >= 2;
 }
 
-// Ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
+// Y product ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
 int tc_stages(int R) {
   const int sb = tc::stage_bytes(R);
   const int half = (227 * 1024) / 2 - 2048;
@@ -585,7 +584,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const bool fused = P->tc && R <= 64;                 // W Gram formed in the W epilogue
   const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
   if (P->tc) {
-    if ((rc = set_smem(tc::k_pi_tc<0>, tsm))) return rc;
+    if ((rc = set_smem(tc::k_pi_y, tsm))) return rc;
     if ((rc = set_smem(tc::k_pi_w, pw_smem(R)))) return rc;
     if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
       P->probe_begin(DSMZ_KID_PI_SPLIT, s);
@@ -598,7 +597,7 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   for (int it = 0; it < iters; ++it) {
     if (P->tc) {
       P->probe_begin(DSMZ_KID_PI_Y, s);
-      tc::k_pi_tc<0><<<P->ntc_y, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
+      tc::k_pi_y<<<P->ntc_y, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
       P->probe_end(DSMZ_KID_PI_Y, s);
       DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
       P->probe_begin(DSMZ_KID_PI_W, s);

@@ -6,10 +6,11 @@
 // pair, B = [X_hi | X_lo] with N = 2R columns, and add the two halves of the fp32 TMEM
 // accumulator in the epilogue (sine ~1e-5 against the exact algorithm).
 //
-// One CTA computes one 128-row output tile:
+// Both kernels run six warps:
 //   warp 0     TMA producer (one lane): A and B tiles into a ring of smem stages
 //   warp 1     TMEM owner + MMA issuer (one lane): tcgen05.mma kind::f16, M=128, N=2R
 //   warps 2-5  epilogue: tcgen05.ld of the 128 x 2R fp32 accumulator, hi+lo, stores
+// k_pi_y computes one 128-token tile of Y per CTA; k_pi_w is persistent over the W tiles.
 // Every mbarrier wait gives up after ~1 s of globaltimer, sets the error word and lets
 // the CTA drain and free its TMEM.
 #pragma once
@@ -148,22 +149,19 @@ struct TileGram {
   }
 };
 
-// MODE 0: Y2T = split(H V), tiles over T.  MODE 1: W = H^T Y, tiles over D.
-template <int MODE>
-__global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restrict__ bases, int nb, int stages,
-                                                         int* err) {
+// Y2T = split(H [V_hi | V_lo]): one 128-token tile per CTA, two CTAs per SM.
+__global__ void __launch_bounds__(kThreadsTC, 2) k_pi_y(const TCBasis* __restrict__ bases, int nb, int stages,
+                                                       int* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned base for the swizzled stages
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
   const int item = blockIdx.x;
-  const int bi = (MODE == 0) ? find_owner(bases, nb, item, [](const TCBasis& b) { return b.ytile0; })
-                             : find_owner(bases, nb, item, [](const TCBasis& b) { return b.wtile0; });
+  const int bi = find_owner(bases, nb, item, [](const TCBasis& b) { return b.ytile0; });
   const TCBasis* B = bases + bi;
   const int R = B->R;
   const int N = 2 * R;
-  const int tile = item - ((MODE == 0) ? B->ytile0 : B->wtile0);
-  const int64_t K = (MODE == 0) ? B->D : B->T;
-  const int nk = static_cast<int>((K + kBK - 1) / kBK);
+  const int tile = item - B->ytile0;
+  const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
   const int sbytes = stage_bytes(R);
   const int a_bytes = kBM * kBK * 2;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes);
@@ -191,10 +189,8 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
 
   if (warp == 0) {
     if (lane == 0) {
-      const CUtensorMap* mA = (MODE == 0) ? &B->mapHy : &B->mapHw;
-      const CUtensorMap* mB = (MODE == 0) ? &B->mapV2 : &B->mapY2;
-      tmap_acquire(mA);
-      tmap_acquire(mB);
+      tmap_acquire(&B->mapHy);
+      tmap_acquire(&B->mapV2);
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
@@ -202,15 +198,9 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
         const uint32_t u = static_cast<uint32_t>(i / stages);
         if (i >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
         unsigned char* As = smem + s * sbytes;
-        unsigned char* Bs = As + a_bytes;
         mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
-        if (MODE == 0) {
-          tma_load_2d(As, mA, i * kBK, tile * kBM, full + s);
-        } else {
-          tma_load_2d(As, mA, tile * kBM, i * kBK, full + s);
-          tma_load_2d(As + a_bytes / 2, mA, tile * kBM + 64, i * kBK, full + s);
-        }
-        tma_load_2d(Bs, mB, i * kBK, 0, full + s);
+        tma_load_2d(As, &B->mapHy, i * kBK, tile * kBM, full + s);
+        tma_load_2d(As + a_bytes, &B->mapV2, i * kBK, 0, full + s);
         issued = i + 1;
       }
       if (!ok) {
@@ -221,7 +211,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(N, MODE == 1 ? 1 : 0, 0);
+      const uint32_t idesc = idesc_bf16(N, 0, 0);
       bool ok = true;
       int done = 0;
       for (int i = 0; i < nk; ++i) {
@@ -231,12 +221,9 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
         const uint32_t a0 = smem_u32(smem + s * sbytes);
         const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          // A: K-major rows of 128 B (MODE 0) or MN-major 64 x 8 atoms, two along MN 8 KB apart (MODE 1)
-          const uint64_t ad = (MODE == 0) ? sdesc(a0 + kk * 32, 16, 1024) : sdesc(a0 + kk * 2048, 8192, 1024);
-          const uint64_t bd = sdesc(b0 + kk * 32, 16, 1024);
-          mma_bf16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBK / 16; ++kk)       // A and B: K-major rows of 128 B
+          mma_bf16(tmem, sdesc(a0 + kk * 32, 16, 1024), sdesc(b0 + kk * 32, 16, 1024), idesc,
+                   (i > 0 || kk > 0) ? 1u : 0u);
         mma_commit(empty + s);
         done = i + 1;
       }
@@ -255,58 +242,23 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_tc(const TCBasis* __restri
         : "=r"(all_ok)
         : "r"(static_cast<uint32_t>(mine))
         : "memory");
-    const bool ok = all_ok != 0;
     tc_fence_after();
-    if (ok) {
+    if (all_ok != 0) {
       const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
-      if (MODE == 0) {
-        const int64_t t = static_cast<int64_t>(tile) * kBM + row;
-        for (int j = 0; j < R; j += 16) {
-          float hi[16], lo[16];
-          tmem_ld16(trow + j, hi);
-          tmem_ld16(trow + R + j, lo);
-          if (t < B->T) {
+      const int64_t t = static_cast<int64_t>(tile) * kBM + row;
+      for (int j = 0; j < R; j += 16) {
+        float hi[16], lo[16];
+        tmem_ld16(trow + j, hi);
+        tmem_ld16(trow + R + j, lo);
+        if (t < B->T) {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              const float y = hi[c] + lo[c];
-              const __nv_bfloat16 yh = __float2bfloat16_rn(y);
-              const __nv_bfloat16 yl = __float2bfloat16_rn(y - __bfloat162float(yh));
-              B->Y2T[static_cast<int64_t>(j + c) * B->ldy2 + t] = yh;
-              B->Y2T[static_cast<int64_t>(R + j + c) * B->ldy2 + t] = yl;
-            }
+          for (int c = 0; c < 16; ++c) {
+            const float y = hi[c] + lo[c];
+            const __nv_bfloat16 yh = __float2bfloat16_rn(y);
+            const __nv_bfloat16 yl = __float2bfloat16_rn(y - __bfloat162float(yh));
+            B->Y2T[static_cast<int64_t>(j + c) * B->ldy2 + t] = yh;
+            B->Y2T[static_cast<int64_t>(R + j + c) * B->ldy2 + t] = yl;
           }
-        }
-      } else {
-        // Each thread stores its W row straight from the accumulator (hi + lo, 16-byte
-        // stores). With Gp, the pipeline stages (drained: every MMA completed before
-        // tmem_full) take the tile as fp64 (rows of w_stage_ld(R) doubles) and the four warps
-        // form its Gram W_tile^T W_tile on the fp64 MMA (rows past D are zero: the H box
-        // there is zero filled); each warp owns the upper blocks q = warp, warp + 4, ...
-        double* wt = reinterpret_cast<double*>(smem);
-        const int tld = w_stage_ld(R);
-        const int64_t d0 = static_cast<int64_t>(tile) * kBM;
-        const bool live = d0 + row < B->D;
-        float* wrow = B->W + (d0 + row) * R;
-        for (int j = 0; j < R; j += 16) {
-          float hi[16], lo[16];
-          tmem_ld16(trow + j, hi);
-          tmem_ld16(trow + R + j, lo);
-#pragma unroll
-          for (int c = 0; c < 16; c += 4) {
-            const float4 w4 = make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
-            if (live) *reinterpret_cast<float4*>(wrow + j + c) = w4;
-            if (B->Gp != nullptr) {
-              double2* st = reinterpret_cast<double2*>(wt + row * tld + j + c);
-              st[0] = make_double2(w4.x, w4.y);
-              st[1] = make_double2(w4.z, w4.w);
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");   // the four epilogue warps
-        if (B->Gp != nullptr) {
-          TileGram gr(tld, R, B->nq, q, lane);
-          gr.rows(wt, tld, kBM);
-          gr.store(B->Gp + static_cast<int64_t>(tile) * B->nq * 64);
         }
       }
     }
