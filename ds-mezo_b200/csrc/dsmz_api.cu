@@ -111,6 +111,31 @@ void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bo
   mats.push_back(m);
 }
 
+// B-side sums: the modules' d_in columns, concatenated in module order, are cut into G
+// equal contiguous ranges, one per CTA (G no larger than the column count, so none is
+// empty). Each module gets its first column col0, the first CTA whose range meets it
+// (chunk0), the number of such CTAs (nchunk, one partial each, summed in order by
+// k_coef) and room for those partials.
+void plan_bside(std::vector<ModD>& mods, int G, Layout& ws, int* grid, int64_t* ncols) {
+  int64_t total = 0;
+  for (ModD& m : mods) { m.col0 = total; total += m.d_in; }
+  if (G > total) G = static_cast<int>(total);
+  if (G < 1) G = 1;
+  auto start = [&](int64_t b) { return b * total / G; };   // first column of CTA b
+  int b = 0;
+  for (ModD& m : mods) {
+    while (b + 1 < G && start(b + 1) <= m.col0) ++b;     // the CTA holding column col0
+    int e = b;
+    while (e + 1 < G && start(e + 1) < m.col0 + m.d_in) ++e;   // the CTA holding the last column
+    m.chunk0 = b;
+    m.nchunk = e - b + 1;
+    const size_t nB = static_cast<size_t>(m.r) * m.rc;
+    m.bpart_off = static_cast<int64_t>(ws.take(static_cast<size_t>(m.nchunk) * 2 * nB * sizeof(float)) / sizeof(float));
+  }
+  *grid = G;
+  *ncols = total;
+}
+
 // Streaming-kernel schedule of a matrix list: TV-vector tiles numbered across the list,
 // cut into G = min(max_ctas, T) contiguous chunks (one per CTA, [c*T/G, (c+1)*T/G)), so no
 // chunk is empty and every chunk between two that touch a matrix lies inside it; a segment
@@ -281,6 +306,7 @@ struct dsmz_plan {
   char* dev_tables = nullptr;
   char* workspace = nullptr;
   int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
+  int64_t bside_cols = 0;   // concatenated d_in columns of the B-side sums (nchunks CTAs over them)
   int sm_count = 0;
   int grid_m = 0, grid_w = 0, grid_w1 = 0;   // streaming-kernel grids (chunks) of mats, w2, w1
   int ndir = 1;                      // SPSA directions per step
@@ -706,7 +732,7 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   if ((rc = set_smem(sk::k_sperturb<0, 2>, P->Lp.total))) return rc;
   if ((rc = set_smem(sk::k_sperturb<0, 4>, P->Lp.total))) return rc;
   P->probe_begin(DSMZ_KID_BSIDE, s);
-  k_bside<<<P->nchunks, kThreads, 0, s>>>(tb);     // B V and var_B V^2: the same for every direction
+  k_bside<<<P->nchunks, kThreads, 0, s>>>(tb, P->bside_cols);     // B V and var_B V^2: the same for every direction
   P->probe_end(DSMZ_KID_BSIDE, s);
   DSMZ_LAUNCHED("B-side sums");
   for (int k = 0; k < P->ndir; ++k) {
@@ -930,12 +956,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     off += dsmz_randn_offset_increment(nB, d->sm_count, d->max_threads_per_sm);
     md.offA = off;
     off += dsmz_randn_offset_increment(nA, d->sm_count, d->max_threads_per_sm);
-    md.chunkw = 2048;
-    md.nchunk = static_cast<int32_t>((m.d_in + md.chunkw - 1) / md.chunkw);
-    md.chunk0 = P->nchunks;
-    P->nchunks += md.nchunk;
     md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
-    md.bpart_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(md.nchunk) * 2 * nB * sizeof(float)) / sizeof(float));
     md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1; md.bdt = d->factor_dtype;
     md.zca_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(nA) * sizeof(float)) / sizeof(float));
     md.dblk0 = P->ndblk;
@@ -953,6 +974,8 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     add_matrix(P->mats, P->ws, b, P->nsegs, true, false);
     P->mods.push_back(md);
   }
+  // B-side sums: two CTAs per SM over the modules' concatenated d_in columns
+  plan_bside(P->mods, 2 * P->sm_count, P->ws, &P->nchunks, &P->bside_cols);
   P->rng_inc1 = off - d->rng_offset_before;
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
@@ -1296,15 +1319,12 @@ static dsmz_plan agzo_plan(int64_t R, int64_t d_in, int64_t RC, int64_t d_out) {
   ModD md{};
   md.r = static_cast<int32_t>(R); md.rc = static_cast<int32_t>(RC); md.rca = rca;
   md.d_out = d_out; md.d_in = d_in; md.basis = 0;
-  md.chunkw = 2048;
-  md.nchunk = static_cast<int32_t>((d_in + md.chunkw - 1) / md.chunkw);
-  md.chunk0 = 0;
-  P.nchunks = md.nchunk;
   const size_t nB = static_cast<size_t>(R) * RC;
   md.coef_off = static_cast<int64_t>(P.ws.take((nB + static_cast<size_t>(R) * rca) * sizeof(float)) / sizeof(float));
-  md.bpart_off = static_cast<int64_t>(P.ws.take(md.nchunk * 2 * nB * sizeof(float)) / sizeof(float));
   md.a = 0; md.b = 1;
   P.mods.push_back(md);
+  // one CTA per 2048 columns (the device is not known yet)
+  plan_bside(P.mods, static_cast<int>((d_in + 2047) / 2048), P.ws, &P.nchunks, &P.bside_cols);
   MatD a{};
   a.nvec = d_out; a.r = R; a.ld = R; a.cs = 1; a.side = 0; a.owner = 0;
   add_matrix(P.mats, P.ws, a, P.nsegs, false);
@@ -1353,7 +1373,7 @@ int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t bs0,
   const size_t ps = perturb_smem(static_cast<int>(R), static_cast<int>(R), static_cast<int>(RC));
   if ((rc = set_smem(k_coef<1>, cs))) return rc;
   if ((rc = set_smem(k_perturb<1>, ps))) return rc;
-  k_bside<<<P.nchunks, kThreads, 0, s>>>(tb);
+  k_bside<<<P.nchunks, kThreads, 0, s>>>(tb, P.bside_cols);
   DSMZ_LAUNCHED("agzo B V");
   k_coef<1><<<1, kThreads, cs, s>>>(tb, 0, 0, norm_floor, 1);
   DSMZ_LAUNCHED("agzo QR");

@@ -45,8 +45,9 @@ struct ModD {
   int64_t d_out, d_in;
   uint64_t offB, offA;        // generator offsets of the two draws, relative to the step base
   int64_t thrB, thrA;         // torch launch width (threads) of each draw
-  int32_t chunk0, nchunk;     // B-side reduction chunks
-  int32_t chunkw, pad0;       // columns per chunk
+  int32_t chunk0, nchunk;     // B-side sums: first CTA whose column range meets this module, and
+                              // the number of such CTAs (one partial each)
+  int64_t col0;               // first column of this module in the concatenated d_in columns
   int64_t coef_off;           // floats: Zc_B (r*rc) then Q (r*rca)
   int64_t bpart_off;          // floats: nchunk * 2 * r*rc partial sums (B V, var_B V^2)
   const float* zcB_ext;       // explicit Zc_B (R x RC) / Zc_A (d_out x RCA) for the drop-in op

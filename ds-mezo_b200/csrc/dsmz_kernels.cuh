@@ -831,31 +831,47 @@ __device__ __forceinline__ float ldg_l2pf(const void* p, int64_t i, int dt) {
   }
   return ldg_l2pf(reinterpret_cast<const float*>(p) + i);
 }
-__global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb) {
-  __shared__ __align__(16) float Bs[kBsJ][kBsP];
-  __shared__ __align__(16) float Ws[kBsJ][kBsP];
-  __shared__ __align__(16) float Vs[kBsJ][kBsP];
-  __shared__ __align__(16) float Qs[kBsJ][kBsP];
-  const int item = blockIdx.x;
-  const int mi = find_owner(tb.mods, tb.nmods, item, [](const ModD& d) { return d.chunk0; });
+__global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb, int64_t ncols) {
+  __shared__ __align__(16) float sh[4][kBsJ][kBsP];
+  float (*Bs)[kBsP] = sh[0];
+  float (*Ws)[kBsP] = sh[1];
+  float (*Vs)[kBsP] = sh[2];
+  float (*Qs)[kBsP] = sh[3];
+  static_assert(4 * kBsJ * kBsP >= 2 * 64 * 64, "the parity reduction reuses the operand tiles");
+  const int tid = threadIdx.x;
+  // Four groups of 64 threads: group g forms product g & 1 (B V, or var_B V^2) over the
+  // columns jj of parity g >> 1. A thread holds rows {4bi..4bi+3, 32+4bi..} x columns
+  // {4bj..4bj+3, 32+4bj..} of the 64 x 64 block: per jj, four 16-byte shared loads (each
+  // quarter-warp reads 128 contiguous bytes) feed 64 FMAs.
+  const int grp = tid >> 6, lt = tid & 63;
+  const int pr = grp & 1, hp = grp >> 1;
+  const int bi = lt >> 3, bj = lt & 7;
+  // this CTA's range of the concatenated d_in columns, and the modules it meets
+  const int64_t G = gridDim.x, cb = blockIdx.x;
+  const int64_t g0 = cb * ncols / G, g1 = (cb + 1) * ncols / G;
+  int mi = 0;
+  for (int lo = 0, hi = tb.nmods - 1; lo <= hi;) {   // last module with col0 <= g0
+    const int mid = (lo + hi) >> 1;
+    if (tb.mods[mid].col0 <= g0) { mi = mid; lo = mid + 1; } else { hi = mid - 1; }
+  }
+  for (; mi < tb.nmods && tb.mods[mi].col0 < g1; ++mi) {
   const ModD D = tb.mods[mi];
   const BasisD Bd = tb.bases[D.basis];
-  const int chunk = item - D.chunk0;
+  const int chunk = static_cast<int>(cb) - D.chunk0;  // this CTA's partial slot of the module
   const int R = D.r, RC = D.rc;
-  const int64_t j0 = static_cast<int64_t>(chunk) * D.chunkw;
-  const int64_t j1 = min(j0 + static_cast<int64_t>(D.chunkw), D.d_in);
+  const int64_t j0 = max(g0, D.col0) - D.col0;
+  const int64_t j1 = min(g1, D.col0 + D.d_in) - D.col0;
   const bool with_var = (D.varB != nullptr);
-  const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
   const float* V = Bd.Vin;
   const int64_t vs0 = Bd.v_s0, vs1 = Bd.v_s1;
   float* outp = reinterpret_cast<float*>(tb.ws) + D.bpart_off + static_cast<int64_t>(chunk) * 2 * R * RC;
   for (int rt = 0; rt < R; rt += 64) {
     for (int ct = 0; ct < RC; ct += 64) {
-      float abv[4][4], avb[4][4];
+      float acc[8][8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { abv[i][j] = 0.f; avb[i][j] = 0.f; }
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
       float lb[8], lw[8], lv[8];
       auto gload = [&](int64_t jb) {                // 24 independent loads per thread
 #pragma unroll
@@ -891,39 +907,47 @@ __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb) {
         }
         __syncthreads();
         if (jb + kBsJ < j1) gload(jb + kBsJ);
+        const float (*As)[kBsP] = pr ? Ws : Bs;
+        const float (*Cs)[kBsP] = pr ? Qs : Vs;
 #pragma unroll 4
-        for (int jj = 0; jj < kBsJ; ++jj) {
-          const float4 b = *reinterpret_cast<const float4*>(&Bs[jj][ti * 4]);
-          const float4 w = *reinterpret_cast<const float4*>(&Ws[jj][ti * 4]);
-          const float4 v = *reinterpret_cast<const float4*>(&Vs[jj][tj * 4]);
-          const float4 q = *reinterpret_cast<const float4*>(&Qs[jj][tj * 4]);
-          const float bb[4] = {b.x, b.y, b.z, b.w}, ww[4] = {w.x, w.y, w.z, w.w};
-          const float vv[4] = {v.x, v.y, v.z, v.w}, qq[4] = {q.x, q.y, q.z, q.w};
+        for (int jj = hp; jj < kBsJ; jj += 2) {
+          const float4 a0 = *reinterpret_cast<const float4*>(&As[jj][4 * bi]);
+          const float4 a1 = *reinterpret_cast<const float4*>(&As[jj][32 + 4 * bi]);
+          const float4 c0 = *reinterpret_cast<const float4*>(&Cs[jj][4 * bj]);
+          const float4 c1 = *reinterpret_cast<const float4*>(&Cs[jj][32 + 4 * bj]);
+          const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              abv[i][j] = fmaf(bb[i], vv[j], abv[i][j]);
-              avb[i][j] = fmaf(ww[i], qq[j], avb[i][j]);
-            }
+            for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], cv[j], acc[i][j]);
         }
       }
+      // the odd-column groups hand their sums to the even-column groups, which write
+      float* red = &sh[0][0][0];
+      __syncthreads();
+      if (hp == 1) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int e = 0; e < 64; ++e) red[pr * 4096 + e * 64 + lt] = acc[e >> 3][e & 7];
+      }
+      __syncthreads();
+      if (hp == 0) {
+        float* o = outp + pr * R * RC;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int rr = rt + ti * 4 + i, cc = ct + tj * 4 + j;
-          if (rr < R && cc < RC) {
-            outp[rr * RC + cc] = abv[i][j];
-            outp[R * RC + rr * RC + cc] = avb[i][j];
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int rr = rt + (i < 4 ? 4 * bi + i : 28 + 4 * bi + i);
+            const int cc = ct + (j < 4 ? 4 * bj + j : 28 + 4 * bj + j);
+            if (rr < R && cc < RC) o[rr * RC + cc] = acc[i][j] + red[pr * 4096 + (i * 8 + j) * 64 + lt];
           }
-        }
+      }
       __syncthreads();                              // the tiles are rewritten by the next block
     }
   }
+  }
 }
 
-// =====================================================================================
 // Per module: sum the chunk partials (fp64), Zc_B = randn(R,RC) * sqrt(var_B V^2)
 // (controller.py:183-186), and Q = MGS(B V)[:, :RCA] (ds_mezo/kernels.py:328-340) in fp64
 // by one warp. MODE 0 draws Zc_B from the torch Philox stream, MODE 1 copies it.
