@@ -369,6 +369,48 @@ def main():
         e2e = {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": host_H.numel() * host_H.element_size(),
                "d2h_bytes_per_step": host_out.numel() * 8, "steps": n_e2e}
 
+    # device-resident activation handoff: every basis's fp32 forward-hook capture converted
+    # into the bf16 activation buffer on the device (a distinct capture per basis, so nothing
+    # is served from L2), against the reference's pinned-host round trip of the same bytes
+    # (timed on the largest capture and scaled by bytes)
+    handoff = None
+    if not args.no_e2e and world == 1:
+        hgen = torch.Generator(device=device).manual_seed(cfg["seed"] + 1)
+        caps = [torch.randn(b.T, b.D, generator=hgen, device=device) for b in aset.bases]
+        hbytes = sum(c.numel() * (4 + aset.H_arena.element_size()) for c in caps)
+        for i, c in enumerate(caps):
+            aset.load_activations(i, c)
+        h0 = torch.cuda.Event(enable_timing=True)
+        h1 = torch.cuda.Event(enable_timing=True)
+        n_h = 3
+        torch.cuda.synchronize()
+        h0.record()
+        for _ in range(n_h):
+            for i, c in enumerate(caps):
+                aset.load_activations(i, c)
+        h1.record()
+        torch.cuda.synchronize()
+        h_ms = h0.elapsed_time(h1) / n_h
+        big = max(caps, key=lambda c: c.numel())
+        pinned = torch.empty(big.shape, dtype=big.dtype, pin_memory=True)
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        pinned.copy_(big, non_blocking=True)
+        big.copy_(pinned, non_blocking=True)
+        torch.cuda.synchronize()
+        r0.record()
+        pinned.copy_(big, non_blocking=True)       # ds_mezo/backend.py:85-86
+        big.copy_(pinned, non_blocking=True)       # ds_mezo/controller.py:171
+        r1.record()
+        torch.cuda.synchronize()
+        ref_ms = r0.elapsed_time(r1) * sum(c.numel() for c in caps) / big.numel()
+        handoff = {"ms_per_step": h_ms, "bytes_per_step": hbytes, "achieved_GBps": hbytes / (h_ms * 1e-3) / 1e9,
+                   "frac": hbytes / (h_ms * 1e-3) / 1e9 / peaks()[0], "launches_per_step": len(caps),
+                   "reference_round_trip_ms_per_step": ref_ms,
+                   "reference_round_trip": "fp32 capture to pinned host and back (torch copies), timed on the "
+                                           "largest capture and scaled by bytes"}
+        del caps, pinned, big
+
     # a bounded wait that gave up sets the plan's error word and the kernels after it stop
     # early: such a run has no valid timing
     derr = aset.device_error()
@@ -403,6 +445,9 @@ def main():
     per_elem = 2 * f + 16 + K * (2 * f + (4 if K == 1 else 8))
     # activations: each of the 3 power iterations reads H twice (Y = H V, then W = H^T Y)
     step_bytes = sum(sstep.layout.sizes) * per_elem + 2 * 3 * act_layer * cfg["layers"]
+    # the reference's power iteration reads each activation once per iteration (Y and H^T Y
+    # per token chunk, ds_mezo/kernels.py:214-225): its compulsory traffic has 3 passes
+    compulsory_bytes = sum(sstep.layout.sizes) * per_elem + 3 * act_layer * cfg["layers"]
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
@@ -423,11 +468,14 @@ def main():
                          (sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9)},
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
-                          "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1)},
+                          "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1),
+                          "compulsory_bytes": compulsory_bytes,
+                          "compulsory_frac": compulsory_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1)},
         "kernels": kern,
         "allgather_ms_per_step": gather_ms,
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "activation_handoff": handoff,
         "gpu_launches": launches_timed,
         "clocks": clk.summary(),
     }

@@ -7,6 +7,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "dsmz_handoff.cuh"
 #include "dsmz_kernels.cuh"
 #include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
@@ -858,6 +859,36 @@ int dsmz_randn(float* out, int64_t n, uint64_t seed, uint64_t offset, int32_t sm
   if (blocks > 65535) blocks = 65535;
   k_randn<<<static_cast<int>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(out, n, seed, offset, thr);
   DSMZ_LAUNCHED("dsmz_randn");
+  return DSMZ_OK;
+}
+
+// ------------------------------------------------------------ activation handoff
+int dsmz_activation_load(int32_t dst_dtype, void* dst, int64_t T, int64_t D, int64_t ld_dst, int32_t src_dtype,
+                         const void* src, int64_t n, int64_t src_s0, int64_t src_s1, dsmz_stream_t stream) {
+  if (!dst || (n > 0 && !src)) return fail(DSMZ_ERR_INVALID, "dsmz_activation_load: null pointer");
+  if ((dst_dtype != DSMZ_F32 && dst_dtype != DSMZ_BF16) || (src_dtype != DSMZ_F32 && src_dtype != DSMZ_BF16))
+    return fail(DSMZ_ERR_INVALID, "dsmz_activation_load: dtypes must be DSMZ_F32 or DSMZ_BF16");
+  if (T <= 0 || D <= 0 || ld_dst < D || n < 0 || n > T || src_s0 < 0 || src_s1 < 0)
+    return fail(DSMZ_ERR_INVALID,
+                "dsmz_activation_load: need T > 0, D > 0, ld_dst >= D, 0 <= n <= T and non-negative strides");
+  const int ses = src_dtype == DSMZ_F32 ? 4 : 2, des = dst_dtype == DSMZ_F32 ? 4 : 2;
+  const bool vec = D % 8 == 0 && (n == 0 || src_s1 == 1) && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                   (src_s0 * ses) % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (ld_dst * des) % 16 == 0;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail("dsmz_activation_load: device query", e);
+  const int64_t work = vec ? T * (D / 8) : T * D;
+  int64_t blocks = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;      // grid-stride beyond eight CTAs per SM
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int g = static_cast<int>(blocks), v = vec ? 1 : 0;
+  if (src_dtype == DSMZ_F32 && dst_dtype == DSMZ_BF16) k_act_load<0, 1><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
+  else if (src_dtype == DSMZ_BF16 && dst_dtype == DSMZ_BF16) k_act_load<1, 1><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
+  else if (src_dtype == DSMZ_F32) k_act_load<0, 0><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
+  else k_act_load<1, 0><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
+  DSMZ_LAUNCHED("dsmz_activation_load");
   return DSMZ_OK;
 }
 

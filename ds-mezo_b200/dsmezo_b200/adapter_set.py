@@ -170,6 +170,28 @@ class AdapterSet:
         s = self.bases[b]
         return self.H_arena[self.offH[b]:self.offH[b] + s.T * s.D].view(s.T, s.D)
 
+    def load_activations(self, b: int, src: torch.Tensor) -> None:
+        """Device-resident activation handoff for basis `b`: the module input a forward hook
+        captured (n <= T rows of D features, fp32 or bf16, on this set's device, any strides)
+        is converted on the device into the activation buffer H(b); rows n..T-1 become zero,
+        which leaves H^T H unchanged. Replaces the reference's pinned-host round trip
+        (ds_mezo/backend.py:68-93 and the .cuda() copy at ds_mezo/controller.py:171).
+        Runs on the current stream."""
+        s = self.bases[b]
+        if src.dim() != 2 or src.shape[1] != s.D or src.shape[0] > s.T:
+            raise ValueError(f"load_activations: basis {b} takes up to {s.T} rows of {s.D} features, "
+                             f"got {tuple(src.shape)}")
+        if src.device != self.H_arena.device:
+            raise ValueError("load_activations: the source must be on the adapter set's device")
+        codes = {torch.float32: DSMZ_F32, torch.bfloat16: DSMZ_BF16}
+        if src.dtype not in codes:
+            raise TypeError("load_activations: the source must be float32 or bfloat16")
+        dst = self.H(b)
+        check(lib().dsmz_activation_load(codes[self.H_arena.dtype], dst.data_ptr(), s.T, s.D, s.D,
+                                         codes[src.dtype], src.data_ptr() if src.numel() else None,
+                                         src.shape[0], src.stride(0), src.stride(1), self._stream()),
+              "dsmz_activation_load")
+
     def V(self, b):
         s = self.bases[b]
         return self.V_arena[self.offV[b]:self.offV[b] + s.D * self.basis_width].view(s.D, self.basis_width)

@@ -98,6 +98,16 @@ int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t param_
  * modified Gram-Schmidt at ds_mezo/kernels.py:227-240 yields). H is T x D (F32 or BF16,
  * any strides), V is D x R (F32, any strides), out is D x R contiguous F32. */
 size_t dsmz_power_iter_workspace_bytes(int64_t T, int64_t D, int64_t R);
+
+/* Device-resident activation handoff. Replaces the round trip of each captured module
+ * input through pinned host memory (ds_mezo/backend.py:68-93: hook, .float(), pinned copy)
+ * and back (ds_mezo/controller.py:171: .cuda()). Converts rows 0..n-1 of a strided source
+ * (F32 or BF16, element (t, c) at src[t*src_s0 + c*src_s1]) into the T x D activation
+ * buffer dst (row pitch ld_dst elements, F32 or BF16), rows n..T-1 zero; fp32 -> bf16
+ * rounds to nearest even, bit for bit as torch's .to(torch.bfloat16) on the GPU. Asynchronous
+ * on `stream`. */
+int dsmz_activation_load(int32_t dst_dtype, void* dst, int64_t T, int64_t D, int64_t ld_dst, int32_t src_dtype,
+                         const void* src, int64_t n, int64_t src_s0, int64_t src_s1, dsmz_stream_t stream);
 int dsmz_power_iter(int32_t h_dtype, const void* H, int64_t T, int64_t D, int64_t h_s0, int64_t h_s1,
                     const float* V, int64_t R, int64_t v_s0, int64_t v_s1,
                     float* out, int32_t num_iters, float norm_floor,

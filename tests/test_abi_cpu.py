@@ -174,3 +174,14 @@ def test_plan_directions_host_only(L, K):
     assert b"direction strides" in L.dsmz_last_error()
     d.directions = 33
     assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 1
+
+
+def test_activation_load_argument_errors_without_gpu(L):
+    # every check of the activation handoff happens before any CUDA call
+    assert L.dsmz_activation_load(1, None, 16, 8, 8, 0, 0x1000, 16, 8, 1, None) == 1
+    assert b"null" in L.dsmz_last_error()
+    assert L.dsmz_activation_load(1, 0x1000, 16, 8, 8, 0, 0x1000, 17, 8, 1, None) == 1   # n > T
+    assert L.dsmz_activation_load(1, 0x1000, 16, 8, 4, 0, 0x1000, 16, 8, 1, None) == 1   # ld < D
+    assert L.dsmz_activation_load(2, 0x1000, 16, 8, 8, 0, 0x1000, 16, 8, 1, None) == 1   # bad dtype
+    assert b"dtypes" in L.dsmz_last_error()
+    assert L.dsmz_activation_load(1, 0x1000, 16, 8, 8, 0, 0x1000, 16, -8, 1, None) == 1  # negative stride
