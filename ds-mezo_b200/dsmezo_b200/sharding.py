@@ -16,7 +16,7 @@ shard, so each all-gather is one NCCL call on contiguous buffers.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -108,6 +108,36 @@ def shard_layout(layers: int, hidden: int, inter: int, kv: int, rank_r: int, tok
     return ShardLayout(ranges, per_layer, incs, sizes, max(sizes) if sizes else 0)
 
 
+# Module path of each adapted projection in a Llama/Qwen decoder, under the PEFT prefix
+# the reference builds ("base_model.model." + the module's name, ds_mezo/model_config.py:30-35).
+PEFT_PATH = {"q_proj": "self_attn.q_proj", "k_proj": "self_attn.k_proj", "v_proj": "self_attn.v_proj",
+             "o_proj": "self_attn.o_proj", "gate_proj": "mlp.gate_proj", "up_proj": "mlp.up_proj",
+             "down_proj": "mlp.down_proj"}
+
+
+def peft_prefix(layer: int, name: str) -> str:
+    return f"base_model.model.model.layers.{layer}.{PEFT_PATH[name]}"
+
+
+def export_index(rank_modules: Sequence[Sequence], rank_r: int, block: int, base: int = 0
+                 ) -> Dict[str, Tuple[int, Tuple[int, int]]]:
+    """Where each PEFT adapter tensor lies in a buffer that holds every rank's factor arena
+    one after another, `block` elements apart, starting at `base` (a direction's offset
+    inside a rank's block). Keys follow ds_mezo/backend.py:21-34: lora_A.weight is the
+    factor B (r x d_in) and lora_B.weight the factor A (d_out x r), the PiSSA/PEFT swap.
+    Values are (element offset, shape). Host only."""
+    out = {}
+    for rk, mods in enumerate(rank_modules):
+        n = rk * block + base
+        for m in mods:
+            pre = peft_prefix(m.layer, m.name)
+            out[f"{pre}.lora_B.weight"] = (n, (m.d_out, rank_r))
+            n += m.d_out * rank_r
+            out[f"{pre}.lora_A.weight"] = (n, (rank_r, m.d_in))
+            n += rank_r * m.d_in
+    return out
+
+
 class ShardedStep:
     """One rank's part of the layer-sharded step (all of it when world == 1)."""
 
@@ -121,6 +151,7 @@ class ShardedStep:
         self.rank = dist.get_rank(process_group) if process_group is not None else 0
         layout = device_layout(device)
         self.layout = shard_layout(layers, hidden, inter, kv, rank_r, tokens, self.world, *layout)
+        self._shape = (layers, hidden, inter, kv, rank_r, tokens)
         lr = self.layout.ranges[self.rank]
         mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)
         # one direction's draws over the whole model: the stride between directions' draws
@@ -173,3 +204,35 @@ class ShardedStep:
         """Rank `rank`'s factor elements inside a gathered buffer."""
         cap = self.layout.capacity
         return buf[rank * cap: rank * cap + self.layout.sizes[rank]]
+
+    def export_adapters(self, which: str = "pos", direction: int = 0) -> Dict[str, torch.Tensor]:
+        """The adapter tensors the rollout engine loads, keyed as the reference's PEFT file
+        (ds_mezo/backend.py:21-36: lora_A.weight = B, lora_B.weight = A, bf16), as device
+        views of the full-model buffer that the last gather(which) filled (the local arena on
+        one GPU). With bf16 factors nothing is copied: this replaces the reference's bf16
+        cast and safetensors write to /dev/shm. fp32 factors are converted once on the device
+        into a bf16 buffer of the same layout. which: 'pos', 'neg' or 'factors'."""
+        if which not in ("pos", "neg", "factors"):
+            raise ValueError("export_adapters: which is 'pos', 'neg' or 'factors'")
+        K = 1 if which == "factors" else self.aset.directions
+        if not 0 <= direction < K:
+            raise ValueError(f"export_adapters: direction must be in [0, {K})")
+        cap = self.layout.capacity
+        if self.world == 1:
+            buf = getattr(self.aset, which)
+        else:
+            buf = self.gathered[which]
+        layers, hidden, inter, kv, rank_r, tokens = self._shape
+        rank_mods = [transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)[0]
+                     for lr in self.layout.ranges]
+        idx = export_index(rank_mods, rank_r, K * cap, direction * cap)
+        if buf.dtype != torch.bfloat16:
+            from ._lib import DSMZ_BF16, DSMZ_F32, check, lib
+            out = torch.empty(buf.numel(), dtype=torch.bfloat16, device=buf.device)
+            check(lib().dsmz_activation_load(DSMZ_BF16, out.data_ptr(), 1, buf.numel(), buf.numel(), DSMZ_F32,
+                                             buf.data_ptr(), 1, buf.numel(), 1,
+                                             torch.cuda.current_stream(buf.device).cuda_stream),
+                  "export_adapters conversion")
+            buf = out
+        return {k: buf[o:o + a * b].view(a, b) for k, (o, (a, b)) in idx.items()}
+

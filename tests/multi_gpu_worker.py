@@ -1,7 +1,8 @@
 """Worker for test_gpu_multi.py (launched by torch.distributed.run, one rank per GPU).
 
 Runs one layer-sharded step and, on rank 0, the same step on one GPU; compares every
-rank's gathered factors, pos and neg with the single-GPU arenas. Prints MULTI_OK."""
+rank's gathered factors, pos and neg, and their PEFT-named exports, with the single-GPU
+ones. Prints MULTI_OK."""
 import datetime
 import os
 import sys
@@ -73,6 +74,15 @@ def main():
                 err = float((got - want).abs().max() / want.abs().max())
                 assert err < 1e-5, (r, name, err)
             off += n
+        # the PEFT export from the gathered buffers names and places every adapter as the
+        # one-GPU set's export does
+        for which in ("factors", "pos"):
+            got, want = st.export_adapters(which), one.export_adapters(which)
+            assert got.keys() == want.keys() and len(got) == 2 * 7 * CFG["layers"]
+            for k in want:
+                assert got[k].shape == want[k].shape and got[k].dtype == torch.bfloat16, k
+                err = float((got[k].float() - want[k].float()).abs().max() / want[k].float().abs().max())
+                assert err < 1e-5, (which, k, err)
         print("MULTI_OK", flush=True)
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()

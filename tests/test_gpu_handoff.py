@@ -162,3 +162,32 @@ def test_adapter_set_handoff_rejects_bad_sources():
         aset.load_activations(0, torch.zeros(T, D + 1, device=DEV))
     with pytest.raises(TypeError):
         aset.load_activations(0, torch.zeros(T, D, dtype=torch.float16, device=DEV))
+
+
+@pytest.mark.parametrize("fdt", [torch.bfloat16, torch.float32])
+def test_adapter_export_views(fdt):
+    # ds_mezo/backend.py:21-36: lora_A.weight = B, lora_B.weight = A, bf16, one per module
+    from dsmezo_b200 import ShardedStep
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    st = ShardedStep(2, 64, 160, 16, 8, 32, eps=1e-3, total_steps=100, generator=gen, factor_dtype=fdt,
+                     act_dtype=torch.bfloat16, device=DEV)
+    a = st.aset
+    g = torch.Generator().manual_seed(1)
+    for i in range(len(a.modules)):
+        a.A(i).copy_(torch.randn(a.A(i).shape, generator=g))
+        a.B(i).copy_(torch.randn(a.B(i).shape, generator=g))
+    for b in range(len(a.bases)):
+        a.V(b).copy_(torch.linalg.qr(torch.randn(a.V(b).shape, generator=g))[0])
+        a.H(b).copy_(torch.randn(a.H(b).shape, generator=g))
+    st.perturb()
+    for which, arena in (("pos", a.pos_dir(0)), ("neg", a.neg_dir(0)), ("factors", a.factors)):
+        ex = st.export_adapters(which)
+        torch.cuda.synchronize()
+        assert len(ex) == 2 * len(a.modules)
+        for i, m in enumerate(a.modules):
+            pre = f"base_model.model.model.layers.{m.layer}." + ("self_attn." if m.name[0] in "qkvo" else "mlp.") + m.name
+            A, B = ex[pre + ".lora_B.weight"], ex[pre + ".lora_A.weight"]
+            assert A.dtype == torch.bfloat16 and B.dtype == torch.bfloat16
+            assert same_bits(A, a.A(i, arena).to(torch.bfloat16)) and same_bits(B, a.B(i, arena).to(torch.bfloat16))
+            if fdt == torch.bfloat16:                       # no copy: views of the arena itself
+                assert A.data_ptr() == a.A(i, arena).data_ptr() and B.data_ptr() == a.B(i, arena).data_ptr()

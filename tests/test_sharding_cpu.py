@@ -162,3 +162,41 @@ def test_collectives_of_the_sharded_step_gloo():
 def test_rank_failure_is_detected_on_the_host():
     res = _run("fail")
     assert res[0][0] == 0 and res[0][1] == "detected"
+
+
+@pytest.mark.parametrize("world,K", [(1, 1), (2, 1), (3, 2)])
+def test_export_index_finds_every_adapter_in_the_gathered_buffer(world, K):
+    # every rank's local arena (K directions, `cap` apart) filled with a code per (rank,
+    # direction, module, factor), gathered rank-major as the all-gather lays it out
+    from dsmezo_b200.sharding import export_index, partition_layers, peft_prefix
+    from dsmezo_b200 import transformer_adapter_shapes
+    layers, hidden, inter, kv, r, tokens = 5, 64, 160, 16, 4, 8
+    ranges = partition_layers(layers, world)
+    rank_mods = [transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)[0] for lr in ranges]
+    sizes = [sum(m.d_out * r + r * m.d_in for m in ms) for ms in rank_mods]
+    cap = max(sizes) + 3                                  # padded shards
+    locals_ = []
+    for rk, ms in enumerate(rank_mods):
+        arena = torch.full((K * cap,), -1.0)
+        for k in range(K):
+            n = k * cap
+            for i, m in enumerate(ms):
+                arena[n:n + m.d_out * r] = 1000 * rk + 100 * k + 2 * i
+                n += m.d_out * r
+                arena[n:n + r * m.d_in] = 1000 * rk + 100 * k + 2 * i + 1
+                n += r * m.d_in
+        locals_.append(arena)
+    gathered = torch.cat(locals_)
+    for k in range(K):
+        idx = export_index(rank_mods, r, K * cap, k * cap)
+        assert len(idx) == 2 * 7 * layers
+        for rk, ms in enumerate(rank_mods):
+            for i, m in enumerate(ms):
+                pre = peft_prefix(m.layer, m.name)
+                oA, shA = idx[f"{pre}.lora_B.weight"]             # the factor A (d_out x r)
+                oB, shB = idx[f"{pre}.lora_A.weight"]             # the factor B (r x d_in)
+                assert shA == (m.d_out, r) and shB == (r, m.d_in)
+                assert torch.all(gathered[oA:oA + m.d_out * r] == 1000 * rk + 100 * k + 2 * i)
+                assert torch.all(gathered[oB:oB + r * m.d_in] == 1000 * rk + 100 * k + 2 * i + 1)
+    assert "base_model.model.model.layers.0.self_attn.q_proj.lora_A.weight" in export_index(rank_mods, r, cap)
+    assert "base_model.model.model.layers.4.mlp.down_proj.lora_B.weight" in export_index(rank_mods, r, cap)
