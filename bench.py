@@ -411,6 +411,36 @@ def main():
                                            "largest capture and scaled by bytes"}
         del caps, pinned, big
 
+    # contrastive scoring loss on the device: the + and - scoring passes' bf16 logits rows
+    # for four completions of 512 scored tokens over the Qwen2.5 vocabulary (152064)
+    scoring = None
+    if not args.no_e2e and world == 1:
+        from dsmezo_b200 import scoring as sc
+        sgen = torch.Generator(device=device).manual_seed(cfg["seed"] + 2)
+        vocab, lens, adv = 152064, [512] * 4, [0.75, -0.25, -0.25, -0.25]
+        rows = {k: (torch.randn(sum(lens), vocab, generator=sgen, device=device) * 4).to(torch.bfloat16)
+                for k in ("pos", "neg")}
+        tg = torch.randint(0, vocab, (sum(lens),), generator=sgen, device=device, dtype=torch.int32)
+        for k in rows:
+            sc.contrastive_loss(rows[k], lens, adv, tg)
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        n_s = 5
+        torch.cuda.synchronize()
+        s0.record()
+        for _ in range(n_s):
+            lp = sc.contrastive_loss(rows["pos"], lens, adv, tg)
+            ln = sc.contrastive_loss(rows["neg"], lens, adv, tg)
+        s1.record()
+        torch.cuda.synchronize()
+        s_ms = s0.elapsed_time(s1) / n_s
+        sbytes = 2 * rows["pos"].numel() * rows["pos"].element_size()
+        scoring = {"ms_per_step": s_ms, "bytes_per_step": sbytes, "achieved_GBps": sbytes / (s_ms * 1e-3) / 1e9,
+                   "frac": sbytes / (s_ms * 1e-3) / 1e9 / peaks()[0], "launches_per_step": 4,
+                   "workload": "4 completions x 512 scored tokens x 152064 vocabulary, bf16 logits, + and -",
+                   "dd": sc.projected_gradient(float(lp), float(ln), 1e-3)}
+        del rows
+
     # a bounded wait that gave up sets the plan's error word and the kernels after it stop
     # early: such a run has no valid timing
     derr = aset.device_error()
@@ -476,6 +506,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "activation_handoff": handoff,
+        "scoring": scoring,
         "gpu_launches": launches_timed,
         "clocks": clk.summary(),
     }

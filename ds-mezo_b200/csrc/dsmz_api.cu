@@ -9,6 +9,7 @@
 
 #include "dsmz_handoff.cuh"
 #include "dsmz_kernels.cuh"
+#include "dsmz_score.cuh"
 #include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
 
@@ -889,6 +890,60 @@ int dsmz_activation_load(int32_t dst_dtype, void* dst, int64_t T, int64_t D, int
   else if (src_dtype == DSMZ_F32) k_act_load<0, 0><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
   else k_act_load<1, 0><<<g, 256, 0, s>>>(dst, T, D, ld_dst, src, n, src_s0, src_s1, v);
   DSMZ_LAUNCHED("dsmz_activation_load");
+  return DSMZ_OK;
+}
+
+// ------------------------------------------------------------ contrastive scoring loss
+size_t dsmz_contrastive_loss_workspace_bytes(int64_t ntok) {
+  return ntok > 0 ? static_cast<size_t>(ntok) * sizeof(double) + 256 : 256;
+}
+
+int dsmz_contrastive_loss(int32_t kind, const void* src, int64_t V, int64_t ld, const int32_t* targets, int64_t ntok,
+                          const int64_t* seq_start, const double* advantages, int32_t nseq, double* out,
+                          void* workspace, size_t workspace_bytes, dsmz_stream_t stream) {
+  if (!src || !out || !workspace || (kind != DSMZ_SCORE_LOGPROBS_F32 && !targets))
+    return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: null pointer");
+  if (kind != DSMZ_SCORE_LOGITS_F32 && kind != DSMZ_SCORE_LOGITS_BF16 && kind != DSMZ_SCORE_LOGPROBS_F32)
+    return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: kind must be a DSMZ_SCORE_* value");
+  if (nseq < 1 || nseq > kMaxScoreSeqs || !seq_start || !advantages)
+    return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: 1 <= nseq <= " + std::to_string(kMaxScoreSeqs) +
+                                      " with host arrays seq_start[nseq + 1] and advantages[nseq]");
+  if (kind != DSMZ_SCORE_LOGPROBS_F32 && (V < 1 || ld < V))
+    return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: need V >= 1 and ld >= V");
+  if (seq_start[0] != 0 || seq_start[nseq] != ntok || ntok < 1)
+    return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: seq_start must run from 0 to ntok >= 1");
+  ScoreSeqs q{};
+  q.n = nseq;
+  for (int i = 0; i < nseq; ++i) {
+    const int64_t len = seq_start[i + 1] - seq_start[i];
+    // the reference's mean over a sequence (ds_mezo/controller.py:14-15) has no empty case
+    if (len < 1) return fail(DSMZ_ERR_INVALID, "dsmz_contrastive_loss: every sequence needs a scored token");
+    q.start[i] = seq_start[i];
+    q.w[i] = advantages[i] / static_cast<double>(len);
+  }
+  q.start[nseq] = ntok;
+  if (workspace_bytes < dsmz_contrastive_loss_workspace_bytes(ntok) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(DSMZ_ERR_WORKSPACE, "dsmz_contrastive_loss: workspace too small or not 16-byte aligned");
+  double* term = static_cast<double*>(workspace);
+  int* err = reinterpret_cast<int*>(static_cast<char*>(workspace) + static_cast<size_t>(ntok) * sizeof(double));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail("dsmz_contrastive_loss: error word", e);
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail("dsmz_contrastive_loss: device query", e);
+  const int64_t cap = static_cast<int64_t>(sms) * 8;
+  const int g = static_cast<int>(ntok < cap ? ntok : cap);
+  const int es = kind == DSMZ_SCORE_LOGITS_BF16 ? 2 : 4;
+  const int per = 16 / es;                              // elements per 16-byte load
+  const int vec = (V % per == 0 && (ld * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) ? 1 : 0;
+  if (kind == DSMZ_SCORE_LOGITS_F32) k_token_nll<0><<<g, 256, 0, s>>>(src, ld, V, targets, ntok, q, vec, term, err);
+  else if (kind == DSMZ_SCORE_LOGITS_BF16) k_token_nll<1><<<g, 256, 0, s>>>(src, ld, V, targets, ntok, q, vec, term, err);
+  else k_token_nll<2><<<g, 256, 0, s>>>(src, ld, V, targets, ntok, q, vec, term, err);
+  DSMZ_LAUNCHED("dsmz_contrastive_loss: token terms");
+  k_seq_sum<<<1, 256, 0, s>>>(term, ntok, err, out);
+  DSMZ_LAUNCHED("dsmz_contrastive_loss: sum");
   return DSMZ_OK;
 }
 

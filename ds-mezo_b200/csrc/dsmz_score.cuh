@@ -1,0 +1,124 @@
+// Contrastive scoring reduction (ds_mezo/controller.py:14-15 and 194-201):
+//   loss = sum_i adv_i * mean_{t in sequence i} nll_t,
+// with nll_t = -log softmax(logits_t)[target_t], the negative of the logprob that vLLM
+// returns for each scored token (ds_mezo/backend.py:98-103), or nll_t = -lp_t when the
+// caller already holds the logprobs. Two kernels:
+//   k_token_nll  one CTA per token row (grid-stride): an online (max, sum of exp) over the
+//                vocabulary in fp32 with 16-byte loads, merged across the CTA, then
+//                nll = max + log(sum) - logit[target], times adv_i / len_i of the row's
+//                sequence, stored as an fp64 term per token;
+//   k_seq_sum    one CTA adds the terms in token order (fixed, so the loss is the same
+//                bit for bit on every run).
+// The log-softmax is the published one (log sum exp with the row maximum subtracted),
+// evaluated in fp32 as vLLM evaluates it.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cstdint>
+
+namespace dsmz {
+
+constexpr int kMaxScoreSeqs = 128;   // sequences per call (the reference scores 4 per step)
+
+struct ScoreSeqs {
+  int32_t n;                         // sequences
+  int32_t pad;
+  int64_t start[kMaxScoreSeqs + 1];  // token rows of sequence i: [start[i], start[i+1])
+  double w[kMaxScoreSeqs];           // adv_i / len_i
+};
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  if (m2 > m) { s = s * expf(m - m2) + s2; m = m2; }
+  else if (m2 != -INFINITY) { s += s2 * expf(m2 - m); }
+}
+
+// DT: 0 = fp32 logits, 1 = bf16 logits, 2 = fp32 logprobs (one per token, no vocabulary)
+template <int DT>
+__global__ void __launch_bounds__(256) k_token_nll(const void* __restrict__ src, int64_t ld, int64_t V,
+                                                   const int32_t* __restrict__ targets, int64_t ntok,
+                                                   ScoreSeqs seqs, int vec, double* __restrict__ term, int* err) {
+  __shared__ float sm[8], ss[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t row = blockIdx.x; row < ntok; row += gridDim.x) {
+    int si = 0;                                        // the row's sequence
+    while (si + 1 < seqs.n && seqs.start[si + 1] <= row) ++si;
+    if (DT == 2) {
+      if (tid == 0) term[row] = -static_cast<double>(reinterpret_cast<const float*>(src)[row]) * seqs.w[si];
+      continue;
+    }
+    float m = -INFINITY, s = 0.f;
+    if (DT == 1 && vec) {
+      const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src) + row * ld);
+      for (int64_t c = tid; c < V / 8; c += blockDim.x) {
+        const uint4 u = p[c];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        float x[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { x[2 * q] = __uint_as_float(w4[q] << 16); x[2 * q + 1] = __uint_as_float(w4[q] & 0xFFFF0000u); }
+        float mx = x[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) mx = fmaxf(mx, x[q]);
+        float sx = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sx += expf(x[q] - mx);
+        lse_merge(m, s, mx, sx);
+      }
+    } else if (DT == 0 && vec) {
+      const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + row * ld);
+      for (int64_t c = tid; c < V / 4; c += blockDim.x) {
+        const float4 u = p[c];
+        const float mx = fmaxf(fmaxf(u.x, u.y), fmaxf(u.z, u.w));
+        const float sx = expf(u.x - mx) + expf(u.y - mx) + expf(u.z - mx) + expf(u.w - mx);
+        lse_merge(m, s, mx, sx);
+      }
+    } else {
+      for (int64_t c = tid; c < V; c += blockDim.x) {
+        const float x = (DT == 0) ? reinterpret_cast<const float*>(src)[row * ld + c]
+                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[row * ld + c]);
+        lse_merge(m, s, x, 1.f);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse_merge(m, s, m2, s2);
+    }
+    if (lane == 0) { sm[warp] = m; ss[warp] = s; }
+    __syncthreads();
+    if (tid == 0) {
+      float M = sm[0], S = ss[0];
+      for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) lse_merge(M, S, sm[w], ss[w]);
+      const int32_t tg = targets[row];
+      double t = 0.0;
+      if (tg < 0 || tg >= V) {
+        atomicExch(err, 2);                            // a target outside the vocabulary
+      } else {
+        const float xt = (DT == 0) ? reinterpret_cast<const float*>(src)[row * ld + tg]
+                                   : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[row * ld + tg]);
+        t = static_cast<double>((M + logf(S)) - xt) * seqs.w[si];
+      }
+      term[row] = t;
+    }
+    __syncthreads();                                   // sm / ss are reused by the next row
+  }
+}
+
+// out[0] = sum of term[0..ntok) in token order: each thread adds a contiguous run, the runs
+// are added in thread order. NaN when a row's target was outside the vocabulary.
+__global__ void __launch_bounds__(256) k_seq_sum(const double* __restrict__ term, int64_t ntok, const int* err,
+                                                 double* out) {
+  __shared__ double part[256];
+  const int tid = threadIdx.x;
+  const int64_t per = (ntok + 255) / 256;
+  double a = 0.0;
+  for (int64_t i = tid * per; i < min(ntok, (tid + 1) * per); ++i) a += term[i];
+  part[tid] = a;
+  __syncthreads();
+  if (tid == 0) {
+    double s = 0.0;
+    for (int i = 0; i < 256; ++i) s += part[i];
+    out[0] = (*err != 0) ? __longlong_as_double(0x7FF8000000000000ll) : s;   // NaN: a bad target
+  }
+}
+
+}  // namespace dsmz

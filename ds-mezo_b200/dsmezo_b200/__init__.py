@@ -9,6 +9,7 @@
 All compute runs in libdsmezo.so (C ABI in include/dsmezo.h); there is no CPU path.
 """
 from . import kernels  # noqa: F401
+from . import scoring  # noqa: F401
 from ._lib import DsmzError, lib  # noqa: F401
 from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ZOController, device_layout,  # noqa: F401
                           draw_increments, kalman_beta_q, rloo_direction_scalars, transformer_adapter_shapes)

@@ -82,6 +82,9 @@ SIGNATURES = {
                                               c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_float,
                                               POINTER(NSSchedule), c_void_p]),
     "dsmz_power_iter_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "dsmz_contrastive_loss_workspace_bytes": (c_size_t, [c_int64]),
+    "dsmz_contrastive_loss": (c_int32, [c_int32, c_void_p, c_int64, c_int64, c_void_p, c_int64, POINTER(c_int64),
+                                        POINTER(c_double), c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     "dsmz_activation_load": (c_int32, [c_int32, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p,
                                        c_int64, c_int64, c_int64, c_void_p]),
     "dsmz_power_iter": (c_int32, [c_int32, c_void_p, c_int64, c_int64, c_int64, c_int64,

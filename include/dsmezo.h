@@ -99,6 +99,23 @@ int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t param_
  * any strides), V is D x R (F32, any strides), out is D x R contiguous F32. */
 size_t dsmz_power_iter_workspace_bytes(int64_t T, int64_t D, int64_t R);
 
+/* Contrastive scoring loss (ds_mezo/controller.py:14-15, 194-201): out[0] (device fp64) =
+ * sum_i advantages[i] * mean over the scored tokens t of sequence i of nll_t, where
+ * nll_t = -log softmax(logits row t)[targets[t]] (the logprob vLLM reports for the token,
+ * ds_mezo/backend.py:98-103; kind DSMZ_SCORE_LOGITS_F32 / _BF16, rows of V logits, row
+ * pitch ld) or nll_t = -src[t] (kind DSMZ_SCORE_LOGPROBS_F32: one logprob per token).
+ * Sequence i owns token rows [seq_start[i], seq_start[i+1]); seq_start (nseq + 1 entries,
+ * 0 .. ntok) and advantages (nseq) are host arrays, nseq <= 128, every sequence non-empty.
+ * Deterministic (fixed summation order). A target outside [0, V) makes out[0] NaN.
+ * dd = (loss(pos) - loss(neg)) / (2 eps) as ds_mezo/controller.py:307. */
+#define DSMZ_SCORE_LOGITS_F32 0
+#define DSMZ_SCORE_LOGITS_BF16 1
+#define DSMZ_SCORE_LOGPROBS_F32 2
+size_t dsmz_contrastive_loss_workspace_bytes(int64_t ntok);
+int dsmz_contrastive_loss(int32_t kind, const void* src, int64_t V, int64_t ld, const int32_t* targets, int64_t ntok,
+                          const int64_t* seq_start, const double* advantages, int32_t nseq, double* out,
+                          void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
+
 /* Device-resident activation handoff. Replaces the round trip of each captured module
  * input through pinned host memory (ds_mezo/backend.py:68-93: hook, .float(), pinned copy)
  * and back (ds_mezo/controller.py:171: .cuda()). Converts rows 0..n-1 of a strided source

@@ -13,6 +13,7 @@ op. Citations are ``path:line`` inside the reference project:
 * ``ds_mezo/kernels.py:188-265``  activation power iteration + MGS  -> ``fused_power_iter``
 * ``ds_mezo/kernels.py:267-397``  AGZO perturbation                 -> ``fused_agzo_perturbation``
 * ``ds_mezo/kernels.py:399-422``  dual perturb                      -> ``fused_perturb_dual``
+* ``ds_mezo/controller.py:14-15, 194-201``  contrastive scoring loss -> ``contrastive_loss``
 * ``ds_mezo/controller.py:78-88, 178-193, 216-229, 236-292``        -> controller helpers below
 
 The restatement is pinned against golden vectors that the reference's own Triton kernels
@@ -258,6 +259,23 @@ def shrinkage_rloo(rewards: Sequence[float], reward_ema: float, momentum: float,
     adv = (r - base).tolist()
     new_ema = momentum * reward_ema + (1.0 - momentum) * r_bar
     return adv, new_ema
+
+
+def contrastive_loss(rows: torch.Tensor, targets: Sequence[int], seq_tokens: Sequence[int],
+                     advantages: Sequence[float]) -> float:
+    """ds_mezo/controller.py:194-201 with _mean_nll (:14-15): sum_i adv_i * mean NLL of
+    sequence i's scored tokens. rows holds the logits that predict each scored token (one
+    row per token, sequences one after another); the logprob of a token is the fp32
+    log-softmax entry vLLM reports (ds_mezo/backend.py:98-103), turned into a Python float,
+    and the sums run over Python floats in the reference's order."""
+    lp = torch.log_softmax(rows.float(), dim=-1)
+    vals = [float(lp[j, int(t)]) for j, t in enumerate(targets)]
+    loss, o = 0, 0
+    for adv, n in zip(advantages, seq_tokens):
+        seq = vals[o:o + n]
+        loss = loss + adv * (-sum(seq) / len(seq))
+        o += n
+    return float(loss)
 
 
 def rloo_advantages(rewards: Sequence[float]) -> List[float]:

@@ -9,6 +9,8 @@ Runs DS-MeZO's own code on CPU and records inputs and outputs:
   ``safetensors.load_file`` (returns the in-memory adapter), and ``device="cuda"``
   (mapped to CPU). The CUDA generator is replaced by a CPU generator whose draws are
   recorded, so the fixtures carry the exact Gaussian values the reference consumed.
+* ``ds_mezo/controller.py`` ``_score_contrastive`` (with ``_mean_nll``) on a stub backend
+  that returns the fp32 log-softmax logprobs of seeded logits (``scoring.pt``).
 
 Usage (needs the reference checkout; writes tests/golden/*.pt):
     python tests/golden/make_golden.py [--ref /root/reference]
@@ -213,12 +215,49 @@ def controller_case(C, MC, g, *, layers, h, inter, kv, r, T, steps, total_steps,
     return record
 
 
+def scoring_cases(C, g):
+    """ds_mezo/controller.py:194-201 (_score_contrastive, with _mean_nll at :14-15) on a stub
+    backend whose score() returns, per trajectory, the fp32 log-softmax logprob of each
+    token after the first (what ds_mezo/backend.py:98-103 extracts from vLLM). Records the
+    scored rows' logits and targets so that the device reduction can start from logits."""
+    cases = []
+    for n_traj, prompt_len, vocab, max_new in [(4, 5, 50, 9), (4, 12, 256, 30), (2, 3, 1000, 4), (6, 1, 17, 6)]:
+        lens = [prompt_len + int(torch.randint(1, max_new + 1, (1,), generator=g)) for _ in range(n_traj)]
+        trajs = [torch.randint(0, vocab, (L,), generator=g).tolist() for L in lens]
+        adv = (torch.randn(n_traj, generator=g) * 0.7).tolist()
+        logits = {k: [torch.randn(L - 1, vocab, generator=g) * 3 for L in lens] for k in ("pos", "neg")}
+
+        class _Score:
+            lora_pos, lora_neg = "pos", "neg"
+
+            def score(self, trajectories, lora):
+                out = []
+                for t, lg in zip(trajectories, logits[lora]):
+                    lp = torch.log_softmax(lg, dim=-1)
+                    out.append([float(lp[j, t[j + 1]]) for j in range(len(t) - 1)])
+                return out
+
+        fake = types.SimpleNamespace(backend=_Score())
+        loss_pos, loss_neg = C.DSMeZO_Controller._score_contrastive(fake, trajs, adv, prompt_len)
+        rows = {k: torch.cat([lg[prompt_len - 1:] for lg in logits[k]]) for k in ("pos", "neg")}
+        targets = torch.tensor([tok for t in trajs for tok in t[prompt_len:]], dtype=torch.int32)
+        cases.append({"prompt_len": prompt_len, "lens": lens, "advantages": adv, "seq_tokens": [L - prompt_len for L in lens],
+                      "targets": targets, "rows_pos": rows["pos"], "rows_neg": rows["neg"],
+                      "loss_pos": float(loss_pos), "loss_neg": float(loss_neg)})
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["scoring"], default=None, help="write only this fixture")
     args = ap.parse_args()
     rec = []
     K, C, MC = load_reference(Path(args.ref), rec)
+    torch.save(scoring_cases(C, torch.Generator().manual_seed(31)), HERE / "scoring.pt")
+    if args.only == "scoring":
+        print("wrote scoring.pt")
+        return
     g = torch.Generator().manual_seed(20260)
     torch.save(kernel_cases(K, g), HERE / "kernels.pt")
     import tempfile

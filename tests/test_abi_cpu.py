@@ -185,3 +185,20 @@ def test_activation_load_argument_errors_without_gpu(L):
     assert L.dsmz_activation_load(2, 0x1000, 16, 8, 8, 0, 0x1000, 16, 8, 1, None) == 1   # bad dtype
     assert b"dtypes" in L.dsmz_last_error()
     assert L.dsmz_activation_load(1, 0x1000, 16, 8, 8, 0, 0x1000, 16, -8, 1, None) == 1  # negative stride
+
+
+def test_contrastive_loss_argument_errors_without_gpu(L):
+    # host-side validation runs before any CUDA call
+    i64 = ctypes.c_int64 * 3
+    f64 = ctypes.c_double * 2
+    ws = 1 << 20
+    ok_start, adv = i64(0, 3, 5), f64(0.5, -0.5)
+    assert L.dsmz_contrastive_loss(1, 0x1000, 50, 50, 0x2000, 5, ok_start, adv, 0, 0x3000, 0x4000, ws, None) == 1
+    assert L.dsmz_contrastive_loss(7, 0x1000, 50, 50, 0x2000, 5, ok_start, adv, 2, 0x3000, 0x4000, ws, None) == 1
+    assert b"kind" in L.dsmz_last_error()
+    assert L.dsmz_contrastive_loss(1, 0x1000, 50, 50, 0x2000, 5, i64(1, 3, 5), adv, 2, 0x3000, 0x4000, ws, None) == 1
+    assert L.dsmz_contrastive_loss(1, 0x1000, 50, 50, 0x2000, 5, i64(0, 0, 5), adv, 2, 0x3000, 0x4000, ws, None) == 1
+    assert b"scored token" in L.dsmz_last_error()
+    assert L.dsmz_contrastive_loss(1, 0x1000, 50, 40, 0x2000, 5, ok_start, adv, 2, 0x3000, 0x4000, ws, None) == 1
+    assert L.dsmz_contrastive_loss(1, 0x1000, 50, 50, 0x2000, 5, ok_start, adv, 2, 0x3000, 0x4000, 16, None) == 2
+    assert L.dsmz_contrastive_loss_workspace_bytes(1000) >= 8000

@@ -131,3 +131,13 @@ def test_controller_steps_match_reference(mini):
             a0 = mini["init"][f"{m.layer}.{m.name}"]
             assert rel(m.A - a0["A"], g["A"] - a0["A"]) < 1e-3
             assert rel(m.B - a0["B"], g["B"] - a0["B"]) < 1e-3
+
+
+def test_contrastive_loss_matches_reference():
+    # the reference's _score_contrastive on a stub backend (tests/golden/make_golden.py)
+    cases = torch.load(GOLD / "scoring.pt", weights_only=False)
+    assert len(cases) == 4
+    for c in cases:
+        for k in ("pos", "neg"):
+            got = ref.contrastive_loss(c[f"rows_{k}"], c["targets"].tolist(), c["seq_tokens"], c["advantages"])
+            assert got == c[f"loss_{k}"], (k, got, c[f"loss_{k}"])
