@@ -280,11 +280,12 @@ int tc_stages(int R) {
 size_t tc_smem(int R) { return static_cast<size_t>(tc_stages(R)) * tc::stage_bytes(R) + 1024 + 512; }
 // Persistent W kernel (one CTA per SM): the ring takes what the fp64 staging region leaves.
 int pw_stages(int R) {
-  const int n = (227 * 1024 - 2048 - tc::w_stage_bytes(R)) / tc::stage_bytes(R);
+  const int n = (227 * 1024 - 2048 - tc::w_stage_bytes(R)) / tc::w_ring_stage_bytes(R, tc::w_halves(R));
   return n > 6 ? 6 : n;
 }
 size_t pw_smem(int R) {
-  return static_cast<size_t>(pw_stages(R)) * tc::stage_bytes(R) + tc::w_stage_bytes(R) + 1024 + 512;
+  return static_cast<size_t>(pw_stages(R)) * tc::w_ring_stage_bytes(R, tc::w_halves(R)) + tc::w_stage_bytes(R) + 1024 +
+         512;
 }
 
 struct TCSlots {             // workspace byte offsets of one basis
@@ -457,7 +458,8 @@ void plan_tc_layout(dsmz_plan* P) {
     tc::TCBasis& c = P->tcb[i];
     c.T = b.T; c.D = b.D; c.R = b.R; c.ldv2 = t.ldv2; c.ldy2 = t.ldy2;
     c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + tc::kBM - 1) / tc::kBM); P->ntc_y += c.nytile;
-    c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + tc::kBM - 1) / tc::kBM); P->ntc_w += c.nwtile;
+    const int64_t wrows = static_cast<int64_t>(tc::w_halves(static_cast<int>(b.R))) * tc::kBM;   // rows per W tile
+    c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + wrows - 1) / wrows); P->ntc_w += c.nwtile;
     c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D + tc::kSplitD - 1) / tc::kSplitD); P->ntc_vt += c.nvt;
     if (b.R <= 64) {           // the W epilogue forms the Gram: one block-major partial per W tile
       const int nb = b.R / 8;
@@ -613,7 +615,8 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
   if (P->tc) {
     if ((rc = set_smem(tc::k_pi_y, tsm))) return rc;
-    if ((rc = set_smem(tc::k_pi_w, pw_smem(R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_w<1>, pw_smem(R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_w<2>, pw_smem(R)))) return rc;
     if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
       P->probe_begin(DSMZ_KID_PI_SPLIT, s);
       tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
@@ -629,8 +632,12 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
       P->probe_end(DSMZ_KID_PI_Y, s);
       DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
       P->probe_begin(DSMZ_KID_PI_W, s);
-      tc::k_pi_w<<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
-                                                                                  pw_stages(R), err);
+      if (tc::w_halves(R) == 2)
+        tc::k_pi_w<2><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
+                                                                                        pw_stages(R), err);
+      else
+        tc::k_pi_w<1><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
+                                                                                        pw_stages(R), err);
       P->probe_end(DSMZ_KID_PI_W, s);
       DSMZ_LAUNCHED("power iteration W = H^T Y (tcgen05)");
     } else {

@@ -274,6 +274,12 @@ __global__ void __launch_bounds__(kThreadsTC, 2) k_pi_y(const TCBasis* __restric
 // Shared-memory bytes of the fp64 staging region of the persistent W kernel's fused Gram
 // (R <= 64), beside the stage ring: one epilogue warp's 32 rows at a time.
 __host__ __device__ inline int w_stage_bytes(int R) { return R <= 64 ? 32 * w_stage_ld(R) * 8 : 0; }
+// 128-row halves per W tile: two for R <= 64 (two accumulators of 2R columns per TMEM
+// buffer, 2 x 2 x 128 = 512 columns), one above.
+__host__ __device__ inline int w_halves(int R) { return R <= 64 ? 2 : 1; }
+// One stage of the W ring: MT x 128 rows of H (two 64 x 64 boxes per half) and the 2R x 64
+// Y operand they share.
+__host__ __device__ inline int w_ring_stage_bytes(int R, int MT) { return MT * kBM * kBK * 2 + 2 * R * kBK * 2; }
 
 // Persistent W = H^T [Y_hi | Y_lo] (+ the fused fp64 Gram of each W tile for R <= 64).
 // One CTA per SM walks the W tiles of every basis, last basis first: the first tiles then
@@ -281,20 +287,23 @@ __host__ __device__ inline int w_stage_bytes(int R) { return R <= 64 ? 32 * w_st
 // two accumulators, so the epilogue of tile j (W rows stored from the accumulator, the tile
 // staged in fp64 and its Gram formed on the fp64 MMA) runs while the MMA warp accumulates
 // tile j + 1; the stage ring runs on across tiles. Every basis of a plan has the same R.
+// A tile is MT halves of 128 rows: both halves' MMAs read the same Y stage, so the Y
+// operand crosses from L2 once per MT x 128 rows of H, and the Gram partial covers them all.
 //   warp 0     TMA producer (one lane)
 //   warp 1     TMEM owner + MMA issuer (one lane); buffer j & 1 for the CTA's j-th tile
 //   warps 2-5  epilogue; each frees its share of the buffer once its tcgen05.ld are done
 // Barriers per TMEM buffer: tfull (one commit per tile) and tempty (one arrival per
 // epilogue warp). Every wait is bounded; on an error each role stops, waits for its own
 // copies or MMAs in flight, and the CTA frees its TMEM.
+template <int MT>
 __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restrict__ bases, int nb, int ntiles,
                                                        int stages, int* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
   const int R = bases[0].R;
   const int N = 2 * R;
-  const int sbytes = stage_bytes(R);
-  const int a_bytes = kBM * kBK * 2;
+  const int sbytes = w_ring_stage_bytes(R, MT);
+  const int a_bytes = MT * kBM * kBK * 2;
   double* wt = reinterpret_cast<double*>(smem + stages * sbytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes + w_stage_bytes(R));
   uint64_t* empty = full + stages;
@@ -303,7 +312,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int acc_cols = tmem_cols(N);
-  const int ncols = 2 * acc_cols;
+  const int ncols = 2 * MT * acc_cols;
   const int G = gridDim.x;
   const int nmine = (ntiles - static_cast<int>(blockIdx.x) + G - 1) / G;
   auto item_of = [&](int j) { return ntiles - 1 - (static_cast<int>(blockIdx.x) + j * G); };
@@ -343,8 +352,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
           if (g >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
           unsigned char* As = smem + s * sbytes;
           mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
-          tma_load_2d(As, &B->mapHw, tile * kBM, i * kBK, full + s);
-          tma_load_2d(As + a_bytes / 2, &B->mapHw, tile * kBM + 64, i * kBK, full + s);
+#pragma unroll
+          for (int h = 0; h < MT; ++h) {
+            const int x = (tile * MT + h) * kBM;
+            tma_load_2d(As + h * (kBM * kBK * 2), &B->mapHw, x, i * kBK, full + s);
+            tma_load_2d(As + h * (kBM * kBK * 2) + kBM * kBK, &B->mapHw, x + 64, i * kBK, full + s);
+          }
           tma_load_2d(As + a_bytes, &B->mapY2, i * kBK, 0, full + s);
           ++g;
         }
@@ -365,7 +378,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
         const int a = j & 1;
         if (j >= 2 && !mbar_wait(tempty + a, static_cast<uint32_t>((j >> 1) - 1) & 1u, err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t dacc = tmem + static_cast<uint32_t>(a * acc_cols);
+        const uint32_t dacc = tmem + static_cast<uint32_t>(a * MT * acc_cols);
         const TCBasis* B = bases + basis_of(item_of(j));
         const int nk = static_cast<int>((B->T + kBK - 1) / kBK);
         for (int i = 0; i < nk; ++i) {
@@ -375,11 +388,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
           const uint32_t a0 = smem_u32(smem + s * sbytes);
           const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            // A: MN-major 64 x 8 atoms, two along MN 8 KB apart; B: K-major rows of 128 B
-            mma_bf16(dacc, sdesc(a0 + kk * 2048, 8192, 1024), sdesc(b0 + kk * 32, 16, 1024), idesc,
-                     (i > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int h = 0; h < MT; ++h)
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              // A: MN-major 64 x 8 atoms, two along MN 8 KB apart (half h 16 KB on); B: K-major
+              // rows of 128 B, the same for both halves
+              mma_bf16(dacc + static_cast<uint32_t>(h * acc_cols), sdesc(a0 + h * 16384 + kk * 2048, 8192, 1024),
+                       sdesc(b0 + kk * 32, 16, 1024), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           mma_commit(empty + s);
           ++g;
         }
@@ -409,58 +425,71 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
       const TCBasis* B = bases + basis_of(item);
       const int tile = item - B->wtile0;
       const bool gram = B->Gp != nullptr;
-      const uint32_t trow = tmem + static_cast<uint32_t>(a * acc_cols) + (static_cast<uint32_t>(q * 32) << 16);
-      const int64_t d0 = static_cast<int64_t>(tile) * kBM;
-      const bool live = d0 + row < B->D;
-      float* wrow = B->W + (d0 + row) * R;
+      const uint32_t tbase = tmem + static_cast<uint32_t>(a * MT * acc_cols) + (static_cast<uint32_t>(q * 32) << 16);
       if (!gram) {
-        for (int c0 = 0; c0 < R; c0 += 16) {
-          float hi[16], lo[16];
-          tmem_ld16(trow + c0, hi);
-          tmem_ld16(trow + R + c0, lo);
 #pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            if (live)
-              *reinterpret_cast<float4*>(wrow + c0 + c) =
-                  make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
+        for (int h = 0; h < MT; ++h) {
+          const uint32_t trow = tbase + static_cast<uint32_t>(h * acc_cols);
+          const int64_t d = (static_cast<int64_t>(tile) * MT + h) * kBM + row;
+          float* wrow = B->W + d * R;
+          for (int c0 = 0; c0 < R; c0 += 16) {
+            float hi[16], lo[16];
+            tmem_ld16(trow + c0, hi);
+            tmem_ld16(trow + R + c0, lo);
+#pragma unroll
+            for (int c = 0; c < 16; c += 4)
+              if (d < B->D)
+                *reinterpret_cast<float4*>(wrow + c0 + c) =
+                    make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty + a);    // this warp's lanes of the buffer are read
         continue;
       }
-      // R <= 64: the row stays in registers; the buffer is released before the Gram
-      float w[64];
-#pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
-        if (c0 < R) {
-          float hi[16], lo[16];
-          tmem_ld16(trow + c0, hi);
-          tmem_ld16(trow + R + c0, lo);
-#pragma unroll
-          for (int c = 0; c < 16; ++c) w[c0 + c] = hi[c] + lo[c];
-#pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            if (live) *reinterpret_cast<float4*>(wrow + c0 + c) = make_float4(w[c0 + c], w[c0 + c + 1], w[c0 + c + 2], w[c0 + c + 3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty + a);
-      // Gram over the tile's four 32-row quarters, one epilogue warp's rows staged at a time
-      // (rows past D are zero: the H box there is zero filled)
+      // R <= 64: half by half, each thread's row stays in registers for the Gram; the buffer
+      // is released once the last half is read. The Gram runs over the tile's 32-row
+      // quarters in row order, one epilogue warp's rows staged at a time (rows past D are
+      // zero: the H box there is zero filled).
       TileGram gr(tld, R, B->nq, q, lane);
 #pragma unroll 1
-      for (int r = 0; r < 4; ++r) {
-        if (q == r) {
-          double* st = wt + lane * tld;
+      for (int h = 0; h < MT; ++h) {
+        const uint32_t trow = tbase + static_cast<uint32_t>(h * acc_cols);
+        const int64_t d = (static_cast<int64_t>(tile) * MT + h) * kBM + row;
+        const bool live = d < B->D;
+        float* wrow = B->W + d * R;
+        float w[64];
 #pragma unroll
-          for (int c = 0; c < 64; c += 2)
-            if (c < R) *reinterpret_cast<double2*>(st + c) = make_double2(w[c], w[c + 1]);
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          if (c0 < R) {
+            float hi[16], lo[16];
+            tmem_ld16(trow + c0, hi);
+            tmem_ld16(trow + R + c0, lo);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) w[c0 + c] = hi[c] + lo[c];
+#pragma unroll
+            for (int c = 0; c < 16; c += 4)
+              if (live) *reinterpret_cast<float4*>(wrow + c0 + c) = make_float4(w[c0 + c], w[c0 + c + 1], w[c0 + c + 2], w[c0 + c + 3]);
+          }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");   // the quarter is staged
-        gr.rows(wt, tld, 32);
-        asm volatile("bar.sync 1, 128;" ::: "memory");   // the staging region is free again
+        if (h == MT - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty + a);
+        }
+#pragma unroll 1
+        for (int r = 0; r < 4; ++r) {
+          if (q == r) {
+            double* st = wt + lane * tld;
+#pragma unroll
+            for (int c = 0; c < 64; c += 2)
+              if (c < R) *reinterpret_cast<double2*>(st + c) = make_double2(w[c], w[c + 1]);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");   // the quarter is staged
+          gr.rows(wt, tld, 32);
+          asm volatile("bar.sync 1, 128;" ::: "memory");   // the staging region is free again
+        }
       }
       gr.store(B->Gp + static_cast<int64_t>(tile) * B->nq * 64);
     }
