@@ -1,4 +1,5 @@
 // C ABI of libdsmezo: plans, launch sequences and the per-op drop-ins declared in dsmezo.h.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -257,7 +258,6 @@ bool encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int tc_stages(int R);
 
 int pw_stages(int R);
 
@@ -268,23 +268,19 @@ bool tc_shape_ok(int hdt, int64_t D, int64_t ld_H, int64_t h_s1, int64_t R, cons
          (reinterpret_cast<uintptr_t>(H) & 15) == 0 && pw_stages(static_cast<int>(R)) >= 2;
 }
 
-// Y product ring depth: two CTAs per SM when three or more stages fit in half the shared memory.
-int tc_stages(int R) {
-  const int sb = tc::stage_bytes(R);
-  const int half = (227 * 1024) / 2 - 2048;
-  const int two = half / sb;
-  if (two >= 3) return two > 6 ? 6 : two;
-  const int one = (227 * 1024 - 2048) / sb;
-  return one > 4 ? 4 : one;
+// Persistent Y kernel (one CTA per SM): ring of up to six stages of w_halves(R) x 128 rows.
+int py_stages(int R) {
+  const int n = (227 * 1024 - 2048) / tc::ring_stage_bytes(R, tc::w_halves(R));
+  return n > 6 ? 6 : n;
 }
-size_t tc_smem(int R) { return static_cast<size_t>(tc_stages(R)) * tc::stage_bytes(R) + 1024 + 512; }
+size_t py_smem(int R) { return static_cast<size_t>(py_stages(R)) * tc::ring_stage_bytes(R, tc::w_halves(R)) + 1024 + 512; }
 // Persistent W kernel (one CTA per SM): the ring takes what the fp64 staging region leaves.
 int pw_stages(int R) {
-  const int n = (227 * 1024 - 2048 - tc::w_stage_bytes(R)) / tc::w_ring_stage_bytes(R, tc::w_halves(R));
+  const int n = (227 * 1024 - 2048 - tc::w_stage_bytes(R)) / tc::ring_stage_bytes(R, tc::w_halves(R));
   return n > 6 ? 6 : n;
 }
 size_t pw_smem(int R) {
-  return static_cast<size_t>(pw_stages(R)) * tc::w_ring_stage_bytes(R, tc::w_halves(R)) + tc::w_stage_bytes(R) + 1024 +
+  return static_cast<size_t>(pw_stages(R)) * tc::ring_stage_bytes(R, tc::w_halves(R)) + tc::w_stage_bytes(R) + 1024 +
          512;
 }
 
@@ -326,6 +322,9 @@ struct dsmz_plan {
   std::vector<CUtensorMap> smaps;     // side-1 tile boxes of the adapter arrays (4 per matrix)
   size_t off_smaps = 0;
   std::vector<tc::TCBasis> tcb;
+  std::vector<int32_t> ysched;       // Y tiles per CTA of the persistent Y kernel (empty: round-robin)
+  int ysched_G = 0;
+  size_t off_ysched = 0;
   std::vector<TCSlots> tcs;
   size_t off_tcb = 0, err_off = 0;
   int ntc_y = 0, ntc_w = 0, ntc_vt = 0;
@@ -384,6 +383,7 @@ struct dsmz_plan {
     off_bases = T.take(bases.size() * sizeof(BasisD), 64);
     off_tcb = T.take(tcb.size() * sizeof(tc::TCBasis), 64);
     off_smaps = T.take(smaps.size() * sizeof(CUtensorMap), 64);
+    off_ysched = T.take(ysched.size() * sizeof(int32_t), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -395,6 +395,7 @@ struct dsmz_plan {
     if (!bases.empty()) std::memcpy(blob.data() + off_bases, bases.data(), bases.size() * sizeof(BasisD));
     if (!tcb.empty()) std::memcpy(blob.data() + off_tcb, tcb.data(), tcb.size() * sizeof(tc::TCBasis));
     if (!smaps.empty()) std::memcpy(blob.data() + off_smaps, smaps.data(), smaps.size() * sizeof(CUtensorMap));
+    if (!ysched.empty()) std::memcpy(blob.data() + off_ysched, ysched.data(), ysched.size() * sizeof(int32_t));
   }
 };
 
@@ -457,8 +458,8 @@ void plan_tc_layout(dsmz_plan* P) {
     t.y2t = P->ws.take(static_cast<size_t>(2 * b.R) * t.ldy2 * 2, 1024);
     tc::TCBasis& c = P->tcb[i];
     c.T = b.T; c.D = b.D; c.R = b.R; c.ldv2 = t.ldv2; c.ldy2 = t.ldy2;
-    c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + tc::kBM - 1) / tc::kBM); P->ntc_y += c.nytile;
-    const int64_t wrows = static_cast<int64_t>(tc::w_halves(static_cast<int>(b.R))) * tc::kBM;   // rows per W tile
+    const int64_t wrows = static_cast<int64_t>(tc::w_halves(static_cast<int>(b.R))) * tc::kBM;   // rows per tile
+    c.ytile0 = P->ntc_y; c.nytile = static_cast<int32_t>((b.T + wrows - 1) / wrows); P->ntc_y += c.nytile;
     c.wtile0 = P->ntc_w; c.nwtile = static_cast<int32_t>((b.D + wrows - 1) / wrows); P->ntc_w += c.nwtile;
     c.vt0 = P->ntc_vt; c.nvt = static_cast<int32_t>((b.D + tc::kSplitD - 1) / tc::kSplitD); P->ntc_vt += c.nvt;
     if (b.R <= 64) {           // the W epilogue forms the Gram: one block-major partial per W tile
@@ -466,6 +467,28 @@ void plan_tc_layout(dsmz_plan* P) {
       c.nq = nb * (nb + 1) / 2;
       t.gp = P->ws.take(static_cast<size_t>(c.nwtile) * c.nq * 64 * sizeof(double));
     }
+  }
+  // Persistent Y kernel: tiles cost ceil(D / 64) k-steps (plus the epilogue), so with the
+  // SM count known the tiles are dealt longest first, each to the least-loaded CTA.
+  P->ysched.clear();
+  P->ysched_G = 0;
+  if (P->sm_count > 0 && P->ntc_y > 0) {
+    const int G = std::min(P->ntc_y, P->sm_count);
+    std::vector<std::pair<int64_t, int>> items;           // (cost, item)
+    for (const tc::TCBasis& c : P->tcb)
+      for (int t = 0; t < c.nytile; ++t) items.push_back({(c.D + tc::kBK - 1) / tc::kBK + 4, c.ytile0 + t});
+    std::stable_sort(items.begin(), items.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
+    std::vector<int64_t> load(G, 0);
+    std::vector<std::vector<int32_t>> lists(G);
+    for (const auto& it : items) {
+      const int c = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+      load[c] += it.first;
+      lists[c].push_back(it.second);
+    }
+    P->ysched.assign(G + 1, 0);
+    for (int c = 0; c < G; ++c) P->ysched[c + 1] = P->ysched[c] + static_cast<int32_t>(lists[c].size());
+    for (int c = 0; c < G; ++c) P->ysched.insert(P->ysched.end(), lists[c].begin(), lists[c].end());
+    P->ysched_G = G;
   }
 }
 
@@ -610,11 +633,11 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   const int nb = static_cast<int>(P->bases.size());
   const tc::TCBasis* dtcb = reinterpret_cast<const tc::TCBasis*>(P->dev_tables + P->off_tcb);
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
-  const size_t tsm = P->tc ? tc_smem(R) : 0;
   const bool fused = P->tc && R <= 64;                 // W Gram formed in the W epilogue
   const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
   if (P->tc) {
-    if ((rc = set_smem(tc::k_pi_y, tsm))) return rc;
+    if ((rc = set_smem(tc::k_pi_yp<1>, py_smem(R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_yp<2>, py_smem(R)))) return rc;
     if ((rc = set_smem(tc::k_pi_w<1>, pw_smem(R)))) return rc;
     if ((rc = set_smem(tc::k_pi_w<2>, pw_smem(R)))) return rc;
     if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
@@ -628,7 +651,14 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
   for (int it = 0; it < iters; ++it) {
     if (P->tc) {
       P->probe_begin(DSMZ_KID_PI_Y, s);
-      tc::k_pi_y<<<P->ntc_y, tc::kThreadsTC, tsm, s>>>(dtcb, nb, tc_stages(R), err);
+      {
+        const int32_t* ys = P->ysched.empty() ? nullptr : reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ysched);
+        const int gy = ys ? P->ysched_G : std::min(P->ntc_y, P->sm_count);
+        if (tc::w_halves(R) == 2)
+          tc::k_pi_yp<2><<<gy, tc::kThreadsTC, py_smem(R), s>>>(dtcb, nb, P->ntc_y, ys, py_stages(R), err);
+        else
+          tc::k_pi_yp<1><<<gy, tc::kThreadsTC, py_smem(R), s>>>(dtcb, nb, P->ntc_y, ys, py_stages(R), err);
+      }
       P->probe_end(DSMZ_KID_PI_Y, s);
       DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
       P->probe_begin(DSMZ_KID_PI_W, s);

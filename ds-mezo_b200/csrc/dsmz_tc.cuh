@@ -10,7 +10,7 @@
 //   warp 0     TMA producer (one lane): A and B tiles into a ring of smem stages
 //   warp 1     TMEM owner + MMA issuer (one lane): tcgen05.mma kind::f16, M=128, N=2R
 //   warps 2-5  epilogue: tcgen05.ld of the 128 x 2R fp32 accumulator, hi+lo, stores
-// k_pi_y computes one 128-token tile of Y per CTA; k_pi_w is persistent over the W tiles.
+// Both are persistent (one CTA per SM) over tiles of one or two 128-row halves (w_halves).
 // Every mbarrier wait gives up after ~1 s of globaltimer, sets the error word and lets
 // the CTA drain and free its TMEM.
 #pragma once
@@ -104,7 +104,6 @@ __host__ __device__ inline int tmem_cols(int n) {
   while (c < n) c <<= 1;
   return c;
 }
-__host__ __device__ inline int stage_bytes(int R) { return kBM * kBK * 2 + 2 * R * kBK * 2; }
 
 // Upper 8 x 8 blocks of a W tile's Gram W_tile^T W_tile on the fp64 MMA, accumulated over
 // rows staged in shared memory as fp64 (pitch tld); epilogue warp q (of four) owns the
@@ -149,128 +148,6 @@ struct TileGram {
   }
 };
 
-// Y2T = split(H [V_hi | V_lo]): one 128-token tile per CTA, two CTAs per SM.
-__global__ void __launch_bounds__(kThreadsTC, 2) k_pi_y(const TCBasis* __restrict__ bases, int nb, int stages,
-                                                       int* err) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte aligned base for the swizzled stages
-  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
-  const int item = blockIdx.x;
-  const int bi = find_owner(bases, nb, item, [](const TCBasis& b) { return b.ytile0; });
-  const TCBasis* B = bases + bi;
-  const int R = B->R;
-  const int N = 2 * R;
-  const int tile = item - B->ytile0;
-  const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
-  const int sbytes = stage_bytes(R);
-  const int a_bytes = kBM * kBK * 2;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes);
-  uint64_t* empty = full + stages;
-  uint64_t* tmem_full = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncols = tmem_cols(N);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    mbar_init(tmem_full, 1);
-    mbar_init_fence();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tmap_acquire(&B->mapHy);
-      tmap_acquire(&B->mapV2);
-      int issued = 0;
-      bool ok = true;
-      for (int i = 0; i < nk && ok; ++i) {
-        const int s = i % stages;
-        const uint32_t u = static_cast<uint32_t>(i / stages);
-        if (i >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
-        unsigned char* As = smem + s * sbytes;
-        mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
-        tma_load_2d(As, &B->mapHy, i * kBK, tile * kBM, full + s);
-        tma_load_2d(As + a_bytes, &B->mapV2, i * kBK, 0, full + s);
-        issued = i + 1;
-      }
-      if (!ok) {
-        // let the loads already issued land before the CTA can exit
-        for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
-          mbar_drain(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(N, 0, 0);
-      bool ok = true;
-      int done = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(full + s, static_cast<uint32_t>(i / stages) & 1u, err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + s * sbytes);
-        const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)       // A and B: K-major rows of 128 B
-          mma_bf16(tmem, sdesc(a0 + kk * 32, 16, 1024), sdesc(b0 + kk * 32, 16, 1024), idesc,
-                   (i > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(empty + s);
-        done = i + 1;
-      }
-      mma_commit(tmem_full);
-      if (!ok && done > 0) mbar_wait(tmem_full, 0, err);
-    }
-  } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const bool mine = mbar_wait(tmem_full, 0, err);
-    // one verdict for the four epilogue warps, so none waits at a barrier the others skip
-    uint32_t all_ok;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(all_ok)
-        : "r"(static_cast<uint32_t>(mine))
-        : "memory");
-    tc_fence_after();
-    if (all_ok != 0) {
-      const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
-      const int64_t t = static_cast<int64_t>(tile) * kBM + row;
-      for (int j = 0; j < R; j += 16) {
-        float hi[16], lo[16];
-        tmem_ld16(trow + j, hi);
-        tmem_ld16(trow + R + j, lo);
-        if (t < B->T) {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float y = hi[c] + lo[c];
-            const __nv_bfloat16 yh = __float2bfloat16_rn(y);
-            const __nv_bfloat16 yl = __float2bfloat16_rn(y - __bfloat162float(yh));
-            B->Y2T[static_cast<int64_t>(j + c) * B->ldy2 + t] = yh;
-            B->Y2T[static_cast<int64_t>(R + j + c) * B->ldy2 + t] = yl;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
-  }
-}
-
 // Shared-memory bytes of the fp64 staging region of the persistent W kernel's fused Gram
 // (R <= 64), beside the stage ring: one epilogue warp's 32 rows at a time.
 __host__ __device__ inline int w_stage_bytes(int R) { return R <= 64 ? 32 * w_stage_ld(R) * 8 : 0; }
@@ -279,7 +156,7 @@ __host__ __device__ inline int w_stage_bytes(int R) { return R <= 64 ? 32 * w_st
 __host__ __device__ inline int w_halves(int R) { return R <= 64 ? 2 : 1; }
 // One stage of the W ring: MT x 128 rows of H (two 64 x 64 boxes per half) and the 2R x 64
 // Y operand they share.
-__host__ __device__ inline int w_ring_stage_bytes(int R, int MT) { return MT * kBM * kBK * 2 + 2 * R * kBK * 2; }
+__host__ __device__ inline int ring_stage_bytes(int R, int MT) { return MT * kBM * kBK * 2 + 2 * R * kBK * 2; }
 
 // Persistent W = H^T [Y_hi | Y_lo] (+ the fused fp64 Gram of each W tile for R <= 64).
 // One CTA per SM walks the W tiles of every basis, last basis first: the first tiles then
@@ -302,7 +179,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
   const int R = bases[0].R;
   const int N = 2 * R;
-  const int sbytes = w_ring_stage_bytes(R, MT);
+  const int sbytes = ring_stage_bytes(R, MT);
   const int a_bytes = MT * kBM * kBK * 2;
   double* wt = reinterpret_cast<double*>(smem + stages * sbytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes + w_stage_bytes(R));
@@ -492,6 +369,166 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_w(const TCBasis* __restric
         }
       }
       gr.store(B->Gp + static_cast<int64_t>(tile) * B->nq * 64);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+// Persistent Y2T = split(H [V_hi | V_lo]) for tiles of MT x 128 tokens: one CTA per SM, two
+// TMEM accumulators (the epilogue of tile j overlaps the mainloop of tile j + 1), the ring
+// running on across tiles, both halves' MMAs sharing each V stage. Tiles cost ceil(D / 64)
+// k-steps, so bases of different widths make them uneven: with `sched` (built on the host,
+// longest tiles first, each to the least-loaded CTA) CTA b takes the tiles
+// sched[G + 1 + sched[b] .. G + 1 + sched[b + 1]); without it, tiles b, b + G, ...
+// Roles, barriers and error handling as in k_pi_w.
+template <int MT>
+__global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restrict__ bases, int nb, int ntiles,
+                                                        const int32_t* __restrict__ sched, int stages, int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // stays a shared pointer
+  const int R = bases[0].R;
+  const int N = 2 * R;
+  const int sbytes = ring_stage_bytes(R, MT);
+  const int a_bytes = MT * kBM * kBK * 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * sbytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;     // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int acc_cols = tmem_cols(N);
+  const int ncols = 2 * MT * acc_cols;
+  const int G = gridDim.x;
+  const int b = static_cast<int>(blockIdx.x);
+  const int first = sched ? sched[b] : 0;
+  const int nmine = sched ? sched[b + 1] - first : (ntiles - b + G - 1) / G;
+  auto item_of = [&](int j) { return sched ? sched[G + 1 + first + j] : b + j * G; };
+  auto basis_of = [&](int item) { return find_owner(bases, nb, item, [](const TCBasis& c) { return c.ytile0; }); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 4); }
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      int cur = -1;
+      bool ok = true;
+      for (int j = 0; j < nmine && ok; ++j) {
+        const int item = item_of(j);
+        const int bi = basis_of(item);
+        const TCBasis* B = bases + bi;
+        if (bi != cur) { tmap_acquire(&B->mapHy); tmap_acquire(&B->mapV2); cur = bi; }
+        const int tile = item - B->ytile0;
+        const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
+          const int s = g % stages;
+          const uint32_t u = static_cast<uint32_t>(g / stages);
+          if (g >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
+          unsigned char* As = smem + s * sbytes;
+          mbar_expect_tx(full + s, static_cast<uint32_t>(sbytes));
+#pragma unroll
+          for (int h = 0; h < MT; ++h)
+            tma_load_2d(As + h * (kBM * kBK * 2), &B->mapHy, i * kBK, (tile * MT + h) * kBM, full + s);
+          tma_load_2d(As + a_bytes, &B->mapV2, i * kBK, 0, full + s);
+          ++g;
+        }
+      }
+      if (!ok) {
+        for (int i = (g > stages ? g - stages : 0); i < g; ++i)
+          mbar_drain(full + (i % stages), static_cast<uint32_t>(i / stages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(N, 0, 0);
+      int g = 0;
+      bool ok = true;
+      int last = -1;
+      for (int j = 0; j < nmine && ok; ++j) {
+        const int a = j & 1;
+        if (j >= 2 && !mbar_wait(tempty + a, static_cast<uint32_t>((j >> 1) - 1) & 1u, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dacc = tmem + static_cast<uint32_t>(a * MT * acc_cols);
+        const TCBasis* B = bases + basis_of(item_of(j));
+        const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
+          const int s = g % stages;
+          if (!mbar_wait(full + s, static_cast<uint32_t>(g / stages) & 1u, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * sbytes);
+          const uint32_t b0 = a0 + static_cast<uint32_t>(a_bytes);
+#pragma unroll
+          for (int h = 0; h < MT; ++h)
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)   // A and B: K-major rows of 128 B (half h 16 KB on)
+              mma_bf16(dacc + static_cast<uint32_t>(h * acc_cols), sdesc(a0 + h * 16384 + kk * 32, 16, 1024),
+                       sdesc(b0 + kk * 32, 16, 1024), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(empty + s);
+          ++g;
+        }
+        mma_commit(tfull + a);
+        last = j;
+      }
+      if (!ok && last >= 0) mbar_drain(tfull + (last & 1), static_cast<uint32_t>(last >> 1) & 1u);
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    for (int j = 0; j < nmine; ++j) {
+      const int a = j & 1;
+      const bool mine = mbar_wait(tfull + a, static_cast<uint32_t>(j >> 1) & 1u, err);
+      uint32_t all_ok;
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+          : "=r"(all_ok)
+          : "r"(static_cast<uint32_t>(mine))
+          : "memory");
+      if (all_ok == 0) break;
+      tc_fence_after();
+      const int item = item_of(j);
+      const TCBasis* B = bases + basis_of(item);
+      const int tile = item - B->ytile0;
+      const uint32_t tbase = tmem + static_cast<uint32_t>(a * MT * acc_cols) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll
+      for (int h = 0; h < MT; ++h) {
+        const int64_t t = (static_cast<int64_t>(tile) * MT + h) * kBM + row;
+        for (int c0 = 0; c0 < R; c0 += 16) {
+          float hi[16], lo[16];
+          tmem_ld16(tbase + static_cast<uint32_t>(h * acc_cols) + c0, hi);
+          tmem_ld16(tbase + static_cast<uint32_t>(h * acc_cols) + R + c0, lo);
+          if (t < B->T) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const float y = hi[c] + lo[c];
+              const __nv_bfloat16 yh = __float2bfloat16_rn(y);
+              const __nv_bfloat16 yl = __float2bfloat16_rn(y - __bfloat162float(yh));
+              B->Y2T[static_cast<int64_t>(c0 + c) * B->ldy2 + t] = yh;
+              B->Y2T[static_cast<int64_t>(R + c0 + c) * B->ldy2 + t] = yl;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + a);    // this warp's lanes of the buffer are read
     }
   }
   tc_fence_before();
