@@ -158,9 +158,9 @@ def alg_bytes(aset, cfg):
 # DRAM bytes per algorithmic byte of each kernel, from ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on the 4-layer cut of the 7B workload, whose launches read more
 # than L2 holds; the full workload's launches do the same work per unit, so traffic scales
-# with the algorithmic bytes (the k_pi_y / k_pi_w and adapter-kernel summaries under profiles/).
-TRAFFIC_PER_ALG_BYTE = {"pi_y": 1.001, "pi_w": 1.010, "perturb": 0.925, "gram": 0.899, "apply": 0.862,
-                        "bside": 0.926}
+# with the algorithmic bytes (the k_pi_yp / k_pi_w and adapter-kernel summaries under profiles/).
+TRAFFIC_PER_ALG_BYTE = {"pi_y": 1.002, "pi_w": 1.002, "perturb": 0.925, "gram": 0.899, "apply": 0.862,
+                        "bside": 0.981}
 
 
 # ----------------------------------------------------------------------------- CPU oracle
