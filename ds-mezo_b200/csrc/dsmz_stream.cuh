@@ -687,25 +687,31 @@ __device__ __forceinline__ void init_bars(uint64_t* full, uint64_t* empty, int S
 // which returns the same first value of the Box-Muller pair).
 // =====================================================================================
 __global__ void __launch_bounds__(256) k_draw_zca(Tables tb, uint64_t seed, uint64_t base_off) {
-  const int mi = find_owner(tb.mods, tb.nmods, static_cast<int>(blockIdx.x), [](const ModD& d) { return d.dblk0; });
-  const ModD D = tb.mods[mi];
-  const int64_t idx = static_cast<int64_t>(blockIdx.x - D.dblk0) * 256 + threadIdx.x;
-  const int64_t thr = D.thrA;
-  const int64_t n = D.d_out * D.rca;
-  if (idx >= thr || idx >= n) return;
-  float* out = reinterpret_cast<float*>(tb.ws) + D.zca_off;
-  curandStatePhilox4_32_10_t st;
-  curand_init(seed, static_cast<unsigned long long>(idx), base_off + D.offA, &st);
-  if (n <= thr) {
-    out[idx] = curand_normal(&st);
-    return;
-  }
-  for (int64_t base = idx; base < n; base += 4 * thr) {
-    const float4 g = curand_normal4(&st);
-    out[base] = g.x;
-    if (base + thr < n) out[base + thr] = g.y;
-    if (base + 2 * thr < n) out[base + 2 * thr] = g.z;
-    if (base + 3 * thr < n) out[base + 3 * thr] = g.w;
+  // grid-stride over the torch launch's blocks (256 of its threads each); the module index
+  // only moves forward, so one search per CTA
+  int mi = -1;
+  for (int vb = static_cast<int>(blockIdx.x); vb < tb.ndblk; vb += static_cast<int>(gridDim.x)) {
+    if (mi < 0) mi = find_owner(tb.mods, tb.nmods, vb, [](const ModD& d) { return d.dblk0; });
+    while (mi + 1 < tb.nmods && tb.mods[mi + 1].dblk0 <= vb) ++mi;
+    const ModD& D = tb.mods[mi];
+    const int64_t idx = static_cast<int64_t>(vb - D.dblk0) * 256 + threadIdx.x;
+    const int64_t thr = D.thrA;
+    const int64_t n = D.d_out * D.rca;
+    if (idx >= thr || idx >= n) continue;
+    float* out = reinterpret_cast<float*>(tb.ws) + D.zca_off;
+    curandStatePhilox4_32_10_t st;
+    curand_init(seed, static_cast<unsigned long long>(idx), base_off + D.offA, &st);
+    if (n <= thr) {
+      out[idx] = curand_normal(&st);
+      continue;
+    }
+    for (int64_t base = idx; base < n; base += 4 * thr) {
+      const float4 g = curand_normal4(&st);
+      out[base] = g.x;
+      if (base + thr < n) out[base + thr] = g.y;
+      if (base + 2 * thr < n) out[base + 2 * thr] = g.z;
+      if (base + 3 * thr < n) out[base + 3 * thr] = g.w;
+    }
   }
 }
 
