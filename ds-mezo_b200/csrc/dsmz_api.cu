@@ -779,7 +779,7 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
     td.dir = k;
     const uint64_t off = offset + static_cast<uint64_t>(k) * P->rng_dir_stride;
     P->probe_begin(DSMZ_KID_DRAW, s);
-    sk::k_draw_zca<<<std::min(P->ndblk, 8 * P->sm_count), 256, 0, s>>>(td, seed, off);
+    sk::k_draw_zca<<<std::min(P->ndblk, 16 * P->sm_count), 256, 0, s>>>(td, seed, off);
     P->probe_end(DSMZ_KID_DRAW, s);
     DSMZ_LAUNCHED("Zc_A draws");
     P->probe_begin(DSMZ_KID_COEF, s);
