@@ -64,10 +64,10 @@ class ClockSampler:
     def __init__(self, gpus):
         self.gpus = gpus
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        import tempfile
+        self.path = os.path.join(tempfile.gettempdir(), f"dsmezo_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -115,11 +115,13 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- setup
 def init_set(aset, cfg, device, layer0):
-    """Seeded synthetic state: factors and momentum ~ N(0,1), var = eps^2, bases = QR of a
-    Gaussian, activations N(0,1) x lognormal(0,1) channel scales."""
+    """Seeded synthetic state: factors and momentum ~ N(0,1) (the factors rounded to the copy
+    dtype and held as fp32 masters), var = eps^2, bases = QR of a Gaussian, activations
+    N(0,1) x lognormal(0,1) channel scales."""
     g = torch.Generator(device=device)
     g.manual_seed(cfg["seed"] * 1000 + layer0)
-    aset.factors[: aset.numel].copy_(torch.randn(aset.numel, generator=g, device=device))
+    aset.factors[: aset.numel].copy_(torch.randn(aset.numel, generator=g, device=device).to(DT[cfg["fdt"]]))
+    aset.sync_shadow()
     aset.mu.normal_(generator=g)
     aset.var.fill_(EPS ** 2)
     for b, s in enumerate(aset.bases):
@@ -129,8 +131,10 @@ def init_set(aset, cfg, device, layer0):
 
 
 def alg_bytes(aset, cfg):
-    """Algorithmic bytes per launch of each streaming kernel (whole set)."""
-    f = aset.factors.element_size()
+    """Algorithmic bytes per launch of each streaming kernel (whole set). Masters, momentum,
+    variance and z are fp32; f is the copy dtype's size (the +/- copies and the shadow)."""
+    f = aset.pos.element_size()
+    fs = f if aset.shadow is not None else 0
     N = aset.numel
     K = aset.directions
     hb = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
@@ -147,11 +151,11 @@ def alg_bytes(aset, cfg):
         "pi_gram": gp if R <= 64 else vr,          # read the per-tile Gram partials (else W)
         "pi_apply": 3 * vr,                        # read W; write V (fp32) and [V_hi|V_lo]^T (bf16)
         "pi_split": 2 * vr,                        # read V, write bf16 [V_hi | V_lo]^T
-        "bside": nB * (f + 8),                     # read B, var_B and the basis rows
-        "perturb": N * (3 * f + 16),               # read p, mu, var, K-operand rows; write pos, neg, z
+        "bside": nB * 12,                          # read B, var_B and the basis rows
+        "perturb": N * (2 * f + 20),               # read p, mu, var, K-operand rows; write pos, neg, z
         "gram": N * 20 if K == 1 else N * 4,       # read mu, var, z, write mu, var (K > 1: read mu2)
         "kalman_dirs": N * (16 + 4 * K),           # read mu, var, K z; write mu, var
-        "apply": N * (f + 4 + f),                  # read p, mu2; write p
+        "apply": N * (12 + fs),                    # read p, mu2; write p and its shadow
     }
 
 
@@ -237,7 +241,7 @@ def main():
     gen.manual_seed(cfg["seed"])
     K = cfg.get("directions", 1)
     sstep = ShardedStep(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"], cfg["tokens"], eps=EPS,
-                        total_steps=TOTAL_STEPS, generator=gen, factor_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
+                        total_steps=TOTAL_STEPS, generator=gen, copy_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
                         schedule=cfg["schedule"], device=device, process_group=pg, directions=K)
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
@@ -468,11 +472,12 @@ def main():
             v["alg_GBps"] = ab[k] / (v["avg_ms"] * 1e-3) / 1e9
             v["frac_hbm"] = v["alg_GBps"] / hbm
     # whole model: every rank's factors and activations
-    f = aset.factors.element_size()
+    f = aset.pos.element_size()
+    fs = f if aset.shadow is not None else 0
     act_layer = cfg["tokens"] * (3 * cfg["hidden"] + cfg["inter"]) * aset.H_arena.element_size()
-    # per element: read p, mu, var and write p, mu, var once; per direction write pos, neg, z
-    # and read z back (K > 1)
-    per_elem = 2 * f + 16 + K * (2 * f + (4 if K == 1 else 8))
+    # per element: read and write the fp32 master, mu and var once, write the shadow; per
+    # direction write pos, neg, z and read z back (K > 1)
+    per_elem = 24 + fs + K * (2 * f + (4 if K == 1 else 8))
     # activations: each of the 3 power iterations reads H twice (Y = H V, then W = H^T Y)
     step_bytes = sum(sstep.layout.sizes) * per_elem + 2 * 3 * act_layer * cfg["layers"]
     # the reference's power iteration reads each activation once per iteration (Y and H^T Y
@@ -491,7 +496,7 @@ def main():
         "momentum, lognormal-scaled N(0,1) activations)",
         "config": {"workload": cfg["workload"], "layers": cfg["layers"], "hidden": cfg["hidden"],
                    "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
-                   "factor_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
+                   "copy_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
                    "directions": K,
                    "power_iters": 3, "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (activations %.2f GB per step per GPU)" %

@@ -313,9 +313,10 @@ struct dsmz_plan {
   uint64_t rng_inc1 = 0, rng_dir_stride = 0;   // one direction's generator advance (this plan / all ranks)
   sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
   sk::Layout Lw{};                     // Gram of the power-iteration W
-  int factor_dtype = DSMZ_F32;
+  int copy_dtype = DSMZ_F32;          // +/- copies and shadows (the masters are fp32)
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
+  size_t norm_off = 0;                // fp64 partials of the factor norms (kNormSlices per matrix)
   uint64_t rng_increment = 0;
   // tensor-core power iteration
   bool tc = false;
@@ -360,7 +361,7 @@ struct dsmz_plan {
     t.wB = reinterpret_cast<const MatD*>(dev_tables + off_w2);
     t.nwsegsA = nwsegsA;
     t.nwsegsB = nwsegsB;
-    t.factor_dtype = factor_dtype;
+    t.copy_dtype = copy_dtype;
     t.ndblk = ndblk;
     t.ws = workspace;
     t.seg_kal_off = seg_kal_off;
@@ -500,7 +501,7 @@ void bind_side1_maps(dsmz_plan* P) {
     if (m.tmap < 0) continue;
     bool ok = TV <= 256 && m.r <= 256 && m.cs == 1;
     const void* arr[4] = {m.param, m.mu, m.var, m.z};
-    const int dt[4] = {P->factor_dtype, DSMZ_F32, DSMZ_F32, DSMZ_F32};
+    const int dt[4] = {DSMZ_F32, DSMZ_F32, DSMZ_F32, DSMZ_F32};
     for (int j = 0; j < 4 && ok; ++j) {
       const int es = (dt[j] == DSMZ_BF16) ? 2 : 4;
       ok = ((reinterpret_cast<uintptr_t>(arr[j]) & 15) == 0) && ((m.ld * es) % 16 == 0) &&
@@ -564,12 +565,12 @@ bool bind_tc(dsmz_plan* P) {
 // most sk::stream_tv(r)) whose perturbation, Gram and apply layouts all fit with a ring
 // of at least kTeams stages for the team kernels (two for the Gram). One width for all of
 // them: their segments (Kalman and Gram partials) follow the same tile chunks.
-bool choose_adapter_layouts(dsmz_plan* P, int fes) {
+bool choose_adapter_layouts(dsmz_plan* P) {
   const int r = P->r, rca = P->r < P->RC ? P->r : P->RC;
   for (int tv = sk::stream_tv(r); tv >= 8; tv = (tv / 2) & ~7) {
-    P->Lp = sk::perturb_layout(r, r, P->RC, rca, fes, 0, kStreamSmem, tv);
+    P->Lp = sk::perturb_layout(r, r, P->RC, rca, kStreamSmem, tv);
     P->Lg = sk::gram_layout(r, 1, kStreamSmem, tv);
-    P->La = sk::apply_layout(r, fes, kStreamSmem, tv);
+    P->La = sk::apply_layout(r, kStreamSmem, tv);
     const bool ok = P->Lp.S >= sk::kTeams && P->La.S >= sk::kTeams && P->Lg.S >= 2 &&
                     P->Lp.total <= kStreamSmem + 2048 && P->La.total <= kStreamSmem + 2048 &&
                     P->Lg.total <= kStreamSmem + 2048;
@@ -740,7 +741,7 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
-  if (P->factor_dtype == DSMZ_BF16)
+  if (P->copy_dtype == DSMZ_BF16)
     sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   else
     sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
@@ -767,9 +768,9 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   const size_t cs = coef_smem(P->r, P->RC);
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
   if ((rc = set_smem(k_coef<0>, cs))) return rc;
-  const bool bf = P->factor_dtype == DSMZ_BF16;
-  if ((rc = set_smem(sk::k_sperturb<0, 2>, P->Lp.total))) return rc;
-  if ((rc = set_smem(sk::k_sperturb<0, 4>, P->Lp.total))) return rc;
+  const bool bf = P->copy_dtype == DSMZ_BF16;
+  if ((rc = set_smem(sk::k_sperturb<2>, P->Lp.total))) return rc;
+  if ((rc = set_smem(sk::k_sperturb<4>, P->Lp.total))) return rc;
   P->probe_begin(DSMZ_KID_BSIDE, s);
   k_bside<<<P->nchunks, kThreads, 0, s>>>(tb, P->bside_cols);     // B V and var_B V^2: the same for every direction
   P->probe_end(DSMZ_KID_BSIDE, s);
@@ -787,8 +788,8 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
     P->probe_end(DSMZ_KID_COEF, s);
     DSMZ_LAUNCHED("AGZO coefficients");
     P->probe_begin(DSMZ_KID_PERTURB, s);
-    if (bf) sk::k_sperturb<0, 2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
-    else sk::k_sperturb<0, 4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
     P->probe_end(DSMZ_KID_PERTURB, s);
     DSMZ_LAUNCHED("perturbation");
     P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
@@ -822,7 +823,7 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
-  if (P->factor_dtype == DSMZ_BF16)
+  if (P->copy_dtype == DSMZ_BF16)
     sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
   else
     sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
@@ -831,6 +832,43 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   return 0;
 }
 
+}  // namespace
+
+// Context lookups of the allocation-free ZO-Muon entry (its scratch array is defined with it).
+namespace {
+struct NoallocSlot {
+  unsigned long long ctx_id = 0;   // 0: no lookup yet
+  void* addr = nullptr;
+};
+std::mutex g_noalloc_mutex;
+NoallocSlot g_noalloc_slot[256];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique ID (never reused in the process) of the calling thread's current context, or 0
+// when there is none yet or the driver cannot say.
+unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_cur || !get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_cur(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 }  // namespace
 
 // ====================================================================== C ABI
@@ -988,8 +1026,8 @@ int dsmz_contrastive_loss(int32_t kind, const void* src, int64_t V, int64_t ld, 
 int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   if (!d || !out) return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: null argument");
   *out = nullptr;
-  if (d->factor_dtype != DSMZ_F32 && d->factor_dtype != DSMZ_BF16)
-    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: factor_dtype must be DSMZ_F32 or DSMZ_BF16");
+  if (d->copy_dtype != DSMZ_F32 && d->copy_dtype != DSMZ_BF16)
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: copy_dtype must be DSMZ_F32 or DSMZ_BF16");
   if (d->num_modules < 0 || d->num_bases < 0 || (d->num_modules > 0 && !d->modules) ||
       (d->num_bases > 0 && !d->bases))
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: bad module/basis arrays");
@@ -1000,7 +1038,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   if (d->directions > 1 && (d->dir_stride_factor <= 0 || d->dir_stride_z <= 0))
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_create: several directions need positive direction strides");
   auto* P = new dsmz_plan();
-  P->factor_dtype = d->factor_dtype;
+  P->copy_dtype = d->copy_dtype;
   P->sm_count = d->sm_count;
   P->ndir = d->directions > 1 ? d->directions : 1;
   P->dstride_f = P->ndir > 1 ? d->dir_stride_factor : 0;
@@ -1080,7 +1118,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     md.offA = off;
     off += dsmz_randn_offset_increment(nA, d->sm_count, d->max_threads_per_sm);
     md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
-    md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1; md.bdt = d->factor_dtype;
+    md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1;
     md.zca_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(nA) * sizeof(float)) / sizeof(float));
     md.dblk0 = P->ndblk;
     md.ndblk = static_cast<int32_t>(md.thrA / 256);
@@ -1089,10 +1127,12 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     md.b = md.a + 1;
     MatD a{};
     a.param = m.A; a.pos = m.pos_A; a.neg = m.neg_A; a.mu = m.mu_A; a.var = m.var_A; a.z = m.z_A;
+    a.shadow = m.shadow_A;
     a.scratch = m.scratch_A; a.nvec = m.d_out; a.r = m.r; a.ld = m.ld_A; a.cs = 1; a.side = 0; a.owner = i;
     add_matrix(P->mats, P->ws, a, P->nsegs, true, false);
     MatD b{};
     b.param = m.B; b.pos = m.pos_B; b.neg = m.neg_B; b.mu = m.mu_B; b.var = m.var_B; b.z = m.z_B;
+    b.shadow = m.shadow_B;
     b.scratch = m.scratch_B; b.nvec = m.d_in; b.r = m.r; b.ld = m.ld_B; b.cs = 1; b.side = 1; b.owner = i;
     add_matrix(P->mats, P->ws, b, P->nsegs, true, false);
     P->mods.push_back(md);
@@ -1103,8 +1143,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
   // streaming layouts, then the tile chunks they imply, then the per-segment buffers
-  const int fes = (P->factor_dtype == DSMZ_BF16) ? 2 : 4;
-  if (P->r > 0 && !choose_adapter_layouts(P, fes)) {
+  if (P->r > 0 && !choose_adapter_layouts(P)) {
     delete P;
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");
   }
@@ -1132,6 +1171,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   }
   P->seg_kal_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(P->nsegs > 0 ? P->nsegs : 1) * 2 * sizeof(double)) / sizeof(double));
   P->kal_sum_off = static_cast<int64_t>(P->ws.take(2 * static_cast<size_t>(P->ndir) * sizeof(double)) / sizeof(double));
+  P->norm_off = P->ws.take((P->mats.empty() ? 1 : P->mats.size()) * kNormSlices * sizeof(double));
   P->pack();
   *out = P;
   return DSMZ_OK;
@@ -1222,6 +1262,21 @@ double* dsmz_step_kalman_sums(const dsmz_plan* P) {
 }
 
 int32_t dsmz_plan_directions(const dsmz_plan* P) { return P ? P->ndir : 0; }
+
+int dsmz_plan_factor_norms(const dsmz_plan* P, float* norms, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_plan_factor_norms");
+  if (rc) return rc;
+  if (!norms) return fail(DSMZ_ERR_INVALID, "dsmz_plan_factor_norms: null output");
+  if (P->mats.empty()) return DSMZ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nm = static_cast<int>(P->mats.size());
+  double* part = reinterpret_cast<double*>(P->workspace + P->norm_off);
+  k_norm_partial<<<dim3(nm, kNormSlices), kThreads, 0, s>>>(P->tables(), part);
+  DSMZ_LAUNCHED("factor norms");
+  k_norm_finish<<<(nm + kThreads - 1) / kThreads, kThreads, 0, s>>>(part, nm, norms);
+  DSMZ_LAUNCHED("factor norms (sum)");
+  return DSMZ_OK;
+}
 
 int dsmz_step_update_directions(const dsmz_plan* P, const float* dd, int32_t n, float beta, float q, float eta,
                                 float norm_floor, const dsmz_ns_schedule* schedule, dsmz_stream_t stream) {
@@ -1334,7 +1389,6 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
   m.param = param; m.mu = const_cast<float*>(buf); m.scratch = scratch;
   m.ld = ps0; m.cs = ps1;   // side B (wide) swaps roles inside vaddr2: element (k=row, v=col)
   P.workspace = static_cast<char*>(workspace);
-  P.factor_dtype = param_dtype;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = upload_small(&P, static_cast<char*>(workspace), s);
   if (rc) return rc;
@@ -1482,7 +1536,7 @@ int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t bs0,
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(DSMZ_ERR_INVALID, "agzo_perturbation: workspace must be 256-byte aligned");
   ModD& md = P.mods[0];
-  md.zcB_ext = zcB; md.zcA_ext = zcA; md.Bp = B; md.varB = nullptr; md.b_s0 = bs0; md.b_s1 = bs1; md.bdt = DSMZ_F32;
+  md.zcB_ext = zcB; md.zcA_ext = zcA; md.Bp = B; md.varB = nullptr; md.b_s0 = bs0; md.b_s1 = bs1;
   P.mats[0].z = z_A;
   P.mats[1].z = z_B;
   BasisD& bd = P.bases[0];
@@ -1495,12 +1549,12 @@ int dsmz_agzo_perturbation(const float* B, int64_t R, int64_t d_in, int64_t bs0,
   const size_t cs = coef_smem(static_cast<int>(R), static_cast<int>(RC));
   const size_t ps = perturb_smem(static_cast<int>(R), static_cast<int>(R), static_cast<int>(RC));
   if ((rc = set_smem(k_coef<1>, cs))) return rc;
-  if ((rc = set_smem(k_perturb<1>, ps))) return rc;
+  if ((rc = set_smem(k_perturb, ps))) return rc;
   k_bside<<<P.nchunks, kThreads, 0, s>>>(tb, P.bside_cols);
   DSMZ_LAUNCHED("agzo B V");
   k_coef<1><<<1, kThreads, cs, s>>>(tb, 0, 0, norm_floor, 1);
   DSMZ_LAUNCHED("agzo QR");
-  k_perturb<1><<<P.nsegs, kThreads, ps, s>>>(tb, 0, 0, eps, KalmanIn{});
+  k_perturb<<<P.nsegs, kThreads, ps, s>>>(tb, eps);
   DSMZ_LAUNCHED("agzo z");
   return DSMZ_OK;
 }
@@ -1520,10 +1574,12 @@ int dsmz_perturb_dual(int32_t dtype, const void* base, const float* z, void* pos
 // ---------------------------------------------------------------------- allocation-free ZO-Muon
 // Scratch of dsmz_zo_muon_update_noalloc: a fixed array in this library, held by every GPU
 // that loads it until the process exits. Host code must not use the symbol's host-side
-// address; the device address is looked up once per device below.
+// address; its device address is looked up with the device current and cached per device
+// together with the unique ID of the context the lookup ran in. A different current context
+// on that device (a context the caller made current, or the primary context created again
+// after cudaDeviceReset) has its own copy of the array, so the lookup is repeated for it.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[DSMZ_NOALLOC_SCRATCH_BYTES];
-static std::mutex g_noalloc_mutex;
-static void* g_noalloc_addr[256];
+
 
 int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t ps0, int64_t ps1, const float* buf,
                                 int64_t bs0, int64_t bs1, float* scratch, int64_t ss0, int64_t ss1, int64_t M,
@@ -1543,13 +1599,16 @@ int dsmz_zo_muon_update_noalloc(int32_t param_dtype, void* param, int64_t ps0, i
   void* ws = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_addr[dev]) {
+    NoallocSlot& slot = g_noalloc_slot[dev];
+    const unsigned long long id = current_ctx_id();
+    if (id == 0 || slot.ctx_id != id || !slot.addr) {
       void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // once per device, that device current
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // with this device (and context) current
       if (e != cudaSuccess) return cuda_fail("zo_muon_update_noalloc: cudaGetSymbolAddress", e);
-      g_noalloc_addr[dev] = p;
+      slot.addr = p;
+      slot.ctx_id = current_ctx_id();   // the lookup has created the primary context if there was none
     }
-    ws = g_noalloc_addr[dev];
+    ws = slot.addr;
   }
   // Every slot the kernels read (tables, Gram partials, solve workspace, apply matrix) is
   // written earlier in the same call, so nothing has to be cleared between calls.

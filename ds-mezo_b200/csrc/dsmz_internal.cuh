@@ -19,6 +19,7 @@ constexpr int kThreads = 256;
 struct MatD {
   void* param; void* pos; void* neg;
   float* mu; float* var; float* z; float* scratch;
+  void* shadow;               // adapters: copy-dtype image of the updated master (NULL: none)
   int64_t nvec, r, ld, cs;    // element (v, k) at side A: v*ld + k*cs, side B: k*ld + v*cs
   int32_t side, owner;        // owner: module index (adapters) or basis index (power iteration)
   int32_t seg0, nseg;         // global index of the first vector segment, segment count
@@ -52,10 +53,9 @@ struct ModD {
   int64_t bpart_off;          // floats: nchunk * 2 * r*rc partial sums (B V, var_B V^2)
   const float* zcB_ext;       // explicit Zc_B (R x RC) / Zc_A (d_out x RCA) for the drop-in op
   const float* zcA_ext;
-  const void* Bp;             // B factor (R x d_in) and its variance, read by the B-side sums
+  const float* Bp;            // B factor (R x d_in, fp32) and its variance, read by the B-side sums
   const float* varB;          // NULL: skip var_B V^2 (drop-in op)
   int64_t b_s0, b_s1;
-  int32_t bdt, pad1;
   int64_t zca_off;            // floats: materialised Zc_A draw (d_out x RCA)
   int32_t dblk0, ndblk;       // blocks of the Zc_A draw kernel (one torch thread each)
 };
@@ -77,7 +77,7 @@ struct Tables {
   const BasisD* bases; int32_t nbases; int32_t nytiles; int32_t nwtiles;
   const MatD* wA; const MatD* wB;                       // W of each basis: CholeskyQR round 1, round 2 (-> V)
   int32_t nwsegsA; int32_t nwsegsB;
-  int32_t factor_dtype; int32_t ndblk;                 // ndblk: blocks of the Zc_A draw
+  int32_t copy_dtype; int32_t ndblk;                   // +/- copies and shadows; ndblk: blocks of the Zc_A draw
   char* ws;                                            // workspace base
   int64_t seg_kal_off;        // doubles: nsegs * 2 per-segment Kalman partials
   int64_t kal_sum_off;        // doubles: 2 summed Kalman scalars per direction

@@ -601,116 +601,6 @@ __global__ void __launch_bounds__(kThreads) k_chol(Tables tb, const MatD* __rest
 // out[v][c] = sum_{a<K} X[v*xld + a] * P[a*pld + c] with fp32 X, fp64 P and fp64 sums,
 // 4 vectors x 8 columns per thread: column pairs 2cb + g*pld/4 (g < 4), so a warp's double2
 // loads of a P row are one contiguous run (pld % 8 == 0, columns zero-padded to pld).
-template <typename Sink>
-__device__ __forceinline__ void rows_x_mat_f64(const float* __restrict__ X, int xld, const double* __restrict__ P,
-                                               int pld, int nv, int K, int nc, Sink sink) {
-  const int cbs = pld >> 3;
-  const int quarter = pld >> 2;
-  const int vbs = (nv + 3) >> 2;
-  for (int blk = threadIdx.x; blk < vbs * cbs; blk += kThreads) {
-    const int vb = blk / cbs, cb = blk - vb * cbs;
-    const int v0 = vb * 4, c0 = cb * 2;
-    double acc[4][8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    const float* x0 = X + v0 * xld;
-#pragma unroll 2
-    for (int a = 0; a < K; ++a) {
-      double pv[8];
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const double2 t = *reinterpret_cast<const double2*>(P + a * pld + g * quarter + c0);
-        pv[2 * g] = t.x;
-        pv[2 * g + 1] = t.y;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const double x = static_cast<double>(x0[i * xld + a]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fma(x, pv[j], acc[i][j]);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (v0 + i >= nv) continue;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = (j >> 1) * quarter + c0 + (j & 1);
-        if (c < nc) sink(v0 + i, c, acc[i][j]);
-      }
-    }
-  }
-}
-
-// =====================================================================================
-// CholeskyQR of the power-iteration W: V = W R^{-1} with fp64 products and sums. With the
-// exact fp64 Gram behind R, one round leaves V orthonormal to fp32 rounding (the second
-// round of CholeskyQR2 only corrects an fp32-accumulated apply). Also writes the bf16
-// pair [V_hi | V_lo]^T that the next tensor-core Y = H V reads (M.v2t, when set).
-// Side A only (W rows are contiguous R-vectors).
-// =====================================================================================
-__global__ void __launch_bounds__(kThreads) k_qr_apply(Tables tb, const MatD* __restrict__ mats, int nmats) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int seg = blockIdx.x;
-  const int mi = find_owner(mats, nmats, seg, [](const MatD& m) { return m.seg0; });
-  const MatD M = mats[mi];
-  const int r = static_cast<int>(M.r);
-  const int r8 = pad8(r);
-  const int TV = tile_vectors(r);
-  const int xld = r8 + 1;
-  double* Ps = reinterpret_cast<double*>(smem_raw);            // r x r8 fp64
-  float* xs = reinterpret_cast<float*>(Ps + r * r8);           // TV x xld
-  float* os = xs + TV * xld;                                   // TV x xld
-  const int tid = threadIdx.x;
-  const double* Rd = reinterpret_cast<const double*>(tb.ws) + M.dw_off + static_cast<int64_t>(r) * r;
-  for (int e = tid; e < r * r8; e += kThreads) {
-    const int a = e / r8, c = e - a * r8;
-    Ps[e] = (c < r) ? Rd[a * r + c] : 0.0;
-  }
-  const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
-  const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
-  const float* W = M.mu;
-  float* V = reinterpret_cast<float*>(M.param);
-  __syncthreads();
-  for (int64_t s0 = v0; s0 < v1; s0 += TV) {
-    const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
-    const int n = nv * r;
-    for (int base = tid; base < n; base += kThreads * kUnroll) {
-      float w0[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int e = base + u * kThreads;
-        if (e < n) w0[u] = W[s0 * M.ld + e];          // rows are contiguous: ld == r
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int e = base + u * kThreads;
-        if (e < n) { const int v = e / r; xs[v * xld + (e - v * r)] = w0[u]; }
-      }
-    }
-    __syncthreads();
-    rows_x_mat_f64(xs, xld, Ps, r8, nv, r, r,
-                   [&](int v, int c, double x) { os[v * xld + c] = static_cast<float>(x); });
-    __syncthreads();
-    for (int e = tid; e < n; e += kThreads) {               // V rows, coalesced
-      const int v = e / r;
-      V[s0 * M.ld + e] = os[v * xld + (e - v * r)];
-    }
-    if (M.v2t) {
-      for (int e = tid; e < n; e += kThreads) {             // [V_hi | V_lo]^T, coalesced along d
-        const int c = e / nv, v = e - c * nv;
-        const float x = os[v * xld + c];
-        const __nv_bfloat16 h = __float2bfloat16_rn(x);
-        M.v2t[static_cast<int64_t>(c) * M.ldv2 + s0 + v] = h;
-        M.v2t[static_cast<int64_t>(r + c) * M.ldv2 + s0 + v] = __float2bfloat16_rn(x - __bfloat162float(h));
-      }
-    }
-    __syncthreads();
-  }
-}
-
 // =====================================================================================
 // Apply: X[v,:] = x_v^T Pm for every vector of every matrix segment.
 // OUT 0: param -= eta * X (factor dtype), optional scratch = X  (ds_mezo/kernels.py:84-92).
@@ -823,14 +713,6 @@ __device__ __forceinline__ float ldg_l2pf(const float* p) {
   asm("ld.global.nc.L2::256B.f32 %0, [%1];" : "=f"(v) : "l"(p));
   return v;
 }
-__device__ __forceinline__ float ldg_l2pf(const void* p, int64_t i, int dt) {
-  if (dt == DSMZ_BF16) {
-    unsigned short u;
-    asm("ld.global.nc.L2::256B.u16 %0, [%1];" : "=h"(u) : "l"(reinterpret_cast<const __nv_bfloat16*>(p) + i));
-    return __bfloat162float(__ushort_as_bfloat16(u));
-  }
-  return ldg_l2pf(reinterpret_cast<const float*>(p) + i);
-}
 __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb, int64_t ncols) {
   __shared__ __align__(16) float sh[4][kBsJ][kBsP];
   float (*Bs)[kBsP] = sh[0];
@@ -883,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb, int64_t ncols)
           const int64_t a = static_cast<int64_t>(rt + rr) * D.b_s0 + j * D.b_s1;
           // out-of-range elements load element 0 (always valid) and are replaced by zero
           const int64_t ac = ok ? a : 0;
-          const float b0 = ldg_l2pf(D.Bp, ac, D.bdt);
+          const float b0 = ldg_l2pf(D.Bp + ac);
           const float w0 = with_var ? ldg_l2pf(D.varB + ac) : 0.f;
           lb[u] = ok ? b0 : 0.f;
           lw[u] = ok ? w0 : 0.f;
@@ -1120,19 +1002,13 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
 }
 
 // =====================================================================================
-// Perturbation pass over every adapter matrix segment (controller.py:178-193, 241-248,
-// 262-270; ds_mezo/kernels.py:290-368, 399-412):
-//   side A: z[i,:] = eps * Zc_A[i,:] Q^T  with Zc_A[i,k] = randn draw A element i*RCA+k
+// The AGZO perturbation of one module for the drop-in op (ds_mezo/kernels.py:290-368):
+//   side A: z[i,:] = eps * Zc_A[i,:] Q^T  (Zc_A from the caller)
 //   side B: z[:,j] = eps * Zc_B V[j,:]^T
-// MODE 0 (step): z stored, pos = p + z, neg = p - z, Kalman sums of this segment
-//                (sum z*beta*mu, sum z*z*(beta^2 var + q)).
-// MODE 1 (drop-in op): z stored only, Zc_A read from the caller's tensor.
+// One CTA per vector segment; the grouped step uses the streaming sk::k_sperturb.
 // =====================================================================================
-template <int MODE>
-__global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, uint64_t base_off, float eps,
-                                                      KalmanIn kin) {
+__global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, float eps) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double red[2][kThreads / 32];
   const int seg = blockIdx.x;
   const int mi = find_owner(tb.mats, tb.nmats, seg, [](const MatD& m) { return m.seg0; });
   const MatD M = tb.mats[mi];
@@ -1160,7 +1036,6 @@ __global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, 
     }
   }
   const BasisD Bd = tb.bases[D.basis];
-  float s_zmu = 0.f, s_zzv = 0.f;
   const int64_t v0 = static_cast<int64_t>(seg - M.seg0) * M.segv;
   const int64_t v1 = min(v0 + static_cast<int64_t>(M.segv), M.nvec);
   __syncthreads();
@@ -1168,68 +1043,59 @@ __global__ void __launch_bounds__(kThreads) k_perturb(Tables tb, uint64_t seed, 
     const int nv = static_cast<int>(min(static_cast<int64_t>(TV), v1 - s0));
     for (int e = tid; e < nv * KW; e += kThreads) {
       const int v = e / KW, k = e - v * KW;
-      float x;
-      if (M.side == 0) {
-        const int64_t li = (s0 + v) * RCA + k;
-        x = (MODE == 0) ? torch_randn_at(seed, base_off + D.offA, D.thrA, li) : D.zcA_ext[li];
-      } else {
-        x = Bd.Vin[(s0 + v) * Bd.v_s0 + static_cast<int64_t>(k) * Bd.v_s1];
-      }
+      const float x = (M.side == 0) ? D.zcA_ext[(s0 + v) * RCA + k]
+                                    : Bd.Vin[(s0 + v) * Bd.v_s0 + static_cast<int64_t>(k) * Bd.v_s1];
       Ks[v * (KW + 1) + k] = x;
     }
     __syncthreads();
     rows_x_mat(Ks, KW + 1, Cs, R8, nv, KW, R, [&](int v, int c, float x) { zs[v * (r + 1) + c] = x * eps; });
     __syncthreads();
     const int n = nv * r;
-    for (int base = tid; base < n; base += kThreads * kUnroll) {
-      float p0[kUnroll], m0[kUnroll], w0[kUnroll];
-      int vv[kUnroll], kk[kUnroll];
-      int64_t ad[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {            // issue every load before using any
-        const int e = base + u * kThreads;
-        elem_vk(M.side, e, r, nv, vv[u], kk[u]);
-        ad[u] = vaddr2(M, s0 + vv[u], kk[u]);
-        if (MODE == 0 && e < n) {
-          p0[u] = ldf(M.param, ad[u], tb.factor_dtype);
-          m0[u] = M.mu[ad[u]];
-          w0[u] = M.var[ad[u]];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (base + u * kThreads >= n) continue;
-        const float z = zs[vv[u] * (r + 1) + kk[u]];
-        M.z[ad[u]] = z;
-        if (MODE == 0) {
-          stf(M.pos, ad[u], __fadd_rn(p0[u], z), tb.factor_dtype);
-          stf(M.neg, ad[u], __fsub_rn(p0[u], z), tb.factor_dtype);
-          const float mu1 = __fmul_rn(m0[u], kin.beta);
-          const float var1 = __fadd_rn(__fmul_rn(w0[u], kin.beta2), kin.q);
-          s_zmu = fmaf(z, mu1, s_zmu);
-          s_zzv = fmaf(__fmul_rn(z, z), var1, s_zzv);
-        }
-      }
+    for (int e = tid; e < n; e += kThreads) {
+      int v, k;
+      elem_vk(M.side, e, r, nv, v, k);
+      M.z[vaddr2(M, s0 + v, k)] = zs[v * (r + 1) + k];
     }
     __syncthreads();
   }
-  if (MODE == 0) {
-    double a = s_zmu, b = s_zzv;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      a += __shfl_xor_sync(0xffffffffu, a, o);
-      b += __shfl_xor_sync(0xffffffffu, b, o);
-    }
-    if ((tid & 31) == 0) { red[0][tid >> 5] = a; red[1][tid >> 5] = b; }
-    __syncthreads();
-    if (tid == 0) {
-      double sa = 0.0, sb = 0.0;
-      for (int w = 0; w < kThreads / 32; ++w) { sa += red[0][w]; sb += red[1][w]; }
-      double* out = reinterpret_cast<double*>(tb.ws) + tb.seg_kal_off + 2 * static_cast<int64_t>(seg);
-      out[0] = sa;
-      out[1] = sb;
-    }
+}
+
+// =====================================================================================
+// Frobenius norms of the fp32 master factors (ds_mezo/controller.py:78-82 takes their
+// median for eps). Block (m, s) sums the squares of slice s of matrix m's elements in fp64;
+// k_norm_finish adds the kNormSlices partials of each matrix in order (deterministic).
+// =====================================================================================
+constexpr int kNormSlices = 16;
+__global__ void __launch_bounds__(kThreads) k_norm_partial(Tables tb, double* part) {
+  __shared__ double red[kThreads / 32];
+  const int m = blockIdx.x, sl = blockIdx.y;
+  const MatD M = tb.mats[m];
+  const int64_t n = M.nvec * M.r;
+  const int64_t e0 = n * sl / kNormSlices, e1 = n * (sl + 1) / kNormSlices;
+  const float* p = reinterpret_cast<const float*>(M.param);
+  double acc = 0.0;
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += kThreads) {
+    int64_t v, k;
+    if (M.side == 0) { v = e / M.r; k = e - v * M.r; } else { k = e / M.nvec; v = e - k * M.nvec; }
+    const double x = p[M.side == 0 ? v * M.ld + k * M.cs : k * M.ld + v * M.cs];
+    acc = fma(x, x, acc);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+    part[m * kNormSlices + sl] = t;
+  }
+}
+__global__ void __launch_bounds__(kThreads) k_norm_finish(const double* part, int nmats, float* norms) {
+  const int m = blockIdx.x * kThreads + threadIdx.x;
+  if (m >= nmats) return;
+  double t = 0.0;
+  for (int s = 0; s < kNormSlices; ++s) t += part[m * kNormSlices + s];
+  norms[m] = static_cast<float>(sqrt(t));
 }
 
 // Sums the per-segment Kalman partials in a fixed order (deterministic).

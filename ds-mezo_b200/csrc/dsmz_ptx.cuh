@@ -121,6 +121,58 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int
       "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// L2 eviction policies for the cache_hint forms of the TMA loads (createpolicy).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// tma_load_2d with an L2 cache policy (no cluster multicast).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// Acquire load of a counter another CTA advances with release semantics.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Orders this thread's generic-proxy global accesses with the async proxy (TMA) accesses
+// that follow (or that other threads make after synchronising with it).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until *p >= target (another CTA's release-ordered counter): false after
+// kTimeoutNs (error word set) or when another role failed.
+__device__ __forceinline__ bool spin_geq(const int* p, int target, int* err) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = gtimer();
+  uint64_t tchk = t0;
+  while (true) {
+    __nanosleep(256);
+    if (ld_acquire_gpu(p) >= target) return true;
+    const uint64_t t = gtimer();
+    if (t - tchk > kPollNs) {
+      tchk = t;
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (t - t0 > kTimeoutNs) {
+        atomicExch(err, 1);
+        return false;
+      }
+    }
+  }
+}
+
 // Barrier over the `n` threads of the consumer warps (id 1; warp-multiple n).
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

@@ -457,26 +457,11 @@ struct Walk {
 };
 
 template <int FES>
-__device__ __forceinline__ float ld_fac(const void* p, int i) {
-  if (FES == 2) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
-  return reinterpret_cast<const float*>(p)[i];
-}
-template <int FES>
 __device__ __forceinline__ void st_fac(void* p, int i, float x) {
   if (FES == 2) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x);
   else reinterpret_cast<float*>(p)[i] = x;
 }
-// Four consecutive factor elements (8 bytes of bf16 or 16 of fp32, aligned).
-template <int FES>
-__device__ __forceinline__ float4 ld_fac4(const void* p, int i) {
-  if (FES == 2) {
-    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-    return make_float4(a.x, a.y, b.x, b.y);
-  }
-  return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
-}
+// Stores four consecutive copy-dtype elements (8 bytes of bf16 or 16 of fp32, aligned).
 template <int FES>
 __device__ __forceinline__ void st_fac4(void* p, int i, float4 x) {
   if (FES == 2) {
@@ -524,19 +509,19 @@ struct Layout {
   int r, pld, zp, rp, xp, nsb, ng;
 };
 
-// Perturb: p, mu, var (unpadded, MODE 0 only) and the K operand rows (Zc_A rows of width
-// RCA, or basis rows of width RC) as a swizzled row image (pitch[3]: bytes per box); the
+// Perturb: p, mu, var (fp32, unpadded) and the K operand rows (Zc_A rows of width RCA, or
+// basis rows of width RC) as a swizzled row image (pitch[3]: bytes per box); the
 // coefficient matrix with KW rounded up to 4 rows (zero rows past KW).
-__host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int fes, int mode, int budget, int TV) {
+__host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, int budget, int TV) {
   Layout L{};
   L.r = r;
   L.TV = TV;
   const int KW = RC > RCA ? RC : RCA;
   const int K4 = (KW + 3) & ~3;
   int o = 0;
-  L.off[0] = o; L.pitch[0] = (mode == 0) ? r * fes : 0;               o += al128(mode == 0 ? TV * r * fes : 0);
-  L.off[1] = o; L.pitch[1] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
-  L.off[2] = o; L.pitch[2] = (mode == 0) ? r * 4 : 0;                 o += al128(mode == 0 ? TV * r * 4 : 0);
+  L.off[0] = o; L.pitch[0] = r * 4;                                   o += al128(TV * r * 4);
+  L.off[1] = o; L.pitch[1] = r * 4;                                   o += al128(TV * r * 4);
+  L.off[2] = o; L.pitch[2] = r * 4;                                   o += al128(TV * r * 4);
   o = al1024(o);
   L.off[3] = o; L.pitch[3] = TV * 128;                                o += swz_bytes(KW, TV);
   L.stage_bytes = al1024(o);
@@ -555,16 +540,17 @@ __host__ __device__ inline Layout perturb_layout(int r, int R, int RC, int RCA, 
   return L;
 }
 
-// Apply: p (unpadded) and mu (side 0: swizzled row image, pitch[1] bytes per box; side 1:
-// dense rows of TV); the r x r apply matrix with r rounded up to 4 rows (zero rows past r).
-__host__ __device__ inline Layout apply_layout(int r, int fes, int budget, int TV) {
+// Apply: p (fp32, unpadded) and mu (side 0: swizzled row image, pitch[1] bytes per box;
+// side 1: dense rows of TV); the r x r apply matrix with r rounded up to 4 rows (zero rows
+// past r).
+__host__ __device__ inline Layout apply_layout(int r, int budget, int TV) {
   Layout L{};
   L.r = r;
   L.TV = TV;
   const int r4 = (r + 3) & ~3;
   const int mub = swz_bytes(r, TV) > TV * r * 4 ? swz_bytes(r, TV) : TV * r * 4;
   int o = 0;
-  L.off[0] = o; L.pitch[0] = r * fes;                                   o += al128(TV * r * fes);
+  L.off[0] = o; L.pitch[0] = r * 4;                                     o += al128(TV * r * 4);
   o = al1024(o);
   L.off[1] = o; L.pitch[1] = TV * 128;                                  o += mub;
   L.stage_bytes = al1024(o);
@@ -725,11 +711,11 @@ __global__ void __launch_bounds__(256) k_draw_zca(Tables tb, uint64_t seed, uint
 // =====================================================================================
 // Perturbation (controller.py:178-193, 241-248, 262-270; ds_mezo/kernels.py:290-368,
 // 399-412). Side A: z[i,:] = eps * Zc_A[i,:] Q^T; side B: z[:,j] = eps * Zc_B V[j,:]^T.
-// MODE 0 (step): z, pos = p + z, neg = p - z, per-segment Kalman partials
-//                (sum z * beta*mu, sum z*z * (beta^2 var + q)).
-// MODE 1 (drop-in op): z only, Zc_A from the caller.
+// z, pos = copy(p + z), neg = copy(p - z) (p the fp32 master, the sum rounded to the copy
+// dtype of FES bytes per element, as the reference's fp32 pos/neg are cast at export), and
+// the per-segment Kalman partials (sum z * beta*mu, sum z*z * (beta^2 var + q)).
 // =====================================================================================
-template <int MODE, int FES>
+template <int FES>
 __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint64_t seed, uint64_t base_off, float eps,
                                                      KalmanIn kin, int* err) {
   extern __shared__ unsigned char smem_raw[];
@@ -740,7 +726,6 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
   TileIt it;
   it.init(tb.mats, tb.nmats, L.TV);
   const int warp = threadIdx.x >> 5;
-  constexpr int fes = FES;
   (void)seed; (void)base_off;
 
   if (warp < kProd) {
@@ -751,16 +736,15 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
       const MatD& M = t.mats[t.mi];
       const ModD& D = tb.mods[M.owner];
       const int r = static_cast<int>(M.r);
-      a[0] = make_src(MODE == 0 ? M.param : nullptr, M, fes, tb, 0);
-      a[1] = make_src(MODE == 0 ? M.mu : nullptr, M, 4, tb, 1);
-      a[2] = make_src(MODE == 0 ? M.var : nullptr, M, 4, tb, 2);
+      a[0] = make_src(M.param, M, 4, tb, 0);
+      a[1] = make_src(M.mu, M, 4, tb, 1);
+      a[2] = make_src(M.var, M, 4, tb, 2);
       // K operand: rows s0.. of Zc_A (d_out x RCA) or of the basis (d_in x RC)
       Src k{};
       k.es = 4; k.side = 0; k.cs = 1; k.swz = 1;
       k.map = (M.kmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.kmap : nullptr;
       if (M.side == 0) {
-        k.base = reinterpret_cast<const char*>(MODE == 0 ? reinterpret_cast<const float*>(tb.ws) + D.zca_off
-                                                         : D.zcA_ext);
+        k.base = reinterpret_cast<const char*>(reinterpret_cast<const float*>(tb.ws) + D.zca_off);
         k.ld = D.rca; k.r = D.rca;
       } else {
         const BasisD& Bd = tb.bases[D.basis];
@@ -768,8 +752,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
         k.ld = Bd.v_s0; k.cs = Bd.v_s1; k.r = D.rc;
       }
       a[3] = k;
-      pitch[0] = side_pitch(M.side, r, L.TV, fes);
-      pitch[1] = pitch[2] = side_pitch(M.side, r, L.TV, 4);
+      pitch[0] = pitch[1] = pitch[2] = side_pitch(M.side, r, L.TV, 4);
       pitch[3] = L.pitch[3];
       }
       const int off[4] = {L.off[0], L.off[1], L.off[2], L.off[3]};
@@ -828,7 +811,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
           const int64_t fo = static_cast<int64_t>(tb.dir) * tb.dstride_f * FES;
           void* post = tile_ptr(reinterpret_cast<char*>(M.pos) + fo, M, it.s0, FES);
           void* negt = tile_ptr(reinterpret_cast<char*>(M.neg) + fo, M, it.s0, FES);
-          const void* ps = stage + L.off[0];
+          const float* ps = reinterpret_cast<const float*>(stage + L.off[0]);
           const float* ms = reinterpret_cast<const float*>(stage + L.off[1]);
           const float* vsg = reinterpret_cast<const float*>(stage + L.off[2]);
           // four elements per step along the contiguous direction when rows and pointers
@@ -846,9 +829,9 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
               for (int q = 0; q < 4; ++q) z[q] = SIDE == 0 ? zs[v * L.zp + k + q] : zs[(v + q) * L.zp + k];
               const int g = SIDE == 0 ? v * ld + k : k * ld + v;
               *reinterpret_cast<float4*>(zt + g) = make_float4(z[0], z[1], z[2], z[3]);
-              if (MODE == 0) {
+              {
                 const int so = SIDE == 0 ? v * r + k : k * L.TV + v;
-                const float4 p4 = ld_fac4<FES>(ps, so);
+                const float4 p4 = *reinterpret_cast<const float4*>(ps + so);
                 const float4 m4 = *reinterpret_cast<const float4*>(ms + so);
                 const float4 w4 = *reinterpret_cast<const float4*>(vsg + so);
                 st_fac4<FES>(post, g, make_float4(__fadd_rn(p4.x, z[0]), __fadd_rn(p4.y, z[1]), __fadd_rn(p4.z, z[2]),
@@ -873,9 +856,9 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
               const float z = zs[w.v * L.zp + w.k];
               const int g = w.goff(ld, cs);
               zt[g] = z;
-              if (MODE == 0) {
+              {
                 const int so = w.soff(r, L.TV);
-                const float p0 = ld_fac<FES>(ps, so);
+                const float p0 = ps[so];
                 const float m0 = ms[so];
                 const float w0 = vsg[so];
                 st_fac<FES>(post, g, __fadd_rn(p0, z));
@@ -903,7 +886,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
       seg_done = it.seg;
       adv = it.next();
     } while (adv == 1);
-    if (MODE == 0) {
+    {
       // segment end: Kalman partials of the segment (fixed reduction order)
       double a = s_zmu, b = s_zzv;
 #pragma unroll
@@ -929,8 +912,9 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
 
 // =====================================================================================
 // Newton-Schulz apply (ds_mezo/kernels.py:84-92 rewritten in Gram space):
-// param -= eta * X, X[v,:] = x_v^T Pm with x_v the (already Kalman-updated) momentum;
-// optional scratch = X.
+// param -= eta * X on the fp32 master, X[v,:] = x_v^T Pm with x_v the (already
+// Kalman-updated) momentum; optional shadow = copy(param) in the copy dtype of FES bytes per
+// element (what the rollout loads), optional scratch = X.
 // =====================================================================================
 template <int FES>
 __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
@@ -943,7 +927,6 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
   TileIt it;
   it.init(mats, nmats, L.TV);
   const int warp = threadIdx.x >> 5;
-  constexpr int fes = FES;
 
   if (warp < kProd) {
     Src a[2];                                   // the segment's copy sources, built at its first tile
@@ -951,13 +934,13 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
     producer_loop<kProd>(it, L, smem, full, empty, err, [&](const TileIt& t, unsigned char* stage, uint64_t* fb, int lane, bool fresh) {
       if (fresh) {
         const MatD& M = t.mats[t.mi];
-        a[0] = make_src(M.param, M, fes, tb, 0);
+        a[0] = make_src(M.param, M, 4, tb, 0);
         a[1] = make_src(M.mu, M, 4, tb, 1);
         if (M.side == 0) {                      // mu rows as the swizzled row image
           a[1].swz = 1;
           a[1].map = (M.rmap >= 0 && tb.smaps != nullptr) ? tb.smaps + M.rmap : nullptr;
         }
-        pitch[0] = side_pitch(M.side, static_cast<int>(M.r), L.TV, fes);
+        pitch[0] = side_pitch(M.side, static_cast<int>(M.r), L.TV, 4);
         pitch[1] = M.side == 0 ? L.pitch[1] : L.TV * 4;
       }
       const int off[2] = {L.off[0], L.off[1]};
@@ -1007,11 +990,12 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
           named_sync(kBarTeam0 + team, kTT);
           const int n = nv * r;
           const int ld = static_cast<int>(M.ld), cs = static_cast<int>(M.cs);
-          void* pt = tile_ptr(reinterpret_cast<char*>(M.param), M, it.s0, FES);
+          float* pt = tile_ptr(reinterpret_cast<float*>(M.param), M, it.s0, 4);
+          void* sht = M.shadow ? tile_ptr(reinterpret_cast<char*>(M.shadow), M, it.s0, FES) : nullptr;
           float* sct = M.scratch ? tile_ptr(M.scratch, M, it.s0, 4) : nullptr;
-          const void* ps = stage + L.off[0];
-          const bool vec = cs == 1 && (ld & 3) == 0 && ((M.side == 0 ? r : nv) & 3) == 0 && aligned_to(pt, 4 * FES) &&
-                           aligned_to(sct, 16);
+          const float* ps = reinterpret_cast<const float*>(stage + L.off[0]);
+          const bool vec = cs == 1 && (ld & 3) == 0 && ((M.side == 0 ? r : nv) & 3) == 0 && aligned_to(pt, 16) &&
+                           aligned_to(sht, 4 * FES) && aligned_to(sct, 16);
           auto body4 = [&](auto side_tag) {             // four elements per step
             constexpr int SIDE = decltype(side_tag)::value;
             Walk4<SIDE> w(tt, kTT, r, nv);
@@ -1021,10 +1005,12 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
               float X[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) X[q] = SIDE == 0 ? os[v * L.zp + k + q] : os[(v + q) * L.zp + k];
-              const float4 p4 = ld_fac4<FES>(ps, SIDE == 0 ? v * r + k : k * L.TV + v);
+              const float4 p4 = *reinterpret_cast<const float4*>(ps + (SIDE == 0 ? v * r + k : k * L.TV + v));
               const int g = SIDE == 0 ? v * ld + k : k * ld + v;
-              st_fac4<FES>(pt, g, make_float4(__fsub_rn(p4.x, __fmul_rn(eta, X[0])), __fsub_rn(p4.y, __fmul_rn(eta, X[1])),
-                                              __fsub_rn(p4.z, __fmul_rn(eta, X[2])), __fsub_rn(p4.w, __fmul_rn(eta, X[3]))));
+              const float4 np = make_float4(__fsub_rn(p4.x, __fmul_rn(eta, X[0])), __fsub_rn(p4.y, __fmul_rn(eta, X[1])),
+                                            __fsub_rn(p4.z, __fmul_rn(eta, X[2])), __fsub_rn(p4.w, __fmul_rn(eta, X[3])));
+              *reinterpret_cast<float4*>(pt + g) = np;
+              if (sht) st_fac4<FES>(sht, g, np);
               if (sct) *reinterpret_cast<float4*>(sct + g) = make_float4(X[0], X[1], X[2], X[3]);
             }
           };
@@ -1033,9 +1019,11 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
             Walk<SIDE> w(tt, kTT, r, nv);
             for (int e = tt; e < n; e += kTT, w.next()) {
               const float X = os[w.v * L.zp + w.k];
-              const float p0 = ld_fac<FES>(ps, w.soff(r, L.TV));
+              const float p0 = ps[w.soff(r, L.TV)];
               const int g = w.goff(ld, cs);
-              st_fac<FES>(pt, g, __fsub_rn(p0, __fmul_rn(eta, X)));
+              const float np = __fsub_rn(p0, __fmul_rn(eta, X));
+              pt[g] = np;
+              if (sht) st_fac<FES>(sht, g, np);
               if (sct) sct[g] = X;
             }
           };

@@ -11,10 +11,11 @@ All compute runs in libdsmezo.so (C ABI in include/dsmezo.h); there is no CPU pa
 from . import kernels  # noqa: F401
 from . import scoring  # noqa: F401
 from ._lib import DsmzError, lib  # noqa: F401
-from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ZOController, device_layout,  # noqa: F401
-                          draw_increments, kalman_beta_q, rloo_direction_scalars, transformer_adapter_shapes)
+from .adapter_set import (AdapterSet, BasisShape, ModuleShape, ShrinkageRLOO, ZOController,  # noqa: F401
+                          device_layout, draw_increments, eps_from_norms, kalman_beta_q, rloo_direction_scalars,
+                          transformer_adapter_shapes)
 from .sharding import ShardedStep, ShardLayout, partition_layers, shard_layout  # noqa: F401
 
 __all__ = ["kernels", "rloo_direction_scalars", "AdapterSet", "ZOController", "ModuleShape", "BasisShape", "transformer_adapter_shapes",
            "draw_increments", "device_layout", "kalman_beta_q", "DsmzError", "lib", "ShardedStep", "ShardLayout",
-           "partition_layers", "shard_layout"]
+           "partition_layers", "shard_layout", "ShrinkageRLOO", "eps_from_norms"]

@@ -12,6 +12,7 @@ from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_int64, c_siz
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdsmezo.so")
 
+ABI_VERSION = 2              # DSMZ_ABI_VERSION of the structs below
 DSMZ_F32 = 0
 DSMZ_BF16 = 1
 MAX_RANK = 128
@@ -30,6 +31,7 @@ class ModuleSpec(ctypes.Structure):
     _fields_ = [
         ("A", c_void_p), ("B", c_void_p),
         ("pos_A", c_void_p), ("pos_B", c_void_p), ("neg_A", c_void_p), ("neg_B", c_void_p),
+        ("shadow_A", c_void_p), ("shadow_B", c_void_p),
         ("mu_A", c_void_p), ("mu_B", c_void_p), ("var_A", c_void_p), ("var_B", c_void_p),
         ("z_A", c_void_p), ("z_B", c_void_p),
         ("scratch_A", c_void_p), ("scratch_B", c_void_p),
@@ -49,7 +51,7 @@ class BasisSpec(ctypes.Structure):
 
 class PlanDesc(ctypes.Structure):
     _fields_ = [
-        ("factor_dtype", c_int32),
+        ("copy_dtype", c_int32),
         ("num_modules", c_int32), ("modules", POINTER(ModuleSpec)),
         ("num_bases", c_int32), ("bases", POINTER(BasisSpec)),
         ("sm_count", c_int32), ("max_threads_per_sm", c_int32),
@@ -108,6 +110,7 @@ SIGNATURES = {
     "dsmz_plan_bind": (c_int32, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_void_p]),
     "dsmz_plan_uses_tensor_cores": (c_int32, [c_void_p]),
     "dsmz_plan_directions": (c_int32, [c_void_p]),
+    "dsmz_plan_factor_norms": (c_int32, [c_void_p, c_void_p, c_void_p]),
     "dsmz_step_update_directions": (c_int32, [c_void_p, POINTER(c_float), c_int32, c_float, c_float, c_float,
                                               c_float, POINTER(NSSchedule), c_void_p]),
     "dsmz_plan_device_error": (c_int32, [c_void_p, c_void_p]),
@@ -140,6 +143,9 @@ def lib() -> ctypes.CDLL:
             fn = getattr(handle, name)
             fn.restype = res
             fn.argtypes = args
+        if handle.dsmz_abi_version() != ABI_VERSION:
+            raise ImportError(f"{LIB_PATH} has ABI version {handle.dsmz_abi_version()}, this binding expects "
+                              f"{ABI_VERSION}; rebuild it with `python -m dsmezo_b200.build`")
         _lib = handle
     return _lib
 

@@ -3,7 +3,11 @@
 ``AdapterSet`` keeps every adapter of every layer in contiguous HBM arenas, in the
 controller's module order (sorted by (layer, module name), ds_mezo/model_config.py:37):
 
-* factor arena (A then B of each module) in the factor dtype, and its +/- copies;
+* the fp32 master factor arena (A then B of each module), as the reference keeps A and B
+  in fp32 (ds_mezo/controller.py:66-67);
+* what the rollout engine loads, in the copy dtype (bf16 for the bf16 configs): the +/-
+  copies (the reference's fp32 pos/neg, cast at export by ds_mezo/backend.py:21-36) and,
+  when the copy dtype is not fp32, a shadow of the masters rewritten by every update;
 * fp32 Kalman mean (momentum) and variance arenas, and the fp32 perturbation z
   (the reference's ``perturbations`` dict, ds_mezo/controller.py:239);
 * one activation buffer H (T x D) and one basis V (D x R, fp32) per unique module input
@@ -94,18 +98,18 @@ class AdapterSet:
     """Arenas + bound plan for one set of modules (all of them, or one rank's layers)."""
 
     def __init__(self, modules: Sequence[ModuleShape], bases: Sequence[BasisShape], rank: int, basis_width: int,
-                 factor_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
+                 copy_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
                  rng_direction_stride: int = 0):
-        if factor_dtype not in _DT or act_dtype not in _DT:
-            raise ValueError("factor and activation dtypes must be float32 or bfloat16")
+        if copy_dtype not in _DT or act_dtype not in _DT:
+            raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
         self.modules = list(modules)
         self.bases = list(bases)
         self.rank = int(rank)
         self.basis_width = int(basis_width)
-        self.factor_dtype = factor_dtype
+        self.copy_dtype = copy_dtype
         self.act_dtype = act_dtype
         if not 1 <= int(directions) <= _lib.MAX_DIRECTIONS:
             raise ValueError(f"directions must be in [1, {_lib.MAX_DIRECTIONS}]")
@@ -125,10 +129,12 @@ class AdapterSet:
         self.capacity = cap
         dev = self.device
         K = self.directions
-        self.factors = torch.zeros(cap, dtype=factor_dtype, device=dev)
+        self.factors = torch.zeros(cap, dtype=torch.float32, device=dev)      # fp32 masters
+        # the updated factors in the copy dtype, written by every update (none for fp32)
+        self.shadow = torch.zeros(cap, dtype=copy_dtype, device=dev) if copy_dtype != torch.float32 else None
         # direction k's +/- copies and z follow direction 0's at a fixed stride
-        self.pos = torch.zeros(K * cap, dtype=factor_dtype, device=dev)
-        self.neg = torch.zeros(K * cap, dtype=factor_dtype, device=dev)
+        self.pos = torch.zeros(K * cap, dtype=copy_dtype, device=dev)
+        self.neg = torch.zeros(K * cap, dtype=copy_dtype, device=dev)
         self.mu = torch.zeros(n, dtype=torch.float32, device=dev)
         self.var = torch.zeros(n, dtype=torch.float32, device=dev)
         self.z = torch.zeros(K * n, dtype=torch.float32, device=dev)
@@ -146,6 +152,22 @@ class AdapterSet:
         self.layout = layout if layout is not None else device_layout(dev)
         self._flags = 0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER
         self._build_plan(int(rng_offset_before))
+
+    @property
+    def export_factors(self) -> torch.Tensor:
+        """The updated factors as the rollout loads them: the copy-dtype shadow, or the fp32
+        masters themselves when the copy dtype is fp32."""
+        return self.shadow if self.shadow is not None else self.factors
+
+    def sync_shadow(self) -> None:
+        """Rewrites the shadow from the masters (round to nearest even, as torch's .to()).
+        Every update does this on its own; call it after writing the masters directly (the
+        initial load of the adapters, a checkpoint restore). Runs on the current stream."""
+        if self.shadow is None or self.numel == 0:
+            return
+        check(lib().dsmz_activation_load(_DT[self.copy_dtype], self.shadow.data_ptr(), 1, self.numel, self.numel,
+                                         DSMZ_F32, self.factors.data_ptr(), 1, self.numel, 1, self._stream()),
+              "sync_shadow")
 
     # ------------------------------------------------------------------ views
     def A(self, i, t=None):
@@ -199,14 +221,17 @@ class AdapterSet:
     # ------------------------------------------------------------------ plan
     def _build_plan(self, rng_offset_before: int):
         L = lib()
-        fdt = _DT[self.factor_dtype]
-        fsz = self.factors.element_size()
+        cdt = _DT[self.copy_dtype]
+        fsz = self.pos.element_size()
         specs = (ModuleSpec * max(len(self.modules), 1))()
         for i, m in enumerate(self.modules):
             s = specs[i]
             a, b = self.offA[i], self.offB[i]
-            s.A = self.factors.data_ptr() + a * fsz
-            s.B = self.factors.data_ptr() + b * fsz
+            s.A = self.factors.data_ptr() + a * 4
+            s.B = self.factors.data_ptr() + b * 4
+            if self.shadow is not None:
+                s.shadow_A = self.shadow.data_ptr() + a * fsz
+                s.shadow_B = self.shadow.data_ptr() + b * fsz
             s.pos_A = self.pos.data_ptr() + a * fsz
             s.pos_B = self.pos.data_ptr() + b * fsz
             s.neg_A = self.neg.data_ptr() + a * fsz
@@ -233,7 +258,7 @@ class AdapterSet:
             s.V = self.V_arena.data_ptr() + self.offV[i] * 4
             s.R = self.basis_width
         desc = PlanDesc()
-        desc.factor_dtype = fdt
+        desc.copy_dtype = cdt
         desc.num_modules = len(self.modules)
         desc.modules = specs
         desc.num_bases = len(self.bases)
@@ -279,6 +304,14 @@ class AdapterSet:
     def device_error(self) -> int:
         """Reads and clears the device error word (synchronises the stream)."""
         return int(lib().dsmz_plan_device_error(self._plan, self._stream()))
+
+    def factor_norms(self) -> torch.Tensor:
+        """Frobenius norms of the fp32 masters, A then B of each module (device, fp32)."""
+        out = torch.empty(2 * len(self.modules), dtype=torch.float32, device=self.device)
+        if self.modules:
+            check(lib().dsmz_plan_factor_norms(self._plan, out.data_ptr(), self._stream()), "factor norms")
+            self.launches += 2
+        return out
 
     def launch_count(self, num_iters: int) -> int:
         return int(lib().dsmz_plan_launch_count(self._plan, num_iters))
@@ -344,6 +377,43 @@ def rloo_direction_scalars(rewards: torch.Tensor, eps: float) -> List[float]:
     return ((lp - lm) / (2.0 * eps)).tolist()
 
 
+def eps_from_norms(norms: torch.Tensor) -> float:
+    """The perturbation scale of ds_mezo/controller.py:78-82 from every factor's Frobenius
+    norm: torch.median (the lower middle value of an even count) times FLT_EPSILON^(1/3)."""
+    v = sorted(float(x) for x in norms.detach().cpu().tolist())
+    if not v:
+        raise ValueError("eps_from_norms: no factors")
+    return v[(len(v) - 1) // 2] * FLT_EPS ** (1.0 / 3.0)
+
+
+class ShrinkageRLOO:
+    """Advantages of one step's rollouts with the James-Stein shrinkage of the RLOO baseline
+    (ds_mezo/controller.py:216-229): with r_bar the mean reward and v the unbiased reward
+    variance, lam = v / (v + (r_bar - ema)^2 + FLT_MIN), the baseline of rollout i is
+    (1 - lam) * (sum - r_i) / (N - 1) + lam * ema, and afterwards
+    ema <- beta * ema + (1 - beta) * r_bar with beta the Kalman momentum of the previous
+    update (0 before the first). The arithmetic follows the reference's: float32 tensors for
+    the rewards, Python floats for the scalars."""
+
+    def __init__(self, norm_floor: float = FLT_MIN):
+        self.reward_ema = 0.0
+        self.norm_floor = float(norm_floor)
+
+    def advantages(self, rewards: Sequence[float], momentum: float) -> List[float]:
+        r = torch.tensor([float(x) for x in rewards], dtype=torch.float32)
+        n = r.numel()
+        if n < 2:
+            raise ValueError("shrinkage RLOO needs at least two rollouts")
+        r_bar = float(r.mean())
+        base_rloo = (r.sum() - r) / (n - 1)
+        rvar = float(r.var())
+        lam = rvar / (rvar + (r_bar - self.reward_ema) ** 2 + self.norm_floor)
+        base = (1.0 - lam) * base_rloo + lam * self.reward_ema
+        adv = (r - base).tolist()
+        self.reward_ema = momentum * self.reward_ema + (1.0 - momentum) * r_bar
+        return adv
+
+
 def kalman_beta_q(step_count: int, total_steps: int, eps: float):
     """ds_mezo/controller.py:255-258."""
     beta = 1.0 - 1.0 / min(step_count, int(math.sqrt(total_steps)))
@@ -360,6 +430,28 @@ class ZOController:
     With a process group the set holds this rank's layers; the two Kalman sums are
     all-reduced between the phases.
     """
+
+    @classmethod
+    def from_factors(cls, aset: AdapterSet, total_steps: int, generator: torch.Generator, **kw) -> "ZOController":
+        """A controller whose eps is derived from the set's masters as the reference's
+        constructor does (ds_mezo/controller.py:78-82): median factor norm times
+        FLT_EPSILON^(1/3). With a process group the per-matrix norms of every rank are
+        gathered (a few KB), so every rank derives the same eps."""
+        norms = aset.factor_norms()
+        pg = kw.get("process_group")
+        if pg is not None:
+            import torch.distributed as dist
+            world = dist.get_world_size(pg)
+            n = torch.tensor([norms.numel()], dtype=torch.int64, device=norms.device)
+            counts = [torch.zeros_like(n) for _ in range(world)]
+            dist.all_gather(counts, n, group=pg)
+            top = int(max(int(c.item()) for c in counts))
+            pad = torch.full((top,), float("nan"), dtype=torch.float32, device=norms.device)
+            pad[:norms.numel()] = norms
+            parts = [torch.empty_like(pad) for _ in range(world)]
+            dist.all_gather(parts, pad, group=pg)
+            norms = torch.cat([p[:int(c.item())] for p, c in zip(parts, counts)])
+        return cls(aset, eps_from_norms(norms), total_steps, generator, **kw)
 
     def __init__(self, aset: AdapterSet, eps: float, total_steps: int, generator: torch.Generator,
                  power_iters: int = 3, schedule="cubic", process_group=None, rng_increment_total: Optional[int] = None,
@@ -379,10 +471,23 @@ class ZOController:
         self.eta = self.eta_max
         self.beta = 0.0
         self.q = 0.0
+        self.rloo = ShrinkageRLOO(norm_floor)
 
     def _step_lr(self):
         t = self.step_count
         self.eta = self.eta_min + 0.5 * (self.eta_max - self.eta_min) * (1.0 + math.cos(math.pi * t / self.total_steps))
+
+    def advantages(self, rewards: Sequence[float]) -> List[float]:
+        """Shrinkage-RLOO advantages of this step's rollout rewards (ds_mezo/controller.py:
+        216-229). Call it before perturb(), as the reference's _explore precedes
+        _perturb_and_sync: the reward EMA then moves with the previous update's momentum."""
+        return self.rloo.advantages(rewards, self.beta)
+
+    def skip(self):
+        """A step whose advantages are all zero (ds_mezo/controller.py:299-301): the step count
+        and the learning rate move on, nothing else does."""
+        self.step_count += 1
+        self._step_lr()
 
     def perturb(self):
         self.step_count += 1

@@ -10,8 +10,9 @@ The step shards by layer (each matrix's work is independent); two things cross r
   generator increments), so a sharded step draws exactly what one GPU would.
 
 After the phases, the rollout needs the full adapter set: pos/neg copies for scoring and
-the updated factors for the next rollout. Each rank's arenas are padded to the largest
-shard, so each all-gather is one NCCL call on contiguous buffers.
+the updated factors for the next rollout, both in the copy dtype it loads (bf16 for the
+bf16 configs; the fp32 masters stay on their rank). Each rank's arenas are padded to the
+largest shard, so each all-gather is one NCCL call on contiguous buffers.
 """
 from __future__ import annotations
 
@@ -142,7 +143,7 @@ class ShardedStep:
     """One rank's part of the layer-sharded step (all of it when world == 1)."""
 
     def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
-                 eps: float, total_steps: int, generator: torch.Generator, factor_dtype=torch.bfloat16,
+                 eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
                  directions: int = 1):
         import torch.distributed as dist
@@ -156,7 +157,7 @@ class ShardedStep:
         mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)
         # one direction's draws over the whole model: the stride between directions' draws
         stride = self.layout.rng_increment_total
-        self.aset = AdapterSet(mods, bases, rank_r, rank_r, factor_dtype=factor_dtype, act_dtype=act_dtype,
+        self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
                                device=device, rng_offset_before=self.layout.rng_offset_before(self.rank),
                                layout=layout, capacity=self.layout.capacity, directions=directions,
                                rng_direction_stride=stride)
@@ -165,7 +166,7 @@ class ShardedStep:
                                 rng_increment_total=stride * directions)
         cap = self.layout.capacity
         self.gathered = {name: torch.empty(cap * self.world * (1 if name == "factors" else directions),
-                                           dtype=factor_dtype, device=device)
+                                           dtype=copy_dtype, device=device)
                          for name in ("factors", "pos", "neg")} if self.world > 1 else None
 
     # ------------------------------------------------------------------ phases
@@ -191,13 +192,18 @@ class ShardedStep:
     def update(self, dd):
         self.ctl.update(dd)
 
+    def _arena(self, name: str) -> torch.Tensor:
+        # 'factors' is what the rollout loads: the copy-dtype shadow (the fp32 masters when
+        # the copy dtype is fp32)
+        return self.aset.export_factors if name == "factors" else getattr(self.aset, name)
+
     def gather(self, *names: str):
         """All-gathers the named arenas ('factors', 'pos', 'neg') into full-model buffers
         laid out rank by rank (each rank's slice padded to the largest shard)."""
         if self.world == 1:
-            return {n: getattr(self.aset, n) for n in names}
+            return {n: self._arena(n) for n in names}
         for n in names:
-            gather_arena(self.gathered[n], getattr(self.aset, n), self.pg)
+            gather_arena(self.gathered[n], self._arena(n), self.pg)
         return {n: self.gathered[n] for n in names}
 
     def full_view(self, buf: torch.Tensor, rank: int) -> torch.Tensor:
@@ -209,9 +215,9 @@ class ShardedStep:
         """The adapter tensors the rollout engine loads, keyed as the reference's PEFT file
         (ds_mezo/backend.py:21-36: lora_A.weight = B, lora_B.weight = A, bf16), as device
         views of the full-model buffer that the last gather(which) filled (the local arena on
-        one GPU). With bf16 factors nothing is copied: this replaces the reference's bf16
-        cast and safetensors write to /dev/shm. fp32 factors are converted once on the device
-        into a bf16 buffer of the same layout. which: 'pos', 'neg' or 'factors'."""
+        one GPU). With a bf16 copy dtype nothing is copied: this replaces the reference's bf16
+        cast and safetensors write to /dev/shm. An fp32 copy dtype is converted once on the
+        device into a bf16 buffer of the same layout. which: 'pos', 'neg' or 'factors'."""
         if which not in ("pos", "neg", "factors"):
             raise ValueError("export_adapters: which is 'pos', 'neg' or 'factors'")
         K = 1 if which == "factors" else self.aset.directions
@@ -219,7 +225,7 @@ class ShardedStep:
             raise ValueError(f"export_adapters: direction must be in [0, {K})")
         cap = self.layout.capacity
         if self.world == 1:
-            buf = getattr(self.aset, which)
+            buf = self._arena(which)
         else:
             buf = self.gathered[which]
         layers, hidden, inter, kv, rank_r, tokens = self._shape

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define DSMZ_ABI_VERSION 1
+#define DSMZ_ABI_VERSION 2
 
 typedef void* dsmz_stream_t; /* cudaStream_t */
 
@@ -162,15 +162,21 @@ int dsmz_randn(float* out, int64_t n, uint64_t seed, uint64_t offset, int32_t sm
 
 /* ---------------------------------------------------------------------------------
  * Grouped optimizer step over an adapter set.
- * A module owns A (d_out x r) and B (r x d_in), each with Kalman mean/variance (F32),
- * +/- copies (factor dtype), the fp32 perturbation z (the reference's z_A, z_B) and an
- * optional NS output buffer. All tensors of one side share its row stride and have unit
- * column stride. Modules must be given in the controller's order (sorted by
+ * A module owns A (d_out x r) and B (r x d_in) as F32 masters, as the reference keeps
+ * them (upcast at load, ds_mezo/controller.py:66-67), each with Kalman mean/variance
+ * (F32, ds_mezo/controller.py:90-100), the F32 perturbation z (the reference's z_A, z_B)
+ * and an optional NS output buffer. What the rollout engine loads is in the plan's copy
+ * dtype: the +/- copies (pos = copy(A + z), neg = copy(A - z), the sum taken in F32 and
+ * then rounded, as the reference's fp32 pos/neg are cast at export, ds_mezo/backend.py:
+ * 21-36) and an optional shadow of the updated masters (shadow = copy(A) after each
+ * update; NULL when not wanted). All tensors of one side share its row stride and have
+ * unit column stride. Modules must be given in the controller's order (sorted by
  * (layer, module name), ds_mezo/model_config.py:37): it fixes the random draws.
  * ------------------------------------------------------------------------------- */
 typedef struct dsmz_module_spec {
-  void* A;  void* B;
-  void* pos_A; void* pos_B; void* neg_A; void* neg_B;
+  float* A;  float* B;                  /* F32 masters, updated in place */
+  void* pos_A; void* pos_B; void* neg_A; void* neg_B;   /* copy dtype */
+  void* shadow_A; void* shadow_B;       /* copy dtype, may be NULL */
   float* mu_A; float* mu_B; float* var_A; float* var_B;
   float* z_A; float* z_B;
   float* scratch_A; float* scratch_B;   /* may be NULL */
@@ -187,7 +193,7 @@ typedef struct dsmz_basis_spec {
 } dsmz_basis_spec;
 
 typedef struct dsmz_plan_desc {
-  int32_t factor_dtype;
+  int32_t copy_dtype;                   /* DSMZ_F32 or DSMZ_BF16: the +/- copies and shadows */
   int32_t num_modules;
   const dsmz_module_spec* modules;
   int32_t num_bases;
@@ -257,6 +263,13 @@ int dsmz_step_perturb(const dsmz_plan* plan, uint64_t seed, uint64_t offset, flo
                       float beta, float q, float norm_floor, dsmz_stream_t stream);
 double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per direction */
 int32_t dsmz_plan_directions(const dsmz_plan* plan);
+
+/* Frobenius norms of the plan's fp32 master factors, A then B of each module in module
+ * order (2 * num_modules floats into the device array `norms`), with fp64 sums in a fixed
+ * order. The reference's perturbation scale is their median times FLT_EPSILON^(1/3)
+ * (ds_mezo/controller.py:78-82: torch.median, i.e. the lower middle value of an even count);
+ * on several ranks gather the norms, not the factors. */
+int dsmz_plan_factor_norms(const dsmz_plan* plan, float* norms, dsmz_stream_t stream);
 
 /* Phase 3 (ds_mezo/controller.py:272-286): Kalman observation update of mu/var with the
  * summed scalars, ZO-Muon Newton-Schulz of every updated mu, param -= eta * X.

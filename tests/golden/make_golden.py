@@ -13,7 +13,7 @@ Runs DS-MeZO's own code on CPU and records inputs and outputs:
   that returns the fp32 log-softmax logprobs of seeded logits (``scoring.pt``).
 
 Usage (needs the reference checkout; writes tests/golden/*.pt):
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>   (or DSMEZO_REFERENCE=<path>)
 """
 from __future__ import annotations
 
@@ -249,9 +249,12 @@ def scoring_cases(C, g):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("DSMEZO_REFERENCE"),
+                    help="path of the reference checkout (default: $DSMEZO_REFERENCE)")
     ap.add_argument("--only", choices=["scoring"], default=None, help="write only this fixture")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or DSMEZO_REFERENCE")
     rec = []
     K, C, MC = load_reference(Path(args.ref), rec)
     torch.save(scoring_cases(C, torch.Generator().manual_seed(31)), HERE / "scoring.pt")

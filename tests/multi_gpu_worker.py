@@ -37,6 +37,7 @@ def init_by_layer(step, layers):
             a.H(b).copy_(torch.randn(s.T, s.D, generator=g, device=a.device) * torch.exp(
                 torch.randn(s.D, generator=g, device=a.device)))
     a.var.fill_(EPS ** 2)
+    a.sync_shadow()
 
 
 def main():
@@ -70,7 +71,8 @@ def main():
             n = st.layout.sizes[r]
             for name, full in (("factors", fac), ("pos", pn["pos"]), ("neg", pn["neg"])):
                 got = st.full_view(full, r).float()
-                want = getattr(one.aset, name)[off:off + n].float()
+                arena = one.aset.export_factors if name == "factors" else getattr(one.aset, name)
+                want = arena[off:off + n].float()
                 err = float((got - want).abs().max() / want.abs().max())
                 assert err < 1e-5, (r, name, err)
             off += n

@@ -13,15 +13,15 @@ import torch
 from oracle import reference_ops as ref
 
 
-def make_inputs(layers, hidden, inter, kv, rank, tokens, seed, factor_dtype=torch.float32, act_dtype=torch.float32):
+def make_inputs(layers, hidden, inter, kv, rank, tokens, seed, copy_dtype=torch.float32, act_dtype=torch.float32):
     """Seeded synthetic adapter set: factors and momentum N(0,1) (momentum 0 for a fresh
     start is a separate case), activations N(0,1) x lognormal(0,1) channel scales,
     bases = QR of a Gaussian."""
     from dsmezo_b200 import transformer_adapter_shapes
     mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
     g = torch.Generator().manual_seed(seed)
-    A = [torch.randn(m.d_out, rank, generator=g).to(factor_dtype) for m in mods]
-    B = [torch.randn(rank, m.d_in, generator=g).to(factor_dtype) for m in mods]
+    A = [torch.randn(m.d_out, rank, generator=g).to(copy_dtype) for m in mods]
+    B = [torch.randn(rank, m.d_in, generator=g).to(copy_dtype) for m in mods]
     V0 = [torch.linalg.qr(torch.randn(b.D, rank, generator=g))[0].contiguous() for b in bases]
     H = []
     for b in bases:

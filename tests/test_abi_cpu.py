@@ -39,7 +39,8 @@ def test_every_declared_symbol_is_exported(L):
 
 
 def test_abi_version(L):
-    assert L.dsmz_abi_version() == 1
+    from dsmezo_b200._lib import ABI_VERSION
+    assert L.dsmz_abi_version() == ABI_VERSION == 2
 
 
 def test_cubic_schedule_matches_reference(L):
@@ -92,7 +93,7 @@ def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None
     if bad == "null":
         specs[1].mu_B = None
     d = _lib.PlanDesc()
-    d.factor_dtype, d.num_modules, d.modules = 1, len(mods), specs
+    d.copy_dtype, d.num_modules, d.modules = 1, len(mods), specs
     d.num_bases, d.bases, d.sm_count, d.max_threads_per_sm = len(bases), bs, 148, 2048
     return mods, d
 

@@ -27,7 +27,7 @@ def test_directions_step(K, fdt):
     from dsmezo_b200 import AdapterSet, ZOController
     layers, hidden, inter, kv, rank, tokens, seed = 1, 384, 1280, 64, 16, 256, 11
     mods, bases, A, B, V0, H = make_inputs(layers, hidden, inter, kv, rank, tokens, seed, fdt, torch.bfloat16)
-    aset = AdapterSet(mods, bases, rank, rank, factor_dtype=fdt, act_dtype=torch.bfloat16, device=DEV,
+    aset = AdapterSet(mods, bases, rank, rank, copy_dtype=fdt, act_dtype=torch.bfloat16, device=DEV,
                       keep_ns_output=True, directions=K)
     scale = TC if aset.uses_tensor_cores else 1.0
     for i in range(len(mods)):

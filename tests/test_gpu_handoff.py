@@ -127,7 +127,7 @@ def test_adapter_set_handoff_gives_the_same_basis():
     mods, bases, A, B, V0, H = make_inputs(1, 256, 704, 64, 16, 512, 21, torch.bfloat16, torch.bfloat16)
     sets = []
     for way in ("handoff", "direct"):
-        aset = AdapterSet(mods, bases, 16, 16, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
+        aset = AdapterSet(mods, bases, 16, 16, copy_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
         for i in range(len(mods)):
             aset.A(i).copy_(A[i])
             aset.B(i).copy_(B[i])
@@ -154,7 +154,7 @@ def test_adapter_set_handoff_rejects_bad_sources():
     from dsmezo_b200 import AdapterSet
     from step_harness import make_inputs
     mods, bases, *_ = make_inputs(1, 256, 704, 64, 16, 512, 22, torch.bfloat16, torch.bfloat16)
-    aset = AdapterSet(mods, bases, 16, 16, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
+    aset = AdapterSet(mods, bases, 16, 16, copy_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
     T, D = aset.H(0).shape
     with pytest.raises(ValueError):
         aset.load_activations(0, torch.zeros(T + 1, D, device=DEV))
@@ -169,18 +169,19 @@ def test_adapter_export_views(fdt):
     # ds_mezo/backend.py:21-36: lora_A.weight = B, lora_B.weight = A, bf16, one per module
     from dsmezo_b200 import ShardedStep
     gen = torch.Generator(device=DEV).manual_seed(9)
-    st = ShardedStep(2, 64, 160, 16, 8, 32, eps=1e-3, total_steps=100, generator=gen, factor_dtype=fdt,
+    st = ShardedStep(2, 64, 160, 16, 8, 32, eps=1e-3, total_steps=100, generator=gen, copy_dtype=fdt,
                      act_dtype=torch.bfloat16, device=DEV)
     a = st.aset
     g = torch.Generator().manual_seed(1)
     for i in range(len(a.modules)):
         a.A(i).copy_(torch.randn(a.A(i).shape, generator=g))
         a.B(i).copy_(torch.randn(a.B(i).shape, generator=g))
+    a.sync_shadow()
     for b in range(len(a.bases)):
         a.V(b).copy_(torch.linalg.qr(torch.randn(a.V(b).shape, generator=g))[0])
         a.H(b).copy_(torch.randn(a.H(b).shape, generator=g))
     st.perturb()
-    for which, arena in (("pos", a.pos_dir(0)), ("neg", a.neg_dir(0)), ("factors", a.factors)):
+    for which, arena in (("pos", a.pos_dir(0)), ("neg", a.neg_dir(0)), ("factors", a.export_factors)):
         ex = st.export_adapters(which)
         torch.cuda.synchronize()
         assert len(ex) == 2 * len(a.modules)

@@ -14,7 +14,7 @@ DEV = "cuda"
 def _set(seed):
     from dsmezo_b200 import AdapterSet
     mods, bases, A, B, V0, H = make_inputs(1, 256, 704, 64, 16, 512, seed, torch.bfloat16, torch.bfloat16)
-    aset = AdapterSet(mods, bases, 16, 16, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
+    aset = AdapterSet(mods, bases, 16, 16, copy_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV)
     for i in range(len(mods)):
         aset.A(i).copy_(A[i])
         aset.B(i).copy_(B[i])

@@ -28,7 +28,7 @@ def test_tc_power_iter_dropin(T, D, R):
 def _set(tc, rank, seed=4):
     from dsmezo_b200 import AdapterSet
     mods, bases, A, B, V0, H = make_inputs(1, 512, 1536, 128, rank, 384, seed, torch.bfloat16, torch.bfloat16)
-    aset = AdapterSet(mods, bases, rank, rank, factor_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV,
+    aset = AdapterSet(mods, bases, rank, rank, copy_dtype=torch.bfloat16, act_dtype=torch.bfloat16, device=DEV,
                       tensor_core_power_iter=tc)
     for b in range(len(bases)):
         aset.V(b).copy_(V0[b])

@@ -67,7 +67,7 @@ def _plan_increment(L, mods, bases_all, rank_r, layer_range, before, per_layer):
         b = bases_all[b0 + i]
         bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = 0x10000, 1, b.T, b.D, b.D, 0x10000, rank_r
     d = _lib.PlanDesc()
-    d.factor_dtype, d.num_modules, d.modules, d.num_bases, d.bases = 1, len(sel), specs, nb, bs
+    d.copy_dtype, d.num_modules, d.modules, d.num_bases, d.bases = 1, len(sel), specs, nb, bs
     d.sm_count, d.max_threads_per_sm, d.rng_offset_before = 148, 2048, before
     h = ctypes.c_void_p()
     assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0

@@ -34,7 +34,7 @@ def _noalloc(L, p, b, s, eta, sched, stream):
 
 
 @pytest.mark.parametrize("M,N,dt", [(3584, 64, torch.float32), (64, 3584, torch.bfloat16), (300, 5, torch.float32),
-                                    (18944, 64, torch.bfloat16)])
+                                    (18944, 64, torch.bfloat16), (8192, 128, torch.float32)])
 def test_noalloc_matches_workspace_entry_on_consecutive_calls(M, N, dt):
     from dsmezo_b200 import _lib
     L = _lib.lib()
@@ -53,6 +53,29 @@ def test_noalloc_matches_workspace_entry_on_consecutive_calls(M, N, dt):
         torch.cuda.synchronize()
         assert rel(s_na, s_ref) < 1e-5           # the Newton-Schulz output tolerance of the suite
         assert rel(p_na.float(), p_ref.float()) < 1e-6
+
+
+def test_noalloc_takes_no_device_memory():
+    """Device-wide free memory (cudaMemGetInfo) is the same before and after calls of the
+    entry point, once its inputs exist and a first call has looked up the scratch array."""
+    from dsmezo_b200 import _lib
+    L = _lib.lib()
+    sched = _lib.schedule("cubic")
+    stream = torch.cuda.current_stream().cuda_stream
+    M, N = 8192, 128                            # close to the scratch size (~1.66 MiB)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(5)
+    param = torch.randn(M, N, generator=g, device=DEV)
+    buf = torch.randn(M, N, generator=g, device=DEV)
+    out = torch.zeros(M, N, device=DEV)
+    assert _noalloc(L, param, buf, out, 0.01, sched, stream) == 0, L.dsmz_last_error()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert _noalloc(L, param, buf, out, 0.01, sched, stream) == 0, L.dsmz_last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
