@@ -113,6 +113,21 @@ class ClockSampler:
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(smax), "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def config_of(cfg, world, act_gb_per_gpu=None):
+    """The workload description both arms print (same keys, so the lines compare)."""
+    act = act_gb_per_gpu
+    if act is None:
+        act = cfg["tokens"] * (3 * cfg["hidden"] + cfg["inter"]) * (2 if cfg["adt"] == "bf16" else 4) * \
+            cfg["layers"] / max(world, 1) / 1e9
+    return {"workload": cfg["workload"], "layers": cfg["layers"], "hidden": cfg["hidden"],
+            "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
+            "copy_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
+            "directions": cfg.get("directions", 1), "power_iters": 3,
+            "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
+            "l2": ("inputs larger than L2 (activations %.2f GB per step per GPU)" % act) if act >= 0.256 else
+                  ("L2 flushed between timed steps (a 256 MB write outside the timing; activations %.3f GB)" % act)}
+
+
 # ----------------------------------------------------------------------------- setup
 def init_set(aset, cfg, device, layer0):
     """Seeded synthetic state: factors and momentum ~ N(0,1) (the factors rounded to the copy
@@ -146,6 +161,9 @@ def alg_bytes(aset, cfg):
     nq = (R // 8) * (R // 8 + 1) // 2
     gp = sum((b.D + 127) // 128 for b in aset.bases) * nq * 64 * 8
     return {
+        # single pass: read H once, [V_hi|V_lo]; write and read back [Y_hi|Y_lo]; write W and
+        # the W-tile Gram partials
+        "pi_fused": hb + 2 * vr + 2 * yr + (gp if R <= 64 else 0),
         "pi_y": hb + vr + yr,                      # read H, bf16 [V_hi|V_lo]; write bf16 [Y_hi|Y_lo]
         "pi_w": hb + yr + vr,                      # read H, [Y_hi|Y_lo]; write W (fp32)
         "pi_gram": gp if R <= 64 else vr,          # read the per-tile Gram partials (else W)
@@ -215,6 +233,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
+    ap.add_argument("--power-iter", default="two-pass", choices=["two-pass", "single-pass"],
+                    help="tensor-core power iteration: two products per iteration (default), or the single-pass "
+                         "kernel that reads each activation from HBM once per iteration")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.layers > 0:
@@ -242,7 +263,8 @@ def main():
     K = cfg.get("directions", 1)
     sstep = ShardedStep(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"], cfg["tokens"], eps=EPS,
                         total_steps=TOTAL_STEPS, generator=gen, copy_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
-                        schedule=cfg["schedule"], device=device, process_group=pg, directions=K)
+                        schedule=cfg["schedule"], device=device, process_group=pg, directions=K,
+                        single_pass_power_iter=args.power_iter == "single-pass")
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
@@ -289,7 +311,7 @@ def main():
     torch.cuda.synchronize()
 
     # per-kernel probes over the timed region
-    per_step = {"pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 3, "pi_split": 3, "bside": 1,
+    per_step = {"pi_fused": 3, "pi_y": 3, "pi_w": 3, "pi_gram": 6, "pi_chol": 6, "pi_apply": 3, "pi_split": 3, "bside": 1,
                 "coef": K, "draw": K, "perturb": K, "kalman_sum": K, "kalman_dirs": 1, "gram": 1, "ns_solve": 1,
                 "apply": 1}
     probes = {}
@@ -308,19 +330,25 @@ def main():
         pr += [arr_s, arr_p]                         # keep the arrays alive while probed
         lib().dsmz_plan_set_probe(aset._plan, KERNEL_IDS[name], arr_s, arr_p, len(st_ev))
 
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_stop = torch.cuda.Event(enable_timing=True)
+    # A step whose activations fit in L2 (the toy set) would find the previous step's data
+    # there: such runs write a buffer larger than L2 between timed steps, outside the timing.
+    act_bytes = sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device) if act_bytes < (256 << 20) else None
+    t_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_stop = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
     launches0 = aset.launches
     with ClockSampler([local_rank] if world == 1 else list(range(world))) as clk:
-        t_start.record()
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(i & 255)
+            t_start[i].record()
             step(record=True)
-        t_stop.record()
+            t_stop[i].record()
         torch.cuda.synchronize()
         barrier()
-    ms_local = t_start.elapsed_time(t_stop) / args.steps
+    ms_local = sum(a.elapsed_time(b) for a, b in zip(t_start, t_stop)) / args.steps
     launches_timed = aset.launches - launches0
     kern = {}
     for name, (st_ev, sp_ev, _, _) in probes.items():
@@ -478,8 +506,10 @@ def main():
     # per element: read and write the fp32 master, mu and var once, write the shadow; per
     # direction write pos, neg, z and read z back (K > 1)
     per_elem = 24 + fs + K * (2 * f + (4 if K == 1 else 8))
-    # activations: each of the 3 power iterations reads H twice (Y = H V, then W = H^T Y)
-    step_bytes = sum(sstep.layout.sizes) * per_elem + 2 * 3 * act_layer * cfg["layers"]
+    # activations: each of the 3 power iterations reads H once on the single-pass path (twice
+    # on the two-product path: Y = H V, then W = H^T Y)
+    passes = 1 if aset.single_pass_power_iter else 2
+    step_bytes = sum(sstep.layout.sizes) * per_elem + passes * 3 * act_layer * cfg["layers"]
     # the reference's power iteration reads each activation once per iteration (Y and H^T Y
     # per token chunk, ds_mezo/kernels.py:214-225): its compulsory traffic has 3 passes
     compulsory_bytes = sum(sstep.layout.sizes) * per_elem + 3 * act_layer * cfg["layers"]
@@ -494,13 +524,8 @@ def main():
         "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": cfg["fdt"] if cfg["fdt"] == "bf16" else "f32", "data": "synthetic (seeded N(0,1) factors and "
         "momentum, lognormal-scaled N(0,1) activations)",
-        "config": {"workload": cfg["workload"], "layers": cfg["layers"], "hidden": cfg["hidden"],
-                   "intermediate": cfg["inter"], "kv_out": cfg["kv"], "rank": cfg["rank"], "tokens": cfg["tokens"],
-                   "copy_dtype": cfg["fdt"], "activation_dtype": cfg["adt"], "ns_schedule": cfg["schedule"],
-                   "directions": K,
-                   "power_iters": 3, "parallelism": f"layer-sharded x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (activations %.2f GB per step per GPU)" %
-                         (sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9)},
+        "config": dict(config_of(cfg, world, sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9),
+                       power_iteration=args.power_iter),
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1),
@@ -527,24 +552,69 @@ def ctypes_void_array(n):
 
 
 def run_reference(args, cfg, world, rank):
-    """Reference arm: the reference algorithm on the host cores (the oracle port, since the
-    reference is Python/Triton with no CPU path of its own), bounded sample per step."""
+    """Reference arm: the reference algorithm on the host cores. The reference is
+    Python/Triton whose only CPU path is the Triton interpreter, and its source is not on
+    the GPU box, so the arm runs the oracle (the reference restated in fp32 torch, pinned to
+    the reference's own outputs) with every host thread. Each timed step is a whole step of
+    the whole configuration (every layer); as many steps are timed as fit in a time budget
+    (at most --steps, at least one), and the line reports that count, so value x steps is
+    the time the arm actually spent. Setup (the synthetic inputs) is outside the timing."""
     if rank != 0:
         return
+    budget_s = float(os.environ.get("DSMEZO_REFERENCE_BUDGET_S", "150"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle import reference_ops as ref
+    from step_harness import make_inputs, oracle_state
+    torch.set_num_threads(os.cpu_count() or 1)
+    K = cfg.get("directions", 1)
+    try:
+        mods, bases, A, B, V0, H = make_inputs(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"],
+                                               cfg["tokens"], cfg["seed"], DT[cfg["fdt"]], torch.float32)
+    except RuntimeError as e:      # host memory: the fp32 activations of the whole model
+        print(json.dumps({"metric": METRIC, "impl": "reference", "unavailable":
+                          f"the fp32 oracle state of the whole {cfg['workload']} does not fit in host memory: {e}"}))
+        return
+    st = oracle_state(mods, A, B, V0, EPS, TOTAL_STEPS, schedule=ref.get_schedule(cfg["schedule"]))
+    g = torch.Generator().manual_seed(cfg["seed"])
+    rca = cfg["rank"]
+
+    def one_step():
+        dirs = []
+        for _ in range(K):
+            draws = []
+            for m in mods:
+                draws.append(torch.randn(cfg["rank"], cfg["rank"], generator=g))
+                draws.append(torch.randn(m.d_out, rca, generator=g))
+            dirs.append(draws)
+        t0 = time.perf_counter()
+        st.step_count += 1
+        if K == 1:
+            perts = ref.perturb_phase(st, H, dirs[0], 3)
+            ref.update_phase(st, perts, 1.0)
+        else:
+            perts = ref.perturb_phase_directions(st, H, dirs, 3)
+            ref.update_phase_directions(st, perts, [1.0] * K)
+        return time.perf_counter() - t0
+
     times = []
-    cores = 1
-    for i in range(args.warmup + args.steps):
-        s, cores = cpu_oracle_sample(cfg, 1, 1, 0)
-        if i >= args.warmup:
-            times.append(s)
-    ms = sum(times) / len(times) * 1e3 * cfg["layers"]
-    out = {"metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-           "config": {"workload": cfg["workload"], "parallelism": "host CPU"},
-           "cpu_baseline": {"value": ms, "unit": "ms", "cores": cores, "kind": "port",
-                            "sample": f"1 of {cfg['layers']} layers per step, scaled x{cfg['layers']}"},
-           "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    t_all = time.perf_counter()
+    while len(times) < max(1, args.steps):
+        times.append(one_step())
+        spent = time.perf_counter() - t_all
+        if spent + times[-1] > budget_s:
+            break
+    ms = sum(times) / len(times) * 1e3
+    cores = torch.get_num_threads()
+    sample = (f"whole steps of the whole configuration ({cfg['layers']} layers, every adapter): {len(times)} timed, "
+              f"no warm-up, {cores} host threads (os.cpu_count() = {os.cpu_count()})")
+    out = {"metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world, "steps": len(times), "warmup": 0,
+           "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+           "dtype": cfg["fdt"] if cfg["fdt"] == "bf16" else "f32", "impl": "reference",
+           "data": "synthetic (seeded N(0,1) factors, lognormal-scaled N(0,1) activations)",
+           "config": dict(config_of(cfg, 1), parallelism="host CPU"),
+           "cpu_baseline": {"value": ms, "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+           "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "requested_steps": args.steps, "requested_warmup": args.warmup, "budget_s": budget_s}
     print(json.dumps(out), flush=True)
 
 

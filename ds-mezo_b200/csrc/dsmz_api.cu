@@ -10,6 +10,7 @@
 
 #include "dsmz_handoff.cuh"
 #include "dsmz_kernels.cuh"
+#include "dsmz_pi_fused.cuh"
 #include "dsmz_score.cuh"
 #include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
@@ -284,6 +285,18 @@ size_t pw_smem(int R) {
          512;
 }
 
+// Single-pass power iteration: stages of 2 x 128 rows plus the shared B operand, shared by
+// the Y ring (the larger half) and the W ring.
+int pf_stages(int R) {
+  const int n = (227 * 1024 - 2048 - tc::fused_fixed_bytes(R)) / tc::fused_stage_bytes(R);
+  return n > 8 ? 8 : n;
+}
+int pf_stages_y(int R) { return (pf_stages(R) + 1) / 2; }
+int pf_stages_w(int R) { return pf_stages(R) / 2; }
+size_t pf_smem(int R) {
+  return static_cast<size_t>(pf_stages(R)) * tc::fused_stage_bytes(R) + tc::fused_fixed_bytes(R) + 1024;
+}
+
 struct TCSlots {             // workspace byte offsets of one basis
   size_t v2t = 0, y2t = 0;
   size_t gp = 0;             // fused W Gram partials (R <= 64), 0: none
@@ -329,6 +342,12 @@ struct dsmz_plan {
   std::vector<TCSlots> tcs;
   size_t off_tcb = 0, err_off = 0;
   int ntc_y = 0, ntc_w = 0, ntc_vt = 0;
+  // single-pass (fused) power iteration, R <= 64: work queue and launch-local counters
+  bool fused = false;
+  std::vector<tc::PiItem> pitems_y, pitems_w;   // the Y and W queues
+  size_t off_pitems_y = 0, off_pitems_w = 0;
+  size_t fsync_off = 0, fsync_bytes = 0, fpart_off = 0;
+  int f_ytiles = 0, f_nslots = 0;
   mutable bool split_current = false;   // [V_hi | V_lo]^T matches V (set by a power iteration)
   struct Probe {
     std::vector<cudaEvent_t> start, stop;
@@ -385,6 +404,8 @@ struct dsmz_plan {
     off_tcb = T.take(tcb.size() * sizeof(tc::TCBasis), 64);
     off_smaps = T.take(smaps.size() * sizeof(CUtensorMap), 64);
     off_ysched = T.take(ysched.size() * sizeof(int32_t), 64);
+    off_pitems_y = T.take(pitems_y.size() * sizeof(tc::PiItem), 64);
+    off_pitems_w = T.take(pitems_w.size() * sizeof(tc::PiItem), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -397,6 +418,8 @@ struct dsmz_plan {
     if (!tcb.empty()) std::memcpy(blob.data() + off_tcb, tcb.data(), tcb.size() * sizeof(tc::TCBasis));
     if (!smaps.empty()) std::memcpy(blob.data() + off_smaps, smaps.data(), smaps.size() * sizeof(CUtensorMap));
     if (!ysched.empty()) std::memcpy(blob.data() + off_ysched, ysched.data(), ysched.size() * sizeof(int32_t));
+    if (!pitems_y.empty()) std::memcpy(blob.data() + off_pitems_y, pitems_y.data(), pitems_y.size() * sizeof(tc::PiItem));
+    if (!pitems_w.empty()) std::memcpy(blob.data() + off_pitems_w, pitems_w.data(), pitems_w.size() * sizeof(tc::PiItem));
   }
 };
 
@@ -491,6 +514,103 @@ void plan_tc_layout(dsmz_plan* P) {
     for (int c = 0; c < G; ++c) P->ysched.insert(P->ysched.end(), lists[c].begin(), lists[c].end());
     P->ysched_G = G;
   }
+}
+
+// Work queues of the single-pass power iteration (R <= 64, see dsmz_pi_fused.cuh).
+// Y queue: bases in windows of kWindowBases (one decoder layer's four module inputs); within
+// a window the bases' 256-token tiles go row by row (tile t of every basis, then t + 1), each
+// tile split over d into items of about kYSplitSteps k-steps, its splits consecutive. Split
+// items write partials into a ring of kPartSlots slots by queue position; an item whose slot
+// was last written by another tile waits for that tile to be reduced first.
+// W queue: the same windows; one item per 256-row d tile of a basis over all of its tokens,
+// the bases of a window dealt in proportion to their tile counts.
+constexpr int kYSplitSteps = 20;
+constexpr int kPartSlots = 512;
+constexpr int kWindowBases = 4;
+
+void plan_pi_fused(dsmz_plan* P) {
+  const int nb = static_cast<int>(P->bases.size());
+  std::vector<int> tile0(nb), ntile(nb), nsplit(nb), kper(nb), nkd(nb);
+  int nt = 0;
+  for (int b = 0; b < nb; ++b) {
+    const BasisD& B = P->bases[b];
+    tile0[b] = nt;
+    ntile[b] = static_cast<int>((B.T + 255) / 256);
+    nt += ntile[b];
+    nkd[b] = static_cast<int>((B.D + tc::kBK - 1) / tc::kBK);
+    int ns = (nkd[b] + kYSplitSteps - 1) / kYSplitSteps;
+    kper[b] = (nkd[b] + ns - 1) / ns;
+    nsplit[b] = (nkd[b] + kper[b] - 1) / kper[b];
+  }
+  P->f_ytiles = nt;
+  P->pitems_y.clear();
+  P->pitems_w.clear();
+  int nslots = 0, nyitems = 0;
+  for (int b = 0; b < nb; ++b) {
+    nyitems += ntile[b] * nsplit[b];
+    if (nsplit[b] > 1) nslots = kPartSlots;
+  }
+  int max_split = 1;
+  for (int b = 0; b < nb; ++b) max_split = std::max(max_split, nsplit[b]);
+  if (nslots) nslots = std::max(nslots, 2 * max_split);   // a tile's own splits never share a slot
+  nslots = std::min(nslots, nyitems);
+  std::vector<int> last_user(std::max(nslots, 1), -1);    // tile whose split last wrote each slot
+  int qpos = 0;
+  for (int w0 = 0; w0 < nb; w0 += kWindowBases) {
+    const int w1 = std::min(nb, w0 + kWindowBases);
+    int rows = 0;
+    for (int b = w0; b < w1; ++b) rows = std::max(rows, ntile[b]);
+    for (int t = 0; t < rows; ++t) {
+      for (int b = w0; b < w1; ++b) {
+        if (t >= ntile[b]) continue;
+        const int slot0 = nslots ? qpos % nslots : 0;
+        for (int ks = 0; ks < nsplit[b]; ++ks, ++qpos) {
+          tc::PiItem it{};
+          it.basis = b;
+          it.tile = t;
+          it.k0 = ks * kper[b];
+          it.k1 = std::min(nkd[b], it.k0 + kper[b]);
+          it.ytile = tile0[b] + t;
+          it.nsplit = nsplit[b];
+          it.ks = ks;
+          it.slot0 = slot0;
+          it.slot = nslots ? qpos % nslots : 0;
+          it.wait_tile = -1;
+          if (nsplit[b] > 1) {
+            const int prev = last_user[it.slot];
+            if (prev >= 0 && prev != it.ytile) it.wait_tile = prev;
+            last_user[it.slot] = it.ytile;
+          }
+          P->pitems_y.push_back(it);
+        }
+      }
+    }
+    // W items of the window, bases dealt in proportion to their d tiles
+    std::vector<int> nwt(w1 - w0), done(w1 - w0, 0);
+    int total = 0;
+    for (int b = w0; b < w1; ++b) { nwt[b - w0] = static_cast<int>((P->bases[b].D + 255) / 256); total += nwt[b - w0]; }
+    for (int e = 0; e < total; ++e) {
+      int best = -1;
+      for (int j = 0; j < w1 - w0; ++j)
+        if (done[j] < nwt[j] && (best < 0 || static_cast<int64_t>(done[j]) * nwt[best] < static_cast<int64_t>(done[best]) * nwt[j]))
+          best = j;
+      const int b = w0 + best;
+      tc::PiItem it{};
+      it.basis = b;
+      it.tile = done[best]++;
+      it.k0 = 0;
+      it.k1 = static_cast<int>((P->bases[b].T + tc::kBK - 1) / tc::kBK);
+      it.ytile = tile0[b];
+      it.wait_tile = -1;
+      P->pitems_w.push_back(it);
+    }
+  }
+  P->f_nslots = nslots;
+  // launch-local counters (zeroed before each launch) and the partial slots
+  P->fsync_bytes = static_cast<size_t>(2 + 2 * nt) * sizeof(int32_t);
+  P->fsync_off = P->ws.take(P->fsync_bytes);
+  P->fpart_off = P->ws.take(static_cast<size_t>(std::max(nslots, 1)) * P->R * 256 * sizeof(float));
+  P->fused = true;
 }
 
 // The four tile-box maps (param, mu, var, z) of every side-1 adapter matrix; a matrix whose
@@ -649,8 +769,29 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
     }
     P->split_current = true;            // the last QR apply writes [V_hi | V_lo]^T of V
   }
+  if (P->fused) {
+    if ((rc = set_smem(tc::k_pi_fused, pf_smem(R)))) return rc;
+  }
   for (int it = 0; it < iters; ++it) {
-    if (P->tc) {
+    if (P->fused) {
+      // one launch: Y tiles stream H from HBM, W tiles re-read it from L2
+      cudaError_t ez = cudaMemsetAsync(P->workspace + P->fsync_off, 0, P->fsync_bytes, s);
+      if (ez != cudaSuccess) return cuda_fail("power iteration counters", ez);
+      tc::PiSync sy;
+      sy.head = reinterpret_cast<int32_t*>(P->workspace + P->fsync_off);
+      sy.ycnt = sy.head + 2;
+      sy.ytdone = sy.ycnt + P->f_ytiles;
+      sy.part = reinterpret_cast<float*>(P->workspace + P->fpart_off);
+      sy.nslots = P->f_nslots;
+      const tc::PiItem* yq = reinterpret_cast<const tc::PiItem*>(P->dev_tables + P->off_pitems_y);
+      const tc::PiItem* wq = reinterpret_cast<const tc::PiItem*>(P->dev_tables + P->off_pitems_w);
+      const int ny = static_cast<int>(P->pitems_y.size()), nw = static_cast<int>(P->pitems_w.size());
+      P->probe_begin(DSMZ_KID_PI_FUSED, s);
+      tc::k_pi_fused<<<std::min(P->sm_count, std::max(ny, nw)), tc::kFusedThreads, pf_smem(R), s>>>(
+          dtcb, yq, ny, wq, nw, sy, pf_stages_y(R), pf_stages_w(R), err);
+      P->probe_end(DSMZ_KID_PI_FUSED, s);
+      DSMZ_LAUNCHED("power iteration W = H^T (H V) (single pass, tcgen05)");
+    } else if (P->tc) {
       P->probe_begin(DSMZ_KID_PI_Y, s);
       {
         const int32_t* ys = P->ysched.empty() ? nullptr : reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ysched);
@@ -1075,6 +1216,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     if (ok) {
       P->tc = true;
       plan_tc_layout(P);
+      if (P->R <= 64 && pf_stages(P->R) >= 4 && (d->flags & DSMZ_PLAN_SINGLE_PASS_POWER_ITER)) plan_pi_fused(P);
     }
   }
   add_w_tables(P);
@@ -1185,9 +1327,9 @@ uint64_t dsmz_plan_rng_increment(const dsmz_plan* p) { return p ? p->rng_increme
 int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   if (!p) return 0;
   int32_t n = 0;
-  // per iteration: Y, W, Gram of W, Cholesky, V; plus the first bf16 split of the caller's
-  // basis on the tensor-core path
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * 5 + (p->tc ? 1 : 0);
+  // per iteration: Y, W (one fused launch on the single-pass path), Gram of W, Cholesky, V;
+  // plus the first bf16 split of the caller's basis on the tensor-core path
+  if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->fused ? 4 : 5) + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }
@@ -1205,7 +1347,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   P->workspace = static_cast<char*>(workspace);
   P->split_current = false;
   patch_ws_pointers(P);
-  if (P->tc && !bind_tc(P)) P->tc = false;   // keep the CUDA-core power iteration
+  if (P->tc && !bind_tc(P)) { P->tc = false; P->fused = false; }   // keep the CUDA-core power iteration
   bind_side1_maps(P);
   bind_swz_maps(P);
   {
@@ -1219,7 +1361,7 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   return DSMZ_OK;
 }
 
-int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* P) { return (P && P->tc) ? 1 : 0; }
+int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* P) { return (P && P->tc) ? (P->fused ? 2 : 1) : 0; }
 
 int32_t dsmz_plan_device_error(const dsmz_plan* P, dsmz_stream_t stream) {
   if (!P || !P->workspace) return 0;

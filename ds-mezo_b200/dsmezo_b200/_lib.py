@@ -68,6 +68,7 @@ PI_BASIS_UNCHANGED = 1        # dsmz_step_power_iteration_ex flag (include/dsmez
 
 
 PLAN_SIMT_POWER_ITER = 1
+PLAN_SINGLE_PASS_POWER_ITER = 2
 
 
 # name -> (restype, argtypes); mirrors include/dsmezo.h
@@ -126,7 +127,7 @@ SIGNATURES = {
 
 KERNEL_IDS = {"pi_y": 0, "pi_w": 1, "pi_gram": 2, "pi_chol": 3, "pi_apply": 4, "bside": 5, "coef": 6,
               "perturb": 7, "kalman_sum": 8, "gram": 9, "ns_solve": 10, "apply": 11, "pi_split": 12, "draw": 13,
-              "kalman_dirs": 14}
+              "kalman_dirs": 14, "pi_fused": 15}
 
 _lib = None
 

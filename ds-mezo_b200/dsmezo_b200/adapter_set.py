@@ -101,7 +101,7 @@ class AdapterSet:
                  copy_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
-                 rng_direction_stride: int = 0):
+                 rng_direction_stride: int = 0, single_pass_power_iter: bool = False):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -150,7 +150,8 @@ class AdapterSet:
         self.H_arena = torch.zeros(max(nh, 1), dtype=act_dtype, device=dev)
         self.V_arena = torch.zeros(max(nv, 1), dtype=torch.float32, device=dev)
         self.layout = layout if layout is not None else device_layout(dev)
-        self._flags = 0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER
+        self._flags = (0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER) | \
+            (_lib.PLAN_SINGLE_PASS_POWER_ITER if single_pass_power_iter else 0)
         self._build_plan(int(rng_offset_before))
 
     @property
@@ -300,6 +301,12 @@ class AdapterSet:
     def uses_tensor_cores(self) -> bool:
         """True when the power iteration runs on tcgen05 tensor cores."""
         return bool(lib().dsmz_plan_uses_tensor_cores(self._plan))
+
+    @property
+    def single_pass_power_iter(self) -> bool:
+        """True when each power iteration reads every activation from HBM once (the W
+        product re-reads each token tile from L2 right after the Y product streamed it)."""
+        return int(lib().dsmz_plan_uses_tensor_cores(self._plan)) == 2
 
     def device_error(self) -> int:
         """Reads and clears the device error word (synchronises the stream)."""

@@ -145,7 +145,7 @@ class ShardedStep:
     def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
-                 directions: int = 1):
+                 directions: int = 1, single_pass_power_iter: bool = False):
         import torch.distributed as dist
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if process_group is not None else 1
@@ -160,7 +160,7 @@ class ShardedStep:
         self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
                                device=device, rng_offset_before=self.layout.rng_offset_before(self.rank),
                                layout=layout, capacity=self.layout.capacity, directions=directions,
-                               rng_direction_stride=stride)
+                               rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter)
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=process_group if self.world > 1 else None,
                                 rng_increment_total=stride * directions)

@@ -222,6 +222,13 @@ typedef struct dsmz_plan_desc {
 /* Power iteration on CUDA cores (fp32 FFMA) even where the tcgen05 path applies. The
  * tcgen05 path needs bf16 activations, D a multiple of 8 and R a multiple of 16. */
 #define DSMZ_PLAN_SIMT_POWER_ITER 1u
+/* Tensor-core power iteration in a single pass over the activations per iteration (R <= 64):
+ * one persistent launch whose Y pipeline streams each activation from HBM and whose W
+ * pipeline re-reads each 256-token tile from L2 once its Y rows are complete. Without the
+ * flag each iteration runs two products (Y = H V, then W = H^T Y), each reading every
+ * activation from HBM; at the 7B shapes that is the faster of the two (the single pass is
+ * bound by its split-K reductions and loses about half of its L2 re-reads). */
+#define DSMZ_PLAN_SINGLE_PASS_POWER_ITER 2u
 
 typedef struct dsmz_plan dsmz_plan;
 
@@ -238,7 +245,8 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* plan, int32_t num_iters);  /* ke
 int dsmz_plan_bind(dsmz_plan* plan, void* device_tables, size_t table_bytes,
                    void* workspace, size_t workspace_bytes, dsmz_stream_t stream);
 
-/* 1 when the plan runs the power iteration on tcgen05 tensor cores, 0 on CUDA cores. */
+/* How the plan runs the power iteration: 0 on CUDA cores, 1 on tcgen05 tensor cores as two
+ * products per iteration, 2 on tcgen05 tensor cores in a single pass over the activations. */
 int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* plan);
 /* Reads and clears the plan's device error word (synchronises the stream): nonzero when a
  * tensor-core kernel gave up on a barrier wait after its time limit. */
@@ -310,7 +318,8 @@ enum dsmz_kernel_id {
   DSMZ_KID_PI_SPLIT = 12,  /* [V_hi | V_lo]^T for the tensor-core products */
   DSMZ_KID_DRAW = 13,      /* Zc_A draws in torch's launch layout */
   DSMZ_KID_KALMAN_DIRS = 14, /* K-direction Kalman observation update */
-  DSMZ_NUM_KIDS = 15
+  DSMZ_KID_PI_FUSED = 15,  /* power iteration W = H^T (H V) in one pass (single-pass path) */
+  DSMZ_NUM_KIDS = 16
 };
 int dsmz_plan_set_probe(dsmz_plan* plan, int32_t kernel, void** start_events, void** stop_events,
                         int32_t capacity);

@@ -98,18 +98,22 @@ def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None
     return mods, d
 
 
-@pytest.mark.parametrize("rank,h_dtype,tc", [(8, 1, 0), (16, 1, 1), (16, 0, 0), (64, 1, 1)])
-def test_plan_create_host_only(L, rank, h_dtype, tc):
+@pytest.mark.parametrize("rank,h_dtype,flags,path", [(8, 1, 0, 0), (16, 1, 0, 1), (16, 0, 0, 0), (64, 1, 0, 1),
+                                                      (64, 1, 2, 2), (16, 1, 2, 2), (128, 1, 2, 1), (16, 0, 2, 0)])
+def test_plan_create_host_only(L, rank, h_dtype, flags, path):
     from dsmezo_b200 import draw_increments
     mods, d = _fake_set(rank=rank, h_dtype=h_dtype)
+    d.flags = flags
     h = ctypes.c_void_p()
     assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
     try:
         assert L.dsmz_plan_table_bytes(h) > 0 and L.dsmz_plan_workspace_bytes(h) > 0
         assert L.dsmz_plan_rng_increment(h) == sum(draw_increments(mods, rank, rank, 148, 2048))
-        # tcgen05 power iteration for bf16 activations and R a multiple of 16
-        assert L.dsmz_plan_uses_tensor_cores(h) == tc
-        assert L.dsmz_plan_launch_count(h, 3) == (3 * 5 + 1 if tc else 3 * 5) + 8
+        # tcgen05 power iteration for bf16 activations and R a multiple of 16: two products per
+        # iteration, or one pass over the activations (R <= 64) when the flag asks for it
+        assert L.dsmz_plan_uses_tensor_cores(h) == path
+        per_iter = {0: 5, 1: 5, 2: 4}[path]
+        assert L.dsmz_plan_launch_count(h, 3) == 3 * per_iter + (1 if path else 0) + 8
         # stepping an unbound plan is an error, not a launch
         assert L.dsmz_step_update(h, 0.0, 0.0, 0.0, 0.0, 0.0, None, None) == 1
         assert b"not bound" in L.dsmz_last_error()
