@@ -19,7 +19,6 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
 import time
 
@@ -61,56 +60,72 @@ def peaks():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """Samples SM clocks and clock-event reasons during the timed region through NVML
+    (read-only queries, every ~2 ms from a thread, so even a short timed region has
+    samples); reports no samples when NVML is not importable."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+
     def __init__(self, gpus):
         self.gpus = gpus
-        self.proc = None
-        import tempfile
-        self.path = os.path.join(tempfile.gettempdir(), f"dsmezo_clocks_{os.getpid()}.csv")
+        self.samples = []          # (sm_mhz, sm_max_mhz, reason bits)
+        self.reasons = set()
+        self._stop = False
+        self._thread = None
+        self._nvml = None
+
+    def _run(self, handles):
+        nv = self._nvml
+        bits = [(name, getattr(nv, attr, 0)) for name, attr in self.REASONS]
+        while not self._stop:
+            for h in handles:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    continue
+                self.samples.append((sm, smax))
+                for name, bit in bits:
+                    if bit and (r & bit):
+                        self.reasons.add(name)
+            time.sleep(0.002)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-i", ",".join(str(g) for g in self.gpus), "-lms", "100"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            import pynvml as nv
+            nv.nvmlInit()
+            self._nvml = nv
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            ids = [int(x) for x in vis.split(",")] if vis else None
+            handles = [nv.nvmlDeviceGetHandleByIndex(ids[g] if ids and g < len(ids) else g) for g in self.gpus]
+            import threading
+            self._thread = threading.Thread(target=self._run, args=(handles,), daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._nvml = None
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if self._nvml is not None:
             try:
-                self.proc.wait(timeout=5)
+                self._nvml.nvmlShutdown()
             except Exception:
-                self.proc.kill()
-            self.f.close()
+                pass
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    smax.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(smax), "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples (NVML unavailable)"]}
+        sm = sorted(x[0] for x in self.samples)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(x[1] for x in self.samples),
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "NVML, 2 ms period"}
 
 
 def config_of(cfg, world, act_gb_per_gpu=None):
@@ -436,7 +451,26 @@ def main():
         r1.record()
         torch.cuda.synchronize()
         ref_ms = r0.elapsed_time(r1) * sum(c.numel() for c in caps) / big.numel()
+        # the step end to end with its activations handed over on the device (the product's
+        # path: forward-hook captures already in HBM), the Kalman sums read back each step
+        host_out = torch.empty(aset.kalman_sums().numel(), dtype=torch.float64, pin_memory=True)
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        d0.record()
+        for _ in range(n_h):
+            for i, c in enumerate(caps):
+                aset.load_activations(i, c)
+            sstep.perturb()
+            host_out.copy_(aset.kalman_sums(), non_blocking=True)
+            sstep.update(sstep.broadcast_dd(next_dd()))
+        d1.record()
+        torch.cuda.synchronize()
+        e2e_dev = {"value": d0.elapsed_time(d1) / n_h, "unit": "ms", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": host_out.numel() * 8, "steps": n_h,
+                   "activations": "fp32 forward-hook captures in HBM, converted into the bf16 buffers on the device"}
         handoff = {"ms_per_step": h_ms, "bytes_per_step": hbytes, "achieved_GBps": hbytes / (h_ms * 1e-3) / 1e9,
+                   "e2e_device_resident": e2e_dev,
                    "frac": hbytes / (h_ms * 1e-3) / 1e9 / peaks()[0], "launches_per_step": len(caps),
                    "reference_round_trip_ms_per_step": ref_ms,
                    "reference_round_trip": "fp32 capture to pinned host and back (torch copies), timed on the "

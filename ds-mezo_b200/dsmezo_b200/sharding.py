@@ -16,6 +16,7 @@ largest shard, so each all-gather is one NCCL call on contiguous buffers.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -58,6 +59,125 @@ def partition_layers(layers: int, world: int, weights: Optional[Sequence[float]]
 
 
 # ----------------------------------------------------------------------------- collectives
+class CollectiveTimeout(RuntimeError):
+    """A collective of the sharded step did not complete within its host-side limit (a peer
+    stalled or left); the process group has been aborted."""
+
+
+def _abort(group) -> None:
+    """Aborts the process group from a daemon thread: on NCCL the ranks' pending
+    collectives end with an error; a backend whose abort waits for the stalled collective
+    (gloo) does not hold up the caller, which raises at once."""
+    import threading
+    import torch.distributed as dist
+    fn = getattr(dist.distributed_c10d, "_abort_process_group", None)
+    if fn is None:
+        return
+
+    def run():
+        try:
+            fn(group) if group is not None else fn()
+        except Exception:
+            pass
+    threading.Thread(target=run, name="dsmezo-abort", daemon=True).start()
+
+
+class Collectives:
+    """The step's collectives, issued asynchronously, each with a host-side time limit.
+
+    On NCCL a collective is ordered on the current CUDA stream at once (work.wait() makes
+    the stream, not the host, wait), so the step's kernels see its result without a host
+    synchronisation; a watchdog thread polls the pending handles, and when one is not
+    complete `timeout_s` after it was issued (a peer stalled or left) it aborts the process
+    group, so that the collectives of the ranks still waiting end with an error instead of
+    hanging, and records a CollectiveTimeout that check() raises at the next phase boundary.
+    settle() waits for every pending handle on the host within the same limit (the gloo
+    backend, whose handles are host-side, is settled this way)."""
+
+    def __init__(self, group=None, timeout_s: float = 60.0, poll_s: float = 1e-3):
+        import threading
+        import torch.distributed as dist
+        self.group = group
+        self.timeout_s = float(timeout_s)
+        self.poll_s = float(poll_s)
+        self.stream_ordered = dist.get_backend(group) == "nccl"
+        self._lock = threading.Lock()
+        self._pending: List[Tuple[object, str, float]] = []
+        self._error: Optional[BaseException] = None
+        self._thread = None
+
+    # ------------------------------------------------------------------ issue
+    def _issue(self, work, what: str) -> None:
+        if self.stream_ordered:
+            work.wait()                      # the current stream waits for the collective
+        with self._lock:
+            self._pending.append((work, what, time.monotonic() + self.timeout_s))
+        if self.stream_ordered and self._thread is None:
+            import threading
+            self._thread = threading.Thread(target=self._watch, name="dsmezo-collective-watchdog", daemon=True)
+            self._thread.start()
+
+    def all_reduce(self, t: torch.Tensor, what: str = "all-reduce") -> None:
+        import torch.distributed as dist
+        self._issue(dist.all_reduce(t, group=self.group, async_op=True), what)
+
+    def broadcast(self, t: torch.Tensor, src: int, what: str = "broadcast") -> None:
+        import torch.distributed as dist
+        self._issue(dist.broadcast(t, src=src, group=self.group, async_op=True), what)
+
+    def all_gather_into(self, out: torch.Tensor, local: torch.Tensor, what: str = "all-gather") -> None:
+        import torch.distributed as dist
+        self._issue(dist.all_gather_into_tensor(out, local, group=self.group, async_op=True), what)
+
+    # ------------------------------------------------------------------ limits
+    def _expire(self, what: str) -> None:
+        self._error = CollectiveTimeout(f"{what}: not complete after {self.timeout_s:g} s (a peer stalled or left); "
+                                        f"the process group was aborted")
+        _abort(self.group)
+
+    def _watch(self) -> None:
+        while self._error is None:
+            with self._lock:
+                items = list(self._pending)
+            now = time.monotonic()
+            done = set()
+            for i, (work, what, deadline) in enumerate(items):
+                if work.is_completed():
+                    done.add(id(work))
+                elif now > deadline:
+                    self._expire(what)
+                    return
+            if done:
+                with self._lock:
+                    self._pending = [p for p in self._pending if id(p[0]) not in done]
+            time.sleep(self.poll_s)
+
+    def check(self) -> None:
+        """Raises the recorded failure, if any (non-blocking)."""
+        if self._error is not None:
+            raise self._error
+
+    def settle(self) -> None:
+        """Waits on the host for every pending collective, within each one's limit."""
+        self.check()
+        with self._lock:
+            items = list(self._pending)
+        t0 = time.monotonic()
+        for work, what, deadline in items:
+            while not work.is_completed():
+                if self._error is not None:
+                    raise self._error
+                now = time.monotonic()
+                if now > deadline:
+                    self._expire(what)
+                    raise self._error
+                # fine polling while the collective is expected to end soon, coarse after
+                time.sleep(2e-5 if now - t0 < 0.01 else self.poll_s)
+            work.wait()                      # a failed collective raises here
+        with self._lock:
+            self._pending = [p for p in self._pending if p[0] not in [w for w, _, _ in items]]
+
+
 def allreduce_sums(t: torch.Tensor, group=None) -> torch.Tensor:
     """In-place sum of the rank-local Kalman sums over the group."""
     import torch.distributed as dist
@@ -145,9 +265,10 @@ class ShardedStep:
     def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
-                 directions: int = 1, single_pass_power_iter: bool = False):
+                 directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0):
         import torch.distributed as dist
         self.pg = process_group
+        self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None
         self.world = dist.get_world_size(process_group) if process_group is not None else 1
         self.rank = dist.get_rank(process_group) if process_group is not None else 0
         layout = device_layout(device)
@@ -162,8 +283,7 @@ class ShardedStep:
                                layout=layout, capacity=self.layout.capacity, directions=directions,
                                rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter)
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
-                                process_group=process_group if self.world > 1 else None,
-                                rng_increment_total=stride * directions)
+                                process_group=None, rng_increment_total=stride * directions)
         cap = self.layout.capacity
         self.gathered = {name: torch.empty(cap * self.world * (1 if name == "factors" else directions),
                                            dtype=copy_dtype, device=device)
@@ -172,24 +292,28 @@ class ShardedStep:
     # ------------------------------------------------------------------ phases
     def perturb(self):
         """Power iteration, perturbation, pos/neg; Kalman sums all-reduced across ranks."""
+        if self.coll is not None:
+            self.coll.check()                 # a collective of an earlier phase ran out of time
         self.ctl.perturb()
+        if self.world > 1:
+            self.coll.all_reduce(self.aset.kalman_sums(), "Kalman sums all-reduce")
 
     def broadcast_dd(self, dd, src: int = 0):
         """The projected-gradient scalar(s) dd = (L+ - L-) / (2 eps) from the scoring rank
         (one float, or one per direction)."""
-        if isinstance(dd, (int, float)):
-            if self.world == 1:
-                return float(dd)
-            return broadcast_scalar(dd, self.pg, src, self.aset.device)
-        vals = [float(x) for x in dd]
+        one = isinstance(dd, (int, float))
+        vals = [float(dd)] if one else [float(x) for x in dd]
         if self.world == 1:
-            return vals
-        import torch.distributed as dist
+            return vals[0] if one else vals
         t = torch.tensor(vals, dtype=torch.float64, device=self.aset.device)
-        dist.broadcast(t, src=src, group=self.pg)
-        return t.tolist()
+        self.coll.check()
+        self.coll.broadcast(t, src, "dd broadcast")
+        self.coll.settle()                    # the value is needed on the host
+        return float(t[0]) if one else t.tolist()
 
     def update(self, dd):
+        if self.coll is not None:
+            self.coll.check()
         self.ctl.update(dd)
 
     def _arena(self, name: str) -> torch.Tensor:
@@ -202,9 +326,15 @@ class ShardedStep:
         laid out rank by rank (each rank's slice padded to the largest shard)."""
         if self.world == 1:
             return {n: self._arena(n) for n in names}
+        self.coll.check()
         for n in names:
-            gather_arena(self.gathered[n], self._arena(n), self.pg)
+            self.coll.all_gather_into(self.gathered[n], self._arena(n), f"{n} all-gather")
         return {n: self.gathered[n] for n in names}
+
+    def synchronize(self) -> None:
+        """Waits (bounded) for every collective issued so far."""
+        if self.coll is not None:
+            self.coll.settle()
 
     def full_view(self, buf: torch.Tensor, rank: int) -> torch.Tensor:
         """Rank `rank`'s factor elements inside a gathered buffer."""

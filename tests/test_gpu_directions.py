@@ -22,7 +22,7 @@ def close(name, ours, o32, o64, what, scale):
     assert d_ours <= max(TOL[name] * scale, 2.0 * d_ref), f"{what}: |ours-exact| {d_ours:.2e}, |ref32-exact| {d_ref:.2e}"
 
 
-@pytest.mark.parametrize("K,fdt", [(3, torch.bfloat16), (2, torch.float32)])
+@pytest.mark.parametrize("K,fdt", [(3, torch.bfloat16), (2, torch.float32), (16, torch.bfloat16)])
 def test_directions_step(K, fdt):
     from dsmezo_b200 import AdapterSet, ZOController
     layers, hidden, inter, kv, rank, tokens, seed = 1, 384, 1280, 64, 16, 256, 11

@@ -30,18 +30,30 @@ from step_harness import cuda_draws, make_inputs, oracle_state, rel
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
-# tolerance against the exact algorithm, per quantity (CUDA-core power iteration)
-TOL = {"V": 1e-5, "z": 2e-5, "pos": 1e-6, "mu": 1e-5, "var": 1e-6, "X": 1e-5, "param": 1e-6}
+# tolerance against the exact algorithm, per quantity (CUDA-core power iteration); at a
+# fresh start mu is proportional to z, so the two share a tolerance
+TOL = {"V": 1e-5, "z": 2e-5, "pos": 1e-6, "mu": 2e-5, "var": 1e-6, "X": 1e-5, "param": 1e-6}
 # The tcgen05 power iteration takes bf16 hi/lo operands: its basis sits ~1e-5 from exact
 # (gate 1e-3), and the z, mu and Newton-Schulz quantities downstream of it follow.
 TC_SCALE = {"V": 10.0, "z": 10.0, "pos": 1.0, "mu": 10.0, "var": 10.0, "X": 10.0, "param": 1.0}
+
+
+# Downstream of an ill-conditioned QR(B V) (a near-square Gaussian B V at a fresh start) z,
+# mu, var and the Newton-Schulz output amplify the basis error by cond(B V). The tensor-core
+# bases carry ~1e-5 of bf16-pair rounding against ~1e-7 for the fp32 reference, so on that
+# path these quantities may sit up to TC_AMP times the fp32 reference's own distance from
+# exact, and never beyond TC_CAP (ten times inside the 2e-2 that bf16 configurations ask of
+# the Newton-Schulz output).
+TC_AMP, TC_CAP = 50.0, 2e-3
 
 
 def close(name, ours, o32, o64, what, tc=False, extra=1.0):
     d_ours = rel(ours, o64)
     d_ref = rel(o32, o64)
     tol = TOL[name] * (TC_SCALE[name] if tc else 1.0) * (extra if name != "param" else 1.0)
-    assert d_ours <= max(tol, 2.0 * d_ref), f"{what}: |ours-exact| {d_ours:.2e}, |ref32-exact| {d_ref:.2e}"
+    amp = TC_AMP if (tc and name in ("z", "mu", "var", "X")) else 2.0
+    ok = d_ours <= max(tol, amp * d_ref) and (not tc or name == "param" or d_ours <= TC_CAP * extra)
+    assert ok, f"{what}: |ours-exact| {d_ours:.2e}, |ref32-exact| {d_ref:.2e}"
 
 
 def _copy_exact(copy, master, z, sign, what):

@@ -117,6 +117,27 @@ def _worker(rank, world, port, mode, q):
             out = torch.empty(cap * world)
             gather_arena(out, local)
             q.put((rank, "ok", sums.tolist(), dd, out.tolist()))
+        elif mode in ("stall", "exit_between"):
+            import time
+            from dsmezo_b200.sharding import Collectives, CollectiveTimeout
+            coll = Collectives(timeout_s=1.5)
+            sums = torch.ones(2, dtype=torch.float64)
+            coll.all_reduce(sums, "step 1 all-reduce")
+            coll.settle()                                # step 1 completes on both ranks
+            if rank == 1:
+                if mode == "exit_between":
+                    os._exit(3)                          # leaves between steps, nothing in flight
+                time.sleep(6.0)                          # stalls past rank 0's limit
+                os._exit(0)
+            t0 = time.monotonic()
+            try:
+                coll.all_reduce(sums, "step 2 all-reduce")
+                coll.settle()
+                q.put((rank, "no error", None, None, None))
+            except CollectiveTimeout as e:
+                q.put((rank, "timeout", time.monotonic() - t0, None, None))
+            except Exception as e:                      # peer gone: the collective fails
+                q.put((rank, "detected", type(e).__name__, time.monotonic() - t0, None))
         else:
             if rank == 1:
                 os._exit(3)                              # dies before the all-reduce
@@ -162,6 +183,22 @@ def test_collectives_of_the_sharded_step_gloo():
 def test_rank_failure_is_detected_on_the_host():
     res = _run("fail")
     assert res[0][0] == 0 and res[0][1] == "detected"
+
+
+def test_stalled_peer_ends_in_a_bounded_timeout():
+    # rank 1 stalls past the 1.5 s limit: rank 0's bounded wait ends with CollectiveTimeout
+    # well before the process group's own 8 s timeout
+    res = _run("stall")
+    rank, status, waited = res[0][:3]
+    assert rank == 0 and status == "timeout" and 1.4 <= waited < 6.0
+
+
+def test_peer_that_leaves_between_steps_is_detected():
+    # rank 1 exits after step 1 with nothing in flight: rank 0's next collective fails or
+    # runs out of its 1.5 s limit instead of hanging
+    res = _run("exit_between")
+    rank, status = res[0][:2]
+    assert rank == 0 and status in ("timeout", "detected")
 
 
 @pytest.mark.parametrize("world,K", [(1, 1), (2, 1), (3, 2)])
