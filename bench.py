@@ -283,7 +283,6 @@ def main():
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
-    gather_events = []
 
     def next_dd():
         """The step's projected-gradient scalar(s): seeded N(0,1) x 10 for one direction; for K
@@ -294,27 +293,15 @@ def main():
         rewards = torch.bernoulli(torch.full((K, cfg["rollouts"]), 0.4), generator=dd_gen)
         return rloo_direction_scalars(rewards, EPS)
 
-    def step(record=False):
+    def step(record=False, gathers=True):
         sstep.perturb()
-        if world > 1:
-            if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record()
+        if world > 1 and gathers:
             sstep.gather("pos", "neg")              # the +/- adapters the scoring pass needs
-            if record:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
         dd = sstep.broadcast_dd(next_dd())
         sstep.update(dd)
-        if world > 1:
-            if record:
-                e2 = torch.cuda.Event(enable_timing=True)
-                e2.record()
-            sstep.gather("factors")                 # updated adapters for the next rollout
-            if record:
-                e3 = torch.cuda.Event(enable_timing=True)
-                e3.record()
-                gather_events.append((e0, e1, e2, e3))
+        if world > 1 and gathers:
+            sstep.gather("factors")                 # updated adapters for the next rollout; it
+                                                    # overlaps the next step's power iteration
 
     def barrier():
         if world > 1:
@@ -361,6 +348,9 @@ def main():
             t_start[i].record()
             step(record=True)
             t_stop[i].record()
+        if world > 1:
+            sstep.synchronize()                     # the last factors gather is part of the run
+            t_stop[-1].record()
         torch.cuda.synchronize()
         barrier()
     ms_local = sum(a.elapsed_time(b) for a, b in zip(t_start, t_stop)) / args.steps
@@ -372,8 +362,46 @@ def main():
         if cnt:
             tot = sum(st_ev[i].elapsed_time(sp_ev[i]) for i in range(cnt))
             kern[name] = {"launches": cnt, "total_ms": tot, "avg_ms": tot / cnt}
-    gather_ms = (sum(a.elapsed_time(b) + c.elapsed_time(d) for a, b, c, d in gather_events) / len(gather_events)
-                 if gather_events else 0.0)
+    # the all-gathers on their own (each timed alone, between synchronisations), and the step
+    # without them: what the gathers add to the step beyond what overlaps
+    gathers = None
+    if world > 1:
+        import torch.distributed as dist
+        g_ms = {}
+        for names in (("pos", "neg"), ("factors",)):
+            ev = []
+            for _ in range(3):
+                barrier()
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record()
+                sstep.gather(*names)
+                sstep.synchronize()
+                a1.record()
+                torch.cuda.synchronize()
+                ev.append(a0.elapsed_time(a1))
+            g_ms["+".join(names)] = sorted(ev)[1]
+        barrier()
+        torch.cuda.synchronize()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(args.steps):
+            step(gathers=False)
+        c1.record()
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([c0.elapsed_time(c1) / args.steps] + list(g_ms.values()), device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        vals = t.tolist()
+        gathers = {"compute_ms_per_step": vals[0], "allgather_ms": dict(zip(g_ms.keys(), vals[1:])),
+                   "bytes_received_per_rank": {k: (world - 1) * sstep.layout.capacity * aset.pos.element_size() *
+                                               (K if k.startswith("pos") else 1) * (2 if k.startswith("pos") else 1)
+                                               for k in g_ms},
+                   "note": "compute_ms_per_step: the same steps without the all-gathers (Kalman all-reduce and dd "
+                           "broadcast kept); allgather_ms: each gather alone; the factors gather overlaps the next "
+                           "step's power iteration in the timed steps"}
+    gather_ms = sum(gathers["allgather_ms"].values()) if gathers else 0.0
     ms = ms_local
     if world > 1:
         import torch.distributed as dist
@@ -404,6 +432,8 @@ def main():
             sstep.update(dd)
             if world > 1:
                 sstep.gather("factors")
+        if world > 1:
+            sstep.synchronize()
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -567,6 +597,7 @@ def main():
                           "compulsory_frac": compulsory_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1)},
         "kernels": kern,
         "allgather_ms_per_step": gather_ms,
+        "gathers": gathers,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "activation_handoff": handoff,

@@ -1222,6 +1222,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   add_w_tables(P);
   // modules
   uint64_t off = d->rng_offset_before;   // draws are placed relative to the step's base offset
+  uint64_t own = 0;                      // this plan's one-direction generator advance
   for (int i = 0; i < d->num_modules; ++i) {
     const dsmz_module_spec& m = d->modules[i];
     const std::string who = "dsmz_plan_create: module " + std::to_string(i);
@@ -1255,10 +1256,14 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     const int64_t nB = static_cast<int64_t>(md.r) * RC, nA = m.d_out * md.rca;
     md.thrB = dsmz_randn_threads(nB, d->sm_count, d->max_threads_per_sm);
     md.thrA = dsmz_randn_threads(nA, d->sm_count, d->max_threads_per_sm);
+    const uint64_t incB = dsmz_randn_offset_increment(nB, d->sm_count, d->max_threads_per_sm);
+    const uint64_t incA = dsmz_randn_offset_increment(nA, d->sm_count, d->max_threads_per_sm);
+    if (d->module_rng_offsets) off = d->module_rng_offsets[i];   // the module's place in the whole model's draws
     md.offB = off;
-    off += dsmz_randn_offset_increment(nB, d->sm_count, d->max_threads_per_sm);
+    off += incB;
     md.offA = off;
-    off += dsmz_randn_offset_increment(nA, d->sm_count, d->max_threads_per_sm);
+    off += incA;
+    own += incB + incA;
     md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
     md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1;
     md.zca_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(nA) * sizeof(float)) / sizeof(float));
@@ -1281,7 +1286,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   }
   // B-side sums: two CTAs per SM over the modules' concatenated d_in columns
   plan_bside(P->mods, 2 * P->sm_count, P->ws, &P->nchunks, &P->bside_cols);
-  P->rng_inc1 = off - d->rng_offset_before;
+  P->rng_inc1 = own;
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
   // streaming layouts, then the tile chunks they imply, then the per-segment buffers

@@ -802,7 +802,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb, int64_t ncols)
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], cv[j], acc[i][j]);
+            for (int j = 0; j < 8; j += 2) {   // packed fp32x2 FMA, each component as fmaf
+              asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %2};\n mov.b64 rb, {%3, %4};\n mov.b64 rc, {%0, %1};\n"
+                  " fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
+                  : "+f"(acc[i][j]), "+f"(acc[i][j + 1])
+                  : "f"(av[i]), "f"(cv[j]), "f"(cv[j + 1]));
+            }
         }
       }
       // the odd-column groups hand their sums to the even-column groups, which write

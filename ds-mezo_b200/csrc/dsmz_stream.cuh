@@ -276,6 +276,16 @@ struct TileIt {
   }
 };
 
+// (d0, d1) += (a, a) * (b0, b1) as one packed fp32x2 FMA: each component rounds exactly as
+// fmaf, and one instruction issues both, which leaves the row products' issue slots to
+// their shared-memory operand loads.
+__device__ __forceinline__ void fma2_bcast(float& d0, float& d1, float a, float b0, float b1) {
+  asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %2};\n mov.b64 rb, {%3, %4};\n mov.b64 rc, {%0, %1};\n"
+      " fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a), "f"(b0), "f"(b1));
+}
+
 // out(v, c) = sum_a X(v, a) P[a*pld + c] with X(v, a) = X[v*vs + a*as] (as = 1 when AS1).
 // A thread block owns vectors {vb + i*Q} (Q = ceil(nv/4)) and columns {4cb..4cb+3,
 // pld/2 + 4cb..+3}: the four vectors a warp reads per step are consecutive rows (distinct
@@ -311,7 +321,7 @@ __device__ __forceinline__ void mm_rows(const float* __restrict__ X, int vs, int
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], pv[j], acc[i][j]);
+        for (int j = 0; j < 8; j += 2) fma2_bcast(acc[i][j], acc[i][j + 1], xv[i], pv[j], pv[j + 1]);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -370,7 +380,7 @@ __device__ __forceinline__ void mm_rows_sw(const unsigned char* __restrict__ X, 
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xv[i], pv[j], acc[i][j]);
+          for (int j = 0; j < 8; j += 2) fma2_bcast(acc[i][j], acc[i][j + 1], xv[i], pv[j], pv[j + 1]);
       }
     }
 #pragma unroll

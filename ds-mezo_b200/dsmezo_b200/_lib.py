@@ -12,7 +12,7 @@ from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_int64, c_siz
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdsmezo.so")
 
-ABI_VERSION = 2              # DSMZ_ABI_VERSION of the structs below
+ABI_VERSION = 3              # DSMZ_ABI_VERSION of the structs below
 DSMZ_F32 = 0
 DSMZ_BF16 = 1
 MAX_RANK = 128
@@ -60,6 +60,7 @@ class PlanDesc(ctypes.Structure):
         ("directions", c_int32), ("pad0", c_int32),
         ("dir_stride_factor", c_int64), ("dir_stride_z", c_int64),
         ("rng_direction_stride", c_uint64),
+        ("module_rng_offsets", POINTER(c_uint64)),
     ]
 
 

@@ -101,7 +101,8 @@ class AdapterSet:
                  copy_dtype=torch.float32, act_dtype=torch.bfloat16, device="cuda",
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
-                 rng_direction_stride: int = 0, single_pass_power_iter: bool = False):
+                 rng_direction_stride: int = 0, single_pass_power_iter: bool = False,
+                 module_rng_offsets: Optional[Sequence[int]] = None):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -152,6 +153,9 @@ class AdapterSet:
         self.layout = layout if layout is not None else device_layout(dev)
         self._flags = (0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER) | \
             (_lib.PLAN_SINGLE_PASS_POWER_ITER if single_pass_power_iter else 0)
+        self._module_offsets = None if module_rng_offsets is None else [int(x) for x in module_rng_offsets]
+        if self._module_offsets is not None and len(self._module_offsets) != len(self.modules):
+            raise ValueError("module_rng_offsets needs one offset per module")
         self._build_plan(int(rng_offset_before))
 
     @property
@@ -271,6 +275,9 @@ class AdapterSet:
         desc.dir_stride_factor = self.capacity
         desc.dir_stride_z = self.numel
         desc.rng_direction_stride = self._rng_dir_stride
+        if self._module_offsets is not None:
+            self._offsets_arr = (ctypes.c_uint64 * max(len(self._module_offsets), 1))(*self._module_offsets)
+            desc.module_rng_offsets = self._offsets_arr
         handle = ctypes.c_void_p()
         check(L.dsmz_plan_create(ctypes.byref(desc), ctypes.byref(handle)), "dsmz_plan_create")
         self._plan = handle

@@ -1,13 +1,17 @@
-"""Layer-sharded optimizer step over one process per GPU.
+"""Sharded optimizer step over one process per GPU.
 
-The step shards by layer (each matrix's work is independent); two things cross ranks:
+The step shards by unit: a unit is one module input of one layer (the qkv, o, gate_up or
+down activation) with its power-iteration basis and the modules that read it (q, k, v;
+o; gate, up; down). Ranks take contiguous runs of units, balanced by their measured cost,
+so a rank may hold part of a layer. Each matrix's work is independent; two things cross
+ranks:
 
 * the two Kalman sums (sum z*mu, sum z^2*var) are sums over every adapter of the model
   (ds_mezo/controller.py:262-274), so they are all-reduced between the perturbation and
   update phases;
-* the random draws: every rank keeps the same torch generator and places its modules'
-  draws after the draws of all lower-ranked modules (a prefix sum of the per-module
-  generator increments), so a sharded step draws exactly what one GPU would.
+* the random draws: every rank keeps the same torch generator and places each module's
+  draws at that module's place in the whole model's controller order (a prefix sum of the
+  per-module generator increments), so a sharded step draws exactly what one GPU would.
 
 After the phases, the rollout needs the full adapter set: pos/neg copies for scoring and
 the updated factors for the next rollout, both in the copy dtype it loads (bf16 for the
@@ -22,7 +26,8 @@ from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
-from .adapter_set import AdapterSet, ZOController, device_layout, draw_increments, transformer_adapter_shapes
+from .adapter_set import (INPUT_OF, INPUT_ORDER, MODULE_NAMES, AdapterSet, BasisShape, ModuleShape, ZOController,
+                          device_layout, draw_increments, transformer_adapter_shapes)
 
 
 def partition_layers(layers: int, world: int, weights: Optional[Sequence[float]] = None) -> List[range]:
@@ -105,11 +110,17 @@ class Collectives:
         self._pending: List[Tuple[object, str, float]] = []
         self._error: Optional[BaseException] = None
         self._thread = None
+        self._deferred: Dict[str, list] = {}
 
     # ------------------------------------------------------------------ issue
-    def _issue(self, work, what: str) -> None:
+    def _issue(self, work, what: str, defer: Optional[str] = None) -> None:
+        """defer: the current stream does not wait for this collective yet; wait_for(defer)
+        orders it later (a collective that overlaps the kernels that follow it)."""
         if self.stream_ordered:
-            work.wait()                      # the current stream waits for the collective
+            if defer is None:
+                work.wait()                  # the current stream waits for the collective
+            else:
+                self._deferred.setdefault(defer, []).append(work)
         with self._lock:
             self._pending.append((work, what, time.monotonic() + self.timeout_s))
         if self.stream_ordered and self._thread is None:
@@ -125,9 +136,15 @@ class Collectives:
         import torch.distributed as dist
         self._issue(dist.broadcast(t, src=src, group=self.group, async_op=True), what)
 
-    def all_gather_into(self, out: torch.Tensor, local: torch.Tensor, what: str = "all-gather") -> None:
+    def all_gather_into(self, out: torch.Tensor, local: torch.Tensor, what: str = "all-gather",
+                        defer: Optional[str] = None) -> None:
         import torch.distributed as dist
-        self._issue(dist.all_gather_into_tensor(out, local, group=self.group, async_op=True), what)
+        self._issue(dist.all_gather_into_tensor(out, local, group=self.group, async_op=True), what, defer)
+
+    def wait_for(self, key: str) -> None:
+        """Orders the deferred collectives of `key` on the current stream (no host wait)."""
+        for work in self._deferred.pop(key, []):
+            work.wait()
 
     # ------------------------------------------------------------------ limits
     def _expire(self, what: str) -> None:
@@ -160,6 +177,8 @@ class Collectives:
     def settle(self) -> None:
         """Waits on the host for every pending collective, within each one's limit."""
         self.check()
+        for key in list(self._deferred):
+            self.wait_for(key)
         with self._lock:
             items = list(self._pending)
         t0 = time.monotonic()
@@ -200,16 +219,62 @@ def gather_arena(out: torch.Tensor, local: torch.Tensor, group=None) -> torch.Te
     return out
 
 
+# Step cost per activation byte and per adapter element, measured on one B200 at the 7B
+# shapes (power iteration 8.02 ms over 6.81 GB of bf16 activations, adapter phase 4.79 ms
+# over 161.5 M elements): the weights that balance the ranks.
+COST_PER_ACT_BYTE = 8.02e-3 / 6.81e9
+COST_PER_ELEMENT = 4.79e-3 / 161.5e6
+
+
+def model_units(layers: int) -> List[Tuple[int, str]]:
+    """Every unit of the model in order: (layer, module input), inputs as INPUT_ORDER."""
+    return [(li, g) for li in range(layers) for g in INPUT_ORDER]
+
+
+def unit_shapes(units: Sequence[Tuple[int, str]], hidden: int, intermediate: int, kv_out: int, tokens: int):
+    """Modules (controller order: by layer, then module name) and bases (one per unit, in
+    the units' order) of a run of units."""
+    dims = {"q_proj": (hidden, hidden), "k_proj": (kv_out, hidden), "v_proj": (kv_out, hidden),
+            "o_proj": (hidden, hidden), "gate_proj": (intermediate, hidden), "up_proj": (intermediate, hidden),
+            "down_proj": (hidden, intermediate)}
+    in_dim = {"qkv": hidden, "o": hidden, "gate_up": hidden, "down": intermediate}
+    bases = [BasisShape(li, g, tokens, in_dim[g]) for li, g in units]
+    index = {u: i for i, u in enumerate(units)}
+    mods = []
+    for li in sorted({li for li, _ in units}):
+        for name in MODULE_NAMES:
+            u = (li, INPUT_OF[name])
+            if u in index:
+                d_out, d_in = dims[name]
+                mods.append(ModuleShape(li, name, d_out, d_in, index[u]))
+    return mods, bases
+
+
+def unit_weight(unit: Tuple[int, str], hidden: int, intermediate: int, kv_out: int, rank_r: int, tokens: int,
+                act_bytes: int = 2) -> float:
+    mods, bases = unit_shapes([unit], hidden, intermediate, kv_out, tokens)
+    elems = sum(m.d_out * rank_r + rank_r * m.d_in for m in mods)
+    return COST_PER_ACT_BYTE * bases[0].T * bases[0].D * act_bytes + COST_PER_ELEMENT * elems
+
+
 @dataclass
 class ShardLayout:
-    ranges: List[range]
-    modules_per_layer: int
+    ranges: List[range]            # per rank: its run of units (indices into model_units)
+    units: List[Tuple[int, str]]
+    rank_modules: List[List[ModuleShape]]
+    rank_bases: List[List[BasisShape]]
     increments: List[int]          # per module of the whole model, controller order
+    offsets: Dict[Tuple[int, str], int]   # (layer, module name) -> generator offset of its draws
     sizes: List[int]               # factor elements per rank
     capacity: int                  # largest shard
 
+    def module_offsets(self, rank: int) -> List[int]:
+        return [self.offsets[(m.layer, m.name)] for m in self.rank_modules[rank]]
+
     def rng_offset_before(self, rank: int) -> int:
-        return sum(self.increments[: self.ranges[rank].start * self.modules_per_layer])
+        """Offset of the rank's first module's draws."""
+        mods = self.rank_modules[rank]
+        return self.offsets[(mods[0].layer, mods[0].name)] if mods else self.rng_increment_total
 
     @property
     def rng_increment_total(self) -> int:
@@ -217,16 +282,23 @@ class ShardLayout:
 
 
 def shard_layout(layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, world: int,
-                 sm_count: int, max_threads_per_sm: int) -> ShardLayout:
+                 sm_count: int, max_threads_per_sm: int, act_bytes: int = 2) -> ShardLayout:
+    units = model_units(layers)
+    weights = [unit_weight(u, hidden, inter, kv, rank_r, tokens, act_bytes) for u in units]
+    ranges = partition_layers(len(units), world, weights)
     mods, _ = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
-    per_layer = len(mods) // layers
     incs = draw_increments(mods, rank_r, rank_r, sm_count, max_threads_per_sm)
-    ranges = partition_layers(layers, world)
-    sizes = []
-    for lr in ranges:
-        ms = mods[lr.start * per_layer: lr.stop * per_layer]
+    offsets, off = {}, 0
+    for m, inc in zip(mods, incs):
+        offsets[(m.layer, m.name)] = off
+        off += inc
+    rank_modules, rank_bases, sizes = [], [], []
+    for r in ranges:
+        ms, bs = unit_shapes([units[i] for i in r], hidden, inter, kv, tokens)
+        rank_modules.append(ms)
+        rank_bases.append(bs)
         sizes.append(sum(m.d_out * rank_r + rank_r * m.d_in for m in ms))
-    return ShardLayout(ranges, per_layer, incs, sizes, max(sizes) if sizes else 0)
+    return ShardLayout(ranges, units, rank_modules, rank_bases, incs, offsets, sizes, max(sizes) if sizes else 0)
 
 
 # Module path of each adapted projection in a Llama/Qwen decoder, under the PEFT prefix
@@ -274,12 +346,11 @@ class ShardedStep:
         layout = device_layout(device)
         self.layout = shard_layout(layers, hidden, inter, kv, rank_r, tokens, self.world, *layout)
         self._shape = (layers, hidden, inter, kv, rank_r, tokens)
-        lr = self.layout.ranges[self.rank]
-        mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)
+        mods, bases = self.layout.rank_modules[self.rank], self.layout.rank_bases[self.rank]
         # one direction's draws over the whole model: the stride between directions' draws
         stride = self.layout.rng_increment_total
         self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
-                               device=device, rng_offset_before=self.layout.rng_offset_before(self.rank),
+                               device=device, module_rng_offsets=self.layout.module_offsets(self.rank),
                                layout=layout, capacity=self.layout.capacity, directions=directions,
                                rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter)
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
@@ -314,6 +385,7 @@ class ShardedStep:
     def update(self, dd):
         if self.coll is not None:
             self.coll.check()
+            self.coll.wait_for("factors")    # the last gather of the shadow before it is rewritten
         self.ctl.update(dd)
 
     def _arena(self, name: str) -> torch.Tensor:
@@ -323,12 +395,19 @@ class ShardedStep:
 
     def gather(self, *names: str):
         """All-gathers the named arenas ('factors', 'pos', 'neg') into full-model buffers
-        laid out rank by rank (each rank's slice padded to the largest shard)."""
+        laid out rank by rank (each rank's slice padded to the largest shard).
+
+        'pos' and 'neg' are ordered on the current stream at once (the scoring pass needs
+        them next). The 'factors' gather is left to overlap the next step's power iteration
+        and perturbation, which do not touch the shadow it sends: the stream waits for it
+        before the next update rewrites the shadow, or when the factors are exported."""
         if self.world == 1:
             return {n: self._arena(n) for n in names}
         self.coll.check()
         for n in names:
-            self.coll.all_gather_into(self.gathered[n], self._arena(n), f"{n} all-gather")
+            self.coll.wait_for(n)            # a buffer still being gathered is not reused
+            self.coll.all_gather_into(self.gathered[n], self._arena(n), f"{n} all-gather",
+                                      defer="factors" if n == "factors" else None)
         return {n: self.gathered[n] for n in names}
 
     def synchronize(self) -> None:
@@ -357,11 +436,10 @@ class ShardedStep:
         if self.world == 1:
             buf = self._arena(which)
         else:
+            self.coll.wait_for(which)
             buf = self.gathered[which]
-        layers, hidden, inter, kv, rank_r, tokens = self._shape
-        rank_mods = [transformer_adapter_shapes(layers, hidden, inter, kv, tokens, layer_range=lr)[0]
-                     for lr in self.layout.ranges]
-        idx = export_index(rank_mods, rank_r, K * cap, direction * cap)
+        rank_r = self._shape[4]
+        idx = export_index(self.layout.rank_modules, rank_r, K * cap, direction * cap)
         if buf.dtype != torch.bfloat16:
             from ._lib import DSMZ_BF16, DSMZ_F32, check, lib
             out = torch.empty(buf.numel(), dtype=torch.bfloat16, device=buf.device)

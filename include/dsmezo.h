@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define DSMZ_ABI_VERSION 2
+#define DSMZ_ABI_VERSION 3
 
 typedef void* dsmz_stream_t; /* cudaStream_t */
 
@@ -215,6 +215,12 @@ typedef struct dsmz_plan_desc {
   int64_t dir_stride_factor;
   int64_t dir_stride_z;
   uint64_t rng_direction_stride;
+  /* Host array of num_modules generator offsets (relative to the step's base offset) at
+   * which each module's two draws start, for a plan whose modules are not one contiguous
+   * run of the whole model's controller order (a rank holding parts of layers); the offset
+   * of module i is the sum of the draw advances of every module before it in that order.
+   * NULL: the draws follow rng_offset_before, module after module. */
+  const uint64_t* module_rng_offsets;
 } dsmz_plan_desc;
 
 #define DSMZ_MAX_DIRECTIONS 32

@@ -40,7 +40,7 @@ def test_every_declared_symbol_is_exported(L):
 
 def test_abi_version(L):
     from dsmezo_b200._lib import ABI_VERSION
-    assert L.dsmz_abi_version() == ABI_VERSION == 2
+    assert L.dsmz_abi_version() == ABI_VERSION == 3
 
 
 def test_cubic_schedule_matches_reference(L):

@@ -49,26 +49,25 @@ def test_partition_by_weight():
     assert [len(p) for p in parts] == [5, 1]
 
 
-def _plan_increment(L, mods, bases_all, rank_r, layer_range, before, per_layer):
-    """rng increment of a host-only plan over the modules of `layer_range`."""
+def _plan_increment(L, mods, bases, rank_r, offsets):
+    """rng increment of a host-only plan over `mods` (basis indices into `bases`) whose draws
+    sit at the given per-module offsets."""
     from dsmezo_b200 import _lib
-    sel = mods[layer_range.start * per_layer: layer_range.stop * per_layer]
-    b0 = layer_range.start * 4
-    specs = (_lib.ModuleSpec * len(sel))()
-    for i, m in enumerate(sel):
+    specs = (_lib.ModuleSpec * len(mods))()
+    for i, m in enumerate(mods):
         s = specs[i]
         for f in ("A", "B", "pos_A", "pos_B", "neg_A", "neg_B", "mu_A", "mu_B", "var_A", "var_B", "z_A", "z_B"):
             setattr(s, f, 0x10000)
         s.d_out, s.d_in, s.r, s.ld_A, s.ld_B = m.d_out, m.d_in, rank_r, rank_r, m.d_in
-        s.basis, s.layer = m.basis - b0, m.layer
-    nb = len(layer_range) * 4
-    bs = (_lib.BasisSpec * nb)()
-    for i in range(nb):
-        b = bases_all[b0 + i]
+        s.basis, s.layer = m.basis, m.layer
+    bs = (_lib.BasisSpec * len(bases))()
+    for i, b in enumerate(bases):
         bs[i].H, bs[i].h_dtype, bs[i].T, bs[i].D, bs[i].ld_H, bs[i].V, bs[i].R = 0x10000, 1, b.T, b.D, b.D, 0x10000, rank_r
     d = _lib.PlanDesc()
-    d.copy_dtype, d.num_modules, d.modules, d.num_bases, d.bases = 1, len(sel), specs, nb, bs
-    d.sm_count, d.max_threads_per_sm, d.rng_offset_before = 148, 2048, before
+    d.copy_dtype, d.num_modules, d.modules, d.num_bases, d.bases = 1, len(mods), specs, len(bases), bs
+    d.sm_count, d.max_threads_per_sm = 148, 2048
+    arr = (ctypes.c_uint64 * len(mods))(*offsets)
+    d.module_rng_offsets = arr
     h = ctypes.c_void_p()
     assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
     inc = L.dsmz_plan_rng_increment(h)
@@ -76,22 +75,46 @@ def _plan_increment(L, mods, bases_all, rank_r, layer_range, before, per_layer):
     return inc
 
 
-@pytest.mark.parametrize("world", [2, 3, 8])
-def test_rank_offsets_chain_to_the_single_gpu_stream(L, world):
-    """Each rank's draws start where the previous rank's end, so the sharded step draws
-    the same Gaussians as one GPU (the reference's per-module torch.randn order)."""
-    from dsmezo_b200 import shard_layout, transformer_adapter_shapes
-    layers, rank_r = 8, 64
+@pytest.mark.parametrize("layers,world", [(8, 2), (8, 3), (28, 8), (3, 2)])
+def test_units_cover_the_model_once_and_offsets_follow_controller_order(L, layers, world):
+    """Every module lands on exactly one rank, ranks hold contiguous runs of units, and each
+    module's draws sit at its place in the whole model's controller order, so the sharded
+    step draws the same Gaussians as one GPU (the reference's per-module torch.randn order)."""
+    from dsmezo_b200 import draw_increments, shard_layout, transformer_adapter_shapes
+    rank_r = 64
     lay = shard_layout(layers, 3584, 18944, 512, rank_r, 4096, world, 148, 2048)
     mods, bases = transformer_adapter_shapes(layers, 3584, 18944, 512, 4096)
-    total = _plan_increment(L, mods, bases, rank_r, range(layers), 0, 7)
-    assert total == lay.rng_increment_total
-    end = 0
+    assert lay.ranges[0].start == 0 and lay.ranges[-1].stop == 4 * layers
+    for a, b in zip(lay.ranges, lay.ranges[1:]):
+        assert a.stop == b.start
+    seen = [(m.layer, m.name) for rm in lay.rank_modules for m in rm]
+    assert sorted(seen) == sorted((m.layer, m.name) for m in mods) and len(set(seen)) == len(seen)
+    incs = draw_increments(mods, rank_r, rank_r, 148, 2048)
+    prefix = 0
+    for m, inc in zip(mods, incs):
+        assert lay.offsets[(m.layer, m.name)] == prefix
+        prefix += inc
+    total = 0
     for r in range(world):
-        before = lay.rng_offset_before(r)
-        assert before == end
-        end = before + _plan_increment(L, mods, bases, rank_r, lay.ranges[r], before, 7)
-    assert end == total
+        rm, rb = lay.rank_modules[r], lay.rank_bases[r]
+        for m in rm:                       # each module's basis is its unit's
+            assert rb[m.basis].layer == m.layer and rb[m.basis].name == {
+                "q_proj": "qkv", "k_proj": "qkv", "v_proj": "qkv", "o_proj": "o", "gate_proj": "gate_up",
+                "up_proj": "gate_up", "down_proj": "down"}[m.name]
+        if rm:
+            total += _plan_increment(L, rm, rb, rank_r, lay.module_offsets(r))
+    assert total == prefix == lay.rng_increment_total
+
+
+@pytest.mark.parametrize("world,bound", [(8, 1.08), (4, 1.05), (2, 1.03)])
+def test_unit_partition_balances_the_7b_set(world, bound):
+    # whole layers on 8 ranks give 4 layers against a mean of 3.5 (1.14); units do better
+    from dsmezo_b200.sharding import model_units, partition_layers, unit_weight
+    units = model_units(28)
+    w = [unit_weight(u, 3584, 18944, 512, 64, 4096) for u in units]
+    parts = partition_layers(len(units), world, w)
+    loads = [sum(w[i] for i in p) for p in parts]
+    assert max(loads) / (sum(loads) / world) <= bound
 
 
 def _free_port():
