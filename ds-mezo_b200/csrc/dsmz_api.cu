@@ -11,6 +11,7 @@
 #include "dsmz_handoff.cuh"
 #include "dsmz_kernels.cuh"
 #include "dsmz_pi_fused.cuh"
+#include "dsmz_calib.cuh"
 #include "dsmz_score.cuh"
 #include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
@@ -349,6 +350,13 @@ struct dsmz_plan {
   size_t fsync_off = 0, fsync_bytes = 0, fpart_off = 0;
   int f_ytiles = 0, f_nslots = 0;
   mutable bool split_current = false;   // [V_hi | V_lo]^T matches V (set by a power iteration)
+  // first-step calibration: per-basis sketches and state, rotation tiles
+  std::vector<CalibD> calib;
+  std::vector<int32_t> rot_tile0;
+  size_t off_calib = 0, off_rot = 0, calib_ws_bytes = 0;
+  int rot_tiles = 0;
+  int64_t calib_total = 0;
+  uint64_t calib_inc = 0;
   struct Probe {
     std::vector<cudaEvent_t> start, stop;
     int count = 0;
@@ -406,6 +414,8 @@ struct dsmz_plan {
     off_ysched = T.take(ysched.size() * sizeof(int32_t), 64);
     off_pitems_y = T.take(pitems_y.size() * sizeof(tc::PiItem), 64);
     off_pitems_w = T.take(pitems_w.size() * sizeof(tc::PiItem), 64);
+    off_calib = T.take(calib.size() * sizeof(CalibD), 64);
+    off_rot = T.take(rot_tile0.size() * sizeof(int32_t), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -420,10 +430,45 @@ struct dsmz_plan {
     if (!ysched.empty()) std::memcpy(blob.data() + off_ysched, ysched.data(), ysched.size() * sizeof(int32_t));
     if (!pitems_y.empty()) std::memcpy(blob.data() + off_pitems_y, pitems_y.data(), pitems_y.size() * sizeof(tc::PiItem));
     if (!pitems_w.empty()) std::memcpy(blob.data() + off_pitems_w, pitems_w.data(), pitems_w.size() * sizeof(tc::PiItem));
+    if (!calib.empty()) std::memcpy(blob.data() + off_calib, calib.data(), calib.size() * sizeof(CalibD));
+    if (!rot_tile0.empty()) std::memcpy(blob.data() + off_rot, rot_tile0.data(), rot_tile0.size() * sizeof(int32_t));
   }
 };
 
 namespace {
+
+// First-step calibration: each basis draws torch.randn(rows, R), rows = D when T >= D, else T
+// (torch.svd_lowrank transposes H when T < D), in basis order from one generator; its
+// calibration state takes 8 partial Grams, the rotation and, for R > 96, the Jacobi rotation.
+void plan_calibration(dsmz_plan* P, int sm_count, int mtps) {
+  Layout L;
+  int64_t e0 = 0;
+  uint64_t off = 0;
+  int tiles = 0;
+  for (const BasisD& b : P->bases) {
+    CalibD c{};
+    c.into_y = b.T < b.D ? 1 : 0;
+    const int64_t rows = c.into_y ? b.T : b.D;
+    c.e0 = e0;
+    c.n = rows * b.R;
+    c.threads = dsmz_randn_threads(c.n, sm_count, mtps);
+    c.offset = off;
+    e0 += c.n;
+    off += dsmz_randn_offset_increment(c.n, sm_count, mtps);
+    const size_t rr = static_cast<size_t>(b.R) * b.R;
+    c.gpart_off = static_cast<int64_t>(L.take(kCalibGroups * rr * sizeof(double), 256) / sizeof(double));
+    c.u_off = static_cast<int64_t>(L.take((rr + b.R) * sizeof(double), 256) / sizeof(double));
+    const size_t jn = static_cast<size_t>(jacobi_n(b.R));
+    c.uw_off = jacobi_u_in_smem(b.R) ? 0 : static_cast<int64_t>(L.take(jn * jn * sizeof(double), 256) / sizeof(double));
+    P->calib.push_back(c);
+    P->rot_tile0.push_back(tiles);
+    tiles += static_cast<int>((b.D + kRotRows - 1) / kRotRows);
+  }
+  P->calib_total = e0;
+  P->calib_inc = off;
+  P->rot_tiles = tiles;
+  P->calib_ws_bytes = L.bytes < 256 ? 256 : L.bytes;
+}
 
 // Workspace-relative slots that hold device pointers (W, Y) are stored as offsets during
 // planning and turned into addresses once the workspace is known.
@@ -737,40 +782,141 @@ void reserve_w_gram(dsmz_plan* P) {
 }
 
 // ---------------------------------------------------------------- launch sequences
-int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s, uint32_t flags = 0u) {
-  if (P->bases.empty() || iters <= 0) return 0;
-  const Tables tb = P->tables();
-  const int R = P->R;
+// Launch helpers of the power iteration: set-up (shared-memory limits, tables), the Y
+// product, and the rest of an iteration (W product, CholeskyQR of W, V = W R^-1).
+struct PiCtx {
+  Tables tb;
+  int R = 0, nb = 0, gpb = 0;
+  const tc::TCBasis* dtcb = nullptr;
+  int* err = nullptr;
+  bool gram_fused = false;   // the tensor-core W epilogue forms the fp64 W Gram (R <= 64)
+  bool small = false;
+};
+
+int pi_setup(const dsmz_plan* P, PiCtx& c) {
+  c.tb = P->tables();
+  c.R = P->R;
+  c.nb = static_cast<int>(P->bases.size());
+  c.dtcb = reinterpret_cast<const tc::TCBasis*>(P->dev_tables + P->off_tcb);
+  c.err = reinterpret_cast<int*>(P->workspace + P->err_off);
+  c.gram_fused = P->tc && c.R <= 64;
+  c.gpb = (c.R * c.R / 2 + c.R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
+  c.small = sk::gram_maxb(c.R) <= 5;
   int rc;
-  const bool small = sk::gram_maxb(R) <= 5;
   if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<2, 4>, P->Lq.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<4, 2>, P->Lq.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<1, 8>, P->Lq.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<8, 1>, P->Lq.total))) return rc;
-  if ((rc = set_smem(k_chol, chol_smem(R)))) return rc;
-  const KalmanIn kin{};
-  const int nb = static_cast<int>(P->bases.size());
-  const tc::TCBasis* dtcb = reinterpret_cast<const tc::TCBasis*>(P->dev_tables + P->off_tcb);
-  int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
-  const bool fused = P->tc && R <= 64;                 // W Gram formed in the W epilogue
-  const int gpb = (R * R / 2 + R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
+  if ((rc = set_smem(k_chol, chol_smem(c.R)))) return rc;
   if (P->tc) {
-    if ((rc = set_smem(tc::k_pi_yp<1>, py_smem(R)))) return rc;
-    if ((rc = set_smem(tc::k_pi_yp<2>, py_smem(R)))) return rc;
-    if ((rc = set_smem(tc::k_pi_w<1>, pw_smem(R)))) return rc;
-    if ((rc = set_smem(tc::k_pi_w<2>, pw_smem(R)))) return rc;
-    if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current)) {
-      P->probe_begin(DSMZ_KID_PI_SPLIT, s);
-      tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(dtcb, nb, 1);
-      P->probe_end(DSMZ_KID_PI_SPLIT, s);
-      DSMZ_LAUNCHED("power iteration basis split");
-    }
-    P->split_current = true;            // the last QR apply writes [V_hi | V_lo]^T of V
+    if ((rc = set_smem(tc::k_pi_yp<1>, py_smem(c.R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_yp<2>, py_smem(c.R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_w<1>, pw_smem(c.R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_w<2>, pw_smem(c.R)))) return rc;
   }
   if (P->fused) {
-    if ((rc = set_smem(tc::k_pi_fused, pf_smem(R)))) return rc;
+    if ((rc = set_smem(tc::k_pi_fused, pf_smem(c.R)))) return rc;
+  }
+  return 0;
+}
+
+// [V_hi | V_lo]^T of the bases as they stand (tensor-core path), from the caller's strided
+// basis when `first`, else from the contiguous result buffer.
+int pi_split(const dsmz_plan* P, const PiCtx& c, cudaStream_t s, int first = 1) {
+  if (!P->tc) return 0;
+  P->probe_begin(DSMZ_KID_PI_SPLIT, s);
+  tc::k_split_vt<<<P->ntc_vt, kThreads, 0, s>>>(c.dtcb, c.nb, first);
+  P->probe_end(DSMZ_KID_PI_SPLIT, s);
+  DSMZ_LAUNCHED("power iteration basis split");
+  return 0;
+}
+
+// Y = H V of every basis: the tensor-core path writes [Y_hi | Y_lo]^T, the CUDA-core path
+// the fp32 Y (from the caller's strided basis when `first`).
+int pi_y(const dsmz_plan* P, const PiCtx& c, cudaStream_t s, int first) {
+  const int R = c.R;
+  P->probe_begin(DSMZ_KID_PI_Y, s);
+  if (P->tc) {
+    const int32_t* ys = P->ysched.empty() ? nullptr : reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ysched);
+    const int gy = ys ? P->ysched_G : std::min(P->ntc_y, P->sm_count);
+    if (tc::w_halves(R) == 2)
+      tc::k_pi_yp<2><<<gy, tc::kThreadsTC, py_smem(R), s>>>(c.dtcb, c.nb, P->ntc_y, ys, py_stages(R), c.err);
+    else
+      tc::k_pi_yp<1><<<gy, tc::kThreadsTC, py_smem(R), s>>>(c.dtcb, c.nb, P->ntc_y, ys, py_stages(R), c.err);
+  } else {
+    k_pi_gemm<0><<<P->nytiles, kThreads, 0, s>>>(c.tb, first);
+  }
+  P->probe_end(DSMZ_KID_PI_Y, s);
+  DSMZ_LAUNCHED(P->tc ? "power iteration Y = H V (tcgen05)" : "power iteration Y = H V");
+  return 0;
+}
+
+int pi_qr_tail(const dsmz_plan* P, const PiCtx& c, float floor_, cudaStream_t s);
+
+// W = H^T Y, the Gram of W, its Cholesky factor and V = W R^-1 (with the bf16 pair of V for
+// the next tensor-core Y product).
+int pi_w_tail(const dsmz_plan* P, const PiCtx& c, float floor_, cudaStream_t s) {
+  const int R = c.R, nb = c.nb;
+  const Tables& tb = c.tb;
+  P->probe_begin(DSMZ_KID_PI_W, s);
+  if (P->tc) {
+    if (tc::w_halves(R) == 2)
+      tc::k_pi_w<2><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(c.dtcb, nb, P->ntc_w,
+                                                                                      pw_stages(R), c.err);
+    else
+      tc::k_pi_w<1><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(c.dtcb, nb, P->ntc_w,
+                                                                                      pw_stages(R), c.err);
+  } else {
+    k_pi_gemm<1><<<P->nwtiles, kThreads, 0, s>>>(tb, 0);
+  }
+  P->probe_end(DSMZ_KID_PI_W, s);
+  DSMZ_LAUNCHED(P->tc ? "power iteration W = H^T Y (tcgen05)" : "power iteration W = H^T Y");
+  return pi_qr_tail(P, c, floor_, s);
+}
+
+// CholeskyQR of W from its exact fp64 Gram (fp64 MMA: fused into the tensor-core W epilogue
+// for R <= 64, else streamed); V = W R^{-1} accumulated in fp64, with the bf16 pair for the
+// next tensor-core Y.
+int pi_qr_tail(const dsmz_plan* P, const PiCtx& c, float floor_, cudaStream_t s) {
+  const int R = c.R, nb = c.nb;
+  const Tables& tb = c.tb;
+  const KalmanIn kin{};
+  P->probe_begin(DSMZ_KID_PI_GRAM, s);
+  if (c.gram_fused) {
+    tc::k_gsum<<<nb * c.gpb, kThreads, 0, s>>>(c.dtcb, tb, tb.wA, c.gpb);
+  } else if (c.small) {
+    sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, c.err);
+  } else {
+    sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, c.err);
+  }
+  P->probe_end(DSMZ_KID_PI_GRAM, s);
+  DSMZ_LAUNCHED("power iteration Gram of W");
+  P->probe_begin(DSMZ_KID_PI_CHOL, s);
+  k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_, c.gram_fused ? 1 : 0);
+  P->probe_end(DSMZ_KID_PI_CHOL, s);
+  DSMZ_LAUNCHED("power iteration Cholesky");
+  P->probe_begin(DSMZ_KID_PI_APPLY, s);
+  switch (sk::qr_variant(P->Lq.TV, P->R)) {
+    case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, c.err); break;
+    case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, c.err); break;
+    case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, c.err); break;
+    default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, c.err); break;
+  }
+  P->probe_end(DSMZ_KID_PI_APPLY, s);
+  DSMZ_LAUNCHED("power iteration V = W R^-1");
+  return 0;
+}
+
+int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_t s, uint32_t flags = 0u) {
+  if (P->bases.empty() || iters <= 0) return 0;
+  PiCtx c;
+  int rc;
+  if ((rc = pi_setup(P, c))) return rc;
+  if (P->tc) {
+    if (!((flags & DSMZ_PI_BASIS_UNCHANGED) && P->split_current) && (rc = pi_split(P, c, s))) return rc;
+    P->split_current = true;            // the last QR apply writes [V_hi | V_lo]^T of V
   }
   for (int it = 0; it < iters; ++it) {
     if (P->fused) {
@@ -787,68 +933,74 @@ int run_power_iteration(const dsmz_plan* P, int iters, float floor_, cudaStream_
       const tc::PiItem* wq = reinterpret_cast<const tc::PiItem*>(P->dev_tables + P->off_pitems_w);
       const int ny = static_cast<int>(P->pitems_y.size()), nw = static_cast<int>(P->pitems_w.size());
       P->probe_begin(DSMZ_KID_PI_FUSED, s);
-      tc::k_pi_fused<<<std::min(P->sm_count, std::max(ny, nw)), tc::kFusedThreads, pf_smem(R), s>>>(
-          dtcb, yq, ny, wq, nw, sy, pf_stages_y(R), pf_stages_w(R), err);
+      tc::k_pi_fused<<<std::min(P->sm_count, std::max(ny, nw)), tc::kFusedThreads, pf_smem(c.R), s>>>(
+          c.dtcb, yq, ny, wq, nw, sy, pf_stages_y(c.R), pf_stages_w(c.R), c.err);
       P->probe_end(DSMZ_KID_PI_FUSED, s);
       DSMZ_LAUNCHED("power iteration W = H^T (H V) (single pass, tcgen05)");
-    } else if (P->tc) {
-      P->probe_begin(DSMZ_KID_PI_Y, s);
-      {
-        const int32_t* ys = P->ysched.empty() ? nullptr : reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ysched);
-        const int gy = ys ? P->ysched_G : std::min(P->ntc_y, P->sm_count);
-        if (tc::w_halves(R) == 2)
-          tc::k_pi_yp<2><<<gy, tc::kThreadsTC, py_smem(R), s>>>(dtcb, nb, P->ntc_y, ys, py_stages(R), err);
-        else
-          tc::k_pi_yp<1><<<gy, tc::kThreadsTC, py_smem(R), s>>>(dtcb, nb, P->ntc_y, ys, py_stages(R), err);
-      }
-      P->probe_end(DSMZ_KID_PI_Y, s);
-      DSMZ_LAUNCHED("power iteration Y = H V (tcgen05)");
-      P->probe_begin(DSMZ_KID_PI_W, s);
-      if (tc::w_halves(R) == 2)
-        tc::k_pi_w<2><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
-                                                                                        pw_stages(R), err);
-      else
-        tc::k_pi_w<1><<<std::min(P->ntc_w, P->sm_count), tc::kThreadsTC, pw_smem(R), s>>>(dtcb, nb, P->ntc_w,
-                                                                                        pw_stages(R), err);
-      P->probe_end(DSMZ_KID_PI_W, s);
-      DSMZ_LAUNCHED("power iteration W = H^T Y (tcgen05)");
+      if ((rc = pi_qr_tail(P, c, floor_, s))) return rc;
     } else {
-    P->probe_begin(DSMZ_KID_PI_Y, s);
-    k_pi_gemm<0><<<P->nytiles, kThreads, 0, s>>>(tb, it == 0 ? 1 : 0);
-    P->probe_end(DSMZ_KID_PI_Y, s);
-    DSMZ_LAUNCHED("power iteration Y = H V");
-    P->probe_begin(DSMZ_KID_PI_W, s);
-    k_pi_gemm<1><<<P->nwtiles, kThreads, 0, s>>>(tb, 0);
-    P->probe_end(DSMZ_KID_PI_W, s);
-    DSMZ_LAUNCHED("power iteration W = H^T Y");
+      if ((rc = pi_y(P, c, s, it == 0 ? 1 : 0))) return rc;
+      if ((rc = pi_w_tail(P, c, floor_, s))) return rc;
     }
-    // CholeskyQR of W from its exact fp64 Gram (fp64 MMA: fused into the tensor-core W
-    // epilogue for R <= 64, else streamed); V = W R^{-1} accumulated in fp64, with the bf16
-    // pair for the next tensor-core Y.
-    P->probe_begin(DSMZ_KID_PI_GRAM, s);
-    if (fused) {
-      tc::k_gsum<<<nb * gpb, kThreads, 0, s>>>(dtcb, tb, tb.wA, gpb);
-    } else if (small) {
-      sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
-    } else {
-      sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, err);
-    }
-    P->probe_end(DSMZ_KID_PI_GRAM, s);
-    DSMZ_LAUNCHED("power iteration Gram of W");
-    P->probe_begin(DSMZ_KID_PI_CHOL, s);
-    k_chol<<<nb, kThreads, chol_smem(R), s>>>(tb, tb.wA, floor_, fused ? 1 : 0);
-    P->probe_end(DSMZ_KID_PI_CHOL, s);
-    DSMZ_LAUNCHED("power iteration Cholesky");
-    P->probe_begin(DSMZ_KID_PI_APPLY, s);
-    switch (sk::qr_variant(P->Lq.TV, P->R)) {
-      case 0: sk::k_sqr_apply<2, 4><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 1: sk::k_sqr_apply<4, 2><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      case 2: sk::k_sqr_apply<1, 8><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-      default: sk::k_sqr_apply<8, 1><<<P->grid_w, sk::kQrThreads, P->Lq.total, s>>>(tb, tb.wB, nb, P->nwsegsB, P->Lq, err); break;
-    }
-    P->probe_end(DSMZ_KID_PI_APPLY, s);
-    DSMZ_LAUNCHED("power iteration V = W R^-1");
   }
+  return 0;
+}
+
+// First-step calibration (the sequence is derived at the top of dsmz_calib.cuh): sketches,
+// niter power iterations, the Ritz stage of the T >= D bases (Gram of Y, one more iteration,
+// eigenvectors of R_W^-T G_Y R_W^-1), that of the T < D bases (Y of the new basis, its Gram,
+// eigenvectors), then V <- V C.
+int run_calibration(const dsmz_plan* P, uint64_t seed, uint64_t offset, int niter, float floor_, char* cws,
+                    float* sv, cudaStream_t s) {
+  if (P->bases.empty()) return 0;
+  PiCtx c;
+  int rc;
+  if ((rc = pi_setup(P, c))) return rc;
+  const int R = c.R, nb = c.nb;
+  if ((rc = set_smem(k_calib_eig, jacobi_smem(R)))) return rc;
+  if ((rc = set_smem(k_calib_rotate, rotate_smem(R)))) return rc;
+  const CalibD* dcd = reinterpret_cast<const CalibD*>(P->dev_tables + P->off_calib);
+  const int32_t* dt0 = reinterpret_cast<const int32_t*>(P->dev_tables + P->off_rot);
+  const tc::TCBasis* ytcb = P->tc ? c.dtcb : nullptr;
+  const int gdraw = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((P->calib_total + kThreads - 1) / kThreads,
+                                                                            static_cast<int64_t>(P->sm_count) * 8)));
+  auto ygram = [&]() {
+    const size_t sm = ygram_smem(R);
+    if (R <= 16) k_calib_ygram<1><<<nb * kCalibGroups, kThreads, sm, s>>>(c.tb, dcd, ytcb, cws);
+    else if (R <= 32) k_calib_ygram<2><<<nb * kCalibGroups, kThreads, sm, s>>>(c.tb, dcd, ytcb, cws);
+    else if (R <= 64) k_calib_ygram<4><<<nb * kCalibGroups, kThreads, sm, s>>>(c.tb, dcd, ytcb, cws);
+    else k_calib_ygram<8><<<nb * kCalibGroups, kThreads, sm, s>>>(c.tb, dcd, ytcb, cws);
+    DSMZ_LAUNCHED("calibration Gram of Y");
+    return 0;
+  };
+  // sketches: V = R_D (T >= D); Y = H V for all bases, then Y = R_T (T < D)
+  k_calib_draw<<<gdraw, kThreads, 0, s>>>(c.tb, dcd, nullptr, P->calib_total, seed, offset, 0);
+  DSMZ_LAUNCHED("calibration sketch (V)");
+  if ((rc = pi_split(P, c, s, 0))) return rc;
+  if ((rc = pi_y(P, c, s, 0))) return rc;
+  k_calib_draw<<<gdraw, kThreads, 0, s>>>(c.tb, dcd, ytcb, P->calib_total, seed, offset, 1);
+  DSMZ_LAUNCHED("calibration sketch (Y)");
+  if (niter >= 1) {
+    if ((rc = pi_w_tail(P, c, floor_, s))) return rc;
+    for (int it = 1; it < niter; ++it) {
+      if ((rc = pi_y(P, c, s, 0))) return rc;
+      if ((rc = pi_w_tail(P, c, floor_, s))) return rc;
+    }
+    if ((rc = pi_y(P, c, s, 0))) return rc;
+  }
+  // T >= D: G_Y, one more iteration (R_W^-1 in the Cholesky workspace), eigenvectors
+  if ((rc = ygram())) return rc;
+  if ((rc = pi_w_tail(P, c, floor_, s))) return rc;
+  k_calib_eig<<<nb, kThreads, jacobi_smem(R), s>>>(c.tb, dcd, cws, 0, sv);
+  DSMZ_LAUNCHED("calibration eigenvectors (T >= D)");
+  // T < D: Y of the new basis, its Gram, eigenvectors
+  if ((rc = pi_y(P, c, s, 0))) return rc;
+  if ((rc = ygram())) return rc;
+  k_calib_eig<<<nb, kThreads, jacobi_smem(R), s>>>(c.tb, dcd, cws, 1, sv);
+  DSMZ_LAUNCHED("calibration eigenvectors (T < D)");
+  k_calib_rotate<<<P->rot_tiles, kThreads, rotate_smem(R), s>>>(c.tb, dcd, dt0, cws);
+  DSMZ_LAUNCHED("calibration rotation");
+  P->split_current = false;
   return 0;
 }
 
@@ -1207,6 +1359,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     fill_basis_tiles(bd, P->nytiles, P->nwtiles);
     P->bases.push_back(bd);
   }
+  plan_calibration(P, d->sm_count, d->max_threads_per_sm);
   if (!P->bases.empty() && !(d->flags & DSMZ_PLAN_SIMT_POWER_ITER)) {
     bool ok = true;
     for (int i = 0; i < d->num_bases; ++i) {
@@ -1409,6 +1562,24 @@ double* dsmz_step_kalman_sums(const dsmz_plan* P) {
 }
 
 int32_t dsmz_plan_directions(const dsmz_plan* P) { return P ? P->ndir : 0; }
+
+size_t dsmz_plan_calibration_workspace_bytes(const dsmz_plan* P) { return P ? P->calib_ws_bytes : 0; }
+uint64_t dsmz_plan_calibration_rng_increment(const dsmz_plan* P) { return P ? P->calib_inc : 0; }
+
+int dsmz_plan_calibrate(const dsmz_plan* P, uint64_t seed, uint64_t offset, int32_t niter, float norm_floor,
+                        void* workspace, size_t workspace_bytes, float* singular_values, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_plan_calibrate");
+  if (rc) return rc;
+  if (niter < 0) return fail(DSMZ_ERR_INVALID, "dsmz_plan_calibrate: niter must be >= 0");
+  if (!workspace || workspace_bytes < P->calib_ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(DSMZ_ERR_WORKSPACE, "dsmz_plan_calibrate: workspace must be 256-byte aligned and hold " +
+                                        std::to_string(P->calib_ws_bytes) + " bytes");
+  for (const BasisD& b : P->bases)
+    if (b.R > b.T || b.R > b.D)
+      return fail(DSMZ_ERR_INVALID, "dsmz_plan_calibrate: the basis width exceeds min(T, D) of a basis");
+  return run_calibration(P, seed, offset, niter, norm_floor, static_cast<char*>(workspace), singular_values,
+                         static_cast<cudaStream_t>(stream));
+}
 
 int dsmz_plan_factor_norms(const dsmz_plan* P, float* norms, dsmz_stream_t stream) {
   int rc = plan_ready(P, "dsmz_plan_factor_norms");

@@ -113,6 +113,10 @@ SIGNATURES = {
     "dsmz_plan_uses_tensor_cores": (c_int32, [c_void_p]),
     "dsmz_plan_directions": (c_int32, [c_void_p]),
     "dsmz_plan_factor_norms": (c_int32, [c_void_p, c_void_p, c_void_p]),
+    "dsmz_plan_calibration_workspace_bytes": (c_size_t, [c_void_p]),
+    "dsmz_plan_calibration_rng_increment": (c_uint64, [c_void_p]),
+    "dsmz_plan_calibrate": (c_int32, [c_void_p, c_uint64, c_uint64, c_int32, c_float, c_void_p, c_size_t,
+                                      c_void_p, c_void_p]),
     "dsmz_step_update_directions": (c_int32, [c_void_p, POINTER(c_float), c_int32, c_float, c_float, c_float,
                                               c_float, POINTER(NSSchedule), c_void_p]),
     "dsmz_plan_device_error": (c_int32, [c_void_p, c_void_p]),

@@ -344,6 +344,37 @@ class AdapterSet:
         self.launches += n - (1 if (unchanged and self.uses_tensor_cores and num_iters > 0) else 0)
         self._v_version = self.V_arena._version if num_iters > 0 else self._v_version
 
+    def calibrate(self, generator: Optional[torch.Generator] = None, niter: int = 3, norm_floor: float = FLT_MIN,
+                  offset: Optional[int] = None, advance: Optional[int] = None,
+                  singular_values: bool = False) -> Optional[torch.Tensor]:
+        """First-step calibration (ds_mezo/controller.py:156-163): every basis becomes V of
+        torch.svd_lowrank(H, q=basis_width, niter) of its loaded activation, the sketches
+        drawn in basis order from `generator` (default: the device's default CUDA generator,
+        which svd_lowrank uses). `offset`: the generator offset of this set's first sketch
+        (default: the generator's current offset); `advance`: how far to move the generator
+        afterwards (default: this set's draws). Returns the Ritz singular values
+        (num_bases x basis_width) when asked."""
+        from .calibration import calibration_launches, generator_of
+        L = lib()
+        gen = generator_of(self.device, generator)
+        seed = gen.initial_seed()
+        off = gen.get_offset() if offset is None else int(offset)
+        start = gen.get_offset()
+        inc = int(L.dsmz_plan_calibration_rng_increment(self._plan))
+        nbytes = int(L.dsmz_plan_calibration_workspace_bytes(self._plan))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        sv = torch.empty((len(self.bases), self.basis_width), dtype=torch.float32, device=self.device) \
+            if singular_values else None
+        check(L.dsmz_plan_calibrate(self._plan, int(seed) & (2 ** 64 - 1), off, int(niter), float(norm_floor),
+                                    ws.data_ptr(), nbytes, sv.data_ptr() if sv is not None else None,
+                                    self._stream()), "calibration")
+        ws.record_stream(torch.cuda.current_stream(self.device))
+        gen.set_offset(start + (inc if advance is None else int(advance)))
+        if self.bases:
+            self.launches += calibration_launches(int(niter), self.uses_tensor_cores)
+        self._v_version = None
+        return sv
+
     def perturb(self, seed: int, offset: int, eps: float, beta: float, q: float, norm_floor: float = FLT_MIN):
         check(lib().dsmz_step_perturb(self._plan, int(seed) & (2 ** 64 - 1), int(offset), float(eps), float(beta),
                                       float(q), float(norm_floor), self._stream()), "perturbation")

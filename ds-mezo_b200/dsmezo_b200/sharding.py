@@ -360,6 +360,20 @@ class ShardedStep:
                                            dtype=copy_dtype, device=device)
                          for name in ("factors", "pos", "neg")} if self.world > 1 else None
 
+    def calibrate(self, generator: Optional[torch.Generator] = None, niter: int = 3):
+        """First-step calibration of this rank's bases (AdapterSet.calibrate) with the
+        sketches the one-GPU calibration would draw: this rank's first sketch sits after
+        the earlier ranks' sketches (the bases are one contiguous run of the model's basis
+        order), and every rank advances the generator by the whole model's draws."""
+        from .calibration import basis_draw_increments, generator_of
+        gen = generator_of(self.aset.device, generator)
+        layout = device_layout(self.aset.device)
+        incs = [basis_draw_increments(bs, self.aset.basis_width, *layout) for bs in self.layout.rank_bases]
+        start = gen.get_offset()
+        before = sum(sum(x) for x in incs[: self.rank])
+        total = sum(sum(x) for x in incs)
+        self.aset.calibrate(generator=gen, niter=niter, offset=start + before, advance=total)
+
     # ------------------------------------------------------------------ phases
     def perturb(self):
         """Power iteration, perturbation, pos/neg; Kalman sums all-reduced across ranks."""

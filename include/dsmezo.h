@@ -285,6 +285,23 @@ int32_t dsmz_plan_directions(const dsmz_plan* plan);
  * on several ranks gather the norms, not the factors. */
 int dsmz_plan_factor_norms(const dsmz_plan* plan, float* norms, dsmz_stream_t stream);
 
+/* First-step calibration of the bases (replaces the torch.svd_lowrank loop of
+ * ds_mezo/controller.py:156-163; the rank choice of :137-154 stays on the host): every
+ * basis V becomes V of torch.svd_lowrank(H, q = R, niter), i.e. the top-R Ritz vectors of
+ * H^T H on the randomized range finder's subspace, columns by descending singular value,
+ * each signed so that its largest entry in the rotation is positive (torch's signs are those
+ * of its SVD backend). The sketches are torch.randn(D, R) (T >= D) or torch.randn(T, R)
+ * (T < D, where svd_lowrank works on H^T), drawn in basis order from the generator at
+ * (seed, offset); the generator advance is dsmz_plan_calibration_rng_increment. R must not
+ * exceed min(T, D). singular_values (device, num_bases x R floats, or NULL) receives the
+ * values svd_lowrank returns. workspace: device memory of
+ * dsmz_plan_calibration_workspace_bytes, 256-byte aligned, free after the call's stream
+ * work. */
+size_t dsmz_plan_calibration_workspace_bytes(const dsmz_plan* plan);
+uint64_t dsmz_plan_calibration_rng_increment(const dsmz_plan* plan);
+int dsmz_plan_calibrate(const dsmz_plan* plan, uint64_t seed, uint64_t offset, int32_t niter, float norm_floor,
+                        void* workspace, size_t workspace_bytes, float* singular_values, dsmz_stream_t stream);
+
 /* Phase 3 (ds_mezo/controller.py:272-286): Kalman observation update of mu/var with the
  * summed scalars, ZO-Muon Newton-Schulz of every updated mu, param -= eta * X.
  * schedule NULL = cubic. */

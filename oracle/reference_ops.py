@@ -499,3 +499,60 @@ def rloo_direction_scalars(rewards: torch.Tensor, eps: float) -> List[float]:
         lm = -sum(adv[N // 2:]) / (N // 2)
         out.append((lp - lm) / (2.0 * eps))
     return out
+
+
+# --------------------------------------------------------------------------------------
+# First-step calibration (ds_mezo/controller.py:135-163)
+# --------------------------------------------------------------------------------------
+def svd_lowrank_sketched(H: torch.Tensor, sketch: torch.Tensor, niter: int, dtype=torch.float64):
+    """(V, S) of torch.svd_lowrank(H, q, niter) with its Gaussian sketch given instead of
+    drawn. The algorithm is torch's (the reference pins torch 2.10.0, uv.lock:4003-4004):
+    torch/_lowrank.py _svd_lowrank and get_approximate_basis, i.e. Halko, Martinsson & Tropp
+    2009, Algorithms 4.4 and 5.1. It transposes H when T < D, so the sketch is (D, q) when
+    T >= D and (T, q) when T < D (torch.randn(A.shape[-1], q) of the transposed A)."""
+    A = H.to(dtype)
+    T, D = A.shape
+    tall = T >= D
+    if not tall:
+        A = A.T
+    Q = torch.linalg.qr(A @ sketch.to(dtype)).Q
+    for _ in range(niter):
+        Q = torch.linalg.qr(A.T @ Q).Q
+        Q = torch.linalg.qr(A @ Q).Q
+    U, S, Vh = torch.linalg.svd(Q.T @ A, full_matrices=False)
+    V, U = Vh.T, Q @ U
+    if not tall:
+        U, V = V, U
+    return V, S
+
+
+def calibrate_bases(activations: Sequence[torch.Tensor], sketches: Sequence[torch.Tensor], niter: int,
+                    dtype=torch.float64):
+    """ds_mezo/controller.py:156-163 over the unique activations in order, with the sketches
+    of their svd_lowrank calls given: the calibrated bases and their Ritz singular values."""
+    return [svd_lowrank_sketched(h, s, niter, dtype) for h, s in zip(activations, sketches)]
+
+
+def mp_median_quadrature(beta: float) -> float:
+    """Median of the Marchenko-Pastur law by numerical quadrature of its density
+    sqrt((b - x)(x - a)) / (2 pi beta x) and root finding (scipy), an independent check of
+    the product's closed-form CDF."""
+    from scipy import integrate, optimize
+    sb = math.sqrt(beta)
+    a, b = (1 - sb) ** 2, (1 + sb) ** 2
+    dens = lambda x: math.sqrt(max((b - x) * (x - a), 0.0)) / (2 * math.pi * beta * x)
+    cdf = lambda x: integrate.quad(dens, a, x, epsabs=1e-14, epsrel=1e-13, limit=200)[0]
+    return optimize.brentq(lambda x: cdf(x) - 0.5, a, b, xtol=1e-15, rtol=1e-15)
+
+
+def optht_rank(sv, beta: float) -> int:
+    """optht(beta, sv, sigma=None) (optht 0.2.0, uv.lock:2464-2465; used at
+    ds_mezo/controller.py:153), from its paper (Gavish & Donoho 2014): the cutoff
+    omega(beta) * median(sv), omega = lambda*(beta) / sqrt(MP median), and the rank is the
+    last index above the cutoff plus one (0 when none is)."""
+    import numpy as np
+    lam = math.sqrt(2 * (beta + 1) + 8 * beta / (beta + 1 + math.sqrt(beta ** 2 + 14 * beta + 1)))
+    omega = lam / math.sqrt(mp_median_quadrature(beta))
+    sv = np.asarray(sv)
+    idx = np.where(sv > omega * np.median(sv))[0]
+    return int(np.max(idx)) + 1 if idx.size else 0
