@@ -537,6 +537,39 @@ def main():
                    "dd": sc.projected_gradient(float(lp), float(ln), 1e-3)}
         del rows
 
+    # first-step calibration of every basis (once per run; after the timed steps, since it
+    # rewrites the bases): ours against the reference's torch.svd_lowrank loop over fp32
+    # activations (its hooks hand over fp32), timed on one layer's four and scaled by layers
+    calib = None
+    if not args.no_e2e and world == 1:
+        from dsmezo_b200.calibration import calibration_launches
+        cgen = torch.Generator(device=device).manual_seed(cfg["seed"] + 3)
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        aset.calibrate(generator=cgen)                       # warm-up
+        torch.cuda.synchronize()
+        c0.record()
+        aset.calibrate(generator=cgen)
+        c1.record()
+        torch.cuda.synchronize()
+        c_ms = c0.elapsed_time(c1)
+        per_layer = 4                                        # the qkv, o, gate_up and down inputs
+        hs = [aset.H(b).float() for b in range(per_layer)]
+        torch.svd_lowrank(hs[0], q=aset.basis_width, niter=3)
+        torch.cuda.synchronize()
+        c0.record()
+        for h in hs:
+            torch.svd_lowrank(h, q=aset.basis_width, niter=3)
+        c1.record()
+        torch.cuda.synchronize()
+        r_ms = c0.elapsed_time(c1) * (len(aset.bases) / per_layer)
+        calib = {"ms": c_ms, "launches": calibration_launches(3, aset.uses_tensor_cores),
+                 "bases": len(aset.bases), "niter": 3,
+                 "reference_svd_lowrank_ms": r_ms,
+                 "reference": "torch.svd_lowrank(H.float(), q=R, niter=3) per basis on this GPU, timed on one "
+                              "layer's 4 activations and scaled by the layer count"}
+        del hs
+
     # a bounded wait that gave up sets the plan's error word and the kernels after it stop
     # early: such a run has no valid timing
     derr = aset.device_error()
@@ -602,6 +635,7 @@ def main():
         "e2e": e2e,
         "activation_handoff": handoff,
         "scoring": scoring,
+        "calibration": calib,
         "gpu_launches": launches_timed,
         "clocks": clk.summary(),
     }

@@ -1,8 +1,8 @@
 """Worker for test_gpu_multi.py (launched by torch.distributed.run, one rank per GPU).
 
-Runs one layer-sharded step and, on rank 0, the same step on one GPU; compares every
-rank's gathered factors, pos and neg, and their PEFT-named exports, with the single-GPU
-ones. Prints MULTI_OK."""
+Calibrates every rank's bases against a one-GPU calibration, then runs one layer-sharded
+step and, on rank 0, the same step on one GPU; compares every rank's gathered factors, pos
+and neg, and their PEFT-named exports, with the single-GPU ones. Prints MULTI_OK."""
 import datetime
 import os
 import sys
@@ -50,6 +50,26 @@ def main():
     gen.manual_seed(7)
     st = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=gen, device=dev, process_group=dist.group.WORLD)
     init_units(st)
+    # first-step calibration: each rank's bases equal the one-GPU calibration's, and every
+    # rank's generator ends where the one-GPU calibration leaves it
+    cgen = torch.Generator(device=dev)
+    cgen.manual_seed(11)
+    st.calibrate(generator=cgen)
+    ref1 = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=torch.Generator(device=dev), device=dev,
+                       process_group=None)
+    init_units(ref1)
+    cg1 = torch.Generator(device=dev)
+    cg1.manual_seed(11)
+    ref1.calibrate(generator=cg1)
+    torch.cuda.synchronize()
+    assert cgen.get_offset() == cg1.get_offset(), "calibration advanced the generators differently"
+    want_v = {(s.layer, s.name): ref1.aset.V(b) for b, s in enumerate(ref1.aset.bases)}
+    for b, s in enumerate(st.aset.bases):
+        err = float((st.aset.V(b) - want_v[(s.layer, s.name)]).abs().max())
+        assert err < 1e-6, ("calibrated basis", s.layer, s.name, err)
+    # the one-GPU step below starts from the same calibrated bases
+    calibrated = {k: v.clone() for k, v in want_v.items()}
+    del ref1
     st.perturb()
     pn = st.gather("pos", "neg")
     pn = {k: v.clone() for k, v in pn.items()}
@@ -63,6 +83,8 @@ def main():
         g1.manual_seed(7)
         one = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=g1, device=dev, process_group=None)
         init_units(one)
+        for b, s in enumerate(one.aset.bases):
+            one.aset.V(b).copy_(calibrated[(s.layer, s.name)])
         one.perturb()
         one.update(4.5)
         torch.cuda.synchronize()
