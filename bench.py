@@ -248,6 +248,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
+    ap.add_argument("--perturb", default="cuda-cores", choices=["cuda-cores", "tensor-cores"],
+                    help="row products of the perturbation: inside the streaming kernel (default), or the "
+                         "tcgen05 kernel (rank <= 64)")
     ap.add_argument("--power-iter", default="two-pass", choices=["two-pass", "single-pass"],
                     help="tensor-core power iteration: two products per iteration (default), or the single-pass "
                          "kernel that reads each activation from HBM once per iteration")
@@ -279,7 +282,8 @@ def main():
     sstep = ShardedStep(cfg["layers"], cfg["hidden"], cfg["inter"], cfg["kv"], cfg["rank"], cfg["tokens"], eps=EPS,
                         total_steps=TOTAL_STEPS, generator=gen, copy_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
                         schedule=cfg["schedule"], device=device, process_group=pg, directions=K,
-                        single_pass_power_iter=args.power_iter == "single-pass")
+                        single_pass_power_iter=args.power_iter == "single-pass",
+                        tensor_core_perturb=args.perturb == "tensor-cores")
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
@@ -453,7 +457,16 @@ def main():
     handoff = None
     if not args.no_e2e and world == 1:
         hgen = torch.Generator(device=device).manual_seed(cfg["seed"] + 1)
-        caps = [torch.randn(b.T, b.D, generator=hgen, device=device) for b in aset.bases]
+        # fp32 captures of the first bases that fit in a quarter of the free memory (all of
+        # them up to the 7B set; a subset of the 70B set, whose captures exceed HBM)
+        budget = torch.cuda.mem_get_info(device)[0] // 4
+        nb_h, tot = 0, 0
+        for b in aset.bases:
+            if tot + b.T * b.D * 4 > budget:
+                break
+            tot += b.T * b.D * 4
+            nb_h += 1
+        caps = [torch.randn(b.T, b.D, generator=hgen, device=device) for b in aset.bases[:nb_h]]
         hbytes = sum(c.numel() * (4 + aset.H_arena.element_size()) for c in caps)
         for i, c in enumerate(caps):
             aset.load_activations(i, c)
@@ -500,6 +513,7 @@ def main():
                    "d2h_bytes_per_step": host_out.numel() * 8, "steps": n_h,
                    "activations": "fp32 forward-hook captures in HBM, converted into the bf16 buffers on the device"}
         handoff = {"ms_per_step": h_ms, "bytes_per_step": hbytes, "achieved_GBps": hbytes / (h_ms * 1e-3) / 1e9,
+                   "bases_handed_over": f"{nb_h} of {len(aset.bases)}",
                    "e2e_device_resident": e2e_dev,
                    "frac": hbytes / (h_ms * 1e-3) / 1e9 / peaks()[0], "launches_per_step": len(caps),
                    "reference_round_trip_ms_per_step": ref_ms,
@@ -542,7 +556,6 @@ def main():
     # activations (its hooks hand over fp32), timed on one layer's four and scaled by layers
     calib = None
     if not args.no_e2e and world == 1:
-        from dsmezo_b200.calibration import calibration_launches
         cgen = torch.Generator(device=device).manual_seed(cfg["seed"] + 3)
         c0 = torch.cuda.Event(enable_timing=True)
         c1 = torch.cuda.Event(enable_timing=True)
@@ -563,7 +576,7 @@ def main():
         c1.record()
         torch.cuda.synchronize()
         r_ms = c0.elapsed_time(c1) * (len(aset.bases) / per_layer)
-        calib = {"ms": c_ms, "launches": calibration_launches(3, aset.uses_tensor_cores),
+        calib = {"ms": c_ms, "launches": aset.calibration_launch_count(3),
                  "bases": len(aset.bases), "niter": 3,
                  "reference_svd_lowrank_ms": r_ms,
                  "reference": "torch.svd_lowrank(H.float(), q=R, niter=3) per basis on this GPU, timed on one "
@@ -622,7 +635,7 @@ def main():
         "dtype": cfg["fdt"] if cfg["fdt"] == "bf16" else "f32", "data": "synthetic (seeded N(0,1) factors and "
         "momentum, lognormal-scaled N(0,1) activations)",
         "config": dict(config_of(cfg, world, sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9),
-                       power_iteration=args.power_iter),
+                       power_iteration=args.power_iter, perturbation=args.perturb),
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1),

@@ -12,6 +12,7 @@
 #include "dsmz_kernels.cuh"
 #include "dsmz_pi_fused.cuh"
 #include "dsmz_calib.cuh"
+#include "dsmz_adapter_tc.cuh"
 #include "dsmz_score.cuh"
 #include "dsmz_stream.cuh"
 #include "dsmz_tc.cuh"
@@ -319,6 +320,8 @@ struct dsmz_plan {
   char* dev_tables = nullptr;
   char* workspace = nullptr;
   int nsegs = 0, nwsegsA = 0, nwsegsB = 0, nchunks = 0, nytiles = 0, nwtiles = 0, ndblk = 0;
+  int ysplit = 1;                   // K splits of the CUDA-core Y product (few output tiles)
+  int64_t ytotal = 0;               // elements of every basis's Y
   int64_t bside_cols = 0;   // concatenated d_in columns of the B-side sums (nchunks CTAs over them)
   int sm_count = 0;
   int grid_m = 0, grid_w = 0, grid_w1 = 0;   // streaming-kernel grids (chunks) of mats, w2, w1
@@ -328,6 +331,10 @@ struct dsmz_plan {
   sk::Layout Lp{}, Lg{}, La{}, Lq{};   // streaming kernels: perturb, Kalman Gram, apply, QR apply
   sk::Layout Lw{};                     // Gram of the power-iteration W
   int copy_dtype = DSMZ_F32;          // +/- copies and shadows (the masters are fp32)
+  bool ptc = false;                   // perturbation on the tensor cores (atc::k_perturb_tc)
+  atc::PLayout Lpt{};                 // its shared-memory layout
+  std::vector<int32_t> ptiles;        // its tiles: first 128-vector tile of each matrix, then the total
+  size_t off_ptiles = 0;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
   size_t norm_off = 0;                // fp64 partials of the factor norms (kNormSlices per matrix)
@@ -350,6 +357,9 @@ struct dsmz_plan {
   size_t fsync_off = 0, fsync_bytes = 0, fpart_off = 0;
   int f_ytiles = 0, f_nslots = 0;
   mutable bool split_current = false;   // [V_hi | V_lo]^T matches V (set by a power iteration)
+  // Zc_A draws of direction 0 issued ahead (dsmz_step_draw) for the perturbation at this key
+  mutable bool pre_drawn = false;
+  mutable uint64_t pre_seed = 0, pre_off = 0;
   // first-step calibration: per-basis sketches and state, rotation tiles
   std::vector<CalibD> calib;
   std::vector<int32_t> rot_tile0;
@@ -383,6 +393,7 @@ struct dsmz_plan {
     t.bases = reinterpret_cast<const BasisD*>(dev_tables + off_bases);
     t.nbases = static_cast<int32_t>(bases.size());
     t.nytiles = nytiles;
+    t.ysplit = ysplit;
     t.nwtiles = nwtiles;
     t.wA = reinterpret_cast<const MatD*>(dev_tables + off_w1);
     t.wB = reinterpret_cast<const MatD*>(dev_tables + off_w2);
@@ -416,6 +427,7 @@ struct dsmz_plan {
     off_pitems_w = T.take(pitems_w.size() * sizeof(tc::PiItem), 64);
     off_calib = T.take(calib.size() * sizeof(CalibD), 64);
     off_rot = T.take(rot_tile0.size() * sizeof(int32_t), 64);
+    off_ptiles = T.take(ptiles.size() * sizeof(int32_t), 64);
     table_bytes = T.bytes < 64 ? 64 : T.bytes;
   }
   void write_blob() {
@@ -432,10 +444,31 @@ struct dsmz_plan {
     if (!pitems_w.empty()) std::memcpy(blob.data() + off_pitems_w, pitems_w.data(), pitems_w.size() * sizeof(tc::PiItem));
     if (!calib.empty()) std::memcpy(blob.data() + off_calib, calib.data(), calib.size() * sizeof(CalibD));
     if (!rot_tile0.empty()) std::memcpy(blob.data() + off_rot, rot_tile0.data(), rot_tile0.size() * sizeof(int32_t));
+    if (!ptiles.empty()) std::memcpy(blob.data() + off_ptiles, ptiles.data(), ptiles.size() * sizeof(int32_t));
   }
 };
 
 namespace {
+
+// The CUDA-core Y product has (T/64) x (R/64) output tiles per basis: when that is well
+// under two CTAs per SM (small sets), K = D is split so each split's CTAs stream their own
+// chunk of H, and k_pi_ysum adds the partials in slot order (deterministic).
+void plan_ysplit(dsmz_plan* P) {
+  P->ysplit = 1;
+  if (P->tc || P->bases.empty()) return;
+  int64_t mind = P->bases[0].D;
+  P->ytotal = 0;
+  for (const BasisD& b : P->bases) {
+    mind = std::min(mind, b.D);
+    P->ytotal += b.T * b.R;
+  }
+  int sp = std::max(1, std::min(8, 296 / std::max(1, P->nytiles)));
+  while (sp > 1 && mind / sp < 128) --sp;
+  P->ysplit = sp;
+  if (sp > 1)
+    for (BasisD& b : P->bases)
+      b.ypart_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(sp) * b.T * b.R * sizeof(float)) / sizeof(float));
+}
 
 // First-step calibration: each basis draws torch.randn(rows, R), rows = D when T >= D, else T
 // (torch.svd_lowrank transposes H when T < D), in basis order from one generator; its
@@ -682,6 +715,25 @@ void bind_side1_maps(dsmz_plan* P) {
 // in the workspace, or the basis rows), of side-0 mu and of W; a slot the driver refuses
 // (alignment, strides) falls back to element copies into the same image (slot = -1).
 void bind_swz_maps(dsmz_plan* P) {
+  // K-operand rows of the perturbation: 128-row boxes for the tensor-core kernel, which needs
+  // every one of them (else the plan keeps the CUDA-core perturbation)
+  if (P->ptc) {
+    for (const MatD& m : P->mats) {
+      const ModD& D = P->mods[m.owner];
+      CUtensorMap tmp;
+      const void* base = m.side == 0 ? static_cast<const void*>(reinterpret_cast<const float*>(P->workspace) + D.zca_off)
+                                      : static_cast<const void*>(P->bases[D.basis].Vin);
+      const int64_t cols = m.side == 0 ? D.rca : D.rc;
+      const int64_t rows = m.side == 0 ? m.nvec : P->bases[D.basis].D;
+      const int64_t ld = m.side == 0 ? D.rca : P->bases[D.basis].v_s0;
+      const int64_t cs = m.side == 0 ? 1 : P->bases[D.basis].v_s1;
+      const bool ok = m.kmap >= 0 && cs == 1 && (reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * 4) % 16 == 0 &&
+                      encode_rows_swz(&tmp, base, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
+                                      static_cast<uint64_t>(ld) * 4, static_cast<uint32_t>(atc::kTile));
+      if (!ok) { P->ptc = false; break; }
+    }
+  }
+  const int krows = P->ptc ? atc::kTile : P->Lp.TV;
   auto enc = [&](int32_t& slot, const void* base, int64_t cols, int64_t rows, int64_t ld, int64_t cs, int TV) {
     if (slot < 0) return;
     const bool ok = base != nullptr && cs == 1 && TV <= 256 && TV % 8 == 0 &&
@@ -693,11 +745,11 @@ void bind_swz_maps(dsmz_plan* P) {
   for (MatD& m : P->mats) {
     const ModD& D = P->mods[m.owner];
     if (m.side == 0) {
-      enc(m.kmap, reinterpret_cast<const float*>(P->workspace) + D.zca_off, D.rca, m.nvec, D.rca, 1, P->Lp.TV);
+      enc(m.kmap, reinterpret_cast<const float*>(P->workspace) + D.zca_off, D.rca, m.nvec, D.rca, 1, krows);
       enc(m.rmap, m.mu, m.r, m.nvec, m.ld, m.cs, P->La.TV);
     } else {
       const BasisD& Bd = P->bases[D.basis];
-      enc(m.kmap, Bd.Vin, D.rc, Bd.D, Bd.v_s0, Bd.v_s1, P->Lp.TV);
+      enc(m.kmap, Bd.Vin, D.rc, Bd.D, Bd.v_s0, Bd.v_s1, krows);
     }
   }
   for (MatD& m : P->w2) enc(m.rmap, m.mu, m.r, m.nvec, m.ld, m.cs, P->Lq.TV);
@@ -730,6 +782,22 @@ bool bind_tc(dsmz_plan* P) {
 // most sk::stream_tv(r)) whose perturbation, Gram and apply layouts all fit with a ring
 // of at least kTeams stages for the team kernels (two for the Gram). One width for all of
 // them: their segments (Kalman and Gram partials) follow the same tile chunks.
+// The tensor-core perturbation's epilogue reads and writes each vector's elements in place:
+// unit component strides, and rows of tall matrices in 16-byte vectors (row length, leading
+// dimension and the arrays' alignment multiples of four elements).
+bool ptc_strides_ok(const dsmz_plan* P) {
+  const int fes = P->copy_dtype == DSMZ_BF16 ? 2 : 4;
+  auto al = [](const void* p, int b) { return (reinterpret_cast<uintptr_t>(p) % b) == 0; };
+  if ((P->dstride_f % 4) != 0 || (P->dstride_z % 4) != 0) return false;
+  for (const MatD& m : P->mats) {
+    if (m.cs != 1) return false;
+    if (m.side == 0 && ((m.ld % 4) != 0 || (m.r % 4) != 0 || !al(m.param, 16) || !al(m.mu, 16) || !al(m.var, 16) ||
+                        !al(m.z, 16) || !al(m.pos, 4 * fes) || !al(m.neg, 4 * fes)))
+      return false;
+  }
+  return true;
+}
+
 bool choose_adapter_layouts(dsmz_plan* P) {
   const int r = P->r, rca = P->r < P->RC ? P->r : P->RC;
   for (int tv = sk::stream_tv(r); tv >= 8; tv = (tv / 2) & ~7) {
@@ -739,7 +807,26 @@ bool choose_adapter_layouts(dsmz_plan* P) {
     const bool ok = P->Lp.S >= sk::kTeams && P->La.S >= sk::kTeams && P->Lg.S >= 2 &&
                     P->Lp.total <= kStreamSmem + 2048 && P->La.total <= kStreamSmem + 2048 &&
                     P->Lg.total <= kStreamSmem + 2048;
-    if (ok) return true;
+    if (ok) {
+      // the tensor-core perturbation when its shapes, strides and shared memory allow
+      const int kw = P->RC > rca ? P->RC : rca;
+      if (P->ptc && atc::perturb_ok(r, kw) && ptc_strides_ok(P)) {
+        P->Lpt = atc::perturb_layout(r, kw, kStreamSmem);
+        P->ptc = P->Lpt.S >= 2 && P->Lpt.total <= kStreamSmem + 2048;
+      } else {
+        P->ptc = false;
+      }
+      if (P->ptc) {
+        P->ptiles.clear();
+        int32_t t = 0;
+        for (const MatD& m : P->mats) {
+          P->ptiles.push_back(t);
+          t += static_cast<int32_t>((m.nvec + atc::kTile - 1) / atc::kTile);
+        }
+        P->ptiles.push_back(t);
+      }
+      return true;
+    }
     if (tv == 8) break;
   }
   return false;
@@ -846,7 +933,12 @@ int pi_y(const dsmz_plan* P, const PiCtx& c, cudaStream_t s, int first) {
     else
       tc::k_pi_yp<1><<<gy, tc::kThreadsTC, py_smem(R), s>>>(c.dtcb, c.nb, P->ntc_y, ys, py_stages(R), c.err);
   } else {
-    k_pi_gemm<0><<<P->nytiles, kThreads, 0, s>>>(c.tb, first);
+    k_pi_gemm<0><<<dim3(P->nytiles, P->ysplit), kThreads, 0, s>>>(c.tb, first);
+    if (P->ysplit > 1) {
+      DSMZ_LAUNCHED("power iteration Y = H V (split)");
+      const int g = static_cast<int>(std::min<int64_t>((P->ytotal + kThreads - 1) / kThreads, 1184));
+      k_pi_ysum<<<g, kThreads, 0, s>>>(c.tb, P->ytotal);
+    }
   }
   P->probe_end(DSMZ_KID_PI_Y, s);
   DSMZ_LAUNCHED(P->tc ? "power iteration Y = H V (tcgen05)" : "power iteration Y = H V");
@@ -1005,7 +1097,6 @@ int run_calibration(const dsmz_plan* P, uint64_t seed, uint64_t offset, int nite
 }
 
 // K directions: joint Kalman observation (k_kalman_dirs) writes mu2 / var2, then the plain
-// fp64 Gram of mu2, the Newton-Schulz solve and the apply.
 int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, const NSArgs& ns, cudaStream_t s) {
   if (P->mats.empty()) return 0;
   const Tables tb = P->tables();
@@ -1062,8 +1153,13 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
   if ((rc = set_smem(k_coef<0>, cs))) return rc;
   const bool bf = P->copy_dtype == DSMZ_BF16;
-  if ((rc = set_smem(sk::k_sperturb<2>, P->Lp.total))) return rc;
-  if ((rc = set_smem(sk::k_sperturb<4>, P->Lp.total))) return rc;
+  if (P->ptc) {
+    if ((rc = set_smem(atc::k_perturb_tc<2>, P->Lpt.total))) return rc;
+    if ((rc = set_smem(atc::k_perturb_tc<4>, P->Lpt.total))) return rc;
+  } else {
+    if ((rc = set_smem(sk::k_sperturb<2>, P->Lp.total))) return rc;
+    if ((rc = set_smem(sk::k_sperturb<4>, P->Lp.total))) return rc;
+  }
   P->probe_begin(DSMZ_KID_BSIDE, s);
   k_bside<<<P->nchunks, kThreads, 0, s>>>(tb, P->bside_cols);     // B V and var_B V^2: the same for every direction
   P->probe_end(DSMZ_KID_BSIDE, s);
@@ -1072,17 +1168,28 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
     Tables td = tb;
     td.dir = k;
     const uint64_t off = offset + static_cast<uint64_t>(k) * P->rng_dir_stride;
-    P->probe_begin(DSMZ_KID_DRAW, s);
-    sk::k_draw_zca<<<std::min(P->ndblk, 16 * P->sm_count), 256, 0, s>>>(td, seed, off);
-    P->probe_end(DSMZ_KID_DRAW, s);
-    DSMZ_LAUNCHED("Zc_A draws");
+    if (!(k == 0 && P->pre_drawn && P->pre_seed == seed && P->pre_off == offset)) {
+      P->probe_begin(DSMZ_KID_DRAW, s);
+      sk::k_draw_zca<<<std::min(P->ndblk, 16 * P->sm_count), 256, 0, s>>>(td, seed, off);
+      P->probe_end(DSMZ_KID_DRAW, s);
+      DSMZ_LAUNCHED("Zc_A draws");
+    }
+    if (k == 0) P->pre_drawn = false;   // consumed (or superseded by this launch's own draws)
     P->probe_begin(DSMZ_KID_COEF, s);
     k_coef<0><<<static_cast<int>(P->mods.size()), kThreads, cs, s>>>(td, seed, off, floor_, k == 0 ? 1 : 0);
     P->probe_end(DSMZ_KID_COEF, s);
     DSMZ_LAUNCHED("AGZO coefficients");
     P->probe_begin(DSMZ_KID_PERTURB, s);
-    if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
-    else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    if (P->ptc) {
+      const int32_t* tt = reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ptiles);
+      const int nt = P->ptiles.back();
+      const int g = std::max(1, std::min(std::min(P->sm_count, P->nsegs), nt));
+      if (bf) atc::k_perturb_tc<2><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin, err);
+      else atc::k_perturb_tc<4><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin, err);
+    } else {
+      if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+      else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+    }
     P->probe_end(DSMZ_KID_PERTURB, s);
     DSMZ_LAUNCHED("perturbation");
     P->probe_begin(DSMZ_KID_KALMAN_SUM, s);
@@ -1372,6 +1479,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
       if (P->R <= 64 && pf_stages(P->R) >= 4 && (d->flags & DSMZ_PLAN_SINGLE_PASS_POWER_ITER)) plan_pi_fused(P);
     }
   }
+  plan_ysplit(P);
   add_w_tables(P);
   // modules
   uint64_t off = d->rng_offset_before;   // draws are placed relative to the step's base offset
@@ -1443,6 +1551,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
   // streaming layouts, then the tile chunks they imply, then the per-segment buffers
+  P->ptc = (d->flags & DSMZ_PLAN_TENSOR_CORE_PERTURB) != 0;
   if (P->r > 0 && !choose_adapter_layouts(P)) {
     delete P;
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");
@@ -1487,7 +1596,8 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   int32_t n = 0;
   // per iteration: Y, W (one fused launch on the single-pass path), Gram of W, Cholesky, V;
   // plus the first bf16 split of the caller's basis on the tensor-core path
-  if (!p->bases.empty() && num_iters > 0) n += num_iters * (p->fused ? 4 : 5) + (p->tc ? 1 : 0);
+  if (!p->bases.empty() && num_iters > 0)
+    n += num_iters * ((p->fused ? 4 : 5) + (p->ysplit > 1 ? 1 : 0)) + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }
@@ -1518,6 +1628,8 @@ int dsmz_plan_bind(dsmz_plan* P, void* device_tables, size_t table_bytes, void* 
   if (e != cudaSuccess) return cuda_fail("dsmz_plan_bind: table upload", e);
   return DSMZ_OK;
 }
+
+int32_t dsmz_plan_perturb_on_tensor_cores(const dsmz_plan* P) { return (P && P->ptc) ? 1 : 0; }
 
 int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* P) { return (P && P->tc) ? (P->fused ? 2 : 1) : 0; }
 
@@ -1556,6 +1668,22 @@ int dsmz_step_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float 
                      static_cast<cudaStream_t>(stream));
 }
 
+int dsmz_step_draw(const dsmz_plan* P, uint64_t seed, uint64_t offset, dsmz_stream_t stream) {
+  int rc = plan_ready(P, "dsmz_step_draw");
+  if (rc) return rc;
+  if (P->mods.empty()) return DSMZ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const Tables tb = P->tables();
+  P->probe_begin(DSMZ_KID_DRAW, s);
+  sk::k_draw_zca<<<std::min(P->ndblk, 16 * P->sm_count), 256, 0, s>>>(tb, seed, offset);
+  P->probe_end(DSMZ_KID_DRAW, s);
+  DSMZ_LAUNCHED("Zc_A draws");
+  P->pre_drawn = true;
+  P->pre_seed = seed;
+  P->pre_off = offset;
+  return DSMZ_OK;
+}
+
 double* dsmz_step_kalman_sums(const dsmz_plan* P) {
   if (!P || !P->workspace) return nullptr;
   return reinterpret_cast<double*>(P->workspace) + P->kal_sum_off;
@@ -1564,6 +1692,14 @@ double* dsmz_step_kalman_sums(const dsmz_plan* P) {
 int32_t dsmz_plan_directions(const dsmz_plan* P) { return P ? P->ndir : 0; }
 
 size_t dsmz_plan_calibration_workspace_bytes(const dsmz_plan* P) { return P ? P->calib_ws_bytes : 0; }
+
+int32_t dsmz_plan_calibration_launch_count(const dsmz_plan* P, int32_t niter) {
+  if (!P || P->bases.empty() || niter < 0) return 0;
+  // sketches 2, Y products niter + 2 (niter 0: 2), W tails niter + 1 of four launches,
+  // Grams of Y 2, eigen-solves 2, rotation 1, the first bf16 split on the tensor-core path
+  const int ny = niter >= 1 ? niter + 2 : 2;
+  return 2 + ny * (1 + (P->ysplit > 1 ? 1 : 0)) + 4 * (niter + 1) + 5 + (P->tc ? 1 : 0);
+}
 uint64_t dsmz_plan_calibration_rng_increment(const dsmz_plan* P) { return P ? P->calib_inc : 0; }
 
 int dsmz_plan_calibrate(const dsmz_plan* P, uint64_t seed, uint64_t offset, int32_t niter, float norm_floor,
@@ -1746,6 +1882,7 @@ static dsmz_plan pi_plan(int64_t T, int64_t D, int64_t R, bool tc) {
   P.R = static_cast<int>(R);
   if (tc) plan_tc_layout(&P);
   P.tc = tc;
+  plan_ysplit(&P);
   add_w_tables(&P);
   reserve_w_gram(&P);
   P.pack();

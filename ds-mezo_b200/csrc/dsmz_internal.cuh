@@ -67,6 +67,7 @@ struct BasisD {
   float* Vout;                // D x R contiguous result of the power iteration
   int64_t y_off, w_off;       // floats: Y (T x R) and W (D x R)
   int32_t ytile0, nytile;     // (T/64) x (R/64) output tiles of Y = H V
+  int64_t ypart_off;          // floats: ysplit partial Y (T x R each) of the split-K Y product
   int32_t wtile0, nwtile;     // (D/64) x (R/64) output tiles of W = H^T Y
 };
 
@@ -75,6 +76,7 @@ struct Tables {
   const MatD* mats; int32_t nmats; int32_t nsegs;      // adapter matrices
   const ModD* mods; int32_t nmods; int32_t nchunks;
   const BasisD* bases; int32_t nbases; int32_t nytiles; int32_t nwtiles;
+  int32_t ysplit;                                       // K splits of the CUDA-core Y product
   const MatD* wA; const MatD* wB;                       // W of each basis: CholeskyQR round 1, round 2 (-> V)
   int32_t nwsegsA; int32_t nwsegsB;
   int32_t copy_dtype; int32_t ndblk;                   // +/- copies and shadows; ndblk: blocks of the Zc_A draw

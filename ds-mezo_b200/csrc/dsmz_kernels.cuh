@@ -1143,7 +1143,16 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
   const int64_t m0 = static_cast<int64_t>(mt) * 64;
   const int n0 = nt * 64;
   const int64_t Mdim = (MODE == 0) ? Bd.T : Bd.D;
-  const int64_t Kdim = (MODE == 0) ? Bd.D : Bd.T;
+  int64_t Kdim = (MODE == 0) ? Bd.D : Bd.T;
+  // Y = H V with K = D split over blockIdx.y (tb.ysplit chunks of a multiple of 16):
+  // chunk s writes its partial product into slot s, summed in order by k_pi_ysum
+  int64_t kbeg = 0;
+  const bool split = MODE == 0 && tb.ysplit > 1;
+  if (split) {
+    const int64_t kc = ((Kdim + tb.ysplit - 1) / tb.ysplit + 15) & ~static_cast<int64_t>(15);
+    kbeg = static_cast<int64_t>(blockIdx.y) * kc;
+    Kdim = min(Kdim, kbeg + kc);
+  }
   float* Y = reinterpret_cast<float*>(tb.ws) + Bd.y_off;
   float* W = reinterpret_cast<float*>(tb.ws) + Bd.w_off;
   const float* Vsrc = first ? Bd.Vin : Bd.Vout;
@@ -1154,7 +1163,7 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int64_t k0 = 0; k0 < Kdim; k0 += 16) {
+  for (int64_t k0 = kbeg; k0 < Kdim; k0 += 16) {
     for (int e = tid; e < 1024; e += kThreads) {
       int mm, kk;
       if (MODE == 0) { mm = e >> 4; kk = e & 15; } else { kk = e >> 6; mm = e & 63; }
@@ -1186,7 +1195,7 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
     }
     __syncthreads();
   }
-  float* C = (MODE == 0) ? Y : W;
+  float* C = (MODE == 0) ? (split ? reinterpret_cast<float*>(tb.ws) + Bd.ypart_off + blockIdx.y * Bd.T * R : Y) : W;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -1195,6 +1204,27 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
       const int n = n0 + tj * 4 + j;
       if (m < Mdim && n < R) C[m * R + n] = acc[i][j];
     }
+}
+
+// Y = sum of the split-K partials of every basis, in slot order (grid-stride over all
+// bases' T x R elements; each basis's elements are a contiguous run of the launch).
+__global__ void __launch_bounds__(kThreads) k_pi_ysum(Tables tb, int64_t total) {
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * kThreads) {
+    int b = 0;
+    int64_t base = 0;
+    for (; b < tb.nbases; ++b) {              // a handful of bases on this path
+      const int64_t n = tb.bases[b].T * tb.bases[b].R;
+      if (e < base + n) break;
+      base += n;
+    }
+    const BasisD& B = tb.bases[b];
+    const int64_t li = e - base, n = B.T * B.R;
+    const float* part = reinterpret_cast<const float*>(tb.ws) + B.ypart_off + li;
+    float s = 0.f;
+    for (int k = 0; k < tb.ysplit; ++k) s += part[k * n];
+    reinterpret_cast<float*>(tb.ws)[B.y_off + li] = s;
+  }
 }
 
 // pos = base + z, neg = base - z (ds_mezo/kernels.py:399-412).

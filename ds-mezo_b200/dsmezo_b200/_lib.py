@@ -70,6 +70,7 @@ PI_BASIS_UNCHANGED = 1        # dsmz_step_power_iteration_ex flag (include/dsmez
 
 PLAN_SIMT_POWER_ITER = 1
 PLAN_SINGLE_PASS_POWER_ITER = 2
+PLAN_TENSOR_CORE_PERTURB = 4
 
 
 # name -> (restype, argtypes); mirrors include/dsmezo.h
@@ -113,8 +114,11 @@ SIGNATURES = {
     "dsmz_plan_uses_tensor_cores": (c_int32, [c_void_p]),
     "dsmz_plan_directions": (c_int32, [c_void_p]),
     "dsmz_plan_factor_norms": (c_int32, [c_void_p, c_void_p, c_void_p]),
+    "dsmz_step_draw": (c_int32, [c_void_p, c_uint64, c_uint64, c_void_p]),
+    "dsmz_plan_perturb_on_tensor_cores": (c_int32, [c_void_p]),
     "dsmz_plan_calibration_workspace_bytes": (c_size_t, [c_void_p]),
     "dsmz_plan_calibration_rng_increment": (c_uint64, [c_void_p]),
+    "dsmz_plan_calibration_launch_count": (c_int32, [c_void_p, c_int32]),
     "dsmz_plan_calibrate": (c_int32, [c_void_p, c_uint64, c_uint64, c_int32, c_float, c_void_p, c_size_t,
                                       c_void_p, c_void_p]),
     "dsmz_step_update_directions": (c_int32, [c_void_p, POINTER(c_float), c_int32, c_float, c_float, c_float,

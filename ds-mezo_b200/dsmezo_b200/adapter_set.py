@@ -102,7 +102,7 @@ class AdapterSet:
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
                  rng_direction_stride: int = 0, single_pass_power_iter: bool = False,
-                 module_rng_offsets: Optional[Sequence[int]] = None):
+                 module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = False):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -152,7 +152,8 @@ class AdapterSet:
         self.V_arena = torch.zeros(max(nv, 1), dtype=torch.float32, device=dev)
         self.layout = layout if layout is not None else device_layout(dev)
         self._flags = (0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER) | \
-            (_lib.PLAN_SINGLE_PASS_POWER_ITER if single_pass_power_iter else 0)
+            (_lib.PLAN_SINGLE_PASS_POWER_ITER if single_pass_power_iter else 0) | \
+            (_lib.PLAN_TENSOR_CORE_PERTURB if tensor_core_perturb else 0)
         self._module_offsets = None if module_rng_offsets is None else [int(x) for x in module_rng_offsets]
         if self._module_offsets is not None and len(self._module_offsets) != len(self.modules):
             raise ValueError("module_rng_offsets needs one offset per module")
@@ -354,7 +355,7 @@ class AdapterSet:
         (default: the generator's current offset); `advance`: how far to move the generator
         afterwards (default: this set's draws). Returns the Ritz singular values
         (num_bases x basis_width) when asked."""
-        from .calibration import calibration_launches, generator_of
+        from .calibration import generator_of
         L = lib()
         gen = generator_of(self.device, generator)
         seed = gen.initial_seed()
@@ -370,10 +371,21 @@ class AdapterSet:
                                     self._stream()), "calibration")
         ws.record_stream(torch.cuda.current_stream(self.device))
         gen.set_offset(start + (inc if advance is None else int(advance)))
-        if self.bases:
-            self.launches += calibration_launches(int(niter), self.uses_tensor_cores)
+        self.launches += int(L.dsmz_plan_calibration_launch_count(self._plan, int(niter)))
         self._v_version = None
         return sv
+
+    @property
+    def perturb_uses_tensor_cores(self) -> bool:
+        return bool(lib().dsmz_plan_perturb_on_tensor_cores(self._plan))
+
+    def calibration_launch_count(self, niter: int = 3) -> int:
+        return int(lib().dsmz_plan_calibration_launch_count(self._plan, int(niter)))
+
+    def draw(self, seed: int, offset: int):
+        """Issue the perturbation's Zc_A draws ahead, on the current stream (dsmz_step_draw);
+        the next perturb with the same seed and offset uses them."""
+        check(lib().dsmz_step_draw(self._plan, int(seed) & (2 ** 64 - 1), int(offset), self._stream()), "draws")
 
     def perturb(self, seed: int, offset: int, eps: float, beta: float, q: float, norm_floor: float = FLT_MIN):
         check(lib().dsmz_step_perturb(self._plan, int(seed) & (2 ** 64 - 1), int(offset), float(eps), float(beta),
@@ -500,8 +512,10 @@ class ZOController:
 
     def __init__(self, aset: AdapterSet, eps: float, total_steps: int, generator: torch.Generator,
                  power_iters: int = 3, schedule="cubic", process_group=None, rng_increment_total: Optional[int] = None,
-                 norm_floor: float = FLT_MIN):
+                 norm_floor: float = FLT_MIN, overlap_draws: bool = True):
         self.aset = aset
+        self.overlap_draws = bool(overlap_draws)   # Zc_A draws on a side stream beside the power iteration
+        self._side = None
         self.eps = float(eps)
         self.total_steps = int(total_steps)
         self.gen = generator
@@ -540,7 +554,19 @@ class ZOController:
         seed = self.gen.initial_seed()
         off = self.gen.get_offset()
         self.gen.set_offset(off + self.rng_increment_total)
-        self.aset.power_iteration(self.power_iters, self.norm_floor)
+        if self.overlap_draws and self.aset.modules and self.aset.bases:
+            # the Zc_A draws depend on nothing the step computes: they run on a side stream
+            # beside the (memory-bound) power iteration
+            main = torch.cuda.current_stream(self.aset.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=self.aset.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                self.aset.draw(seed, off)
+            self.aset.power_iteration(self.power_iters, self.norm_floor)
+            main.wait_stream(self._side)
+        else:
+            self.aset.power_iteration(self.power_iters, self.norm_floor)
         self.aset.perturb(seed, off, self.eps, self.beta, self.q, self.norm_floor)
         if self.pg is not None:
             from .sharding import allreduce_sums

@@ -116,17 +116,6 @@ def basis_draw_increments(bases: Sequence, width: int, sm_count: int, max_thread
             for b in bases]
 
 
-def calibration_launches(niter: int, tensor_cores: bool) -> int:
-    """Launches of one dsmz_plan_calibrate: the two sketches, the first Y product (with the
-    bf16 split on the tensor-core path), niter iterations with the W tail of the first, the
-    Ritz stages (Gram of Y, W tail and eigen-solve; Y, Gram of Y and eigen-solve) and the
-    rotation."""
-    n = 3 + (1 if tensor_cores else 0)
-    if niter >= 1:
-        n += 4 + 5 * (niter - 1) + 1
-    return n + 1 + 4 + 1 + 1 + 1 + 1 + 1
-
-
 def generator_of(device: torch.device, generator: Optional[torch.Generator]) -> torch.Generator:
     """The generator svd_lowrank would draw from: the device's default CUDA generator unless
     one is given."""

@@ -337,7 +337,8 @@ class ShardedStep:
     def __init__(self, layers: int, hidden: int, inter: int, kv: int, rank_r: int, tokens: int, *,
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
-                 directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0):
+                 directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0,
+                 tensor_core_perturb: bool = False):
         import torch.distributed as dist
         self.pg = process_group
         self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None
@@ -352,7 +353,8 @@ class ShardedStep:
         self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
                                device=device, module_rng_offsets=self.layout.module_offsets(self.rank),
                                layout=layout, capacity=self.layout.capacity, directions=directions,
-                               rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter)
+                               rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter,
+                               tensor_core_perturb=tensor_core_perturb)
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=None, rng_increment_total=stride * directions)
         cap = self.layout.capacity

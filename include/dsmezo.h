@@ -235,6 +235,14 @@ typedef struct dsmz_plan_desc {
  * activation from HBM; at the 7B shapes that is the faster of the two (the single pass is
  * bound by its split-K reductions and loses about half of its L2 re-reads). */
 #define DSMZ_PLAN_SINGLE_PASS_POWER_ITER 2u
+/* Perturbation on the tensor cores (opt-in): z^T / eps = X C^T per 128-vector tile on
+ * tcgen05 (kind::tf32 with both operands split into tf32 pairs, fp32 accumulation in TMEM),
+ * the epilogue streaming each vector's master, momentum and variance from global memory.
+ * Needs r <= 64, a basis width <= 64, unit component strides and 16-byte rows of tall
+ * matrices. Without the flag the row products run on the CUDA cores inside the streaming
+ * kernel, which stages the tile's arrays with bulk copies; at the 7B shapes that is the
+ * faster of the two (the tensor-core kernel's epilogue is bound by its global-load latency). */
+#define DSMZ_PLAN_TENSOR_CORE_PERTURB 4u
 
 typedef struct dsmz_plan dsmz_plan;
 
@@ -254,6 +262,8 @@ int dsmz_plan_bind(dsmz_plan* plan, void* device_tables, size_t table_bytes,
 /* How the plan runs the power iteration: 0 on CUDA cores, 1 on tcgen05 tensor cores as two
  * products per iteration, 2 on tcgen05 tensor cores in a single pass over the activations. */
 int32_t dsmz_plan_uses_tensor_cores(const dsmz_plan* plan);
+/* 1 when the plan runs the perturbation on the tensor cores. */
+int32_t dsmz_plan_perturb_on_tensor_cores(const dsmz_plan* plan);
 /* Reads and clears the plan's device error word (synchronises the stream): nonzero when a
  * tensor-core kernel gave up on a barrier wait after its time limit. */
 int32_t dsmz_plan_device_error(const dsmz_plan* plan, dsmz_stream_t stream);
@@ -276,6 +286,13 @@ int dsmz_step_power_iteration_ex(const dsmz_plan* plan, int32_t num_iters, float
 int dsmz_step_perturb(const dsmz_plan* plan, uint64_t seed, uint64_t offset, float eps,
                       float beta, float q, float norm_floor, dsmz_stream_t stream);
 double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per direction */
+
+/* The Zc_A draws of direction 0 of the perturbation at (seed, offset)
+ * (ds_mezo/controller.py:187-188), issued ahead: they depend on nothing the step computes,
+ * so a host can run them on a second stream while dsmz_step_power_iteration runs, and make
+ * the perturbation's stream wait for them. The next dsmz_step_perturb with the same seed and
+ * offset then skips its own draw. No reference counterpart (an ordering of the same work). */
+int dsmz_step_draw(const dsmz_plan* plan, uint64_t seed, uint64_t offset, dsmz_stream_t stream);
 int32_t dsmz_plan_directions(const dsmz_plan* plan);
 
 /* Frobenius norms of the plan's fp32 master factors, A then B of each module in module
@@ -299,6 +316,7 @@ int dsmz_plan_factor_norms(const dsmz_plan* plan, float* norms, dsmz_stream_t st
  * work. */
 size_t dsmz_plan_calibration_workspace_bytes(const dsmz_plan* plan);
 uint64_t dsmz_plan_calibration_rng_increment(const dsmz_plan* plan);
+int32_t dsmz_plan_calibration_launch_count(const dsmz_plan* plan, int32_t niter);
 int dsmz_plan_calibrate(const dsmz_plan* plan, uint64_t seed, uint64_t offset, int32_t niter, float norm_floor,
                         void* workspace, size_t workspace_bytes, float* singular_values, dsmz_stream_t stream);
 

@@ -73,6 +73,11 @@ def test_generator_layout(L, n, sm, mt):
     assert L.dsmz_randn_offset_increment(0, sm, mt) == 0
 
 
+def _bases(rank, layers=2, hidden=64, inter=176, kv=16, tokens=48):
+    from dsmezo_b200 import transformer_adapter_shapes
+    return transformer_adapter_shapes(layers, hidden, inter, kv, tokens)[1]
+
+
 def _fake_set(layers=2, hidden=64, inter=176, kv=16, rank=8, tokens=48, bad=None, h_dtype=1):
     from dsmezo_b200 import _lib, transformer_adapter_shapes
     mods, bases = transformer_adapter_shapes(layers, hidden, inter, kv, tokens)
@@ -114,6 +119,14 @@ def test_plan_create_host_only(L, rank, h_dtype, flags, path):
         assert L.dsmz_plan_uses_tensor_cores(h) == path
         per_iter = {0: 5, 1: 5, 2: 4}[path]
         assert L.dsmz_plan_launch_count(h, 3) == 3 * per_iter + (1 if path else 0) + 8
+        # calibration: 2 sketches, niter + 2 Y products, niter + 1 W tails of 4 launches, 2 Grams
+        # of Y, 2 eigen-solves, the rotation, the first bf16 split on the tensor-core path
+        tcs = 1 if path else 0
+        assert L.dsmz_plan_calibration_launch_count(h, 3) == 2 + 5 + 16 + 5 + tcs
+        assert L.dsmz_plan_calibration_launch_count(h, 0) == 2 + 2 + 4 + 5 + tcs
+        assert L.dsmz_plan_calibration_workspace_bytes(h) > 0
+        assert L.dsmz_plan_calibration_rng_increment(h) == sum(
+            int(L.dsmz_randn_offset_increment((b.D if b.T >= b.D else b.T) * rank, 148, 2048)) for b in _bases(rank))
         # stepping an unbound plan is an error, not a launch
         assert L.dsmz_step_update(h, 0.0, 0.0, 0.0, 0.0, 0.0, None, None) == 1
         assert b"not bound" in L.dsmz_last_error()

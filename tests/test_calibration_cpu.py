@@ -85,7 +85,7 @@ def test_oracle_svd_lowrank_matches_torch(T, D, q, niter):
 
 def test_basis_draw_increments_follow_svd_lowrank_shapes():
     from dsmezo_b200 import transformer_adapter_shapes
-    from dsmezo_b200.calibration import basis_draw_increments, calibration_launches
+    from dsmezo_b200.calibration import basis_draw_increments
     from dsmezo_b200._lib import lib
     _, bases = transformer_adapter_shapes(1, 512, 1408, 128, 1024)
     inc = basis_draw_increments(bases, 8, 148, 2048)
@@ -93,8 +93,6 @@ def test_basis_draw_increments_follow_svd_lowrank_shapes():
     want = [int(L.dsmz_randn_offset_increment((b.D if b.T >= b.D else b.T) * 8, 148, 2048)) for b in bases]
     assert inc == want
     assert bases[3].T < bases[3].D and bases[0].T >= bases[0].D
-    assert calibration_launches(3, True) == calibration_launches(3, False) + 1
-    assert calibration_launches(0, False) == 13    # 2 sketches, Y, Ritz stages 6 + 3, rotation
 
 
 def _rank_worker(rank, world, port, results):
