@@ -248,9 +248,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small profiling cases)")
-    ap.add_argument("--perturb", default="cuda-cores", choices=["cuda-cores", "tensor-cores"],
-                    help="row products of the perturbation: inside the streaming kernel (default), or the "
-                         "tcgen05 kernel (rank <= 64)")
+    ap.add_argument("--perturb", default="tensor-cores", choices=["tensor-cores", "cuda-cores"],
+                    help="row products of the perturbation: the tcgen05 kernel (default, rank <= 64), or the "
+                         "CUDA cores inside the streaming kernel")
     ap.add_argument("--power-iter", default="two-pass", choices=["two-pass", "single-pass"],
                     help="tensor-core power iteration: two products per iteration (default), or the single-pass "
                          "kernel that reads each activation from HBM once per iteration")

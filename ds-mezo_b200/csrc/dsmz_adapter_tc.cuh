@@ -7,11 +7,10 @@
 // V^2)). Both are fp32; each is split into a tf32 pair (x = hi + lo, hi = tf32(x), lo
 // exact) and D = X_hi C_hi^T + X_hi C_lo^T + X_lo C_hi^T on tcgen05 (kind::tf32, fp32
 // accumulation in TMEM): the dropped X_lo C_lo^T and lo's own tf32 rounding are below 2^-21
-// of each product term. TMEM lane v holds vector v, so the epilogue thread of vector v
-// reads its r values of z and streams the vector's fp32 master, momentum and variance
-// straight from global memory (a warp covers 32 consecutive vectors: consecutive columns
-// of a wide B, coalesced; rows of a tall A, 16-byte vectors along the row) and writes z,
-// pos, neg and the Kalman partials.
+// of each product term. TMEM lane v holds vector v; the group moves z into shared memory in
+// the matrix's own element order, then streams the tile's fp32 master, momentum and
+// variance from global memory in that order (16-byte units, coalesced) and writes z, pos,
+// neg and the Kalman partials.
 //
 // Warps: 0 TMA producer (one lane); 1 spare; 2-9 two groups of four (one warp per TMEM lane
 // quadrant) that take alternate tiles: wait for the tile, split it (hi in the stage, lo in
@@ -48,7 +47,7 @@ __host__ __device__ inline PLayout perturb_layout(int r, int KW, int budget) {
   L.nbk = (KW + 31) / 32;
   L.npad = (r + 15) & ~15;
   L.stage_bytes = L.nbk * kTile * 128;
-  L.lo_bytes = L.stage_bytes;
+  L.lo_bytes = L.stage_bytes > kTile * L.npad * 4 ? L.stage_bytes : kTile * L.npad * 4;   // lo half, then the z tile
   L.c_bytes = 2 * L.nbk * L.npad * 128;
   const int fixed = kGroups * L.lo_bytes + kGroups * ((L.c_bytes + 1023) & ~1023) + 2048;
   L.S = (budget - fixed) / L.stage_bytes;
@@ -61,7 +60,10 @@ __host__ __device__ inline PLayout perturb_layout(int r, int KW, int budget) {
   L.total = o + 1024;
   return L;
 }
-__host__ __device__ inline bool perturb_ok(int r, int KW) { return r >= 1 && r <= 64 && KW >= 1 && KW <= 64; }
+// r padded to 16, 32 or 64 (the z tile's 16-byte chunks swizzle within groups of eight)
+__host__ __device__ inline bool perturb_ok(int r, int KW) {
+  return r >= 1 && r <= 64 && ((r + 15) & ~15) != 48 && KW >= 1 && KW <= 64;
+}
 
 // the tile's matrix: last m with tt[m] <= t
 __device__ __forceinline__ int tile_owner(const int32_t* tt, int n, int t) {
@@ -156,15 +158,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int
       dead = !sk::agree(kBarGroup0 + grp, 128, w);
       if (dead) break;
       const int mi = tile_owner(ttab, tb.nmats, t);
-      const MatD& M = tb.mats[mi];
-      const ModD& D = tb.mods[M.owner];
-      const int r = static_cast<int>(M.r);
-      const int KW = (M.side == 0) ? D.rca : D.rc;
+      // the matrix's fields in registers (the stores below could alias the tables as far as
+      // the compiler can tell, which would reload them every unit)
+      const MatD& Mg = tb.mats[mi];
+      const int side = Mg.side;
+      const int r = static_cast<int>(Mg.r);
+      const int64_t mnvec = Mg.nvec, ld = Mg.ld;
+      const float* pm = reinterpret_cast<const float*>(Mg.param);   // the fp32 master
+      const float* mup = Mg.mu;
+      const float* vap = Mg.var;
+      float* const zbase = Mg.z;
+      char* const posbase = reinterpret_cast<char*>(Mg.pos);
+      char* const negbase = reinterpret_cast<char*>(Mg.neg);
+      const ModD& D = tb.mods[Mg.owner];
+      const int KW = (side == 0) ? D.rca : D.rc;
       if (mi != cur) {
         // C of this module side (r x KW, row c), split into [C_hi | C_lo]: npad rows each
         const float* coef = reinterpret_cast<const float*>(tb.ws) + D.coef_off;
-        const float* Cm = (M.side == 0) ? coef + static_cast<int64_t>(D.r) * D.rc : coef;
-        const int cld = (M.side == 0) ? D.rca : D.rc;
+        const float* Cm = (side == 0) ? coef + static_cast<int64_t>(D.r) * D.rc : coef;
+        const int cld = (side == 0) ? D.rca : D.rc;
         const int wdt = 32 * L.nbk, half = L.nbk * L.npad * 128;
         for (int e = gt; e < L.npad * wdt; e += 128) {
           const int c = e / wdt, k = e - c * wdt;
@@ -200,45 +212,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int
         }
         tc::mma_commit(mbar + grp);
       }
-      // the vector's master, momentum and variance, 16 components per chunk: each chunk's
-      // loads are issued together one chunk ahead (the first while the MMAs run), so a
-      // thread has up to 96 values in flight
+      // the tile's elements in memory order, four per unit (16 bytes): master, momentum and
+      // variance in, z, pos, neg and the Kalman partials out. kU units per thread per batch;
+      // the first batch's loads are issued while the MMAs run.
       const int64_t s0 = static_cast<int64_t>(t - ttab[mi]) * kTile;
-      const bool live = s0 + v < M.nvec;
-      const int64_t ld = M.ld;
-      const float* pm = reinterpret_cast<const float*>(M.param);   // the fp32 master
-      const float* mup = M.mu;
-      const float* vap = M.var;
-      auto gidx = [&](int c) -> int64_t {
-        return M.side == 0 ? (s0 + v) * ld + c : static_cast<int64_t>(c) * ld + s0 + v;
+      const int nv = static_cast<int>(min(static_cast<int64_t>(kTile), mnvec - s0));
+      const int nch = L.npad / 4, sw = (nch < 8 ? nch : 8) - 1;
+      const int upr = (side == 0) ? nch : kTile / 4;              // units per tile row (a power of 2)
+      const int ush = 31 - __clz(upr);
+      const int nunits = ((side == 0) ? nv : r) * upr;
+      constexpr int kU = 8;
+      float4 P[kU], Mu[kU], W[kU];
+      auto unit = [&](int u, int& row, int& col, int64_t& g) {
+        row = u >> ush;
+        col = u & (upr - 1);
+        g = (side == 0) ? (s0 + row) * ld + 4 * col : static_cast<int64_t>(row) * ld + s0 + 4 * col;
+        return u < nunits && (side == 0 ? 4 * col < r : 4 * col < nv);
       };
-      auto load = [&](int c0, float (&P)[16], float (&Mu)[16], float (&W)[16]) {
-        if (!live) return;
-        if (M.side == 0) {
+      auto load = [&](int u0) {
 #pragma unroll
-          for (int u = 0; u < 16; u += 4) {
-            if (c0 + u >= r) continue;
-            const int64_t g = gidx(c0 + u);
-            const float4 p4 = __ldg(reinterpret_cast<const float4*>(pm + g));
-            const float4 m4 = __ldg(reinterpret_cast<const float4*>(mup + g));
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(vap + g));
-            P[u] = p4.x; P[u + 1] = p4.y; P[u + 2] = p4.z; P[u + 3] = p4.w;
-            Mu[u] = m4.x; Mu[u + 1] = m4.y; Mu[u + 2] = m4.z; Mu[u + 3] = m4.w;
-            W[u] = w4.x; W[u + 1] = w4.y; W[u + 2] = w4.z; W[u + 3] = w4.w;
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            if (c0 + u >= r) continue;
-            const int64_t g = gidx(c0 + u);
-            P[u] = __ldg(pm + g);
-            Mu[u] = __ldg(mup + g);
-            W[u] = __ldg(vap + g);
+        for (int k = 0; k < kU; ++k) {
+          int row, col;
+          int64_t g;
+          if (unit(u0 + k * 128, row, col, g)) {
+            P[k] = __ldg(reinterpret_cast<const float4*>(pm + g));
+            Mu[k] = __ldg(reinterpret_cast<const float4*>(mup + g));
+            W[k] = __ldg(reinterpret_cast<const float4*>(vap + g));
           }
         }
       };
-      float Pc[16], Mc[16], Wc[16];
-      load(0, Pc, Mc, Wc);
+      load(gt);
       pending = true;
       const bool wm = mbar_wait(mbar + grp, mphase & 1u, err);
       dead = !sk::agree(kBarGroup0 + grp, 128, wm);
@@ -248,56 +251,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int
       tc::tc_fence_after();
       __syncwarp();
       if (lane == 0) mbar_arrive(empty + s);             // the MMAs have read the stage
-      // epilogue: vector v of the tile
-      float* zt = M.z + static_cast<int64_t>(tb.dir) * tb.dstride_z;
-      const int64_t fo = static_cast<int64_t>(tb.dir) * tb.dstride_f * FES;
-      char* posb = reinterpret_cast<char*>(M.pos) + fo;
-      char* negb = reinterpret_cast<char*>(M.neg) + fo;
+      // z = eps D into the group's lo buffer (free now) in the matrix's memory order: side 0
+      // row-major [v][c] with 16-byte chunks swizzled by the row, side 1 [c][v]
+      float* zs = reinterpret_cast<float*>(lo);
       const uint32_t trow = acc + (static_cast<uint32_t>(32 * q) << 16);
       for (int c0 = 0; c0 < L.npad; c0 += 16) {
-        float Pn[16], Mn[16], Wn[16];
-        if (c0 + 16 < r) load(c0 + 16, Pn, Mn, Wn);
         float zz[16];
         tc::tmem_ld16(trow + c0, zz);
-        if (live) {
-          if (M.side == 0) {
-            const int64_t g0 = gidx(c0);
+        if (side == 0) {
 #pragma unroll
-            for (int u = 0; u < 16; u += 4) {
-              if (c0 + u >= r) continue;
-              const int64_t g = g0 + u;
-              const float z[4] = {zz[u] * eps, zz[u + 1] * eps, zz[u + 2] * eps, zz[u + 3] * eps};
-              *reinterpret_cast<float4*>(zt + g) = make_float4(z[0], z[1], z[2], z[3]);
-              sk::st_fac4<FES>(posb, g, make_float4(__fadd_rn(Pc[u], z[0]), __fadd_rn(Pc[u + 1], z[1]),
-                                                    __fadd_rn(Pc[u + 2], z[2]), __fadd_rn(Pc[u + 3], z[3])));
-              sk::st_fac4<FES>(negb, g, make_float4(__fsub_rn(Pc[u], z[0]), __fsub_rn(Pc[u + 1], z[1]),
-                                                    __fsub_rn(Pc[u + 2], z[2]), __fsub_rn(Pc[u + 3], z[3])));
+          for (int u = 0; u < 16; u += 4) {
+            const int ch = (c0 + u) >> 2;
+            *reinterpret_cast<float4*>(zs + v * L.npad + 4 * (ch ^ (v & sw))) =
+                make_float4(zz[u] * eps, zz[u + 1] * eps, zz[u + 2] * eps, zz[u + 3] * eps);
+          }
+        } else {
 #pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                const float mu1 = __fmul_rn(Mc[u + qq], kin.beta);
-                const float var1 = __fadd_rn(__fmul_rn(Wc[u + qq], kin.beta2), kin.q);
-                s_zmu = fmaf(z[qq], mu1, s_zmu);
-                s_zzv = fmaf(__fmul_rn(z[qq], z[qq]), var1, s_zzv);
-              }
-            }
-          } else {
+          for (int u = 0; u < 16; ++u) zs[(c0 + u) * kTile + v] = zz[u] * eps;
+        }
+      }
+      tc::tc_fence_before();
+      named_sync(kBarGroup0 + grp, 128);
+      float* zt = zbase + static_cast<int64_t>(tb.dir) * tb.dstride_z;
+      const int64_t fo = static_cast<int64_t>(tb.dir) * tb.dstride_f * FES;
+      char* posb = posbase + fo;
+      char* negb = negbase + fo;
+      for (int u0 = gt; u0 < nunits; u0 += 128 * kU) {
+        if (u0 != gt) load(u0);
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              if (c0 + u >= r) continue;
-              const int64_t g = gidx(c0 + u);
-              const float z = zz[u] * eps;
-              zt[g] = z;
-              sk::st_fac<FES>(posb, g, __fadd_rn(Pc[u], z));
-              sk::st_fac<FES>(negb, g, __fsub_rn(Pc[u], z));
-              const float mu1 = __fmul_rn(Mc[u], kin.beta);
-              const float var1 = __fadd_rn(__fmul_rn(Wc[u], kin.beta2), kin.q);
-              s_zmu = fmaf(z, mu1, s_zmu);
-              s_zzv = fmaf(__fmul_rn(z, z), var1, s_zzv);
-            }
+        for (int k = 0; k < kU; ++k) {
+          int row, col;
+          int64_t g;
+          if (!unit(u0 + k * 128, row, col, g)) continue;
+          const float4 z4 = (side == 0)
+              ? *reinterpret_cast<const float4*>(zs + row * L.npad + 4 * (col ^ (row & sw)))
+              : *reinterpret_cast<const float4*>(zs + row * kTile + 4 * col);
+          *reinterpret_cast<float4*>(zt + g) = z4;
+          sk::st_fac4<FES>(posb, g, make_float4(__fadd_rn(P[k].x, z4.x), __fadd_rn(P[k].y, z4.y),
+                                                __fadd_rn(P[k].z, z4.z), __fadd_rn(P[k].w, z4.w)));
+          sk::st_fac4<FES>(negb, g, make_float4(__fsub_rn(P[k].x, z4.x), __fsub_rn(P[k].y, z4.y),
+                                                __fsub_rn(P[k].z, z4.z), __fsub_rn(P[k].w, z4.w)));
+          const float z[4] = {z4.x, z4.y, z4.z, z4.w};
+          const float mv[4] = {Mu[k].x, Mu[k].y, Mu[k].z, Mu[k].w}, wv[4] = {W[k].x, W[k].y, W[k].z, W[k].w};
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const float mu1 = __fmul_rn(mv[qq], kin.beta);
+            const float var1 = __fadd_rn(__fmul_rn(wv[qq], kin.beta2), kin.q);
+            s_zmu = fmaf(z[qq], mu1, s_zmu);
+            s_zzv = fmaf(__fmul_rn(z[qq], z[qq]), var1, s_zzv);
           }
         }
-#pragma unroll
-        for (int u = 0; u < 16; ++u) { Pc[u] = Pn[u]; Mc[u] = Mn[u]; Wc[u] = Wn[u]; }
       }
       tc::tc_fence_before();
       named_sync(kBarGroup0 + grp, 128);                 // TMEM, lo and C are free again

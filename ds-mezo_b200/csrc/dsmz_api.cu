@@ -782,18 +782,18 @@ bool bind_tc(dsmz_plan* P) {
 // most sk::stream_tv(r)) whose perturbation, Gram and apply layouts all fit with a ring
 // of at least kTeams stages for the team kernels (two for the Gram). One width for all of
 // them: their segments (Kalman and Gram partials) follow the same tile chunks.
-// The tensor-core perturbation's epilogue reads and writes each vector's elements in place:
-// unit component strides, and rows of tall matrices in 16-byte vectors (row length, leading
-// dimension and the arrays' alignment multiples of four elements).
+// The tensor-core perturbation's epilogue moves the tile's elements in 16-byte units: unit
+// component strides, leading dimensions, row lengths (tall matrices) or column counts (wide
+// ones) and the arrays' alignment multiples of four elements.
 bool ptc_strides_ok(const dsmz_plan* P) {
   const int fes = P->copy_dtype == DSMZ_BF16 ? 2 : 4;
   auto al = [](const void* p, int b) { return (reinterpret_cast<uintptr_t>(p) % b) == 0; };
   if ((P->dstride_f % 4) != 0 || (P->dstride_z % 4) != 0) return false;
   for (const MatD& m : P->mats) {
-    if (m.cs != 1) return false;
-    if (m.side == 0 && ((m.ld % 4) != 0 || (m.r % 4) != 0 || !al(m.param, 16) || !al(m.mu, 16) || !al(m.var, 16) ||
-                        !al(m.z, 16) || !al(m.pos, 4 * fes) || !al(m.neg, 4 * fes)))
+    if (m.cs != 1 || (m.ld % 4) != 0 || !al(m.param, 16) || !al(m.mu, 16) || !al(m.var, 16) || !al(m.z, 16) ||
+        !al(m.pos, 4 * fes) || !al(m.neg, 4 * fes))
       return false;
+    if (m.side == 0 ? (m.r % 4) != 0 : (m.nvec % 4) != 0) return false;
   }
   return true;
 }
@@ -1551,7 +1551,7 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
   P->rng_dir_stride = d->rng_direction_stride ? d->rng_direction_stride : P->rng_inc1;
   P->rng_increment = P->rng_inc1 * static_cast<uint64_t>(P->ndir);
   // streaming layouts, then the tile chunks they imply, then the per-segment buffers
-  P->ptc = (d->flags & DSMZ_PLAN_TENSOR_CORE_PERTURB) != 0;
+  P->ptc = (d->flags & DSMZ_PLAN_CUDA_CORE_PERTURB) == 0;
   if (P->r > 0 && !choose_adapter_layouts(P)) {
     delete P;
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_create: rank too large for the streaming kernels' shared memory");

@@ -70,7 +70,7 @@ PI_BASIS_UNCHANGED = 1        # dsmz_step_power_iteration_ex flag (include/dsmez
 
 PLAN_SIMT_POWER_ITER = 1
 PLAN_SINGLE_PASS_POWER_ITER = 2
-PLAN_TENSOR_CORE_PERTURB = 4
+PLAN_CUDA_CORE_PERTURB = 4
 
 
 # name -> (restype, argtypes); mirrors include/dsmezo.h

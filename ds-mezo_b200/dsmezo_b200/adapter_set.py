@@ -102,7 +102,7 @@ class AdapterSet:
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
                  rng_direction_stride: int = 0, single_pass_power_iter: bool = False,
-                 module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = False):
+                 module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = True):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -153,7 +153,7 @@ class AdapterSet:
         self.layout = layout if layout is not None else device_layout(dev)
         self._flags = (0 if tensor_core_power_iter else _lib.PLAN_SIMT_POWER_ITER) | \
             (_lib.PLAN_SINGLE_PASS_POWER_ITER if single_pass_power_iter else 0) | \
-            (_lib.PLAN_TENSOR_CORE_PERTURB if tensor_core_perturb else 0)
+            (0 if tensor_core_perturb else _lib.PLAN_CUDA_CORE_PERTURB)
         self._module_offsets = None if module_rng_offsets is None else [int(x) for x in module_rng_offsets]
         if self._module_offsets is not None and len(self._module_offsets) != len(self.modules):
             raise ValueError("module_rng_offsets needs one offset per module")

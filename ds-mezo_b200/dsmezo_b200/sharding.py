@@ -338,7 +338,7 @@ class ShardedStep:
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
                  directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0,
-                 tensor_core_perturb: bool = False):
+                 tensor_core_perturb: bool = True):
         import torch.distributed as dist
         self.pg = process_group
         self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None

@@ -235,14 +235,13 @@ typedef struct dsmz_plan_desc {
  * activation from HBM; at the 7B shapes that is the faster of the two (the single pass is
  * bound by its split-K reductions and loses about half of its L2 re-reads). */
 #define DSMZ_PLAN_SINGLE_PASS_POWER_ITER 2u
-/* Perturbation on the tensor cores (opt-in): z^T / eps = X C^T per 128-vector tile on
- * tcgen05 (kind::tf32 with both operands split into tf32 pairs, fp32 accumulation in TMEM),
- * the epilogue streaming each vector's master, momentum and variance from global memory.
- * Needs r <= 64, a basis width <= 64, unit component strides and 16-byte rows of tall
- * matrices. Without the flag the row products run on the CUDA cores inside the streaming
- * kernel, which stages the tile's arrays with bulk copies; at the 7B shapes that is the
- * faster of the two (the tensor-core kernel's epilogue is bound by its global-load latency). */
-#define DSMZ_PLAN_TENSOR_CORE_PERTURB 4u
+/* Perturbation's row products on the CUDA cores (fp32 FFMA inside the streaming kernel)
+ * even where the tensor-core kernel applies. The tensor-core kernel (the default) computes
+ * z^T / eps = X C^T per 128-vector tile on tcgen05 (kind::tf32 with both operands split
+ * into tf32 pairs, fp32 accumulation in TMEM) and streams the tile's arrays in 16-byte
+ * units; it needs r <= 64 (padded to 16, 32 or 64), a basis width <= 64 and unit-stride,
+ * 16-byte-aligned arrays. */
+#define DSMZ_PLAN_CUDA_CORE_PERTURB 4u
 
 typedef struct dsmz_plan dsmz_plan;
 

@@ -63,13 +63,17 @@ def _copy_exact(copy, master, z, sign, what):
 
 
 def _run_case(layers, hidden, inter, kv, rank, tokens, seed, copy_dtype, act_dtype, steps=2, total_steps=100,
-              eps=1e-3, schedule="cubic", warm_mu=False, tc=True, extra=1.0, tcp=False):
+              eps=1e-3, schedule="cubic", warm_mu=False, tc=True, extra=1.0, tcp=None):
     from dsmezo_b200 import AdapterSet, ZOController
     mods, bases, A, B, V0, H = make_inputs(layers, hidden, inter, kv, rank, tokens, seed, copy_dtype, act_dtype)
     aset = AdapterSet(mods, bases, rank, rank, copy_dtype=copy_dtype, act_dtype=act_dtype, device=DEV,
-                      keep_ns_output=True, tensor_core_power_iter=tc, tensor_core_perturb=tcp)
-    # the opt-in tensor-core perturbation applies to the ranks of the benchmark sets
-    assert aset.perturb_uses_tensor_cores == (tcp and rank in (8, 16, 64))
+                      keep_ns_output=True, tensor_core_power_iter=tc,
+                      tensor_core_perturb=tc if tcp is None else tcp)
+    # the tensor-core perturbation (the default) applies to the ranks of the benchmark sets;
+    # the CUDA-core variants of the cases run the streaming kernel's row products
+    tcp = tc if tcp is None else tcp
+    if not tcp or rank in (8, 16, 64):
+        assert aset.perturb_uses_tensor_cores == tcp
     tc = aset.uses_tensor_cores
     g = torch.Generator().manual_seed(seed + 1)
     mu0 = [(torch.randn(m.d_out, rank, generator=g), torch.randn(rank, m.d_in, generator=g)) for m in mods] \
@@ -180,10 +184,11 @@ def test_step_rank64_bf16(tc):
 @pytest.mark.parametrize("rank,copy_dtype,act_dtype", [(64, torch.bfloat16, torch.bfloat16),
                                                        (16, torch.bfloat16, torch.bfloat16),
                                                        (8, torch.float32, torch.float32)])
-def test_step_tensor_core_perturbation(rank, copy_dtype, act_dtype):
-    """The opt-in tcgen05 perturbation (tf32-pair products): z, pos/neg and the Kalman sums
-    under the same two-oracle criterion, over two steps."""
-    _run_case(1, 384, 1280, 128, rank, 384, seed=6, copy_dtype=copy_dtype, act_dtype=act_dtype, tcp=True)
+@pytest.mark.parametrize("tcp", [True, False], ids=["tcgen05", "cuda_cores"])
+def test_step_perturbation_paths(rank, copy_dtype, act_dtype, tcp):
+    """Both perturbation kernels (tcgen05 tf32-pair products, CUDA-core FFMA): z, pos/neg and
+    the Kalman sums under the same two-oracle criterion, over two steps."""
+    _run_case(1, 384, 1280, 128, rank, 384, seed=6, copy_dtype=copy_dtype, act_dtype=act_dtype, tcp=tcp)
 
 
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "cuda_cores"])
