@@ -464,9 +464,13 @@ __device__ void cta_chol_rinv8(double* A, double* Ri, int r, double fl) {
     double* AJJ = A + 8 * J * r + 8 * J;
     double* RJJ = Ri + 8 * J * r + 8 * J;
     if (warp == 0) {
+      double idj = 0.0;                              // lane jj keeps 1 / R_jj of this block
       for (int jj = 0; jj < 8; ++jj) {               // the 8 x 8 diagonal block, in place
+        // one reciprocal square root per column (the chain of divisions and square roots is
+        // the serial path of the factorisation): 1/d, d = dd/d and 1/dd = (1/d)^2
         const double dd = fmax(AJJ[jj * r + jj], fl);
-        const double idd = 1.0 / dd, d = sqrt(dd), id = 1.0 / d;
+        const double id = rsqrt(dd), d = dd * id, idd = id * id;
+        if (lane == jj) idj = id;
         int p = lane, a = jj + 1;                    // pair (a, b), jj < a <= b < 8, per lane
         while (a < 8 && p >= 8 - a) { p -= 8 - a; ++a; }
         const int b = a + p;
@@ -480,7 +484,7 @@ __device__ void cta_chol_rinv8(double* A, double* Ri, int r, double fl) {
         __syncwarp();
       }
       for (int i = 7; i >= 0; --i) {                 // its inverse, rows from the bottom
-        const double irii = 1.0 / AJJ[i * r + i];
+        const double irii = __shfl_sync(0xffffffffu, idj, i);
         const int c = lane >> 2, sl = lane & 3;
         double acc = 0.0;
         if (c > i)
@@ -1163,8 +1167,13 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int64_t k0 = kbeg; k0 < Kdim; k0 += 16) {
-    for (int e = tid; e < 1024; e += kThreads) {
+  // the next 16 K-columns' operands are loaded into registers while the current ones are
+  // multiplied from shared memory (four A and four B values per thread)
+  float ra[4], rb[4];
+  auto gload = [&](int64_t k0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = tid + u * kThreads;
       int mm, kk;
       if (MODE == 0) { mm = e >> 4; kk = e & 15; } else { kk = e >> 6; mm = e & 63; }
       const int64_t m = m0 + mm, k = k0 + kk;
@@ -1173,16 +1182,27 @@ __global__ void __launch_bounds__(kThreads) k_pi_gemm(Tables tb, int first) {
         const int64_t ad = (MODE == 0) ? (m * Bd.h_s0 + k * Bd.h_s1) : (k * Bd.h_s0 + m * Bd.h_s1);
         a = ldf(Bd.H, ad, Bd.hdt);
       }
-      As[kk][mm] = a;
+      ra[u] = a;
       const int kb = e >> 6, nn = e & 63;
       const int64_t kg = k0 + kb;
-      float b = 0.f;
+      float bval = 0.f;
       if (kg < Kdim && n0 + nn < R) {
-        b = (MODE == 0) ? Vsrc[kg * vs0 + static_cast<int64_t>(n0 + nn) * vs1] : Y[kg * R + n0 + nn];
+        bval = (MODE == 0) ? Vsrc[kg * vs0 + static_cast<int64_t>(n0 + nn) * vs1] : Y[kg * R + n0 + nn];
       }
-      Bs[kb][nn] = b;
+      rb[u] = bval;
+    }
+  };
+  static_assert(4 * kThreads == 1024, "four operand values per thread per K-step");
+  if (kbeg < Kdim) gload(kbeg);
+  for (int64_t k0 = kbeg; k0 < Kdim; k0 += 16) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = tid + u * kThreads;
+      if (MODE == 0) As[e & 15][e >> 4] = ra[u]; else As[e >> 6][e & 63] = ra[u];
+      Bs[e >> 6][e & 63] = rb[u];
     }
     __syncthreads();
+    if (k0 + 16 < Kdim) gload(k0 + 16);
 #pragma unroll
     for (int kk = 0; kk < 16; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(&As[kk][ti * 4]);
