@@ -65,6 +65,16 @@ __host__ __device__ inline bool perturb_ok(int r, int KW) {
   return r >= 1 && r <= 64 && ((r + 15) & ~15) != 48 && KW >= 1 && KW <= 64;
 }
 
+// Fused +/- all-gather: the byte distances from this rank's +/- gather buffers to each
+// peer's (mapped over NVLink); every +/- store also lands at those distances, so each rank
+// receives every shard while the perturbation runs instead of in an all-gather after it.
+constexpr int kMaxPeers = 7;
+struct GatherPeers {
+  int32_t n;
+  int32_t pad;
+  int64_t dpos[kMaxPeers], dneg[kMaxPeers];
+};
+
 // the tile's matrix: last m with tt[m] <= t
 __device__ __forceinline__ int tile_owner(const int32_t* tt, int n, int t) {
   int lo = 0, hi = n - 1;
@@ -77,7 +87,8 @@ __device__ __forceinline__ int tile_owner(const int32_t* tt, int n, int t) {
 
 template <int FES>
 __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int32_t* __restrict__ ttab, int ntiles,
-                                                            int nsegs, PLayout L, float eps, KalmanIn kin, int* err) {
+                                                            int nsegs, PLayout L, float eps, KalmanIn kin,
+                                                            GatherPeers gp, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = sk::aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
@@ -287,10 +298,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int
               ? *reinterpret_cast<const float4*>(zs + row * L.npad + 4 * (col ^ (row & sw)))
               : *reinterpret_cast<const float4*>(zs + row * kTile + 4 * col);
           *reinterpret_cast<float4*>(zt + g) = z4;
-          sk::st_fac4<FES>(posb, g, make_float4(__fadd_rn(P[k].x, z4.x), __fadd_rn(P[k].y, z4.y),
-                                                __fadd_rn(P[k].z, z4.z), __fadd_rn(P[k].w, z4.w)));
-          sk::st_fac4<FES>(negb, g, make_float4(__fsub_rn(P[k].x, z4.x), __fsub_rn(P[k].y, z4.y),
-                                                __fsub_rn(P[k].z, z4.z), __fsub_rn(P[k].w, z4.w)));
+          const float4 pv = make_float4(__fadd_rn(P[k].x, z4.x), __fadd_rn(P[k].y, z4.y),
+                                        __fadd_rn(P[k].z, z4.z), __fadd_rn(P[k].w, z4.w));
+          const float4 nv4 = make_float4(__fsub_rn(P[k].x, z4.x), __fsub_rn(P[k].y, z4.y),
+                                         __fsub_rn(P[k].z, z4.z), __fsub_rn(P[k].w, z4.w));
+          sk::st_fac4<FES>(posb, g, pv);
+          sk::st_fac4<FES>(negb, g, nv4);
+#pragma unroll
+          for (int pp = 0; pp < kMaxPeers; ++pp) {     // the peers' copies of this shard
+            if (pp >= gp.n) break;
+            sk::st_fac4<FES>(posb + gp.dpos[pp], g, pv);
+            sk::st_fac4<FES>(negb + gp.dneg[pp], g, nv4);
+          }
           const float z[4] = {z4.x, z4.y, z4.z, z4.w};
           const float mv[4] = {Mu[k].x, Mu[k].y, Mu[k].z, Mu[k].w}, wv[4] = {W[k].x, W[k].y, W[k].z, W[k].w};
 #pragma unroll
@@ -328,6 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_perturb_tc(Tables tb, const int
     if (b == 0)
       for (int i = static_cast<int>(G); i < nsegs; ++i) { out[2 * i] = 0.0; out[2 * i + 1] = 0.0; }
   }
+  if (gp.n > 0) __threadfence_system();               // the peer stores precede this rank's next collective
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(static_cast<uint32_t>(ncols))
                  : "memory");

@@ -334,6 +334,7 @@ struct dsmz_plan {
   bool ptc = false;                   // perturbation on the tensor cores (atc::k_perturb_tc)
   atc::PLayout Lpt{};                 // its shared-memory layout
   std::vector<int32_t> ptiles;        // its tiles: first 128-vector tile of each matrix, then the total
+  atc::GatherPeers gpeers{};          // fused +/- all-gather: byte distances to the peers' buffers
   size_t off_ptiles = 0;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
@@ -1184,8 +1185,10 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
       const int32_t* tt = reinterpret_cast<const int32_t*>(P->dev_tables + P->off_ptiles);
       const int nt = P->ptiles.back();
       const int g = std::max(1, std::min(std::min(P->sm_count, P->nsegs), nt));
-      if (bf) atc::k_perturb_tc<2><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin, err);
-      else atc::k_perturb_tc<4><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin, err);
+      if (bf) atc::k_perturb_tc<2><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin,
+                                                                          P->gpeers, err);
+      else atc::k_perturb_tc<4><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin,
+                                                                       P->gpeers, err);
     } else {
       if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
       else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
@@ -1666,6 +1669,63 @@ int dsmz_step_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float 
   if (rc) return rc;
   return run_perturb(P, seed, offset, eps, make_kin(beta, q, 0.f, norm_floor), norm_floor,
                      static_cast<cudaStream_t>(stream));
+}
+
+int dsmz_plan_set_gather_peers(dsmz_plan* P, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta) {
+  if (!P) return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: null plan");
+  if (npeers < 0 || npeers > atc::kMaxPeers || (npeers > 0 && (!pos_delta || !neg_delta)))
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: 0 to " + std::to_string(atc::kMaxPeers) + " peers");
+  if (npeers > 0 && !P->ptc)
+    return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_set_gather_peers: the plan's perturbation is not the tensor-core kernel");
+  for (int i = 0; i < npeers; ++i)
+    if ((pos_delta[i] % 16) != 0 || (neg_delta[i] % 16) != 0)
+      return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: distances must be multiples of 16 bytes");
+  P->gpeers = atc::GatherPeers{};
+  P->gpeers.n = npeers;
+  for (int i = 0; i < npeers; ++i) { P->gpeers.dpos[i] = pos_delta[i]; P->gpeers.dneg[i] = neg_delta[i]; }
+  return DSMZ_OK;
+}
+
+// CUDA IPC of a device buffer: the handle of the allocation that holds `ptr`, and ptr's
+// offset in it; a peer process opens the handle and adds the offset.
+int dsmz_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return fail(DSMZ_ERR_INVALID, "dsmz_ipc_export: null argument");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+      return fail(DSMZ_ERR_CUDA, "dsmz_ipc_export: cuMemGetAddressRange unavailable");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(DSMZ_ERR_CUDA, "dsmz_ipc_export: not a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail("dsmz_ipc_export", e);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return DSMZ_OK;
+}
+
+int dsmz_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  if (!handle || !ptr || offset < 0) return fail(DSMZ_ERR_INVALID, "dsmz_ipc_import: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail("dsmz_ipc_import", e);
+  *ptr = static_cast<char*>(base) + offset;
+  return DSMZ_OK;
+}
+
+int dsmz_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr) return DSMZ_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
+  return e == cudaSuccess ? DSMZ_OK : cuda_fail("dsmz_ipc_close", e);
 }
 
 int dsmz_step_draw(const dsmz_plan* P, uint64_t seed, uint64_t offset, dsmz_stream_t stream) {

@@ -102,7 +102,8 @@ class AdapterSet:
                  keep_ns_output: bool = False, rng_offset_before: int = 0, layout: Optional[tuple] = None,
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
                  rng_direction_stride: int = 0, single_pass_power_iter: bool = False,
-                 module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = True):
+                 module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = True,
+                 pos_buffer: Optional[torch.Tensor] = None, neg_buffer: Optional[torch.Tensor] = None):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -134,8 +135,15 @@ class AdapterSet:
         # the updated factors in the copy dtype, written by every update (none for fp32)
         self.shadow = torch.zeros(cap, dtype=copy_dtype, device=dev) if copy_dtype != torch.float32 else None
         # direction k's +/- copies and z follow direction 0's at a fixed stride
-        self.pos = torch.zeros(K * cap, dtype=copy_dtype, device=dev)
-        self.neg = torch.zeros(K * cap, dtype=copy_dtype, device=dev)
+        # (or the caller's buffers: this rank's slices of the gather buffers of a sharded step)
+        def copies(buf):
+            if buf is None:
+                return torch.zeros(K * cap, dtype=copy_dtype, device=dev)
+            if buf.dtype != copy_dtype or buf.numel() != K * cap or not buf.is_contiguous() or buf.device != dev:
+                raise ValueError("a +/- buffer must be contiguous, of the copy dtype and hold directions x capacity")
+            return buf
+        self.pos = copies(pos_buffer)
+        self.neg = copies(neg_buffer)
         self.mu = torch.zeros(n, dtype=torch.float32, device=dev)
         self.var = torch.zeros(n, dtype=torch.float32, device=dev)
         self.z = torch.zeros(K * n, dtype=torch.float32, device=dev)
@@ -378,6 +386,14 @@ class AdapterSet:
     @property
     def perturb_uses_tensor_cores(self) -> bool:
         return bool(lib().dsmz_plan_perturb_on_tensor_cores(self._plan))
+
+    def set_gather_peers(self, pos_deltas: Sequence[int], neg_deltas: Sequence[int]):
+        """Byte distances from this set's +/- buffers to each peer's mapped buffers: the
+        perturbation stores every +/- element there too (dsmz_plan_set_gather_peers)."""
+        n = len(pos_deltas)
+        pa = (ctypes.c_int64 * max(n, 1))(*[int(x) for x in pos_deltas])
+        na = (ctypes.c_int64 * max(n, 1))(*[int(x) for x in neg_deltas])
+        check(lib().dsmz_plan_set_gather_peers(self._plan, n, pa, na), "gather peers")
 
     def calibration_launch_count(self, niter: int = 3) -> int:
         return int(lib().dsmz_plan_calibration_launch_count(self._plan, int(niter)))

@@ -338,7 +338,7 @@ class ShardedStep:
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
                  directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0,
-                 tensor_core_perturb: bool = True):
+                 tensor_core_perturb: bool = True, fused_gather: bool = True):
         import torch.distributed as dist
         self.pg = process_group
         self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None
@@ -350,17 +350,90 @@ class ShardedStep:
         mods, bases = self.layout.rank_modules[self.rank], self.layout.rank_bases[self.rank]
         # one direction's draws over the whole model: the stride between directions' draws
         stride = self.layout.rng_increment_total
-        self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
-                               device=device, module_rng_offsets=self.layout.module_offsets(self.rank),
-                               layout=layout, capacity=self.layout.capacity, directions=directions,
-                               rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter,
-                               tensor_core_perturb=tensor_core_perturb)
-        self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
-                                process_group=None, rng_increment_total=stride * directions)
         cap = self.layout.capacity
-        self.gathered = {name: torch.empty(cap * self.world * (1 if name == "factors" else directions),
+        self.gathered = {name: torch.zeros(cap * self.world * (1 if name == "factors" else directions),
                                            dtype=copy_dtype, device=device)
                          for name in ("factors", "pos", "neg")} if self.world > 1 else None
+        # on several ranks the +/- copies are written straight into this rank's slice of the
+        # gather buffers (an in-place all-gather, or the peers' stores of the fused one)
+        sl = slice(self.rank * directions * cap, (self.rank + 1) * directions * cap)
+        self.aset = AdapterSet(mods, bases, rank_r, rank_r, copy_dtype=copy_dtype, act_dtype=act_dtype,
+                               device=device, module_rng_offsets=self.layout.module_offsets(self.rank),
+                               layout=layout, capacity=cap, directions=directions,
+                               rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter,
+                               tensor_core_perturb=tensor_core_perturb,
+                               pos_buffer=self.gathered["pos"][sl] if self.world > 1 else None,
+                               neg_buffer=self.gathered["neg"][sl] if self.world > 1 else None)
+        self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
+                                process_group=None, rng_increment_total=stride * directions)
+        self.fused_gather = False
+        self._ipc: List[Tuple[int, int]] = []
+        if fused_gather and self.world > 1 and self.coll.stream_ordered:
+            self._setup_fused_gather()
+
+    def _setup_fused_gather(self) -> None:
+        """Maps every peer's +/- gather buffers into this process (CUDA IPC) and hands the
+        byte distances to the plan, whose tensor-core perturbation then stores each +/-
+        element into every rank's buffer. All ranks turn it on, or none (a rank without the
+        tensor-core perturbation or a failed mapping keeps the NCCL all-gather for all)."""
+        import ctypes
+        import torch.distributed as dist
+        from ._lib import DsmzError, lib
+        L = lib()
+        ok = self.aset.perturb_uses_tensor_cores and bool(self.aset.modules)
+        mine = {}
+        if ok:
+            for name in ("pos", "neg"):
+                h = ctypes.create_string_buffer(64)
+                off = ctypes.c_int64(0)
+                if L.dsmz_ipc_export(self.gathered[name].data_ptr(), h, ctypes.byref(off)) != 0:
+                    ok = False
+                    break
+                mine[name] = (h.raw, off.value)
+        allh = [None] * self.world
+        dist.all_gather_object(allh, (ok, mine), group=self.pg)
+        ok = all(x[0] for x in allh)
+        deltas = {"pos": [], "neg": []}
+        if ok:
+            for p in range(self.world):
+                if p == self.rank:
+                    continue
+                for name in ("pos", "neg"):
+                    h, off = allh[p][1][name]
+                    ptr = ctypes.c_void_p(0)
+                    if L.dsmz_ipc_import(ctypes.create_string_buffer(h, 64), off, ctypes.byref(ptr)) != 0:
+                        ok = False
+                        break
+                    self._ipc.append((ptr.value, off))
+                    deltas[name].append(ptr.value - self.gathered[name].data_ptr())
+                if not ok:
+                    break
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.aset.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
+        if int(flag.item()) == 1:
+            try:
+                self.aset.set_gather_peers(deltas["pos"], deltas["neg"])
+                self.fused_gather = True
+            except DsmzError:
+                self.fused_gather = False
+        flag.fill_(1 if self.fused_gather else 0)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
+        if int(flag.item()) == 0:
+            if self.fused_gather:
+                self.aset.set_gather_peers([], [])
+            self.fused_gather = False
+            self.close()
+        self._barrier = torch.zeros(1, dtype=torch.int32, device=self.aset.device)
+
+    def close(self) -> None:
+        """Unmaps the peers' gather buffers (fused all-gather)."""
+        from ._lib import lib
+        if self.fused_gather:
+            self.aset.set_gather_peers([], [])
+            self.fused_gather = False
+        for ptr, off in self._ipc:
+            lib().dsmz_ipc_close(ptr, off)
+        self._ipc = []
 
     def calibrate(self, generator: Optional[torch.Generator] = None, niter: int = 3):
         """First-step calibration of this rank's bases (AdapterSet.calibrate) with the
@@ -381,6 +454,10 @@ class ShardedStep:
         """Power iteration, perturbation, pos/neg; Kalman sums all-reduced across ranks."""
         if self.coll is not None:
             self.coll.check()                 # a collective of an earlier phase ran out of time
+        if self.fused_gather:
+            # the peers' stores land in every rank's +/- buffers: every rank has finished
+            # reading the previous step's copies (its reads precede this on its stream)
+            self.coll.all_reduce(self._barrier, "+/- buffers barrier")
         self.ctl.perturb()
         if self.world > 1:
             self.coll.all_reduce(self.aset.kalman_sums(), "Kalman sums all-reduce")
@@ -421,6 +498,9 @@ class ShardedStep:
             return {n: self._arena(n) for n in names}
         self.coll.check()
         for n in names:
+            if self.fused_gather and n in ("pos", "neg"):
+                continue                     # the perturbation stored them on every rank; the
+                                             # Kalman all-reduce after it ordered those stores
             self.coll.wait_for(n)            # a buffer still being gathered is not reused
             self.coll.all_gather_into(self.gathered[n], self._arena(n), f"{n} all-gather",
                                       defer="factors" if n == "factors" else None)

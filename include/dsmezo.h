@@ -286,6 +286,25 @@ int dsmz_step_perturb(const dsmz_plan* plan, uint64_t seed, uint64_t offset, flo
                       float beta, float q, float norm_floor, dsmz_stream_t stream);
 double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per direction */
 
+/* Fused +/- all-gather (one process per GPU of one node, no reference counterpart: the
+ * reference has one process). npeers (<= 7) byte distances, multiples of 16, from this
+ * plan's +/- copy buffers to each peer's buffers mapped into this process (dsmz_ipc_*):
+ * every +/- element the perturbation stores is also stored at those distances, so the
+ * peers receive this rank's shard over NVLink while the perturbation runs. The buffers are
+ * this rank's slices of gather buffers laid out the same on every rank. The stores are
+ * complete and visible system-wide when the perturbation kernel has finished: a
+ * stream-ordered collective after it (the Kalman-sum all-reduce) orders every rank's reads
+ * after every rank's stores. Needs the tensor-core perturbation (DSMZ_ERR_UNSUPPORTED
+ * otherwise). npeers 0 turns it off. */
+int dsmz_plan_set_gather_peers(dsmz_plan* plan, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta);
+/* CUDA IPC of a device buffer: export writes the 64-byte handle of the allocation holding
+ * ptr and ptr's offset in it; import (in another process on the same node) maps it and
+ * returns the buffer's address there; close unmaps what import returned. */
+#define DSMZ_IPC_HANDLE_BYTES 64
+int dsmz_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int dsmz_ipc_import(const void* handle, int64_t offset, void** ptr);
+int dsmz_ipc_close(void* ptr, int64_t offset);
+
 /* The Zc_A draws of direction 0 of the perturbation at (seed, offset)
  * (ds_mezo/controller.py:187-188), issued ahead: they depend on nothing the step computes,
  * so a host can run them on a second stream while dsmz_step_power_iteration runs, and make

@@ -100,7 +100,12 @@ def main():
                 err = float((got[k].float() - want[k].float()).abs().max() / want[k].float().abs().max())
                 assert err < 1e-5, (which, k, err)
         print("MULTI_OK", flush=True)
+    # every rank's +/- copies reached every rank through the perturbation's peer stores when
+    # the fused gather is on (NVLink); the comparison above covers either path
+    if rank == 0:
+        print("FUSED_GATHER", st.fused_gather, flush=True)
     dist.barrier(device_ids=[local])
+    st.close()
     dist.destroy_process_group()
 
 

@@ -25,3 +25,5 @@ def test_two_rank_step_matches_one_gpu():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "MULTI_OK" in r.stdout
+    # two GPUs of one node: the +/- copies are gathered by the perturbation's peer stores
+    assert "FUSED_GATHER True" in r.stdout, r.stdout[-2000:]
