@@ -402,13 +402,15 @@ def main():
                    "bytes_received_per_rank": {k: (world - 1) * sstep.layout.capacity * aset.pos.element_size() *
                                                (K if k.startswith("pos") else 1) * (2 if k.startswith("pos") else 1)
                                                for k in g_ms},
-                   "fused_pos_neg": sstep.fused_gather,
+                   "fused_pos_neg": sstep.fused_gather, "fused_factors": sstep.fused_factors,
                    "note": "compute_ms_per_step: the same steps without the all-gathers (Kalman all-reduce and dd "
                            "broadcast kept); allgather_ms: each gather alone; the factors gather overlaps the next "
                            "step's power iteration in the timed steps" +
                            ("; +/- copies: stored into every rank's buffers by the perturbation itself (NVLink "
                             "peer stores), so their gather is part of compute_ms_per_step" if sstep.fused_gather
-                            else "")}
+                            else "") +
+                           ("; factors: the update stores the bf16 shadow into every rank's buffer (NVLink peer "
+                            "stores); their 'gather' is a one-integer barrier" if sstep.fused_factors else "")}
     gather_ms = sum(gathers["allgather_ms"].values()) if gathers else 0.0
     ms = ms_local
     if world > 1:

@@ -65,15 +65,8 @@ __host__ __device__ inline bool perturb_ok(int r, int KW) {
   return r >= 1 && r <= 64 && ((r + 15) & ~15) != 48 && KW >= 1 && KW <= 64;
 }
 
-// Fused +/- all-gather: the byte distances from this rank's +/- gather buffers to each
-// peer's (mapped over NVLink); every +/- store also lands at those distances, so each rank
-// receives every shard while the perturbation runs instead of in an all-gather after it.
-constexpr int kMaxPeers = 7;
-struct GatherPeers {
-  int32_t n;
-  int32_t pad;
-  int64_t dpos[kMaxPeers], dneg[kMaxPeers];
-};
+using dsmz::GatherPeers;
+using dsmz::kMaxPeers;
 
 // the tile's matrix: last m with tt[m] <= t
 __device__ __forceinline__ int tile_owner(const int32_t* tt, int n, int t) {

@@ -334,7 +334,8 @@ struct dsmz_plan {
   bool ptc = false;                   // perturbation on the tensor cores (atc::k_perturb_tc)
   atc::PLayout Lpt{};                 // its shared-memory layout
   std::vector<int32_t> ptiles;        // its tiles: first 128-vector tile of each matrix, then the total
-  atc::GatherPeers gpeers{};          // fused +/- all-gather: byte distances to the peers' buffers
+  GatherPeers gpeers{};               // fused +/- all-gather: byte distances to the peers' buffers
+  GatherPeers speers{};               // fused factor all-gather: distances to the peers' shadows (dpos)
   size_t off_ptiles = 0;
   int r = 0, R = 0, RC = 0;
   int64_t seg_kal_off = 0, kal_sum_off = 0;
@@ -1127,9 +1128,9 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
   if (P->copy_dtype == DSMZ_BF16)
-    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, P->speers, err);
   else
-    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, P->speers, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;
@@ -1227,9 +1228,9 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
   if (P->copy_dtype == DSMZ_BF16)
-    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<2><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, P->speers, err);
   else
-    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, err);
+    sk::k_sapply<4><<<P->grid_m, sk::kSTP, P->La.total, s>>>(tb, tb.mats, nm, P->nsegs, P->La, eta, P->speers, err);
   P->probe_end(DSMZ_KID_APPLY, s);
   DSMZ_LAUNCHED("Kalman + ZO-Muon apply");
   return 0;
@@ -1671,18 +1672,26 @@ int dsmz_step_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float 
                      static_cast<cudaStream_t>(stream));
 }
 
-int dsmz_plan_set_gather_peers(dsmz_plan* P, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta) {
+int dsmz_plan_set_gather_peers(dsmz_plan* P, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta,
+                               const int64_t* shadow_delta) {
   if (!P) return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: null plan");
-  if (npeers < 0 || npeers > atc::kMaxPeers || (npeers > 0 && (!pos_delta || !neg_delta)))
-    return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: 0 to " + std::to_string(atc::kMaxPeers) + " peers");
+  if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && (!pos_delta || !neg_delta)))
+    return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: 0 to " + std::to_string(kMaxPeers) + " peers");
   if (npeers > 0 && !P->ptc)
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_set_gather_peers: the plan's perturbation is not the tensor-core kernel");
+  if (npeers > 0 && shadow_delta && P->copy_dtype == DSMZ_F32)
+    return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_set_gather_peers: fp32 copies have no factor shadow");
   for (int i = 0; i < npeers; ++i)
-    if ((pos_delta[i] % 16) != 0 || (neg_delta[i] % 16) != 0)
+    if ((pos_delta[i] % 16) != 0 || (neg_delta[i] % 16) != 0 || (shadow_delta && (shadow_delta[i] % 16) != 0))
       return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: distances must be multiples of 16 bytes");
-  P->gpeers = atc::GatherPeers{};
+  P->gpeers = GatherPeers{};
+  P->speers = GatherPeers{};
   P->gpeers.n = npeers;
   for (int i = 0; i < npeers; ++i) { P->gpeers.dpos[i] = pos_delta[i]; P->gpeers.dneg[i] = neg_delta[i]; }
+  if (shadow_delta) {
+    P->speers.n = npeers;
+    for (int i = 0; i < npeers; ++i) P->speers.dpos[i] = shadow_delta[i];
+  }
   return DSMZ_OK;
 }
 

@@ -71,6 +71,17 @@ struct BasisD {
   int32_t wtile0, nwtile;     // (D/64) x (R/64) output tiles of W = H^T Y
 };
 
+// Fused all-gathers (one process per GPU of a node): byte distances from this rank's gather
+// buffers (+/- copies, and the factor shadow) to each peer's, mapped over NVLink; a kernel
+// that stores an element of its shard also stores it at those distances, so every rank
+// receives every shard while the kernel runs instead of in an all-gather after it.
+constexpr int kMaxPeers = 7;
+struct GatherPeers {
+  int32_t n;
+  int32_t pad;
+  int64_t dpos[kMaxPeers], dneg[kMaxPeers];
+};
+
 // Everything a launch needs, passed by value.
 struct Tables {
   const MatD* mats; int32_t nmats; int32_t nsegs;      // adapter matrices

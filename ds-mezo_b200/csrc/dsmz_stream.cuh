@@ -928,7 +928,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
 // =====================================================================================
 template <int FES>
 __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
-                                                   Layout L, float eta, int* err) {
+                                                   Layout L, float eta, GatherPeers gp, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
@@ -1020,7 +1020,14 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
               const float4 np = make_float4(__fsub_rn(p4.x, __fmul_rn(eta, X[0])), __fsub_rn(p4.y, __fmul_rn(eta, X[1])),
                                             __fsub_rn(p4.z, __fmul_rn(eta, X[2])), __fsub_rn(p4.w, __fmul_rn(eta, X[3])));
               *reinterpret_cast<float4*>(pt + g) = np;
-              if (sht) st_fac4<FES>(sht, g, np);
+              if (sht) {
+                st_fac4<FES>(sht, g, np);
+#pragma unroll
+                for (int pp = 0; pp < kMaxPeers; ++pp) {   // the peers' copies of the shadow (dpos)
+                  if (pp >= gp.n) break;
+                  st_fac4<FES>(reinterpret_cast<char*>(sht) + gp.dpos[pp], g, np);
+                }
+              }
               if (sct) *reinterpret_cast<float4*>(sct + g) = make_float4(X[0], X[1], X[2], X[3]);
             }
           };
@@ -1033,7 +1040,14 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
               const int g = w.goff(ld, cs);
               const float np = __fsub_rn(p0, __fmul_rn(eta, X));
               pt[g] = np;
-              if (sht) st_fac<FES>(sht, g, np);
+              if (sht) {
+                st_fac<FES>(sht, g, np);
+#pragma unroll
+                for (int pp = 0; pp < kMaxPeers; ++pp) {
+                  if (pp >= gp.n) break;
+                  st_fac<FES>(reinterpret_cast<char*>(sht) + gp.dpos[pp], g, np);
+                }
+              }
               if (sct) sct[g] = X;
             }
           };
@@ -1054,6 +1068,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sapply(Tables tb, const MatD* __res
     } while (adv == 1);
     more = (adv == 2);
   }
+  if (gp.n > 0) __threadfence_system();   // the peer stores precede this rank's next collective
 }
 
 // =====================================================================================

@@ -115,7 +115,7 @@ SIGNATURES = {
     "dsmz_plan_directions": (c_int32, [c_void_p]),
     "dsmz_plan_factor_norms": (c_int32, [c_void_p, c_void_p, c_void_p]),
     "dsmz_step_draw": (c_int32, [c_void_p, c_uint64, c_uint64, c_void_p]),
-    "dsmz_plan_set_gather_peers": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p]),
+    "dsmz_plan_set_gather_peers": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "dsmz_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
     "dsmz_ipc_import": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),
     "dsmz_ipc_close": (c_int32, [c_void_p, c_int64]),

@@ -103,7 +103,8 @@ class AdapterSet:
                  tensor_core_power_iter: bool = True, capacity: int = 0, directions: int = 1,
                  rng_direction_stride: int = 0, single_pass_power_iter: bool = False,
                  module_rng_offsets: Optional[Sequence[int]] = None, tensor_core_perturb: bool = True,
-                 pos_buffer: Optional[torch.Tensor] = None, neg_buffer: Optional[torch.Tensor] = None):
+                 pos_buffer: Optional[torch.Tensor] = None, neg_buffer: Optional[torch.Tensor] = None,
+                 shadow_buffer: Optional[torch.Tensor] = None):
         if copy_dtype not in _DT or act_dtype not in _DT:
             raise ValueError("copy and activation dtypes must be float32 or bfloat16")
         self.device = torch.device(device)
@@ -133,7 +134,12 @@ class AdapterSet:
         K = self.directions
         self.factors = torch.zeros(cap, dtype=torch.float32, device=dev)      # fp32 masters
         # the updated factors in the copy dtype, written by every update (none for fp32)
-        self.shadow = torch.zeros(cap, dtype=copy_dtype, device=dev) if copy_dtype != torch.float32 else None
+        self.shadow = None
+        if copy_dtype != torch.float32:
+            self.shadow = torch.zeros(cap, dtype=copy_dtype, device=dev) if shadow_buffer is None else shadow_buffer
+            if shadow_buffer is not None and (shadow_buffer.dtype != copy_dtype or shadow_buffer.numel() != cap or
+                                              not shadow_buffer.is_contiguous() or shadow_buffer.device != dev):
+                raise ValueError("the shadow buffer must be contiguous, of the copy dtype and hold capacity elements")
         # direction k's +/- copies and z follow direction 0's at a fixed stride
         # (or the caller's buffers: this rank's slices of the gather buffers of a sharded step)
         def copies(buf):
@@ -387,13 +393,16 @@ class AdapterSet:
     def perturb_uses_tensor_cores(self) -> bool:
         return bool(lib().dsmz_plan_perturb_on_tensor_cores(self._plan))
 
-    def set_gather_peers(self, pos_deltas: Sequence[int], neg_deltas: Sequence[int]):
-        """Byte distances from this set's +/- buffers to each peer's mapped buffers: the
-        perturbation stores every +/- element there too (dsmz_plan_set_gather_peers)."""
+    def set_gather_peers(self, pos_deltas: Sequence[int], neg_deltas: Sequence[int],
+                         shadow_deltas: Optional[Sequence[int]] = None):
+        """Byte distances from this set's +/- buffers (and factor shadow) to each peer's
+        mapped buffers: the perturbation (and the update) store every element there too
+        (dsmz_plan_set_gather_peers)."""
         n = len(pos_deltas)
         pa = (ctypes.c_int64 * max(n, 1))(*[int(x) for x in pos_deltas])
         na = (ctypes.c_int64 * max(n, 1))(*[int(x) for x in neg_deltas])
-        check(lib().dsmz_plan_set_gather_peers(self._plan, n, pa, na), "gather peers")
+        sa = (ctypes.c_int64 * max(n, 1))(*[int(x) for x in shadow_deltas]) if shadow_deltas else None
+        check(lib().dsmz_plan_set_gather_peers(self._plan, n, pa, na, sa), "gather peers")
 
     def calibration_launch_count(self, niter: int = 3) -> int:
         return int(lib().dsmz_plan_calibration_launch_count(self._plan, int(niter)))

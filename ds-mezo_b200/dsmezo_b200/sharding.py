@@ -363,10 +363,13 @@ class ShardedStep:
                                rng_direction_stride=stride, single_pass_power_iter=single_pass_power_iter,
                                tensor_core_perturb=tensor_core_perturb,
                                pos_buffer=self.gathered["pos"][sl] if self.world > 1 else None,
-                               neg_buffer=self.gathered["neg"][sl] if self.world > 1 else None)
+                               neg_buffer=self.gathered["neg"][sl] if self.world > 1 else None,
+                               shadow_buffer=(self.gathered["factors"][self.rank * cap:(self.rank + 1) * cap]
+                                              if self.world > 1 and copy_dtype != torch.float32 else None))
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=None, rng_increment_total=stride * directions)
         self.fused_gather = False
+        self.fused_factors = False
         self._ipc: List[Tuple[int, int]] = []
         if fused_gather and self.world > 1 and self.coll.stream_ordered:
             self._setup_fused_gather()
@@ -381,9 +384,10 @@ class ShardedStep:
         from ._lib import DsmzError, lib
         L = lib()
         ok = self.aset.perturb_uses_tensor_cores and bool(self.aset.modules)
+        names = ("pos", "neg", "factors") if self.aset.shadow is not None else ("pos", "neg")
         mine = {}
         if ok:
-            for name in ("pos", "neg"):
+            for name in names:
                 h = ctypes.create_string_buffer(64)
                 off = ctypes.c_int64(0)
                 if L.dsmz_ipc_export(self.gathered[name].data_ptr(), h, ctypes.byref(off)) != 0:
@@ -393,12 +397,14 @@ class ShardedStep:
         allh = [None] * self.world
         dist.all_gather_object(allh, (ok, mine), group=self.pg)
         ok = all(x[0] for x in allh)
-        deltas = {"pos": [], "neg": []}
+        deltas = {n: [] for n in names}
+        if ok and any(set(x[1].keys()) != set(names) for x in allh):
+            ok = False                        # every rank fuses the same gathers
         if ok:
             for p in range(self.world):
                 if p == self.rank:
                     continue
-                for name in ("pos", "neg"):
+                for name in names:
                     h, off = allh[p][1][name]
                     ptr = ctypes.c_void_p(0)
                     if L.dsmz_ipc_import(ctypes.create_string_buffer(h, 64), off, ctypes.byref(ptr)) != 0:
@@ -412,8 +418,9 @@ class ShardedStep:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
         if int(flag.item()) == 1:
             try:
-                self.aset.set_gather_peers(deltas["pos"], deltas["neg"])
+                self.aset.set_gather_peers(deltas["pos"], deltas["neg"], deltas.get("factors"))
                 self.fused_gather = True
+                self.fused_factors = "factors" in deltas
             except DsmzError:
                 self.fused_gather = False
         flag.fill_(1 if self.fused_gather else 0)
@@ -422,6 +429,7 @@ class ShardedStep:
             if self.fused_gather:
                 self.aset.set_gather_peers([], [])
             self.fused_gather = False
+            self.fused_factors = False
             self.close()
         self._barrier = torch.zeros(1, dtype=torch.int32, device=self.aset.device)
 
@@ -431,6 +439,7 @@ class ShardedStep:
         if self.fused_gather:
             self.aset.set_gather_peers([], [])
             self.fused_gather = False
+            self.fused_factors = False
         for ptr, off in self._ipc:
             lib().dsmz_ipc_close(ptr, off)
         self._ipc = []
@@ -501,6 +510,11 @@ class ShardedStep:
             if self.fused_gather and n in ("pos", "neg"):
                 continue                     # the perturbation stored them on every rank; the
                                              # Kalman all-reduce after it ordered those stores
+            if self.fused_factors and n == "factors":
+                # the update stored the shadow on every rank: a stream-ordered barrier orders
+                # every rank's reads after every rank's stores
+                self.coll.all_reduce(self._barrier, "factor buffers barrier")
+                continue
             self.coll.wait_for(n)            # a buffer still being gathered is not reused
             self.coll.all_gather_into(self.gathered[n], self._arena(n), f"{n} all-gather",
                                       defer="factors" if n == "factors" else None)

@@ -295,8 +295,11 @@ double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per directi
  * complete and visible system-wide when the perturbation kernel has finished: a
  * stream-ordered collective after it (the Kalman-sum all-reduce) orders every rank's reads
  * after every rank's stores. Needs the tensor-core perturbation (DSMZ_ERR_UNSUPPORTED
- * otherwise). npeers 0 turns it off. */
-int dsmz_plan_set_gather_peers(dsmz_plan* plan, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta);
+ * otherwise). shadow_delta (or NULL): the same for the bf16 factor shadow the update writes
+ * (the factor all-gather; a stream-ordered collective after the update orders it). npeers 0
+ * turns both off. */
+int dsmz_plan_set_gather_peers(dsmz_plan* plan, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta,
+                               const int64_t* shadow_delta);
 /* CUDA IPC of a device buffer: export writes the 64-byte handle of the allocation holding
  * ptr and ptr's offset in it; import (in another process on the same node) maps it and
  * returns the buffer's address there; close unmaps what import returned. */

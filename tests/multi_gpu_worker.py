@@ -103,7 +103,7 @@ def main():
     # every rank's +/- copies reached every rank through the perturbation's peer stores when
     # the fused gather is on (NVLink); the comparison above covers either path
     if rank == 0:
-        print("FUSED_GATHER", st.fused_gather, flush=True)
+        print("FUSED_GATHER", st.fused_gather, st.fused_factors, flush=True)
     dist.barrier(device_ids=[local])
     st.close()
     dist.destroy_process_group()

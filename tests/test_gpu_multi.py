@@ -26,4 +26,4 @@ def test_two_rank_step_matches_one_gpu():
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "MULTI_OK" in r.stdout
     # two GPUs of one node: the +/- copies are gathered by the perturbation's peer stores
-    assert "FUSED_GATHER True" in r.stdout, r.stdout[-2000:]
+    assert "FUSED_GATHER True True" in r.stdout, r.stdout[-2000:]
