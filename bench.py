@@ -254,6 +254,9 @@ def main():
     ap.add_argument("--power-iter", default="two-pass", choices=["two-pass", "single-pass"],
                     help="tensor-core power iteration: two products per iteration (default), or the single-pass "
                          "kernel that reads each activation from HBM once per iteration")
+    ap.add_argument("--factor-gather", default="copy-engine", choices=["copy-engine", "fused", "nccl"],
+                    help="N > 1: how the updated factors reach every rank: one copy-engine copy per peer beside "
+                         "the next power iteration (default), peer stores inside the update kernel, or NCCL")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.layers > 0:
@@ -283,7 +286,7 @@ def main():
                         total_steps=TOTAL_STEPS, generator=gen, copy_dtype=DT[cfg["fdt"]], act_dtype=DT[cfg["adt"]],
                         schedule=cfg["schedule"], device=device, process_group=pg, directions=K,
                         single_pass_power_iter=args.power_iter == "single-pass",
-                        tensor_core_perturb=args.perturb == "tensor-cores")
+                        tensor_core_perturb=args.perturb == "tensor-cores", factor_gather=args.factor_gather)
     aset = sstep.aset
     init_set(aset, cfg, device, sstep.layout.ranges[rank].start)
     dd_gen = torch.Generator().manual_seed(cfg["seed"])
@@ -402,7 +405,7 @@ def main():
                    "bytes_received_per_rank": {k: (world - 1) * sstep.layout.capacity * aset.pos.element_size() *
                                                (K if k.startswith("pos") else 1) * (2 if k.startswith("pos") else 1)
                                                for k in g_ms},
-                   "fused_pos_neg": sstep.fused_gather, "fused_factors": sstep.fused_factors,
+                   "fused_pos_neg": sstep.fused_gather, "factor_gather": sstep.factor_gather,
                    "note": "compute_ms_per_step: the same steps without the all-gathers (Kalman all-reduce and dd "
                            "broadcast kept); allgather_ms: each gather alone; the factors gather overlaps the next "
                            "step's power iteration in the timed steps" +
@@ -410,7 +413,11 @@ def main():
                             "peer stores), so their gather is part of compute_ms_per_step" if sstep.fused_gather
                             else "") +
                            ("; factors: the update stores the bf16 shadow into every rank's buffer (NVLink peer "
-                            "stores); their 'gather' is a one-integer barrier" if sstep.fused_factors else "")}
+                            "stores); their 'gather' is a one-integer barrier" if sstep.factor_gather == "fused"
+                            else "") +
+                           ("; factors: a barrier, then one copy-engine copy per peer of this rank's shadow on its "
+                            "own stream, beside the next step's power iteration; the timed run ends with a barrier "
+                            "after the last copies" if sstep.factor_gather == "copy-engine" else "")}
     gather_ms = sum(gathers["allgather_ms"].values()) if gathers else 0.0
     ms = ms_local
     if world > 1:
@@ -642,7 +649,8 @@ def main():
         "dtype": cfg["fdt"] if cfg["fdt"] == "bf16" else "f32", "data": "synthetic (seeded N(0,1) factors and "
         "momentum, lognormal-scaled N(0,1) activations)",
         "config": dict(config_of(cfg, world, sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9),
-                       power_iteration=args.power_iter, perturbation=args.perturb),
+                       power_iteration=args.power_iter, perturbation=args.perturb,
+                       factor_gather=args.factor_gather if world > 1 else None),
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1),

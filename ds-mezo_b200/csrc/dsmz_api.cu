@@ -79,10 +79,14 @@ size_t perturb_smem(int r, int R, int RC) {
          sizeof(float);
 }
 size_t coef_smem(int R, int RC) {
-  const size_t rca = static_cast<size_t>(R < RC ? R : RC);
-  return (static_cast<size_t>(R + 4) * RC + (rca <= 64 ? 2 * rca * rca : 0)) * sizeof(double);
+  const int rca = R < RC ? R : RC;
+  return (static_cast<size_t>(R + 4) * RC +
+          (coef_qr_in_smem(R, rca) ? 2 * static_cast<size_t>(rca) * rca : 0)) * sizeof(double);
 }
-size_t ns_smem(int r) { return r <= 64 ? 3 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double) : 0; }
+size_t ns_smem(int r) {
+  return r <= 64 ? 3 * static_cast<size_t>(pad8(r)) * ns_ld(r) * sizeof(double)
+                 : 3 * static_cast<size_t>(ns_packed_blocks(r)) * 64 * sizeof(double);
+}
 size_t chol_smem(int R) { return R <= 64 ? 2 * static_cast<size_t>(R) * R * sizeof(double) : 0; }
 
 // Dynamic shared memory of a streaming-kernel CTA (one CTA per SM).
@@ -93,6 +97,20 @@ int set_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
     if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+  }
+  return 0;
+}
+
+// Newton-Schulz solve of nm matrices of rank r: r <= 64 two CTAs per SM with the matrices
+// in shared memory; larger r the packed-symmetric kernel (one CTA per SM).
+int launch_ns_solve(const Tables& tb, const MatD* mats, int nm, int r, const NSArgs& ns, cudaStream_t s) {
+  int rc;
+  if (r <= 64) {
+    if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
+    k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, mats, ns);
+  } else {
+    if ((rc = set_smem(k_ns_solve_packed, ns_smem(r)))) return rc;
+    k_ns_solve_packed<<<nm, kNsPThreads, ns_smem(r), s>>>(tb, mats, ns);
   }
   return 0;
 }
@@ -1111,7 +1129,6 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
-  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
   P->probe_begin(DSMZ_KID_KALMAN_DIRS, s);
   sk::k_kalman_dirs<<<8 * P->sm_count, 256, 0, s>>>(tb, kd, P->Lg.TV);   // plain stream: many CTAs per SM
   P->probe_end(DSMZ_KID_KALMAN_DIRS, s);
@@ -1123,7 +1140,7 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Gram of the updated momentum");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
-  k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, tb.mats, ns);
+  if ((rc = launch_ns_solve(tb, tb.mats, nm, r, ns, s))) return rc;
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
@@ -1191,8 +1208,8 @@ int run_perturb(const dsmz_plan* P, uint64_t seed, uint64_t offset, float eps, K
       else atc::k_perturb_tc<4><<<g, atc::kThreads, P->Lpt.total, s>>>(td, tt, nt, P->nsegs, P->Lpt, eps, kin,
                                                                        P->gpeers, err);
     } else {
-      if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
-      else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, err);
+      if (bf) sk::k_sperturb<2><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, P->gpeers, err);
+      else sk::k_sperturb<4><<<P->grid_m, sk::kSTP, P->Lp.total, s>>>(td, P->Lp, seed, off, eps, kin, P->gpeers, err);
     }
     P->probe_end(DSMZ_KID_PERTURB, s);
     DSMZ_LAUNCHED("perturbation");
@@ -1222,8 +1239,7 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");
   P->probe_begin(DSMZ_KID_NS_SOLVE, s);
-  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
-  k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, tb.mats, ns);
+  if ((rc = launch_ns_solve(tb, tb.mats, nm, r, ns, s))) return rc;
   P->probe_end(DSMZ_KID_NS_SOLVE, s);
   DSMZ_LAUNCHED("Newton-Schulz solve");
   P->probe_begin(DSMZ_KID_APPLY, s);
@@ -1530,6 +1546,8 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     off += incA;
     own += incB + incA;
     md.coef_off = static_cast<int64_t>(P->ws.take((nB + static_cast<size_t>(md.r) * md.rca) * sizeof(float)) / sizeof(float));
+    md.qrw_off = coef_qr_in_smem(md.r, md.rca) ? 0 : static_cast<int64_t>(
+        P->ws.take(2 * static_cast<size_t>(md.rca) * md.rca * sizeof(double)) / sizeof(double));
     md.Bp = m.B; md.varB = m.var_B; md.b_s0 = m.ld_B; md.b_s1 = 1;
     md.zca_off = static_cast<int64_t>(P->ws.take(static_cast<size_t>(nA) * sizeof(float)) / sizeof(float));
     md.dblk0 = P->ndblk;
@@ -1677,8 +1695,6 @@ int dsmz_plan_set_gather_peers(dsmz_plan* P, int32_t npeers, const int64_t* pos_
   if (!P) return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: null plan");
   if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && (!pos_delta || !neg_delta)))
     return fail(DSMZ_ERR_INVALID, "dsmz_plan_set_gather_peers: 0 to " + std::to_string(kMaxPeers) + " peers");
-  if (npeers > 0 && !P->ptc)
-    return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_set_gather_peers: the plan's perturbation is not the tensor-core kernel");
   if (npeers > 0 && shadow_delta && P->copy_dtype == DSMZ_F32)
     return fail(DSMZ_ERR_UNSUPPORTED, "dsmz_plan_set_gather_peers: fp32 copies have no factor shadow");
   for (int i = 0; i < npeers; ++i)
@@ -1735,6 +1751,16 @@ int dsmz_ipc_close(void* ptr, int64_t offset) {
   if (!ptr) return DSMZ_OK;
   cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
   return e == cudaSuccess ? DSMZ_OK : cuda_fail("dsmz_ipc_close", e);
+}
+
+// One device-to-device copy on `stream` (a copy engine moves it; between this GPU's memory
+// and a peer's mapped buffer it crosses NVLink without taking an SM).
+int dsmz_peer_copy(void* dst, const void* src, int64_t bytes, dsmz_stream_t stream) {
+  if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(DSMZ_ERR_INVALID, "dsmz_peer_copy: bad argument");
+  if (bytes == 0) return DSMZ_OK;
+  cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice,
+                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? DSMZ_OK : cuda_fail("dsmz_peer_copy", e);
 }
 
 int dsmz_step_draw(const dsmz_plan* P, uint64_t seed, uint64_t offset, dsmz_stream_t stream) {
@@ -1927,8 +1953,7 @@ int dsmz_zo_muon_update(int32_t param_dtype, void* param, int64_t ps0, int64_t p
     k_gram<0, 8, double><<<P.nsegs, kThreads, gs, s>>>(tb, tb.mats, 1, kin);
   }
   DSMZ_LAUNCHED("zo_muon_update Gram");
-  if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
-  k_ns_solve<<<1, kThreads, ns_smem(r), s>>>(tb, tb.mats, make_ns(schedule, norm_floor));
+  if ((rc = launch_ns_solve(tb, tb.mats, 1, r, make_ns(schedule, norm_floor), s))) return rc;
   DSMZ_LAUNCHED("zo_muon_update solve");
   if ((rc = set_smem(k_apply<0, 0>, as))) return rc;
   k_apply<0, 0><<<P.nsegs, kThreads, as, s>>>(tb, tb.mats, 1, kin, eta, param_dtype);
@@ -2022,6 +2047,8 @@ static dsmz_plan agzo_plan(int64_t R, int64_t d_in, int64_t RC, int64_t d_out) {
   md.d_out = d_out; md.d_in = d_in; md.basis = 0;
   const size_t nB = static_cast<size_t>(R) * RC;
   md.coef_off = static_cast<int64_t>(P.ws.take((nB + static_cast<size_t>(R) * rca) * sizeof(float)) / sizeof(float));
+  md.qrw_off = coef_qr_in_smem(md.r, rca) ? 0 : static_cast<int64_t>(
+      P.ws.take(2 * static_cast<size_t>(rca) * rca * sizeof(double)) / sizeof(double));
   md.a = 0; md.b = 1;
   P.mods.push_back(md);
   // one CTA per 2048 columns (the device is not known yet)

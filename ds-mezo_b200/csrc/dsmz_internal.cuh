@@ -58,6 +58,8 @@ struct ModD {
   int64_t b_s0, b_s1;
   int64_t zca_off;            // floats: materialised Zc_A draw (d_out x RCA)
   int32_t dblk0, ndblk;       // blocks of the Zc_A draw kernel (one torch thread each)
+  int64_t qrw_off;            // doubles: G and R^{-1} (rca x rca each) of the QR of B V when they do
+                              // not fit beside it in shared memory (r or rca > 64), else 0
 };
 
 struct BasisD {

@@ -406,6 +406,166 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
   }
 }
 
+// =====================================================================================
+// Newton-Schulz solve for 64 < r <= 128: the same iteration as k_ns_solve with the three
+// matrices in shared memory. They are symmetric, so only their upper 8 x 8 blocks are
+// stored (packed row by row: 136 blocks, 204 KB for r = 128); a block holds all 64 entries,
+// XOR-swizzled (column j of row i at i*8 + (j ^ 4*((i>>1)&1))) so that the MMA fragments of
+// a block or of its transpose are two wavefronts. Sixteen warps, up to nine output blocks
+// each: every product is one pass, held in registers across a barrier and written in place.
+// =====================================================================================
+constexpr int kNsPThreads = 512, kNsPU = 9;
+__host__ __device__ inline int ns_packed_blocks(int r) { const int nb = pad8(r) >> 3; return nb * (nb + 1) / 2; }
+
+// Shared-memory index of element (row, col) of a packed symmetric matrix with nb block rows.
+__device__ __forceinline__ int nsp_idx(int row, int col, int nb) {
+  int bi = row >> 3, bj = col >> 3, i = row & 7, j = col & 7;
+  if (bi > bj) { const int t = bi; bi = bj; bj = t; const int u = i; i = j; j = u; }
+  const int q = bi * nb - ((bi * (bi - 1)) >> 1) + (bj - bi);
+  return q * 64 + i * 8 + (j ^ (((i >> 1) & 1) << 2));
+}
+
+// C = A B (symmetric, commuting, packed); C may be A or B. Per k block kb a warp reads, for
+// each of its output blocks (bi, bj), block (bi, kb) of A and (kb, bj) of B, each stored
+// as itself or as its transpose: in-block offsets dir (row g, column k) and tr (row k,
+// column g) are fixed per thread, so a k step costs a few integer adds per block.
+__device__ __forceinline__ int nsp_row0(int b, int nb) { return b * nb - ((b * (b - 1)) >> 1); }
+__device__ void nsp_mm(double* C, const double* A, const double* B, int nb) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int nw = kNsPThreads / 32;
+  const int nq = nb * (nb + 1) / 2;
+  int bi[kNsPU], bj[kNsPU], rsi[kNsPU], rsj[kNsPU];
+  double acc[kNsPU][2];
+#pragma unroll
+  for (int u = 0; u < kNsPU; ++u) {
+    int q = warp + u * nw;
+    bi[u] = -1; bj[u] = 0;
+    acc[u][0] = 0.0; acc[u][1] = 0.0;
+    if (q < nq) {
+      int row = 0;
+      while (q >= nb - row) { q -= nb - row; ++row; }
+      bi[u] = row; bj[u] = row + q;
+    }
+    rsi[u] = nsp_row0(bi[u] < 0 ? 0 : bi[u], nb);
+    rsj[u] = nsp_row0(bj[u], nb);
+  }
+  int dir[2], tr[2];                                   // k half kh: columns / rows 4kh + t
+#pragma unroll
+  for (int kh = 0; kh < 2; ++kh) {
+    const int k = 4 * kh + t;
+    dir[kh] = g * 8 + (k ^ (((g >> 1) & 1) << 2));
+    tr[kh] = k * 8 + (g ^ (((k >> 1) & 1) << 2));
+  }
+  for (int kb = 0; kb < nb; ++kb) {
+    const int rsk = nsp_row0(kb, nb);
+#pragma unroll
+    for (int u = 0; u < kNsPU; ++u) {
+      if (bi[u] < 0) continue;
+      const bool at = bi[u] <= kb, bt = kb <= bj[u];
+      const double* a = A + 64 * (at ? rsi[u] + kb - bi[u] : rsk + bi[u] - kb);
+      const double* b = B + 64 * (bt ? rsk + bj[u] - kb : rsj[u] + kb - bj[u]);
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh)
+        dmma8x8x4(acc[u][0], acc[u][1], a[at ? dir[kh] : tr[kh]], b[bt ? tr[kh] : dir[kh]]);
+    }
+  }
+  __syncthreads();                                     // every read of A and B is done
+#pragma unroll
+  for (int u = 0; u < kNsPU; ++u) {
+    if (bi[u] < 0) continue;
+    const int row = 8 * bi[u] + g;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int col = 8 * bj[u] + 2 * t + h;
+      if (bi[u] == bj[u] && col < row) continue;          // the mirror of the upper half
+      C[nsp_idx(row, col, nb)] = acc[u][h];
+      if (bi[u] == bj[u] && col != row) C[nsp_idx(col, row, nb)] = acc[u][h];
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ double red[kNsPThreads];
+  const MatD M = mats[blockIdx.x];
+  const int r = static_cast<int>(M.r);
+  const int rr = r * r;
+  const int nb = pad8(r) >> 3, mm = ns_packed_blocks(r) * 64;
+  const int tid = threadIdx.x;
+  double* G = reinterpret_cast<double*>(smem_raw);
+  double* P = G + mm;
+  double* S = P + mm;
+  for (int e = tid; e < 3 * mm; e += kNsPThreads) G[e] = 0.0;   // padding rows and columns stay zero
+  __syncthreads();
+  double tr = 0.0;
+  const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
+  constexpr int kSumU = 4;                             // independent partial loads in flight
+  for (int e0 = tid; e0 < rr; e0 += kSumU * kNsPThreads) {
+    double v[kSumU];
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) v[u] = 0.0;
+    for (int sg = 0; sg < M.nseg; ++sg) {
+#pragma unroll
+      for (int u = 0; u < kSumU; ++u) {
+        const int e = e0 + u * kNsPThreads;
+        if (e < rr) v[u] += part[static_cast<int64_t>(sg) * rr + e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSumU; ++u) {
+      const int e = e0 + u * kNsPThreads;
+      if (e >= rr) continue;
+      const int a = e / r, b = e - a * r;
+      if ((a >> 3) > (b >> 3)) continue;               // the lower blocks are the upper ones
+      G[nsp_idx(a, b, nb)] = v[u];
+      if (a == b) tr += v[u];
+    }
+  }
+  red[tid] = tr;
+  __syncthreads();
+  for (int w = kNsPThreads / 2; w > 0; w >>= 1) {
+    if (tid < w) red[tid] += red[tid + w];
+    __syncthreads();
+  }
+  const double norm_sq = red[0];
+  const double inv = 1.0 / sqrt(fmax(norm_sq, static_cast<double>(ns.norm_floor)));
+  const double inv2 = inv * inv;
+  // every stored element: block q, entry (i, j) -> matrix element (8bi+i, 8bj+j')
+  auto each = [&](auto&& f) {
+    for (int e = tid; e < mm; e += kNsPThreads) {
+      int q = e >> 6, row = 0;
+      while (q >= nb - row) { q -= nb - row; ++row; }
+      const int i = (e >> 3) & 7, js = e & 7;
+      const int a = 8 * row + i, b = 8 * (row + q) + (js ^ (((i >> 1) & 1) << 2));
+      if (a < r && b < r) f(e, a, b);
+    }
+  };
+  each([&](int e, int a, int b) {
+    G[e] *= inv2;
+    P[e] = (a == b) ? 1.0 : 0.0;
+  });
+  __syncthreads();
+  for (int it = 0; it < ns.iters; ++it) {
+    const double c0 = ns.c[it][0], c1 = ns.c[it][1], c2 = ns.c[it][2];
+    if (c2 != 0.0) nsp_mm(S, G, G, nb);
+    each([&](int e, int a, int b) {
+      const double g2 = (c2 != 0.0) ? S[e] : 0.0;
+      S[e] = ((a == b) ? c0 : 0.0) + c1 * G[e] + c2 * g2;
+    });
+    __syncthreads();
+    nsp_mm(P, P, S, nb);                               // P <- P S
+    nsp_mm(G, S, G, nb);                               // G <- S G S
+    nsp_mm(G, G, S, nb);
+  }
+  float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
+  for (int e = tid; e < rr; e += kNsPThreads) {
+    const int a = e / r, b = e - a * r;
+    Pm[e] = static_cast<float>(P[nsp_idx(a, b, nb)] * inv);
+  }
+}
+
 // Cholesky of the r x r symmetric matrix A (row-major, pitch r) in place and the inverse
 // of its upper factor: afterwards A's upper triangle holds R (G = R^T R, pivots
 // sqrt(max(d, fl)), the clamp of the reference MGS norms) and Ri holds R^{-1} (zero below
@@ -843,7 +1003,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_bside(Tables tb, int64_t ncols)
 // (controller.py:183-186), and Q = MGS(B V)[:, :RCA] (ds_mezo/kernels.py:328-340) in fp64
 // by one warp. MODE 0 draws Zc_B from the torch Philox stream, MODE 1 copies it.
 // =====================================================================================
-constexpr int kQBlocks = 8;    // output blocks per warp of the Q update (64 x 64: 64 blocks)
+constexpr int kQBlocks = 8;    // output blocks per warp per pass of the Q update (64 x 64: one pass)
+// The QR of B V keeps G and R^{-1} in shared memory beside B V up to 64 x 64; beyond that
+// they live in the module's fp64 workspace (qrw_off) and B V alone stays on chip.
+__host__ __device__ inline bool coef_qr_in_smem(int R, int RCA) { return RCA <= 64 && R <= 64; }
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uint64_t base_off, float norm_floor,
                                                    int with_qr) {
@@ -877,10 +1040,12 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
   __syncthreads();
   // Q = QR(B V)[:, :RCA] with a positive diagonal, the factor the reference's modified
   // Gram-Schmidt produces (ds_mezo/kernels.py:328-340), as CholeskyQR2 in fp64: two rounds of
-  // G = Q^T Q, G = R^T R, Q <- Q R^{-1}, every step parallel over the CTA.
-  if (RCA <= 64 && R <= 64) {
+  // G = Q^T Q, G = R^T R, Q <- Q R^{-1}, every step parallel over the CTA. Up to 64 x 64 any
+  // shape; beyond, blocks of 8 (G and R^{-1} in the workspace).
+  const bool in_smem = coef_qr_in_smem(R, RCA);
+  if (in_smem || ((R & 7) == 0 && (RCA & 7) == 0)) {
   __shared__ double piv[DSMZ_MAX_RANK];
-  double* G = BVt + RC * bld;                 // RCA x RCA
+  double* G = in_smem ? BVt + RC * bld : reinterpret_cast<double*>(tb.ws) + D.qrw_off;   // RCA x RCA
   double* Rm = G + RCA * RCA;               // inverse of the upper factor
   for (int round = 0; round < 2; ++round) {
     if ((R & 3) == 0 && (RCA & 7) == 0) {
@@ -919,33 +1084,41 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
     __syncthreads();
     if ((RCA & 7) == 0) cta_chol_rinv8(G, Rm, RCA, static_cast<double>(norm_floor));
     else cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
-    if ((R & 7) == 0 && (RCA & 7) == 0 && R <= 64) {
+    if ((R & 7) == 0 && (RCA & 7) == 0) {
       // Q <- Q R^{-1} on the fp64 MMA, as Q^T <- R^{-T} Q^T on BVt (Q^T row-major): output
       // block (column block cb of Q, row block ib of Q) = sum_{a < 8cb+8} R^{-1}[a][8cb+..]
       // Q^T[a][8ib+..] (R^{-1} upper), held in registers across a barrier, then in place.
+      // Passes take column blocks from the last: a pass writes only rows of Q^T that later
+      // passes (lower column blocks) no longer read. 64 x 64 is one pass, 128 x 128 four.
       const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, kq = lane & 3;
-      const int ncb = RCA >> 3, nib = R >> 3, nblk = ncb * nib;
-      double o[kQBlocks][2];
-      int cbq[kQBlocks], ibq[kQBlocks];
+      const int ncb = RCA >> 3, nib = R >> 3;
+      const int cpp = (kQBlocks * (kThreads / 32)) / nib;     // column blocks per pass (>= 4)
+      for (int chi = ncb - 1; chi >= 0; chi -= cpp) {
+        const int clo = chi - cpp + 1 > 0 ? chi - cpp + 1 : 0;
+        const int nblk = (chi - clo + 1) * nib;
+        double o[kQBlocks][2];
+        int cbq[kQBlocks], ibq[kQBlocks];
 #pragma unroll
-      for (int u = 0; u < kQBlocks; ++u) {
-        const int q = warp + u * (kThreads / 32);
-        cbq[u] = q < nblk ? q / nib : -1;
-        ibq[u] = q < nblk ? q - (q / nib) * nib : 0;
-        o[u][0] = 0.0; o[u][1] = 0.0;
-        if (cbq[u] < 0) continue;
-        const double* ra = Rm + kq * RCA + 8 * cbq[u] + g;
-        const double* qb = BVt + kq * bld + 8 * ibq[u] + g;
-        for (int k0 = 0; k0 < 8 * cbq[u] + 8; k0 += 4)
-          dmma8x8x4(o[u][0], o[u][1], ra[k0 * RCA], qb[k0 * bld]);
-      }
-      __syncthreads();
+        for (int u = 0; u < kQBlocks; ++u) {
+          const int q = warp + u * (kThreads / 32);
+          cbq[u] = q < nblk ? clo + q / nib : -1;
+          ibq[u] = q < nblk ? q - (q / nib) * nib : 0;
+          o[u][0] = 0.0; o[u][1] = 0.0;
+          if (cbq[u] < 0) continue;
+          const double* ra = Rm + kq * RCA + 8 * cbq[u] + g;
+          const double* qb = BVt + kq * bld + 8 * ibq[u] + g;
+          for (int k0 = 0; k0 < 8 * cbq[u] + 8; k0 += 4)
+            dmma8x8x4(o[u][0], o[u][1], ra[k0 * RCA], qb[k0 * bld]);
+        }
+        __syncthreads();
 #pragma unroll
-      for (int u = 0; u < kQBlocks; ++u) {
-        if (cbq[u] < 0) continue;
-        double* dst = BVt + (8 * cbq[u] + g) * bld + 8 * ibq[u] + 2 * kq;
-        dst[0] = o[u][0];
-        dst[1] = o[u][1];
+        for (int u = 0; u < kQBlocks; ++u) {
+          if (cbq[u] < 0) continue;
+          double* dst = BVt + (8 * cbq[u] + g) * bld + 8 * ibq[u] + 2 * kq;
+          dst[0] = o[u][0];
+          dst[1] = o[u][1];
+        }
+        __syncthreads();
       }
     } else {
     // Q <- Q R^{-1}: every output (i, c) = sum_{a<=c} Q[i][a] R^{-1}[a][c] held in registers

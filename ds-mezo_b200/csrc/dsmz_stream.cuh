@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(256) k_draw_zca(Tables tb, uint64_t seed, uint
 // =====================================================================================
 template <int FES>
 __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint64_t seed, uint64_t base_off, float eps,
-                                                     KalmanIn kin, int* err) {
+                                                     KalmanIn kin, GatherPeers gp, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
@@ -844,10 +844,18 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
                 const float4 p4 = *reinterpret_cast<const float4*>(ps + so);
                 const float4 m4 = *reinterpret_cast<const float4*>(ms + so);
                 const float4 w4 = *reinterpret_cast<const float4*>(vsg + so);
-                st_fac4<FES>(post, g, make_float4(__fadd_rn(p4.x, z[0]), __fadd_rn(p4.y, z[1]), __fadd_rn(p4.z, z[2]),
-                                                  __fadd_rn(p4.w, z[3])));
-                st_fac4<FES>(negt, g, make_float4(__fsub_rn(p4.x, z[0]), __fsub_rn(p4.y, z[1]), __fsub_rn(p4.z, z[2]),
-                                                  __fsub_rn(p4.w, z[3])));
+                const float4 pv = make_float4(__fadd_rn(p4.x, z[0]), __fadd_rn(p4.y, z[1]), __fadd_rn(p4.z, z[2]),
+                                              __fadd_rn(p4.w, z[3]));
+                const float4 nv4 = make_float4(__fsub_rn(p4.x, z[0]), __fsub_rn(p4.y, z[1]), __fsub_rn(p4.z, z[2]),
+                                               __fsub_rn(p4.w, z[3]));
+                st_fac4<FES>(post, g, pv);
+                st_fac4<FES>(negt, g, nv4);
+#pragma unroll
+                for (int pp = 0; pp < kMaxPeers; ++pp) {   // the peers' copies of the +/- buffers
+                  if (pp >= gp.n) break;
+                  st_fac4<FES>(reinterpret_cast<char*>(post) + gp.dpos[pp], g, pv);
+                  st_fac4<FES>(reinterpret_cast<char*>(negt) + gp.dneg[pp], g, nv4);
+                }
                 const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -873,6 +881,12 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
                 const float w0 = vsg[so];
                 st_fac<FES>(post, g, __fadd_rn(p0, z));
                 st_fac<FES>(negt, g, __fsub_rn(p0, z));
+#pragma unroll
+                for (int pp = 0; pp < kMaxPeers; ++pp) {
+                  if (pp >= gp.n) break;
+                  st_fac<FES>(reinterpret_cast<char*>(post) + gp.dpos[pp], g, __fadd_rn(p0, z));
+                  st_fac<FES>(reinterpret_cast<char*>(negt) + gp.dneg[pp], g, __fsub_rn(p0, z));
+                }
                 const float mu1 = __fmul_rn(m0, kin.beta);
                 const float var1 = __fadd_rn(__fmul_rn(w0, kin.beta2), kin.q);
                 s_zmu = fmaf(z, mu1, s_zmu);
@@ -918,6 +932,7 @@ __global__ void __launch_bounds__(kSTP, 1) k_sperturb(Tables tb, Layout L, uint6
     }
     more = (adv == 2);
   }
+  if (gp.n > 0) __threadfence_system();   // the peer stores precede this rank's next collective
 }
 
 // =====================================================================================

@@ -119,6 +119,7 @@ SIGNATURES = {
     "dsmz_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
     "dsmz_ipc_import": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),
     "dsmz_ipc_close": (c_int32, [c_void_p, c_int64]),
+    "dsmz_peer_copy": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
     "dsmz_plan_perturb_on_tensor_cores": (c_int32, [c_void_p]),
     "dsmz_plan_calibration_workspace_bytes": (c_size_t, [c_void_p]),
     "dsmz_plan_calibration_rng_increment": (c_uint64, [c_void_p]),

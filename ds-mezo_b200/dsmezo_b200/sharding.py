@@ -338,7 +338,8 @@ class ShardedStep:
                  eps: float, total_steps: int, generator: torch.Generator, copy_dtype=torch.bfloat16,
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
                  directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0,
-                 tensor_core_perturb: bool = True, fused_gather: bool = True):
+                 tensor_core_perturb: bool = True, fused_gather: Optional[bool] = None,
+                 factor_gather: str = "copy-engine"):
         import torch.distributed as dist
         self.pg = process_group
         self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None
@@ -368,23 +369,45 @@ class ShardedStep:
                                               if self.world > 1 and copy_dtype != torch.float32 else None))
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=None, rng_increment_total=stride * directions)
+        if factor_gather not in ("copy-engine", "fused", "nccl"):
+            raise ValueError("factor_gather: 'copy-engine', 'fused' or 'nccl'")
         self.fused_gather = False
         self.fused_factors = False
+        self.factor_gather = "nccl"
         self._ipc: List[Tuple[int, int]] = []
-        if fused_gather and self.world > 1 and self.coll.stream_ordered:
-            self._setup_fused_gather()
+        self._push: List[Tuple[torch.cuda.Stream, int]] = []
+        self._factors_pending = False
+        if fused_gather is None:
+            # the +/- peer stores cost the tensor-core perturbation little at any N; the
+            # CUDA-core kernel (rank > 64) stores far more per unit of its run time, and stores
+            # issued by SMs to a single peer drain at ~275 GB/s (measured, 70B on 2 GPUs:
+            # 12 ms added to a 14 ms kernel), so it fuses only where several peers share them
+            fused_gather = self.aset.perturb_uses_tensor_cores or self.world >= 4
+        if self.world > 1 and self.coll.stream_ordered and (fused_gather or factor_gather != "nccl"):
+            self._setup_peer_gathers(fused_gather, factor_gather)
 
-    def _setup_fused_gather(self) -> None:
-        """Maps every peer's +/- gather buffers into this process (CUDA IPC) and hands the
-        byte distances to the plan, whose tensor-core perturbation then stores each +/-
-        element into every rank's buffer. All ranks turn it on, or none (a rank without the
-        tensor-core perturbation or a failed mapping keeps the NCCL all-gather for all)."""
+    def _setup_peer_gathers(self, fuse_pos_neg: bool, factor_mode: str) -> None:
+        """Maps every peer's gather buffers into this process (CUDA IPC) for the gathers that
+        move data over NVLink without NCCL:
+
+        * +/- copies (fuse_pos_neg): the plan's perturbation stores each +/- element into
+          every rank's buffer as well (byte distances handed to the plan);
+        * factors, factor_mode 'fused': the update stores the bf16 shadow the same way;
+          'copy-engine': gather('factors') pushes this rank's shadow into every peer's buffer
+          with one device-to-device copy per peer on its own stream (copy engines, no SM).
+
+        Every rank takes the same choice: a rank that cannot (no shadow, a failed mapping)
+        makes all of them keep the NCCL all-gather."""
         import ctypes
         import torch.distributed as dist
         from ._lib import DsmzError, lib
         L = lib()
-        ok = self.aset.perturb_uses_tensor_cores and bool(self.aset.modules)
-        names = ("pos", "neg", "factors") if self.aset.shadow is not None else ("pos", "neg")
+        names = []
+        if fuse_pos_neg:
+            names += ["pos", "neg"]
+        if self.aset.shadow is not None and (factor_mode == "copy-engine" or (factor_mode == "fused" and names)):
+            names.append("factors")
+        ok = bool(self.aset.modules) and bool(names)
         mine = {}
         if ok:
             for name in names:
@@ -399,7 +422,7 @@ class ShardedStep:
         ok = all(x[0] for x in allh)
         deltas = {n: [] for n in names}
         if ok and any(set(x[1].keys()) != set(names) for x in allh):
-            ok = False                        # every rank fuses the same gathers
+            ok = False                        # every rank maps the same gathers
         if ok:
             for p in range(self.world):
                 if p == self.rank:
@@ -416,30 +439,48 @@ class ShardedStep:
                     break
         flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.aset.device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
-        if int(flag.item()) == 1:
+        ok = int(flag.item()) == 1
+        fuse = "pos" in names
+        fuse_f = fuse and factor_mode == "fused" and "factors" in names
+        if ok and fuse:
             try:
-                self.aset.set_gather_peers(deltas["pos"], deltas["neg"], deltas.get("factors"))
-                self.fused_gather = True
-                self.fused_factors = "factors" in deltas
+                self.aset.set_gather_peers(deltas["pos"], deltas["neg"], deltas["factors"] if fuse_f else None)
             except DsmzError:
-                self.fused_gather = False
-        flag.fill_(1 if self.fused_gather else 0)
+                ok = False
+        flag.fill_(1 if ok else 0)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
         if int(flag.item()) == 0:
-            if self.fused_gather:
+            if ok and fuse:
                 self.aset.set_gather_peers([], [])
-            self.fused_gather = False
-            self.fused_factors = False
             self.close()
+            return
+        self.fused_gather = fuse
+        self.fused_factors = fuse_f
         self._barrier = torch.zeros(1, dtype=torch.int32, device=self.aset.device)
+        if "factors" in names and not fuse_f:
+            # one stream per peer, so the copies run side by side on the copy engines; the
+            # destination is this rank's slice of the peer's gather buffer
+            self.factor_gather = "copy-engine"
+            self._cstream = torch.cuda.Stream(device=self.aset.device)
+            self._barrier_f = torch.zeros(2, dtype=torch.int32, device=self.aset.device)
+            mine_at = self.gathered["factors"].data_ptr() + \
+                self.rank * self.layout.capacity * self.gathered["factors"].element_size()
+            self._push = [(torch.cuda.Stream(device=self.aset.device), mine_at + d)
+                          for d in deltas["factors"]]
+        elif fuse_f:
+            self.factor_gather = "fused"
 
     def close(self) -> None:
-        """Unmaps the peers' gather buffers (fused all-gather)."""
+        """Unmaps the peers' gather buffers (after the copies still in flight into them)."""
         from ._lib import lib
+        if self._push:
+            self._cstream.synchronize()
+            self._push = []
         if self.fused_gather:
             self.aset.set_gather_peers([], [])
-            self.fused_gather = False
-            self.fused_factors = False
+        self.fused_gather = False
+        self.fused_factors = False
+        self.factor_gather = "nccl"
         for ptr, off in self._ipc:
             lib().dsmz_ipc_close(ptr, off)
         self._ipc = []
@@ -488,7 +529,39 @@ class ShardedStep:
         if self.coll is not None:
             self.coll.check()
             self.coll.wait_for("factors")    # the last gather of the shadow before it is rewritten
+            if self._push:                   # ... or the last copies out of it
+                torch.cuda.current_stream(self.aset.device).wait_stream(self._cstream)
         self.ctl.update(dd)
+
+    def _push_factors(self) -> None:
+        """Copy-engine factor gather: after a barrier (every rank's earlier reads of its
+        gathered factors are done), one copy per peer of this rank's shadow into its slice
+        of the peer's buffer, each on its own stream, beside whatever the current stream runs
+        next. _land_factors() orders their arrival."""
+        from ._lib import check, lib
+        cur = torch.cuda.current_stream(self.aset.device)
+        cs = self._cstream
+        cs.wait_stream(cur)                  # the update has written the shadow
+        with torch.cuda.stream(cs):
+            self.coll.all_reduce(self._barrier_f[:1], "factor buffers barrier")
+        src = self.aset.shadow.data_ptr()
+        nbytes = self.layout.sizes[self.rank] * self.aset.shadow.element_size()
+        for st, dst in self._push:
+            st.wait_stream(cs)
+            check(lib().dsmz_peer_copy(dst, src, nbytes, st.cuda_stream), "factor copy to a peer")
+        for st, _ in self._push:
+            cs.wait_stream(st)
+        self._factors_pending = True
+
+    def _land_factors(self) -> None:
+        """Orders every rank's factor copies into this rank's buffer on the current stream (a
+        barrier after each rank's copies)."""
+        if not self._factors_pending:
+            return
+        with torch.cuda.stream(self._cstream):
+            self.coll.all_reduce(self._barrier_f[1:], "factor copies landed")
+        torch.cuda.current_stream(self.aset.device).wait_stream(self._cstream)
+        self._factors_pending = False
 
     def _arena(self, name: str) -> torch.Tensor:
         # 'factors' is what the rollout loads: the copy-dtype shadow (the fp32 masters when
@@ -502,11 +575,15 @@ class ShardedStep:
         'pos' and 'neg' are ordered on the current stream at once (the scoring pass needs
         them next). The 'factors' gather is left to overlap the next step's power iteration
         and perturbation, which do not touch the shadow it sends: the stream waits for it
-        before the next update rewrites the shadow, or when the factors are exported."""
+        before the next update rewrites the shadow, or when the factors are exported. With
+        copy-engine factor gathers the copies run on their own streams (no SM)."""
         if self.world == 1:
             return {n: self._arena(n) for n in names}
         self.coll.check()
         for n in names:
+            if n == "factors" and self._push:
+                self._push_factors()         # each peer's copies follow its earlier ones on
+                continue                     # its streams, so earlier ones need no wait here
             if self.fused_gather and n in ("pos", "neg"):
                 continue                     # the perturbation stored them on every rank; the
                                              # Kalman all-reduce after it ordered those stores
@@ -521,8 +598,9 @@ class ShardedStep:
         return {n: self.gathered[n] for n in names}
 
     def synchronize(self) -> None:
-        """Waits (bounded) for every collective issued so far."""
+        """Waits (bounded) for every collective and factor copy issued so far."""
         if self.coll is not None:
+            self._land_factors()
             self.coll.settle()
 
     def full_view(self, buf: torch.Tensor, rank: int) -> torch.Tensor:
@@ -536,7 +614,9 @@ class ShardedStep:
         views of the full-model buffer that the last gather(which) filled (the local arena on
         one GPU). With a bf16 copy dtype nothing is copied: this replaces the reference's bf16
         cast and safetensors write to /dev/shm. An fp32 copy dtype is converted once on the
-        device into a bf16 buffer of the same layout. which: 'pos', 'neg' or 'factors'."""
+        device into a bf16 buffer of the same layout. which: 'pos', 'neg' or 'factors'. With
+        copy-engine factor gathers, export_adapters('factors') issues a collective (a barrier
+        after every rank's copies): call it on every rank."""
         if which not in ("pos", "neg", "factors"):
             raise ValueError("export_adapters: which is 'pos', 'neg' or 'factors'")
         K = 1 if which == "factors" else self.aset.directions
@@ -547,6 +627,8 @@ class ShardedStep:
             buf = self._arena(which)
         else:
             self.coll.wait_for(which)
+            if which == "factors":
+                self._land_factors()
             buf = self.gathered[which]
         rank_r = self._shape[4]
         idx = export_index(self.layout.rank_modules, rank_r, K * cap, direction * cap)

@@ -289,15 +289,14 @@ double* dsmz_step_kalman_sums(const dsmz_plan* plan);   /* 2 doubles per directi
 /* Fused +/- all-gather (one process per GPU of one node, no reference counterpart: the
  * reference has one process). npeers (<= 7) byte distances, multiples of 16, from this
  * plan's +/- copy buffers to each peer's buffers mapped into this process (dsmz_ipc_*):
- * every +/- element the perturbation stores is also stored at those distances, so the
- * peers receive this rank's shard over NVLink while the perturbation runs. The buffers are
- * this rank's slices of gather buffers laid out the same on every rank. The stores are
- * complete and visible system-wide when the perturbation kernel has finished: a
- * stream-ordered collective after it (the Kalman-sum all-reduce) orders every rank's reads
- * after every rank's stores. Needs the tensor-core perturbation (DSMZ_ERR_UNSUPPORTED
- * otherwise). shadow_delta (or NULL): the same for the bf16 factor shadow the update writes
- * (the factor all-gather; a stream-ordered collective after the update orders it). npeers 0
- * turns both off. */
+ * every +/- element the perturbation stores (tensor-core or CUDA-core kernel) is also
+ * stored at those distances, so the peers receive this rank's shard over NVLink while the
+ * perturbation runs. The buffers are this rank's slices of gather buffers laid out the same
+ * on every rank. The stores are complete and visible system-wide when the perturbation
+ * kernel has finished: a stream-ordered collective after it (the Kalman-sum all-reduce)
+ * orders every rank's reads after every rank's stores. shadow_delta (or NULL): the same for
+ * the bf16 factor shadow the update writes (the factor all-gather; a stream-ordered
+ * collective after the update orders it). npeers 0 turns both off. */
 int dsmz_plan_set_gather_peers(dsmz_plan* plan, int32_t npeers, const int64_t* pos_delta, const int64_t* neg_delta,
                                const int64_t* shadow_delta);
 /* CUDA IPC of a device buffer: export writes the 64-byte handle of the allocation holding
@@ -307,6 +306,11 @@ int dsmz_plan_set_gather_peers(dsmz_plan* plan, int32_t npeers, const int64_t* p
 int dsmz_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int dsmz_ipc_import(const void* handle, int64_t offset, void** ptr);
 int dsmz_ipc_close(void* ptr, int64_t offset);
+/* One device-to-device copy of `bytes` on `stream`, for pushing this rank's shard into a
+ * peer's buffer mapped by dsmz_ipc_import: a copy engine moves it over NVLink, so it runs
+ * beside kernels that hold every SM (the factor all-gather beside the next power iteration).
+ * One call per copy. */
+int dsmz_peer_copy(void* dst, const void* src, int64_t bytes, dsmz_stream_t stream);
 
 /* The Zc_A draws of direction 0 of the perturbation at (seed, offset)
  * (ds_mezo/controller.py:187-188), issued ahead: they depend on nothing the step computes,

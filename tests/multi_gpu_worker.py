@@ -1,8 +1,10 @@
 """Worker for test_gpu_multi.py (launched by torch.distributed.run, one rank per GPU).
 
-Calibrates every rank's bases against a one-GPU calibration, then runs one layer-sharded
-step and, on rank 0, the same step on one GPU; compares every rank's gathered factors, pos
-and neg, and their PEFT-named exports, with the single-GPU ones. Prints MULTI_OK."""
+Calibrates every rank's bases against a one-GPU calibration, then runs two layer-sharded
+steps and, on rank 0, the same steps on one GPU; compares every rank's gathered factors, pos
+and neg of the last step, and their PEFT-named exports, with the single-GPU ones. The
+factor gather mode comes from DSMZ_FACTOR_GATHER (copy-engine, fused or nccl), the
+perturbation kernel from DSMZ_PERTURB (tensor-cores or cuda-cores). Prints MULTI_OK."""
 import datetime
 import os
 import sys
@@ -15,6 +17,7 @@ sys.path.insert(0, os.path.join(ROOT, "ds-mezo_b200"))
 
 CFG = dict(layers=3, hidden=512, inter=1536, kv=128, rank_r=16, tokens=256)   # 12 units: ranks split a layer
 EPS, TOTAL = 1e-3, 100
+DDS = (4.5, -2.0)                       # the steps' projected-gradient scalars
 
 
 def init_units(step):
@@ -48,7 +51,11 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     gen = torch.Generator(device=dev)
     gen.manual_seed(7)
-    st = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=gen, device=dev, process_group=dist.group.WORLD)
+    mode = os.environ.get("DSMZ_FACTOR_GATHER", "copy-engine")
+    tcp = os.environ.get("DSMZ_PERTURB", "tensor-cores") == "tensor-cores"
+    st = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=gen, device=dev, process_group=dist.group.WORLD,
+                     factor_gather=mode, tensor_core_perturb=tcp, fused_gather=True)
+    assert st.aset.perturb_uses_tensor_cores == tcp
     init_units(st)
     # first-step calibration: each rank's bases equal the one-GPU calibration's, and every
     # rank's generator ends where the one-GPU calibration leaves it
@@ -70,23 +77,26 @@ def main():
     # the one-GPU step below starts from the same calibrated bases
     calibrated = {k: v.clone() for k, v in want_v.items()}
     del ref1
-    st.perturb()
-    pn = st.gather("pos", "neg")
-    pn = {k: v.clone() for k, v in pn.items()}
-    st.update(st.broadcast_dd(4.5))
-    st.gather("factors")
+    for dd in DDS:                           # the second step's copies follow the first's
+        st.perturb()
+        pn = st.gather("pos", "neg")
+        pn = {k: v.clone() for k, v in pn.items()}
+        st.update(st.broadcast_dd(dd))
+        st.gather("factors")
     st.synchronize()                         # the factors gather overlaps what follows it
     fac = st.gathered["factors"].clone()
     assert st.aset.device_error() == 0
     if rank == 0:
         g1 = torch.Generator(device=dev)
         g1.manual_seed(7)
-        one = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=g1, device=dev, process_group=None)
+        one = ShardedStep(**CFG, eps=EPS, total_steps=TOTAL, generator=g1, device=dev, process_group=None,
+                          tensor_core_perturb=tcp)
         init_units(one)
         for b, s in enumerate(one.aset.bases):
             one.aset.V(b).copy_(calibrated[(s.layer, s.name)])
-        one.perturb()
-        one.update(4.5)
+        for dd in DDS:
+            one.perturb()
+            one.update(dd)
         torch.cuda.synchronize()
         assert g1.get_offset() == gen.get_offset(), "generators advanced differently"
         # every adapter, keyed as the reference's PEFT file, from the gathered buffers equals
@@ -103,7 +113,7 @@ def main():
     # every rank's +/- copies reached every rank through the perturbation's peer stores when
     # the fused gather is on (NVLink); the comparison above covers either path
     if rank == 0:
-        print("FUSED_GATHER", st.fused_gather, st.fused_factors, flush=True)
+        print("FUSED_GATHER", st.fused_gather, st.factor_gather, flush=True)
     dist.barrier(device_ids=[local])
     st.close()
     dist.destroy_process_group()

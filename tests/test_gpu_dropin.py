@@ -116,15 +116,18 @@ def test_agzo_golden(K, kern, name):
     assert rel(z_A, c["z_A"]) < 1e-5
 
 
-def test_agzo_strided_and_contiguity(K):
+@pytest.mark.parametrize("R,d_in,RC,d_out", [(64, 3000, 64, 700), (128, 2000, 128, 500), (96, 800, 128, 200),
+                                              (128, 1500, 96, 300), (100, 600, 100, 150)])
+def test_agzo_strided_and_contiguity(K, R, d_in, RC, d_out):
+    """Square and rectangular B V; past 64 x 64 the QR keeps G and R^-1 in the workspace (or,
+    for a rank that is not a multiple of 8, runs modified Gram-Schmidt)."""
     g = torch.Generator().manual_seed(11)
-    R, d_in, RC, d_out = 64, 3000, 64, 700
     B = torch.randn(d_in, R, generator=g).t()         # strided view
     V = torch.linalg.qr(torch.randn(d_in, RC, generator=g))[0]
     zcB = torch.randn(R, RC, generator=g)
-    zcA = torch.randn(d_out, RC, generator=g)
+    zcA = torch.randn(d_out, min(R, RC), generator=g)
     z_A, z_B = K.fused_agzo_perturbation(B.to(DEV), V.to(DEV), zcB.to(DEV), zcA.to(DEV), 1e-3, FLOOR)
-    # square 64 x 64 B V: compare with the exact (fp64) algorithm; fp32 MGS carries ~1e-7*cond noise
+    # compare with the exact (fp64) algorithm; fp32 MGS carries ~1e-7*cond noise
     wA, wB = ref.fused_agzo_perturbation(B.contiguous(), V, zcB, zcA, 1e-3, FLOOR, dtype=torch.float64)
     torch.cuda.synchronize()
     assert rel(z_B, wB) < 1e-5 and rel(z_A, wA) < 1e-5
