@@ -101,24 +101,25 @@ int set_smem(K kernel, size_t bytes) {
   return 0;
 }
 
-// Newton-Schulz solve of nm matrices of rank r: r <= 64 two CTAs per SM with the matrices
-// in shared memory; larger r the packed-symmetric kernel (one CTA per SM).
+// Newton-Schulz solve of nm matrices of rank r: r <= 64 two CTAs per SM with the full
+// matrices in shared memory (k_ns_solve); larger r the packed-symmetric kernel (one CTA per
+// SM). The packed kernel at r <= 64 (four warps, four CTAs per SM) took 291 us per matrix
+// against ~150 us: its per-block addressing makes it issue-bound at that size.
 int launch_ns_solve(const Tables& tb, const MatD* mats, int nm, int r, const NSArgs& ns, cudaStream_t s) {
   int rc;
   if (r <= 64) {
     if ((rc = set_smem(k_ns_solve, ns_smem(r)))) return rc;
     k_ns_solve<<<nm, kThreads, ns_smem(r), s>>>(tb, mats, ns);
   } else {
-    if ((rc = set_smem(k_ns_solve_packed, ns_smem(r)))) return rc;
-    k_ns_solve_packed<<<nm, kNsPThreads, ns_smem(r), s>>>(tb, mats, ns);
+    if ((rc = set_smem(k_ns_solve_packed<kNsPThreads>, ns_smem(r)))) return rc;
+    k_ns_solve_packed<kNsPThreads><<<nm, kNsPThreads, ns_smem(r), s>>>(tb, mats, ns);
   }
   return 0;
 }
 
 // One adapter matrix (or W basis matrix) with its segment and workspace slots. Without
 // alloc_gram the Gram partials are placed later by chunk_matrices.
-void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bool with_solve,
-                bool alloc_gram = true) {
+void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bool alloc_gram = true) {
   m.segv = seg_vectors(static_cast<int>(m.r));
   m.nseg = static_cast<int32_t>((m.nvec + m.segv - 1) / m.segv);
   if (m.nseg < 1) m.nseg = 1;
@@ -130,8 +131,7 @@ void add_matrix(std::vector<MatD>& mats, Layout& L, MatD m, int& seg_counter, bo
   m.kmap = -1;
   m.rmap = -1;
   m.p_off = static_cast<int64_t>(L.take((rr + 4) * sizeof(float)) / sizeof(float));
-  m.dw_off = with_solve ? static_cast<int64_t>(L.take(4 * static_cast<size_t>(pad8(static_cast<int>(m.r))) *
-                                                      ns_ld(static_cast<int>(m.r)) * sizeof(double)) / sizeof(double)) : 0;
+  m.dw_off = 0;                                  // the Newton-Schulz solve works in shared memory
   mats.push_back(m);
 }
 
@@ -1559,12 +1559,12 @@ int dsmz_plan_create(const dsmz_plan_desc* d, dsmz_plan** out) {
     a.param = m.A; a.pos = m.pos_A; a.neg = m.neg_A; a.mu = m.mu_A; a.var = m.var_A; a.z = m.z_A;
     a.shadow = m.shadow_A;
     a.scratch = m.scratch_A; a.nvec = m.d_out; a.r = m.r; a.ld = m.ld_A; a.cs = 1; a.side = 0; a.owner = i;
-    add_matrix(P->mats, P->ws, a, P->nsegs, true, false);
+    add_matrix(P->mats, P->ws, a, P->nsegs, false);
     MatD b{};
     b.param = m.B; b.pos = m.pos_B; b.neg = m.neg_B; b.mu = m.mu_B; b.var = m.var_B; b.z = m.z_B;
     b.shadow = m.shadow_B;
     b.scratch = m.scratch_B; b.nvec = m.d_in; b.r = m.r; b.ld = m.ld_B; b.cs = 1; b.side = 1; b.owner = i;
-    add_matrix(P->mats, P->ws, b, P->nsegs, true, false);
+    add_matrix(P->mats, P->ws, b, P->nsegs, false);
     P->mods.push_back(md);
   }
   // B-side sums: two CTAs per SM over the modules' concatenated d_in columns
@@ -1900,7 +1900,7 @@ static dsmz_plan muon_plan(int64_t M, int64_t N, Layout* L_out) {
   m.nvec = tall ? M : N;
   m.r = tall ? N : M;
   m.side = tall ? 0 : 1;
-  add_matrix(P.mats, P.ws, m, P.nsegs, true);
+  add_matrix(P.mats, P.ws, m, P.nsegs);
   P.r = static_cast<int>(m.r);
   P.pack();
   if (L_out) *L_out = P.ws;
@@ -2055,10 +2055,10 @@ static dsmz_plan agzo_plan(int64_t R, int64_t d_in, int64_t RC, int64_t d_out) {
   plan_bside(P.mods, static_cast<int>((d_in + 2047) / 2048), P.ws, &P.nchunks, &P.bside_cols);
   MatD a{};
   a.nvec = d_out; a.r = R; a.ld = R; a.cs = 1; a.side = 0; a.owner = 0;
-  add_matrix(P.mats, P.ws, a, P.nsegs, false);
+  add_matrix(P.mats, P.ws, a, P.nsegs);
   MatD b{};
   b.nvec = d_in; b.r = R; b.ld = d_in; b.cs = 1; b.side = 1; b.owner = 0;
-  add_matrix(P.mats, P.ws, b, P.nsegs, false);
+  add_matrix(P.mats, P.ws, b, P.nsegs);
   BasisD bd{};
   bd.R = static_cast<int32_t>(RC); bd.D = d_in;
   P.bases.push_back(bd);

@@ -26,7 +26,8 @@ struct MatD {
   int32_t segv, pad0;         // vectors per segment
   int64_t gram_off;           // doubles: nseg * r*r Gram partials
   int64_t p_off;              // floats: r*r apply matrix (fp32), then 4 floats of scalars
-  int64_t dw_off;             // doubles: 4 * r*r fp64 solve workspace
+  int64_t dw_off;             // doubles: W matrices of the power iteration: 3 * r*r fp64 (Gram,
+                              // R^{-1} for the QR apply, R^{-1}); 0 for adapter matrices
   __nv_bfloat16* v2t;         // power-iteration W only: [V_hi | V_lo]^T output (NULL: none)
   int64_t ldv2;
   // streaming kernels: the global tile space (TV-vector tiles of every matrix in order) is

@@ -327,7 +327,8 @@ __host__ __device__ inline int ns_ld(int r) { return pad8(r) + 4; }
 // X_k = X_0 P_k with P_k a polynomial of G_0 = X_0^T X_0, so the 12 X-space passes become
 // G <- S G S, P <- P S on r x r (fp64), S = c0 I + c1 G + c2 G^2. Stores the fp32 apply
 // matrix Pm with X[v,:] = x_v^T Pm for every vector x_v of the matrix (P is symmetric, so
-// tall and wide matrices use it alike).
+// tall and wide matrices use it alike). r <= 64: three matrices in shared memory (two CTAs
+// per SM), products in place (one pass of cta_symm_mm); k_ns_solve_packed takes larger r.
 // =====================================================================================
 __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -337,16 +338,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
   const int rr = r * r;
   const int rp = pad8(r), ld = ns_ld(r), mm = rp * ld;
   const int tid = threadIdx.x;
-  // r <= 64: three matrices in shared memory (two CTAs per SM), products in place (one
-  // pass of cta_symm_mm); larger r: four in the fp64 workspace, products out of place.
-  const bool small = r <= 64;
-  double* dw = small ? reinterpret_cast<double*>(smem_raw) : reinterpret_cast<double*>(tb.ws) + M.dw_off;
+  double* dw = reinterpret_cast<double*>(smem_raw);
   double* G = dw;
   double* P = dw + mm;
   double* S = dw + 2 * mm;
-  double* U = dw + 3 * mm;
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
-  for (int e = tid; e < (small ? 3 : 4) * mm; e += kThreads) dw[e] = 0.0;
+  for (int e = tid; e < 3 * mm; e += kThreads) dw[e] = 0.0;
   __syncthreads();
   double tr = 0.0;
   constexpr int kSumU = 8;                             // independent partial loads in flight
@@ -388,16 +385,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
       S[a * ld + b] = ((a == b) ? c0 : 0.0) + c1 * G[a * ld + b] + c2 * g2;
     }
     __syncthreads();
-    if (small) {
-      cta_symm_mm(P, P, S, rp, ld);          // P <- P S
-      cta_symm_mm(G, S, G, rp, ld);          // G <- S G S
-      cta_symm_mm(G, G, S, rp, ld);
-    } else {
-      cta_symm_mm(U, P, S, rp, ld);
-      double* t = P; P = U; U = t;
-      cta_symm_mm(U, S, G, rp, ld);
-      cta_symm_mm(G, U, S, rp, ld);
-    }
+    cta_symm_mm(P, P, S, rp, ld);            // P <- P S
+    cta_symm_mm(G, S, G, rp, ld);            // G <- S G S
+    cta_symm_mm(G, G, S, rp, ld);
   }
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
   for (int e = tid; e < rr; e += kThreads) {
@@ -407,12 +397,13 @@ __global__ void __launch_bounds__(kThreads, 2) k_ns_solve(Tables tb, const MatD*
 }
 
 // =====================================================================================
-// Newton-Schulz solve for 64 < r <= 128: the same iteration as k_ns_solve with the three
-// matrices in shared memory. They are symmetric, so only their upper 8 x 8 blocks are
-// stored (packed row by row: 136 blocks, 204 KB for r = 128); a block holds all 64 entries,
-// XOR-swizzled (column j of row i at i*8 + (j ^ 4*((i>>1)&1))) so that the MMA fragments of
-// a block or of its transpose are two wavefronts. Sixteen warps, up to nine output blocks
-// each: every product is one pass, held in registers across a barrier and written in place.
+// Newton-Schulz solve with the three matrices in shared memory. They are symmetric, so only
+// their upper 8 x 8 blocks are stored (packed row by row: 136 blocks, 204 KB for r = 128);
+// a block holds all 64 entries, XOR-swizzled (column j of row i
+// at i*8 + (j ^ 4*((i>>1)&1))) so that the MMA fragments of a block or of its transpose are
+// two wavefronts. NT / 32 warps, up to nine output blocks each: every product is one pass,
+// held in registers across a barrier and written in place. Launched for 64 < r <= 128
+// with sixteen warps.
 // =====================================================================================
 constexpr int kNsPThreads = 512, kNsPU = 9;
 __host__ __device__ inline int ns_packed_blocks(int r) { const int nb = pad8(r) >> 3; return nb * (nb + 1) / 2; }
@@ -430,10 +421,11 @@ __device__ __forceinline__ int nsp_idx(int row, int col, int nb) {
 // as itself or as its transpose: in-block offsets dir (row g, column k) and tr (row k,
 // column g) are fixed per thread, so a k step costs a few integer adds per block.
 __device__ __forceinline__ int nsp_row0(int b, int nb) { return b * nb - ((b * (b - 1)) >> 1); }
+template <int NT>
 __device__ void nsp_mm(double* C, const double* A, const double* B, int nb) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  constexpr int nw = kNsPThreads / 32;
+  constexpr int nw = NT / 32;
   const int nq = nb * (nb + 1) / 2;
   int bi[kNsPU], bj[kNsPU], rsi[kNsPU], rsj[kNsPU];
   double acc[kNsPU][2];
@@ -486,9 +478,11 @@ __device__ void nsp_mm(double* C, const double* A, const double* B, int nb) {
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, const MatD* __restrict__ mats, NSArgs ns) {
+template <int NT>
+__global__ void __launch_bounds__(NT, 1) k_ns_solve_packed(Tables tb, const MatD* __restrict__ mats,
+                                                                                 NSArgs ns) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double red[kNsPThreads];
+  __shared__ double red[NT];
   const MatD M = mats[blockIdx.x];
   const int r = static_cast<int>(M.r);
   const int rr = r * r;
@@ -497,25 +491,25 @@ __global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, c
   double* G = reinterpret_cast<double*>(smem_raw);
   double* P = G + mm;
   double* S = P + mm;
-  for (int e = tid; e < 3 * mm; e += kNsPThreads) G[e] = 0.0;   // padding rows and columns stay zero
+  for (int e = tid; e < 3 * mm; e += NT) G[e] = 0.0;   // padding rows and columns stay zero
   __syncthreads();
   double tr = 0.0;
   const double* part = reinterpret_cast<const double*>(tb.ws) + M.gram_off;
   constexpr int kSumU = 4;                             // independent partial loads in flight
-  for (int e0 = tid; e0 < rr; e0 += kSumU * kNsPThreads) {
+  for (int e0 = tid; e0 < rr; e0 += kSumU * NT) {
     double v[kSumU];
 #pragma unroll
     for (int u = 0; u < kSumU; ++u) v[u] = 0.0;
     for (int sg = 0; sg < M.nseg; ++sg) {
 #pragma unroll
       for (int u = 0; u < kSumU; ++u) {
-        const int e = e0 + u * kNsPThreads;
+        const int e = e0 + u * NT;
         if (e < rr) v[u] += part[static_cast<int64_t>(sg) * rr + e];
       }
     }
 #pragma unroll
     for (int u = 0; u < kSumU; ++u) {
-      const int e = e0 + u * kNsPThreads;
+      const int e = e0 + u * NT;
       if (e >= rr) continue;
       const int a = e / r, b = e - a * r;
       if ((a >> 3) > (b >> 3)) continue;               // the lower blocks are the upper ones
@@ -525,7 +519,7 @@ __global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, c
   }
   red[tid] = tr;
   __syncthreads();
-  for (int w = kNsPThreads / 2; w > 0; w >>= 1) {
+  for (int w = NT / 2; w > 0; w >>= 1) {
     if (tid < w) red[tid] += red[tid + w];
     __syncthreads();
   }
@@ -534,7 +528,7 @@ __global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, c
   const double inv2 = inv * inv;
   // every stored element: block q, entry (i, j) -> matrix element (8bi+i, 8bj+j')
   auto each = [&](auto&& f) {
-    for (int e = tid; e < mm; e += kNsPThreads) {
+    for (int e = tid; e < mm; e += NT) {
       int q = e >> 6, row = 0;
       while (q >= nb - row) { q -= nb - row; ++row; }
       const int i = (e >> 3) & 7, js = e & 7;
@@ -549,18 +543,18 @@ __global__ void __launch_bounds__(kNsPThreads, 1) k_ns_solve_packed(Tables tb, c
   __syncthreads();
   for (int it = 0; it < ns.iters; ++it) {
     const double c0 = ns.c[it][0], c1 = ns.c[it][1], c2 = ns.c[it][2];
-    if (c2 != 0.0) nsp_mm(S, G, G, nb);
+    if (c2 != 0.0) nsp_mm<NT>(S, G, G, nb);
     each([&](int e, int a, int b) {
       const double g2 = (c2 != 0.0) ? S[e] : 0.0;
       S[e] = ((a == b) ? c0 : 0.0) + c1 * G[e] + c2 * g2;
     });
     __syncthreads();
-    nsp_mm(P, P, S, nb);                               // P <- P S
-    nsp_mm(G, S, G, nb);                               // G <- S G S
-    nsp_mm(G, G, S, nb);
+    nsp_mm<NT>(P, P, S, nb);                               // P <- P S
+    nsp_mm<NT>(G, S, G, nb);                               // G <- S G S
+    nsp_mm<NT>(G, G, S, nb);
   }
   float* Pm = reinterpret_cast<float*>(tb.ws) + M.p_off;
-  for (int e = tid; e < rr; e += kNsPThreads) {
+  for (int e = tid; e < rr; e += NT) {
     const int a = e / r, b = e - a * r;
     Pm[e] = static_cast<float>(P[nsp_idx(a, b, nb)] * inv);
   }

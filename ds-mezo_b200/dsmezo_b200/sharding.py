@@ -378,11 +378,11 @@ class ShardedStep:
         self._push: List[Tuple[torch.cuda.Stream, int]] = []
         self._factors_pending = False
         if fused_gather is None:
-            # the +/- peer stores cost the tensor-core perturbation little at any N; the
-            # CUDA-core kernel (rank > 64) stores far more per unit of its run time, and stores
-            # issued by SMs to a single peer drain at ~275 GB/s (measured, 70B on 2 GPUs:
-            # 12 ms added to a 14 ms kernel), so it fuses only where several peers share them
-            fused_gather = self.aset.perturb_uses_tensor_cores or self.world >= 4
+            # the +/- peer stores cost the tensor-core perturbation little; the CUDA-core
+            # kernel (rank > 64) stores far more per unit of its run time, and stores issued by
+            # SMs to one peer drained at ~275 GB/s (70B on 2 GPUs: 12 ms added to a 14 ms
+            # kernel, against ~5 ms for the NCCL all-gather), so it keeps NCCL unless asked
+            fused_gather = self.aset.perturb_uses_tensor_cores
         if self.world > 1 and self.coll.stream_ordered and (fused_gather or factor_gather != "nccl"):
             self._setup_peer_gathers(fused_gather, factor_gather)
 
