@@ -908,9 +908,9 @@ int pi_setup(const dsmz_plan* P, PiCtx& c) {
   c.err = reinterpret_cast<int*>(P->workspace + P->err_off);
   c.gram_fused = P->tc && c.R <= 64;
   c.gpb = (c.R * c.R / 2 + c.R * 4 + kThreads - 1) / kThreads;   // k_gsum CTAs per basis
-  c.small = sk::gram_nsb(c.R) == 2;
+  c.small = sk::gram_maxb(c.R) <= 5;
   int rc;
-  if ((rc = set_smem(sk::k_sgram<0, 2>, P->Lw.total))) return rc;
+  if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lw.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<2, 4>, P->Lq.total))) return rc;
   if ((rc = set_smem(sk::k_sqr_apply<4, 2>, P->Lq.total))) return rc;
@@ -999,7 +999,7 @@ int pi_qr_tail(const dsmz_plan* P, const PiCtx& c, float floor_, cudaStream_t s)
   if (c.gram_fused) {
     tc::k_gsum<<<nb * c.gpb, kThreads, 0, s>>>(c.dtcb, tb, tb.wA, c.gpb);
   } else if (c.small) {
-    sk::k_sgram<0, 2><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, c.err);
+    sk::k_sgram<0, 5><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, c.err);
   } else {
     sk::k_sgram<0, 17><<<P->grid_w1, sk::kSTG, P->Lw.total, s>>>(tb, tb.wA, nb, P->nwsegsA, P->Lw, kin, c.err);
   }
@@ -1124,8 +1124,8 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   const int nm = static_cast<int>(P->mats.size());
   int rc;
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
-  const bool small = sk::gram_nsb(r) == 2;
-  if ((rc = set_smem(sk::k_sgram<0, 2>, P->Lg.total))) return rc;
+  const bool small = sk::gram_maxb(r) <= 5;
+  if ((rc = set_smem(sk::k_sgram<0, 5>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sgram<0, 17>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
@@ -1135,7 +1135,7 @@ int run_update_dirs(const dsmz_plan* P, const sk::KalmanDirs& kd, float eta, con
   DSMZ_LAUNCHED("K-direction Kalman update");
   const KalmanIn none{};
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (small) sk::k_sgram<0, 2><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
+  if (small) sk::k_sgram<0, 5><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
   else sk::k_sgram<0, 17><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, none, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Gram of the updated momentum");
@@ -1228,13 +1228,13 @@ int run_update(const dsmz_plan* P, KalmanIn kin, float eta, const NSArgs& ns, cu
   const int nm = static_cast<int>(P->mats.size());
   int rc;
   int* err = reinterpret_cast<int*>(P->workspace + P->err_off);
-  const bool small = sk::gram_nsb(r) == 2;
-  if ((rc = set_smem(sk::k_sgram<1, 2>, P->Lg.total))) return rc;
+  const bool small = sk::gram_maxb(r) <= 5;
+  if ((rc = set_smem(sk::k_sgram<1, 5>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sgram<1, 17>, P->Lg.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<2>, P->La.total))) return rc;
   if ((rc = set_smem(sk::k_sapply<4>, P->La.total))) return rc;
   P->probe_begin(DSMZ_KID_GRAM, s);
-  if (small) sk::k_sgram<1, 2><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
+  if (small) sk::k_sgram<1, 5><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   else sk::k_sgram<1, 17><<<P->grid_m, sk::kSTG, P->Lg.total, s>>>(tb, tb.mats, nm, P->nsegs, P->Lg, kin, err);
   P->probe_end(DSMZ_KID_GRAM, s);
   DSMZ_LAUNCHED("Kalman Gram");

@@ -1308,18 +1308,13 @@ __global__ void __launch_bounds__(kQrThreads, 1) k_sqr_apply(Tables tb, const Ma
 // Tile image: side 0 X[v][c] with pitch rp + 8 doubles, side 1 X[c][v] with pitch TV + 4
 // (either way a fragment load of a warp touches 256 bytes in two wavefronts).
 // =====================================================================================
-// MMA warps own 2 x 2 groups of the upper 8 x 8 blocks ("quads": block rows 2I, 2I+1 x
-// block columns 2J, 2J+1, I <= J; a diagonal quad has three blocks). The fragment of an
-// 8-column chunk of the tile is the same value as an A operand and as a B operand, so a
-// quad's four blocks cost four fragment loads (a diagonal one two) instead of two per block.
-// Quads are dealt largest first to the warp with the fewest blocks, at most two each (r <=
-// 64: 10 quads). Past r = 64 (36 quads) the quad accumulators do not fit beside the prep
-// warps' registers, and each warp owns up to 17 single blocks (two fragment loads each).
-// NSB: 2 (quads) or 17 (single blocks).
-__host__ __device__ inline int gram_nsb(int r) { return pad8(r) <= 64 ? 2 : 17; }
-constexpr int kQuadSlots = 8;                    // table slots per MMA warp
+// MAXB: upper 8 x 8 blocks per MMA warp (5 up to r = 64, 17 up to r = 128)
+__host__ __device__ inline int gram_maxb(int r) {
+  const int nb = (r + 7) / 8;
+  return (nb * (nb + 1) / 2 + kMmaWarps - 1) / kMmaWarps;
+}
 
-template <int SRC, int NSB>
+template <int SRC, int MAXB>
 __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __restrict__ mats, int nmats, int nsegs,
                                                   Layout L, KalmanIn kin, int* err) {
   extern __shared__ unsigned char smem_raw[];
@@ -1329,36 +1324,16 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
   uint64_t* xfull = empty + L.S;                 // [2]: prep -> MMA
   uint64_t* xempty = xfull + 2;                  // [2]: MMA -> prep
   const int rp = L.rp, nb = rp / 8;
+  const int nblk = nb * (nb + 1) / 2;
   double* X0 = reinterpret_cast<double*>(smem + L.o_x);
   const int xbuf = (L.o_red - L.o_x) / 16;       // doubles per buffer (two buffers)
-  // quads: [kMmaWarps][kQuadSlots] then the counts; single blocks: block b -> warp b % 8
-  int* qtab = reinterpret_cast<int*>(smem + L.o_red);
+  int* btab = reinterpret_cast<int*>(smem + L.o_red);
   // zero both fp64 buffers (padding columns stay zero), block table, barriers
   for (int e = threadIdx.x; e < 2 * xbuf; e += kSTG) X0[e] = 0.0;
-  if (threadIdx.x == 0 && NSB > 2) {
+  if (threadIdx.x == 0) {
     int q = 0;
     for (int bi = 0; bi < nb; ++bi)
-      for (int bj = bi; bj < nb; ++bj) qtab[q++] = (bi << 8) | bj;
-  }
-  if (threadIdx.x == 0 && NSB <= 2) {
-    const int nq = (nb + 1) / 2;
-    int* cnt = qtab + kMmaWarps * kQuadSlots;
-    int load[kMmaWarps];
-    for (int w = 0; w < kMmaWarps; ++w) { cnt[w] = 0; load[w] = 0; }
-    for (int size = 4; size >= 1; --size)        // blocks in the quad, largest first
-      for (int I = 0; I < nq; ++I)
-        for (int J = I; J < nq; ++J) {
-          const int ni = (2 * I + 1 < nb) ? 2 : 1, nj = (2 * J + 1 < nb) ? 2 : 1;
-          const int nblk = I == J ? ni * (ni + 1) / 2 : ni * nj;
-          if (nblk != size) continue;
-          int best = -1;
-          for (int w = 0; w < kMmaWarps; ++w)
-            if (cnt[w] < NSB && (best < 0 || load[w] < load[best])) best = w;
-          qtab[best * kQuadSlots + cnt[best]++] = (I << 8) | J;
-          load[best] += nblk;
-        }
-  }
-  if (threadIdx.x == 0) {
+      for (int bj = bi; bj < nb; ++bj) btab[q++] = (bi << 8) | bj;
     for (int i = 0; i < L.S; ++i) { mbar_init(full + i, kFullArrivals); mbar_init(empty + i, kPrepWarps); }
     for (int i = 0; i < 2; ++i) { mbar_init(xfull + i, kPrepWarps); mbar_init(xempty + i, kMmaWarps); }
     mbar_init_fence();
@@ -1511,164 +1486,70 @@ __global__ void __launch_bounds__(kSTG, 1) k_sgram(Tables tb, const MatD* __rest
   }
 
   // -------------------------------------------------------------- MMA warps
-  if constexpr (NSB <= 2) {
-    const int mw = warp - 1 - kPrepWarps;
-    const int fv = lane & 3, fc = lane >> 2;
-    const int nmine = qtab[kMmaWarps * kQuadSlots + mw];
-    // quad q = (I, J): chunks 2I, 2I+1 (block rows) and 2J, 2J+1 (block columns); sub-block
-    // u = 2 * row half + column half, bit u of onm[q] set when it is formed (a chunk past the
-    // last block, or the mirrored sub-block of a diagonal quad, is off; a missing chunk's
-    // fragment is loaded from its pair's, in range); bits 16, 32: chunk 2I+1, 2J+1 exists
-    int qt[NSB], onm[NSB];
+  const int mw = warp - 1 - kPrepWarps;
+  const int fv = lane & 3, fc = lane >> 2;
+  const int nmine = (nblk - mw + kMmaWarps - 1) / kMmaWarps;
+  double acc[MAXB][2];
 #pragma unroll
-    for (int q = 0; q < NSB; ++q) {
-      const int t = (q < nmine) ? qtab[mw * kQuadSlots + q] : 0;
-      const int I = t >> 8, J = t & 0xff;
-      const bool i1 = 2 * I + 1 < nb, j1 = 2 * J + 1 < nb;
-      qt[q] = t;
-      onm[q] = (q < nmine) ? (1 | (j1 ? 2 : 0) | (i1 && I != J ? 4 : 0) | (i1 && j1 ? 8 : 0) | (i1 ? 16 : 0) |
-                              (j1 ? 32 : 0)) : 0;
+  for (int q = 0; q < MAXB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
+  int i = 0;
+  bool dead = false;
+  if (!it.start_seg()) return;
+  int adv;
+  do {
+    const MatD& M = it.mats[it.mi];
+    const int r = static_cast<int>(M.r), nv = it.nv();
+    const int b = i & 1;
+    if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(xfull + b, static_cast<uint32_t>(i >> 1) & 1u, err));
+    if (!dead) {
+      const double* X = X0 + b * xbuf;
+      const int sv = (M.side == 0) ? L.xp : 1;
+      const int sc = (M.side == 0) ? 1 : L.zp;
+      int oa[MAXB], ob[MAXB];
+#pragma unroll
+      for (int q = 0; q < MAXB; ++q) {
+        const int t = (q < nmine) ? btab[mw + q * kMmaWarps] : 0;
+        oa[q] = 8 * (t >> 8) * sc;
+        ob[q] = 8 * (t & 0xff) * sc;
+      }
+      const int nv4 = (nv + 3) & ~3;
+      const double* xr = X + fv * sv + fc * sc;
+      for (int v0 = 0; v0 < nv4; v0 += 4, xr += 4 * sv) {
+#pragma unroll
+        for (int q = 0; q < MAXB; ++q)
+          if (q < nmine) dmma8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xempty + b);
     }
-    auto chunk = [&](int q, int u) {               // u 0, 1: block rows; 2, 3: block columns
-      const int c0 = 2 * ((u < 2) ? (qt[q] >> 8) : (qt[q] & 0xff));
-      return ((u & 1) && c0 + 1 < nb) ? c0 + 1 : c0;
-    };
-    double acc[NSB][4][2];
-#pragma unroll
-    for (int q = 0; q < NSB; ++q)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) { acc[q][u][0] = 0.0; acc[q][u][1] = 0.0; }
-    int i = 0;
-    bool dead = false;
-    if (!it.start_seg()) return;
-    int adv;
-    do {
-      const MatD& M = it.mats[it.mi];
-      const int r = static_cast<int>(M.r), nv = it.nv();
-      const int b = i & 1;
-      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(xfull + b, static_cast<uint32_t>(i >> 1) & 1u, err));
+    ++i;
+    const int seg_done = it.seg;
+    adv = it.next();
+    if (adv != 1) {
+      // segment end: this warp's blocks (and their mirror images) of the partial
       if (!dead) {
-        const double* X = X0 + b * xbuf;
-        const int sv = (M.side == 0) ? L.xp : 1;
-        const int sc = (M.side == 0) ? 1 : L.zp;
-        const int d8 = 8 * sc;                     // one chunk further
-        int ro[NSB], co[NSB];
+        double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
 #pragma unroll
-        for (int q = 0; q < NSB; ++q) { ro[q] = 2 * (qt[q] >> 8) * d8; co[q] = 2 * (qt[q] & 0xff) * d8; }
-        const int nv4 = (nv + 3) & ~3;
-        const double* xr = X + fv * sv + fc * sc;
-        for (int v0 = 0; v0 < nv4; v0 += 4, xr += 4 * sv) {
+        for (int q = 0; q < MAXB; ++q) {
+          if (q < nmine) {
+            const int t = btab[mw + q * kMmaWarps];
+            const int bi = t >> 8, bj = t & 0xff;
+            const int row = 8 * bi + (lane >> 2);
 #pragma unroll
-          for (int q = 0; q < NSB; ++q) {
-            if (q >= nmine) continue;
-            const double a0 = xr[ro[q]], a1 = xr[ro[q] + ((onm[q] & 16) ? d8 : 0)];
-            const double b0 = xr[co[q]], b1 = xr[co[q] + ((onm[q] & 32) ? d8 : 0)];
-            if (onm[q] & 1) dmma8x8x4(acc[q][0][0], acc[q][0][1], a0, b0);
-            if (onm[q] & 2) dmma8x8x4(acc[q][1][0], acc[q][1][1], a0, b1);
-            if (onm[q] & 4) dmma8x8x4(acc[q][2][0], acc[q][2][1], a1, b0);
-            if (onm[q] & 8) dmma8x8x4(acc[q][3][0], acc[q][3][1], a1, b1);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(xempty + b);
-      }
-      ++i;
-      const int seg_done = it.seg;
-      adv = it.next();
-      if (adv != 1) {
-        // segment end: this warp's blocks (and their mirror images) of the partial
-        if (!dead) {
-          double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
-#pragma unroll
-          for (int q = 0; q < NSB; ++q) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              if (!(onm[q] & (1 << u))) continue;
-              const int bi = chunk(q, u >> 1), bj = chunk(q, 2 + (u & 1));
-              const int row = 8 * bi + (lane >> 2);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int col = 8 * bj + 2 * (lane & 3) + h;
-                if (row < r && col < r) {
-                  gout[row * r + col] = acc[q][u][h];
-                  gout[col * r + row] = acc[q][u][h];
-                }
+            for (int h = 0; h < 2; ++h) {
+              const int col = 8 * bj + 2 * (lane & 3) + h;
+              if (row < r && col < r) {
+                gout[row * r + col] = acc[q][h];
+                gout[col * r + row] = acc[q][h];
               }
             }
           }
         }
-#pragma unroll
-        for (int q = 0; q < NSB; ++q)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) { acc[q][u][0] = 0.0; acc[q][u][1] = 0.0; }
       }
-    } while (adv != 0);
-  } else {
-    const int mw = warp - 1 - kPrepWarps;
-    const int fv = lane & 3, fc = lane >> 2;
-    const int nmine = (nb * (nb + 1) / 2 - mw + kMmaWarps - 1) / kMmaWarps;
-    double acc[NSB][2];
 #pragma unroll
-    for (int q = 0; q < NSB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
-    int i = 0;
-    bool dead = false;
-    if (!it.start_seg()) return;
-    int adv;
-    do {
-      const MatD& M = it.mats[it.mi];
-      const int r = static_cast<int>(M.r), nv = it.nv();
-      const int b = i & 1;
-      if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(xfull + b, static_cast<uint32_t>(i >> 1) & 1u, err));
-      if (!dead) {
-        const double* X = X0 + b * xbuf;
-        const int sv = (M.side == 0) ? L.xp : 1;
-        const int sc = (M.side == 0) ? 1 : L.zp;
-        int oa[NSB], ob[NSB];
-#pragma unroll
-        for (int q = 0; q < NSB; ++q) {
-          const int t = (q < nmine) ? qtab[mw + q * kMmaWarps] : 0;
-          oa[q] = 8 * (t >> 8) * sc;
-          ob[q] = 8 * (t & 0xff) * sc;
-        }
-        const int nv4 = (nv + 3) & ~3;
-        const double* xr = X + fv * sv + fc * sc;
-        for (int v0 = 0; v0 < nv4; v0 += 4, xr += 4 * sv) {
-#pragma unroll
-          for (int q = 0; q < NSB; ++q)
-            if (q < nmine) dmma8x8x4(acc[q][0], acc[q][1], xr[oa[q]], xr[ob[q]]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(xempty + b);
-      }
-      ++i;
-      const int seg_done = it.seg;
-      adv = it.next();
-      if (adv != 1) {
-        // segment end: this warp's blocks (and their mirror images) of the partial
-        if (!dead) {
-          double* gout = reinterpret_cast<double*>(tb.ws) + M.gram_off + static_cast<int64_t>(seg_done - M.seg0) * r * r;
-#pragma unroll
-          for (int q = 0; q < NSB; ++q) {
-            if (q < nmine) {
-              const int t = qtab[mw + q * kMmaWarps];
-              const int bi = t >> 8, bj = t & 0xff;
-              const int row = 8 * bi + (lane >> 2);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int col = 8 * bj + 2 * (lane & 3) + h;
-                if (row < r && col < r) {
-                  gout[row * r + col] = acc[q][h];
-                  gout[col * r + row] = acc[q][h];
-                }
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < NSB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
-      }
-    } while (adv != 0);
-  }
+      for (int q = 0; q < MAXB; ++q) { acc[q][0] = 0.0; acc[q][1] = 0.0; }
+    }
+  } while (adv != 0);
 }
 
 // =====================================================================================
