@@ -1076,8 +1076,42 @@ __global__ void __launch_bounds__(kThreads) k_coef(Tables tb, uint64_t seed, uin
       }
     }
     __syncthreads();
-    if ((RCA & 7) == 0) cta_chol_rinv8(G, Rm, RCA, static_cast<double>(norm_floor));
-    else cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
+    // Second round: after an fp64 first round, G = Q1^T Q1 = I + E with |E| ~ u cond(B V)^2,
+    // and R = I + U + O(E^2), R^{-1} = I - U + O(E^2) with U = E's upper triangle, its
+    // diagonal halved. For max|E| <= 1e-6 the dropped terms are below 1e-10 of Q's entries,
+    // far under the fp32 Q written here, so the second factorisation (the serial part of this
+    // kernel) is skipped; a larger or non-finite E factors G in full.
+    bool near_identity = false;
+    if (round == 1) {
+      __shared__ double s_emax[kThreads / 32];
+      double e = 0.0;
+      for (int idx = tid; idx < RCA * RCA; idx += kThreads) {
+        const int a = idx / RCA, c = idx - a * RCA;
+        const double x = fabs(G[idx] - (a == c ? 1.0 : 0.0));
+        if (!(x <= e)) e = x;                          // NaN propagates
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const double y = __shfl_xor_sync(0xffffffffu, e, o);
+        if (!(y <= e)) e = y;
+      }
+      if ((tid & 31) == 0) s_emax[tid >> 5] = e;
+      __syncthreads();
+      e = 0.0;
+      for (int w = 0; w < kThreads / 32; ++w) if (!(s_emax[w] <= e)) e = s_emax[w];
+      near_identity = e <= 1e-6;
+      if (near_identity) {
+        for (int idx = tid; idx < RCA * RCA; idx += kThreads) {
+          const int a = idx / RCA, c = idx - a * RCA;
+          Rm[idx] = (a == c) ? 1.0 - 0.5 * (G[idx] - 1.0) : (a < c ? -G[idx] : 0.0);
+        }
+        __syncthreads();
+      }
+    }
+    if (!near_identity) {
+      if ((RCA & 7) == 0) cta_chol_rinv8(G, Rm, RCA, static_cast<double>(norm_floor));
+      else cta_chol_rinv(G, Rm, piv, RCA, static_cast<double>(norm_floor));
+    }
     if ((R & 7) == 0 && (RCA & 7) == 0) {
       // Q <- Q R^{-1} on the fp64 MMA, as Q^T <- R^{-T} Q^T on BVt (Q^T row-major): output
       // block (column block cb of Q, row block ib of Q) = sum_{a < 8cb+8} R^{-1}[a][8cb+..]
