@@ -49,7 +49,7 @@ constexpr int kQrCT = 32 * kQrGroups * kQrGroupWarps;   // consumer threads
 constexpr int kQrThreads = kQrCT + 32 * kProd;
 constexpr int kBarAll = 1;               // named barrier: all consumer threads (one role)
 // Role-split fp64 Gram: producer warp, prep warps, MMA warps.
-constexpr int kPrepWarps = 4, kMmaWarps = 8;
+constexpr int kPrepWarps = 6, kMmaWarps = 8;
 constexpr int kSTG = 32 * (1 + kPrepWarps + kMmaWarps);
 constexpr int kBarTeam0 = 2;             // named barriers 2..5: one per team
 
