@@ -171,6 +171,27 @@ def test_rloo_direction_scalars_match_oracle():
         rloo_direction_scalars(torch.ones(2, 7), 1e-3)
 
 
+def test_plan_splits_wide_y_tiles(L):
+    """A set whose widest basis sits on one Y tile (one layer, 256 tokens, d_in 4096 for the
+    down projection) leaves the deal of whole tiles to 148 CTAs uneven: the plan cuts that
+    tile into chunks of k-steps, and each power iteration launches the chunk sum as well."""
+    h = ctypes.c_void_p()
+    _, d = _fake_set(layers=1, hidden=256, inter=4096, kv=64, rank=16, tokens=256)
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
+    try:
+        assert L.dsmz_plan_uses_tensor_cores(h) == 1
+        assert L.dsmz_plan_launch_count(h, 3) == 3 * (5 + 1) + 1 + 8
+    finally:
+        L.dsmz_plan_destroy(h)
+    # the same shapes without a wide basis keep whole tiles
+    _, d = _fake_set(layers=1, hidden=256, inter=512, kv=64, rank=16, tokens=256)
+    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
+    try:
+        assert L.dsmz_plan_launch_count(h, 3) == 3 * 5 + 1 + 8
+    finally:
+        L.dsmz_plan_destroy(h)
+
+
 @pytest.mark.parametrize("K", [2, 16])
 def test_plan_directions_host_only(L, K):
     from dsmezo_b200 import draw_increments
