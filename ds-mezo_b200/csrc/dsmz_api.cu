@@ -598,8 +598,12 @@ void plan_tc_layout(dsmz_plan* P) {
   // SM count known the tiles are dealt longest first, each to the least-loaded CTA. Wide
   // bases on few tiles (the units of one rank when they are sharded over several GPUs) leave
   // that deal uneven, so tiles may be cut into chunks of at most C k-steps: each chunk writes
-  // an fp32 partial and k_ysum adds them in chunk order. C is the candidate (none, or the
-  // widest tile's k-steps / 2 .. / 8) whose deal has the shortest longest CTA.
+  // an fp32 partial and k_ysum adds them in chunk order. C is the candidate (the widest
+  // tile's k-steps / 2 .. / 8) whose deal has the shortest longest CTA, each chunk charged
+  // kChunkCost more for its partial; it is used only when that deal is at least 10% shorter
+  // than the deal of whole tiles (7B shapes: at 8 ranks, 300 -> 220; at 2 ranks the chunks
+  // measured slower than whole tiles) and the set is at least a wave's worth of work.
+  constexpr int kChunkCost = 12;
   P->ysched.clear();
   P->ysched_G = 0;
   P->tc_ysplit = false;
@@ -618,7 +622,8 @@ void plan_tc_layout(dsmz_plan* P) {
         const int nk = nk_of(c), ns = chunks_of(nk, C), ch = (nk + ns - 1) / ns;
         for (int t = 0; t < c.nytile; ++t)
           for (int kc = 0; kc < ns; ++kc)
-            items.push_back({std::min(ch, nk - kc * ch) + 4, (c.ytile0 + t) | (ns > 1 ? kc << tc::kYChunkShift : 0)});
+            items.push_back({std::min(ch, nk - kc * ch) + 4 + (ns > 1 ? kChunkCost : 0),
+                             (c.ytile0 + t) | (ns > 1 ? kc << tc::kYChunkShift : 0)});
       }
       std::stable_sort(items.begin(), items.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
       const int G = std::min(static_cast<int>(items.size()), P->sm_count);
@@ -637,13 +642,20 @@ void plan_tc_layout(dsmz_plan* P) {
     int nkmax = 0;
     for (const tc::TCBasis& c : P->tcb) nkmax = std::max(nkmax, nk_of(c));
     int bestC = 0;
-    int64_t best = deal_of(0, nullptr);
+    const int64_t whole = deal_of(0, nullptr);
+    int64_t best = whole;
     if (P->ntc_y * 8 < (1 << tc::kYChunkShift))
       for (int d = 2; d <= 8; ++d) {
         const int C = (nkmax + d - 1) / d;
         const int64_t m = deal_of(C, nullptr);
         if (m < best) { best = m; bestC = C; }
       }
+    if (best * 11 > whole * 10) bestC = 0;             // under 10% shorter: whole tiles
+    // a set that is a fraction of one wave (under 32 k-steps per CTA on average) gains nothing
+    // measurable from chunks; it keeps whole tiles
+    int64_t work = 0;
+    for (const tc::TCBasis& c : P->tcb) work += c.nytile * (nk_of(c) + 4);
+    if (work < 32ll * P->sm_count) bestC = 0;
     for (size_t i = 0; i < P->tcb.size(); ++i) {
       tc::TCBasis& c = P->tcb[i];
       const int ns = chunks_of(nk_of(c), bestC);
