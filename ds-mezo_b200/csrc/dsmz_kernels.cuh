@@ -601,78 +601,111 @@ __device__ void cta_chol_rinv(double* A, double* Ri, double* piv, int r, double 
   }
 }
 
-// Blocked form of cta_chol_rinv for r % 8 == 0 (same factor and inverse up to rounding):
-// per 8-wide block column J, warp 0 factors the diagonal block (scalar steps, the same
-// pivot clamp) and inverts it into Ri's diagonal block; the row panel R_JK = R_JJ^{-T} A_JK
-// and the trailing update A_KL -= R_JK^T R_JL (upper blocks) run on the fp64 MMA, one
-// block per warp. R^{-1}'s off-diagonal blocks follow by block back-substitution,
-// X_IJ = -R_II^{-1} sum_{I<K<=J} R_IK X_KJ, block rows from the bottom. About 3 barriers per
-// block column instead of 2 per scalar column. A's lower triangle is left as it was.
+// Blocked form of cta_chol_rinv for r % 8 == 0 (same factor and inverse up to rounding),
+// with look-ahead: one barrier per 8-wide block column J. In phase J the warps apply the
+// trailing update of every upper block (K, L), J < K <= L, each recomputing the row-panel
+// products it needs, P_K = R_JJ^{-T} A_JK, from the unmodified row J (two fp64 MMAs per
+// block, transposed into operand layout by shuffles); warp 0 updates (J+1, J+1) first and
+// then factors it (scalar steps, the same pivot clamp) and inverts it into Ri's diagonal
+// block while the other warps finish; the others also write row J-1's panel R_{J-1,K} in
+// place (nobody reads row J-1 in phase J). R^{-1}'s off-diagonal blocks follow by block
+// back-substitution, X_IJ = -R_II^{-1} sum_{I<K<=J} R_IK X_KJ, block rows from the bottom.
+// A's lower triangle is left as it was.
 __device__ void cta_chol_rinv8(double* A, double* Ri, int r, double fl) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, kq = lane & 3;
   const int nb = r >> 3, nw = kThreads / 32;
   for (int e = tid; e < r * r; e += kThreads) Ri[e] = 0.0;
   __syncthreads();
-  for (int J = 0; J < nb; ++J) {
+  // warp 0: factor the 8 x 8 diagonal block J in place and write its inverse into Ri
+  auto diag = [&](int J) {
     double* AJJ = A + 8 * J * r + 8 * J;
     double* RJJ = Ri + 8 * J * r + 8 * J;
-    if (warp == 0) {
-      double idj = 0.0;                              // lane jj keeps 1 / R_jj of this block
-      for (int jj = 0; jj < 8; ++jj) {               // the 8 x 8 diagonal block, in place
-        // one reciprocal square root per column (the chain of divisions and square roots is
-        // the serial path of the factorisation): 1/d, d = dd/d and 1/dd = (1/d)^2
-        const double dd = fmax(AJJ[jj * r + jj], fl);
-        const double id = rsqrt(dd), d = dd * id, idd = id * id;
-        if (lane == jj) idj = id;
-        int p = lane, a = jj + 1;                    // pair (a, b), jj < a <= b < 8, per lane
-        while (a < 8 && p >= 8 - a) { p -= 8 - a; ++a; }
-        const int b = a + p;
-        double upd = 0.0, rowv = 0.0;
-        if (a < 8) upd = fma(-AJJ[jj * r + a] * idd, AJJ[jj * r + b], AJJ[a * r + b]);
-        if (lane > jj && lane < 8) rowv = AJJ[jj * r + lane] * id;
-        __syncwarp();
-        if (a < 8) AJJ[a * r + b] = upd;
-        if (lane == jj) AJJ[jj * r + jj] = d;
-        if (lane > jj && lane < 8) AJJ[jj * r + lane] = rowv;
-        __syncwarp();
-      }
-      for (int i = 7; i >= 0; --i) {                 // its inverse, rows from the bottom
-        const double irii = __shfl_sync(0xffffffffu, idj, i);
-        const int c = lane >> 2, sl = lane & 3;
-        double acc = 0.0;
-        if (c > i)
-          for (int k = i + 1 + sl; k <= c; k += 4) acc += AJJ[i * r + k] * RJJ[k * r + c];
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (sl == 0 && c >= i) RJJ[i * r + c] = (c == i) ? irii : -acc * irii;
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    for (int K = J + 1 + warp; K < nb; K += nw) {    // row panel: R_JK = R_JJ^{-T} A_JK
-      double* AJK = A + 8 * J * r + 8 * K;
-      double c0 = 0.0, c1 = 0.0;
-#pragma unroll
-      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(c0, c1, RJJ[(k0 + kq) * r + g], AJK[(k0 + kq) * r + g]);
+    double idj = 0.0;                                // lane jj keeps 1 / R_jj of this block
+    for (int jj = 0; jj < 8; ++jj) {
+      // one reciprocal square root per column (the chain of divisions and square roots is
+      // the serial path of the factorisation): 1/d, d = dd/d and 1/dd = (1/d)^2
+      const double dd = fmax(AJJ[jj * r + jj], fl);
+      const double id = rsqrt(dd), d = dd * id, idd = id * id;
+      if (lane == jj) idj = id;
+      int p = lane, a = jj + 1;                      // pair (a, b), jj < a <= b < 8, per lane
+      while (a < 8 && p >= 8 - a) { p -= 8 - a; ++a; }
+      const int b = a + p;
+      double upd = 0.0, rowv = 0.0;
+      if (a < 8) upd = fma(-AJJ[jj * r + a] * idd, AJJ[jj * r + b], AJJ[a * r + b]);
+      if (lane > jj && lane < 8) rowv = AJJ[jj * r + lane] * id;
       __syncwarp();
-      AJK[g * r + 2 * kq] = c0;
-      AJK[g * r + 2 * kq + 1] = c1;
+      if (a < 8) AJJ[a * r + b] = upd;
+      if (lane == jj) AJJ[jj * r + jj] = d;
+      if (lane > jj && lane < 8) AJJ[jj * r + lane] = rowv;
+      __syncwarp();
     }
-    __syncthreads();
+    for (int i = 7; i >= 0; --i) {                   // its inverse, rows from the bottom
+      const double irii = __shfl_sync(0xffffffffu, idj, i);
+      const int c = lane >> 2, sl = lane & 3;
+      double acc = 0.0;
+      if (c > i)
+        for (int k = i + 1 + sl; k <= c; k += 4) acc += AJJ[i * r + k] * RJJ[k * r + c];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (sl == 0 && c >= i) RJJ[i * r + c] = (c == i) ? irii : -acc * irii;
+      __syncwarp();
+    }
+  };
+  // operand fragment of column c of a transposed panel product held as an MMA result
+  // (lane (g, kq) holds P^T[g][2kq], P^T[g][2kq + 1]): P^T[g][c] for this lane's c
+  auto frag = [&](double p0, double p1, int c) {
+    const int src = (lane & ~3) | (c >> 1);
+    const double v0 = __shfl_sync(0xffffffffu, p0, src), v1 = __shfl_sync(0xffffffffu, p1, src);
+    return (c & 1) ? v1 : v0;
+  };
+  if (warp == 0) diag(0);
+  __syncthreads();
+  for (int J = 0; J < nb; ++J) {
+    const double* RJJ = Ri + 8 * J * r + 8 * J;      // R_JJ^{-1}
     const int m = nb - 1 - J, np = m * (m + 1) / 2;
-    for (int p0 = warp; p0 < np; p0 += nw) {         // trailing update of the upper blocks
-      int p = p0, K = J + 1;
+    // P_K^T = A_JK^T R_JJ^{-1} (lane (g, kq): P_K^T[g][2kq..2kq+1])
+    auto panelT = [&](int K, double& p0, double& p1) {
+      const double* AJK = A + 8 * J * r + 8 * K;
+      p0 = 0.0; p1 = 0.0;
+#pragma unroll
+      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(p0, p1, AJK[(k0 + kq) * r + g], RJJ[(k0 + kq) * r + g]);
+    };
+    auto trailing = [&](int q) {                     // A_KL -= P_K^T P_L for upper block q
+      int p = q, K = J + 1;
       while (p >= nb - K) { p -= nb - K; ++K; }
       const int L = K + p;
+      double pk0, pk1, pl0, pl1;
+      panelT(K, pk0, pk1);
+      if (L == K) { pl0 = pk0; pl1 = pk1; } else panelT(L, pl0, pl1);
       double* AKL = A + 8 * K * r + 8 * L;
-      const double* RJK = A + 8 * J * r + 8 * K;
-      const double* RJL = A + 8 * J * r + 8 * L;
       double c0 = AKL[g * r + 2 * kq], c1 = AKL[g * r + 2 * kq + 1];
 #pragma unroll
-      for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(c0, c1, -RJK[(k0 + kq) * r + g], RJL[(k0 + kq) * r + g]);
+      for (int k0 = 0; k0 < 8; k0 += 4)
+        dmma8x8x4(c0, c1, -frag(pk0, pk1, k0 + kq), frag(pl0, pl1, k0 + kq));
       AKL[g * r + 2 * kq] = c0;
       AKL[g * r + 2 * kq + 1] = c1;
+    };
+    if (warp == 0) {
+      if (np > 0) {                                  // (J+1, J+1), then factor it
+        trailing(0);
+        __syncwarp();
+        diag(J + 1);
+      }
+    } else {
+      for (int q = warp; q < np; q += nw - 1) trailing(q);
+      if (J > 0) {                                   // row J-1's panel: R_{J-1,K} in place
+        const double* RPP = Ri + 8 * (J - 1) * r + 8 * (J - 1);
+        for (int K = J + warp - 1; K < nb; K += nw - 1) {
+          double* APK = A + 8 * (J - 1) * r + 8 * K;
+          double c0 = 0.0, c1 = 0.0;
+#pragma unroll
+          for (int k0 = 0; k0 < 8; k0 += 4) dmma8x8x4(c0, c1, RPP[(k0 + kq) * r + g], APK[(k0 + kq) * r + g]);
+          __syncwarp();
+          APK[g * r + 2 * kq] = c0;
+          APK[g * r + 2 * kq + 1] = c1;
+        }
+      }
     }
     __syncthreads();
   }
