@@ -254,9 +254,10 @@ def main():
     ap.add_argument("--power-iter", default="two-pass", choices=["two-pass", "single-pass"],
                     help="tensor-core power iteration: two products per iteration (default), or the single-pass "
                          "kernel that reads each activation from HBM once per iteration")
-    ap.add_argument("--factor-gather", default="copy-engine", choices=["copy-engine", "fused", "nccl"],
+    ap.add_argument("--factor-gather", default=None, choices=["copy-engine", "fused", "nccl"],
                     help="N > 1: how the updated factors reach every rank: one copy-engine copy per peer beside "
-                         "the next power iteration (default), peer stores inside the update kernel, or NCCL")
+                         "the next power iteration, peer stores inside the update kernel, or NCCL (default: "
+                         "copy engines on 2 GPUs, peer stores on more)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.layers > 0:
@@ -650,7 +651,7 @@ def main():
         "momentum, lognormal-scaled N(0,1) activations)",
         "config": dict(config_of(cfg, world, sum(b.T * b.D for b in aset.bases) * aset.H_arena.element_size() / 1e9),
                        power_iteration=args.power_iter, perturbation=args.perturb,
-                       factor_gather=args.factor_gather if world > 1 else None),
+                       factor_gather=sstep.factor_gather if world > 1 else None),
         "roofline": roof,
         "step_roofline": {"alg_bytes": step_bytes, "achieved_GBps": step_bytes / (ms * 1e-3) / 1e9,
                           "frac": step_bytes / (ms * 1e-3) / 1e9 / hbm / (world if world > 1 else 1),

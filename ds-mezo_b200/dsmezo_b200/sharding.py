@@ -339,7 +339,7 @@ class ShardedStep:
                  act_dtype=torch.bfloat16, schedule="cubic", device="cuda", process_group=None, power_iters: int = 3,
                  directions: int = 1, single_pass_power_iter: bool = False, collective_timeout_s: float = 60.0,
                  tensor_core_perturb: bool = True, fused_gather: Optional[bool] = None,
-                 factor_gather: str = "copy-engine"):
+                 factor_gather: Optional[str] = None):
         import torch.distributed as dist
         self.pg = process_group
         self.coll = Collectives(process_group, collective_timeout_s) if process_group is not None else None
@@ -369,6 +369,10 @@ class ShardedStep:
                                               if self.world > 1 and copy_dtype != torch.float32 else None))
         self.ctl = ZOController(self.aset, eps, total_steps, generator, power_iters=power_iters, schedule=schedule,
                                 process_group=None, rng_increment_total=stride * directions)
+        if factor_gather is None:
+            # copy engines beside the next power iteration are measured and tested on two GPUs;
+            # with more ranks the update's peer stores (measured at four and eight) stand
+            factor_gather = "copy-engine" if self.world <= 2 else "fused"
         if factor_gather not in ("copy-engine", "fused", "nccl"):
             raise ValueError("factor_gather: 'copy-engine', 'fused' or 'nccl'")
         self.fused_gather = False
