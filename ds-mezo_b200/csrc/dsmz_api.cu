@@ -4,7 +4,6 @@
 #include <cstring>
 #include <mutex>
 #include <string>
-#include <queue>
 #include <vector>
 
 #include <cudaTypedefs.h>
@@ -321,7 +320,6 @@ size_t pf_smem(int R) {
 struct TCSlots {             // workspace byte offsets of one basis
   size_t v2t = 0, y2t = 0;
   size_t gp = 0;             // fused W Gram partials (R <= 64), 0: none
-  size_t ypart = 0;          // split Y tiles: fp32 partials per (tile, chunk), 0: none
   int64_t ldv2 = 0, ldy2 = 0;
 };
 
@@ -372,8 +370,6 @@ struct dsmz_plan {
   std::vector<TCSlots> tcs;
   size_t off_tcb = 0, err_off = 0;
   int ntc_y = 0, ntc_w = 0, ntc_vt = 0;
-  bool tc_ysplit = false;            // some Y tiles are dealt in chunks of k-steps (k_ysum sums them)
-  int ysum_blocks = 0;               // k_ysum grid: 64-token blocks of the longest basis
   // single-pass (fused) power iteration, R <= 64: work queue and launch-local counters
   bool fused = false;
   std::vector<tc::PiItem> pitems_y, pitems_w;   // the Y and W queues
@@ -595,81 +591,14 @@ void plan_tc_layout(dsmz_plan* P) {
     }
   }
   // Persistent Y kernel: tiles cost ceil(D / 64) k-steps (plus the epilogue), so with the
-  // SM count known the tiles are dealt longest first, each to the least-loaded CTA. Wide
-  // bases on few tiles (the units of one rank when they are sharded over several GPUs) leave
-  // that deal uneven, so tiles may be cut into chunks of at most C k-steps: each chunk writes
-  // an fp32 partial and k_ysum adds them in chunk order. C is the candidate (the widest
-  // tile's k-steps / 2 .. / 8) whose deal has the shortest longest CTA, each chunk charged
-  // kChunkCost more for its partial; it is used only when that deal is at least 10% shorter
-  // than the deal of whole tiles (7B shapes: at 8 ranks, 300 -> 220; at 2 ranks the chunks
-  // measured slower than whole tiles) and the set is at least a wave's worth of work.
-  constexpr int kChunkCost = 12;
+  // SM count known the tiles are dealt longest first, each to the least-loaded CTA.
   P->ysched.clear();
   P->ysched_G = 0;
-  P->tc_ysplit = false;
-  P->ysum_blocks = 0;
   if (P->sm_count > 0 && P->ntc_y > 0) {
-    auto nk_of = [](const tc::TCBasis& c) { return static_cast<int>((c.D + tc::kBK - 1) / tc::kBK); };
-    auto chunks_of = [](int nk, int C) {            // chunks of a tile of nk k-steps (1: whole)
-      if (C <= 0 || nk <= C || nk < 16) return 1;
-      const int ns = std::min(8, (nk + C - 1) / C);
-      const int ch = (nk + ns - 1) / ns;
-      return (nk + ch - 1) / ch;                    // every chunk non-empty
-    };
-    auto deal_of = [&](int C, std::vector<std::pair<int64_t, int>>* out) {   // longest CTA of the deal
-      std::vector<std::pair<int64_t, int>> items;   // (cost, item)
-      for (const tc::TCBasis& c : P->tcb) {
-        const int nk = nk_of(c), ns = chunks_of(nk, C), ch = (nk + ns - 1) / ns;
-        for (int t = 0; t < c.nytile; ++t)
-          for (int kc = 0; kc < ns; ++kc)
-            items.push_back({std::min(ch, nk - kc * ch) + 4 + (ns > 1 ? kChunkCost : 0),
-                             (c.ytile0 + t) | (ns > 1 ? kc << tc::kYChunkShift : 0)});
-      }
-      std::stable_sort(items.begin(), items.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
-      const int G = std::min(static_cast<int>(items.size()), P->sm_count);
-      std::priority_queue<int64_t, std::vector<int64_t>, std::greater<int64_t>> load;
-      for (int g = 0; g < G; ++g) load.push(0);
-      int64_t longest = 0;
-      for (const auto& it : items) {
-        const int64_t x = load.top() + it.first;
-        load.pop();
-        load.push(x);
-        longest = std::max(longest, x);
-      }
-      if (out) *out = std::move(items);
-      return longest;
-    };
-    int nkmax = 0;
-    for (const tc::TCBasis& c : P->tcb) nkmax = std::max(nkmax, nk_of(c));
-    int bestC = 0;
-    const int64_t whole = deal_of(0, nullptr);
-    int64_t best = whole;
-    if (P->ntc_y * 8 < (1 << tc::kYChunkShift))
-      for (int d = 2; d <= 8; ++d) {
-        const int C = (nkmax + d - 1) / d;
-        const int64_t m = deal_of(C, nullptr);
-        if (m < best) { best = m; bestC = C; }
-      }
-    if (best * 11 > whole * 10) bestC = 0;             // under 10% shorter: whole tiles
-    // a set that is a fraction of one wave (under 32 k-steps per CTA on average) gains nothing
-    // measurable from chunks; it keeps whole tiles
-    int64_t work = 0;
-    for (const tc::TCBasis& c : P->tcb) work += c.nytile * (nk_of(c) + 4);
-    if (work < 32ll * P->sm_count) bestC = 0;
-    for (size_t i = 0; i < P->tcb.size(); ++i) {
-      tc::TCBasis& c = P->tcb[i];
-      const int ns = chunks_of(nk_of(c), bestC);
-      c.ysplit = ns > 1 ? ns : 0;
-      if (ns > 1) {
-        const int64_t wrows = static_cast<int64_t>(tc::w_halves(static_cast<int>(c.R))) * tc::kBM;
-        P->tcs[i].ypart = P->ws.take(static_cast<size_t>(c.nytile) * ns * wrows * c.R * sizeof(float));
-        P->tc_ysplit = true;
-        P->ysum_blocks = std::max<int>(P->ysum_blocks, static_cast<int>((c.T + 63) / 64));
-      }
-    }
-    std::vector<std::pair<int64_t, int>> items;
-    deal_of(bestC, &items);
-    const int G = std::min(static_cast<int>(items.size()), P->sm_count);
+    const int G = std::min(P->ntc_y, P->sm_count);
+    std::vector<std::pair<int64_t, int>> items;           // (cost, item)
+    for (const tc::TCBasis& c : P->tcb)
+      for (int t = 0; t < c.nytile; ++t) items.push_back({(c.D + tc::kBK - 1) / tc::kBK + 4, c.ytile0 + t});
     std::stable_sort(items.begin(), items.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
     std::vector<int64_t> load(G, 0);
     std::vector<std::vector<int32_t>> lists(G);
@@ -857,7 +786,6 @@ bool bind_tc(dsmz_plan* P) {
     c.Y2T = reinterpret_cast<__nv_bfloat16*>(P->workspace + t.y2t);
     c.W = reinterpret_cast<float*>(P->workspace) + b.w_off;
     c.Gp = t.gp ? reinterpret_cast<double*>(P->workspace + t.gp) : nullptr;
-    c.Ypart = t.ypart ? reinterpret_cast<float*>(P->workspace + t.ypart) : nullptr;
     c.Vsrc = b.Vin; c.v_s0 = b.v_s0; c.v_s1 = b.v_s1; c.Vout = b.Vout;
     const uint32_t n2 = static_cast<uint32_t>(2 * b.R);
     if (!encode_bf16_2d(&c.mapHy, b.H, b.D, b.T, b.h_s0 * 2, 64, 128) ||
@@ -1024,11 +952,6 @@ int pi_y(const dsmz_plan* P, const PiCtx& c, cudaStream_t s, int first) {
       tc::k_pi_yp<2><<<gy, tc::kThreadsTC, py_smem(R), s>>>(c.dtcb, c.nb, P->ntc_y, ys, py_stages(R), c.err);
     else
       tc::k_pi_yp<1><<<gy, tc::kThreadsTC, py_smem(R), s>>>(c.dtcb, c.nb, P->ntc_y, ys, py_stages(R), c.err);
-    if (P->tc_ysplit && ys) {
-      DSMZ_LAUNCHED("power iteration Y = H V (tcgen05, chunks)");
-      if (tc::w_halves(R) == 2) tc::k_ysum<2><<<dim3(P->ysum_blocks, c.nb), 256, 0, s>>>(c.dtcb);
-      else tc::k_ysum<1><<<dim3(P->ysum_blocks, c.nb), 256, 0, s>>>(c.dtcb);
-    }
   } else {
     k_pi_gemm<0><<<dim3(P->nytiles, P->ysplit), kThreads, 0, s>>>(c.tb, first);
     if (P->ysplit > 1) {
@@ -1696,8 +1619,7 @@ int32_t dsmz_plan_launch_count(const dsmz_plan* p, int32_t num_iters) {
   // per iteration: Y, W (one fused launch on the single-pass path), Gram of W, Cholesky, V;
   // plus the first bf16 split of the caller's basis on the tensor-core path
   if (!p->bases.empty() && num_iters > 0)
-    n += num_iters * ((p->fused ? 4 : 5) + (p->ysplit > 1 ? 1 : 0) + (p->tc && !p->fused && p->tc_ysplit ? 1 : 0)) +
-         (p->tc ? 1 : 0);
+    n += num_iters * ((p->fused ? 4 : 5) + (p->ysplit > 1 ? 1 : 0)) + (p->tc ? 1 : 0);
   if (!p->mods.empty()) n += 1 + 4 * p->ndir + (p->ndir > 1 ? 4 : 3);   // B-side, per direction 4, update
   return n;
 }

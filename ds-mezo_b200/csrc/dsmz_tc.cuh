@@ -42,25 +42,13 @@ struct alignas(64) TCBasis {
   int64_t v_s0, v_s1;
   int64_t ldv2, ldy2;
   int64_t T, D;
-  int32_t R;
-  int32_t ysplit;         // Y product: chunks of k-steps per tile (0 or 1: whole tiles)
+  int32_t R, pad0;
   int32_t ytile0, nytile, wtile0, nwtile;
   int32_t vt0, nvt;       // blocks of the split kernel
   double* Gp;             // fused W Gram (R <= 64): per W tile, its upper 8 x 8 blocks of
                           // W_tile^T W_tile (block-major, 64 doubles each); NULL: not fused
   int32_t nq, pad1;       // upper blocks per tile
-  float* Ypart;           // ysplit > 1: fp32 partial Y per (tile, chunk), MT * 128 rows x R each
 };
-
-// Y tiles of a split basis are dealt as (tile, chunk) items: item = tile | chunk << 16.
-constexpr int kYChunkShift = 16;
-__device__ __forceinline__ void y_krange(const TCBasis* B, int kc, int& k0, int& k1) {
-  const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
-  if (B->ysplit <= 1) { k0 = 0; k1 = nk; return; }
-  const int ch = (nk + B->ysplit - 1) / B->ysplit;   // the host makes every chunk non-empty
-  k0 = kc * ch;
-  k1 = k0 + ch < nk ? k0 + ch : nk;
-}
 
 // Pitch (doubles) of the fp64 W tile staged by the W kernel's epilogue for the fused Gram:
 // R + 4 (R % 16 == 0, so 4 mod 16): each half-warp's fragment (four rows x four columns of
@@ -466,14 +454,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restri
       bool ok = true;
       for (int j = 0; j < nmine && ok; ++j) {
         const int item = item_of(j);
-        const int tid_ = item & ((1 << kYChunkShift) - 1);
-        const int bi = basis_of(tid_);
+        const int bi = basis_of(item);
         const TCBasis* B = bases + bi;
         if (bi != cur) { tmap_acquire(&B->mapHy); tmap_acquire(&B->mapV2); cur = bi; }
-        const int tile = tid_ - B->ytile0;
-        int k0, k1;
-        y_krange(B, item >> kYChunkShift, k0, k1);
-        for (int i = k0; i < k1; ++i) {
+        const int tile = item - B->ytile0;
+        const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
           const int s = g % stages;
           const uint32_t u = static_cast<uint32_t>(g / stages);
           if (g >= stages && !mbar_wait(empty + s, (u & 1u) ^ 1u, err)) { ok = false; break; }
@@ -502,11 +488,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restri
         if (j >= 2 && !mbar_wait(tempty + a, static_cast<uint32_t>((j >> 1) - 1) & 1u, err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dacc = tmem + static_cast<uint32_t>(a * MT * acc_cols);
-        const int item = item_of(j);
-        const TCBasis* B = bases + basis_of(item & ((1 << kYChunkShift) - 1));
-        int k0, k1;
-        y_krange(B, item >> kYChunkShift, k0, k1);
-        for (int i = k0; i < k1; ++i) {
+        const TCBasis* B = bases + basis_of(item_of(j));
+        const int nk = static_cast<int>((B->D + kBK - 1) / kBK);
+        for (int i = 0; i < nk; ++i) {
           const int s = g % stages;
           if (!mbar_wait(full + s, static_cast<uint32_t>(g / stages) & 1u, err)) { ok = false; break; }
           tc_fence_after();
@@ -517,7 +501,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restri
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)   // A and B: K-major rows of 128 B (half h 16 KB on)
               mma_bf16(dacc + static_cast<uint32_t>(h * acc_cols), sdesc(a0 + h * 16384 + kk * 32, 16, 1024),
-                       sdesc(b0 + kk * 32, 16, 1024), idesc, (i > k0 || kk > 0) ? 1u : 0u);
+                       sdesc(b0 + kk * 32, 16, 1024), idesc, (i > 0 || kk > 0) ? 1u : 0u);
           mma_commit(empty + s);
           ++g;
         }
@@ -541,27 +525,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restri
       if (all_ok == 0) break;
       tc_fence_after();
       const int item = item_of(j);
-      const int kc = item >> kYChunkShift;
-      const TCBasis* B = bases + basis_of(item & ((1 << kYChunkShift) - 1));
-      const int tile = (item & ((1 << kYChunkShift) - 1)) - B->ytile0;
+      const TCBasis* B = bases + basis_of(item);
+      const int tile = item - B->ytile0;
       const uint32_t tbase = tmem + static_cast<uint32_t>(a * MT * acc_cols) + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll
       for (int h = 0; h < MT; ++h) {
         const int64_t t = (static_cast<int64_t>(tile) * MT + h) * kBM + row;
-        // split tile: this chunk's fp32 partial row (k_ysum adds the chunks in order)
-        float* prow = B->ysplit > 1
-                          ? B->Ypart + ((static_cast<int64_t>(tile) * B->ysplit + kc) * (MT * kBM) + h * kBM + row) * R
-                          : nullptr;
         for (int c0 = 0; c0 < R; c0 += 16) {
           float hi[16], lo[16];
           tmem_ld16(tbase + static_cast<uint32_t>(h * acc_cols) + c0, hi);
           tmem_ld16(tbase + static_cast<uint32_t>(h * acc_cols) + R + c0, lo);
-          if (prow) {
-#pragma unroll
-            for (int c = 0; c < 16; c += 4)
-              *reinterpret_cast<float4*>(prow + c0 + c) =
-                  make_float4(hi[c] + lo[c], hi[c + 1] + lo[c + 1], hi[c + 2] + lo[c + 2], hi[c + 3] + lo[c + 3]);
-          } else if (t < B->T) {
+          if (t < B->T) {
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
               const float y = hi[c] + lo[c];
@@ -583,43 +557,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1) k_pi_yp(const TCBasis* __restri
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
-  }
-}
-
-// Split Y tiles: adds the chunks' fp32 partials of each row in chunk order (the same
-// summation on every run) and writes the row's [Y_hi | Y_lo]^T like the Y kernel's epilogue.
-// Grid (row blocks of 64 tokens, basis); bases without a split return at once. The 64 x R
-// block goes through shared memory so that both the partial reads (along R) and the
-// transposed writes (along the tokens) are coalesced.
-template <int MT>
-__global__ void __launch_bounds__(256) k_ysum(const TCBasis* __restrict__ bases) {
-  __shared__ float blk[64][DSMZ_MAX_RANK + 1];
-  const TCBasis* B = bases + blockIdx.y;
-  const int ns = B->ysplit;
-  if (ns <= 1) return;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 64;
-  if (t0 >= B->T) return;
-  const int R = B->R;
-  for (int e = threadIdx.x; e < 64 * R; e += 256) {
-    const int rr = e / R, c = e - rr * R;
-    const int64_t t = t0 + rr;
-    float y = 0.f;
-    if (t < B->T) {
-      const int64_t tile = t / (MT * kBM), row = t - tile * (MT * kBM);
-      const float* p = B->Ypart + (tile * ns * (MT * kBM) + row) * R + c;
-      for (int kc = 0; kc < ns; ++kc) y += p[static_cast<int64_t>(kc) * (MT * kBM) * R];
-    }
-    blk[rr][c] = y;
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < 64 * R; e += 256) {
-    const int c = e / 64, rr = e - c * 64;
-    const int64_t t = t0 + rr;
-    if (t >= B->T) continue;
-    const float y = blk[rr][c];
-    const __nv_bfloat16 yh = __float2bfloat16_rn(y);
-    B->Y2T[static_cast<int64_t>(c) * B->ldy2 + t] = yh;
-    B->Y2T[static_cast<int64_t>(R + c) * B->ldy2 + t] = __float2bfloat16_rn(y - __bfloat162float(yh));
   }
 }
 

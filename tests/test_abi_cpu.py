@@ -171,25 +171,6 @@ def test_rloo_direction_scalars_match_oracle():
         rloo_direction_scalars(torch.ones(2, 7), 1e-3)
 
 
-@pytest.mark.parametrize("layers,hidden,inter,tokens,chunks", [
-    (1, 3584, 18944, 4096, True),     # one 7B layer: 16 down tiles of 296 k-steps on 148 CTAs
-    (28, 3584, 18944, 4096, False),   # the whole 7B set: whole tiles deal within 3%
-    (1, 256, 4096, 256, False),       # a wide tile, but a fraction of one wave of work
-    (1, 256, 512, 256, False)])       # no wide tile
-def test_plan_splits_wide_y_tiles(L, layers, hidden, inter, tokens, chunks):
-    """When the widest bases sit on few Y tiles (one rank's share of a sharded set), the deal
-    of whole tiles to 148 CTAs is uneven: the plan cuts those tiles into chunks of k-steps,
-    and each power iteration launches the chunk sum as well."""
-    h = ctypes.c_void_p()
-    _, d = _fake_set(layers=layers, hidden=hidden, inter=inter, kv=64, rank=64, tokens=tokens)
-    assert L.dsmz_plan_create(ctypes.byref(d), ctypes.byref(h)) == 0
-    try:
-        assert L.dsmz_plan_uses_tensor_cores(h) == 1
-        assert L.dsmz_plan_launch_count(h, 3) == 3 * (5 + (1 if chunks else 0)) + 1 + 8
-    finally:
-        L.dsmz_plan_destroy(h)
-
-
 @pytest.mark.parametrize("K", [2, 16])
 def test_plan_directions_host_only(L, K):
     from dsmezo_b200 import draw_increments
